@@ -1,0 +1,171 @@
+/*
+ * kg_abi.h — C ABI of libkgcuda, the B200 (sm_100a) backend for katgpt-rs's
+ * per-token transformer forward (prefill + batched decode).
+ *
+ * The reference's only plugin seam for this path is the `InferenceBackend`
+ * trait (src/inference_backend.rs:45-92): one `forward(ctx, weights, cache,
+ * token, pos, config) -> &mut [f32]` per token, plus device_name /
+ * supports_stateful / reset / compile / is_compiled / recompile_hint. A Rust
+ * `CudaBackend` implementing that trait binds the entry points below through
+ * a thin `extern "C"` block; the batched entry points are
+ * the extension the trait lacks (prefill over T positions, decode over many
+ * sequences).
+ *
+ * Conventions: every call returns an int status (0 = ok, negative = kg_status)
+ * and never transfers ownership. Host buffers are caller-allocated. The `_dev`
+ * variants take device pointers and a cudaStream_t (as void*) and do not
+ * synchronise. Calls on one context must be serialised by the caller (the
+ * trait takes &mut self). There is no CPU fallback: a context needs a B200,
+ * and forward entry points return KG_ERR_UNSUPPORTED for a model shape that
+ * has no device kernel (the TurboQuant codec still works for any shape).
+ */
+#ifndef KG_ABI_H
+#define KG_ABI_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kg_ctx kg_ctx;
+
+/* Status codes. Mirrors CompileError (src/inference_backend.rs:14-40):
+ * KG_ERR_INVALID_WEIGHTS ~ InvalidWeights, KG_ERR_UNSUPPORTED ~
+ * UnsupportedBackend, KG_ERR_CUDA/KG_ERR_OOM ~ DeviceError. */
+typedef enum {
+    KG_OK = 0,
+    KG_ERR_INVALID_ARG = -1,
+    KG_ERR_OOM = -2,
+    KG_ERR_CUDA = -3,
+    KG_ERR_TIMEOUT = -4,
+    KG_ERR_NOT_COMPILED = -5,
+    KG_ERR_UNSUPPORTED = -6,
+    KG_ERR_INVALID_WEIGHTS = -7
+} kg_status;
+
+/* Which reference forward a context reproduces. */
+typedef enum {
+    KG_KV_F32 = 0,     /* transformer::forward -> forward_base, f32 KV (src/transformer.rs:398-429,1821-2200) */
+    KG_KV_TQ = 1,      /* transformer::forward_quantized<TurboQuantKVCache> (src/transformer.rs:4042-4233) */
+    KG_KV_SPKV_TQ = 2  /* sp_kv::forward::forward_sp_kv_quant, SpKvGateMode::Hard (src/sp_kv/forward.rs:610-822) */
+} kg_kv_mode;
+
+typedef enum {
+    KG_W_F32 = 0,  /* f32 weights, reference operation order (exact path) */
+    KG_W_BF16 = 1  /* bf16 weights, tensor-core path */
+} kg_weight_dtype;
+
+/* Fields of the reference `Config` (crates/katgpt-types/src/config.rs:14-180)
+ * that the path reads, plus backend knobs. */
+typedef struct {
+    int32_t vocab_size;
+    int32_t block_size;
+    int32_t n_embd;
+    int32_t n_head;
+    int32_t head_dim;
+    int32_t n_kv_head;
+    int32_t mlp_hidden;
+    int32_t n_layer;
+    int32_t bos_token;
+    float temperature;
+    float sparse_threshold; /* TwELL switch: dense W2 recompute when alive/m > 1 - this */
+    int32_t kv_mode;        /* kg_kv_mode */
+    int32_t key_bits;       /* TurboQuant bits (2,3,4,8) for KG_KV_TQ / KG_KV_SPKV_TQ */
+    int32_t val_bits;
+    int32_t weight_dtype;   /* kg_weight_dtype */
+    int32_t max_seqs;       /* sequence slots in the device KV arena */
+    int32_t spkv_window;    /* SpKvConfig::window (src/sp_kv/types.rs:44-56), default 128 */
+    float spkv_threshold;   /* SpKvConfig::threshold, default 0.5 */
+    float spkv_init_bias;   /* SpKvConfig::predictor_init_bias, default 5.0 */
+    uint64_t tq_seed;       /* rotation seed, 42 in TurboQuantKVCache::new (src/turboquant/kv_cache.rs:63-77) */
+} kg_config;
+
+/* Fill `c` with Config::micro() (config.rs:226-316) and the defaults above. */
+void kg_config_micro(kg_config *c);
+
+/* ---- context lifecycle (InferenceBackend::compile / is_compiled) ---- */
+
+/* Create a context on CUDA device `device`: allocates the KV arena for
+ * cfg->max_seqs sequences and builds the TurboQuant tables (codebook,
+ * rotation) bit-identically to TurboQuantKVCache::new. */
+int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out);
+void kg_ctx_destroy(kg_ctx *ctx);
+/* Last error message of this context ("" if none). */
+const char *kg_last_error(const kg_ctx *ctx);
+const char *kg_status_string(int status);
+/* InferenceBackend::device_name */
+const char *kg_device_name(const kg_ctx *ctx);
+
+/* Number of floats in the flat weight layout: wte[V*n], wpe[block*n], per
+ * layer {wq[n*n], wk[kvd*n], wv[kvd*n], wo[n*n], w1[m*n], w2[n*m]},
+ * lm_head[V*n], delta_routing_query[L*n], delta_routing_norm[L*n] — the
+ * TransformerWeights field order (crates/katgpt-transformer/src/weights.rs:76-177). */
+int64_t kg_weights_count(const kg_config *cfg);
+
+/* TransformerWeights::new(config, Rng::new(seed)) (weights.rs:76-177) into a
+ * host buffer of kg_weights_count floats. scale_mode 0: the reference's
+ * scales; 1: every tensor ~ N(0, std_) drawn in the same order. */
+int kg_reference_weights(const kg_config *cfg, uint64_t seed, int scale_mode, float std_,
+                         float *out);
+
+/* Upload weights (flat layout above, host f32). For KG_W_BF16 contexts the
+ * values are rounded to bf16 (nearest-even) on the device. Marks the context
+ * compiled (InferenceBackend::compile). */
+int kg_upload_weights(kg_ctx *ctx, const float *host_weights, int64_t count);
+/* Same, from a device f32 buffer. */
+int kg_upload_weights_dev(kg_ctx *ctx, const float *dev_weights, int64_t count);
+/* InferenceBackend::is_compiled */
+int kg_is_compiled(const kg_ctx *ctx);
+
+/* ---- sequences (InferenceBackend::reset) ---- */
+
+/* Clear sequence slot `seq` (KV codes, norms, caches) for a new sequence,
+ * as MultiLayerKVCache::reset / TurboQuantKVCache::reset / SpKvQuantCache::reset. */
+int kg_seq_reset(kg_ctx *ctx, int32_t seq);
+int kg_seq_reset_all(kg_ctx *ctx);
+
+/* ---- forward ---- */
+
+/* InferenceBackend::forward: one token of sequence `seq` at position `pos`;
+ * writes vocab_size logits to host `logits_out`. */
+int kg_forward_token(kg_ctx *ctx, int32_t seq, int32_t token, int32_t pos, float *logits_out);
+
+/* Teacher-forced batch: for each i < n_seq, sequence seq_ids[i] runs tokens
+ * [i*T .. i*T+T) at positions start_pos[i] .. start_pos[i]+T-1 (start_pos may
+ * be NULL = all zero). Equals T successive `forward` calls per sequence.
+ * logits_out [n_seq][T][V] and probs_out [n_seq][T][V] (softmax_scaled with
+ * 1/temperature, math.rs:36-50) are written when non-NULL. Host pointers. */
+int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                     const int32_t *start_pos, int32_t T, float *logits_out, float *probs_out);
+
+/* Device-pointer form of kg_forward_batch on `stream` (cudaStream_t). All
+ * pointers are device pointers; no host synchronisation. */
+int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids,
+                         const int32_t *tokens, const int32_t *start_pos, int32_t T,
+                         float *logits_out, float *probs_out, void *stream);
+
+/* ---- TurboQuant codec access (parity / inspection) ---- */
+
+/* Packed bytes per vector for `bits` at dimension `dim` (kv_cache.rs:499-509). */
+int64_t kg_tq_packed_len(int64_t dim, int32_t bits);
+/* Copy the context's tables to host: rotation [kvd*kvd] row-major, key and
+ * value centroids [2^bits] and boundaries [2^bits-1]. Any pointer may be NULL. */
+int kg_tq_tables(const kg_ctx *ctx, float *rotation, float *key_centroids, float *key_boundaries,
+                 float *val_centroids, float *val_boundaries);
+/* Encode n_vec host vectors [n_vec][kvd] with the key (which=0) or value
+ * (which=1) codebook: packed codes [n_vec][packed_len] and norms [n_vec]
+ * (TurboQuantKVCache::store_key/store_value, kv_cache.rs:156-237). */
+int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed,
+                 float *norms);
+/* Read back the stored codes and norms of (seq, layer, pos): key codes, value
+ * codes, norms[2] = {key, value}. */
+int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *key_codes,
+                uint8_t *val_codes, float *norms);
+/* SP-KV utility of (seq, layer, pos) (SpKvQuantLayerMeta::utilities). */
+int kg_spkv_utility(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, float *utility);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

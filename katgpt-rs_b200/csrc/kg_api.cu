@@ -1,0 +1,495 @@
+// kg_api.cu — the C ABI (include/kg_abi.h): context lifecycle, weight upload,
+// TurboQuant table construction, batch forward dispatch, codec access.
+//
+// This is the host runtime behind a `CudaBackend: InferenceBackend`
+// (src/inference_backend.rs:45-92): one context per device owns the weights,
+// the per-sequence KV arena and a CUDA stream. There is no CPU fallback: any
+// configuration without a device kernel is rejected at creation.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "kg_internal.h"
+
+namespace kg {
+void host_normals(uint64_t seed, int64_t n, float *out);
+int64_t weights_count(const kg_config &c);
+void reference_weights(const kg_config &c, uint64_t seed, int scale_mode, float std_, float *out);
+void lloyd_max(int64_t dim, int bits, std::vector<float> &cent, std::vector<float> &bnd);
+void predictor_weights(int64_t n, int64_t hidden, int64_t nkv, float init_bias, std::vector<float> &out);
+}  // namespace kg
+
+namespace {
+
+int fail(kg_ctx *ctx, int code, const std::string &msg) {
+    if (ctx) ctx->err = msg;
+    return code;
+}
+int cuda_fail(kg_ctx *ctx, cudaError_t e, const char *what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    if (e == cudaErrorMemoryAllocation) return fail(ctx, KG_ERR_OOM, m);
+    return fail(ctx, KG_ERR_CUDA, m);
+}
+#define KG_CUDA(ctx, call)                                        \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return cuda_fail((ctx), e_, #call); \
+    } while (0)
+
+int64_t packed_len(int64_t n, int bits) {  // src/turboquant/kv_cache.rs:499-509
+    switch (bits) {
+        case 2: return (n + 3) / 4;
+        case 3:
+        case 4: return (n + 1) / 2;
+        case 8: return n;
+        default: return (n * bits + 7) / 8;
+    }
+}
+
+template <typename T>
+int dalloc(kg_ctx *ctx, T **p, size_t count) {
+    void *q = nullptr;
+    if (count == 0) count = 1;
+    cudaError_t e = cudaMalloc(&q, count * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMalloc");
+    ctx->allocs.push_back(q);
+    *p = static_cast<T *>(q);
+    return 0;
+}
+
+int ensure_stage(kg_ctx *ctx, size_t bytes) {
+    if (ctx->stage_bytes >= bytes) return 0;
+    if (ctx->stage) cudaFree(ctx->stage);
+    ctx->stage = nullptr;
+    ctx->stage_bytes = 0;
+    size_t want = std::max(bytes, (size_t)1 << 20);
+    KG_CUDA(ctx, cudaMalloc(&ctx->stage, want));
+    ctx->stage_bytes = want;
+    return 0;
+}
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int validate(const kg_config *c, std::string &why) {
+    if (!c) return why = "null config", -1;
+    if (c->n_embd <= 0 || c->n_head <= 0 || c->head_dim <= 0 || c->n_kv_head <= 0 ||
+        c->n_layer <= 0 || c->vocab_size <= 0 || c->mlp_hidden <= 0 || c->block_size <= 0)
+        return why = "non-positive dimension", -1;
+    if ((int64_t)c->n_head * c->head_dim != c->n_embd) return why = "n_head*head_dim != n_embd", -1;
+    if (c->n_head % c->n_kv_head) return why = "n_head not a multiple of n_kv_head", -1;
+    if (c->max_seqs <= 0) return why = "max_seqs must be positive", -1;
+    if (c->kv_mode < KG_KV_F32 || c->kv_mode > KG_KV_SPKV_TQ) return why = "bad kv_mode", -1;
+    if (c->kv_mode != KG_KV_F32) {
+        for (int b : {c->key_bits, c->val_bits})
+            if (b < 2 || b > 8) return why = "TurboQuant bits must be in [2, 8]", -1;
+        if ((int64_t)c->n_kv_head * c->head_dim < 3) return why = "kv_dim must be >= 3", -1;
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+void kg_config_micro(kg_config *c) {
+    std::memset(c, 0, sizeof(*c));
+    c->vocab_size = 27;
+    c->block_size = 16;
+    c->n_embd = 16;
+    c->n_head = 4;
+    c->head_dim = 4;
+    c->n_kv_head = 4;
+    c->mlp_hidden = 64;
+    c->n_layer = 1;
+    c->bos_token = 26;
+    c->temperature = 0.5f;
+    c->sparse_threshold = 0.8f;
+    c->kv_mode = KG_KV_F32;
+    c->key_bits = 3;
+    c->val_bits = 3;
+    c->weight_dtype = KG_W_F32;
+    c->max_seqs = 1;
+    c->spkv_window = 128;
+    c->spkv_threshold = 0.5f;
+    c->spkv_init_bias = 5.0f;
+    c->tq_seed = 42;
+}
+
+const char *kg_status_string(int s) {
+    switch (s) {
+        case KG_OK: return "ok";
+        case KG_ERR_INVALID_ARG: return "invalid argument";
+        case KG_ERR_OOM: return "device out of memory";
+        case KG_ERR_CUDA: return "CUDA error";
+        case KG_ERR_TIMEOUT: return "timeout";
+        case KG_ERR_NOT_COMPILED: return "weights not uploaded";
+        case KG_ERR_UNSUPPORTED: return "unsupported configuration";
+        case KG_ERR_INVALID_WEIGHTS: return "invalid weights";
+        default: return "unknown status";
+    }
+}
+
+const char *kg_last_error(const kg_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+const char *kg_device_name(const kg_ctx *ctx) { return ctx ? ctx->dev_name.c_str() : "CUDA"; }
+int64_t kg_weights_count(const kg_config *cfg) { return cfg ? kg::weights_count(*cfg) : -1; }
+int64_t kg_tq_packed_len(int64_t dim, int32_t bits) { return packed_len(dim, bits); }
+int kg_is_compiled(const kg_ctx *ctx) { return ctx && ctx->compiled ? 1 : 0; }
+
+int kg_reference_weights(const kg_config *cfg, uint64_t seed, int scale_mode, float std_, float *out) {
+    std::string why;
+    if (validate(cfg, why) || !out) return KG_ERR_INVALID_ARG;
+    kg::reference_weights(*cfg, seed, scale_mode, std_, out);
+    return KG_OK;
+}
+
+void kg_ctx_destroy(kg_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (void *p : ctx->allocs) cudaFree(p);
+    if (ctx->stage) cudaFree(ctx->stage);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
+    if (!out) return KG_ERR_INVALID_ARG;
+    *out = nullptr;
+    std::string why;
+    if (validate(cfg, why)) {
+        std::fprintf(stderr, "kg_ctx_create: %s\n", why.c_str());
+        return KG_ERR_INVALID_ARG;
+    }
+    kg_ctx *ctx = new kg_ctx;
+    ctx->micro = kg::micro_supported(*cfg) == 0;
+    ctx->cfg = *cfg;
+    ctx->device = device;
+    int rc = 0;
+    auto bail = [&](int r) {
+        std::fprintf(stderr, "kg_ctx_create: %s\n", ctx->err.c_str());
+        kg_ctx_destroy(ctx);
+        return r;
+    };
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "cudaSetDevice"));
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "cudaGetDeviceProperties"));
+    if (prop.major != 10) return bail(fail(ctx, KG_ERR_UNSUPPORTED, "device is not sm_100 (B200)"));
+    ctx->dev_name = std::string("CUDA:") + prop.name;
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "cudaStreamCreate"));
+
+    const kg_config &c = ctx->cfg;
+    ctx->n = c.n_embd; ctx->nh = c.n_head; ctx->hd = c.head_dim; ctx->nkv = c.n_kv_head;
+    ctx->kvd = ctx->nkv * ctx->hd; ctx->m = c.mlp_hidden; ctx->V = c.vocab_size;
+    ctx->L = c.n_layer; ctx->B = c.block_size;
+    ctx->w_count = kg::weights_count(c);
+    const bool tq = c.kv_mode != KG_KV_F32;
+    ctx->kpl = tq ? packed_len(ctx->kvd, c.key_bits) : 0;
+    ctx->vpl = tq ? packed_len(ctx->kvd, c.val_bits) : 0;
+    ctx->ph = std::max<int64_t>(ctx->n / 4, 16);
+
+    // ---- KV arena (exact micro path: f32 K/V or dequantized cache + codes)
+    const size_t S = (size_t)c.max_seqs, rows = ctx->micro ? S * ctx->L * ctx->B : 0;
+    if ((rc = dalloc(ctx, &ctx->Kf, rows * ctx->kvd))) return bail(rc);
+    if ((rc = dalloc(ctx, &ctx->Vf, rows * ctx->kvd))) return bail(rc);
+    if ((rc = dalloc(ctx, &ctx->codes, rows * (ctx->kpl + ctx->vpl)))) return bail(rc);
+    if ((rc = dalloc(ctx, &ctx->norms, rows * 2))) return bail(rc);
+    if ((rc = dalloc(ctx, &ctx->util, rows))) return bail(rc);
+    if ((rc = dalloc(ctx, &ctx->d_err, 1))) return bail(rc);
+
+    // ---- TurboQuant tables (TurboQuantKVCache::new, kv_cache.rs:56-99)
+    const int64_t kvd = ctx->kvd;
+    std::vector<float> kc, kb, vc, vb;
+    if (tq) {
+        kg::lloyd_max(kvd, c.key_bits, kc, kb);
+        kg::lloyd_max(kvd, c.val_bits, vc, vb);
+        std::vector<float> g(kvd * kvd);
+        kg::host_normals(c.tq_seed, kvd * kvd, g.data());
+        float *dg = nullptr, *work = nullptr;
+        if ((rc = dalloc(ctx, &dg, kvd * kvd))) return bail(rc);
+        if ((rc = dalloc(ctx, &work, kvd * kvd))) return bail(rc);
+        if ((rc = dalloc(ctx, &ctx->rot, kvd * kvd))) return bail(rc);
+        if ((rc = dalloc(ctx, &ctx->rot_t, kvd * kvd))) return bail(rc);
+        e = cudaMemcpyAsync(dg, g.data(), kvd * kvd * 4, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "upload gaussian"));
+        e = kg::tq_rotation_device((int)kvd, dg, ctx->rot, ctx->rot_t, work, ctx->stream);
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "rotation build"));
+        ctx->h_rot.resize(kvd * kvd);
+        e = cudaMemcpyAsync(ctx->h_rot.data(), ctx->rot, kvd * kvd * 4, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "download rotation"));
+        e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "rotation build sync"));
+        ctx->h_kc = kc; ctx->h_kb = kb; ctx->h_vc = vc; ctx->h_vb = vb;
+        if ((rc = dalloc(ctx, &ctx->kc, kc.size()))) return bail(rc);
+        if ((rc = dalloc(ctx, &ctx->kb, kb.size()))) return bail(rc);
+        if ((rc = dalloc(ctx, &ctx->vc, vc.size()))) return bail(rc);
+        if ((rc = dalloc(ctx, &ctx->vb, vb.size()))) return bail(rc);
+        cudaMemcpy(ctx->kc, kc.data(), kc.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->kb, kb.data(), kb.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->vc, vc.data(), vc.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->vb, vb.data(), vb.size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (c.kv_mode == KG_KV_SPKV_TQ)
+        kg::predictor_weights(ctx->n, ctx->ph, ctx->nkv, c.spkv_init_bias, ctx->h_pred);
+
+    if (!ctx->micro) {
+        // Codec-only context: TurboQuant tables and the encoder are available;
+        // forward entry points return KG_ERR_UNSUPPORTED for this shape.
+        *out = ctx;
+        return KG_OK;
+    }
+    // ---- micro pack: weights | rot | rot_t | kc | kb | vc | vb | predictor
+    kg::MicroArgs &a = ctx->margs;
+    int64_t off = 0;
+    const int64_t n = ctx->n, V = ctx->V, L = ctx->L;
+    a.off_wte = 0;
+    a.off_wpe = (int)(V * n);
+    a.off_layers = (int)(a.off_wpe + ctx->B * n);
+    a.layer_stride = (int)(2 * n * n + 2 * kvd * n + 2 * ctx->m * n);
+    a.off_lm = (int)(a.off_layers + L * a.layer_stride);
+    a.off_dq = (int)(a.off_lm + V * n);
+    a.off_dn = (int)(a.off_dq + L * n);
+    off = a.off_dn + L * n;  // == w_count
+    a.off_rot = (int)off; off += tq ? kvd * kvd : 0;
+    a.off_rot_t = (int)off; off += tq ? kvd * kvd : 0;
+    a.off_kc = (int)off; off += (int64_t)kc.size();
+    a.off_kb = (int)off; off += (int64_t)kb.size();
+    a.off_vc = (int)off; off += (int64_t)vc.size();
+    a.off_vb = (int)off; off += (int64_t)vb.size();
+    a.off_pw1 = (int)off; off += ctx->ph * n;
+    a.off_pb1 = (int)off; off += ctx->ph;
+    a.off_pw2 = (int)off; off += ctx->nkv * ctx->ph;
+    a.off_pb2 = (int)off; off += ctx->nkv;
+    off = (off + 3) / 4 * 4;
+    ctx->pack_floats = off;
+    if (off * 4 > 200 * 1024) return bail(fail(ctx, KG_ERR_UNSUPPORTED, "micro weights exceed shared memory"));
+    if ((rc = dalloc(ctx, &ctx->pack, off))) return bail(rc);
+    KG_CUDA(ctx, cudaMemset(ctx->pack, 0, off * 4));
+    if (tq) {
+        std::vector<float> rt(kvd * kvd);
+        for (int64_t i = 0; i < kvd; ++i)
+            for (int64_t j = 0; j < kvd; ++j) rt[i * kvd + j] = ctx->h_rot[j * kvd + i];
+        cudaMemcpy(ctx->pack + a.off_rot, ctx->h_rot.data(), kvd * kvd * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->pack + a.off_rot_t, rt.data(), kvd * kvd * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->pack + a.off_kc, kc.data(), kc.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->pack + a.off_kb, kb.data(), kb.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->pack + a.off_vc, vc.data(), vc.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(ctx->pack + a.off_vb, vb.data(), vb.size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (!ctx->h_pred.empty())
+        cudaMemcpy(ctx->pack + a.off_pw1, ctx->h_pred.data(), ctx->h_pred.size() * 4, cudaMemcpyHostToDevice);
+    a.pack = ctx->pack;
+    a.pack_floats = (int)ctx->pack_floats;
+    a.L = (int)L;
+    a.kbits = c.key_bits; a.vbits = c.val_bits;
+    a.kpl = (int)ctx->kpl; a.vpl = (int)ctx->vpl;
+    a.sparse_threshold = c.sparse_threshold;
+    a.inv_temp = 1.0f / c.temperature;
+    a.Kf = ctx->Kf; a.Vf = ctx->Vf; a.codes = ctx->codes; a.norms = ctx->norms; a.util = ctx->util;
+    a.n_slots = c.max_seqs;
+    a.err = ctx->d_err;
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "context init"));
+    if ((rc = kg_seq_reset_all(ctx))) return bail(rc);
+    *out = ctx;
+    return KG_OK;
+}
+
+int kg_upload_weights(kg_ctx *ctx, const float *w, int64_t count) {
+    if (!ctx || !w) return KG_ERR_INVALID_ARG;
+    if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
+    if (count != ctx->w_count)
+        return fail(ctx, KG_ERR_INVALID_WEIGHTS,
+                    "weight count " + std::to_string(count) + " != " + std::to_string(ctx->w_count));
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    KG_CUDA(ctx, cudaMemcpyAsync(ctx->pack, w, count * 4, cudaMemcpyHostToDevice, ctx->stream));
+    KG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    ctx->compiled = true;
+    return KG_OK;
+}
+
+int kg_upload_weights_dev(kg_ctx *ctx, const float *w, int64_t count) {
+    if (!ctx || !w) return KG_ERR_INVALID_ARG;
+    if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
+    if (count != ctx->w_count) return fail(ctx, KG_ERR_INVALID_WEIGHTS, "weight count mismatch");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    KG_CUDA(ctx, cudaMemcpyAsync(ctx->pack, w, count * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    KG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    ctx->compiled = true;
+    return KG_OK;
+}
+
+int kg_seq_reset(kg_ctx *ctx, int32_t seq) {
+    if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs) return KG_ERR_INVALID_ARG;
+    if (!ctx->micro) return KG_OK;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t rows = (size_t)ctx->L * ctx->B, r0 = (size_t)seq * rows;
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->Kf + r0 * ctx->kvd, 0, rows * ctx->kvd * 4, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->Vf + r0 * ctx->kvd, 0, rows * ctx->kvd * 4, s));
+    if (ctx->kpl + ctx->vpl)
+        KG_CUDA(ctx, cudaMemsetAsync(ctx->codes + r0 * (ctx->kpl + ctx->vpl), 0, rows * (ctx->kpl + ctx->vpl), s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->norms + r0 * 2, 0, rows * 2 * 4, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->util + r0, 0, rows * 4, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    return KG_OK;
+}
+
+int kg_seq_reset_all(kg_ctx *ctx) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (!ctx->micro) return KG_OK;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t rows = (size_t)ctx->cfg.max_seqs * ctx->L * ctx->B;
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->Kf, 0, rows * ctx->kvd * 4, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->Vf, 0, rows * ctx->kvd * 4, s));
+    if (ctx->kpl + ctx->vpl) KG_CUDA(ctx, cudaMemsetAsync(ctx->codes, 0, rows * (ctx->kpl + ctx->vpl), s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->norms, 0, rows * 2 * 4, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->util, 0, rows * 4, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->d_err, 0, 4, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    return KG_OK;
+}
+
+int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                         const int32_t *start_pos, int32_t T, float *logits, float *probs, void *stream) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
+    if (!ctx->compiled) return fail(ctx, KG_ERR_NOT_COMPILED, "weights not uploaded");
+    if (n_seq < 0 || T < 1 || T > ctx->B || T > 16 || !seq_ids || !tokens)
+        return fail(ctx, KG_ERR_INVALID_ARG, "bad batch shape");
+    if (n_seq == 0) return KG_OK;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    kg::MicroArgs a = ctx->margs;
+    a.n_seq = n_seq;
+    a.T = T;
+    a.seq_ids = seq_ids;
+    a.tokens = tokens;
+    a.start_pos = start_pos;
+    a.logits = logits;
+    a.probs = probs;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    KG_CUDA(ctx, kg::launch_micro(ctx->cfg, a, s));
+    return KG_OK;
+}
+
+int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                     const int32_t *start_pos, int32_t T, float *logits_out, float *probs_out) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (n_seq < 0 || T < 1 || T > ctx->B || !seq_ids || !tokens)
+        return fail(ctx, KG_ERR_INVALID_ARG, "bad batch shape");
+    if (n_seq == 0) return KG_OK;
+    // host-side argument checks (the kernel re-checks device-side)
+    for (int32_t i = 0; i < n_seq; ++i) {
+        if (seq_ids[i] < 0 || seq_ids[i] >= ctx->cfg.max_seqs)
+            return fail(ctx, KG_ERR_INVALID_ARG, "sequence id out of range");
+        int32_t p0 = start_pos ? start_pos[i] : 0;
+        if (p0 < 0 || p0 + T > ctx->B) return fail(ctx, KG_ERR_INVALID_ARG, "position beyond block_size");
+    }
+    for (int64_t i = 0; i < (int64_t)n_seq * T; ++i)
+        if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, KG_ERR_INVALID_ARG, "token out of range");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t b_ids = align256(n_seq * 4), b_tok = align256((size_t)n_seq * T * 4);
+    const size_t b_out = align256((size_t)n_seq * T * ctx->V * 4);
+    int rc = ensure_stage(ctx, 3 * b_ids + b_tok + 2 * b_out);
+    if (rc) return rc;
+    char *st = static_cast<char *>(ctx->stage);
+    int32_t *d_ids = reinterpret_cast<int32_t *>(st);
+    int32_t *d_pos = reinterpret_cast<int32_t *>(st + b_ids);
+    int32_t *d_tok = reinterpret_cast<int32_t *>(st + 2 * b_ids);
+    float *d_log = reinterpret_cast<float *>(st + 2 * b_ids + b_tok);
+    float *d_prb = reinterpret_cast<float *>(st + 2 * b_ids + b_tok + b_out);
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemcpyAsync(d_ids, seq_ids, n_seq * 4, cudaMemcpyHostToDevice, s));
+    if (start_pos) KG_CUDA(ctx, cudaMemcpyAsync(d_pos, start_pos, n_seq * 4, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(d_tok, tokens, (size_t)n_seq * T * 4, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->d_err, 0, 4, s));
+    rc = kg_forward_batch_dev(ctx, n_seq, d_ids, d_tok, start_pos ? d_pos : nullptr, T,
+                              logits_out ? d_log : nullptr, probs_out ? d_prb : nullptr, s);
+    if (rc) return rc;
+    const size_t ob = (size_t)n_seq * T * ctx->V * 4;
+    if (logits_out) KG_CUDA(ctx, cudaMemcpyAsync(logits_out, d_log, ob, cudaMemcpyDeviceToHost, s));
+    if (probs_out) KG_CUDA(ctx, cudaMemcpyAsync(probs_out, d_prb, ob, cudaMemcpyDeviceToHost, s));
+    int herr = 0;
+    KG_CUDA(ctx, cudaMemcpyAsync(&herr, ctx->d_err, 4, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    if (herr) return fail(ctx, KG_ERR_INVALID_ARG, "device rejected a token, position or slot");
+    return KG_OK;
+}
+
+int kg_forward_token(kg_ctx *ctx, int32_t seq, int32_t token, int32_t pos, float *logits_out) {
+    return kg_forward_batch(ctx, 1, &seq, &token, &pos, 1, logits_out, nullptr);
+}
+
+int kg_tq_tables(const kg_ctx *ctx, float *rot, float *kc, float *kb, float *vc, float *vb) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (ctx->cfg.kv_mode == KG_KV_F32) return KG_ERR_INVALID_ARG;
+    if (rot) std::memcpy(rot, ctx->h_rot.data(), ctx->h_rot.size() * 4);
+    if (kc) std::memcpy(kc, ctx->h_kc.data(), ctx->h_kc.size() * 4);
+    if (kb) std::memcpy(kb, ctx->h_kb.data(), ctx->h_kb.size() * 4);
+    if (vc) std::memcpy(vc, ctx->h_vc.data(), ctx->h_vc.size() * 4);
+    if (vb) std::memcpy(vb, ctx->h_vb.data(), ctx->h_vb.size() * 4);
+    return KG_OK;
+}
+
+int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed, float *norms) {
+    if (!ctx || !x || !packed || !norms || n_vec < 0 || (which != 0 && which != 1))
+        return KG_ERR_INVALID_ARG;
+    if (ctx->cfg.kv_mode == KG_KV_F32) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
+    if (n_vec == 0) return KG_OK;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int64_t kvd = ctx->kvd;
+    const int bits = which == 0 ? ctx->cfg.key_bits : ctx->cfg.val_bits;
+    const int64_t pl = packed_len(kvd, bits);
+    const size_t bx = align256(n_vec * kvd * 4), bp = align256(n_vec * pl), bn = align256(n_vec * 4);
+    int rc = ensure_stage(ctx, bx + bp + bn);
+    if (rc) return rc;
+    char *st = static_cast<char *>(ctx->stage);
+    float *dx = reinterpret_cast<float *>(st);
+    uint8_t *dp = reinterpret_cast<uint8_t *>(st + bx);
+    float *dn = reinterpret_cast<float *>(st + bx + bp);
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemcpyAsync(dx, x, n_vec * kvd * 4, cudaMemcpyHostToDevice, s));
+    // codes of a zero-norm vector are left untouched: start from the caller's bytes
+    KG_CUDA(ctx, cudaMemcpyAsync(dp, packed, n_vec * pl, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, kg::tq_encode_device((int)kvd, bits, n_vec, dx, ctx->rot, which == 0 ? ctx->kb : ctx->vb,
+                                      dp, pl, dn, 1, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(packed, dp, n_vec * pl, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(norms, dn, n_vec * 4, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    return KG_OK;
+}
+
+int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *kcodes, uint8_t *vcodes,
+                float *norms) {
+    if (ctx && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no KV arena for this model shape");
+    if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs || layer < 0 || layer >= ctx->L || pos < 0 || pos >= ctx->B)
+        return KG_ERR_INVALID_ARG;
+    if (ctx->cfg.kv_mode == KG_KV_F32) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int64_t row = ((int64_t)seq * ctx->L + layer) * ctx->B + pos;
+    cudaStream_t s = ctx->stream;
+    if (kcodes) KG_CUDA(ctx, cudaMemcpyAsync(kcodes, ctx->codes + row * (ctx->kpl + ctx->vpl), ctx->kpl, cudaMemcpyDeviceToHost, s));
+    if (vcodes) KG_CUDA(ctx, cudaMemcpyAsync(vcodes, ctx->codes + row * (ctx->kpl + ctx->vpl) + ctx->kpl, ctx->vpl, cudaMemcpyDeviceToHost, s));
+    if (norms) KG_CUDA(ctx, cudaMemcpyAsync(norms, ctx->norms + row * 2, 8, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    return KG_OK;
+}
+
+int kg_spkv_utility(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, float *utility) {
+    if (ctx && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no KV arena for this model shape");
+    if (!ctx || !utility || seq < 0 || seq >= ctx->cfg.max_seqs || layer < 0 || layer >= ctx->L || pos < 0 ||
+        pos >= ctx->B)
+        return KG_ERR_INVALID_ARG;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int64_t row = ((int64_t)seq * ctx->L + layer) * ctx->B + pos;
+    KG_CUDA(ctx, cudaMemcpy(utility, ctx->util + row, 4, cudaMemcpyDeviceToHost));
+    return KG_OK;
+}
+
+}  // extern "C"

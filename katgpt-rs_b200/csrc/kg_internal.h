@@ -1,0 +1,82 @@
+// kg_internal.h — host/device shared structures of libkgcuda (not part of the ABI).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/kg_abi.h"
+
+namespace kg {
+
+// Arguments of the exact-order micro forward kernel (kg_micro.cu).
+struct MicroArgs {
+    // packed read-only data copied to shared memory: weights (flat reference
+    // layout), TurboQuant tables, SP-KV predictor
+    const float *pack;
+    int pack_floats;
+    int off_wte, off_wpe, off_layers, layer_stride, off_lm, off_dq, off_dn;
+    int off_rot, off_rot_t, off_kc, off_kb, off_vc, off_vb;
+    int off_pw1, off_pb1, off_pw2, off_pb2;
+    int L;
+    int kbits, vbits, kpl, vpl;
+    float sparse_threshold, inv_temp;
+    // batch
+    int n_seq, T;
+    const int32_t *seq_ids, *tokens, *start_pos;
+    float *logits, *probs;
+    // per-sequence device state, [slot][layer][pos][...]
+    float *Kf, *Vf;          // f32 K/V (forward_base) or dequantized K/V cache (TurboQuant modes)
+    uint8_t *codes;          // [.. ][kpl + vpl]
+    float *norms;            // [.. ][2]
+    float *util;             // [.. ]
+    int n_slots;
+    int *err;                // set to a nonzero code on an invalid token/position/slot
+};
+
+// Returns 0 if the model shape has a compiled micro kernel.
+int micro_supported(const kg_config &c);
+cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s);
+
+// TurboQuant device helpers (kg_tq.cu)
+// Modified Gram-Schmidt of a row-major dim x dim Gaussian matrix `g`
+// (device) into `rot` (row-major Q, columns = basis), bit-identical to
+// generate_rotation_matrix (src/turboquant/rotation.rs:11-52). `work` holds
+// dim*dim floats.
+cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t, float *work,
+                               cudaStream_t s);
+// Encode n_vec vectors [n_vec][dim] (exact reference order).
+cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
+                             const float *bnd, uint8_t *packed, int64_t packed_stride,
+                             float *norms, int64_t norm_stride, cudaStream_t s);
+
+}  // namespace kg
+
+// Host-side context (InferenceBackend state for one device).
+struct kg_ctx {
+    kg_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    std::string dev_name;
+    bool compiled = false;
+    bool micro = false;  // shape has the exact-order micro kernel
+    int64_t n = 0, nh = 0, hd = 0, nkv = 0, kvd = 0, m = 0, V = 0, L = 0, B = 0;
+    int64_t kpl = 0, vpl = 0, ph = 0;
+    int64_t w_count = 0;
+    // device buffers
+    float *pack = nullptr;  // micro pack: weights + tables + predictor
+    int64_t pack_floats = 0;
+    kg::MicroArgs margs{};
+    float *Kf = nullptr, *Vf = nullptr, *norms = nullptr, *util = nullptr;
+    uint8_t *codes = nullptr;
+    float *rot = nullptr, *rot_t = nullptr, *kc = nullptr, *kb = nullptr, *vc = nullptr, *vb = nullptr;
+    int *d_err = nullptr;
+    // host copies of the TurboQuant tables
+    std::vector<float> h_rot, h_kc, h_kb, h_vc, h_vb, h_pred;
+    // staging for host-pointer calls
+    void *stage = nullptr;
+    size_t stage_bytes = 0;
+    std::vector<void *> allocs;
+};

@@ -1,0 +1,478 @@
+// kg_micro.cu — exact-order f32 forward for the reference's micro model family.
+//
+// One thread owns one (sequence, position). All T new positions of a sequence
+// sit in one CTA, so a teacher-forced prefill of every position and every
+// layer is a single launch: per layer, each thread projects its own token,
+// writes K/V (f32, or TurboQuant codes + dequantized cache) to the device
+// arena, the CTA synchronises, and each thread attends over positions
+// 0..pos of its sequence. Weights, rotation tables and the SP-KV predictor
+// (about 20 KB for Config::micro()) are staged in shared memory; every
+// warp reads the same weight element at once (broadcast).
+//
+// Arithmetic follows the reference's x86-64 AVX2 operation order (see
+// kg_exact.cuh), so logits and codes are bit-identical to the CPU path for
+// forward_base / forward_quantized; forward_sp_kv_quant calls libm expf,
+// reproduced to the correctly rounded value.
+//
+// References (katgpt-rs):
+//   forward_base          src/transformer.rs:1821-2200
+//   attention_head        src/transformer.rs:333-389
+//   forward_quantized     src/transformer.rs:4042-4233
+//   forward_sp_kv_quant   src/sp_kv/forward.rs:610-822, attention_head_core :166-245
+//   utility predictor     src/sp_kv/utility_predictor.rs:51-87
+//   TurboQuant store/deq  src/turboquant/kv_cache.rs:156-317
+//   delta routing         src/transformer.rs:1707-1765, 2129-2158
+//   softmax_scaled        crates/katgpt-types/src/math.rs:36-50
+#include "kg_exact.cuh"
+#include "kg_internal.h"
+
+namespace kg {
+namespace {
+
+constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2;
+
+template <int KVD>
+__device__ __forceinline__ uint8_t quantize(float r, const float *bnd, int nb) {
+    int c = 0;
+    for (int j = 0; j < nb; ++j) c += (r >= bnd[j]) ? 1 : 0;  // partition_point on monotone boundaries
+    return (uint8_t)c;
+}
+
+// TurboQuantKVCache::store_* followed by dequantize_*_into for one vector.
+// Writes packed codes (unless norm < 1e-8: indices untouched, as the reference)
+// and the norm; returns the dequantized vector in `deq`.
+template <int KVD>
+__device__ __forceinline__ void tq_roundtrip(const float (&vec)[KVD], const float *rot,
+                                             const float *rot_t, const float *cent,
+                                             const float *bnd, int bits, int pl, uint8_t *codes,
+                                             float *norm_out, float (&deq)[KVD]) {
+    float ss = kgx::sum_sq<KVD>(vec);
+    float norm = sqrtf(ss);
+    *norm_out = norm;
+    if (norm < 1e-8f) {
+#pragma unroll
+        for (int i = 0; i < KVD; ++i) deq[i] = 0.0f;
+        return;
+    }
+    float inv = 1.0f / norm;
+    float xn[KVD];
+#pragma unroll
+    for (int i = 0; i < KVD; ++i) xn[i] = vec[i] * inv;
+    const int nb = (1 << bits) - 1;
+    uint8_t cd[KVD];
+#pragma unroll
+    for (int i = 0; i < KVD; ++i) cd[i] = quantize<KVD>(kgx::dot<KVD>(rot + i * KVD, xn), bnd, nb);
+    // pack (kv_cache.rs:560-632)
+    if (bits == 2) {
+#pragma unroll
+        for (int b = 0; b < (KVD + 3) / 4; ++b) {
+            uint8_t v = 0;
+#pragma unroll
+            for (int s = 0; s < 4; ++s)
+                if (4 * b + s < KVD) v |= (uint8_t)((cd[4 * b + s] & 3) << (2 * s));
+            codes[b] = v;
+        }
+    } else if (bits == 3 || bits == 4) {
+#pragma unroll
+        for (int b = 0; b < (KVD + 1) / 2; ++b) {
+            uint8_t v = cd[2 * b] & 15;
+            if (2 * b + 1 < KVD) v |= (uint8_t)((cd[2 * b + 1] & 15) << 4);
+            codes[b] = v;
+        }
+    } else {
+#pragma unroll
+        for (int b = 0; b < KVD; ++b) codes[b] = cd[b];
+    }
+    (void)pl;
+    // dequantize: centroid lookup, R^T * c, * norm
+    float c[KVD];
+#pragma unroll
+    for (int i = 0; i < KVD; ++i) c[i] = cent[cd[i]];
+#pragma unroll
+    for (int i = 0; i < KVD; ++i) deq[i] = kgx::dot<KVD>(rot_t + i * KVD, c) * norm;
+}
+
+// rmsnorm / rmsnorm_with_gamma(gamma = 1): x * (1 / sqrt(sum_sq/n + 1e-5))
+template <int N>
+__device__ __forceinline__ void rmsnorm(float (&x)[N]) {
+    float ss = kgx::sum_sq<N>(x);
+    float inv = 1.0f / sqrtf(ss / (float)N + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < N; ++i) x[i] = x[i] * inv;
+}
+
+template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE>
+__global__ void __launch_bounds__(128) micro_forward(const MicroArgs p) {
+    constexpr int KVD = NKV * HD;
+    constexpr int PH = (N / 4 > 16) ? N / 4 : 16;
+    extern __shared__ float4 sm4[];
+    float *sm = reinterpret_cast<float *>(sm4);
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(p.pack);
+        for (int e = threadIdx.x; e < p.pack_floats / 4; e += blockDim.x) sm4[e] = src[e];
+    }
+    __syncthreads();
+
+    const int T = p.T;
+    const int SB = blockDim.x / T;
+    const int sl = threadIdx.x / T, tl = threadIdx.x - sl * T;
+    const int i = blockIdx.x * SB + sl;
+    bool active = (sl < SB) && (i < p.n_seq);
+    int slot = 0, pos = 0, tok = 0;
+    if (active) {
+        slot = p.seq_ids[i];
+        pos = (p.start_pos ? p.start_pos[i] : 0) + tl;
+        tok = p.tokens[(int64_t)i * T + tl];
+        if (slot < 0 || slot >= p.n_slots || pos < 0 || pos >= BLK || tok < 0 || tok >= VOC) {
+            atomicExch(p.err, 1);
+            active = false;
+        }
+    }
+    const float *wte = sm + p.off_wte, *wpe = sm + p.off_wpe;
+    float x[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) x[j] = active ? wte[tok * N + j] + wpe[pos * N + j] : 0.0f;
+    float delta[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) delta[j] = 0.0f;
+    const float scale = 1.0f / sqrtf((float)HD);
+
+    for (int l = 0; l < p.L; ++l) {
+        const float *wl = sm + p.off_layers + l * p.layer_stride;
+        const float *wq = wl, *wk = wq + N * N, *wv = wk + KVD * N, *wo = wv + KVD * N;
+        const float *w1 = wo + N * N, *w2 = w1 + M * N;
+        const int64_t row = ((int64_t)slot * p.L + l) * BLK;  // [slot][layer] base (positions)
+
+        rmsnorm<N>(x);
+        float xr[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) xr[j] = x[j];
+        float util = 0.0f;
+        if constexpr (MODE == MODE_SPKV) {
+            rmsnorm<N>(x);  // double norm (sp_kv/forward.rs:648-651)
+            const float *pw1 = sm + p.off_pw1, *pb1 = sm + p.off_pb1;
+            const float *pw2 = sm + p.off_pw2, *pb2 = sm + p.off_pb2;
+            float hbuf[PH];
+#pragma unroll
+            for (int h = 0; h < PH; ++h) {
+                float v = kgx::dot<N>(pw1 + h * N, x) + pb1[h];
+                hbuf[h] = v * (1.0f / (1.0f + kgx::expf_libm(-v)));  // silu
+            }
+#pragma unroll
+            for (int kh = 0; kh < NKV; ++kh) {
+                float u = 1.0f / (1.0f + kgx::expf_libm(-(kgx::dot<PH>(pw2 + kh * PH, hbuf) + pb2[kh])));
+                util = kh == 0 ? u : kgx::fmax_rs(util, u);
+            }
+        }
+        float q[N], k[KVD], v[KVD];
+#pragma unroll
+        for (int r = 0; r < N; ++r) q[r] = kgx::dot<N>(wq + r * N, x);
+#pragma unroll
+        for (int r = 0; r < KVD; ++r) k[r] = kgx::dot<N>(wk + r * N, x);
+#pragma unroll
+        for (int r = 0; r < KVD; ++r) v[r] = kgx::dot<N>(wv + r * N, x);
+
+        if (active) {
+            float *kd = p.Kf + (row + pos) * KVD, *vd = p.Vf + (row + pos) * KVD;
+            if constexpr (MODE == MODE_BASE) {
+#pragma unroll
+                for (int j = 0; j < KVD; ++j) {
+                    kd[j] = k[j];
+                    vd[j] = v[j];
+                }
+            } else {
+                uint8_t *cb = p.codes + (row + pos) * (p.kpl + p.vpl);
+                float *nb = p.norms + (row + pos) * 2;
+                float dk[KVD], dv[KVD];
+                tq_roundtrip<KVD>(k, sm + p.off_rot, sm + p.off_rot_t, sm + p.off_kc, sm + p.off_kb,
+                                  p.kbits, p.kpl, cb, nb, dk);
+                tq_roundtrip<KVD>(v, sm + p.off_rot, sm + p.off_rot_t, sm + p.off_vc, sm + p.off_vb,
+                                  p.vbits, p.vpl, cb + p.kpl, nb + 1, dv);
+#pragma unroll
+                for (int j = 0; j < KVD; ++j) {
+                    kd[j] = dk[j];
+                    vd[j] = dv[j];
+                }
+                if constexpr (MODE == MODE_SPKV) p.util[row + pos] = util;
+            }
+        }
+        __syncthreads();  // every position of this layer is written
+
+        // ---- attention over positions 0..pos
+        float att[N];
+        const int tn = pos + 1;
+        const float *Kb = p.Kf + row * KVD, *Vb = p.Vf + row * KVD;
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+            const int g = h * NKV / NH;
+            float sc[BLK];
+            if constexpr (MODE != MODE_SPKV) {
+                // attention_head: dot, scale, max, shift, Cephes exp, sum, normalise, P.V
+#pragma unroll
+                for (int t = 0; t < BLK; ++t)
+                    sc[t] = (active && t < tn) ? kgx::dot<HD>(q + h * HD, Kb + t * KVD + g * HD) : 0.0f;
+#pragma unroll
+                for (int t = 0; t < BLK; ++t) sc[t] = sc[t] * scale;
+                float mx = sc[0];
+#pragma unroll
+                for (int t = 1; t < BLK; ++t)
+                    if (t < tn && sc[t] > mx) mx = sc[t];
+#pragma unroll
+                for (int t = 0; t < BLK; ++t) sc[t] = sc[t] + (-mx);
+                const int body = tn / 8 * 8;
+#pragma unroll
+                for (int t = 0; t < BLK; ++t)
+                    sc[t] = t < body ? kgx::cephes_lane(sc[t], true) : kgx::cephes_scalar(sc[t]);
+                float sum = kgx::sum_rt<BLK>(sc, tn);
+                float inv = 1.0f / sum;
+#pragma unroll
+                for (int t = 0; t < BLK; ++t) sc[t] = sc[t] * inv;
+                float o[HD];
+#pragma unroll
+                for (int d = 0; d < HD; ++d) o[d] = 0.0f;
+#pragma unroll
+                for (int t = 0; t < BLK; ++t)
+                    if (active && t < tn) {
+                        const float *vr = Vb + t * KVD + g * HD;
+#pragma unroll
+                        for (int d = 0; d < HD; ++d)  // fused_scale_acc: fma body, mul+add tail
+                            o[d] = (d < HD / 8 * 8) ? fmaf(sc[t], vr[d], o[d]) : o[d] + sc[t] * vr[d];
+                    }
+#pragma unroll
+                for (int d = 0; d < HD; ++d) att[h * HD + d] = o[d];
+            } else {
+                // attention_head_core<GateBias>: bias 0 for every position (each
+                // written position is retained; block_size <= window)
+                float mx = -INFINITY;
+#pragma unroll
+                for (int t = 0; t < BLK; ++t) {
+                    float s = (active && t < tn) ? kgx::dot<HD>(q + h * HD, Kb + t * KVD + g * HD) * scale + 0.0f : 0.0f;
+                    sc[t] = s;
+                    if (t < tn) mx = kgx::fmax_rs(mx, s);
+                }
+                float sum = 0.0f;
+#pragma unroll
+                for (int t = 0; t < BLK; ++t)
+                    if (t < tn) {
+                        float e = kgx::expf_libm(sc[t] - mx);
+                        sc[t] = e;
+                        sum = sum + e;
+                    }
+                float inv = 1.0f / sum;
+#pragma unroll
+                for (int d = 0; d < HD; ++d) {
+                    float o = 0.0f;
+#pragma unroll
+                    for (int t = 0; t < BLK; ++t)
+                        if (active && t < tn) o = o + (sc[t] * inv) * Vb[t * KVD + g * HD + d];
+                    att[h * HD + d] = o;
+                }
+            }
+        }
+
+        // ---- output projection + residual
+        float xo[N];
+#pragma unroll
+        for (int r = 0; r < N; ++r) xo[r] = kgx::dot<N>(wo + r * N, att);
+#pragma unroll
+        for (int j = 0; j < N; ++j) x[j] = xo[j] + xr[j];
+
+        // ---- MLP: xr2 = x; norm; relu(W1 x); TwELL sparse / dense W2; += xr2
+        float xr2[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) xr2[j] = x[j];
+        rmsnorm<N>(x);
+        float hid[M];
+        int alive = 0;
+#pragma unroll
+        for (int r = 0; r < M; ++r) {
+            float s = kgx::dot<N>(w1 + r * N, x);
+            hid[r] = s > 0.0f ? s : 0.0f;
+            alive += hid[r] > 0.0f ? 1 : 0;
+        }
+        if ((float)alive / (float)M > (1.0f - p.sparse_threshold)) {
+#pragma unroll
+            for (int r = 0; r < N; ++r) x[r] = kgx::dot<M>(w2 + r * M, hid);
+        } else {
+            // sparse_matmul: ascending alive list, gathered dot (sparse.rs:22-75,159-218)
+            int aidx[M];
+            float aval[M];
+            int na = 0;
+            for (int c = 0; c < M; ++c)
+                if (hid[c] > 0.0f) {
+                    aidx[na] = c;
+                    aval[na] = hid[c];
+                    ++na;
+                }
+            for (int r = 0; r < N; ++r) {
+                const float *wr = w2 + r * M;
+                float s;
+                if (na <= 4) {
+                    s = 0.0f;
+                    for (int a = 0; a < na; ++a) s = s + wr[aidx[a]] * aval[a];
+                } else {
+                    float acc[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
+                    int a = 0;
+                    for (; a + 8 <= na; a += 8)
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) acc[u] = fmaf(wr[aidx[a + u]], aval[a + u], acc[u]);
+                    s = kgx::hsum8(acc);
+                    for (; a < na; ++a) s = s + wr[aidx[a]] * aval[a];
+                }
+                x[r] = s;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) x[j] = x[j] + xr2[j];
+
+        // ---- delta routing (not in the sp_kv path)
+        if constexpr (MODE != MODE_SPKV) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) delta[j] = delta[j] + (x[j] - xr[j]);
+            if ((l & 3) == 3) {
+                const int b = l >> 2;  // sources: blocks 0..b-1 (already zeroed) and b
+                const float *qw = sm + p.off_dq + l * N, *nw = sm + p.off_dn + l * N;
+                float lg[16];
+                float zero_logit;
+                {
+                    float z[N];
+#pragma unroll
+                    for (int j = 0; j < N; ++j) z[j] = 0.0f;
+                    float rms = sqrtf(kgx::sum_sq<N>(z) / (float)N + 1e-5f);
+                    float inv = 1.0f / rms;
+#pragma unroll
+                    for (int j = 0; j < N; ++j)
+                        z[j] = (j < N / 8 * 8) ? nw[j] * (z[j] * inv) : nw[j] * z[j] * inv;
+                    zero_logit = kgx::dot<N>(z, qw);
+                }
+                float own_logit;
+                {
+                    float sd[N];
+                    float rms = sqrtf(kgx::sum_sq<N>(delta) / (float)N + 1e-5f);
+                    float inv = 1.0f / rms;
+#pragma unroll
+                    for (int j = 0; j < N; ++j)
+                        sd[j] = (j < N / 8 * 8) ? nw[j] * (delta[j] * inv) : nw[j] * delta[j] * inv;
+                    own_logit = kgx::dot<N>(sd, qw);
+                }
+                const int ns = b + 1;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int s = 0; s < 16; ++s) {
+                    lg[s] = s < b ? zero_logit : own_logit;
+                    if (s < ns) mx = kgx::fmax_rs(mx, lg[s]);
+                }
+                const int body = ns / 8 * 8;
+#pragma unroll
+                for (int s = 0; s < 16; ++s) {
+                    float e = lg[s] + (-mx);
+                    lg[s] = s < body ? kgx::cephes_lane(e, true) : kgx::cephes_scalar(e);
+                }
+                float se = kgx::sum_rt<16>(lg, ns);
+                float inv_sum = 1.0f / se;
+#pragma unroll
+                for (int s = 0; s < 16; ++s)
+                    if (s < ns) {
+                        float w = lg[s] * inv_sum;
+#pragma unroll
+                        for (int j = 0; j < N; ++j) {
+                            float src = s < b ? 0.0f : delta[j];
+                            x[j] = (j < N / 8 * 8) ? fmaf(w, src, x[j]) : x[j] + w * src;
+                        }
+                    }
+#pragma unroll
+                for (int j = 0; j < N; ++j) delta[j] = 0.0f;
+            }
+        }
+    }
+
+    // ---- lm_head (+ softmax_scaled)
+    if (!active) return;
+    const float *lm = sm + p.off_lm;
+    float lg[VOC];
+#pragma unroll
+    for (int r = 0; r < VOC; ++r) lg[r] = kgx::dot<N>(lm + r * N, x);
+    const int64_t orow = ((int64_t)i * T + tl) * VOC;
+    if (p.logits) {
+#pragma unroll
+        for (int r = 0; r < VOC; ++r) p.logits[orow + r] = lg[r];
+    }
+    if (p.probs) {
+        float mx = lg[0];
+#pragma unroll
+        for (int r = 1; r < VOC; ++r) mx = lg[r] > mx ? lg[r] : mx;
+#pragma unroll
+        for (int r = 0; r < VOC; ++r) lg[r] = (lg[r] - mx) * p.inv_temp;
+        // simd_exp_sum_inplace: unclamped lanes over 8-chunks, scalar tail
+        constexpr int C4 = VOC / 32, REM = (VOC - C4 * 32) / 8, T0 = C4 * 32 + REM * 8;
+        float acc[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) acc[u] = 0.0f;
+#pragma unroll
+        for (int r = 0; r < C4 * 32; ++r) {
+            lg[r] = kgx::cephes_lane(lg[r], false);
+            acc[r & 31] = acc[r & 31] + lg[r];
+        }
+        float t8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t8[u] = (acc[u] + acc[8 + u]) + (acc[16 + u] + acc[24 + u]);
+        float sum = kgx::hsum8(t8);
+        float rr[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) rr[u] = 0.0f;
+#pragma unroll
+        for (int r = C4 * 32; r < T0; ++r) {
+            lg[r] = kgx::cephes_lane(lg[r], false);
+            rr[(r - C4 * 32) & 7] = rr[(r - C4 * 32) & 7] + lg[r];
+        }
+        sum = sum + kgx::hsum8(rr);
+#pragma unroll
+        for (int r = T0; r < VOC; ++r) {
+            lg[r] = kgx::cephes_scalar(lg[r]);
+            sum = sum + lg[r];
+        }
+        float inv = 1.0f / sum;
+#pragma unroll
+        for (int r = 0; r < VOC; ++r) p.probs[orow + r] = lg[r] * inv;
+    }
+}
+
+template <int MODE>
+cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
+    const int T = a.T;
+    const int SB = 128 / T;
+    const int threads = SB * T;
+    const int blocks = (a.n_seq + SB - 1) / SB;
+    const size_t smem = (size_t)a.pack_floats * sizeof(float);
+    auto kfn = micro_forward<16, 4, 4, 4, 64, 27, 16, MODE>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kfn<<<blocks, threads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int micro_supported(const kg_config &c) {
+    // Instantiated shape: Config::micro() widths (any n_layer).
+    bool ok = c.n_embd == 16 && c.n_head == 4 && c.head_dim == 4 && c.n_kv_head == 4 &&
+              c.mlp_hidden == 64 && c.vocab_size == 27 && c.block_size == 16 &&
+              c.weight_dtype == KG_W_F32 && c.n_layer >= 1 && c.n_layer <= 60;
+    if (c.kv_mode == KG_KV_SPKV_TQ) ok = ok && c.spkv_window >= c.block_size;
+    return ok ? 0 : -1;
+}
+
+cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s) {
+    if (a.n_seq <= 0) return cudaSuccess;
+    if (a.T < 1 || a.T > 16) return cudaErrorInvalidValue;
+    switch (c.kv_mode) {
+        case KG_KV_F32: return launch_mode<MODE_BASE>(a, s);
+        case KG_KV_TQ: return launch_mode<MODE_QUANT>(a, s);
+        case KG_KV_SPKV_TQ: return launch_mode<MODE_SPKV>(a, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace kg

@@ -1,0 +1,229 @@
+// kg_tq.cu — TurboQuant codec kernels in the reference's exact operation order.
+//
+// * Rotation build: modified Gram-Schmidt of the seeded Gaussian matrix
+//   (src/turboquant/rotation.rs:11-52). The reference is left-looking (column i
+//   subtracts its projections on q_0..q_{i-1}, each dot a sequential f32 sum);
+//   this is the right-looking order of the same operations: at step j every
+//   column i > j subtracts its projection on q_j. Column i sees the same
+//   operands in the same sequence, so the result is bit-identical, and the
+//   columns update in parallel (one thread per column).
+// * Encode (store_key / store_value, src/turboquant/kv_cache.rs:156-237):
+//   norm = sqrt(simd_sum_sq), x/norm, R*x with simd_dot_f32 order, boundary
+//   count, pack. A warp computes one dot: lane L owns the chain of elements
+//   k = L (mod 32) (AVX2 accumulator L/8, lane L%8), and the chains are
+//   reduced with shuffles in the fixed ((acc0+acc1)+(acc2+acc3)) +
+//   horizontal_sum_256 tree.
+//
+// Compiled with -fmad=false.
+#include "kg_exact.cuh"
+#include "kg_internal.h"
+
+namespace kg {
+namespace {
+
+// Fixed-order reduction of 32 lane chains (see file header).
+__device__ __forceinline__ float tree32(float a) {
+    float u = a + __shfl_down_sync(0xffffffffu, a, 8);   // acc0+acc1 (lanes 0-7), acc2+acc3 (16-23)
+    float t = u + __shfl_down_sync(0xffffffffu, u, 16);  // (acc0+acc1)+(acc2+acc3), lanes 0-7
+    float s = t + __shfl_down_sync(0xffffffffu, t, 4);   // lo128 + hi128, lanes 0-3
+    float w = s + __shfl_down_sync(0xffffffffu, s, 1);   // v0+v1 (lane 0), v2+v3 (lane 2)
+    float r = w + __shfl_down_sync(0xffffffffu, w, 2);   // (v0+v1)+(v2+v3), lane 0
+    return __shfl_sync(0xffffffffu, r, 0);
+}
+// hsum8 of lanes 0..7 (an 8-lane accumulator), result broadcast.
+__device__ __forceinline__ float tree8(float a) {
+    float s = a + __shfl_down_sync(0xffffffffu, a, 4);
+    float w = s + __shfl_down_sync(0xffffffffu, s, 1);
+    float r = w + __shfl_down_sync(0xffffffffu, w, 2);
+    return __shfl_sync(0xffffffffu, r, 0);
+}
+
+// simd_sum_sq over x[0..len) by one warp (result in every lane).
+__device__ float warp_sum_sq(const float *x, int len, int stride) {
+    const int lane = threadIdx.x & 31;
+    const int c2 = len / 16;
+    float acc = 0.0f;
+    if (lane < 16)
+        for (int c = 0; c < c2; ++c) {
+            float v = x[(int64_t)(16 * c + lane) * stride];
+            acc = fmaf(v, v, acc);
+        }
+    // t[l] = a0[l] + a1[l] = chain l + chain l+8, then hsum8
+    float t = acc + __shfl_down_sync(0xffffffffu, acc, 8);
+    float sum = tree8(t);
+    const int rem = (len - c2 * 16) / 8;
+    float r = 0.0f;
+    if (lane < 8 && rem > 0) {
+        float v = x[(int64_t)(c2 * 16 + lane) * stride];
+        r = fmaf(v, v, r);
+    }
+    sum = sum + tree8(r);
+    for (int i = c2 * 16 + rem * 8; i < len; ++i) {
+        float v = x[(int64_t)i * stride];
+        sum = sum + v * v;
+    }
+    return sum;
+}
+
+// simd_dot_f32(a, b, len) by one warp (result in every lane).
+__device__ __forceinline__ float warp_dot(const float *a, const float *b, int len) {
+    const int lane = threadIdx.x & 31;
+    const int c4 = len / 32;
+    float acc = 0.0f;
+    for (int c = 0; c < c4; ++c) acc = fmaf(a[32 * c + lane], b[32 * c + lane], acc);
+    float sum = tree32(acc);
+    const int rem = (len - c4 * 32) / 8;
+    float r = 0.0f;
+    if (lane < 8)
+        for (int c = 0; c < rem; ++c) r = fmaf(a[c4 * 32 + 8 * c + lane], b[c4 * 32 + 8 * c + lane], r);
+    sum = sum + tree8(r);
+    for (int i = c4 * 32 + rem * 8; i < len; ++i) sum = sum + a[i] * b[i];
+    return sum;
+}
+
+// One MGS step j. V is row-major (V[k*dim + i] = row k of column i) so that
+// the per-column threads read coalesced rows.
+__global__ void mgs_step(int dim, int j, float *V, float *Q) {
+    extern __shared__ float qj[];
+    __shared__ float s_norm;
+    if (threadIdx.x < 32) {
+        float ss = warp_sum_sq(V + j, dim, dim);
+        if (threadIdx.x == 0) s_norm = sqrtf(ss);
+    }
+    __syncthreads();
+    const float nrm = s_norm;
+    for (int k = threadIdx.x; k < dim; k += blockDim.x) {
+        float qv = nrm > 1e-8f ? V[(int64_t)k * dim + j] / nrm : 0.0f;
+        qj[k] = qv;
+        if (blockIdx.x == 0 && nrm > 1e-8f) Q[(int64_t)k * dim + j] = qv;
+    }
+    __syncthreads();
+    const int i = j + 1 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    float d = -0.0f;  // Iterator::<f32>::sum starts from -0.0
+    for (int k = 0; k < dim; ++k) d = d + qj[k] * V[(int64_t)k * dim + i];
+    for (int k = 0; k < dim; ++k) V[(int64_t)k * dim + i] = V[(int64_t)k * dim + i] - d * qj[k];
+}
+
+__global__ void transpose_sq(int dim, const float *a, float *t) {
+    __shared__ float tile[32][33];
+    int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        int row = by + r, col = bx + threadIdx.x;
+        if (row < dim && col < dim) tile[r][threadIdx.x] = a[(int64_t)row * dim + col];
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        int row = bx + r, col = by + threadIdx.x;
+        if (row < dim && col < dim) t[(int64_t)row * dim + col] = tile[threadIdx.x][r];
+    }
+}
+
+// Encode: one warp per vector, rows in sequence. smem per warp: xn[dim] + codes[dim].
+__global__ void tq_encode_warp(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
+                               const float *bnd, uint8_t *packed, int64_t pstride, float *norms,
+                               int64_t nstride) {
+    extern __shared__ float smf[];
+    const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x & 31;
+    float *xn = smf + (size_t)w * dim;
+    uint8_t *cd = reinterpret_cast<uint8_t *>(smf + (size_t)warps * dim) + (size_t)w * dim;
+    const int nb = (1 << bits) - 1;
+    for (int64_t v = (int64_t)blockIdx.x * warps + w; v < n_vec; v += (int64_t)gridDim.x * warps) {
+        const float *xv = x + v * dim;
+        float norm = sqrtf(warp_sum_sq(xv, dim, 1));
+        if (lane == 0) norms[v * nstride] = norm;
+        if (norm < 1e-8f) continue;  // indices untouched (reference quirk)
+        const float inv = 1.0f / norm;
+        for (int k = lane; k < dim; k += 32) xn[k] = xv[k] * inv;
+        __syncwarp();
+        for (int i = 0; i < dim; ++i) {
+            float r = warp_dot(rot + (int64_t)i * dim, xn, dim);
+            if (lane == 0) {
+                int c = 0;
+                for (int b = 0; b < nb; ++b) c += (r >= bnd[b]) ? 1 : 0;
+                cd[i] = (uint8_t)c;
+            }
+        }
+        __syncwarp();
+        uint8_t *out = packed + v * pstride;
+        if (bits == 2) {
+            for (int b = lane; b < (dim + 3) / 4; b += 32) {
+                uint8_t o = 0;
+                for (int s = 0; s < 4; ++s)
+                    if (4 * b + s < dim) o |= (uint8_t)((cd[4 * b + s] & 3) << (2 * s));
+                out[b] = o;
+            }
+        } else if (bits == 3 || bits == 4) {
+            for (int b = lane; b < (dim + 1) / 2; b += 32) {
+                uint8_t o = cd[2 * b] & 15;
+                if (2 * b + 1 < dim) o |= (uint8_t)((cd[2 * b + 1] & 15) << 4);
+                out[b] = o;
+            }
+        } else if (bits == 8) {
+            for (int b = lane; b < dim; b += 32) out[b] = cd[b];
+        } else {
+            if (lane == 0) {
+                const int pl = (dim * bits + 7) / 8;
+                for (int b = 0; b < pl; ++b) out[b] = 0;
+                int64_t bp = 0;
+                for (int i = 0; i < dim; ++i, bp += bits) {
+                    int byte = (int)(bp / 8), sh = (int)(bp % 8);
+                    out[byte] |= (uint8_t)(cd[i] << sh);
+                    if (sh + bits > 8) out[byte + 1] |= (uint8_t)(cd[i] >> (8 - sh));
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace
+
+cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t, float *work,
+                               cudaStream_t s) {
+    // V (row-major, V[k*dim+i] = column i) is the Gaussian matrix itself:
+    // the reference fills column vectors v_col[row] = mat[row][col].
+    cudaError_t e = cudaMemcpyAsync(work, g, (size_t)dim * dim * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(rot, 0, (size_t)dim * dim * sizeof(float), s);
+    if (e != cudaSuccess) return e;
+    const int threads = 128;
+    const size_t smem = (size_t)dim * sizeof(float);
+    if (smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(mgs_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    for (int j = 0; j < dim; ++j) {
+        int cols = dim - j - 1;
+        int blocks = cols > 0 ? (cols + threads - 1) / threads : 1;
+        mgs_step<<<blocks, threads, smem, s>>>(dim, j, work, rot);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 tb(32, 8), gb((dim + 31) / 32, (dim + 31) / 32);
+    transpose_sq<<<gb, tb, 0, s>>>(dim, rot, rot_t);
+    return cudaGetLastError();
+}
+
+cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
+                             const float *bnd, uint8_t *packed, int64_t pstride, float *norms,
+                             int64_t nstride, cudaStream_t s) {
+    if (n_vec <= 0) return cudaSuccess;
+    int warps = 4;
+    size_t smem = (size_t)warps * dim * (sizeof(float) + 1);
+    while (smem > 200 * 1024 && warps > 1) {
+        warps /= 2;
+        smem = (size_t)warps * dim * (sizeof(float) + 1);
+    }
+    cudaError_t e = cudaFuncSetAttribute(tq_encode_warp, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    int64_t blocks = (n_vec + warps - 1) / warps;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    tq_encode_warp<<<(unsigned)blocks, warps * 32, smem, s>>>(dim, bits, n_vec, x, rot, bnd, packed,
+                                                             pstride, norms, nstride);
+    return cudaGetLastError();
+}
+
+}  // namespace kg

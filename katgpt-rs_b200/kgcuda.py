@@ -1,0 +1,227 @@
+"""ctypes host mirror of the reference `InferenceBackend` seam over libkgcuda.
+
+`CudaBackend` follows the trait in src/inference_backend.rs:45-92 of
+katgpt-rs (forward / device_name / supports_stateful / reset / compile /
+is_compiled / recompile_hint) and adds the batched prefill/decode extension.
+Every call goes through the C ABI declared in include/kg_abi.h; there is no
+CPU fallback — if the shared library or a GPU is missing, construction fails.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBPATH = os.path.join(HERE, "lib", "libkgcuda.so")
+
+KG_KV_F32, KG_KV_TQ, KG_KV_SPKV_TQ = 0, 1, 2
+KG_W_F32, KG_W_BF16 = 0, 1
+
+STATUS = {0: "ok", -1: "invalid argument", -2: "device out of memory", -3: "CUDA error",
+          -4: "timeout", -5: "weights not uploaded", -6: "unsupported configuration",
+          -7: "invalid weights"}
+
+
+class KgConfig(ctypes.Structure):
+    """Mirror of kg_config (include/kg_abi.h)."""
+    _fields_ = [
+        ("vocab_size", ctypes.c_int32), ("block_size", ctypes.c_int32),
+        ("n_embd", ctypes.c_int32), ("n_head", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("n_kv_head", ctypes.c_int32),
+        ("mlp_hidden", ctypes.c_int32), ("n_layer", ctypes.c_int32),
+        ("bos_token", ctypes.c_int32), ("temperature", ctypes.c_float),
+        ("sparse_threshold", ctypes.c_float), ("kv_mode", ctypes.c_int32),
+        ("key_bits", ctypes.c_int32), ("val_bits", ctypes.c_int32),
+        ("weight_dtype", ctypes.c_int32), ("max_seqs", ctypes.c_int32),
+        ("spkv_window", ctypes.c_int32), ("spkv_threshold", ctypes.c_float),
+        ("spkv_init_bias", ctypes.c_float), ("tq_seed", ctypes.c_uint64),
+    ]
+
+    def kvd(self):
+        return self.n_kv_head * self.head_dim
+
+
+class KgError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load libkgcuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIBPATH):
+            raise OSError(f"{LIBPATH} not built (run katgpt-rs_b200/build.py)")
+        L = ctypes.CDLL(LIBPATH)
+        P, I32, I64, F32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+        cfgp = ctypes.POINTER(KgConfig)
+        sig = {
+            "kg_config_micro": (None, [cfgp]),
+            "kg_ctx_create": (ctypes.c_int, [cfgp, ctypes.c_int, ctypes.POINTER(P)]),
+            "kg_ctx_destroy": (None, [P]),
+            "kg_last_error": (ctypes.c_char_p, [P]),
+            "kg_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+            "kg_device_name": (ctypes.c_char_p, [P]),
+            "kg_weights_count": (I64, [cfgp]),
+            "kg_reference_weights": (ctypes.c_int, [cfgp, ctypes.c_uint64, ctypes.c_int, F32, P]),
+            "kg_upload_weights": (ctypes.c_int, [P, P, I64]),
+            "kg_upload_weights_dev": (ctypes.c_int, [P, P, I64]),
+            "kg_is_compiled": (ctypes.c_int, [P]),
+            "kg_seq_reset": (ctypes.c_int, [P, I32]),
+            "kg_seq_reset_all": (ctypes.c_int, [P]),
+            "kg_forward_token": (ctypes.c_int, [P, I32, I32, I32, P]),
+            "kg_forward_batch": (ctypes.c_int, [P, I32, P, P, P, I32, P, P]),
+            "kg_forward_batch_dev": (ctypes.c_int, [P, I32, P, P, P, I32, P, P, P]),
+            "kg_tq_packed_len": (I64, [I64, I32]),
+            "kg_tq_tables": (ctypes.c_int, [P, P, P, P, P, P]),
+            "kg_tq_encode": (ctypes.c_int, [P, I32, I64, P, P, P]),
+            "kg_kv_codes": (ctypes.c_int, [P, I32, I32, I32, P, P, P]),
+            "kg_spkv_utility": (ctypes.c_int, [P, I32, I32, I32, P]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols():
+    """Names of every kg_* function the header declares (for ABI checks)."""
+    lib()
+    return sorted(n for n in dir(_lib) if n.startswith("kg_"))
+
+
+def micro_config(**kw):
+    c = KgConfig()
+    lib().kg_config_micro(ctypes.byref(c))
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def _ptr(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def reference_weights(cfg, seed=42, scale_mode=0, std=0.02):
+    """TransformerWeights::new(config, Rng::new(seed)) in the flat layout."""
+    n = lib().kg_weights_count(ctypes.byref(cfg))
+    w = np.empty(n, np.float32)
+    rc = lib().kg_reference_weights(ctypes.byref(cfg), seed, scale_mode, std, _ptr(w))
+    if rc:
+        raise KgError(rc, "kg_reference_weights")
+    return w
+
+
+class CudaBackend:
+    """InferenceBackend for one B200, backed by libkgcuda (one context)."""
+
+    def __init__(self, cfg, device=0):
+        self.cfg = cfg
+        self._h = ctypes.c_void_p()
+        rc = lib().kg_ctx_create(ctypes.byref(cfg), device, ctypes.byref(self._h))
+        if rc:
+            raise KgError(rc, "kg_ctx_create")
+
+    def close(self):
+        if self._h:
+            lib().kg_ctx_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc):
+        if rc:
+            raise KgError(rc, lib().kg_last_error(self._h).decode())
+
+    # ---- trait methods
+    def device_name(self):
+        return lib().kg_device_name(self._h).decode()
+
+    def supports_stateful(self):
+        return True  # the KV cache lives on the device
+
+    def compile(self, weights):
+        w = np.ascontiguousarray(weights, dtype=np.float32)
+        self._check(lib().kg_upload_weights(self._h, _ptr(w), w.size))
+
+    def is_compiled(self):
+        return bool(lib().kg_is_compiled(self._h))
+
+    def recompile_hint(self):
+        pass  # weights are re-uploaded explicitly with compile()
+
+    def reset(self, seq=None):
+        if seq is None:
+            self._check(lib().kg_seq_reset_all(self._h))
+        else:
+            self._check(lib().kg_seq_reset(self._h, seq))
+
+    def forward(self, token, pos, seq=0):
+        out = np.empty(self.cfg.vocab_size, np.float32)
+        self._check(lib().kg_forward_token(self._h, seq, token, pos, _ptr(out)))
+        return out
+
+    # ---- batched extension
+    def forward_batch(self, tokens, seq_ids=None, start_pos=None, probs=False, logits=True):
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        if tokens.ndim == 1:
+            tokens = tokens[:, None]
+        n_seq, T = tokens.shape
+        ids = np.arange(n_seq, dtype=np.int32) if seq_ids is None else np.ascontiguousarray(seq_ids, np.int32)
+        sp = None if start_pos is None else np.ascontiguousarray(start_pos, np.int32)
+        V = self.cfg.vocab_size
+        lo = np.empty((n_seq, T, V), np.float32) if logits else None
+        pr = np.empty((n_seq, T, V), np.float32) if probs else None
+        self._check(lib().kg_forward_batch(self._h, n_seq, _ptr(ids), _ptr(tokens), _ptr(sp), T,
+                                           _ptr(lo), _ptr(pr)))
+        if probs and logits:
+            return lo, pr
+        return lo if logits else pr
+
+    def forward_batch_dev(self, n_seq, T, ids_ptr, tok_ptr, pos_ptr, logits_ptr, probs_ptr, stream_ptr):
+        """Device-pointer form (integers are raw device addresses)."""
+        self._check(lib().kg_forward_batch_dev(self._h, n_seq, ids_ptr, tok_ptr, pos_ptr, T,
+                                               logits_ptr, probs_ptr, stream_ptr))
+
+    # ---- codec access
+    def tq_tables(self):
+        kvd = self.cfg.kvd()
+        rot = np.empty(kvd * kvd, np.float32)
+        nk, nv = 1 << self.cfg.key_bits, 1 << self.cfg.val_bits
+        kc, kb = np.empty(nk, np.float32), np.empty(nk - 1, np.float32)
+        vc, vb = np.empty(nv, np.float32), np.empty(nv - 1, np.float32)
+        self._check(lib().kg_tq_tables(self._h, _ptr(rot), _ptr(kc), _ptr(kb), _ptr(vc), _ptr(vb)))
+        return rot.reshape(kvd, kvd), kc, kb, vc, vb
+
+    def tq_encode(self, x, which=0, packed_init=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n_vec = x.shape[0]
+        bits = self.cfg.key_bits if which == 0 else self.cfg.val_bits
+        pl = lib().kg_tq_packed_len(self.cfg.kvd(), bits)
+        packed = np.zeros((n_vec, pl), np.uint8) if packed_init is None else np.array(packed_init, np.uint8)
+        norms = np.empty(n_vec, np.float32)
+        self._check(lib().kg_tq_encode(self._h, which, n_vec, _ptr(x), _ptr(packed), _ptr(norms)))
+        return packed, norms
+
+    def kv_codes(self, seq, layer, pos):
+        kvd = self.cfg.kvd()
+        kp = np.empty(lib().kg_tq_packed_len(kvd, self.cfg.key_bits), np.uint8)
+        vp = np.empty(lib().kg_tq_packed_len(kvd, self.cfg.val_bits), np.uint8)
+        nr = np.empty(2, np.float32)
+        self._check(lib().kg_kv_codes(self._h, seq, layer, pos, _ptr(kp), _ptr(vp), _ptr(nr)))
+        return kp, vp, nr
+
+    def spkv_utility(self, seq, layer, pos):
+        u = np.empty(1, np.float32)
+        self._check(lib().kg_spkv_utility(self._h, seq, layer, pos, _ptr(u)))
+        return float(u[0])

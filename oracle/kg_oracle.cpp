@@ -1,0 +1,1217 @@
+// kg_oracle.cpp — CPU oracle (test infrastructure only; see kg_oracle.h).
+//
+// Restates the reference's x86-64 AVX2 path operation for operation. Build with
+// -O2 -mavx2 -mfma -ffp-contract=off and WITHOUT -ffast-math: Rust never
+// contracts a*b+c, so FMAs appear only where the reference uses an FMA
+// intrinsic. libm calls (logf, cosf, powf, expf, log, exp, sin) are the glibc
+// ones that Rust's f32/f64 methods lower to on x86-64 Linux.
+//
+// Every function cites the reference file:line it follows (paths relative to
+// the katgpt-rs repository root).
+
+#include "kg_oracle.h"
+
+#include <immintrin.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+namespace {
+
+// ------------------------------------------------------------------------
+// Rng — crates/katgpt-types/src/rng.rs:26-72
+// ------------------------------------------------------------------------
+struct Rng {
+    uint64_t state;
+    explicit Rng(uint64_t seed) {
+        // SplitMix64 finaliser (rng.rs:26-38)
+        uint64_t z = seed + 0x9E3779B97F4A7C15ULL;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+        uint64_t s = z ^ (z >> 31);
+        state = s == 0 ? 1 : s;
+    }
+    uint64_t next() {  // rng.rs:42-47
+        state ^= state << 13;
+        state ^= state >> 7;
+        state ^= state << 17;
+        return state;
+    }
+    float uniform() {  // rng.rs:56-62
+        uint32_t bits = ((uint32_t)(next() >> 40) & 0x007fffffu) | 0x3f800000u;
+        float f;
+        std::memcpy(&f, &bits, 4);
+        return f - 1.0f;
+    }
+    float normal() {  // rng.rs:66-71 (Box-Muller, glibc logf/cosf)
+        float u1 = uniform();
+        if (!(u1 > 1e-10f)) u1 = 1e-10f;  // f32::max(u1, 1e-10)
+        float u2 = uniform();
+        const float two_pi = 2.0f * 3.14159265358979323846f;   // 2.0 * PI (exact doubling)
+        return sqrtf(-2.0f * logf(u1)) * cosf(two_pi * u2);
+    }
+};
+
+// ------------------------------------------------------------------------
+// Horizontal reducers — crates/katgpt-types/src/simd/horizontal.rs:10-51
+// ------------------------------------------------------------------------
+static inline float hsum128(__m128 v) {
+    __m128 sh = _mm_shuffle_ps(v, v, 0xB1);
+    __m128 s = _mm_add_ps(v, sh);
+    __m128 sh2 = _mm_shuffle_ps(s, s, 0x2A);
+    return _mm_cvtss_f32(_mm_add_ss(s, sh2));
+}
+static inline float hsum256(__m256 v) {
+    return hsum128(_mm_add_ps(_mm256_castps256_ps128(v), _mm256_extractf128_ps(v, 1)));
+}
+static inline float hmax256(__m256 v) {
+    __m128 m = _mm_max_ps(_mm256_castps256_ps128(v), _mm256_extractf128_ps(v, 1));
+    __m128 m2 = _mm_max_ps(m, _mm_shuffle_ps(m, m, 0xB1));
+    __m128 m3 = _mm_max_ps(m2, _mm_shuffle_ps(m2, m2, 0x4E));
+    return _mm_cvtss_f32(m3);
+}
+
+// f32::max (IEEE maxNum: NaN operand ignored)
+static inline float fmax_rs(float a, float b) {
+    if (std::isnan(a)) return b;
+    if (std::isnan(b)) return a;
+    return a > b ? a : b;
+}
+
+// ------------------------------------------------------------------------
+// Dot product — simd/dot.rs:157-229 (avx2_dot_f32)
+// ------------------------------------------------------------------------
+static float dot(const float *a, const float *b, int64_t len) {
+    __m256 a0 = _mm256_setzero_ps(), a1 = a0, a2 = a0, a3 = a0;
+    int64_t i = 0;
+    for (int64_t c = 0, n4 = len / 32; c < n4; ++c, i += 32) {
+        a0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), a0);
+        a1 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 8), _mm256_loadu_ps(b + i + 8), a1);
+        a2 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 16), _mm256_loadu_ps(b + i + 16), a2);
+        a3 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 24), _mm256_loadu_ps(b + i + 24), a3);
+    }
+    float sum = hsum256(_mm256_add_ps(_mm256_add_ps(a0, a1), _mm256_add_ps(a2, a3)));
+    __m256 acc = _mm256_setzero_ps();
+    for (int64_t c = 0, r = (len - i) / 8; c < r; ++c, i += 8)
+        acc = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), acc);
+    sum += hsum256(acc);
+    for (; i < len; ++i) sum += a[i] * b[i];
+    return sum;
+}
+
+// simd/research.rs:298-338 (avx2_sum_sq)
+static float sum_sq(const float *x, int64_t len) {
+    __m256 a0 = _mm256_setzero_ps(), a1 = a0;
+    int64_t i = 0;
+    for (int64_t c = 0, n2 = len / 16; c < n2; ++c, i += 16) {
+        __m256 v0 = _mm256_loadu_ps(x + i);
+        a0 = _mm256_fmadd_ps(v0, v0, a0);
+        __m256 v1 = _mm256_loadu_ps(x + i + 8);
+        a1 = _mm256_fmadd_ps(v1, v1, a1);
+    }
+    float sum = hsum256(_mm256_add_ps(a0, a1));
+    __m256 acc = _mm256_setzero_ps();
+    for (int64_t c = 0, r = (len - i) / 8; c < r; ++c, i += 8) {
+        __m256 v = _mm256_loadu_ps(x + i);
+        acc = _mm256_fmadd_ps(v, v, acc);
+    }
+    sum += hsum256(acc);
+    for (; i < len; ++i) sum += x[i] * x[i];
+    return sum;
+}
+
+// simd/elementwise.rs:1004-1050 (avx2_sum_f32)
+static float sum_f32(const float *x, int64_t len) {
+    __m256 a0 = _mm256_setzero_ps(), a1 = a0, a2 = a0, a3 = a0;
+    int64_t i = 0;
+    for (int64_t c = 0, n4 = len / 32; c < n4; ++c, i += 32) {
+        a0 = _mm256_add_ps(a0, _mm256_loadu_ps(x + i));
+        a1 = _mm256_add_ps(a1, _mm256_loadu_ps(x + i + 8));
+        a2 = _mm256_add_ps(a2, _mm256_loadu_ps(x + i + 16));
+        a3 = _mm256_add_ps(a3, _mm256_loadu_ps(x + i + 24));
+    }
+    float sum = hsum256(_mm256_add_ps(_mm256_add_ps(a0, a1), _mm256_add_ps(a2, a3)));
+    __m256 acc = _mm256_setzero_ps();
+    for (int64_t c = 0, r = (len - i) / 8; c < r; ++c, i += 8)
+        acc = _mm256_add_ps(acc, _mm256_loadu_ps(x + i));
+    sum += hsum256(acc);
+    for (; i < len; ++i) sum += x[i];
+    return sum;
+}
+
+// simd/elementwise.rs:348-380, 1163-1215 (simd_max_f32 / avx2_max_f32)
+static float max_f32(const float *x, int64_t len) {
+    if (len == 0) return -INFINITY;
+    if (len < 8) {
+        float m = x[0];
+        for (int64_t j = 1; j < len; ++j)
+            if (x[j] > m) m = x[j];
+        return m;
+    }
+    __m256 v0 = _mm256_loadu_ps(x), v1 = v0, v2 = v0, v3 = v0;
+    int64_t i = 0;
+    for (int64_t c = 0, n4 = len / 32; c < n4; ++c, i += 32) {
+        v0 = _mm256_max_ps(v0, _mm256_loadu_ps(x + i));
+        v1 = _mm256_max_ps(v1, _mm256_loadu_ps(x + i + 8));
+        v2 = _mm256_max_ps(v2, _mm256_loadu_ps(x + i + 16));
+        v3 = _mm256_max_ps(v3, _mm256_loadu_ps(x + i + 24));
+    }
+    __m256 v = _mm256_max_ps(_mm256_max_ps(v0, v1), _mm256_max_ps(v2, v3));
+    for (; i + 8 <= len; i += 8) v = _mm256_max_ps(v, _mm256_loadu_ps(x + i));
+    float m = hmax256(v);
+    for (; i < len; ++i)
+        if (x[i] > m) m = x[i];
+    return m;
+}
+
+// Elementwise kernels — simd/elementwise.rs (AVX2 bodies are one lane-wise op;
+// tails restate the scalar expression as written).
+static void scale_inplace(float *x, int64_t len, float s) {  // :88-113
+    for (int64_t i = 0; i < len; ++i) x[i] *= s;
+}
+static void add_scalar_inplace(float *x, int64_t len, float v) {  // :945-965
+    for (int64_t i = 0; i < len; ++i) x[i] += v;
+}
+static void fused_sub_scale_inplace(float *x, int64_t len, float sub, float s) {  // :967-1000
+    for (int64_t i = 0; i < len; ++i) x[i] = (x[i] - sub) * s;
+}
+static void add_into(float *d, const float *a, const float *b, int64_t len) {  // :1141-1160
+    for (int64_t i = 0; i < len; ++i) d[i] = a[i] + b[i];
+}
+static void add_inplace(float *d, const float *s, int64_t len) {  // :923-943
+    for (int64_t i = 0; i < len; ++i) d[i] += s[i];
+}
+static void scale_mul_inplace(float *x, const float *g, int64_t len, float s) {  // :1249-1270
+    int64_t body = len / 8 * 8;
+    for (int64_t i = 0; i < body; ++i) x[i] = g[i] * (x[i] * s);   // vector: g*(x*s)
+    for (int64_t i = body; i < len; ++i) x[i] = g[i] * x[i] * s;   // tail: (g*x)*s
+}
+// simd/research.rs:1054-1075 (avx2_fused_scale_acc): dst += s*src
+static void fused_scale_acc(float *d, const float *src, float s, int64_t len) {
+    int64_t body = len / 8 * 8;
+    for (int64_t i = 0; i < body; ++i) d[i] = fmaf(s, src[i], d[i]);
+    for (int64_t i = body; i < len; ++i) d[i] += s * src[i];
+}
+// simd/research.rs:967-990 (avx2_fused_sub_acc): dst += a - b
+static void fused_sub_acc(float *d, const float *a, const float *b, int64_t len) {
+    for (int64_t i = 0; i < len; ++i) d[i] += a[i] - b[i];
+}
+
+// ------------------------------------------------------------------------
+// Cephes exp — simd/activations.rs:18-20, 189-221, 405-480, 660-748
+// ------------------------------------------------------------------------
+static const float kLn2Hi = 6.9314575e-1f;
+static const float kLn2Lo = 1.4286068e-6f;
+static const float kInvLn2 = 1.44269504088896340736f;  // std::f32::consts::LOG2_E
+
+static inline float f32_from_bits(uint32_t b) {
+    float f;
+    std::memcpy(&f, &b, 4);
+    return f;
+}
+// Rust `f as i32`: saturating, NaN -> 0
+static inline int32_t sat_i32(float f) {
+    if (std::isnan(f)) return 0;
+    if (f >= 2147483648.0f) return INT32_MAX;
+    if (f <= -2147483648.0f) return INT32_MIN;
+    return (int32_t)f;
+}
+static inline float cephes_poly(float g) {
+    const float one = 1.0f;
+    float p6 = one + g * (1.0f / 6.0f);
+    float p5 = one + (g * 0.2f) * p6;
+    float p4 = one + (g * 0.25f) * p5;
+    float p3 = one + (g * (1.0f / 3.0f)) * p4;
+    float p2 = one + (g * 0.5f) * p3;
+    return one + g * p2;
+}
+// activations.rs:189-221 (scalar tail: round half away from zero, early exits)
+static float cephes_exp_scalar(float x) {
+    int32_t n = sat_i32(roundf(x * kInvLn2));
+    if (n < -126) return 0.0f;
+    if (n > 127) return INFINITY;
+    float nf = (float)n;
+    float g = (x - nf * kLn2Hi) - nf * kLn2Lo;
+    float q = cephes_poly(g);
+    return f32_from_bits((uint32_t)(n + 127) << 23) * q;
+}
+// One AVX2 lane of avx2_exp_inplace (clamped) / avx2_exp_sum_inplace (unclamped).
+static inline float cephes_exp_lane(float x, bool clamp) {
+    float nf = nearbyintf(x * kInvLn2);  // _mm256_round_ps(.., nearest-even)
+    // _mm256_cvtps_epi32 of an integral value: exact; out-of-range/NaN -> INT_MIN
+    int32_t ni = (std::isnan(nf) || nf >= 2147483648.0f || nf < -2147483648.0f) ? INT32_MIN
+                                                                                : (int32_t)nf;
+    float g = (x - nf * kLn2Hi) - nf * kLn2Lo;
+    float q = cephes_poly(g);
+    int32_t e = ni;
+    if (clamp) e = std::max(std::min(e, 127), -126);
+    uint32_t bits = (uint32_t)((uint32_t)e + 127u) << 23;  // wrapping add, then shift
+    return f32_from_bits(bits) * q;
+}
+static void exp_inplace(float *x, int64_t len) {  // activations.rs:405-480
+    int64_t body = len / 8 * 8;
+    for (int64_t i = 0; i < body; ++i) x[i] = cephes_exp_lane(x[i], true);
+    for (int64_t i = body; i < len; ++i) x[i] = cephes_exp_scalar(x[i]);
+}
+static float exp_sum_inplace(float *x, int64_t len) {  // activations.rs:660-748
+    float acc[4][8] = {};
+    int64_t i = 0;
+    for (int64_t c = 0, n4 = len / 32; c < n4; ++c, i += 32)
+        for (int j = 0; j < 4; ++j)
+            for (int l = 0; l < 8; ++l) {
+                float r = cephes_exp_lane(x[i + 8 * j + l], false);
+                x[i + 8 * j + l] = r;
+                acc[j][l] = acc[j][l] + r;
+            }
+    __m256 A0 = _mm256_loadu_ps(acc[0]), A1 = _mm256_loadu_ps(acc[1]);
+    __m256 A2 = _mm256_loadu_ps(acc[2]), A3 = _mm256_loadu_ps(acc[3]);
+    float sum = hsum256(_mm256_add_ps(_mm256_add_ps(A0, A1), _mm256_add_ps(A2, A3)));
+    float rem[8] = {};
+    for (int64_t c = 0, r = (len - i) / 8; c < r; ++c, i += 8)
+        for (int l = 0; l < 8; ++l) {
+            float e = cephes_exp_lane(x[i + l], false);
+            x[i + l] = e;
+            rem[l] = rem[l] + e;
+        }
+    sum += hsum256(_mm256_loadu_ps(rem));
+    for (; i < len; ++i) {
+        float e = cephes_exp_scalar(x[i]);
+        x[i] = e;
+        sum += e;
+    }
+    return sum;
+}
+
+// ------------------------------------------------------------------------
+// Sparse dot — simd/sparse.rs:22-75, 159-218
+// ------------------------------------------------------------------------
+static float sparse_dot(const float *w, const int64_t *idx, const float *val, int64_t alive) {
+    if (alive <= 4) {
+        float s = 0.0f;
+        for (int64_t i = 0; i < alive; ++i) s += w[idx[i]] * val[i];
+        return s;
+    }
+    __m256 acc = _mm256_setzero_ps();
+    int64_t i = 0;
+    for (int64_t c = 0, n = alive / 8; c < n; ++c, i += 8) {
+        __m256i vi = _mm256_set_epi32((int)idx[i + 7], (int)idx[i + 6], (int)idx[i + 5],
+                                      (int)idx[i + 4], (int)idx[i + 3], (int)idx[i + 2],
+                                      (int)idx[i + 1], (int)idx[i]);
+        __m256 ww = _mm256_i32gather_ps(w, vi, 4);
+        acc = _mm256_fmadd_ps(ww, _mm256_loadu_ps(val + i), acc);
+    }
+    float s = hsum256(acc);
+    for (; i < alive; ++i) s += w[idx[i]] * val[i];
+    return s;
+}
+
+// ------------------------------------------------------------------------
+// Math — crates/katgpt-types/src/math.rs
+// ------------------------------------------------------------------------
+static void matmul(float *out, const float *w, const float *x, int64_t rows, int64_t cols) {
+    for (int64_t r = 0; r < rows; ++r) out[r] = dot(w + r * cols, x, cols);  // math.rs:238-240
+}
+static void matmul_relu(float *out, const float *w, const float *x, int64_t rows, int64_t cols) {
+    for (int64_t r = 0; r < rows; ++r) {  // dot.rs:699-713
+        float s = dot(w + r * cols, x, cols);
+        out[r] = s > 0.0f ? s : 0.0f;
+    }
+}
+static void rmsnorm(float *x, int64_t n) {  // math.rs:56-69
+    float ss = sum_sq(x, n);
+    float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
+    scale_inplace(x, n, inv);
+}
+static void rmsnorm_gamma(float *x, const float *g, int64_t n) {  // math.rs:218-233
+    float ss = sum_sq(x, n);
+    float inv = 1.0f / sqrtf(ss / (float)n + (float)1e-5);
+    scale_mul_inplace(x, g, n, inv);
+}
+// math.rs:315-355 + dot.rs/sparse.rs:300-316: returns alive count
+static int64_t sparse_matmul(float *out, const float *w, const float *in, int64_t rows,
+                             int64_t cols, int64_t *aidx, float *aval) {
+    int64_t alive = 0;
+    for (int64_t c = 0; c < cols; ++c)
+        if (in[c] > 0.0f) {
+            aidx[alive] = c;
+            aval[alive] = in[c];
+            ++alive;
+        }
+    for (int64_t r = 0; r < rows; ++r) out[r] = sparse_dot(w + r * cols, aidx, aval, alive);
+    return alive;
+}
+// math.rs:36-50
+static void softmax_scaled(float *x, int64_t len, float inv_temp) {
+    if (len == 0) return;
+    float m = max_f32(x, len);
+    fused_sub_scale_inplace(x, len, m, inv_temp);
+    float s = exp_sum_inplace(x, len);
+    scale_inplace(x, len, 1.0f / s);
+}
+
+// ------------------------------------------------------------------------
+// Model
+// ------------------------------------------------------------------------
+struct Dims {
+    int64_t V, B, n, nh, hd, nkv, kvd, m, L, nblocks;
+};
+static Dims dims_of(const or_config *c) {
+    Dims d;
+    d.V = c->vocab_size;
+    d.B = c->block_size;
+    d.n = c->n_embd;
+    d.nh = c->n_head;
+    d.hd = c->head_dim;
+    d.nkv = c->n_kv_head;
+    d.kvd = (int64_t)c->n_kv_head * c->head_dim;  // config.rs:1581 kv_dim
+    d.m = c->mlp_hidden;
+    d.L = c->n_layer;
+    d.nblocks = (d.L + 3) / 4;  // delta routing B=4 (transformer.rs:166-170)
+    return d;
+}
+struct LayerW {
+    const float *wq, *wk, *wv, *wo, *w1, *w2;
+};
+struct Weights {
+    const float *wte, *wpe, *lm_head, *dq, *dn;
+    std::vector<LayerW> layers;
+};
+static int64_t weights_count(const Dims &d) {
+    int64_t per_layer = 2 * d.n * d.n + 2 * d.kvd * d.n + 2 * d.m * d.n;
+    return d.V * d.n + d.B * d.n + d.L * per_layer + d.V * d.n + 2 * d.L * d.n;
+}
+static Weights view_weights(const Dims &d, const float *w) {
+    Weights W;
+    const float *p = w;
+    W.wte = p; p += d.V * d.n;
+    W.wpe = p; p += d.B * d.n;
+    for (int64_t l = 0; l < d.L; ++l) {
+        LayerW lw;
+        lw.wq = p; p += d.n * d.n;
+        lw.wk = p; p += d.kvd * d.n;
+        lw.wv = p; p += d.kvd * d.n;
+        lw.wo = p; p += d.n * d.n;
+        lw.w1 = p; p += d.m * d.n;
+        lw.w2 = p; p += d.n * d.m;
+        W.layers.push_back(lw);
+    }
+    W.lm_head = p; p += d.V * d.n;
+    W.dq = p; p += d.L * d.n;
+    W.dn = p;
+    return W;
+}
+
+// transformer.rs:333-389 (attention_head, Cephes exp, AVX2 helpers)
+static void attention_head(const float *q, const float *K, const float *Vc, float *out,
+                           float *scores, int64_t qoff, int64_t kvoff, int64_t kvd, int64_t hd,
+                           int64_t tn, float scale) {
+    for (int64_t t = 0; t < tn; ++t) scores[t] = dot(q + qoff, K + t * kvd + kvoff, hd);
+    scale_inplace(scores, tn, scale);
+    float mx = max_f32(scores, tn);
+    add_scalar_inplace(scores, tn, -mx);
+    exp_inplace(scores, tn);
+    float sum = sum_f32(scores, tn);
+    float inv = 1.0f / sum;
+    scale_inplace(scores, tn, inv);
+    for (int64_t d = 0; d < hd; ++d) out[qoff + d] = 0.0f;
+    for (int64_t t = 0; t < tn; ++t) fused_scale_acc(out + qoff, Vc + t * kvd + kvoff, scores[t], hd);
+}
+
+// src/sp_kv/forward.rs:166-245 (attention_head_core<GateBias>, libm expf, d-outer PV)
+static void attention_head_gated(const float *q, const float *K, const float *Vc, float *out,
+                                 float *scores, int64_t qoff, int64_t kvoff, int64_t kvd,
+                                 int64_t hd, int64_t tn, float scale, const float *bias) {
+    float mx = -INFINITY;
+    for (int64_t t = 0; t < tn; ++t) {
+        float b = bias[t];
+        if (b == -INFINITY) {
+            scores[t] = -INFINITY;
+            continue;
+        }
+        float s = dot(q + qoff, K + t * kvd + kvoff, hd) * scale + b;
+        scores[t] = s;
+        mx = fmax_rs(mx, s);
+    }
+    float sum = 0.0f;
+    for (int64_t t = 0; t < tn; ++t) {
+        float e = expf(scores[t] - mx);
+        scores[t] = e;
+        sum += e;
+    }
+    float inv = 1.0f / sum;
+    for (int64_t d = 0; d < hd; ++d) {
+        float v = 0.0f;
+        for (int64_t t = 0; t < tn; ++t) v += scores[t] * inv * Vc[t * kvd + kvoff + d];
+        out[qoff + d] = v;
+    }
+}
+
+// transformer.rs:1707-1765 (depth_route_with_indices) + :287-320 (depth_route_blocks)
+static void depth_route(float *x, std::vector<std::vector<float>> &deltas, int64_t bidx,
+                        const float *query, const float *normw, int64_t n,
+                        std::vector<float> &scaled) {
+    int64_t limit = std::min<int64_t>(bidx + 1, (int64_t)deltas.size());
+    float logits[64];
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < limit; ++i) {
+        const float *src = deltas[i].data();
+        float ss = sum_sq(src, n);
+        float rms = sqrtf(ss / (float)n + 1e-5f);
+        float inv = 1.0f / rms;
+        std::memcpy(scaled.data(), src, n * sizeof(float));
+        scale_mul_inplace(scaled.data(), normw, n, inv);
+        float lg = dot(scaled.data(), query, n);
+        logits[i] = lg;
+        mx = fmax_rs(mx, lg);
+    }
+    add_scalar_inplace(logits, limit, -mx);
+    exp_inplace(logits, limit);
+    float se = sum_f32(logits, limit);
+    float inv_sum = 1.0f / se;
+    for (int64_t i = 0; i < limit; ++i)
+        fused_scale_acc(x, deltas[i].data(), logits[i] * inv_sum, n);
+    std::fill(deltas[bidx].begin(), deltas[bidx].end(), 0.0f);
+}
+
+// ------------------------------------------------------------------------
+// TurboQuant — src/turboquant/*
+// ------------------------------------------------------------------------
+static int64_t packed_len(int64_t n, int bits) {  // kv_cache.rs:499-509
+    switch (bits) {
+        case 2: return (n + 3) / 4;
+        case 3:
+        case 4: return (n + 1) / 2;
+        case 8: return n;
+        default: return (n * bits + 7) / 8;
+    }
+}
+static void pack_into(const uint8_t *idx, int64_t n, int bits, uint8_t *out) {  // :560-632
+    int64_t pl = packed_len(n, bits);
+    if (bits == 8) {
+        std::memcpy(out, idx, n);
+        return;
+    }
+    std::memset(out, 0, pl);
+    if (bits == 2) {
+        for (int64_t i = 0; i < n; ++i) out[i / 4] |= (uint8_t)((idx[i] & 0x3) << ((i % 4) * 2));
+    } else if (bits == 3 || bits == 4) {
+        for (int64_t i = 0; i < n; ++i) out[i / 2] |= (uint8_t)((idx[i] & 0xF) << ((i % 2) * 4));
+    } else {
+        int64_t bp = 0;
+        for (int64_t i = 0; i < n; ++i, bp += bits) {
+            int64_t byte = bp / 8, sh = bp % 8;
+            out[byte] |= (uint8_t)(idx[i] << sh);
+            if (sh + bits > 8) out[byte + 1] |= (uint8_t)(idx[i] >> (8 - sh));
+        }
+    }
+}
+static void unpack_into(const uint8_t *p, int64_t n, int bits, uint8_t *out) {  // :688-757
+    if (bits == 2) {
+        for (int64_t i = 0; i < n; ++i) out[i] = (p[i / 4] >> ((i % 4) * 2)) & 0x3;
+    } else if (bits == 3 || bits == 4) {
+        for (int64_t i = 0; i < n; ++i) out[i] = (p[i / 2] >> ((i % 2) * 4)) & 0xF;
+    } else if (bits == 8) {
+        std::memcpy(out, p, n);
+    } else {
+        uint8_t mask = (uint8_t)((1u << bits) - 1);
+        int64_t bp = 0;
+        for (int64_t i = 0; i < n; ++i, bp += bits) {
+            int64_t byte = bp / 8, sh = bp % 8;
+            uint8_t v = (p[byte] >> sh) & mask;
+            if (sh + bits > 8) v |= (uint8_t)(p[byte + 1] << (8 - sh)) & mask;
+            out[i] = v;
+        }
+    }
+}
+
+// codebook.rs:84-117 (Lanczos ln_gamma)
+static double ln_gamma(double x) {
+    const double g = 7.0;
+    static const double coef[9] = {0.99999999999980993,  676.5203681218851,
+                                   -1259.1392167224028,  771.32342877765313,
+                                   -176.61502916214059,  12.507343278686905,
+                                   -0.13857109526572012, 9.9843695780195716e-6,
+                                   1.5056327351493116e-7};
+    const double PI = 3.14159265358979323846;
+    if (x < 0.5) return PI / log(sin(PI * x)) - ln_gamma(1.0 - x);
+    double z = x - 1.0;
+    double acc = coef[0];
+    double t = z + g + 0.5;
+    for (int i = 0; i < 8; ++i) acc = acc + coef[i + 1] / (z + (double)i + 1.0);
+    return ((log(sqrt(2.0 * PI)) + log(t + 0.5) * (z + 0.5)) - t) + log(acc);
+}
+// codebook.rs:79-82
+static float gamma_ratio(int64_t d) {
+    double df = (double)d;
+    const double PI = 3.14159265358979323846;
+    double lr = ln_gamma(df / 2.0) - ln_gamma((df - 1.0) / 2.0) - log(PI / 2.0);
+    return (float)exp(lr);
+}
+// codebook.rs:67-73
+static float beta_pdf(float x, int64_t d) {
+    if (fabsf(x) >= 1.0f) return 0.0f;
+    float expo = (float)(d - 3) / 2.0f;
+    float c = gamma_ratio(d);
+    return c * powf(1.0f - x * x, expo);
+}
+// codebook.rs:124-158
+static void compute_centroids(const std::vector<float> &bnd, int64_t dim, std::vector<float> &cent) {
+    size_t n = bnd.size() + 1;
+    cent.assign(n, 0.0f);
+    const int ns = 1000;
+    std::vector<float> edges(n + 1);
+    edges[0] = -1.0f;
+    for (size_t i = 0; i + 1 < n; ++i) edges[i + 1] = bnd[i];
+    edges[n] = 1.0f;
+    for (size_t i = 0; i < n; ++i) {
+        float lo = edges[i], hi = edges[i + 1];
+        float dx = (hi - lo) / (float)ns;
+        double sfx = 0.0, sxfx = 0.0;
+        for (int j = 0; j <= ns; ++j) {
+            float x = lo + dx * (float)j;
+            float pdf = beta_pdf(x, dim);
+            double w = (j == 0 || j == ns) ? 0.5 : 1.0;
+            sfx += (double)pdf * w;
+            sxfx += (double)x * (double)pdf * w;
+        }
+        cent[i] = sfx > 1e-12 ? (float)(sxfx / sfx) : (lo + hi) / 2.0f;
+    }
+}
+// codebook.rs:175-198
+static float compute_mse(const std::vector<float> &bnd, const std::vector<float> &cent, int64_t dim) {
+    size_t n = cent.size();
+    std::vector<float> edges(n + 1);
+    edges[0] = -1.0f;
+    for (size_t i = 0; i + 1 < n; ++i) edges[i + 1] = bnd[i];
+    edges[n] = 1.0f;
+    const int ns = 500;
+    double total = 0.0;
+    for (size_t i = 0; i < n; ++i) {
+        float lo = edges[i], hi = edges[i + 1];
+        float dx = (hi - lo) / (float)ns;
+        double im = 0.0;
+        for (int j = 0; j <= ns; ++j) {
+            float x = lo + dx * (float)j;
+            float pdf = beta_pdf(x, dim);
+            double w = (j == 0 || j == ns) ? 0.5 : 1.0;
+            double diff = (double)x - (double)cent[i];
+            im += diff * diff * (double)pdf * w;
+        }
+        total += im * (double)dx;
+    }
+    return (float)total;
+}
+// codebook.rs:20-60
+static void codebook(int64_t dim, int bits, std::vector<float> &cent, std::vector<float> &bnd,
+                     float *mse) {
+    int64_t nl = (int64_t)1 << bits;
+    int64_t nb = nl - 1;
+    bnd.resize(nb);
+    for (int64_t i = 0; i < nb; ++i) bnd[i] = -1.0f + 2.0f * (float)(i + 1) / (float)nl;
+    std::vector<float> c, nbd(nb);
+    for (int it = 0; it < 50; ++it) {
+        compute_centroids(bnd, dim, c);
+        for (int64_t i = 0; i < nb; ++i) nbd[i] = (c[i] + c[i + 1]) / 2.0f;
+        bool conv = true;
+        for (int64_t i = 0; i < nb; ++i)
+            if (!(fabsf(bnd[i] - nbd[i]) < 1e-6f)) conv = false;
+        bnd = nbd;
+        if (conv) break;
+    }
+    compute_centroids(bnd, dim, cent);
+    if (mse) *mse = compute_mse(bnd, cent, dim);
+}
+// rotation.rs:11-52 (modified Gram-Schmidt, scalar sequential sums)
+static void rotation_from(int64_t dim, const float *mat, float *q);
+static void rotation(int64_t dim, uint64_t seed, float *q) {
+    Rng rng(seed);
+    std::vector<float> mat(dim * dim);
+    for (auto &e : mat) e = rng.normal();
+    rotation_from(dim, mat.data(), q);
+}
+static void rotation_from(int64_t dim, const float *mat, float *q) {
+    std::vector<float> v(dim * dim);
+    for (int64_t col = 0; col < dim; ++col)
+        for (int64_t row = 0; row < dim; ++row) v[col * dim + row] = mat[row * dim + col];
+    std::fill(q, q + dim * dim, 0.0f);
+    // Right-looking order: column i receives the projections of q_0, q_1, ...
+    // in the same sequence (and with the same operands) as the reference's
+    // left-looking loop, so every value is bit-identical; it only lets the
+    // columns be updated in parallel.
+    unsigned nt = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    for (int64_t j = 0; j < dim; ++j) {
+        float *vj = &v[j * dim];
+        float nrm = sqrtf(sum_sq(vj, dim));
+        if (nrm > 1e-8f)
+            for (int64_t k = 0; k < dim; ++k) q[k * dim + j] = vj[k] / nrm;
+        auto work = [&](int64_t i0, int64_t i1) {
+            for (int64_t i = i0; i < i1; ++i) {
+                float *vi = &v[i * dim];
+                float d = -0.0f;  // Iterator::<f32>::sum starts at -0.0
+                for (int64_t k = 0; k < dim; ++k) d = d + q[k * dim + j] * vi[k];
+                for (int64_t k = 0; k < dim; ++k) vi[k] -= d * q[k * dim + j];
+            }
+        };
+        int64_t rem = dim - (j + 1);
+        if (rem <= 0) continue;
+        if (rem < 64 || nt == 1) {
+            work(j + 1, dim);
+        } else {
+            std::vector<std::thread> th;
+            int64_t per = (rem + nt - 1) / nt;
+            for (unsigned t = 0; t < nt; ++t) {
+                int64_t a = j + 1 + t * per, b = std::min<int64_t>(dim, a + per);
+                if (a < b) th.emplace_back(work, a, b);
+            }
+            for (auto &t : th) t.join();
+        }
+    }
+}
+static inline uint8_t quantize(const float *bnd, int64_t nb, float v) {  // codebook.rs:202-204
+    int64_t c = 0;
+    while (c < nb && v >= bnd[c]) ++c;  // partition_point(|b| v >= b) on monotone boundaries
+    return (uint8_t)c;
+}
+
+struct TQ {
+    int64_t dim;
+    int kbits, vbits;
+    std::vector<float> rot, rot_t, kc, kb, vc, vb;
+};
+static const TQ &tq_tables(int64_t dim, int kbits, int vbits) {
+    // small process-wide cache (tables are deterministic in (dim, bits))
+    static std::vector<TQ *> cache;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    for (TQ *t : cache)
+        if (t->dim == dim && t->kbits == kbits && t->vbits == vbits) return *t;
+    TQ *t = new TQ;
+    t->dim = dim;
+    t->kbits = kbits;
+    t->vbits = vbits;
+    t->rot.resize(dim * dim);
+    rotation(dim, 42, t->rot.data());  // kv_cache.rs:63-77: seed 42, shared by layers
+    t->rot_t.resize(dim * dim);
+    for (int64_t i = 0; i < dim; ++i)
+        for (int64_t j = 0; j < dim; ++j) t->rot_t[i * dim + j] = t->rot[j * dim + i];
+    codebook(dim, kbits, t->kc, t->kb, nullptr);
+    codebook(dim, vbits, t->vc, t->vb, nullptr);
+    cache.push_back(t);
+    return *t;
+}
+
+// kv_cache.rs:156-195 (store_key / store_value)
+static void tq_store(const float *rot, const float *bnd, int bits, int64_t dim, const float *x,
+                     uint8_t *packed, float *norm_out, float *scratch_n, float *scratch_r,
+                     uint8_t *scratch_i) {
+    float norm = sqrtf(sum_sq(x, dim));
+    *norm_out = norm;
+    if (norm < 1e-8f) return;  // indices left untouched (reference quirk)
+    float inv = 1.0f / norm;
+    std::memcpy(scratch_n, x, dim * sizeof(float));
+    scale_inplace(scratch_n, dim, inv);
+    matmul(scratch_r, rot, scratch_n, dim, dim);
+    int64_t nb = ((int64_t)1 << bits) - 1;
+    for (int64_t i = 0; i < dim; ++i) scratch_i[i] = quantize(bnd, nb, scratch_r[i]);
+    pack_into(scratch_i, dim, bits, packed);
+}
+// kv_cache.rs:279-317 (dequantize_*_into)
+static void tq_dequant(const float *rot_t, const float *cent, int bits, int64_t dim,
+                       const uint8_t *packed, float norm, float *out, float *scratch_r,
+                       uint8_t *scratch_i) {
+    if (norm < 1e-8f) {
+        std::fill(out, out + dim, 0.0f);
+        return;
+    }
+    unpack_into(packed, dim, bits, scratch_i);
+    int64_t nl = (int64_t)1 << bits;
+    for (int64_t i = 0; i < dim; ++i) scratch_r[i] = scratch_i[i] < nl ? cent[scratch_i[i]] : 0.0f;
+    matmul(out, rot_t, scratch_r, dim, dim);
+    scale_inplace(out, dim, norm);
+}
+
+// utility predictor — src/sp_kv/utility_predictor.rs:16-87, weights types.rs:224-258
+struct Predictor {
+    int64_t hidden;
+    std::vector<float> w1, b1, w2, b2;
+};
+static Predictor make_predictor(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias) {
+    Predictor p;
+    p.hidden = hidden;
+    float s1 = sqrtf(2.0f / (float)d_model), s2 = sqrtf(2.0f / (float)hidden);
+    Rng rng(42);
+    p.w1.resize(hidden * d_model);
+    for (auto &e : p.w1) e = rng.normal() * s1;
+    p.b1.assign(hidden, 0.0f);
+    p.w2.resize(nkv * hidden);
+    for (auto &e : p.w2) e = rng.normal() * s2;
+    p.b2.assign(nkv, init_bias);
+    return p;
+}
+static float silu(float x) { return x * (1.0f / (1.0f + expf(-x))); }
+static float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ------------------------------------------------------------------------
+// Per-sequence forward state
+// ------------------------------------------------------------------------
+struct Seq {
+    Dims d;
+    const Weights *W;
+    int mode;
+    bool quant_shared_flat;  // forward_quantized as written (one flat buffer for all layers)
+    // scratch (ForwardContext, transformer.rs:59-176)
+    std::vector<float> x, xr, xr2, q, k, v, att, scores, hidden, aval, scaled, logits;
+    std::vector<int64_t> aidx;
+    std::vector<std::vector<float>> deltas;
+    // f32 KV (MultiLayerKVCache)
+    std::vector<float> Kc, Vc;
+    // TurboQuant cache
+    const TQ *tq = nullptr;
+    int kbits = 4, vbits = 4;
+    int64_t kpl = 0, vpl = 0;
+    std::vector<uint8_t> kcodes, vcodes;
+    std::vector<float> knorm, vnorm;
+    std::vector<float> flatK, flatV;  // [L][B][kvd] (or [B][kvd] when shared)
+    std::vector<int64_t> dequant_pos;
+    std::vector<float> sn, sr;
+    std::vector<uint8_t> si;
+    // SP-KV
+    const Predictor *pred = nullptr;
+    std::vector<float> pbuf, hu, util, bias;
+    std::vector<uint8_t> retained;
+
+    void init(const Dims &dd, const Weights *w, int md, int kb, int vb) {
+        d = dd;
+        W = w;
+        mode = md;
+        quant_shared_flat = false;
+        x.assign(d.n, 0.f); xr = x; xr2 = x; q = x; att = x; scaled = x;
+        k.assign(d.kvd, 0.f); v = k;
+        scores.assign(d.B, 0.f);
+        hidden.assign(d.m, 0.f); aval = hidden; aidx.assign(d.m, 0);
+        logits.assign(d.V, 0.f);
+        deltas.assign(d.nblocks, std::vector<float>(d.n, 0.f));
+        if (mode == OR_MODE_BASE) {
+            Kc.assign(d.L * d.B * d.kvd, 0.f);
+            Vc = Kc;
+        } else {
+            kbits = kb;
+            vbits = vb;
+            kpl = packed_len(d.kvd, kb);
+            vpl = packed_len(d.kvd, vb);
+            kcodes.assign(d.L * d.B * kpl, 0);
+            vcodes.assign(d.L * d.B * vpl, 0);
+            knorm.assign(d.L * d.B, 0.f);
+            vnorm = knorm;
+            flatK.assign(d.L * d.B * d.kvd, 0.f);
+            flatV = flatK;
+            dequant_pos.assign(d.L, 0);
+            sn.assign(d.kvd, 0.f); sr = sn; si.assign(d.kvd, 0);
+            util.assign(d.L * d.B, 0.f);
+            retained.assign(d.L * d.B, 0);
+            bias.assign(d.B, 0.f);
+        }
+    }
+
+    void store_kv(int64_t l, int64_t pos) {
+        int64_t at = l * d.B + pos;
+        tq_store(tq->rot.data(), tq->kb.data(), kbits, d.kvd, k.data(), &kcodes[at * kpl],
+                 &knorm[at], sn.data(), sr.data(), si.data());
+        tq_store(tq->rot.data(), tq->vb.data(), vbits, d.kvd, v.data(), &vcodes[at * vpl],
+                 &vnorm[at], sn.data(), sr.data(), si.data());
+    }
+    void deq_key(int64_t l, int64_t t, float *out) {
+        int64_t at = l * d.B + t;
+        tq_dequant(tq->rot_t.data(), tq->kc.data(), kbits, d.kvd, &kcodes[at * kpl], knorm[at], out,
+                   sr.data(), si.data());
+    }
+    void deq_val(int64_t l, int64_t t, float *out) {
+        int64_t at = l * d.B + t;
+        tq_dequant(tq->rot_t.data(), tq->vc.data(), vbits, d.kvd, &vcodes[at * vpl], vnorm[at], out,
+                   sr.data(), si.data());
+    }
+
+    // MLP block shared by all three forwards: xr2=x; norm; relu(W1); sparse/dense W2; += xr2
+    void mlp(const LayerW &lw, bool gamma_norm, const float *ones) {
+        xr2 = x;
+        if (gamma_norm) rmsnorm_gamma(x.data(), ones, d.n);
+        else rmsnorm(x.data(), d.n);
+        matmul_relu(hidden.data(), lw.w1, x.data(), d.m, d.n);
+        int64_t alive = sparse_matmul(x.data(), lw.w2, hidden.data(), d.n, d.m, aidx.data(), aval.data());
+        // transformer.rs:2080-2101: dense recompute when alive fraction > 1 - threshold
+        if ((float)alive / (float)d.m > (1.0f - sparse_threshold))
+            matmul(x.data(), lw.w2, hidden.data(), d.n, d.m);
+        add_inplace(x.data(), xr2.data(), d.n);
+    }
+    float sparse_threshold = 0.8f;
+
+    void delta_route(int64_t l) {  // transformer.rs:2129-2158
+        int64_t bidx = l / 4, pib = l % 4;
+        if (bidx < (int64_t)deltas.size()) fused_sub_acc(deltas[bidx].data(), x.data(), xr.data(), d.n);
+        if (pib == 3 && bidx < (int64_t)deltas.size())
+            depth_route(x.data(), deltas, bidx, W->dq + l * d.n, W->dn + l * d.n, d.n, scaled);
+    }
+
+    // transformer.rs:1821-2200 (forward_base, default features, lora=None)
+    void forward_base(int64_t tok, int64_t pos, const float *ones) {
+        add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
+        float scale = 1.0f / sqrtf((float)d.hd);
+        for (int64_t l = 0; l < d.L; ++l) {
+            const LayerW &lw = W->layers[l];
+            rmsnorm_gamma(x.data(), ones, d.n);
+            xr = x;
+            matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+            matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+            matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+            float *K = &Kc[l * d.B * d.kvd], *Vv = &Vc[l * d.B * d.kvd];
+            std::memcpy(K + pos * d.kvd, k.data(), d.kvd * 4);
+            std::memcpy(Vv + pos * d.kvd, v.data(), d.kvd * 4);
+            for (int64_t h = 0; h < d.nh; ++h) {
+                int64_t g = h * d.nkv / d.nh;
+                attention_head(q.data(), K, Vv, att.data(), scores.data(), h * d.hd, g * d.hd,
+                               d.kvd, d.hd, pos + 1, scale);
+            }
+            matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+            add_inplace(x.data(), xr.data(), d.n);
+            mlp(lw, true, ones);
+            delta_route(l);
+        }
+        matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
+    }
+
+    // transformer.rs:4042-4233 (forward_quantized<TurboQuantKVCache>)
+    void forward_quant(int64_t tok, int64_t pos) {
+        add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
+        float scale = 1.0f / sqrtf((float)d.hd);
+        int64_t tn = pos + 1;
+        for (int64_t l = 0; l < d.L; ++l) {
+            const LayerW &lw = W->layers[l];
+            rmsnorm(x.data(), d.n);
+            xr = x;
+            matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+            matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+            matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+            store_kv(l, pos);
+            // Per-layer flat buffers (the intended semantics). With
+            // quant_shared_flat the single ForwardContext buffer of the
+            // reference is reproduced as written.
+            int64_t fo = quant_shared_flat ? 0 : l * d.B * d.kvd;
+            float *FK = &flatK[fo], *FV = &flatV[fo];
+            int64_t last = dequant_pos[l];
+            if (last + 1 == pos && pos > 0) {
+                deq_key(l, pos, FK + pos * d.kvd);
+                deq_val(l, pos, FV + pos * d.kvd);
+            } else {
+                for (int64_t t = 0; t < tn; ++t) {
+                    deq_key(l, t, FK + t * d.kvd);
+                    deq_val(l, t, FV + t * d.kvd);
+                }
+            }
+            dequant_pos[l] = pos;
+            for (int64_t h = 0; h < d.nh; ++h) {
+                int64_t g = h * d.nkv / d.nh;
+                attention_head(q.data(), FK, FV, att.data(), scores.data(), h * d.hd, g * d.hd,
+                               d.kvd, d.hd, tn, scale);
+            }
+            matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+            add_inplace(x.data(), xr.data(), d.n);
+            mlp(lw, false, nullptr);
+            delta_route(l);
+        }
+        matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
+    }
+
+    // src/sp_kv/forward.rs:610-822 (forward_sp_kv_quant, Hard gate, default SpKvConfig)
+    void forward_spkv(int64_t tok, int64_t pos) {
+        const int64_t window = 128;
+        const float threshold = 0.5f;
+        add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
+        int64_t tn = pos + 1;
+        for (int64_t l = 0; l < d.L; ++l) {
+            const LayerW &lw = W->layers[l];
+            rmsnorm(x.data(), d.n);
+            xr = x;
+            rmsnorm(x.data(), d.n);
+            // utility predictor (utility_predictor.rs:51-87), Max aggregation
+            for (int64_t i = 0; i < pred->hidden; ++i)
+                pbuf[i] = silu(dot(&pred->w1[i * d.n], x.data(), d.n) + pred->b1[i]);
+            for (int64_t kh = 0; kh < d.nkv; ++kh)
+                hu[kh] = sigmoid(dot(&pred->w2[kh * pred->hidden], pbuf.data(), pred->hidden) + pred->b2[kh]);
+            float u = hu[0];
+            for (int64_t kh = 1; kh < d.nkv; ++kh) u = fmax_rs(u, hu[kh]);
+            matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+            matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+            matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+            // write_gated(pos_is_in_window = true) — types.rs:505-527
+            util[l * d.B + pos] = u;
+            store_kv(l, pos);
+            retained[l * d.B + pos] = 1;
+            // build_hard — types.rs:343-356
+            for (int64_t s = 0; s <= pos; ++s) {
+                bool inw = (pos - s) < window;
+                bool keep = inw || util[l * d.B + s] >= threshold || retained[l * d.B + s];
+                bias[s] = keep ? 0.0f : -INFINITY;
+            }
+            // dequantize_retained_*_into — full rebuild 0..=pos (types.rs:534-575)
+            float *FK = &flatK[0], *FV = &flatV[0];
+            for (int64_t t = 0; t < tn; ++t) {
+                if (retained[l * d.B + t]) {
+                    deq_key(l, t, FK + t * d.kvd);
+                    deq_val(l, t, FV + t * d.kvd);
+                } else {
+                    std::fill(FK + t * d.kvd, FK + (t + 1) * d.kvd, 0.f);
+                    std::fill(FV + t * d.kvd, FV + (t + 1) * d.kvd, 0.f);
+                }
+            }
+            float scale = 1.0f / sqrtf((float)d.hd);
+            std::fill(att.begin(), att.end(), 0.f);
+            for (int64_t h = 0; h < d.nh; ++h) {
+                int64_t g = h * d.nkv / d.nh;
+                attention_head_gated(q.data(), FK, FV, att.data(), scores.data(), h * d.hd,
+                                     g * d.hd, d.kvd, d.hd, tn, scale, bias.data());
+            }
+            matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+            add_inplace(x.data(), xr.data(), d.n);
+            mlp(lw, false, nullptr);
+        }
+        matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
+    }
+};
+
+static const Predictor &predictor_for(int64_t n, int64_t nkv) {
+    static std::vector<std::pair<std::pair<int64_t, int64_t>, Predictor *>> cache;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto &e : cache)
+        if (e.first.first == n && e.first.second == nkv) return *e.second;
+    int64_t hidden = std::max<int64_t>(n / 4, 16);  // SpKvConfig::resolve_hidden (types.rs:58-65)
+    Predictor *p = new Predictor(make_predictor(n, hidden, nkv, 5.0f));
+    cache.push_back({{n, nkv}, p});
+    return *p;
+}
+
+static int run_one(const or_config *c, int mode, int kb, int vb, const Weights &W, const Dims &d,
+                   const int32_t *tokens, int32_t T, float *logits, int32_t t0, uint8_t *codes,
+                   float *norms, float *utilities, bool shared_flat, Seq &s,
+                   const std::vector<float> &ones) {
+    s.init(d, &W, mode == 3 ? OR_MODE_QUANT : mode, kb, vb);
+    s.sparse_threshold = c->sparse_threshold;
+    s.quant_shared_flat = shared_flat;
+    if (mode != OR_MODE_BASE) s.tq = &tq_tables(d.kvd, kb, vb);
+    if (mode == OR_MODE_SPKV_QUANT) {
+        s.pred = &predictor_for(d.n, d.nkv);
+        s.pbuf.assign(s.pred->hidden, 0.f);
+        s.hu.assign(d.nkv, 0.f);
+    }
+    for (int32_t p = 0; p < T; ++p) {
+        int64_t tok = tokens[p];
+        if (tok < 0 || tok >= d.V) return -2;
+        if (mode == OR_MODE_BASE) s.forward_base(tok, p, ones.data());
+        else if (mode == OR_MODE_SPKV_QUANT) s.forward_spkv(tok, p);
+        else s.forward_quant(tok, p);
+        if (logits && p >= t0) std::memcpy(logits + (int64_t)(p - t0) * d.V, s.logits.data(), d.V * 4);
+    }
+    if (mode != OR_MODE_BASE) {
+        for (int64_t l = 0; l < d.L; ++l)
+            for (int64_t p = 0; p < T; ++p) {
+                int64_t at = l * d.B + p;
+                int64_t o = (l * T + p);
+                if (codes) {
+                    std::memcpy(codes + o * (s.kpl + s.vpl), &s.kcodes[at * s.kpl], s.kpl);
+                    std::memcpy(codes + o * (s.kpl + s.vpl) + s.kpl, &s.vcodes[at * s.vpl], s.vpl);
+                }
+                if (norms) {
+                    norms[o * 2] = s.knorm[at];
+                    norms[o * 2 + 1] = s.vnorm[at];
+                }
+                if (utilities) utilities[o] = s.util[at];
+            }
+    }
+    return 0;
+}
+
+static int check_cfg(const or_config *c, int32_t T) {
+    if (!c || c->n_embd <= 0 || c->n_head <= 0 || c->head_dim <= 0 || c->n_kv_head <= 0 ||
+        c->n_layer <= 0 || c->vocab_size <= 0 || c->mlp_hidden <= 0)
+        return -1;
+    if (T < 0 || T > c->block_size) return -1;
+    if ((int64_t)c->n_head * c->head_dim != c->n_embd) return -1;
+    if (c->n_head % c->n_kv_head != 0) return -1;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+void or_rng_uniforms(uint64_t seed, int64_t n, float *out) {
+    Rng r(seed);
+    for (int64_t i = 0; i < n; ++i) out[i] = r.uniform();
+}
+void or_rng_normals(uint64_t seed, int64_t n, float *out) {
+    Rng r(seed);
+    for (int64_t i = 0; i < n; ++i) out[i] = r.normal();
+}
+
+int64_t or_weights_count(const or_config *c) { return weights_count(dims_of(c)); }
+
+void or_weights_init(const or_config *c, uint64_t seed, int scale_mode, float std_, float *out) {
+    Dims d = dims_of(c);
+    Rng rng(seed);
+    float es = sqrtf(2.0f / (float)d.n);                       // weights.rs:79
+    float ls = sqrtf(2.0f / ((float)d.n * (float)d.L));        // weights.rs:80
+    if (scale_mode == 1) es = ls = std_;
+    float *p = out;
+    for (int64_t i = 0; i < d.V * d.n; ++i) *p++ = rng.normal() * es;
+    for (int64_t i = 0; i < d.B * d.n; ++i) *p++ = rng.normal() * es;
+    for (int64_t l = 0; l < d.L; ++l) {
+        int64_t cnt = 2 * d.n * d.n + 2 * d.kvd * d.n + 2 * d.m * d.n;
+        for (int64_t i = 0; i < cnt; ++i) *p++ = rng.normal() * ls;
+    }
+    for (int64_t i = 0; i < d.V * d.n; ++i) *p++ = rng.normal() * es;
+    for (int64_t i = 0; i < d.L * d.n; ++i) *p++ = 0.0f;  // delta query: zeros (weights.rs:161-168)
+    for (int64_t i = 0; i < d.L * d.n; ++i) *p++ = 1.0f;  // delta norm gamma: ones (:169-176)
+}
+
+float or_dot(const float *a, const float *b, int64_t len) { return dot(a, b, len); }
+float or_sum_sq(const float *x, int64_t len) { return sum_sq(x, len); }
+float or_sum(const float *x, int64_t len) { return sum_f32(x, len); }
+float or_max(const float *x, int64_t len) { return max_f32(x, len); }
+void or_exp_inplace(float *x, int64_t len) { exp_inplace(x, len); }
+float or_exp_sum_inplace(float *x, int64_t len) { return exp_sum_inplace(x, len); }
+float or_sparse_dot(const float *w, const int64_t *idx, const float *val, int64_t alive) {
+    return sparse_dot(w, idx, val, alive);
+}
+void or_softmax_scaled(float *x, int64_t len, float inv_temp) { softmax_scaled(x, len, inv_temp); }
+float or_scalar_exp(float x) { return cephes_exp_scalar(x); }
+
+// math.rs:398-422 (sample_token_into)
+int64_t or_sample_token(const float *probs, int64_t n, uint64_t seed) {
+    Rng rng(seed);
+    float r = rng.uniform();
+    while (r == 0.0f) r = rng.uniform();
+    if (n == 0) return 0;
+    std::vector<float> cdf(n);
+    float s = 0.0f;
+    for (int64_t i = 0; i < n; ++i) {
+        s += probs[i];
+        cdf[i] = s;
+    }
+    int64_t idx = std::partition_point(cdf.begin(), cdf.end(), [&](float c) { return c <= r; }) -
+                  cdf.begin();
+    return std::min(idx, n - 1);
+}
+
+int64_t or_tq_packed_len(int64_t dim, int bits) { return packed_len(dim, bits); }
+
+void or_tq_codebook(int64_t dim, int bits, float *centroids, float *boundaries, float *mse) {
+    std::vector<float> c, b;
+    codebook(dim, bits, c, b, mse);
+    std::memcpy(centroids, c.data(), c.size() * 4);
+    std::memcpy(boundaries, b.data(), b.size() * 4);
+}
+void or_tq_rotation(int64_t dim, uint64_t seed, float *rot) { rotation(dim, seed, rot); }
+void or_tq_rotation_from(int64_t dim, const float *gauss, float *rot) { rotation_from(dim, gauss, rot); }
+void or_rng_normals_rawstate(uint64_t state, int64_t n, float *out) {
+    // Rng before the SplitMix64 seed expansion (katgpt-core CHANGELOG, issue 296):
+    // the seed itself is the XorShift64 state.
+    Rng r(0);
+    r.state = state == 0 ? 1 : state;
+    for (int64_t i = 0; i < n; ++i) out[i] = r.normal();
+}
+
+void or_tq_store(const float *rot, const float *bnd, int bits, int64_t dim, const float *x,
+                 uint8_t *packed, float *norm) {
+    std::vector<float> sn(dim), sr(dim);
+    std::vector<uint8_t> si(dim);
+    tq_store(rot, bnd, bits, dim, x, packed, norm, sn.data(), sr.data(), si.data());
+}
+void or_tq_dequant(const float *rot_t, const float *cent, int bits, int64_t dim,
+                   const uint8_t *packed, float norm, float *out) {
+    std::vector<float> sr(dim);
+    std::vector<uint8_t> si(dim);
+    tq_dequant(rot_t, cent, bits, dim, packed, norm, out, sr.data(), si.data());
+}
+// kv_cache.rs:243-258 + :471-495 (dequantize_key: scalar column loop over R)
+void or_tq_dequant_scalar(const float *rot, const float *cent, int bits, int64_t dim,
+                          const uint8_t *packed, float norm, float *out) {
+    if (norm < 1e-8f) {
+        std::fill(out, out + dim, 0.0f);
+        return;
+    }
+    std::vector<uint8_t> idx(dim);
+    unpack_into(packed, dim, bits, idx.data());
+    std::vector<float> r(dim);
+    int64_t nl = (int64_t)1 << bits;
+    for (int64_t i = 0; i < dim; ++i) r[i] = idx[i] < nl ? cent[idx[i]] : 0.0f;
+    for (int64_t i = 0; i < dim; ++i) {
+        float s = 0.0f;
+        for (int64_t j = 0; j < dim; ++j) s += rot[j * dim + i] * r[j];
+        out[i] = s * norm;
+    }
+}
+void or_tq_pack(const uint8_t *idx, int64_t n, int bits, uint8_t *out) { pack_into(idx, n, bits, out); }
+void or_tq_unpack(const uint8_t *p, int64_t n, int bits, uint8_t *out) { unpack_into(p, n, bits, out); }
+
+// src/turboquant/forward.rs:171-180
+float or_cosine(const float *a, const float *b, int64_t len) {
+    float dd = dot(a, b, len);
+    float na = sqrtf(dot(a, a, len)), nb = sqrtf(dot(b, b, len));
+    if (na < 1e-8f || nb < 1e-8f) return 0.0f;
+    return dd / (na * nb);
+}
+
+int or_run_sequence(const or_config *c, int mode, int kb, int vb, const float *weights,
+                    const int32_t *tokens, int32_t T, float *logits, uint8_t *codes, float *norms,
+                    float *utilities) {
+    if (check_cfg(c, T)) return -1;
+    if (mode < 0 || mode > 3) return -1;
+    Dims d = dims_of(c);
+    Weights W = view_weights(d, weights);
+    std::vector<float> ones(d.n, 1.0f);
+    Seq s;
+    // mode 3: forward_quantized with the reference's single shared flat buffer
+    return run_one(c, mode, kb, vb, W, d, tokens, T, logits, 0, codes, norms, utilities, mode == 3,
+                   s, ones);
+}
+
+int or_run_batch_tail(const or_config *c, int mode, int kb, int vb, const float *weights,
+                      const int32_t *tokens, int32_t n_seq, int32_t T, int32_t t0, float *logits,
+                      int n_threads) {
+    if (check_cfg(c, T)) return -1;
+    if (mode < 0 || mode > 3 || t0 < 0 || t0 > T) return -1;
+    Dims d = dims_of(c);
+    Weights W = view_weights(d, weights);
+    std::vector<float> ones(d.n, 1.0f);
+    if (mode != OR_MODE_BASE) tq_tables(d.kvd, kb, vb);
+    if (mode == OR_MODE_SPKV_QUANT) predictor_for(d.n, d.nkv);
+    if (n_threads < 1) n_threads = 1;
+    std::vector<int> rc(n_threads, 0);
+    auto worker = [&](int tid) {
+        Seq s;  // per-worker context (generate_batch map_init, transformer.rs:3588-3606)
+        for (int32_t i = tid; i < n_seq; i += n_threads) {
+            float *lo = logits ? logits + (int64_t)i * (T - t0) * d.V : nullptr;
+            int r = run_one(c, mode, kb, vb, W, d, tokens + (int64_t)i * T, T, lo, t0, nullptr,
+                            nullptr, nullptr, mode == 3, s, ones);
+            if (r) rc[tid] = r;
+        }
+    };
+    std::vector<std::thread> th;
+    for (int t = 1; t < n_threads; ++t) th.emplace_back(worker, t);
+    worker(0);
+    for (auto &t : th) t.join();
+    for (int r : rc)
+        if (r) return r;
+    return 0;
+}
+
+int or_run_batch(const or_config *c, int mode, int kb, int vb, const float *weights,
+                 const int32_t *tokens, int32_t n_seq, int32_t T, float *logits, int n_threads) {
+    return or_run_batch_tail(c, mode, kb, vb, weights, tokens, n_seq, T, 0, logits, n_threads);
+}
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+/*
+ * kg_oracle.h — CPU oracle for the katgpt-rs per-token transformer forward.
+ *
+ * TEST INFRASTRUCTURE ONLY. This library restates, in C++ with the same AVX2
+ * intrinsics and the same operation order, the x86-64 code path that the
+ * reference (katopz/katgpt-rs, Rust) takes under its default features plus
+ * `turboquant` + `sp_kv`. It is the parity checker for the CUDA library and the
+ * timed CPU baseline. Nothing in the product (libkgcuda) links or calls it.
+ *
+ * Parity pin: the reference cannot be compiled here (no Rust toolchain) and has
+ * no golden files; the oracle is pinned against the reference's published
+ * TurboQuant quality table (.docs/04_performance.md:323-328, inputs from
+ * tests/bench_turboquant.rs:23-27) and the structural asserts of its unit
+ * tests. See the test files under tests/ for each pin.
+ *
+ * All functions are plain C ABI (ctypes-friendly): pointers + sizes.
+ */
+#ifndef KG_ORACLE_H
+#define KG_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Subset of the reference `Config` (crates/katgpt-types/src/config.rs:14-180)
+ * that the forward path reads. */
+typedef struct {
+    int32_t vocab_size;
+    int32_t block_size;
+    int32_t n_embd;
+    int32_t n_head;
+    int32_t head_dim;
+    int32_t n_kv_head;
+    int32_t mlp_hidden;
+    int32_t n_layer;
+    int32_t bos_token;
+    float temperature;
+    float sparse_threshold;
+} or_config;
+
+/* Forward flavours (one per reference entry point). */
+enum {
+    OR_MODE_BASE = 0,      /* transformer::forward -> forward_base (src/transformer.rs:398-429,1821-2200) */
+    OR_MODE_QUANT = 1,     /* transformer::forward_quantized<TurboQuantKVCache> (:4042-4233) */
+    OR_MODE_SPKV_QUANT = 2 /* sp_kv::forward::forward_sp_kv_quant, Hard gate (src/sp_kv/forward.rs:610-800) */
+};
+
+/* ---- Rng (crates/katgpt-types/src/rng.rs:26-72) ---- */
+void or_rng_uniforms(uint64_t seed, int64_t n, float *out);
+void or_rng_normals(uint64_t seed, int64_t n, float *out);
+
+/* ---- weights (crates/katgpt-transformer/src/weights.rs:76-177) ----
+ * Flat layout, reference init order: wte[V*n], wpe[block*n], per layer
+ * {wq[n*n], wk[kvd*n], wv[kvd*n], wo[n*n], w1[m*n], w2[n*m]}, lm_head[V*n],
+ * then delta-routing query[L*n] (zeros) and norm[L*n] (ones). */
+int64_t or_weights_count(const or_config *c);
+/* scale_mode 0: reference scales sqrt(2/n), sqrt(2/(n*L)); 1: fixed std `std`. */
+void or_weights_init(const or_config *c, uint64_t seed, int scale_mode, float std_, float *out);
+
+/* ---- SIMD kernels, exposed for the SIMD-vs-scalar parity tests ---- */
+float or_dot(const float *a, const float *b, int64_t len);
+float or_sum_sq(const float *x, int64_t len);
+float or_sum(const float *x, int64_t len);
+float or_max(const float *x, int64_t len);
+void or_exp_inplace(float *x, int64_t len);
+float or_exp_sum_inplace(float *x, int64_t len);
+float or_sparse_dot(const float *w_row, const int64_t *idx, const float *val, int64_t alive);
+void or_softmax_scaled(float *x, int64_t len, float inv_temp);
+int64_t or_sample_token(const float *probs, int64_t n, uint64_t seed);
+/* scalar (non-SIMD) restatements used to cross-check the AVX2 ones */
+float or_scalar_exp(float x);
+
+/* ---- TurboQuant (src/turboquant/...) ---- */
+int64_t or_tq_packed_len(int64_t dim, int bits);
+/* centroids[2^bits], boundaries[2^bits-1], *mse */
+void or_tq_codebook(int64_t dim, int bits, float *centroids, float *boundaries, float *mse);
+/* row-major dim*dim orthogonal Q (columns = MGS basis) */
+void or_tq_rotation(int64_t dim, uint64_t seed, float *rot);
+/* same, from a caller-supplied row-major dim*dim Gaussian matrix */
+void or_tq_rotation_from(int64_t dim, const float *gauss, float *rot);
+/* normals from the pre-SplitMix64 Rng (state = seed), used to reproduce the
+ * reference's published TurboQuant table, which predates that change */
+void or_rng_normals_rawstate(uint64_t state, int64_t n, float *out);
+/* encode one vector: codes packed into `packed`, norm into *norm */
+void or_tq_store(const float *rot, const float *boundaries, int bits, int64_t dim,
+                 const float *x, uint8_t *packed, float *norm);
+/* decode one vector through rotation_t (row-major transpose of rot) */
+void or_tq_dequant(const float *rot_t, const float *centroids, int bits, int64_t dim,
+                   const uint8_t *packed, float norm, float *out);
+/* allocating decode through the scalar column loop (mat_vec_t) */
+void or_tq_dequant_scalar(const float *rot, const float *centroids, int bits, int64_t dim,
+                          const uint8_t *packed, float norm, float *out);
+void or_tq_pack(const uint8_t *idx, int64_t n, int bits, uint8_t *out);
+void or_tq_unpack(const uint8_t *packed, int64_t n, int bits, uint8_t *out);
+float or_cosine(const float *a, const float *b, int64_t len);
+
+/* ---- teacher-forced sequence runners ----
+ * Runs positions 0..T-1 of one sequence through the chosen forward and writes
+ * logits[T*V]. For the quantized modes, codes[L][T][2][packed] and
+ * norms[L][T][2] (K then V) are written when non-NULL; utilities[L][T] for
+ * SP-KV. weights: flat layout above. key_bits/val_bits for quantized modes.
+ * Returns 0 on success. */
+int or_run_sequence(const or_config *c, int mode, int key_bits, int val_bits,
+                    const float *weights, const int32_t *tokens, int32_t T,
+                    float *logits, uint8_t *codes, float *norms, float *utilities);
+
+/* Multi-sequence runner: n_seq sequences of T tokens each (row-major),
+ * spread over n_threads std::threads (one per core, as the reference's rayon
+ * generate_batch). logits may be NULL (discarded) for timing runs. */
+int or_run_batch(const or_config *c, int mode, int key_bits, int val_bits,
+                 const float *weights, const int32_t *tokens, int32_t n_seq, int32_t T,
+                 float *logits, int n_threads);
+
+/* Same, but only positions [t0, T) of each sequence are kept in `logits`
+ * (logits laid out [n_seq][T - t0][V]); all positions are still computed. */
+int or_run_batch_tail(const or_config *c, int mode, int key_bits, int val_bits,
+                      const float *weights, const int32_t *tokens, int32_t n_seq, int32_t T,
+                      int32_t t0, float *logits, int n_threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

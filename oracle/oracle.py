@@ -1,0 +1,285 @@
+"""ctypes wrapper of the CPU oracle (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+module, and only as the checker. It wraps oracle/_build/libkgoracle.so, a C++
+restatement of katgpt-rs's x86-64 AVX2 forward path (see kg_oracle.h).
+
+Parity pin: partial. The reference has no golden files and cannot be built
+here (Rust); the oracle is pinned to the reference's own test assertions and
+invariants (tests/test_oracle.py), not to reference-produced outputs.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBPATH = os.path.join(HERE, "_build", "libkgoracle.so")
+
+MODE_BASE, MODE_QUANT, MODE_SPKV, MODE_QUANT_AS_WRITTEN = 0, 1, 2, 3
+
+
+class OrConfig(ctypes.Structure):
+    _fields_ = [("vocab_size", ctypes.c_int32), ("block_size", ctypes.c_int32),
+                ("n_embd", ctypes.c_int32), ("n_head", ctypes.c_int32),
+                ("head_dim", ctypes.c_int32), ("n_kv_head", ctypes.c_int32),
+                ("mlp_hidden", ctypes.c_int32), ("n_layer", ctypes.c_int32),
+                ("bos_token", ctypes.c_int32), ("temperature", ctypes.c_float),
+                ("sparse_threshold", ctypes.c_float)]
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIBPATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIBPATH):
+            build()
+        L = ctypes.CDLL(LIBPATH)
+        P, I32, I64, F32, U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
+        cp = ctypes.POINTER(OrConfig)
+        sig = {
+            "or_rng_uniforms": (None, [U64, I64, P]),
+            "or_rng_normals": (None, [U64, I64, P]),
+            "or_rng_normals_rawstate": (None, [U64, I64, P]),
+            "or_weights_count": (I64, [cp]),
+            "or_weights_init": (None, [cp, U64, ctypes.c_int, F32, P]),
+            "or_dot": (F32, [P, P, I64]),
+            "or_sum_sq": (F32, [P, I64]),
+            "or_sum": (F32, [P, I64]),
+            "or_max": (F32, [P, I64]),
+            "or_exp_inplace": (None, [P, I64]),
+            "or_exp_sum_inplace": (F32, [P, I64]),
+            "or_sparse_dot": (F32, [P, P, P, I64]),
+            "or_softmax_scaled": (None, [P, I64, F32]),
+            "or_sample_token": (I64, [P, I64, U64]),
+            "or_scalar_exp": (F32, [F32]),
+            "or_tq_packed_len": (I64, [I64, ctypes.c_int]),
+            "or_tq_codebook": (None, [I64, ctypes.c_int, P, P, P]),
+            "or_tq_rotation": (None, [I64, U64, P]),
+            "or_tq_rotation_from": (None, [I64, P, P]),
+            "or_tq_store": (None, [P, P, ctypes.c_int, I64, P, P, P]),
+            "or_tq_dequant": (None, [P, P, ctypes.c_int, I64, P, F32, P]),
+            "or_tq_dequant_scalar": (None, [P, P, ctypes.c_int, I64, P, F32, P]),
+            "or_tq_pack": (None, [P, I64, ctypes.c_int, P]),
+            "or_tq_unpack": (None, [P, I64, ctypes.c_int, P]),
+            "or_cosine": (F32, [P, P, I64]),
+            "or_run_sequence": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, P, P, P, P]),
+            "or_run_batch": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, P, ctypes.c_int]),
+            "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
+        }
+        for k, (r, a) in sig.items():
+            f = getattr(L, k)
+            f.restype = r
+            f.argtypes = a
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def config(vocab_size=27, block_size=16, n_embd=16, n_head=4, head_dim=4, n_kv_head=4,
+           mlp_hidden=64, n_layer=1, bos_token=26, temperature=0.5, sparse_threshold=0.8):
+    """Config::micro() by default (crates/katgpt-types/src/config.rs:226-316)."""
+    return OrConfig(vocab_size, block_size, n_embd, n_head, head_dim, n_kv_head, mlp_hidden,
+                    n_layer, bos_token, temperature, sparse_threshold)
+
+
+def from_kg(kc):
+    """OrConfig from a kgcuda.KgConfig."""
+    return config(kc.vocab_size, kc.block_size, kc.n_embd, kc.n_head, kc.head_dim, kc.n_kv_head,
+                  kc.mlp_hidden, kc.n_layer, kc.bos_token, kc.temperature, kc.sparse_threshold)
+
+
+def normals(seed, n):
+    out = np.empty(n, np.float32)
+    lib().or_rng_normals(seed, n, _p(out))
+    return out
+
+
+def uniforms(seed, n):
+    out = np.empty(n, np.float32)
+    lib().or_rng_uniforms(seed, n, _p(out))
+    return out
+
+
+def weights(cfg, seed=42, scale_mode=0, std=0.02):
+    n = lib().or_weights_count(ctypes.byref(cfg))
+    w = np.empty(n, np.float32)
+    lib().or_weights_init(ctypes.byref(cfg), seed, scale_mode, std, _p(w))
+    return w
+
+
+def dot(a, b):
+    a, b = f32(a), f32(b)
+    return lib().or_dot(_p(a), _p(b), a.size)
+
+
+def sum_sq(x):
+    x = f32(x)
+    return lib().or_sum_sq(_p(x), x.size)
+
+
+def vsum(x):
+    x = f32(x)
+    return lib().or_sum(_p(x), x.size)
+
+
+def vmax(x):
+    x = f32(x)
+    return lib().or_max(_p(x), x.size)
+
+
+def exp_inplace(x):
+    x = f32(x).copy()
+    lib().or_exp_inplace(_p(x), x.size)
+    return x
+
+
+def exp_sum_inplace(x):
+    x = f32(x).copy()
+    s = lib().or_exp_sum_inplace(_p(x), x.size)
+    return x, s
+
+
+def scalar_exp(v):
+    return lib().or_scalar_exp(float(v))
+
+
+def sparse_dot(w_row, idx, val):
+    w_row, val = f32(w_row), f32(val)
+    idx = np.ascontiguousarray(idx, dtype=np.int64)
+    return lib().or_sparse_dot(_p(w_row), _p(idx), _p(val), idx.size)
+
+
+def softmax_scaled(x, inv_temp):
+    x = f32(x).copy()
+    lib().or_softmax_scaled(_p(x), x.size, inv_temp)
+    return x
+
+
+def sample_token(probs, seed):
+    p = f32(probs)
+    return lib().or_sample_token(_p(p), p.size, seed)
+
+
+def packed_len(dim, bits):
+    return lib().or_tq_packed_len(dim, bits)
+
+
+def codebook(dim, bits):
+    c = np.empty(1 << bits, np.float32)
+    b = np.empty((1 << bits) - 1, np.float32)
+    mse = ctypes.c_float()
+    lib().or_tq_codebook(dim, bits, _p(c), _p(b), ctypes.byref(mse))
+    return c, b, mse.value
+
+
+def rotation(dim, seed=42):
+    r = np.empty(dim * dim, np.float32)
+    lib().or_tq_rotation(dim, seed, _p(r))
+    return r.reshape(dim, dim)
+
+
+def rotation_from(gauss):
+    g = f32(gauss)
+    dim = g.shape[0]
+    r = np.empty(dim * dim, np.float32)
+    lib().or_tq_rotation_from(dim, _p(g), _p(r))
+    return r.reshape(dim, dim)
+
+
+def normals_rawstate(state, n):
+    out = np.empty(n, np.float32)
+    lib().or_rng_normals_rawstate(state, n, _p(out))
+    return out
+
+
+def tq_store(rot, bnd, bits, x, packed_init=None):
+    rot, bnd, x = f32(rot), f32(bnd), f32(x)
+    dim = x.size
+    pk = np.zeros(packed_len(dim, bits), np.uint8) if packed_init is None else np.array(packed_init, np.uint8)
+    nrm = ctypes.c_float()
+    lib().or_tq_store(_p(rot), _p(bnd), bits, dim, _p(x), _p(pk), ctypes.byref(nrm))
+    return pk, nrm.value
+
+
+def tq_dequant(rot_t, cent, bits, packed, norm):
+    rot_t, cent = f32(rot_t), f32(cent)
+    packed = np.ascontiguousarray(packed, np.uint8)
+    dim = rot_t.shape[0]
+    out = np.empty(dim, np.float32)
+    lib().or_tq_dequant(_p(rot_t), _p(cent), bits, dim, _p(packed), norm, _p(out))
+    return out
+
+
+def tq_dequant_scalar(rot, cent, bits, packed, norm):
+    rot, cent = f32(rot), f32(cent)
+    packed = np.ascontiguousarray(packed, np.uint8)
+    dim = rot.shape[0]
+    out = np.empty(dim, np.float32)
+    lib().or_tq_dequant_scalar(_p(rot), _p(cent), bits, dim, _p(packed), norm, _p(out))
+    return out
+
+
+def tq_pack(idx, bits):
+    idx = np.ascontiguousarray(idx, np.uint8)
+    out = np.zeros(packed_len(idx.size, bits), np.uint8)
+    lib().or_tq_pack(_p(idx), idx.size, bits, _p(out))
+    return out
+
+
+def tq_unpack(packed, n, bits):
+    packed = np.ascontiguousarray(packed, np.uint8)
+    out = np.zeros(n, np.uint8)
+    lib().or_tq_unpack(_p(packed), n, bits, _p(out))
+    return out
+
+
+def cosine(a, b):
+    a, b = f32(a), f32(b)
+    return lib().or_cosine(_p(a), _p(b), a.size)
+
+
+def run_sequence(cfg, mode, w, tokens, key_bits=3, val_bits=3):
+    """Teacher-forced forward of one sequence. Returns (logits[T,V], codes, norms, utilities)."""
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    T = tokens.size
+    logits = np.empty((T, cfg.vocab_size), np.float32)
+    codes = norms = util = None
+    if mode != MODE_BASE:
+        kvd = cfg.n_kv_head * cfg.head_dim
+        pl = packed_len(kvd, key_bits) + packed_len(kvd, val_bits)
+        codes = np.zeros((cfg.n_layer, T, pl), np.uint8)
+        norms = np.zeros((cfg.n_layer, T, 2), np.float32)
+        util = np.zeros((cfg.n_layer, T), np.float32)
+    rc = lib().or_run_sequence(ctypes.byref(cfg), mode, key_bits, val_bits, _p(f32(w)), _p(tokens), T,
+                               _p(logits), _p(codes), _p(norms), _p(util))
+    if rc:
+        raise RuntimeError(f"or_run_sequence failed: {rc}")
+    return logits, codes, norms, util
+
+
+def run_batch(cfg, mode, w, tokens, key_bits=3, val_bits=3, threads=None, keep_logits=True, t0=0):
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    n_seq, T = tokens.shape
+    threads = threads or os.cpu_count() or 1
+    logits = np.empty((n_seq, T - t0, cfg.vocab_size), np.float32) if keep_logits else None
+    rc = lib().or_run_batch_tail(ctypes.byref(cfg), mode, key_bits, val_bits, _p(f32(w)), _p(tokens),
+                                 n_seq, T, t0, _p(logits), threads)
+    if rc:
+        raise RuntimeError(f"or_run_batch failed: {rc}")
+    return logits

@@ -1,0 +1,71 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+that include/kg_abi.h declares, and its host-side functions agree with the
+oracle bit for bit (weights init, packed sizes)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(kg_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for must in ("kg_ctx_create", "kg_forward_token", "kg_forward_batch", "kg_tq_encode", "kg_kv_codes"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol(kg):
+    lib = ctypes.CDLL(kg.LIBPATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_config_micro_defaults(kg):
+    c = kg.micro_config()
+    assert (c.vocab_size, c.block_size, c.n_embd, c.n_head, c.head_dim, c.n_kv_head,
+            c.mlp_hidden, c.n_layer, c.bos_token) == (27, 16, 16, 4, 4, 4, 64, 1, 26)
+    assert c.temperature == 0.5 and abs(c.sparse_threshold - 0.8) < 1e-7
+    assert c.tq_seed == 42 and c.spkv_window == 128
+
+
+@pytest.mark.parametrize("shape", [dict(), dict(n_layer=4), dict(n_layer=2, n_embd=32, n_head=4, head_dim=8,
+                                                                   mlp_hidden=128, vocab_size=50)])
+def test_reference_weights_match_oracle(kg, orc, shape):
+    c = kg.micro_config(**shape)
+    w = kg.reference_weights(c, seed=42)
+    o = orc.weights(orc.from_kg(c), 42)
+    assert w.shape == o.shape and np.array_equal(w, o)
+    w2 = kg.reference_weights(c, seed=7, scale_mode=1, std=0.02)
+    o2 = orc.weights(orc.from_kg(c), 7, 1, 0.02)
+    assert np.array_equal(w2, o2)
+
+
+def test_packed_len_matches_oracle(kg, orc):
+    for dim in (1, 15, 16, 17, 768, 4096):
+        for bits in (2, 3, 4, 5, 8):
+            assert kg.lib().kg_tq_packed_len(dim, bits) == orc.packed_len(dim, bits)
+
+
+def test_status_strings(kg):
+    for s in range(-7, 1):
+        assert kg.lib().kg_status_string(s)
+
+
+def test_invalid_config_rejected_without_device(kg):
+    c = kg.micro_config(n_head=3)  # n_head * head_dim != n_embd
+    h = ctypes.c_void_p()
+    rc = kg.lib().kg_ctx_create(ctypes.byref(c), 0, ctypes.byref(h))
+    assert rc == -1 and not h
