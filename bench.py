@@ -36,7 +36,7 @@ SEED = 42
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n-seq", type=int, default=N_SEQ)
@@ -59,51 +59,56 @@ def workload_config(n_seq):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the
+    timed region (one long-running nvidia-smi process; no per-sample fork)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
         self.rows = []
-        self._stop = threading.Event()
-        self._t = None
-
-    def _run(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True,
-                                     text=True, timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([x.strip() for x in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+        self.proc = None
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.rows = [[x.strip() for x in ln.split(",")] for ln in out.splitlines() if ln.strip()]
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in self.rows if len(r) > 2 and num(r[1]) is not None]
+        mx = [num(r[2]) for r in self.rows if len(r) > 2 and num(r[2]) is not None]
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows for i in range(4)
                           if len(r) > 5 + i and r[5 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
 
 
-def cpu_baseline(n_threads=None, budget_s=15.0):
+def cpu_baseline(n_threads=None, budget_s=10.0):
     """The oracle (C++ restatement of the reference's x86 AVX2 path) on host cores."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
@@ -117,7 +122,7 @@ def cpu_baseline(n_threads=None, budget_s=15.0):
         oracle.run_batch(cfg, oracle.MODE_SPKV, w, toks[:n], threads=threads, keep_logits=False)
         done += n * T
         el = time.perf_counter() - t0
-        if el > budget_s or done >= N_SEQ * T:
+        if el > budget_s:
             break
         n = min(N_SEQ, n * 2)
     return {"value": done / el, "unit": UNIT, "cores": threads, "kind": "port",
@@ -189,8 +194,10 @@ def main():
     d_pos = torch.arange(T, dtype=torch.int32, device=dev)[:, None].expand(T, n_seq).contiguous()
     d_log = torch.empty((T, n_seq, 27), dtype=torch.float32, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(dev)          # kernels, flushes and events share this stream
+    torch.cuda.set_stream(stream)
     sp = ctypes.c_void_p(stream.cuda_stream)
+    assert sp.value, "need a non-default stream handle"
 
     def step():
         for t in range(T):

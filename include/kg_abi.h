@@ -139,8 +139,10 @@ int kg_forward_token(kg_ctx *ctx, int32_t seq, int32_t token, int32_t pos, float
 int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
                      const int32_t *start_pos, int32_t T, float *logits_out, float *probs_out);
 
-/* Device-pointer form of kg_forward_batch on `stream` (cudaStream_t). All
- * pointers are device pointers; no host synchronisation. */
+/* Device-pointer form of kg_forward_batch, enqueued on `stream` (a
+ * cudaStream_t; NULL is the CUDA legacy default stream). All pointers are
+ * device pointers; no host synchronisation. Device-side argument checks set a
+ * flag that the next host-pointer call on the context reports. */
 int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids,
                          const int32_t *tokens, const int32_t *start_pos, int32_t T,
                          float *logits_out, float *probs_out, void *stream);

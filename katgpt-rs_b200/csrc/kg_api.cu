@@ -373,8 +373,8 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
     a.start_pos = start_pos;
     a.logits = logits;
     a.probs = probs;
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    KG_CUDA(ctx, kg::launch_micro(ctx->cfg, a, s));
+    // `stream` is used as given: NULL is the CUDA legacy default stream.
+    KG_CUDA(ctx, kg::launch_micro(ctx->cfg, a, static_cast<cudaStream_t>(stream)));
     return KG_OK;
 }
 

@@ -1,0 +1,381 @@
+// kg_bf16.cu — BF16 tensor-core GEMM and the small per-token kernels of the
+// large-model path (embedding, RMSNorm, delta routing, TwELL sparse W2,
+// temperature softmax).
+//
+// The GEMM is C = A * B^T with A [M x K] activations and B [N x K] weights,
+// both K-contiguous (the reference's row-major [out, in] weight layout), f32
+// accumulation and fused epilogues (residual add, ReLU + alive count, row
+// scale). Tiles of 128 x 128 x 32 go through a 4-stage cp.async pipeline into
+// XOR-swizzled shared memory and feed mma.sync m16n8k16 via ldmatrix.
+#include <algorithm>
+
+#include "kg_bf16.cuh"
+
+namespace kg {
+namespace bf {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 4, THREADS = 256;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
+    int sz = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(sz));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 16-byte chunk (row, c) of a [rows x 32] bf16 tile: 4 chunks per row,
+// swizzled so the 8 rows an ldmatrix reads fall in distinct banks.
+__device__ __forceinline__ int swz(int row, int c) { return row * 4 + (c ^ ((row >> 1) & 3)); }
+
+__global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
+    extern __shared__ uint4 sm[];
+    uint4 *sA = sm;                         // STAGES x BM x 4 chunks
+    uint4 *sB = sm + STAGES * BM * 4;       // STAGES x BN x 4 chunks
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps, warp tile 64 x 32
+    const int bm = blockIdx.y * BM, bn = blockIdx.x * BN, z = blockIdx.z;
+    const bf16 *A = g.A + z * g.sA;
+    const bf16 *B = g.B + z * g.sB;
+    const int KT = g.K / BK;
+
+    auto load = [&](int stage, int kt) {
+        const int k0 = kt * BK;
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            int idx = tid + it * THREADS;  // 0..511
+            int row = idx >> 2, c = idx & 3;
+            int gr = bm + row;
+            const bf16 *src = A + (int64_t)min(gr, g.M - 1) * g.lda + k0 + c * 8;
+            cp_async16(smem_u32(sA + stage * BM * 4 + swz(row, c)), src, gr < g.M);
+            int gn = bn + row;
+            const bf16 *srcb = B + (int64_t)min(gn, g.N - 1) * g.ldb + k0 + c * 8;
+            cp_async16(smem_u32(sB + stage * BN * 4 + swz(row, c)), srcb, gn < g.N);
+        }
+    };
+
+    float acc[4][4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
+
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < KT) load(s, s);
+        cp_commit();
+    }
+    for (int kt = 0; kt < KT; ++kt) {
+        cp_wait<STAGES - 2>();
+        __syncthreads();
+        if (kt + STAGES - 1 < KT) load((kt + STAGES - 1) % STAGES, kt + STAGES - 1);
+        cp_commit();
+        const int st = kt % STAGES;
+        const uint4 *tA = sA + st * BM * 4, *tB = sB + st * BN * 4;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {  // two k16 steps per BK = 32
+            uint32_t af[4][4], bfr[4][2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                int row = wm * 64 + i * 16 + (lane & 15);
+                int c = kk * 2 + (lane >> 4);
+                ldsm_x4(smem_u32(tA + swz(row, c)), af[i][0], af[i][1], af[i][2], af[i][3]);
+            }
+#pragma unroll
+            for (int j2 = 0; j2 < 2; ++j2) {
+                int row = wn * 32 + j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+                int c = kk * 2 + ((lane >> 3) & 1);
+                uint32_t r0, r1, r2, r3;
+                ldsm_x4(smem_u32(tB + swz(row, c)), r0, r1, r2, r3);
+                bfr[j2 * 2][0] = r0;
+                bfr[j2 * 2][1] = r1;
+                bfr[j2 * 2 + 1][0] = r2;
+                bfr[j2 * 2 + 1][1] = r3;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) mma_bf16(acc[i][j], af[i], bfr[j][0], bfr[j][1]);
+        }
+    }
+    cp_wait<0>();
+
+    // ---- epilogue
+    const int g8 = lane >> 2, c4 = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int hrow = 0; hrow < 2; ++hrow) {
+            const int row = bm + wm * 64 + i * 16 + g8 + hrow * 8;
+            const bool rok = row < g.M;
+            int alive = 0;
+            float rs = 1.0f;
+            if (rok && (g.epi == EPI_F32_ROWSCALE || g.epi == EPI_BF16_ROWSCALE)) rs = g.row_scale[z * g.sRs + row];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int col = bn + wn * 32 + j * 8 + c4 * 2;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int cc = col + e;
+                    if (!rok || cc >= g.N) continue;
+                    float v = acc[i][j][hrow * 2 + e];
+                    switch (g.epi) {
+                        case EPI_F32: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v; break;
+                        case EPI_F32_RESID:
+                            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
+                            break;
+                        case EPI_RELU_BF16: {
+                            float r = v > 0.0f ? v : 0.0f;
+                            alive += v > 0.0f ? 1 : 0;
+                            g.Cb[z * g.sCb + (int64_t)row * g.ldcb + cc] = __float2bfloat16_rn(r);
+                            break;
+                        }
+                        case EPI_BF16: g.Cb[z * g.sCb + (int64_t)row * g.ldcb + cc] = __float2bfloat16_rn(v); break;
+                        case EPI_F32_ROWSCALE: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v * rs; break;
+                        case EPI_BF16_ROWSCALE:
+                            g.Cb[z * g.sCb + (int64_t)row * g.ldcb + cc] = __float2bfloat16_rn(v * rs);
+                            break;
+                    }
+                }
+            }
+            if (g.epi == EPI_RELU_BF16) {
+                alive += __shfl_xor_sync(0xffffffffu, alive, 1);
+                alive += __shfl_xor_sync(0xffffffffu, alive, 2);
+                if (rok && c4 == 0 && alive) atomicAdd(&g.row_alive[row], alive);
+            }
+        }
+    }
+}
+
+// ---- small kernels ---------------------------------------------------------
+
+__global__ void embed_kernel(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n,
+                             int M, float *x) {
+    const int m = blockIdx.x;
+    if (m >= M) return;
+    const bf16 *a = wte + (int64_t)tok[m] * n, *b = wpe + (int64_t)pos[m] * n;
+    for (int j = threadIdx.x; j < n; j += blockDim.x)
+        x[(int64_t)m * n + j] = __bfloat162float(a[j]) + __bfloat162float(b[j]);
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+    return s;
+}
+__device__ __forceinline__ float block_max(float v, float *red) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float s = -INFINITY;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s = fmaxf(s, red[i]);
+    return s;
+}
+
+__global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb, int twice) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const float *xr = x + (int64_t)m * n;
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) ss += xr[j] * xr[j];
+    ss = block_sum(ss, red);
+    float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
+    if (twice) {
+        float ss2 = 0.0f;
+        for (int j = threadIdx.x; j < n; j += blockDim.x) {
+            float v = xr[j] * inv;
+            ss2 += v * v;
+        }
+        ss2 = block_sum(ss2, red);
+        float inv2 = 1.0f / sqrtf(ss2 / (float)n + 1e-5f);
+        for (int j = threadIdx.x; j < n; j += blockDim.x) {
+            float v = (xr[j] * inv) * inv2;
+            if (yf) yf[(int64_t)m * n + j] = v;
+            if (yb) yb[(int64_t)m * n + j] = __float2bfloat16_rn(v);
+        }
+        return;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        float v = xr[j] * inv;
+        if (yf) yf[(int64_t)m * n + j] = v;
+        if (yb) yb[(int64_t)m * n + j] = __float2bfloat16_rn(v);
+    }
+}
+
+__global__ void to_bf16_kernel(const float *x, int64_t ldx, int n, int M, bf16 *y, int64_t ldy) {
+    const int m = blockIdx.x;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) y[(int64_t)m * ldy + j] = __float2bfloat16_rn(x[(int64_t)m * ldx + j]);
+}
+
+__global__ void flat_bf16_kernel(const float *x, int64_t count, bf16 *y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// delta routing for one token (one block per token)
+__global__ void delta_route_kernel(float *x, const float *xr, float *delta, const float *query, const float *normw,
+                                   int n, int layer) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    float *xm = x + (int64_t)m * n, *dm = delta + (int64_t)m * n;
+    const float *xrm = xr + (int64_t)m * n;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) dm[j] = dm[j] + (xm[j] - xrm[j]);
+    if ((layer & 3) != 3) return;
+    const int b = layer >> 2;  // sources: b zeroed blocks and the current block
+    __syncthreads();
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) ss += dm[j] * dm[j];
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
+    const float inv0 = 1.0f / sqrtf(1e-5f);
+    float lg = 0.0f, lz = 0.0f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        lg += normw[j] * (dm[j] * inv) * query[j];
+        lz += normw[j] * (0.0f * inv0) * query[j];
+    }
+    lg = block_sum(lg, red);
+    lz = block_sum(lz, red);
+    float mx = lg;
+    if (b > 0) mx = fmaxf(mx, lz);
+    const float eo = expf(lg - mx), ez = expf(lz - mx);
+    const float w = eo / (eo + (float)b * ez);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        xm[j] = xm[j] + w * dm[j];
+        dm[j] = 0.0f;
+    }
+}
+
+// TwELL sparse W2 for one token (one block per row); skips rows over threshold
+__global__ void twell_kernel(const bf16 *hidden, const int *row_alive, const bf16 *w2t, const float *resid,
+                             float *out, int n, int m, float threshold) {
+    extern __shared__ int s_idx[];
+    __shared__ int s_cnt;
+    const int r = blockIdx.x;
+    const int alive = row_alive[r];
+    if (!((float)alive / (float)m <= 1.0f - threshold)) return;  // dense result stands
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    const bf16 *h = hidden + (int64_t)r * m;
+    float *s_val = reinterpret_cast<float *>(s_idx + m);
+    // pack alive indices (ascending order is not needed for an f32 sum)
+    for (int j = threadIdx.x; j < m; j += blockDim.x) {
+        float v = __bfloat162float(h[j]);
+        if (v > 0.0f) {
+            int k = atomicAdd(&s_cnt, 1);
+            s_idx[k] = j;
+            s_val[k] = v;
+        }
+    }
+    __syncthreads();
+    const int na = s_cnt;
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        float acc = 0.0f;
+        for (int a = 0; a < na; ++a) acc += s_val[a] * __bfloat162float(w2t[(int64_t)s_idx[a] * n + c]);
+        out[(int64_t)r * n + c] = acc + resid[(int64_t)r * n + c];
+    }
+}
+
+__global__ void softmax_kernel(const float *logits, float *probs, int V, float inv_temp) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const float *l = logits + (int64_t)m * V;
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) mx = fmaxf(mx, l[j]);
+    mx = block_max(mx, red);
+    float s = 0.0f;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) s += expf((l[j] - mx) * inv_temp);
+    s = block_sum(s, red);
+    const float inv = 1.0f / s;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) probs[(int64_t)m * V + j] = expf((l[j] - mx) * inv_temp) * inv;
+}
+
+}  // namespace
+
+cudaError_t gemm(const Gemm &g, cudaStream_t s) {
+    if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
+    if (g.K % BK != 0 || g.lda % 8 != 0 || g.ldb % 8 != 0) return cudaErrorInvalidValue;
+    const int smem = STAGES * (BM + BN) * BK * 2;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+    gemm_kernel<<<grid, THREADS, smem, s>>>(g);
+    return cudaGetLastError();
+}
+
+cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M, float *x,
+                  cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    embed_kernel<<<M, 256, 0, s>>>(tok, pos, wte, wpe, n, M, x);
+    return cudaGetLastError();
+}
+cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bool twice, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    rmsnorm_kernel<<<M, 256, 0, s>>>(x, n, M, yf, yb, twice ? 1 : 0);
+    return cudaGetLastError();
+}
+cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, int64_t ldy, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    to_bf16_kernel<<<M, 256, 0, s>>>(x, ldx, n, M, y, ldy);
+    return cudaGetLastError();
+}
+cudaError_t f32_to_bf16_flat(const float *x, int64_t count, bf16 *y, cudaStream_t s) {
+    if (count <= 0) return cudaSuccess;
+    flat_bf16_kernel<<<1184, 256, 0, s>>>(x, count, y);
+    return cudaGetLastError();
+}
+cudaError_t delta_route(float *x, const float *xr, float *delta, const float *query, const float *normw, int n,
+                        int M, int layer, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    delta_route_kernel<<<M, 256, 0, s>>>(x, xr, delta, query, normw, n, layer);
+    return cudaGetLastError();
+}
+cudaError_t twell_sparse_w2(const bf16 *hidden, const int *row_alive, const bf16 *w2t, const float *resid, float *out,
+                            int n, int m, int M, float threshold, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    const size_t smem = (size_t)m * 8;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(twell_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    twell_kernel<<<M, 256, smem, s>>>(hidden, row_alive, w2t, resid, out, n, m, threshold);
+    return cudaGetLastError();
+}
+cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    softmax_kernel<<<M, 256, 0, s>>>(logits, probs, V, inv_temp);
+    return cudaGetLastError();
+}
+
+}  // namespace bf
+}  // namespace kg

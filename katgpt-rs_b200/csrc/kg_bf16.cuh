@@ -1,0 +1,67 @@
+// kg_bf16.cuh — interfaces of the BF16 tensor-core path (kg_bf16.cu, kg_attn.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace kg {
+namespace bf {
+
+using bf16 = __nv_bfloat16;
+
+enum Epi : int {
+    EPI_F32 = 0,        // C = acc
+    EPI_F32_RESID = 1,  // C = acc + R
+    EPI_RELU_BF16 = 2,  // Cb = bf16(max(acc, 0)); row_alive[row] += #(acc > 0)
+    EPI_BF16 = 3,       // Cb = bf16(acc)
+    EPI_F32_ROWSCALE = 4,  // C = acc * row_scale[row]
+    EPI_BF16_ROWSCALE = 5  // Cb = bf16(acc * row_scale[row])
+};
+
+// C[M x N] = A[M x K] * B[N x K]^T (+ epilogue); A, B bf16 row-major (K contiguous).
+// Batched over blockIdx.z with element strides sA/sB/sC/sR/sCb/sRs.
+struct Gemm {
+    const bf16 *A;
+    int64_t lda, sA;
+    const bf16 *B;
+    int64_t ldb, sB;
+    int M, N, K, batch;
+    int epi;
+    float *C;
+    int64_t ldc, sC;
+    const float *R;
+    int64_t ldr, sR;
+    bf16 *Cb;
+    int64_t ldcb, sCb;
+    int *row_alive;
+    const float *row_scale;
+    int64_t sRs;
+};
+
+cudaError_t gemm(const Gemm &g, cudaStream_t s);
+
+// x[m, :] = wte[tok[m], :] + wpe[pos[m], :] (bf16 tables, f32 out)
+cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M,
+                  float *x, cudaStream_t s);
+// per row: y = x / sqrt(mean(x^2) + 1e-5); `twice` applies it twice (sp_kv double norm).
+// Writes f32 (if yf) and bf16 (if yb). In-place allowed (yf == x).
+cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bool twice, cudaStream_t s);
+// f32 -> bf16 (strided rows)
+cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, int64_t ldy, cudaStream_t s);
+// round a flat f32 array to bf16 (nearest-even)
+cudaError_t f32_to_bf16_flat(const float *x, int64_t count, bf16 *y, cudaStream_t s);
+// delta routing (src/transformer.rs:1707-1765, 2129-2158) for one layer l:
+// delta += x - xr; at l % 4 == 3 route over b = l/4 zeroed blocks + delta, then zero delta.
+cudaError_t delta_route(float *x, const float *xr, float *delta, const float *query, const float *normw,
+                        int n, int M, int layer, cudaStream_t s);
+// TwELL (math.rs:315-355): for rows whose alive fraction <= 1 - threshold, recompute
+// out = sum over alive j of h[j] * W2[:, j] + resid (gather over W2^T rows) in f32.
+cudaError_t twell_sparse_w2(const bf16 *hidden, const int *row_alive, const bf16 *w2t, const float *resid,
+                            float *out, int n, int m, int M, float threshold, cudaStream_t s);
+// softmax_scaled (math.rs:36-50) per row of logits [M x V]
+cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s);
+
+}  // namespace bf
+}  // namespace kg

@@ -127,6 +127,27 @@ __device__ __forceinline__ float sum_rt(const float (&x)[MAXN], int n) {
     return sum;
 }
 
+// simd_sum_f32 over x[0..n) for n < 32 (no 32-wide chunk): sum = hsum(0),
+// then one accumulator over 8-chunks, then the scalar tail.
+template <int MAXN>
+__device__ __forceinline__ float sum_small(const float *x, int n) {
+    static_assert(MAXN < 32, "sum_small handles n < 32");
+    float r[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) r[l] = 0.0f;
+    const int rem = n / 8;
+#pragma unroll 1
+    for (int c = 0; c < rem; ++c)
+#pragma unroll
+        for (int l = 0; l < 8; ++l) r[l] = r[l] + x[8 * c + l];
+    float z[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    float sum = hsum8(z);
+    sum = sum + hsum8(r);
+#pragma unroll 1
+    for (int i = rem * 8; i < n; ++i) sum = sum + x[i];
+    return sum;
+}
+
 // ---- Cephes exp (crates/katgpt-types/src/simd/activations.rs:18-20,189-221,405-480,660-748)
 __device__ __forceinline__ float cephes_poly(float g) {
     float p6 = 1.0f + g * (1.0f / 6.0f);

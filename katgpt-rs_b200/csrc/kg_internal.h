@@ -50,6 +50,10 @@ cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t
 cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
                              const float *bnd, uint8_t *packed, int64_t packed_stride,
                              float *norms, int64_t norm_stride, cudaStream_t s);
+// Same, reading row v at x + v*ldx and writing arena row (slot[v]*L + layer)*B + pos[v].
+cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
+                              const float *bnd, uint8_t *packed, int64_t pstride, float *norms, int64_t nstride,
+                              const int32_t *slot, const int32_t *pos, int L, int B, int layer, cudaStream_t s);
 
 }  // namespace kg
 

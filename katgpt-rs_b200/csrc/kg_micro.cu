@@ -23,6 +23,8 @@
 //   TurboQuant store/deq  src/turboquant/kv_cache.rs:156-317
 //   delta routing         src/transformer.rs:1707-1765, 2129-2158
 //   softmax_scaled        crates/katgpt-types/src/math.rs:36-50
+#include <algorithm>
+
 #include "kg_exact.cuh"
 #include "kg_internal.h"
 
@@ -102,7 +104,7 @@ __device__ __forceinline__ void rmsnorm(float (&x)[N]) {
 }
 
 template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE>
-__global__ void __launch_bounds__(128) micro_forward(const MicroArgs p) {
+__global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     constexpr int KVD = NKV * HD;
     constexpr int PH = (N / 4 > 16) ? N / 4 : 16;
     extern __shared__ float4 sm4[];
@@ -116,7 +118,11 @@ __global__ void __launch_bounds__(128) micro_forward(const MicroArgs p) {
     const int T = p.T;
     const int SB = blockDim.x / T;
     const int sl = threadIdx.x / T, tl = threadIdx.x - sl * T;
-    const int i = blockIdx.x * SB + sl;
+    const int n_groups = (p.n_seq + SB - 1) / SB;
+    float *scs = sm + p.pack_floats + threadIdx.x * (BLK + 1);  // per-thread score row
+    for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
+    __syncthreads();  // previous group's attention reads are done
+    const int i = grp * SB + sl;
     bool active = (sl < SB) && (i < p.n_seq);
     int slot = 0, pos = 0, tok = 0;
     if (active) {
@@ -202,72 +208,69 @@ __global__ void __launch_bounds__(128) micro_forward(const MicroArgs p) {
         float att[N];
         const int tn = pos + 1;
         const float *Kb = p.Kf + row * KVD, *Vb = p.Vf + row * KVD;
-#pragma unroll
+#pragma unroll 1
         for (int h = 0; h < NH; ++h) {
             const int g = h * NKV / NH;
-            float sc[BLK];
-            if constexpr (MODE != MODE_SPKV) {
-                // attention_head: dot, scale, max, shift, Cephes exp, sum, normalise, P.V
+            float qh[HD];
 #pragma unroll
-                for (int t = 0; t < BLK; ++t)
-                    sc[t] = (active && t < tn) ? kgx::dot<HD>(q + h * HD, Kb + t * KVD + g * HD) : 0.0f;
+            for (int d = 0; d < HD; ++d) qh[d] = q[h * HD + d];
+            float o[HD];
 #pragma unroll
-                for (int t = 0; t < BLK; ++t) sc[t] = sc[t] * scale;
-                float mx = sc[0];
-#pragma unroll
-                for (int t = 1; t < BLK; ++t)
-                    if (t < tn && sc[t] > mx) mx = sc[t];
-#pragma unroll
-                for (int t = 0; t < BLK; ++t) sc[t] = sc[t] + (-mx);
-                const int body = tn / 8 * 8;
-#pragma unroll
-                for (int t = 0; t < BLK; ++t)
-                    sc[t] = t < body ? kgx::cephes_lane(sc[t], true) : kgx::cephes_scalar(sc[t]);
-                float sum = kgx::sum_rt<BLK>(sc, tn);
-                float inv = 1.0f / sum;
-#pragma unroll
-                for (int t = 0; t < BLK; ++t) sc[t] = sc[t] * inv;
-                float o[HD];
-#pragma unroll
-                for (int d = 0; d < HD; ++d) o[d] = 0.0f;
-#pragma unroll
-                for (int t = 0; t < BLK; ++t)
-                    if (active && t < tn) {
+            for (int d = 0; d < HD; ++d) o[d] = 0.0f;
+            if (active) {
+                if constexpr (MODE != MODE_SPKV) {
+                    // attention_head: dot, scale, max, shift, Cephes exp, sum, normalise, P.V
+                    float mx = 0.0f;
+#pragma unroll 1
+                    for (int t = 0; t < tn; ++t) {
+                        float sv = kgx::dot<HD>(qh, Kb + t * KVD + g * HD) * scale;
+                        scs[t] = sv;
+                        mx = (t == 0 || sv > mx) ? sv : mx;
+                    }
+                    const int body = tn / 8 * 8;
+#pragma unroll 1
+                    for (int t = 0; t < tn; ++t) {
+                        float e = scs[t] + (-mx);
+                        scs[t] = t < body ? kgx::cephes_lane(e, true) : kgx::cephes_scalar(e);
+                    }
+                    float inv = 1.0f / kgx::sum_small<BLK>(scs, tn);
+#pragma unroll 1
+                    for (int t = 0; t < tn; ++t) {
+                        const float pt = scs[t] * inv;
                         const float *vr = Vb + t * KVD + g * HD;
 #pragma unroll
                         for (int d = 0; d < HD; ++d)  // fused_scale_acc: fma body, mul+add tail
-                            o[d] = (d < HD / 8 * 8) ? fmaf(sc[t], vr[d], o[d]) : o[d] + sc[t] * vr[d];
+                            o[d] = (d < HD / 8 * 8) ? fmaf(pt, vr[d], o[d]) : o[d] + pt * vr[d];
                     }
-#pragma unroll
-                for (int d = 0; d < HD; ++d) att[h * HD + d] = o[d];
-            } else {
-                // attention_head_core<GateBias>: bias 0 for every position (each
-                // written position is retained; block_size <= window)
-                float mx = -INFINITY;
-#pragma unroll
-                for (int t = 0; t < BLK; ++t) {
-                    float s = (active && t < tn) ? kgx::dot<HD>(q + h * HD, Kb + t * KVD + g * HD) * scale + 0.0f : 0.0f;
-                    sc[t] = s;
-                    if (t < tn) mx = kgx::fmax_rs(mx, s);
-                }
-                float sum = 0.0f;
-#pragma unroll
-                for (int t = 0; t < BLK; ++t)
-                    if (t < tn) {
-                        float e = kgx::expf_libm(sc[t] - mx);
-                        sc[t] = e;
+                } else {
+                    // attention_head_core<GateBias>: bias 0 for every position (each
+                    // written position is retained; block_size <= window)
+                    float mx = -INFINITY;
+#pragma unroll 1
+                    for (int t = 0; t < tn; ++t) {
+                        float sv = kgx::dot<HD>(qh, Kb + t * KVD + g * HD) * scale + 0.0f;
+                        scs[t] = sv;
+                        mx = kgx::fmax_rs(mx, sv);
+                    }
+                    float sum = 0.0f;
+#pragma unroll 1
+                    for (int t = 0; t < tn; ++t) {
+                        float e = kgx::expf_libm(scs[t] - mx);
+                        scs[t] = e;
                         sum = sum + e;
                     }
-                float inv = 1.0f / sum;
+                    const float inv = 1.0f / sum;
+#pragma unroll 1
+                    for (int t = 0; t < tn; ++t) {
+                        const float pt = scs[t] * inv;
+                        const float *vr = Vb + t * KVD + g * HD;
 #pragma unroll
-                for (int d = 0; d < HD; ++d) {
-                    float o = 0.0f;
-#pragma unroll
-                    for (int t = 0; t < BLK; ++t)
-                        if (active && t < tn) o = o + (sc[t] * inv) * Vb[t * KVD + g * HD + d];
-                    att[h * HD + d] = o;
+                        for (int d = 0; d < HD; ++d) o[d] = o[d] + pt * vr[d];
+                    }
                 }
             }
+#pragma unroll
+            for (int d = 0; d < HD; ++d) att[h * HD + d] = o[d];
         }
 
         // ---- output projection + residual
@@ -389,7 +392,7 @@ __global__ void __launch_bounds__(128) micro_forward(const MicroArgs p) {
     }
 
     // ---- lm_head (+ softmax_scaled)
-    if (!active) return;
+    if (!active) continue;
     const float *lm = sm + p.off_lm;
     float lg[VOC];
 #pragma unroll
@@ -437,6 +440,7 @@ __global__ void __launch_bounds__(128) micro_forward(const MicroArgs p) {
 #pragma unroll
         for (int r = 0; r < VOC; ++r) p.probs[orow + r] = lg[r] * inv;
     }
+    }  // sequence groups
 }
 
 template <int MODE>
@@ -445,11 +449,20 @@ cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     const int SB = 128 / T;
     const int threads = SB * T;
     const int blocks = (a.n_seq + SB - 1) / SB;
-    const size_t smem = (size_t)a.pack_floats * sizeof(float);
+    const size_t smem = ((size_t)a.pack_floats + 128 * 17) * sizeof(float);
     auto kfn = micro_forward<16, 4, 4, 4, 64, 27, 16, MODE>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    kfn<<<blocks, threads, smem, s>>>(a);
+    static int n_sm = 0, per_sm = 0;
+    if (!n_sm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, 128, smem);
+        if (per_sm < 1) per_sm = 1;
+    }
+    const int grid = std::min(blocks, n_sm * per_sm);
+    kfn<<<grid, threads, smem, s>>>(a);
     return cudaGetLastError();
 }
 

@@ -120,18 +120,21 @@ __global__ void transpose_sq(int dim, const float *a, float *t) {
 }
 
 // Encode: one warp per vector, rows in sequence. smem per warp: xn[dim] + codes[dim].
-__global__ void tq_encode_warp(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
+__global__ void tq_encode_warp(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
                                const float *bnd, uint8_t *packed, int64_t pstride, float *norms,
-                               int64_t nstride) {
+                               int64_t nstride, const int32_t *slot, const int32_t *pos, int L, int B,
+                               int layer) {
     extern __shared__ float smf[];
     const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x & 31;
     float *xn = smf + (size_t)w * dim;
     uint8_t *cd = reinterpret_cast<uint8_t *>(smf + (size_t)warps * dim) + (size_t)w * dim;
     const int nb = (1 << bits) - 1;
     for (int64_t v = (int64_t)blockIdx.x * warps + w; v < n_vec; v += (int64_t)gridDim.x * warps) {
-        const float *xv = x + v * dim;
+        const float *xv = x + v * ldx;
+        // destination row: v itself, or the arena row of token v
+        const int64_t drow = slot ? ((int64_t)slot[v] * L + layer) * B + pos[v] : v;
         float norm = sqrtf(warp_sum_sq(xv, dim, 1));
-        if (lane == 0) norms[v * nstride] = norm;
+        if (lane == 0) norms[drow * nstride] = norm;
         if (norm < 1e-8f) continue;  // indices untouched (reference quirk)
         const float inv = 1.0f / norm;
         for (int k = lane; k < dim; k += 32) xn[k] = xv[k] * inv;
@@ -145,7 +148,7 @@ __global__ void tq_encode_warp(int dim, int bits, int64_t n_vec, const float *x,
             }
         }
         __syncwarp();
-        uint8_t *out = packed + v * pstride;
+        uint8_t *out = packed + drow * pstride;
         if (bits == 2) {
             for (int b = lane; b < (dim + 3) / 4; b += 32) {
                 uint8_t o = 0;
@@ -209,6 +212,13 @@ cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t
 cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
                              const float *bnd, uint8_t *packed, int64_t pstride, float *norms,
                              int64_t nstride, cudaStream_t s) {
+    return tq_encode_scatter(dim, bits, n_vec, x, dim, rot, bnd, packed, pstride, norms, nstride, nullptr,
+                             nullptr, 0, 0, 0, s);
+}
+
+cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
+                              const float *bnd, uint8_t *packed, int64_t pstride, float *norms, int64_t nstride,
+                              const int32_t *slot, const int32_t *pos, int L, int B, int layer, cudaStream_t s) {
     if (n_vec <= 0) return cudaSuccess;
     int warps = 4;
     size_t smem = (size_t)warps * dim * (sizeof(float) + 1);
@@ -221,8 +231,8 @@ cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, c
     if (e != cudaSuccess) return e;
     int64_t blocks = (n_vec + warps - 1) / warps;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    tq_encode_warp<<<(unsigned)blocks, warps * 32, smem, s>>>(dim, bits, n_vec, x, rot, bnd, packed,
-                                                             pstride, norms, nstride);
+    tq_encode_warp<<<(unsigned)blocks, warps * 32, smem, s>>>(dim, bits, n_vec, x, ldx, rot, bnd, packed,
+                                                             pstride, norms, nstride, slot, pos, L, B, layer);
     return cudaGetLastError();
 }
 
