@@ -117,6 +117,14 @@ int kg_upload_weights(kg_ctx *ctx, const float *host_weights, int64_t count);
 int kg_upload_weights_dev(kg_ctx *ctx, const float *dev_weights, int64_t count);
 /* InferenceBackend::is_compiled */
 int kg_is_compiled(const kg_ctx *ctx);
+/* Synthetic benchmark weights for the bf16 path, generated on the device:
+ * every bf16 tensor ~ N(0, std_) from a counter-based generator keyed by
+ * `seed`, delta-routing query 0 and norm 1 (no reference counterpart: the
+ * reference draws its weights on the host with Rng, weights.rs:76-177). */
+int kg_random_weights(kg_ctx *ctx, uint64_t seed, float std_);
+/* Copy the context's weights back to host f32 in the flat layout (bf16 path),
+ * e.g. so a CPU checker runs on exactly the device's bf16-rounded values. */
+int kg_download_weights(kg_ctx *ctx, float *host_out, int64_t count);
 
 /* ---- sequences (InferenceBackend::reset) ---- */
 

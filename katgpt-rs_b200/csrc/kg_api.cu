@@ -238,8 +238,15 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
         kg::predictor_weights(ctx->n, ctx->ph, ctx->nkv, c.spkv_init_bias, ctx->h_pred);
 
     if (!ctx->micro) {
-        // Codec-only context: TurboQuant tables and the encoder are available;
-        // forward entry points return KG_ERR_UNSUPPORTED for this shape.
+        std::string bwhy;
+        if (kg::big_supported(c, bwhy) == 0) {
+            ctx->big_path = true;
+            e = kg::big_init(ctx);
+            if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "bf16 path init"));
+            if ((rc = kg_seq_reset_all(ctx))) return bail(rc);
+        }
+        // Otherwise a codec-only context: TurboQuant tables and the encoder
+        // work; forward entry points return KG_ERR_UNSUPPORTED for this shape.
         *out = ctx;
         return KG_OK;
     }
@@ -302,6 +309,25 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
 
 int kg_upload_weights(kg_ctx *ctx, const float *w, int64_t count) {
     if (!ctx || !w) return KG_ERR_INVALID_ARG;
+    if (ctx->big_path) {
+        if (count != ctx->w_count) return fail(ctx, KG_ERR_INVALID_WEIGHTS, "weight count mismatch");
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        const int64_t chunk = (int64_t)64 << 20;  // floats per staged copy
+        int rc = ensure_stage(ctx, (size_t)chunk * 4);
+        if (rc) return rc;
+        float *st = static_cast<float *>(ctx->stage);
+        const int64_t nbf = ctx->big.nbf;
+        for (int64_t off = 0; off < nbf; off += chunk) {
+            const int64_t cnt = std::min(chunk, nbf - off);
+            KG_CUDA(ctx, cudaMemcpyAsync(st, w + off, cnt * 4, cudaMemcpyHostToDevice, ctx->stream));
+            KG_CUDA(ctx, kg::big_upload_chunk(ctx, st, off, cnt));
+            KG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        }
+        KG_CUDA(ctx, cudaMemcpyAsync(st, w + nbf, (count - nbf) * 4, cudaMemcpyHostToDevice, ctx->stream));
+        KG_CUDA(ctx, kg::big_finish_upload(ctx, st));
+        ctx->compiled = true;
+        return KG_OK;
+    }
     if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
     if (count != ctx->w_count)
         return fail(ctx, KG_ERR_INVALID_WEIGHTS,
@@ -315,6 +341,14 @@ int kg_upload_weights(kg_ctx *ctx, const float *w, int64_t count) {
 
 int kg_upload_weights_dev(kg_ctx *ctx, const float *w, int64_t count) {
     if (!ctx || !w) return KG_ERR_INVALID_ARG;
+    if (ctx->big_path) {
+        if (count != ctx->w_count) return fail(ctx, KG_ERR_INVALID_WEIGHTS, "weight count mismatch");
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        KG_CUDA(ctx, kg::big_upload_chunk(ctx, w, 0, ctx->big.nbf));
+        KG_CUDA(ctx, kg::big_finish_upload(ctx, w + ctx->big.nbf));
+        ctx->compiled = true;
+        return KG_OK;
+    }
     if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
     if (count != ctx->w_count) return fail(ctx, KG_ERR_INVALID_WEIGHTS, "weight count mismatch");
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
@@ -324,8 +358,45 @@ int kg_upload_weights_dev(kg_ctx *ctx, const float *w, int64_t count) {
     return KG_OK;
 }
 
+int kg_random_weights(kg_ctx *ctx, uint64_t seed, float std_) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (!ctx->big_path) return fail(ctx, KG_ERR_UNSUPPORTED, "synthetic weights are for the bf16 path");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    KG_CUDA(ctx, kg::big_random_weights(ctx, seed, std_));
+    ctx->compiled = true;
+    return KG_OK;
+}
+
+int kg_download_weights(kg_ctx *ctx, float *out, int64_t count) {
+    if (!ctx || !out) return KG_ERR_INVALID_ARG;
+    if (!ctx->big_path) return fail(ctx, KG_ERR_UNSUPPORTED, "download is for the bf16 path");
+    if (count != ctx->w_count) return fail(ctx, KG_ERR_INVALID_ARG, "weight count mismatch");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int64_t chunk = (int64_t)64 << 20;
+    int rc = ensure_stage(ctx, (size_t)chunk * 4);
+    if (rc) return rc;
+    float *st = static_cast<float *>(ctx->stage);
+    const int64_t nbf = ctx->big.nbf;
+    for (int64_t off = 0; off < nbf; off += chunk) {
+        const int64_t cnt = std::min(chunk, nbf - off);
+        KG_CUDA(ctx, kg::big_download(ctx, st, off, cnt));
+        KG_CUDA(ctx, cudaMemcpyAsync(out + off, st, cnt * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        KG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    }
+    KG_CUDA(ctx, cudaMemcpyAsync(out + nbf, ctx->big.dq, ctx->L * ctx->n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    KG_CUDA(ctx, cudaMemcpyAsync(out + nbf + ctx->L * ctx->n, ctx->big.dn, ctx->L * ctx->n * 4,
+                                 cudaMemcpyDeviceToHost, ctx->stream));
+    KG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return KG_OK;
+}
+
 int kg_seq_reset(kg_ctx *ctx, int32_t seq) {
     if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs) return KG_ERR_INVALID_ARG;
+    if (ctx->big_path) {
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        KG_CUDA(ctx, kg::big_reset(ctx, seq, 1));
+        return KG_OK;
+    }
     if (!ctx->micro) return KG_OK;
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t rows = (size_t)ctx->L * ctx->B, r0 = (size_t)seq * rows;
@@ -342,6 +413,12 @@ int kg_seq_reset(kg_ctx *ctx, int32_t seq) {
 
 int kg_seq_reset_all(kg_ctx *ctx) {
     if (!ctx) return KG_ERR_INVALID_ARG;
+    if (ctx->big_path) {
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        KG_CUDA(ctx, kg::big_reset(ctx, 0, ctx->cfg.max_seqs));
+        KG_CUDA(ctx, cudaMemset(ctx->d_err, 0, 4));
+        return KG_OK;
+    }
     if (!ctx->micro) return KG_OK;
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t rows = (size_t)ctx->cfg.max_seqs * ctx->L * ctx->B;
@@ -359,11 +436,20 @@ int kg_seq_reset_all(kg_ctx *ctx) {
 int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
                          const int32_t *start_pos, int32_t T, float *logits, float *probs, void *stream) {
     if (!ctx) return KG_ERR_INVALID_ARG;
-    if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
+    if (!ctx->micro && !ctx->big_path) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
     if (!ctx->compiled) return fail(ctx, KG_ERR_NOT_COMPILED, "weights not uploaded");
-    if (n_seq < 0 || T < 1 || T > ctx->B || T > 16 || !seq_ids || !tokens)
+    if (n_seq < 0 || T < 1 || T > ctx->B || (ctx->micro && T > 16) || !seq_ids || !tokens)
         return fail(ctx, KG_ERR_INVALID_ARG, "bad batch shape");
     if (n_seq == 0) return KG_OK;
+    if (ctx->big_path) {
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        cudaError_t e = kg::big_forward(ctx, n_seq, seq_ids, tokens, start_pos, T, logits, probs,
+                                        static_cast<cudaStream_t>(stream));
+        if (e == cudaErrorNotSupported)
+            return fail(ctx, KG_ERR_UNSUPPORTED, "bf16 path: a multi-position call must start at position 0");
+        KG_CUDA(ctx, e);
+        return KG_OK;
+    }
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     kg::MicroArgs a = ctx->margs;
     a.n_seq = n_seq;
@@ -393,6 +479,12 @@ int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const i
     }
     for (int64_t i = 0; i < (int64_t)n_seq * T; ++i)
         if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, KG_ERR_INVALID_ARG, "token out of range");
+    if (ctx->big_path && T > 1 && start_pos) {
+        for (int32_t i = 0; i < n_seq; ++i)
+            if (start_pos[i] != 0)
+                return fail(ctx, KG_ERR_UNSUPPORTED, "bf16 path: a multi-position call must start at position 0");
+        start_pos = nullptr;
+    }
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t b_ids = align256(n_seq * 4), b_tok = align256((size_t)n_seq * T * 4);
     const size_t b_out = align256((size_t)n_seq * T * ctx->V * 4);
@@ -467,9 +559,22 @@ int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint
 
 int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *kcodes, uint8_t *vcodes,
                 float *norms) {
-    if (ctx && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no KV arena for this model shape");
     if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs || layer < 0 || layer >= ctx->L || pos < 0 || pos >= ctx->B)
         return KG_ERR_INVALID_ARG;
+    if (ctx->big_path) {
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        const int64_t row = ((int64_t)seq * ctx->L + layer) * ctx->B + pos;
+        cudaStream_t s = ctx->stream;
+        if (kcodes) KG_CUDA(ctx, cudaMemcpyAsync(kcodes, ctx->big.kcodes + row * ctx->kpl, ctx->kpl, cudaMemcpyDeviceToHost, s));
+        if (vcodes) KG_CUDA(ctx, cudaMemcpyAsync(vcodes, ctx->big.vcodes + row * ctx->vpl, ctx->vpl, cudaMemcpyDeviceToHost, s));
+        if (norms) {
+            KG_CUDA(ctx, cudaMemcpyAsync(norms, ctx->big.knorm + row, 4, cudaMemcpyDeviceToHost, s));
+            KG_CUDA(ctx, cudaMemcpyAsync(norms + 1, ctx->big.vnorm + row, 4, cudaMemcpyDeviceToHost, s));
+        }
+        KG_CUDA(ctx, cudaStreamSynchronize(s));
+        return KG_OK;
+    }
+    if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no KV arena for this model shape");
     if (ctx->cfg.kv_mode == KG_KV_F32) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const int64_t row = ((int64_t)seq * ctx->L + layer) * ctx->B + pos;

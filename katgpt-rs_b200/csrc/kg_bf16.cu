@@ -33,28 +33,57 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<bf16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <typename T>
+__device__ __forceinline__ T to_t(float v);
+template <>
+__device__ __forceinline__ bf16 to_t<bf16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half to_t<__half>(float v) { return __float2half_rn(v); }
+template <typename T>
+__device__ __forceinline__ float from_t(T v);
+template <>
+__device__ __forceinline__ float from_t<bf16>(bf16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float from_t<__half>(__half v) { return __half2float(v); }
 
-// 16-byte chunk (row, c) of a [rows x 32] bf16 tile: 4 chunks per row,
+// 16-byte chunk (row, c) of a [rows x 32] 16-bit tile: 4 chunks per row,
 // swizzled so the 8 rows an ldmatrix reads fall in distinct banks.
 __device__ __forceinline__ int swz(int row, int c) { return row * 4 + (c ^ ((row >> 1) & 3)); }
 
+template <typename T, bool SA, bool SB>
 __global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
     extern __shared__ uint4 sm[];
-    uint4 *sA = sm;                         // STAGES x BM x 4 chunks
-    uint4 *sB = sm + STAGES * BM * 4;       // STAGES x BN x 4 chunks
+    constexpr int TA = BM * 4, TB = BN * 4;  // 16-byte chunks per tile
+    constexpr int PER_STAGE = TA * (SA ? 2 : 1) + TB * (SB ? 2 : 1);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps, warp tile 64 x 32
     const int bm = blockIdx.y * BM, bn = blockIdx.x * BN, z = blockIdx.z;
-    const bf16 *A = g.A + z * g.sA;
-    const bf16 *B = g.B + z * g.sB;
+    const T *A = static_cast<const T *>(g.A) + z * g.sA;
+    const T *A2 = SA ? static_cast<const T *>(g.A2) + z * g.sA : nullptr;
+    const T *B = static_cast<const T *>(g.B) + z * g.sB;
+    const T *B2 = SB ? static_cast<const T *>(g.B2) + z * g.sB : nullptr;
     const int KT = g.K / BK;
+
+    auto tileA = [&](int st, int part) { return sm + st * PER_STAGE + part * TA; };
+    auto tileB = [&](int st, int part) { return sm + st * PER_STAGE + TA * (SA ? 2 : 1) + part * TB; };
 
     auto load = [&](int stage, int kt) {
         const int k0 = kt * BK;
@@ -63,11 +92,13 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
             int idx = tid + it * THREADS;  // 0..511
             int row = idx >> 2, c = idx & 3;
             int gr = bm + row;
-            const bf16 *src = A + (int64_t)min(gr, g.M - 1) * g.lda + k0 + c * 8;
-            cp_async16(smem_u32(sA + stage * BM * 4 + swz(row, c)), src, gr < g.M);
+            const int64_t ao = (int64_t)min(gr, g.M - 1) * g.lda + k0 + c * 8;
+            cp_async16(smem_u32(tileA(stage, 0) + swz(row, c)), A + ao, gr < g.M);
+            if (SA) cp_async16(smem_u32(tileA(stage, 1) + swz(row, c)), A2 + ao, gr < g.M);
             int gn = bn + row;
-            const bf16 *srcb = B + (int64_t)min(gn, g.N - 1) * g.ldb + k0 + c * 8;
-            cp_async16(smem_u32(sB + stage * BN * 4 + swz(row, c)), srcb, gn < g.N);
+            const int64_t bo = (int64_t)min(gn, g.N - 1) * g.ldb + k0 + c * 8;
+            cp_async16(smem_u32(tileB(stage, 0) + swz(row, c)), B + bo, gn < g.N);
+            if (SB) cp_async16(smem_u32(tileB(stage, 1) + swz(row, c)), B2 + bo, gn < g.N);
         }
     };
 
@@ -90,36 +121,44 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
         if (kt + STAGES - 1 < KT) load((kt + STAGES - 1) % STAGES, kt + STAGES - 1);
         cp_commit();
         const int st = kt % STAGES;
-        const uint4 *tA = sA + st * BM * 4, *tB = sB + st * BN * 4;
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {  // two k16 steps per BK = 32
-            uint32_t af[4][4], bfr[4][2];
+            uint32_t bfr[2][4][2];
+#pragma unroll
+            for (int part = 0; part < (SB ? 2 : 1); ++part)
+#pragma unroll
+                for (int j2 = 0; j2 < 2; ++j2) {
+                    int row = wn * 32 + j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+                    int c = kk * 2 + ((lane >> 3) & 1);
+                    uint32_t r0, r1, r2, r3;
+                    ldsm_x4(smem_u32(tileB(st, part) + swz(row, c)), r0, r1, r2, r3);
+                    bfr[part][j2 * 2][0] = r0;
+                    bfr[part][j2 * 2][1] = r1;
+                    bfr[part][j2 * 2 + 1][0] = r2;
+                    bfr[part][j2 * 2 + 1][1] = r3;
+                }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                int row = wm * 64 + i * 16 + (lane & 15);
-                int c = kk * 2 + (lane >> 4);
-                ldsm_x4(smem_u32(tA + swz(row, c)), af[i][0], af[i][1], af[i][2], af[i][3]);
+                uint32_t af[4], af2[4];
+                {
+                    int row = wm * 64 + i * 16 + (lane & 15);
+                    int c = kk * 2 + (lane >> 4);
+                    ldsm_x4(smem_u32(tileA(st, 0) + swz(row, c)), af[0], af[1], af[2], af[3]);
+                    if (SA) ldsm_x4(smem_u32(tileA(st, 1) + swz(row, c)), af2[0], af2[1], af2[2], af2[3]);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    mma16816<T>(acc[i][j], af, bfr[0][j][0], bfr[0][j][1]);
+                    if (SA) mma16816<T>(acc[i][j], af2, bfr[0][j][0], bfr[0][j][1]);
+                    if (SB) mma16816<T>(acc[i][j], af, bfr[1][j][0], bfr[1][j][1]);
+                }
             }
-#pragma unroll
-            for (int j2 = 0; j2 < 2; ++j2) {
-                int row = wn * 32 + j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
-                int c = kk * 2 + ((lane >> 3) & 1);
-                uint32_t r0, r1, r2, r3;
-                ldsm_x4(smem_u32(tB + swz(row, c)), r0, r1, r2, r3);
-                bfr[j2 * 2][0] = r0;
-                bfr[j2 * 2][1] = r1;
-                bfr[j2 * 2 + 1][0] = r2;
-                bfr[j2 * 2 + 1][1] = r3;
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) mma_bf16(acc[i][j], af[i], bfr[j][0], bfr[j][1]);
         }
     }
     cp_wait<0>();
 
     // ---- epilogue
+    T *Cb = static_cast<T *>(g.Cb), *Cb2 = static_cast<T *>(g.Cb2);
     const int g8 = lane >> 2, c4 = lane & 3;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -129,7 +168,7 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
             const bool rok = row < g.M;
             int alive = 0;
             float rs = 1.0f;
-            if (rok && (g.epi == EPI_F32_ROWSCALE || g.epi == EPI_BF16_ROWSCALE)) rs = g.row_scale[z * g.sRs + row];
+            if (rok && (g.epi == EPI_F32_ROWSCALE || g.epi == EPI_OUT_ROWSCALE)) rs = g.row_scale[z * g.sRs + row];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int col = bn + wn * 32 + j * 8 + c4 * 2;
@@ -138,26 +177,28 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
                     const int cc = col + e;
                     if (!rok || cc >= g.N) continue;
                     float v = acc[i][j][hrow * 2 + e];
+                    const int64_t ob = z * g.sCb + (int64_t)row * g.ldcb + cc;
                     switch (g.epi) {
                         case EPI_F32: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v; break;
                         case EPI_F32_RESID:
                             g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
                             break;
-                        case EPI_RELU_BF16: {
-                            float r = v > 0.0f ? v : 0.0f;
-                            alive += v > 0.0f ? 1 : 0;
-                            g.Cb[z * g.sCb + (int64_t)row * g.ldcb + cc] = __float2bfloat16_rn(r);
-                            break;
-                        }
-                        case EPI_BF16: g.Cb[z * g.sCb + (int64_t)row * g.ldcb + cc] = __float2bfloat16_rn(v); break;
                         case EPI_F32_ROWSCALE: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v * rs; break;
-                        case EPI_BF16_ROWSCALE:
-                            g.Cb[z * g.sCb + (int64_t)row * g.ldcb + cc] = __float2bfloat16_rn(v * rs);
-                            break;
+                        default: {
+                            if (g.epi == EPI_RELU) {
+                                alive += v > 0.0f ? 1 : 0;
+                                v = v > 0.0f ? v : 0.0f;
+                            } else if (g.epi == EPI_OUT_ROWSCALE) {
+                                v = v * rs;
+                            }
+                            const T hi = to_t<T>(v);
+                            Cb[ob] = hi;
+                            if (Cb2) Cb2[ob] = to_t<T>(v - from_t<T>(hi));
+                        }
                     }
                 }
             }
-            if (g.epi == EPI_RELU_BF16) {
+            if (g.epi == EPI_RELU) {
                 alive += __shfl_xor_sync(0xffffffffu, alive, 1);
                 alive += __shfl_xor_sync(0xffffffffu, alive, 2);
                 if (rok && c4 == 0 && alive) atomicAdd(&g.row_alive[row], alive);
@@ -198,7 +239,13 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return s;
 }
 
-__global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb, int twice) {
+__device__ __forceinline__ void put_split(bf16 *yb, bf16 *yb2, int64_t i, float v) {
+    const bf16 hi = __float2bfloat16_rn(v);
+    if (yb) yb[i] = hi;
+    if (yb2) yb2[i] = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+
+__global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, int twice) {
     __shared__ float red[32];
     const int m = blockIdx.x;
     const float *xr = x + (int64_t)m * n;
@@ -217,7 +264,7 @@ __global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb
         for (int j = threadIdx.x; j < n; j += blockDim.x) {
             float v = (xr[j] * inv) * inv2;
             if (yf) yf[(int64_t)m * n + j] = v;
-            if (yb) yb[(int64_t)m * n + j] = __float2bfloat16_rn(v);
+            put_split(yb, yb2, (int64_t)m * n + j, v);
         }
         return;
     }
@@ -225,13 +272,31 @@ __global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
         float v = xr[j] * inv;
         if (yf) yf[(int64_t)m * n + j] = v;
-        if (yb) yb[(int64_t)m * n + j] = __float2bfloat16_rn(v);
+        put_split(yb, yb2, (int64_t)m * n + j, v);
     }
 }
 
-__global__ void to_bf16_kernel(const float *x, int64_t ldx, int n, int M, bf16 *y, int64_t ldy) {
+__global__ void to_bf16_kernel(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy) {
     const int m = blockIdx.x;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) y[(int64_t)m * ldy + j] = __float2bfloat16_rn(x[(int64_t)m * ldx + j]);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) put_split(y, y2, (int64_t)m * ldy + j, x[(int64_t)m * ldx + j]);
+}
+
+__global__ void to_f16_kernel(const float *x, int64_t ldx, int n, __half *hi, __half *lo, int64_t ldy) {
+    const int m = blockIdx.x;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const float v = x[(int64_t)m * ldx + j];
+        const __half h = __float2half_rn(v);
+        hi[(int64_t)m * ldy + j] = h;
+        lo[(int64_t)m * ldy + j] = __float2half_rn(v - __half2float(h));
+    }
+}
+
+__global__ void f16_split_kernel(const float *x, int64_t count, __half *hi, __half *lo) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        const __half h = __float2half_rn(x[i]);
+        hi[i] = h;
+        lo[i] = __float2half_rn(x[i] - __half2float(h));
+    }
 }
 
 __global__ void flat_bf16_kernel(const float *x, int64_t count, bf16 *y) {
@@ -273,8 +338,8 @@ __global__ void delta_route_kernel(float *x, const float *xr, float *delta, cons
 }
 
 // TwELL sparse W2 for one token (one block per row); skips rows over threshold
-__global__ void twell_kernel(const bf16 *hidden, const int *row_alive, const bf16 *w2t, const float *resid,
-                             float *out, int n, int m, float threshold) {
+__global__ void twell_kernel(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t,
+                             const float *resid, float *out, int n, int m, float threshold) {
     extern __shared__ int s_idx[];
     __shared__ int s_cnt;
     const int r = blockIdx.x;
@@ -283,10 +348,11 @@ __global__ void twell_kernel(const bf16 *hidden, const int *row_alive, const bf1
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     const bf16 *h = hidden + (int64_t)r * m;
+    const bf16 *hl = hidden_lo ? hidden_lo + (int64_t)r * m : nullptr;
     float *s_val = reinterpret_cast<float *>(s_idx + m);
     // pack alive indices (ascending order is not needed for an f32 sum)
     for (int j = threadIdx.x; j < m; j += blockDim.x) {
-        float v = __bfloat162float(h[j]);
+        float v = __bfloat162float(h[j]) + (hl ? __bfloat162float(hl[j]) : 0.0f);
         if (v > 0.0f) {
             int k = atomicAdd(&s_cnt, 1);
             s_idx[k] = j;
@@ -318,19 +384,32 @@ __global__ void softmax_kernel(const float *logits, float *probs, int V, float i
 
 }  // namespace
 
-cudaError_t gemm(const Gemm &g, cudaStream_t s) {
-    if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
-    if (g.K % BK != 0 || g.lda % 8 != 0 || g.ldb % 8 != 0) return cudaErrorInvalidValue;
-    const int smem = STAGES * (BM + BN) * BK * 2;
+template <typename T, bool SA, bool SB>
+cudaError_t launch_gemm(const Gemm &g, cudaStream_t s) {
+    const int smem = STAGES * (BM * (SA ? 2 : 1) + BN * (SB ? 2 : 1)) * BK * 2;
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<T, SA, SB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attr = true;
     }
     dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
-    gemm_kernel<<<grid, THREADS, smem, s>>>(g);
+    gemm_kernel<T, SA, SB><<<grid, THREADS, smem, s>>>(g);
     return cudaGetLastError();
+}
+
+cudaError_t gemm(const Gemm &g, cudaStream_t s) {
+    if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return cudaSuccess;
+    if (g.K % BK != 0 || g.lda % 8 != 0 || g.ldb % 8 != 0) return cudaErrorInvalidValue;
+    const bool sa = g.A2 != nullptr, sb = g.B2 != nullptr;
+    if (g.dtype == DT_BF16) {
+        if (sb) return cudaErrorInvalidValue;  // bf16 B operands are exact weights
+        return sa ? launch_gemm<bf16, true, false>(g, s) : launch_gemm<bf16, false, false>(g, s);
+    }
+    if (sa && sb) return launch_gemm<__half, true, true>(g, s);
+    if (sa) return launch_gemm<__half, true, false>(g, s);
+    if (sb) return launch_gemm<__half, false, true>(g, s);
+    return launch_gemm<__half, false, false>(g, s);
 }
 
 cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M, float *x,
@@ -339,14 +418,24 @@ cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const
     embed_kernel<<<M, 256, 0, s>>>(tok, pos, wte, wpe, n, M, x);
     return cudaGetLastError();
 }
-cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bool twice, cudaStream_t s) {
+cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<M, 256, 0, s>>>(x, n, M, yf, yb, twice ? 1 : 0);
+    rmsnorm_kernel<<<M, 256, 0, s>>>(x, n, M, yf, yb, yb2, twice ? 1 : 0);
     return cudaGetLastError();
 }
-cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, int64_t ldy, cudaStream_t s) {
+cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    to_bf16_kernel<<<M, 256, 0, s>>>(x, ldx, n, M, y, ldy);
+    to_bf16_kernel<<<M, 256, 0, s>>>(x, ldx, n, M, y, y2, ldy);
+    return cudaGetLastError();
+}
+cudaError_t to_f16(const float *x, int64_t ldx, int n, int M, __half *hi, __half *lo, int64_t ldy, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    to_f16_kernel<<<M, 256, 0, s>>>(x, ldx, n, hi, lo, ldy);
+    return cudaGetLastError();
+}
+cudaError_t f32_to_f16_split(const float *x, int64_t count, __half *hi, __half *lo, cudaStream_t s) {
+    if (count <= 0) return cudaSuccess;
+    f16_split_kernel<<<1184, 256, 0, s>>>(x, count, hi, lo);
     return cudaGetLastError();
 }
 cudaError_t f32_to_bf16_flat(const float *x, int64_t count, bf16 *y, cudaStream_t s) {
@@ -360,15 +449,15 @@ cudaError_t delta_route(float *x, const float *xr, float *delta, const float *qu
     delta_route_kernel<<<M, 256, 0, s>>>(x, xr, delta, query, normw, n, layer);
     return cudaGetLastError();
 }
-cudaError_t twell_sparse_w2(const bf16 *hidden, const int *row_alive, const bf16 *w2t, const float *resid, float *out,
-                            int n, int m, int M, float threshold, cudaStream_t s) {
+cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t,
+                            const float *resid, float *out, int n, int m, int M, float threshold, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
     const size_t smem = (size_t)m * 8;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(twell_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    twell_kernel<<<M, 256, smem, s>>>(hidden, row_alive, w2t, resid, out, n, m, threshold);
+    twell_kernel<<<M, 256, smem, s>>>(hidden, hidden_lo, row_alive, w2t, resid, out, n, m, threshold);
     return cudaGetLastError();
 }
 cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s) {

@@ -12,28 +12,34 @@ namespace bf {
 using bf16 = __nv_bfloat16;
 
 enum Epi : int {
-    EPI_F32 = 0,        // C = acc
-    EPI_F32_RESID = 1,  // C = acc + R
-    EPI_RELU_BF16 = 2,  // Cb = bf16(max(acc, 0)); row_alive[row] += #(acc > 0)
-    EPI_BF16 = 3,       // Cb = bf16(acc)
+    EPI_F32 = 0,           // C = acc
+    EPI_F32_RESID = 1,     // C = acc + R
+    EPI_RELU = 2,          // Cb(+Cb2) = split(max(acc, 0)); row_alive[row] += #(acc > 0)
+    EPI_OUT = 3,           // Cb(+Cb2) = split(acc)
     EPI_F32_ROWSCALE = 4,  // C = acc * row_scale[row]
-    EPI_BF16_ROWSCALE = 5  // Cb = bf16(acc * row_scale[row])
+    EPI_OUT_ROWSCALE = 5   // Cb(+Cb2) = split(acc * row_scale[row])
 };
+enum DType : int { DT_BF16 = 0, DT_F16 = 1 };
 
-// C[M x N] = A[M x K] * B[N x K]^T (+ epilogue); A, B bf16 row-major (K contiguous).
+// C[M x N] = A[M x K] * B[N x K]^T (+ epilogue), A/B row-major with K contiguous,
+// f32 accumulation. Operands are bf16 or f16 (`dtype`, the same for A and B).
+// A2 / B2 optional "lo" parts: an operand is then hi + lo (a split of an f32
+// value into two 16-bit floats), and the product is hi*hi + lo*hi + hi*lo,
+// which carries about 16 (bf16) or 22 (f16) mantissa bits. Outputs Cb / Cb2
+// receive the hi / lo split of the result (Cb2 may be null).
 // Batched over blockIdx.z with element strides sA/sB/sC/sR/sCb/sRs.
 struct Gemm {
-    const bf16 *A;
+    const void *A, *A2;
     int64_t lda, sA;
-    const bf16 *B;
+    const void *B, *B2;
     int64_t ldb, sB;
     int M, N, K, batch;
-    int epi;
+    int epi, dtype;
     float *C;
     int64_t ldc, sC;
     const float *R;
     int64_t ldr, sR;
-    bf16 *Cb;
+    void *Cb, *Cb2;
     int64_t ldcb, sCb;
     int *row_alive;
     const float *row_scale;
@@ -46,10 +52,14 @@ cudaError_t gemm(const Gemm &g, cudaStream_t s);
 cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M,
                   float *x, cudaStream_t s);
 // per row: y = x / sqrt(mean(x^2) + 1e-5); `twice` applies it twice (sp_kv double norm).
-// Writes f32 (if yf) and bf16 (if yb). In-place allowed (yf == x).
-cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bool twice, cudaStream_t s);
-// f32 -> bf16 (strided rows)
-cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, int64_t ldy, cudaStream_t s);
+// Writes f32 (if yf) and the bf16 hi/lo split (if yb / yb2). In-place allowed (yf == x).
+cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s);
+// f32 -> bf16 hi (+ lo) split (strided rows)
+cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy, cudaStream_t s);
+// f32 -> f16 hi + lo split (strided rows)
+cudaError_t to_f16(const float *x, int64_t ldx, int n, int M, __half *hi, __half *lo, int64_t ldy, cudaStream_t s);
+// f32 -> f16 hi + lo split of a flat array
+cudaError_t f32_to_f16_split(const float *x, int64_t count, __half *hi, __half *lo, cudaStream_t s);
 // round a flat f32 array to bf16 (nearest-even)
 cudaError_t f32_to_bf16_flat(const float *x, int64_t count, bf16 *y, cudaStream_t s);
 // delta routing (src/transformer.rs:1707-1765, 2129-2158) for one layer l:
@@ -58,7 +68,7 @@ cudaError_t delta_route(float *x, const float *xr, float *delta, const float *qu
                         int n, int M, int layer, cudaStream_t s);
 // TwELL (math.rs:315-355): for rows whose alive fraction <= 1 - threshold, recompute
 // out = sum over alive j of h[j] * W2[:, j] + resid (gather over W2^T rows) in f32.
-cudaError_t twell_sparse_w2(const bf16 *hidden, const int *row_alive, const bf16 *w2t, const float *resid,
+cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t, const float *resid,
                             float *out, int n, int m, int M, float threshold, cudaStream_t s);
 // softmax_scaled (math.rs:36-50) per row of logits [M x V]
 cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s);

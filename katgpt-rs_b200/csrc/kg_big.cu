@@ -1,0 +1,441 @@
+// kg_big.cu — the BF16 tensor-core forward for full-size models (host side).
+//
+// Reproduces forward_quantized (src/transformer.rs:4042-4233; KG_KV_TQ) and
+// forward_sp_kv_quant (src/sp_kv/forward.rs:610-822; KG_KV_SPKV_TQ) on f32
+// arithmetic over bf16-rounded weights, with bf16 GEMM inputs:
+//   per layer: RMSNorm -> fused QKV GEMM (Kog layout: [Wq; Wk; Wv] rows,
+//   weights.rs:236-249) -> exact TurboQuant encode of K and V into the code
+//   arena -> attention over the codes -> Wo GEMM + residual -> RMSNorm ->
+//   W1 GEMM + ReLU (+ alive count) -> W2 GEMM + residual (TwELL sparse rows
+//   recomputed by gather) -> delta routing; then lm_head GEMM (+ softmax).
+// Decode (T = 1) attends in the rotated domain straight from the codes;
+// prefill (T > 1 from position 0) dequantizes the prompt's K/V once and runs
+// causal flash attention.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "kg_attn.cuh"
+#include "kg_bf16.cuh"
+#include "kg_internal.h"
+
+namespace kg {
+
+using bf::bf16;
+
+namespace {
+
+__global__ void expand_tokens_kernel(const int32_t *seq_ids, const int32_t *start_pos, int T, int n_seq, int B,
+                                     int n_slots, int V, const int32_t *tokens, int32_t *slot_of, int32_t *pos_of,
+                                     int *err) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= n_seq * T) return;
+    const int i = m / T, t = m - i * T;
+    const int s = seq_ids[i];
+    const int p = (start_pos ? start_pos[i] : 0) + t;
+    const int tok = tokens[m];
+    if (s < 0 || s >= n_slots || p < 0 || p >= B || tok < 0 || tok >= V) {
+        atomicExch(err, 1);
+        slot_of[m] = 0;
+        pos_of[m] = 0;
+        return;
+    }
+    slot_of[m] = s;
+    pos_of[m] = p;
+}
+
+__global__ void transpose_bf16_kernel(const bf16 *a, int rows, int cols, bf16 *t) {
+    __shared__ bf16 tile[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int row = by + r, col = bx + threadIdx.x;
+        if (row < rows && col < cols) tile[r][threadIdx.x] = a[(int64_t)row * cols + col];
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int row = bx + r, col = by + threadIdx.x;
+        if (row < cols && col < rows) t[(int64_t)row * rows + col] = tile[threadIdx.x][r];
+    }
+}
+
+__global__ void sanitize_tokens_kernel(const int32_t *tokens, int M, int V, int32_t *out) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < M) out[m] = min(max(tokens[m], 0), V - 1);
+}
+
+template <typename T>
+cudaError_t dalloc(T **p, size_t count, std::vector<void *> &owned) {
+    void *q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T));
+    if (e != cudaSuccess) return e;
+    owned.push_back(q);
+    *p = static_cast<T *>(q);
+    return cudaSuccess;
+}
+
+#define BIG_TRY(call)                            \
+    do {                                         \
+        cudaError_t e_ = (call);                 \
+        if (e_ != cudaSuccess) return e_;        \
+    } while (0)
+
+}  // namespace
+
+int big_supported(const kg_config &c, std::string &why) {
+    if (c.kv_mode == KG_KV_F32) return why = "the bf16 path needs a TurboQuant KV mode", -1;
+    for (int b : {c.key_bits, c.val_bits})
+        if (b != 3 && b != 4) return why = "the bf16 path packs 3/4-bit codes", -1;
+    const int kvd = c.n_kv_head * c.head_dim;
+    if (kvd % 64) return why = "kv_dim must be a multiple of 64", -1;
+    if (c.head_dim != 64 && c.head_dim != 128) return why = "head_dim must be 64 or 128", -1;
+    if (c.n_embd % 32 || c.mlp_hidden % 32) return why = "n_embd and mlp_hidden must be multiples of 32", -1;
+    if (c.n_head > 32) return why = "at most 32 heads", -1;
+    if ((c.n_head + 15) / 16 > 2) return why = "at most 32 heads", -1;
+    return 0;
+}
+
+cudaError_t big_init(kg_ctx *ctx) {
+    BigState &g = ctx->big;
+    const kg_config &c = ctx->cfg;
+    const int64_t n = ctx->n, kvd = ctx->kvd, m = ctx->m, V = ctx->V, L = ctx->L, B = ctx->B, S = c.max_seqs;
+    g.ws_tokens = std::max<int64_t>(S, 8192);
+    g.Tpad = (B + 31) / 32 * 32;
+    g.nhp = (ctx->nh + 15) / 16 * 16;
+    auto &own = ctx->allocs;
+    // weights (bf16), one block in the flat reference order
+    g.nbf = V * n + B * n + L * (2 * n * n + 2 * kvd * n + 2 * m * n) + V * n;
+    BIG_TRY(dalloc(&g.wall, g.nbf, own));
+    g.wte = g.wall;
+    g.wpe = g.wte + V * n;
+    g.layers = g.wpe + B * n;
+    g.lm = g.layers + L * (2 * n * n + 2 * kvd * n + 2 * m * n);
+    BIG_TRY(dalloc(&g.w2t, L * m * n, own));
+    BIG_TRY(dalloc(&g.dq, L * n, own));
+    BIG_TRY(dalloc(&g.dn, L * n, own));
+    BIG_TRY(dalloc(&g.rot_h, kvd * kvd, own));
+    BIG_TRY(dalloc(&g.rot_l, kvd * kvd, own));
+    BIG_TRY(dalloc(&g.rot_th, kvd * kvd, own));
+    BIG_TRY(dalloc(&g.rot_tl, kvd * kvd, own));
+    // code arena
+    BIG_TRY(dalloc(&g.kcodes, (size_t)S * L * B * ctx->kpl, own));
+    BIG_TRY(dalloc(&g.vcodes, (size_t)S * L * B * ctx->vpl, own));
+    BIG_TRY(dalloc(&g.knorm, (size_t)S * L * B, own));
+    BIG_TRY(dalloc(&g.vnorm, (size_t)S * L * B, own));
+    // workspace (ws_tokens rows)
+    const int64_t W = g.ws_tokens;
+    const int64_t nqkv = n + 2 * kvd;
+    BIG_TRY(dalloc(&g.x, W * n, own));
+    BIG_TRY(dalloc(&g.xr, W * n, own));
+    BIG_TRY(dalloc(&g.xr2, W * n, own));
+    BIG_TRY(dalloc(&g.delta, W * n, own));
+    BIG_TRY(dalloc(&g.attf, W * n, own));
+    BIG_TRY(dalloc(&g.xb, W * n, own));
+    BIG_TRY(dalloc(&g.xb2, W * n, own));
+    BIG_TRY(dalloc(&g.attb, W * n, own));
+    BIG_TRY(dalloc(&g.attb2, W * n, own));
+    BIG_TRY(dalloc(&g.qkv, W * nqkv, own));
+    BIG_TRY(dalloc(&g.qh, W * n, own));
+    BIG_TRY(dalloc(&g.ql, W * n, own));
+    BIG_TRY(dalloc(&g.hid, W * m, own));
+    BIG_TRY(dalloc(&g.hid2, W * m, own));
+    BIG_TRY(dalloc(&g.alive, W, own));
+    BIG_TRY(dalloc(&g.slot_of, W, own));
+    BIG_TRY(dalloc(&g.pos_of, W, own));
+    BIG_TRY(dalloc(&g.tok_of, W, own));
+    // prefill attention scratch
+    BIG_TRY(dalloc(&g.cent, W * kvd, own));
+    BIG_TRY(dalloc(&g.cent2, W * kvd, own));
+    BIG_TRY(dalloc(&g.kt, W * kvd, own));
+    BIG_TRY(dalloc(&g.kt2, W * kvd, own));
+    BIG_TRY(dalloc(&g.vt, W * kvd, own));
+    BIG_TRY(dalloc(&g.vt2, W * kvd, own));
+    BIG_TRY(dalloc(&g.nrm, W, own));
+    // decode attention scratch (max_seqs rows)
+    BIG_TRY(dalloc(&g.qrot, S * ctx->nh * kvd, own));
+    BIG_TRY(dalloc(&g.qrot2, S * ctx->nh * kvd, own));
+    BIG_TRY(dalloc(&g.U, S * ctx->nh * kvd, own));
+    BIG_TRY(dalloc(&g.U2, S * ctx->nh * kvd, own));
+    BIG_TRY(dalloc(&g.Sbuf, S * ctx->nh * g.Tpad, own));
+    BIG_TRY(dalloc(&g.P, S * g.nhp * g.Tpad, own));
+    BIG_TRY(dalloc(&g.P2, S * g.nhp * g.Tpad, own));
+    // centroid tables
+    BIG_TRY(dalloc(&g.kcent, 16, own));
+    BIG_TRY(dalloc(&g.vcent, 16, own));
+    std::vector<float> kc(16, 0.0f), vc(16, 0.0f);
+    std::copy(ctx->h_kc.begin(), ctx->h_kc.end(), kc.begin());
+    std::copy(ctx->h_vc.begin(), ctx->h_vc.end(), vc.begin());
+    BIG_TRY(cudaMemcpy(g.kcent, kc.data(), 64, cudaMemcpyHostToDevice));
+    BIG_TRY(cudaMemcpy(g.vcent, vc.data(), 64, cudaMemcpyHostToDevice));
+    // f16 hi/lo splits of the rotation for the tensor-core GEMMs
+    BIG_TRY(bf::f32_to_f16_split(ctx->rot, kvd * kvd, g.rot_h, g.rot_l, ctx->stream));
+    BIG_TRY(bf::f32_to_f16_split(ctx->rot_t, kvd * kvd, g.rot_th, g.rot_tl, ctx->stream));
+    BIG_TRY(cudaStreamSynchronize(ctx->stream));
+    return cudaSuccess;
+}
+
+cudaError_t big_reset(kg_ctx *ctx, int64_t slot0, int64_t nslots) {
+    BigState &g = ctx->big;
+    const size_t rows = (size_t)ctx->L * ctx->B;
+    cudaStream_t s = ctx->stream;
+    BIG_TRY(cudaMemsetAsync(g.kcodes + slot0 * rows * ctx->kpl, 0, nslots * rows * ctx->kpl, s));
+    BIG_TRY(cudaMemsetAsync(g.vcodes + slot0 * rows * ctx->vpl, 0, nslots * rows * ctx->vpl, s));
+    BIG_TRY(cudaMemsetAsync(g.knorm + slot0 * rows, 0, nslots * rows * 4, s));
+    BIG_TRY(cudaMemsetAsync(g.vnorm + slot0 * rows, 0, nslots * rows * 4, s));
+    return cudaStreamSynchronize(s);
+}
+
+// Convert flat f32 weights [offset, offset+count) (device pointer) into the bf16 block.
+cudaError_t big_upload_chunk(kg_ctx *ctx, const float *dsrc, int64_t offset, int64_t count) {
+    BigState &g = ctx->big;
+    if (offset < 0 || offset + count > g.nbf) return cudaErrorInvalidValue;
+    return bf::f32_to_bf16_flat(dsrc, count, g.wall + offset, ctx->stream);
+}
+
+// Delta-routing tables (f32, [2][L][n]) and W2^T for the TwELL gather.
+cudaError_t big_finish_upload(kg_ctx *ctx, const float *dq_dn_dev) {
+    BigState &g = ctx->big;
+    const int64_t n = ctx->n, kvd = ctx->kvd, m = ctx->m, L = ctx->L;
+    cudaStream_t s = ctx->stream;
+    const int64_t per_layer = 2 * n * n + 2 * kvd * n + 2 * m * n;
+    if (dq_dn_dev) {
+        BIG_TRY(cudaMemcpyAsync(g.dq, dq_dn_dev, L * n * 4, cudaMemcpyDeviceToDevice, s));
+        BIG_TRY(cudaMemcpyAsync(g.dn, dq_dn_dev + L * n, L * n * 4, cudaMemcpyDeviceToDevice, s));
+    }
+    for (int64_t l = 0; l < L; ++l) {
+        const bf16 *w2 = g.layers + l * per_layer + 2 * n * n + 2 * kvd * n + m * n;  // [n x m]
+        dim3 tb(32, 8), gb((m + 31) / 32, (n + 31) / 32);
+        transpose_bf16_kernel<<<gb, tb, 0, s>>>(w2, (int)n, (int)m, g.w2t + l * m * n);
+    }
+    BIG_TRY(cudaGetLastError());
+    return cudaStreamSynchronize(s);
+}
+
+namespace {
+// counter-based normal generator for synthetic benchmark weights
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ULL;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+__global__ void random_bf16_kernel(bf16 *w, int64_t count, uint64_t seed, float std_) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        uint64_t r = mix64(seed ^ mix64((uint64_t)i));
+        float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        float u2 = ((float)((r >> 16) & 0xFFFFFF)) * (1.0f / 16777216.0f);
+        float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        w[i] = __float2bfloat16_rn(z * std_);
+    }
+}
+__global__ void fill_kernel(float *p, int64_t count, float v) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) p[i] = v;
+}
+__global__ void bf16_to_f32_kernel(const bf16 *a, int64_t count, float *o) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+        o[i] = __bfloat162float(a[i]);
+}
+}  // namespace
+
+// Synthetic weights N(0, std) for every bf16 tensor; delta query 0, norm 1.
+cudaError_t big_random_weights(kg_ctx *ctx, uint64_t seed, float std_) {
+    BigState &g = ctx->big;
+    cudaStream_t s = ctx->stream;
+    random_bf16_kernel<<<2048, 256, 0, s>>>(g.wall, g.nbf, seed, std_);
+    fill_kernel<<<64, 256, 0, s>>>(g.dq, ctx->L * ctx->n, 0.0f);
+    fill_kernel<<<64, 256, 0, s>>>(g.dn, ctx->L * ctx->n, 1.0f);
+    BIG_TRY(cudaGetLastError());
+    return big_finish_upload(ctx, nullptr);
+}
+
+// bf16 block [offset, offset+count) back to f32 (device pointer)
+cudaError_t big_download(kg_ctx *ctx, float *dst, int64_t offset, int64_t count) {
+    BigState &g = ctx->big;
+    if (offset < 0 || offset + count > g.nbf) return cudaErrorInvalidValue;
+    bf16_to_f32_kernel<<<1024, 256, 0, ctx->stream>>>(g.wall + offset, count, dst);
+    return cudaGetLastError();
+}
+
+namespace {
+
+bf::Gemm gemm0() {
+    bf::Gemm q;
+    std::memset(&q, 0, sizeof(q));
+    q.batch = 1;
+    return q;
+}
+
+// One pass over all layers for M tokens (rows of the workspace). Every GEMM
+// operand that is not an exact bf16 weight is a 16-bit hi/lo split, so the
+// products keep about f32 accuracy (the 4-bit KV codes are discontinuous in
+// their inputs: plain bf16 activations move rotated coordinates across
+// codebook boundaries).
+cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaStream_t s) {
+    BigState &g = ctx->big;
+    const kg_config &c = ctx->cfg;
+    const int n = (int)ctx->n, kvd = (int)ctx->kvd, m = (int)ctx->m, L = (int)ctx->L, B = (int)ctx->B;
+    const int nh = (int)ctx->nh, hd = (int)ctx->hd;
+    const int nqkv = n + 2 * kvd;
+    const int64_t per_layer = 2 * (int64_t)n * n + 2 * (int64_t)kvd * n + 2 * (int64_t)m * n;
+    const bool spkv = c.kv_mode == KG_KV_SPKV_TQ;
+    const float scale = 1.0f / sqrtf((float)hd);
+    BIG_TRY(cudaMemsetAsync(g.delta, 0, (size_t)M * n * 4, s));
+    for (int l = 0; l < L; ++l) {
+        const bf16 *wqkv = g.layers + l * per_layer;
+        const bf16 *wo = wqkv + (int64_t)(n + 2 * kvd) * n;
+        const bf16 *w1 = wo + (int64_t)n * n;
+        const bf16 *w2 = w1 + (int64_t)m * n;
+        // pre-attention norm: residual xr = norm(x); sp_kv normalises a second time
+        if (spkv) {
+            BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, nullptr, nullptr, false, s));
+            BIG_TRY(bf::rmsnorm(g.xr, n, M, nullptr, g.xb, g.xb2, false, s));
+        } else {
+            BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, g.xb, g.xb2, false, s));
+        }
+        // fused QKV projection
+        bf::Gemm q = gemm0();
+        q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = wqkv; q.ldb = n; q.M = M; q.N = nqkv; q.K = n;
+        q.epi = bf::EPI_F32; q.C = g.qkv; q.ldc = nqkv;
+        BIG_TRY(bf::gemm(q, s));
+        // TurboQuant encode of K and V into the arena (exact reference order)
+        BIG_TRY(tq_encode_scatter(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
+                                  g.knorm, 1, g.slot_of, g.pos_of, L, B, l, s));
+        BIG_TRY(tq_encode_scatter(kvd, c.val_bits, M, g.qkv + n + kvd, nqkv, ctx->rot, ctx->vb, g.vcodes, ctx->vpl,
+                                  g.vnorm, 1, g.slot_of, g.pos_of, L, B, l, s));
+        BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
+        if (prefill) {
+            // dequantize the prompt's K and V: k~ = norm * (c R)
+            for (int kv = 0; kv < 2; ++kv) {
+                const uint8_t *codes = kv ? g.vcodes : g.kcodes;
+                const int pl = (int)(kv ? ctx->vpl : ctx->kpl);
+                BIG_TRY(attn::centroids(codes, pl, g.slot_of, g.pos_of, L, B, l, kv ? g.vcent : g.kcent, kvd, M,
+                                        g.cent, g.cent2, s));
+                BIG_TRY(attn::gather_norms(kv ? g.vnorm : g.knorm, g.slot_of, g.pos_of, L, B, l, M, g.nrm, s));
+                bf::Gemm d = gemm0();
+                d.dtype = bf::DT_F16;
+                d.A = g.cent; d.A2 = g.cent2; d.lda = kvd; d.B = g.rot_th; d.B2 = g.rot_tl; d.ldb = kvd;
+                d.M = M; d.N = kvd; d.K = kvd;
+                d.epi = bf::EPI_OUT_ROWSCALE; d.Cb = kv ? g.vt : g.kt; d.Cb2 = kv ? g.vt2 : g.kt2; d.ldcb = kvd;
+                d.row_scale = g.nrm;
+                BIG_TRY(bf::gemm(d, s));
+            }
+            attn::FlashArgs fa;
+            fa.Q = g.qh; fa.Q_lo = g.ql; fa.K = g.kt; fa.K_lo = g.kt2; fa.V = g.vt; fa.V_lo = g.vt2; fa.O = g.attf;
+            fa.ldq = n; fa.ldk = kvd; fa.ldo = n;
+            fa.n_seq = n_seq; fa.T = T; fa.nh = nh; fa.nkv = (int)ctx->nkv; fa.hd = hd; fa.scale = scale;
+            BIG_TRY(attn::flash_prefill(fa, s));
+        } else {
+            // q~_h = R[:, head cols] q_h  (batched over heads)
+            bf::Gemm r = gemm0();
+            r.dtype = bf::DT_F16;
+            r.A = g.qh; r.A2 = g.ql; r.lda = n; r.sA = hd;
+            r.B = g.rot_h; r.B2 = g.rot_l; r.ldb = kvd; r.sB = hd;
+            r.M = M; r.N = kvd; r.K = hd; r.batch = nh;
+            r.epi = bf::EPI_OUT; r.Cb = g.qrot; r.Cb2 = g.qrot2; r.ldcb = (int64_t)nh * kvd; r.sCb = kvd;
+            BIG_TRY(bf::gemm(r, s));
+            attn::ScoreArgs sa;
+            sa.kcodes = g.kcodes; sa.knorm = g.knorm; sa.kcent = g.kcent; sa.qrot = g.qrot; sa.qrot_lo = g.qrot2;
+            sa.slot = g.slot_of; sa.pos = g.pos_of; sa.S = g.Sbuf;
+            sa.M = M; sa.nh = nh; sa.kvd = kvd; sa.kpl = (int)ctx->kpl; sa.L = L; sa.B = B; sa.layer = l;
+            sa.Tpad = (int)g.Tpad; sa.Tmax = B; sa.scale = scale;
+            BIG_TRY(attn::scores(sa, s));
+            attn::SoftmaxArgs sm;
+            sm.S = g.Sbuf; sm.vnorm = g.vnorm; sm.slot = g.slot_of; sm.pos = g.pos_of; sm.P = g.P; sm.P_lo = g.P2;
+            sm.M = M; sm.nh = nh; sm.nhp = (int)g.nhp; sm.L = L; sm.B = B; sm.layer = l; sm.Tpad = (int)g.Tpad;
+            BIG_TRY(attn::softmax(sm, s));
+            attn::ValueArgs va;
+            va.vcodes = g.vcodes; va.vcent = g.vcent; va.P = g.P; va.P_lo = g.P2; va.slot = g.slot_of;
+            va.pos = g.pos_of; va.U = g.U; va.U_lo = g.U2; va.M = M; va.nh = nh; va.nhp = (int)g.nhp; va.kvd = kvd;
+            va.vpl = (int)ctx->vpl; va.L = L; va.B = B; va.layer = l; va.Tpad = (int)g.Tpad;
+            BIG_TRY(attn::values(va, s));
+            // out_h = R[:, head cols]^T u~_h
+            bf::Gemm o = gemm0();
+            o.dtype = bf::DT_F16;
+            o.A = g.U; o.A2 = g.U2; o.lda = (int64_t)nh * kvd; o.sA = kvd;
+            o.B = g.rot_th; o.B2 = g.rot_tl; o.ldb = kvd; o.sB = (int64_t)hd * kvd;
+            o.M = M; o.N = hd; o.K = kvd; o.batch = nh;
+            o.epi = bf::EPI_F32; o.C = g.attf; o.ldc = n; o.sC = hd;
+            BIG_TRY(bf::gemm(o, s));
+        }
+        BIG_TRY(bf::to_bf16(g.attf, n, n, M, g.attb, g.attb2, n, s));
+        // output projection + residual: x = Wo att + xr
+        bf::Gemm w = gemm0();
+        w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
+        w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n;
+        BIG_TRY(bf::gemm(w, s));
+        // MLP
+        BIG_TRY(cudaMemcpyAsync(g.xr2, g.x, (size_t)M * n * 4, cudaMemcpyDeviceToDevice, s));
+        BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s));
+        BIG_TRY(cudaMemsetAsync(g.alive, 0, (size_t)M * 4, s));
+        bf::Gemm u = gemm0();
+        u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
+        u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;
+        BIG_TRY(bf::gemm(u, s));
+        bf::Gemm dn = gemm0();
+        dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
+        dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
+        BIG_TRY(bf::gemm(dn, s));
+        BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
+                                    c.sparse_threshold, s));
+        if (!spkv) BIG_TRY(bf::delta_route(g.x, g.xr, g.delta, g.dq + (int64_t)l * n, g.dn + (int64_t)l * n, n, M, l, s));
+    }
+    return cudaSuccess;
+}
+
+cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, cudaStream_t s) {
+    BigState &g = ctx->big;
+    const int n = (int)ctx->n, V = (int)ctx->V;
+    if (!logits && !probs) return cudaSuccess;
+    BIG_TRY(bf::to_bf16(g.x, n, n, M, g.xb, g.xb2, n, s));
+    float *lo = logits ? logits : probs;  // logits land in the probs buffer when only probs are wanted
+    bf::Gemm q = gemm0();
+    q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = g.lm; q.ldb = n; q.M = M; q.N = V; q.K = n;
+    q.epi = bf::EPI_F32; q.C = lo; q.ldc = V;
+    BIG_TRY(bf::gemm(q, s));
+    if (probs) BIG_TRY(bf::softmax_rows(lo, probs, V, M, 1.0f / ctx->cfg.temperature, s));
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                        const int32_t *start_pos, int T, float *logits, float *probs, cudaStream_t s) {
+    BigState &g = ctx->big;
+    const int n = (int)ctx->n;
+    if (T > 1 && start_pos) return cudaErrorNotSupported;  // prefill starts at position 0
+    const int64_t V = ctx->V;
+    if (T == 1) {
+        // decode: tokens of up to ws_tokens sequences per pass
+        for (int i0 = 0; i0 < n_seq; i0 += (int)std::min<int64_t>(g.ws_tokens, ctx->cfg.max_seqs)) {
+            const int cnt = std::min<int>(n_seq - i0, (int)std::min<int64_t>(g.ws_tokens, ctx->cfg.max_seqs));
+            expand_tokens_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(seq_ids + i0, start_pos ? start_pos + i0 : nullptr,
+                                                                  1, cnt, (int)ctx->B, ctx->cfg.max_seqs, (int)V,
+                                                                  tokens + i0, g.slot_of, g.pos_of, ctx->d_err);
+            sanitize_tokens_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(tokens + i0, cnt, (int)V, g.tok_of);
+            BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, cnt, g.x, s));
+            BIG_TRY(run_layers(ctx, cnt, false, cnt, 1, s));
+            BIG_TRY(lm_head(ctx, cnt, logits ? logits + (int64_t)i0 * V : nullptr,
+                            probs ? probs + (int64_t)i0 * V : nullptr, s));
+        }
+        return cudaGetLastError();
+    }
+    // prefill: whole sequences per pass
+    const int per = (int)std::max<int64_t>(1, g.ws_tokens / T);
+    for (int i0 = 0; i0 < n_seq; i0 += per) {
+        const int cnt = std::min(per, n_seq - i0);
+        const int M = cnt * T;
+        expand_tokens_kernel<<<(M + 255) / 256, 256, 0, s>>>(seq_ids + i0, nullptr, T, cnt, (int)ctx->B,
+                                                            ctx->cfg.max_seqs, (int)V, tokens + (int64_t)i0 * T,
+                                                            g.slot_of, g.pos_of, ctx->d_err);
+        sanitize_tokens_kernel<<<(M + 255) / 256, 256, 0, s>>>(tokens + (int64_t)i0 * T, M, (int)V, g.tok_of);
+        BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, M, g.x, s));
+        BIG_TRY(run_layers(ctx, M, true, cnt, T, s));
+        BIG_TRY(lm_head(ctx, M, logits ? logits + (int64_t)i0 * T * V : nullptr,
+                        probs ? probs + (int64_t)i0 * T * V : nullptr, s));
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace kg

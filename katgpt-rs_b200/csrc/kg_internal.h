@@ -1,5 +1,7 @@
 // kg_internal.h — host/device shared structures of libkgcuda (not part of the ABI).
 #pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -57,6 +59,31 @@ cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, 
 
 }  // namespace kg
 
+namespace kg {
+// Device state of the BF16 tensor-core path (kg_big.cu).
+struct BigState {
+    __nv_bfloat16 *wall = nullptr;  // [wte | wpe | layers | lm_head] in flat reference order
+    __nv_bfloat16 *wte = nullptr, *wpe = nullptr, *layers = nullptr, *lm = nullptr, *w2t = nullptr;
+    float *dq = nullptr, *dn = nullptr;                // delta routing query / norm [L][n]
+    __half *rot_h = nullptr, *rot_l = nullptr, *rot_th = nullptr, *rot_tl = nullptr;  // f16 hi/lo of R, R^T
+    float *kcent = nullptr, *vcent = nullptr;          // 16 centroids each
+    uint8_t *kcodes = nullptr, *vcodes = nullptr;      // [slot][layer][pos][pl]
+    float *knorm = nullptr, *vnorm = nullptr;          // [slot][layer][pos]
+    int64_t ws_tokens = 0, Tpad = 0, nhp = 0, nbf = 0;
+    // workspace (hi/lo pairs are 16-bit splits of f32 values)
+    float *x = nullptr, *xr = nullptr, *xr2 = nullptr, *delta = nullptr, *qkv = nullptr, *nrm = nullptr,
+          *attf = nullptr;
+    __nv_bfloat16 *xb = nullptr, *xb2 = nullptr, *attb = nullptr, *attb2 = nullptr, *hid = nullptr, *hid2 = nullptr;
+    __half *qh = nullptr, *ql = nullptr, *cent = nullptr, *cent2 = nullptr, *kt = nullptr, *kt2 = nullptr,
+           *vt = nullptr, *vt2 = nullptr, *qrot = nullptr, *qrot2 = nullptr, *U = nullptr, *U2 = nullptr,
+           *P = nullptr, *P2 = nullptr;
+    float *Sbuf = nullptr;
+    int *alive = nullptr;
+    int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;
+};
+int big_supported(const kg_config &c, std::string &why);
+}  // namespace kg
+
 // Host-side context (InferenceBackend state for one device).
 struct kg_ctx {
     kg_config cfg{};
@@ -65,7 +92,9 @@ struct kg_ctx {
     std::string err;
     std::string dev_name;
     bool compiled = false;
-    bool micro = false;  // shape has the exact-order micro kernel
+    bool micro = false;     // shape has the exact-order micro kernel
+    bool big_path = false;  // shape runs on the BF16 tensor-core path
+    kg::BigState big;
     int64_t n = 0, nh = 0, hd = 0, nkv = 0, kvd = 0, m = 0, V = 0, L = 0, B = 0;
     int64_t kpl = 0, vpl = 0, ph = 0;
     int64_t w_count = 0;
@@ -84,3 +113,14 @@ struct kg_ctx {
     size_t stage_bytes = 0;
     std::vector<void *> allocs;
 };
+
+namespace kg {
+cudaError_t big_init(kg_ctx *ctx);
+cudaError_t big_reset(kg_ctx *ctx, int64_t slot0, int64_t nslots);
+cudaError_t big_upload_chunk(kg_ctx *ctx, const float *dsrc, int64_t offset, int64_t count);
+cudaError_t big_finish_upload(kg_ctx *ctx, const float *dq_dn_dev);
+cudaError_t big_random_weights(kg_ctx *ctx, uint64_t seed, float std_);
+cudaError_t big_download(kg_ctx *ctx, float *dst_dev, int64_t offset, int64_t count);
+cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                        const int32_t *start_pos, int T, float *logits, float *probs, cudaStream_t s);
+}  // namespace kg

@@ -71,6 +71,8 @@ def lib():
             "kg_upload_weights": (ctypes.c_int, [P, P, I64]),
             "kg_upload_weights_dev": (ctypes.c_int, [P, P, I64]),
             "kg_is_compiled": (ctypes.c_int, [P]),
+            "kg_random_weights": (ctypes.c_int, [P, ctypes.c_uint64, F32]),
+            "kg_download_weights": (ctypes.c_int, [P, P, I64]),
             "kg_seq_reset": (ctypes.c_int, [P, I32]),
             "kg_seq_reset_all": (ctypes.c_int, [P]),
             "kg_forward_token": (ctypes.c_int, [P, I32, I32, I32, P]),
@@ -94,6 +96,13 @@ def exported_symbols():
     """Names of every kg_* function the header declares (for ABI checks)."""
     lib()
     return sorted(n for n in dir(_lib) if n.startswith("kg_"))
+
+
+def bf16_round(a):
+    """Round f32 to bf16 (nearest-even) and back, as the device does on upload."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
 
 
 def micro_config(**kw):
@@ -153,6 +162,16 @@ class CudaBackend:
     def compile(self, weights):
         w = np.ascontiguousarray(weights, dtype=np.float32)
         self._check(lib().kg_upload_weights(self._h, _ptr(w), w.size))
+
+    def random_weights(self, seed=0, std=0.02):
+        """Synthetic N(0, std) bf16 weights generated on the device (bf16 path)."""
+        self._check(lib().kg_random_weights(self._h, seed, std))
+
+    def download_weights(self):
+        n = lib().kg_weights_count(ctypes.byref(self.cfg))
+        w = np.empty(n, np.float32)
+        self._check(lib().kg_download_weights(self._h, _ptr(w), n))
+        return w
 
     def is_compiled(self):
         return bool(lib().kg_is_compiled(self._h))
