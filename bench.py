@@ -1,14 +1,19 @@
 """Benchmark: decode tokens/s of katgpt-rs's per-token forward on B200.
 
-Default workload (N=1): the micro model with AttentionMode::SpKvQuant and the
-3-bit TurboQuant KV codec — 65,536 independent sequences x 16 teacher-forced
-positions (BOS + 15 uniform ids in 1..26), Config::micro() weights from
-TransformerWeights::new(Rng::new(42)). One step decodes all 16 positions of
-every sequence, one kernel launch per position (decode, T = 1 per launch).
+Workloads (`--workload`):
+  c3 (default): n_layer 12, n_embd 768, 12 heads, mlp 3072, vocab 32000,
+      block 2048, bf16 weights ~N(0, 0.02), 4-bit TurboQuant KV
+      (forward_quantized). 64 sequences: a 1024-token prefill from uniform
+      random ids (untimed setup), then teacher-forced decode steps; one step =
+      one token for every sequence (64 tokens). KV-attention roofline from the
+      device timers around the kernels that read the codes.
+  c2: Config::micro with AttentionMode::SpKvQuant and the 3-bit TurboQuant
+      codec; 65,536 sequences x 16 positions; one step decodes all 16
+      positions (one launch per position).
 Multi-GPU: one process per GPU (torchrun), weak scaling — each rank owns its
-own 65,536 sequences; there is no data-path collective.
+own sequences, weights replicated; no data-path collective.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c2]
 
 Prints one JSON line on rank 0.
 """
@@ -18,7 +23,6 @@ import json
 import os
 import subprocess
 import sys
-import threading
 import time
 
 import numpy as np
@@ -28,9 +32,12 @@ sys.path.insert(0, os.path.join(ROOT, "katgpt-rs_b200"))
 
 METRIC = "decode tokens/s (box)"
 UNIT = "tokens/s"
-N_SEQ = 65536
-T = 16
 SEED = 42
+
+C3 = dict(vocab_size=32000, block_size=2048, n_embd=768, n_head=12, head_dim=64, n_kv_head=12,
+          mlp_hidden=3072, n_layer=12, key_bits=4, val_bits=4)
+C3_SEQS, C3_PREFILL = 64, 1024
+C2_SEQS, C2_T = 65536, 16
 
 
 def parse():
@@ -39,23 +46,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--n-seq", type=int, default=N_SEQ)
+    ap.add_argument("--workload", default="c3", choices=["c3", "c2"])
     return ap.parse_args()
 
 
-def tokens_for_rank(rank, n_seq):
-    rng = np.random.default_rng(1000 + rank)
-    t = rng.integers(1, 27, size=(n_seq, T)).astype(np.int32)
-    t[:, 0] = 26  # BOS
-    return t
-
-
-def workload_config(n_seq):
-    return {"workload": "micro SpKvQuant TurboQuant-3bit teacher-forced decode",
-            "model": "Config::micro (vocab 27, n_embd 16, n_head 4, mlp 64, n_layer 1)",
-            "kv": "SpKvQuant + TurboQuant 3-bit K/V", "sequences_per_gpu": n_seq,
-            "positions": T, "weights": "TransformerWeights::new(Rng(42)), f32",
-            "l2": "flushed between steps (256 MiB write, outside the timed events)"}
+def load_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return {}
 
 
 class ClockSampler:
@@ -108,61 +107,297 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm)}
 
 
-def cpu_baseline(n_threads=None, budget_s=10.0):
-    """The oracle (C++ restatement of the reference's x86 AVX2 path) on host cores."""
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle (C++ restatement of the reference's x86 AVX2 path)
+
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
+    return oracle
+
+
+def cpu_sample_c3(budget_s=15.0, threads=None):
+    """forward_quantized of the C3 model on host cores: one sequence per thread,
+    positions 0.. until the budget is spent (short contexts: the attention part
+    of the reference's cost at position ~1100 is not included)."""
+    oracle = _oracle()
+    threads = threads or os.cpu_count() or 1
+    cfg = oracle.config(vocab_size=C3["vocab_size"], block_size=C3["block_size"], n_embd=768, n_head=12,
+                        head_dim=64, n_kv_head=12, mlp_hidden=3072, n_layer=12)
+    w = oracle.weights(cfg, SEED, 1, 0.02)
+    rng = np.random.default_rng(7)
+    T = 8
+    while True:
+        toks = rng.integers(0, C3["vocab_size"], size=(threads, T)).astype(np.int32)
+        t0 = time.perf_counter()
+        oracle.run_batch(cfg, oracle.MODE_QUANT, w, toks, key_bits=4, val_bits=4, threads=threads,
+                         keep_logits=False)
+        el = time.perf_counter() - t0
+        if el > budget_s / 3 or T >= 256:
+            break
+        T *= 2
+    return threads * T / el, threads, f"{threads} sequences x positions 0..{T - 1} (forward_quantized, {el:.1f} s)"
+
+
+def cpu_sample_c2(budget_s=10.0, threads=None):
+    oracle = _oracle()
+    threads = threads or os.cpu_count() or 1
     cfg = oracle.config()
     w = oracle.weights(cfg, SEED)
-    threads = n_threads or os.cpu_count() or 1
-    toks = tokens_for_rank(0, N_SEQ)
+    toks = c2_tokens(0, C2_SEQS)
     n, done, t0 = 1024, 0, time.perf_counter()
     while True:
         oracle.run_batch(cfg, oracle.MODE_SPKV, w, toks[:n], threads=threads, keep_logits=False)
-        done += n * T
+        done += n * C2_T
         el = time.perf_counter() - t0
         if el > budget_s:
             break
-        n = min(N_SEQ, n * 2)
-    return {"value": done / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{done // T} sequences x {T} positions of the same workload, "
-                      f"forward_sp_kv_quant restated in C++ (oracle), {threads} threads, {el:.1f} s"}
+        n = min(C2_SEQS, n * 2)
+    return done / el, threads, f"{done // C2_T} sequences x {C2_T} positions (forward_sp_kv_quant, {el:.1f} s)"
 
 
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """The reference arm: the oracle on all host cores, rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return 0
-    steps, warm = args.steps, args.warmup
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
-    oracle.build()
-    cfg = oracle.config()
-    w = oracle.weights(cfg, SEED)
-    threads = os.cpu_count() or 1
-    toks = tokens_for_rank(0, N_SEQ)
-    # bounded per-step sample so the whole run ends within minutes
-    sample = 4096
-    for _ in range(warm):
-        oracle.run_batch(cfg, oracle.MODE_SPKV, w, toks[:sample], threads=threads, keep_logits=False)
     t0 = time.perf_counter()
-    for s in range(steps):
-        sl = toks[(s * sample) % N_SEQ:(s * sample) % N_SEQ + sample]
-        oracle.run_batch(cfg, oracle.MODE_SPKV, w, sl, threads=threads, keep_logits=False)
-    el = time.perf_counter() - t0
-    v = steps * sample * T / el
-    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-            "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference", "config": dict(workload_config(sample), sequences_per_step=sample),
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{sample} sequences x {T} positions per step on {threads} host threads "
-                                       "(the reference is Rust and cannot be built here; its x86 AVX2 path "
-                                       "restated in C++)"},
+    vals = []
+    for _ in range(max(1, min(args.steps, 3))):
+        v, cores, sample = (cpu_sample_c3 if args.workload == "c3" else cpu_sample_c2)(budget_s=8.0)
+        vals.append(v)
+    v = float(np.median(vals))
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": len(vals),
+            "warmup": 0, "ms_per_step": 1000.0 * (time.perf_counter() - t0) / len(vals), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": args.workload, "note": "reference = its x86 AVX2 CPU path restated in C++ "
+                       "(the Rust reference cannot be built here)"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------------------
+
+def c2_tokens(rank, n_seq):
+    rng = np.random.default_rng(1000 + rank)
+    t = rng.integers(1, 27, size=(n_seq, C2_T)).astype(np.int32)
+    t[:, 0] = 26  # BOS
+    return t
+
+
+def timed_steps(torch, stream, steps, step_fn, flush):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s in range(steps):
+        flush.fill_(s & 0xFF)
+        ev[s][0].record(stream)
+        step_fn(s)
+        ev[s][1].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def bench_c3(args, torch, dist, kgcuda, world, rank, local):
+    dev = torch.device("cuda", local)
+    cfg = kgcuda.micro_config(kv_mode=kgcuda.KG_KV_TQ, weight_dtype=kgcuda.KG_W_BF16, max_seqs=C3_SEQS, **C3)
+    be = kgcuda.CudaBackend(cfg, device=local)
+    be.random_weights(seed=SEED, std=0.02)
+    n, V = C3_SEQS, C3["vocab_size"]
+    total_dec = args.warmup + args.steps
+    e_steps = min(max(3, args.steps // 4), 64)
+    assert C3_PREFILL + total_dec + e_steps + 2 <= C3["block_size"], "too many steps for block_size 2048"
+    rng = np.random.default_rng(1000 + rank)
+    toks = rng.integers(0, V, size=(n, C3["block_size"])).astype(np.int32)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    d_ids = torch.arange(n, dtype=torch.int32, device=dev)
+    d_pre = torch.from_numpy(np.ascontiguousarray(toks[:, :C3_PREFILL])).to(dev)
+    d_dec = torch.from_numpy(np.ascontiguousarray(toks[:, C3_PREFILL:].T)).to(dev)       # [pos][seq]
+    d_pos = (torch.arange(C3["block_size"] - C3_PREFILL, dtype=torch.int32, device=dev)[:, None]
+             + C3_PREFILL).expand(-1, n).contiguous()
+    d_log = torch.empty((n, V), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    # prefill (untimed setup of the decode benchmark; its device time is reported)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    be.forward_batch_dev(n, C3_PREFILL, P(d_ids), P(d_pre), None, None, None, sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+
+    def step(s):
+        be.forward_batch_dev(n, 1, P(d_ids), P(d_dec[s]), P(d_pos[s]), P(d_log), None, sp)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    be.profile_read()          # clear
+    be.profile(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        step_ms = timed_steps(torch, stream, args.steps, lambda s: step(args.warmup + s), flush)
+    be.profile(False)
+    ph_ms, ph_cnt = be.profile_read()
+    ph_ms = [float(x) for x in ph_ms]
+    if world > 1:
+        dist.barrier()
+    my_ms = float(np.sum(step_ms))
+    t = torch.tensor([my_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item()) / args.steps
+    value = world * n / (ms_per_step / 1000.0)
+
+    # end to end through the public host API with pinned host buffers
+    base = C3_PREFILL + total_dec
+    h_tok = torch.from_numpy(np.ascontiguousarray(toks[:, base:base + e_steps].T)).pin_memory()
+    h_ids = torch.arange(n, dtype=torch.int32).pin_memory()
+    h_pos = (torch.arange(e_steps, dtype=torch.int32)[:, None] + base).expand(-1, n).contiguous().pin_memory()
+    h_log = torch.empty((n, V), dtype=torch.float32).pin_memory()
+    lib = kgcuda.lib()
+
+    def e2e_step(s):
+        rc = lib.kg_forward_batch(be._h, n, P(h_ids), P(h_tok[s]), P(h_pos[s]), 1, P(h_log), None)
+        if rc:
+            raise RuntimeError(lib.kg_last_error(be._h))
+
+    e2e_step(0)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for s in range(1, e_steps):
+        e2e_step(s)
+    e_el = time.perf_counter() - t0
+    te = torch.tensor([e_el], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = world * n * (e_steps - 1) / float(te.item())
+
+    kpl = kvpl = C3["n_embd"] // 2
+    L = C3["n_layer"]
+    positions = [C3_PREFILL + args.warmup + s for s in range(args.steps)]
+    attn_bytes = sum(n * L * (p + 1) * (kpl + kvpl + 8) for p in positions)
+    attn_gbs = attn_bytes / (ph_ms[0] / 1000.0) / 1e9 if ph_ms[0] > 0 else None
+    nbf = sum([V * 768, 2048 * 768, L * (4 * 768 * 768 + 2 * 768 * 3072), V * 768])
+    gemm_bytes = args.steps * (nbf - 2048 * 768 - V * 768) * 2  # streamed weights (wte/wpe gathered, not streamed)
+    gemm_gbs = gemm_bytes / (ph_ms[2] / 1000.0) / 1e9 if ph_ms[2] > 0 else None
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "c3: n_layer 12, n_embd 768, 12 heads, mlp 3072, vocab 32000, block 2048, "
+                               "bf16 weights N(0,0.02), 4-bit TurboQuant KV (forward_quantized); 64 sequences, "
+                               "1024-token prefill then teacher-forced decode",
+                   "global_batch": world * n, "seq_len": C3_PREFILL, "parallelism": f"dp{world} (sequence shards)",
+                   "l2": "flushed between steps (256 MiB write, outside the timed events)"},
+        "gpu_launches": None,
+        "roofline": {"bound": "hbm", "kernel": "decode KV attention (scores + softmax + values over 4-bit codes)",
+                     "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": (attn_gbs / peak) if attn_gbs else None, "traffic": None,
+                     "algorithmic_bytes_per_step": attn_bytes / args.steps,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        "phases_ms_per_step": {"kv_attention": float(ph_ms[0]) / args.steps, "tq_encode": float(ph_ms[1]) / args.steps,
+                               "weight_gemms": float(ph_ms[2]) / args.steps},
+        "weight_gemm_gbs": gemm_gbs,
+        "prefill": {"tokens": n * C3_PREFILL, "ms": prefill_ms, "tokens_per_s": n * C3_PREFILL / (prefill_ms / 1000.0)},
+        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(n * 4 * 3), "d2h_bytes_per_step": int(n * V * 4)},
+        "clocks": clk.summary(),
+    }
+    be.close()
+    return line
+
+
+def bench_c2(args, torch, dist, kgcuda, world, rank, local):
+    dev = torch.device("cuda", local)
+    n_seq = C2_SEQS
+    cfg = kgcuda.micro_config(kv_mode=kgcuda.KG_KV_SPKV_TQ, max_seqs=n_seq)
+    be = kgcuda.CudaBackend(cfg, device=local)
+    be.compile(kgcuda.reference_weights(cfg, SEED))
+    toks = c2_tokens(rank, n_seq)
+    d_tok = torch.from_numpy(np.ascontiguousarray(toks.T)).to(dev)        # [T][n_seq]
+    d_ids = torch.arange(n_seq, dtype=torch.int32, device=dev)
+    d_pos = torch.arange(C2_T, dtype=torch.int32, device=dev)[:, None].expand(C2_T, n_seq).contiguous()
+    d_log = torch.empty((C2_T, n_seq, 27), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step(_s):
+        for t in range(C2_T):
+            be.forward_batch_dev(n_seq, 1, P(d_ids), P(d_tok[t]), P(d_pos[t]), P(d_log[t]), None, sp)
+
+    for s in range(max(3, args.warmup)):
+        step(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        step_ms = timed_steps(torch, stream, args.steps, step, flush)
+    my_ms = float(np.sum(step_ms))
+    tm = torch.tensor([my_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    ms_per_step = float(tm.item()) / args.steps
+    value = world * n_seq * C2_T / (ms_per_step / 1000.0)
+    lo_dec = d_log[:, :64].permute(1, 0, 2).cpu().numpy()
+    h_tok = torch.from_numpy(np.ascontiguousarray(toks.T)).pin_memory()
+    h_ids = torch.arange(n_seq, dtype=torch.int32).pin_memory()
+    h_pos = torch.arange(C2_T, dtype=torch.int32)[:, None].expand(C2_T, n_seq).contiguous().pin_memory()
+    h_log = torch.empty((C2_T, n_seq, 27), dtype=torch.float32).pin_memory()
+    lib = kgcuda.lib()
+
+    def e2e_step():
+        for t in range(C2_T):
+            rc = lib.kg_forward_batch(be._h, n_seq, P(h_ids), P(h_tok[t]), P(h_pos[t]), 1, P(h_log[t]), None)
+            if rc:
+                raise RuntimeError(lib.kg_last_error(be._h))
+
+    e2e_step()
+    e_steps = 3
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e_steps):
+        e2e_step()
+    te = torch.tensor([time.perf_counter() - t0], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = world * n_seq * C2_T * e_steps / float(te.item())
+    self_diff = float(np.abs(h_log[:, :64].permute(1, 0, 2).numpy() - lo_dec).max())
+    code_b = 2 * 12 + 2 * 4
+    bytes_per_step = n_seq * sum(4 + t * code_b + code_b + 4 + 27 * 4 for t in range(C2_T))
+    achieved = bytes_per_step / (ms_per_step / 1000.0) / 1e9
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "c2: Config::micro + SpKvQuant + TurboQuant 3-bit, 65536 sequences x 16 positions",
+                   "global_batch": world * n_seq, "seq_len": C2_T, "parallelism": f"dp{world} (sequence shards)",
+                   "l2": "flushed between steps (256 MiB write, outside the timed events)"},
+        "gpu_launches": C2_T * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "micro_forward", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "note": "exact-order f32 kernel: issue-bound, not HBM-bound",
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(3 * C2_T * n_seq * 4),
+                "d2h_bytes_per_step": int(h_log.numel() * 4)},
+        "self_check_max_abs_diff": self_diff,
+        "clocks": clk.summary(),
+    }
+    be.close()
+    return line
 
 
 def main():
@@ -181,134 +416,15 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    n_seq = args.n_seq
-    cfg = kgcuda.micro_config(kv_mode=kgcuda.KG_KV_SPKV_TQ, max_seqs=n_seq)
-    be = kgcuda.CudaBackend(cfg, device=local)
-    w = kgcuda.reference_weights(cfg, SEED)
-    be.compile(w)
-
-    toks = tokens_for_rank(rank, n_seq)
-    d_tok = torch.from_numpy(np.ascontiguousarray(toks.T)).to(dev)        # [T][n_seq]
-    d_ids = torch.arange(n_seq, dtype=torch.int32, device=dev)
-    d_pos = torch.arange(T, dtype=torch.int32, device=dev)[:, None].expand(T, n_seq).contiguous()
-    d_log = torch.empty((T, n_seq, 27), dtype=torch.float32, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.Stream(dev)          # kernels, flushes and events share this stream
-    torch.cuda.set_stream(stream)
-    sp = ctypes.c_void_p(stream.cuda_stream)
-    assert sp.value, "need a non-default stream handle"
-
-    def step():
-        for t in range(T):
-            be.forward_batch_dev(n_seq, 1, ctypes.c_void_p(d_ids.data_ptr()),
-                                 ctypes.c_void_p(d_tok[t].data_ptr()), ctypes.c_void_p(d_pos[t].data_ptr()),
-                                 ctypes.c_void_p(d_log[t].data_ptr()), None, sp)
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    # per-launch kernel time (the dominant kernel) on the launching stream
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        wall0 = time.perf_counter()
-        for s in range(args.steps):
-            flush.fill_(s & 0xFF)
-            ev[s][0].record(stream)
-            step()
-            ev[s][1].record(stream)
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - wall0
-    if world > 1:
-        dist.barrier()
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    my_ms = float(np.sum(step_ms))
-    tmax = torch.tensor([my_ms], device=dev)
-    if world > 1:
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-    total_ms = float(tmax.item())
-    ms_per_step = total_ms / args.steps
-    tokens_per_step = world * n_seq * T
-    value = tokens_per_step / (ms_per_step / 1000.0)
-
-    lo_dec = d_log[:, :64].permute(1, 0, 2).cpu().numpy()   # decode-path logits, first 64 sequences
-
-    # ---- end to end through the public host API: the same 16 decode launches per
-    # step, each a kg_forward_batch call on pinned host buffers (H2D tokens and
-    # positions, D2H logits inside the timed region)
-    h_tok = torch.from_numpy(np.ascontiguousarray(toks.T)).pin_memory()          # [T][n_seq]
-    h_ids = torch.arange(n_seq, dtype=torch.int32).pin_memory()
-    h_pos = torch.arange(T, dtype=torch.int32)[:, None].expand(T, n_seq).contiguous().pin_memory()
-    h_log = torch.empty((T, n_seq, 27), dtype=torch.float32).pin_memory()
-    lib = kgcuda.lib()
-
-    def e2e_step():
-        for t in range(T):
-            rc = lib.kg_forward_batch(be._h, n_seq, ctypes.c_void_p(h_ids.data_ptr()),
-                                      ctypes.c_void_p(h_tok[t].data_ptr()), ctypes.c_void_p(h_pos[t].data_ptr()),
-                                      1, ctypes.c_void_p(h_log[t].data_ptr()), None)
-            if rc:
-                raise RuntimeError(lib.kg_last_error(be._h))
-
-    for _ in range(2):
-        e2e_step()
-    e_steps = max(3, args.steps)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(e_steps):
-        e2e_step()
-    e_el = time.perf_counter() - t0
-    te = torch.tensor([e_el], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e_el = float(te.item())
-    e2e_val = world * n_seq * T * e_steps / e_el
-    # the host-API run and the device-pointer run must agree bit for bit
-    self_diff = float(np.abs(h_log[:, :64].permute(1, 0, 2).numpy() - lo_dec).max())
-
+    fn = bench_c3 if args.workload == "c3" else bench_c2
+    line = fn(args, torch, dist, kgcuda, world, rank, local)
     if rank == 0:
-        # roofline of the dominant kernel: algorithmic HBM bytes per decode launch,
-        # averaged over the 16 positions of a step (reads: token, stored codes+norms
-        # of positions < t; writes: new codes+norms, utility, logits)
-        code_b = 2 * 12 + 2 * 4
-        bytes_per_step = n_seq * sum(4 + t * code_b + code_b + 4 + 27 * 4 for t in range(T))
-        achieved = bytes_per_step / (ms_per_step / 1000.0) / 1e9
-        peaks = {}
         try:
-            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        except Exception:
-            pass
-        peak = peaks.get("hbm_gbs", 6650.0)
-        flops_tok = 2 * (4 * 16 * 16 + 2 * 16 * 64 + 27 * 16) + 2 * (16 * 16 + 4 * 16) + 4 * 2 * 16 * 16
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(workload_config(n_seq), parallelism=f"dp{world} (sequence shards)"),
-            "gpu_launches": T * args.steps,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback",
-                         "note": "exact-order f32 kernel: FP32-issue bound; see fp32_tflops",
-                         "fp32_tflops": flops_tok * tokens_per_step / world / (ms_per_step / 1000.0) / 1e12},
-            "e2e": {"value": e2e_val, "unit": UNIT,
-                    "h2d_bytes_per_step": int(h_tok.numel() * 4 + h_pos.numel() * 4 + T * n_seq * 4),
-                    "d2h_bytes_per_step": int(h_log.numel() * 4 + T * 4)},
-            "self_check_max_abs_diff": self_diff,
-            "clocks": clk.summary(),
-            "wall_s_timed": wall,
-        }
-        try:
-            line["cpu_baseline"] = cpu_baseline()
+            v, cores, sample = (cpu_sample_c3 if args.workload == "c3" else cpu_sample_c2)()
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
         except Exception as ex:  # the baseline must not break the bench line
-            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": 0, "kind": "port",
-                                    "sample": f"failed: {ex}"}
-        print(json.dumps(line), flush=True)
-    be.close()
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": 0, "kind": "port", "sample": f"failed: {ex}"}
+        print(json.dumps(line, default=float), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -175,6 +175,22 @@ int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *k
 /* SP-KV utility of (seq, layer, pos) (SpKvQuantLayerMeta::utilities). */
 int kg_spkv_utility(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, float *utility);
 
+/* ---- phase timing (no reference counterpart; the reference's MBU helpers,
+ * src/mbu.rs, estimate the same bandwidth figures from formulas) ---- */
+enum {
+    KG_PROF_ATTN = 0,   /* decode attention kernels that read the KV codes */
+    KG_PROF_ENCODE = 1, /* TurboQuant encode of new K/V */
+    KG_PROF_GEMM = 2,   /* weight GEMMs (QKV, Wo, W1, W2, lm_head) */
+    KG_PROF_N = 3
+};
+/* Enable (1) or disable (0) recording of CUDA events around each phase on
+ * the stream the kernels run on (bf16 path). */
+int kg_profile(kg_ctx *ctx, int enable);
+/* Synchronise the context's device, then write the summed device time in ms
+ * of every phase since the last read (ms[KG_PROF_N]) and the number of timed
+ * intervals (count[KG_PROF_N]); resets the sums. */
+int kg_profile_read(kg_ctx *ctx, float *ms, int64_t *count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -152,6 +152,9 @@ void kg_ctx_destroy(kg_ctx *ctx) {
     for (void *p : ctx->allocs) cudaFree(p);
     if (ctx->stage) cudaFree(ctx->stage);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    for (int p = 0; p < KG_PROF_N; ++p)
+        for (int e = 0; e < 2; ++e)
+            for (cudaEvent_t ev : ctx->prof_ev[p][e]) cudaEventDestroy(ev);
     delete ctx;
 }
 
@@ -539,18 +542,25 @@ int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint
     const int bits = which == 0 ? ctx->cfg.key_bits : ctx->cfg.val_bits;
     const int64_t pl = packed_len(kvd, bits);
     const size_t bx = align256(n_vec * kvd * 4), bp = align256(n_vec * pl), bn = align256(n_vec * 4);
-    int rc = ensure_stage(ctx, bx + bp + bn);
+    const size_t bs = align256(n_vec);
+    int rc = ensure_stage(ctx, 2 * bx + bp + bn + bs);
     if (rc) return rc;
     char *st = static_cast<char *>(ctx->stage);
     float *dx = reinterpret_cast<float *>(st);
     uint8_t *dp = reinterpret_cast<uint8_t *>(st + bx);
     float *dn = reinterpret_cast<float *>(st + bx + bp);
+    float *dxn = reinterpret_cast<float *>(st + bx + bp + bn);
+    uint8_t *dskip = reinterpret_cast<uint8_t *>(st + 2 * bx + bp + bn);
     cudaStream_t s = ctx->stream;
     KG_CUDA(ctx, cudaMemcpyAsync(dx, x, n_vec * kvd * 4, cudaMemcpyHostToDevice, s));
     // codes of a zero-norm vector are left untouched: start from the caller's bytes
     KG_CUDA(ctx, cudaMemcpyAsync(dp, packed, n_vec * pl, cudaMemcpyHostToDevice, s));
-    KG_CUDA(ctx, kg::tq_encode_device((int)kvd, bits, n_vec, dx, ctx->rot, which == 0 ? ctx->kb : ctx->vb,
-                                      dp, pl, dn, 1, s));
+    const float *bnd = which == 0 ? ctx->kb : ctx->vb;
+    if (kvd % 128 == 0 && (bits == 3 || bits == 4))
+        KG_CUDA(ctx, kg::tq_encode_tiled((int)kvd, bits, n_vec, dx, kvd, ctx->rot, bnd, dp, pl, dn, nullptr,
+                                         nullptr, 0, 0, 0, dxn, dskip, s));
+    else
+        KG_CUDA(ctx, kg::tq_encode_device((int)kvd, bits, n_vec, dx, ctx->rot, bnd, dp, pl, dn, 1, s));
     KG_CUDA(ctx, cudaMemcpyAsync(packed, dp, n_vec * pl, cudaMemcpyDeviceToHost, s));
     KG_CUDA(ctx, cudaMemcpyAsync(norms, dn, n_vec * 4, cudaMemcpyDeviceToHost, s));
     KG_CUDA(ctx, cudaStreamSynchronize(s));
@@ -597,4 +607,44 @@ int kg_spkv_utility(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, float 
     return KG_OK;
 }
 
+int kg_profile(kg_ctx *ctx, int enable) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    ctx->prof = enable != 0;
+    return KG_OK;
+}
+
+int kg_profile_read(kg_ctx *ctx, float *ms, int64_t *count) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    KG_CUDA(ctx, cudaDeviceSynchronize());
+    for (int p = 0; p < KG_PROF_N; ++p) {
+        float tot = 0.0f;
+        for (size_t i = 0; i < ctx->prof_used[p]; ++i) {
+            float t = 0.0f;
+            KG_CUDA(ctx, cudaEventElapsedTime(&t, ctx->prof_ev[p][0][i], ctx->prof_ev[p][1][i]));
+            tot += t;
+        }
+        if (ms) ms[p] = tot;
+        if (count) count[p] = (int64_t)ctx->prof_used[p];
+        ctx->prof_used[p] = 0;
+    }
+    return KG_OK;
+}
+
 }  // extern "C"
+
+namespace kg {
+// Record the begin (end = 0) or end (end = 1) event of one interval of `phase`.
+void prof_mark(kg_ctx *ctx, int phase, int end, cudaStream_t s) {
+    if (!ctx->prof) return;
+    auto &evs = ctx->prof_ev[phase][end];
+    size_t i = ctx->prof_used[phase];
+    while (evs.size() <= i) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return;
+        evs.push_back(e);
+    }
+    cudaEventRecord(evs[i], s);
+    if (end) ctx->prof_used[phase] = i + 1;
+}
+}  // namespace kg

@@ -153,6 +153,8 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.vt, W * kvd, own));
     BIG_TRY(dalloc(&g.vt2, W * kvd, own));
     BIG_TRY(dalloc(&g.nrm, W, own));
+    BIG_TRY(dalloc(&g.xn, W * kvd, own));
+    BIG_TRY(dalloc(&g.skip, W, own));
     // decode attention scratch (max_seqs rows)
     BIG_TRY(dalloc(&g.qrot, S * ctx->nh * kvd, own));
     BIG_TRY(dalloc(&g.qrot2, S * ctx->nh * kvd, own));
@@ -298,12 +300,23 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         bf::Gemm q = gemm0();
         q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = wqkv; q.ldb = n; q.M = M; q.N = nqkv; q.K = n;
         q.epi = bf::EPI_F32; q.C = g.qkv; q.ldc = nqkv;
+        prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(bf::gemm(q, s));
+        prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // TurboQuant encode of K and V into the arena (exact reference order)
-        BIG_TRY(tq_encode_scatter(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
-                                  g.knorm, 1, g.slot_of, g.pos_of, L, B, l, s));
-        BIG_TRY(tq_encode_scatter(kvd, c.val_bits, M, g.qkv + n + kvd, nqkv, ctx->rot, ctx->vb, g.vcodes, ctx->vpl,
-                                  g.vnorm, 1, g.slot_of, g.pos_of, L, B, l, s));
+        prof_mark(ctx, KG_PROF_ENCODE, 0, s);
+        if (kvd % 128 == 0) {
+            BIG_TRY(tq_encode_tiled(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
+                                    g.knorm, g.slot_of, g.pos_of, L, B, l, g.xn, g.skip, s));
+            BIG_TRY(tq_encode_tiled(kvd, c.val_bits, M, g.qkv + n + kvd, nqkv, ctx->rot, ctx->vb, g.vcodes,
+                                    ctx->vpl, g.vnorm, g.slot_of, g.pos_of, L, B, l, g.xn, g.skip, s));
+        } else {
+            BIG_TRY(tq_encode_scatter(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
+                                      g.knorm, 1, g.slot_of, g.pos_of, L, B, l, s));
+            BIG_TRY(tq_encode_scatter(kvd, c.val_bits, M, g.qkv + n + kvd, nqkv, ctx->rot, ctx->vb, g.vcodes,
+                                      ctx->vpl, g.vnorm, 1, g.slot_of, g.pos_of, L, B, l, s));
+        }
+        prof_mark(ctx, KG_PROF_ENCODE, 1, s);
         BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
         if (prefill) {
             // dequantize the prompt's K and V: k~ = norm * (c R)
@@ -340,6 +353,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             sa.slot = g.slot_of; sa.pos = g.pos_of; sa.S = g.Sbuf;
             sa.M = M; sa.nh = nh; sa.kvd = kvd; sa.kpl = (int)ctx->kpl; sa.L = L; sa.B = B; sa.layer = l;
             sa.Tpad = (int)g.Tpad; sa.Tmax = B; sa.scale = scale;
+            prof_mark(ctx, KG_PROF_ATTN, 0, s);
             BIG_TRY(attn::scores(sa, s));
             attn::SoftmaxArgs sm;
             sm.S = g.Sbuf; sm.vnorm = g.vnorm; sm.slot = g.slot_of; sm.pos = g.pos_of; sm.P = g.P; sm.P_lo = g.P2;
@@ -350,6 +364,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             va.pos = g.pos_of; va.U = g.U; va.U_lo = g.U2; va.M = M; va.nh = nh; va.nhp = (int)g.nhp; va.kvd = kvd;
             va.vpl = (int)ctx->vpl; va.L = L; va.B = B; va.layer = l; va.Tpad = (int)g.Tpad;
             BIG_TRY(attn::values(va, s));
+            prof_mark(ctx, KG_PROF_ATTN, 1, s);
             // out_h = R[:, head cols]^T u~_h
             bf::Gemm o = gemm0();
             o.dtype = bf::DT_F16;
@@ -364,7 +379,9 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         bf::Gemm w = gemm0();
         w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
         w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n;
+        prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(bf::gemm(w, s));
+        prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // MLP
         BIG_TRY(cudaMemcpyAsync(g.xr2, g.x, (size_t)M * n * 4, cudaMemcpyDeviceToDevice, s));
         BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s));
@@ -372,11 +389,15 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         bf::Gemm u = gemm0();
         u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
         u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;
+        prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(bf::gemm(u, s));
+        prof_mark(ctx, KG_PROF_GEMM, 1, s);
         bf::Gemm dn = gemm0();
         dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
         dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
+        prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(bf::gemm(dn, s));
+        prof_mark(ctx, KG_PROF_GEMM, 1, s);
         BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
                                     c.sparse_threshold, s));
         if (!spkv) BIG_TRY(bf::delta_route(g.x, g.xr, g.delta, g.dq + (int64_t)l * n, g.dn + (int64_t)l * n, n, M, l, s));
@@ -393,7 +414,9 @@ cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, cudaStream_
     bf::Gemm q = gemm0();
     q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = g.lm; q.ldb = n; q.M = M; q.N = V; q.K = n;
     q.epi = bf::EPI_F32; q.C = lo; q.ldc = V;
+    prof_mark(ctx, KG_PROF_GEMM, 0, s);
     BIG_TRY(bf::gemm(q, s));
+    prof_mark(ctx, KG_PROF_GEMM, 1, s);
     if (probs) BIG_TRY(bf::softmax_rows(lo, probs, V, M, 1.0f / ctx->cfg.temperature, s));
     return cudaSuccess;
 }

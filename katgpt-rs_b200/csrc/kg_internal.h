@@ -52,6 +52,12 @@ cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t
 cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, const float *rot,
                              const float *bnd, uint8_t *packed, int64_t packed_stride,
                              float *norms, int64_t norm_stride, cudaStream_t s);
+// Tiled form for many vectors (dim % 128 == 0, 3/4-bit): same codes and norms;
+// xn_scratch holds n_vec*dim floats and skip_scratch n_vec bytes.
+cudaError_t tq_encode_tiled(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
+                            const float *bnd, uint8_t *packed, int64_t pstride, float *norms,
+                            const int32_t *slot, const int32_t *pos, int L, int B, int layer, float *xn_scratch,
+                            uint8_t *skip_scratch, cudaStream_t s);
 // Same, reading row v at x + v*ldx and writing arena row (slot[v]*L + layer)*B + pos[v].
 cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
                               const float *bnd, uint8_t *packed, int64_t pstride, float *norms, int64_t nstride,
@@ -77,7 +83,8 @@ struct BigState {
     __half *qh = nullptr, *ql = nullptr, *cent = nullptr, *cent2 = nullptr, *kt = nullptr, *kt2 = nullptr,
            *vt = nullptr, *vt2 = nullptr, *qrot = nullptr, *qrot2 = nullptr, *U = nullptr, *U2 = nullptr,
            *P = nullptr, *P2 = nullptr;
-    float *Sbuf = nullptr;
+    float *Sbuf = nullptr, *xn = nullptr;  // xn: normalised K/V rows for the tiled encoder
+    uint8_t *skip = nullptr;
     int *alive = nullptr;
     int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;
 };
@@ -95,6 +102,10 @@ struct kg_ctx {
     bool micro = false;     // shape has the exact-order micro kernel
     bool big_path = false;  // shape runs on the BF16 tensor-core path
     kg::BigState big;
+    // phase timing (kg_profile): CUDA event pairs recorded on the launching stream
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_ev[KG_PROF_N][2];
+    size_t prof_used[KG_PROF_N] = {};
     int64_t n = 0, nh = 0, hd = 0, nkv = 0, kvd = 0, m = 0, V = 0, L = 0, B = 0;
     int64_t kpl = 0, vpl = 0, ph = 0;
     int64_t w_count = 0;
@@ -115,6 +126,7 @@ struct kg_ctx {
 };
 
 namespace kg {
+void prof_mark(kg_ctx *ctx, int phase, int end, cudaStream_t s);
 cudaError_t big_init(kg_ctx *ctx);
 cudaError_t big_reset(kg_ctx *ctx, int64_t slot0, int64_t nslots);
 cudaError_t big_upload_chunk(kg_ctx *ctx, const float *dsrc, int64_t offset, int64_t count);

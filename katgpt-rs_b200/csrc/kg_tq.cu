@@ -180,6 +180,120 @@ __global__ void tq_encode_warp(int dim, int bits, int64_t n_vec, const float *x,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tiled exact encoder. Phase 1 (norm_kernel): per vector, norm = sqrt(simd_sum_sq)
+// and xn = x * (1/norm) in the reference order; vectors with norm < 1e-8 are
+// flagged (their codes stay untouched). Phase 2 (rotate_kernel): r = R xn for a
+// tile of 64 rows x 16 vectors per CTA (8 warps of 16 x 8); lane L of a warp
+// owns the AVX2 lane chain k = L (mod 32) of all 128 outputs of the warp, so
+// each output's FMAs run in the reference order, then tree32 reduces it.
+// Requires dim % 128 == 0.
+constexpr int ER = 64, EV = 16, EK = 128;  // rows, vectors, columns per stage
+
+__global__ void norm_kernel(int dim, int64_t n_vec, const float *x, int64_t ldx, float *xn, uint8_t *skip,
+                            float *norms, const int32_t *slot, const int32_t *pos, int L, int B, int layer) {
+    const int lane = threadIdx.x & 31;
+    const int64_t v = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (v >= n_vec) return;
+    const float *xv = x + v * ldx;
+    const float norm = sqrtf(warp_sum_sq(xv, dim, 1));
+    const int64_t drow = slot ? ((int64_t)slot[v] * L + layer) * B + pos[v] : v;
+    if (lane == 0) {
+        norms[drow] = norm;
+        skip[v] = norm < 1e-8f ? 1 : 0;
+    }
+    const float inv = norm < 1e-8f ? 0.0f : 1.0f / norm;
+    for (int k = lane; k < dim; k += 32) xn[v * dim + k] = xv[k] * inv;
+}
+
+__device__ __forceinline__ void cp16(void *dst, const void *src, bool pred) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(pred ? 16 : 0));
+}
+
+__global__ void __launch_bounds__(256) rotate_kernel(int dim, int bits, int64_t n_vec, const float *xn,
+                                                     const uint8_t *skip, const float *rot, const float *bnd,
+                                                     uint8_t *packed, int64_t pstride, const int32_t *slot,
+                                                     const int32_t *pos, int L, int B, int layer) {
+    extern __shared__ float4 esm[];
+    float *Rs = reinterpret_cast<float *>(esm);   // [2][ER][EK]
+    float *Xs = Rs + 2 * ER * EK;                 // [2][EV][EK]
+    __shared__ uint8_t codes[EV][ER];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wr = warp >> 1, wv = warp & 1;  // 4 x 2 warps: 16 rows x 8 vectors each
+    const int r0 = blockIdx.x * ER;
+    const int64_t v0 = (int64_t)blockIdx.y * EV;
+    const int nst = dim / EK;
+    auto stage = [&](int buf, int st) {
+        const int c0 = st * EK;
+        for (int e = tid; e < ER * EK / 4; e += 256) {  // R rows: 32 chunks of 16 B per row
+            const int r = e / (EK / 4), ch = e % (EK / 4);
+            cp16(Rs + (buf * ER + r) * EK + ch * 4, rot + (int64_t)(r0 + r) * dim + c0 + ch * 4, true);
+        }
+        for (int e = tid; e < EV * EK / 4; e += 256) {
+            const int vv = e / (EK / 4), ch = e % (EK / 4);
+            const int64_t gv = v0 + vv;
+            cp16(Xs + (buf * EV + vv) * EK + ch * 4, xn + min(gv, n_vec - 1) * dim + c0 + ch * 4, gv < n_vec);
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+    };
+    float acc[16][8];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) acc[i][v] = 0.0f;
+    stage(0, 0);
+    for (int st = 0; st < nst; ++st) {
+        const int buf = st & 1;
+        if (st + 1 < nst) {
+            stage(buf ^ 1, st + 1);
+            asm volatile("cp.async.wait_group 1;\n" ::);
+        } else {
+            asm volatile("cp.async.wait_group 0;\n" ::);
+        }
+        __syncthreads();
+        const float *Rb = Rs + (buf * ER + wr * 16) * EK;
+        const float *Xb = Xs + (buf * EV + wv * 8) * EK;
+#pragma unroll
+        for (int cc = 0; cc < EK / 32; ++cc) {  // one 32-wide chunk: lane L holds element 32*c + L
+            float xv[8];
+#pragma unroll
+            for (int v = 0; v < 8; ++v) xv[v] = Xb[v * EK + cc * 32 + lane];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float r = Rb[i * EK + cc * 32 + lane];
+#pragma unroll
+                for (int v = 0; v < 8; ++v) acc[i][v] = fmaf(r, xv[v], acc[i][v]);
+            }
+        }
+        __syncthreads();  // buffer reused by the stage after next
+    }
+    // fixed-order reductions; the remaining-8-chunk and tail terms are empty (dim % 32 == 0),
+    // so sum = tree32 + hsum(0) = tree32 + 0
+    const int nb = (1 << bits) - 1;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            float r = tree32(acc[i][v]);
+            r = r + 0.0f;
+            if (lane == 0) {
+                int c = 0;
+                for (int b = 0; b < nb; ++b) c += (r >= bnd[b]) ? 1 : 0;
+                codes[wv * 8 + v][wr * 16 + i] = (uint8_t)c;
+            }
+        }
+    __syncthreads();
+    // pack 64 codes per vector: 32 bytes (3/4-bit) at byte offset r0/2
+    for (int e = tid; e < EV * (ER / 2); e += 256) {
+        const int vv = e / (ER / 2), b = e % (ER / 2);
+        const int64_t gv = v0 + vv;
+        if (gv >= n_vec || skip[gv]) continue;
+        const int64_t drow = slot ? ((int64_t)slot[gv] * L + layer) * B + pos[gv] : gv;
+        packed[drow * pstride + r0 / 2 + b] = (uint8_t)((codes[vv][2 * b] & 15) | ((codes[vv][2 * b + 1] & 15) << 4));
+    }
+}
+
 }  // namespace
 
 cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t, float *work,
@@ -214,6 +328,27 @@ cudaError_t tq_encode_device(int dim, int bits, int64_t n_vec, const float *x, c
                              int64_t nstride, cudaStream_t s) {
     return tq_encode_scatter(dim, bits, n_vec, x, dim, rot, bnd, packed, pstride, norms, nstride, nullptr,
                              nullptr, 0, 0, 0, s);
+}
+
+cudaError_t tq_encode_tiled(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
+                            const float *bnd, uint8_t *packed, int64_t pstride, float *norms,
+                            const int32_t *slot, const int32_t *pos, int L, int B, int layer, float *xn_scratch,
+                            uint8_t *skip_scratch, cudaStream_t s) {
+    if (n_vec <= 0) return cudaSuccess;
+    if (dim % EK || (bits != 3 && bits != 4)) return cudaErrorInvalidValue;
+    norm_kernel<<<(unsigned)((n_vec + 7) / 8), 256, 0, s>>>(dim, n_vec, x, ldx, xn_scratch, skip_scratch, norms, slot,
+                                                             pos, L, B, layer);
+    const int smem = 2 * (ER + EV) * EK * 4;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    dim3 grid(dim / ER, (unsigned)((n_vec + EV - 1) / EV));
+    rotate_kernel<<<grid, 256, smem, s>>>(dim, bits, n_vec, xn_scratch, skip_scratch, rot, bnd, packed, pstride, slot,
+                                          pos, L, B, layer);
+    return cudaGetLastError();
 }
 
 cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,

@@ -83,6 +83,8 @@ def lib():
             "kg_tq_encode": (ctypes.c_int, [P, I32, I64, P, P, P]),
             "kg_kv_codes": (ctypes.c_int, [P, I32, I32, I32, P, P, P]),
             "kg_spkv_utility": (ctypes.c_int, [P, I32, I32, I32, P]),
+            "kg_profile": (ctypes.c_int, [P, ctypes.c_int]),
+            "kg_profile_read": (ctypes.c_int, [P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -239,6 +241,16 @@ class CudaBackend:
         nr = np.empty(2, np.float32)
         self._check(lib().kg_kv_codes(self._h, seq, layer, pos, _ptr(kp), _ptr(vp), _ptr(nr)))
         return kp, vp, nr
+
+    def profile(self, enable=True):
+        self._check(lib().kg_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self):
+        """Summed device ms and interval counts per phase (attn, encode, gemm)."""
+        ms = np.zeros(3, np.float32)
+        cnt = np.zeros(3, np.int64)
+        self._check(lib().kg_profile_read(self._h, _ptr(ms), _ptr(cnt)))
+        return ms, cnt
 
     def spkv_utility(self, seq, layer, pos):
         u = np.empty(1, np.float32)
