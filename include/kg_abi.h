@@ -7,7 +7,7 @@
  * token, pos, config) -> &mut [f32]` per token, plus device_name /
  * supports_stateful / reset / compile / is_compiled / recompile_hint. A Rust
  * `CudaBackend` implementing that trait binds the entry points below through
- * a thin `extern "C"` block; the batched entry points are
+ * a thin `extern "C"` block over these declarations; the batched entry points are
  * the extension the trait lacks (prefill over T positions, decode over many
  * sequences).
  *

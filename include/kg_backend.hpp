@@ -1,0 +1,80 @@
+// kg_backend.hpp — C++ host mirror of the reference's InferenceBackend trait
+// (src/inference_backend.rs:45-92) over the C ABI in kg_abi.h.
+//
+// The reference's host language is Rust; without a Rust toolchain, this
+// header is the host-side mirror of the trait in C++ (a Rust binding is a thin
+// extern "C" block over kg_abi.h). Method names, argument
+// meaning and error behaviour follow the trait:
+//   forward        -> one token at `pos`; returns vocab_size logits that stay
+//                     valid until the next call (the trait returns a slice
+//                     borrowed from ForwardContext::logits)
+//   device_name    -> "CUDA:<device>"
+//   supports_stateful -> true (the KV cache lives on the device)
+//   reset          -> a new sequence (MultiLayerKVCache::reset semantics)
+//   compile        -> upload weights; failures map to CompileError variants
+//   is_compiled, recompile_hint
+// forward() cannot fail in the trait; here a device error throws (the Metal
+// backend's forward panics through expect() in the same situation).
+#pragma once
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "kg_abi.h"
+
+namespace katgpt {
+
+// CompileError (src/inference_backend.rs:14-40)
+struct CompileError : std::runtime_error {
+    enum Kind { UnsupportedBackend, DeviceError, InvalidWeights } kind;
+    CompileError(Kind k, const std::string &m) : std::runtime_error(m), kind(k) {}
+};
+
+class CudaBackend {
+   public:
+    explicit CudaBackend(const kg_config &cfg, int device = 0, int32_t seq = 0) : cfg_(cfg), seq_(seq) {
+        int rc = kg_ctx_create(&cfg_, device, &ctx_);
+        if (rc != KG_OK) throw CompileError(CompileError::DeviceError, kg_status_string(rc));
+        logits_.resize(cfg_.vocab_size);
+    }
+    ~CudaBackend() { kg_ctx_destroy(ctx_); }
+    CudaBackend(const CudaBackend &) = delete;
+    CudaBackend &operator=(const CudaBackend &) = delete;
+
+    // InferenceBackend::forward (the ForwardContext/MultiLayerKVCache arguments
+    // of the trait are owned on the device here)
+    std::vector<float> &forward(int32_t token, int32_t pos) {
+        int rc = kg_forward_token(ctx_, seq_, token, pos, logits_.data());
+        if (rc != KG_OK) throw std::runtime_error(std::string("kg_forward_token: ") + kg_last_error(ctx_));
+        return logits_;
+    }
+    const char *device_name() const { return kg_device_name(ctx_); }
+    bool supports_stateful() const { return true; }
+    void reset() { kg_seq_reset(ctx_, seq_); }
+    // weights: the flat TransformerWeights layout (kg_weights_count floats)
+    void compile(const std::vector<float> &weights) {
+        int rc = kg_upload_weights(ctx_, weights.data(), (int64_t)weights.size());
+        if (rc == KG_ERR_INVALID_WEIGHTS) throw CompileError(CompileError::InvalidWeights, kg_last_error(ctx_));
+        if (rc == KG_ERR_UNSUPPORTED) throw CompileError(CompileError::UnsupportedBackend, kg_last_error(ctx_));
+        if (rc != KG_OK) throw CompileError(CompileError::DeviceError, kg_last_error(ctx_));
+    }
+    bool is_compiled() const { return kg_is_compiled(ctx_) != 0; }
+    void recompile_hint() { /* weights are re-uploaded explicitly by compile() */ }
+
+    // batched extension: teacher-forced positions [start, start+T) of n_seq sequences
+    void forward_batch(int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, const int32_t *start_pos,
+                       int32_t T, float *logits, float *probs = nullptr) {
+        int rc = kg_forward_batch(ctx_, n_seq, seq_ids, tokens, start_pos, T, logits, probs);
+        if (rc != KG_OK) throw std::runtime_error(std::string("kg_forward_batch: ") + kg_last_error(ctx_));
+    }
+    kg_ctx *handle() { return ctx_; }
+
+   private:
+    kg_config cfg_;
+    kg_ctx *ctx_ = nullptr;
+    int32_t seq_;
+    std::vector<float> logits_;
+};
+
+}  // namespace katgpt

@@ -69,3 +69,15 @@ def test_invalid_config_rejected_without_device(kg):
     h = ctypes.c_void_p()
     rc = kg.lib().kg_ctx_create(ctypes.byref(c), 0, ctypes.byref(h))
     assert rc == -1 and not h
+
+
+def test_cpp_trait_mirror_compiles(tmp_path):
+    """include/kg_backend.hpp (the C++ InferenceBackend mirror) compiles against kg_abi.h."""
+    import subprocess
+    src = tmp_path / "t.cpp"
+    src.write_text('#include "kg_backend.hpp"\n'
+                   'int main() { kg_config c; kg_config_micro(&c); katgpt::CudaBackend b(c); '
+                   'b.reset(); return b.is_compiled() ? 0 : 1; }\n')
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.join(ROOT, "include"), str(src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
