@@ -168,6 +168,23 @@ int kg_tq_tables(const kg_ctx *ctx, float *rotation, float *key_centroids, float
  * (TurboQuantKVCache::store_key/store_value, kv_cache.rs:156-237). */
 int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed,
                  float *norms);
+/* Allocation-free form of kg_tq_encode (no counterpart in the reference).
+ * For callers that cannot allocate device memory while they encode: a decode
+ * loop between captured or latency-critical stages (cudaMalloc/cudaFree
+ * synchronise the whole device) or a host that fixes the library's memory
+ * budget up front. x [n_vec][kv_dim], packed [n_vec][packed_len] and norms
+ * [n_vec] are caller-owned DEVICE pointers; the work is enqueued on `stream`
+ * (cudaStream_t, NULL = legacy default stream) and the call does not
+ * synchronise. The encoder's scratch lives in a fixed device array of
+ * 1,048,576 floats (4 MiB) plus 65,536 flag bytes that every GPU loading the
+ * library holds until exit: calls with n_vec * kv_dim > 1,048,576 are
+ * rejected with KG_ERR_INVALID_ARG. The first call on a device looks up that
+ * array's address (make it before any stream capture). Calls share the array,
+ * so calls that overlap on the GPU race; nothing in it needs clearing (each
+ * call writes every scratch row it reads). Codes of zero-norm vectors are
+ * left as found in `packed`, as in kg_tq_encode. */
+int kg_tq_encode_noalloc(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed,
+                         float *norms, void *stream);
 /* Read back the stored codes and norms of (seq, layer, pos): key codes, value
  * codes, norms[2] = {key, value}. */
 int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *key_codes,

@@ -15,6 +15,9 @@
 //   horizontal_sum_256 tree.
 //
 // Compiled with -fmad=false.
+#include <mutex>
+#include <string>
+
 #include "kg_exact.cuh"
 #include "kg_internal.h"
 
@@ -372,3 +375,92 @@ cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, 
 }
 
 }  // namespace kg
+
+// ---------------------------------------------------------------------------
+// Allocation-free encoder entry point.
+//
+// Some callers cannot allocate device memory at the moment they encode: code
+// running between the stages of a captured or latency-critical decode loop
+// (cudaMalloc and cudaFree synchronise the whole device), and hosts that hand
+// the library a fixed memory budget up front and forbid growth afterwards
+// (the zero-alloc discipline of the reference's TurboQuant hot path). For
+// them kg_tq_encode_noalloc takes device pointers for its inputs and outputs
+// and keeps the encoder's scratch (normalised rows and zero-norm flags) in the
+// file-scope arrays below, which every GPU that loads this library holds
+// until the process exits.
+namespace kg {
+namespace {
+constexpr int64_t kNoAllocMaxFloats = int64_t(1) << 20;  // 4 MiB of normalised rows (n_vec * kv_dim)
+constexpr int64_t kNoAllocMaxVectors = int64_t(1) << 16;  // zero-norm flags
+static __device__ __align__(256) float g_noalloc_xn[kNoAllocMaxFloats];
+static __device__ __align__(256) uint8_t g_noalloc_skip[kNoAllocMaxVectors];
+
+// Device addresses of the arrays above, looked up once per device with that
+// device current (the host-side names are stand-ins, not device addresses).
+std::mutex g_noalloc_mu;
+float *g_noalloc_xn_ptr[64] = {};
+uint8_t *g_noalloc_skip_ptr[64] = {};
+
+cudaError_t noalloc_scratch(int device, float **xn, uint8_t **skip) {
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_xn_ptr[device]) {
+        void *a = nullptr, *b = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&a, g_noalloc_xn);
+        if (e != cudaSuccess) return e;
+        e = cudaGetSymbolAddress(&b, g_noalloc_skip);
+        if (e != cudaSuccess) return e;
+        g_noalloc_xn_ptr[device] = static_cast<float *>(a);
+        g_noalloc_skip_ptr[device] = static_cast<uint8_t *>(b);
+    }
+    *xn = g_noalloc_xn_ptr[device];
+    *skip = g_noalloc_skip_ptr[device];
+    return cudaSuccess;
+}
+}  // namespace
+}  // namespace kg
+
+extern "C" int kg_tq_encode_noalloc(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed,
+                                    float *norms, void *stream) {
+    if (!ctx || !x || !packed || !norms || n_vec < 0 || (which != 0 && which != 1)) return KG_ERR_INVALID_ARG;
+    if (ctx->cfg.kv_mode == KG_KV_F32) {
+        ctx->err = "context has no TurboQuant codec";
+        return KG_ERR_INVALID_ARG;
+    }
+    const int64_t kvd = ctx->kvd;
+    if (n_vec * kvd > kg::kNoAllocMaxFloats || n_vec > kg::kNoAllocMaxVectors) {
+        ctx->err = "kg_tq_encode_noalloc: n_vec * kv_dim exceeds the fixed scratch of " +
+                   std::to_string(kg::kNoAllocMaxFloats) + " floats (at most " +
+                   std::to_string(kg::kNoAllocMaxFloats / kvd) + " vectors at this kv_dim)";
+        return KG_ERR_INVALID_ARG;
+    }
+    if (n_vec == 0) return KG_OK;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) {
+        ctx->err = std::string("cudaSetDevice: ") + cudaGetErrorString(e);
+        return KG_ERR_CUDA;
+    }
+    float *xn = nullptr;
+    uint8_t *skip = nullptr;
+    e = kg::noalloc_scratch(ctx->device, &xn, &skip);
+    if (e != cudaSuccess) {
+        ctx->err = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e);
+        return KG_ERR_CUDA;
+    }
+    const int bits = which == 0 ? ctx->cfg.key_bits : ctx->cfg.val_bits;
+    const float *bnd = which == 0 ? ctx->kb : ctx->vb;
+    const int64_t pl = (bits == 2) ? (kvd + 3) / 4 : (bits == 3 || bits == 4) ? (kvd + 1) / 2 : (bits == 8) ? kvd
+                                                                                               : (kvd * bits + 7) / 8;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (kvd % 128 == 0 && (bits == 3 || bits == 4))
+        e = kg::tq_encode_tiled((int)kvd, bits, n_vec, x, kvd, ctx->rot, bnd, packed, pl, norms, nullptr, nullptr, 0, 0,
+                                0, xn, skip, s);
+    else
+        e = kg::tq_encode_device((int)kvd, bits, n_vec, x, ctx->rot, bnd, packed, pl, norms, 1, s);
+    if (e != cudaSuccess) {
+        ctx->err = std::string("kg_tq_encode_noalloc: ") + cudaGetErrorString(e);
+        return KG_ERR_CUDA;
+    }
+    return KG_OK;
+}
+

@@ -81,6 +81,7 @@ def lib():
             "kg_tq_packed_len": (I64, [I64, I32]),
             "kg_tq_tables": (ctypes.c_int, [P, P, P, P, P, P]),
             "kg_tq_encode": (ctypes.c_int, [P, I32, I64, P, P, P]),
+            "kg_tq_encode_noalloc": (ctypes.c_int, [P, I32, I64, P, P, P, P]),
             "kg_kv_codes": (ctypes.c_int, [P, I32, I32, I32, P, P, P]),
             "kg_spkv_utility": (ctypes.c_int, [P, I32, I32, I32, P]),
             "kg_profile": (ctypes.c_int, [P, ctypes.c_int]),
