@@ -19,6 +19,10 @@
 // the dequantized cache), softmax with 1/sqrt(head_dim) (transformer.rs:333-389).
 #include <cuda_bf16.h>
 
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
 #include "kg_attn.cuh"
 
 namespace kg {
@@ -26,6 +30,7 @@ namespace attn {
 namespace {
 
 using bf16 = __nv_bfloat16;
+namespace cg = cooperative_groups;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -70,221 +75,371 @@ __device__ __forceinline__ void build_lut(uint2 *lut, const float *cent) {
 }
 
 // ---------------------------------------------------------------------------
-// Decode scores: one warp = 16 positions x all heads, K = kv_dim.
-// The k dimension is permuted per 64-dim block so that each thread reads 8
-// contiguous code bytes of a row (see file notes); q~ is permuted the same way.
-template <int NT>  // n-tiles of 8 heads
-__global__ void __launch_bounds__(128) scores_kernel(const ScoreArgs a) {
-    __shared__ uint2 lut[256];
-    build_lut(lut, a.kcent);
+// 256-entry byte table (byte -> centroid pair of its two nibbles, f16 hi/lo)
+// replicated 16 times: entry (b, r) sits at b * 16 + r and lane l reads
+// replica l & 15, so the 32 lookups of a warp land in 16 distinct bank pairs
+// (two wavefronts for any byte pattern).
+constexpr int LUT_ENTRIES = 256 * 16;
+__device__ __forceinline__ void build_lut_rep(uint2 *lut, const float *cent) {
+    __shared__ uint2 base[256];
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+        uint32_t hi, lo;
+        split_h2(cent[b & 15], cent[b >> 4], hi, lo);
+        base[b] = make_uint2(hi, lo);
+    }
     __syncthreads();
-    const int m = blockIdx.y;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < LUT_ENTRIES; i += blockDim.x) lut[i] = base[i >> 4];
+}
+// byte k (0..3) of w through the replicated table (lutl = lut + (lane & 15))
+__device__ __forceinline__ uint2 lut_byte(const uint2 *lutl, uint32_t w, int k) {
+    return lutl[((w >> (8 * k)) & 0xffu) << 4];
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
+    const int sz = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(sz));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src));
+}
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// ---------------------------------------------------------------------------
+// Decode attention, flash-decoding style, one kernel. The positions [0, tn)
+// of a token are cut into ATTEND_CHUNKS equal chunks (multiples of 16); one
+// CTA per chunk, and the chunk CTAs of a token form a thread-block cluster.
+//  A. scores of the chunk, s[h, t] = norm_k[t] * scale * <centroid(code_k[t]), q~_h>:
+//     mma.sync m16n8k16, positions as M, heads as N (NT tiles of 8), kv_dim
+//     as K in 64-dim blocks. A thread reads 8 code bytes of each of its rows
+//     per block; byte 2st (dims 16c + 4st, +1) feeds k-cols 2c, 2c + 1 of
+//     step st, byte 2st + 1 (dims 16c + 4st + 2, +3) k-cols 2c + 8, 2c + 9,
+//     so q~ is consumed in natural dim order. Codes of the block and q~ go
+//     through a cp.async ring in shared memory.
+//  B. local softmax per head: m = max s, l = sum exp(s - m),
+//     p = exp(s - m) * norm_v as an f16 hi/lo tile.
+//  C. u~_chunk[h, d] = sum_t p[h, t] * centroid(code_v[t, d]): heads as M
+//     (A = p via ldmatrix), dims as N, positions as K, over a ring of 16-row
+//     code tiles. A thread reads the 4-byte word (dims 8g .. 8g + 7 of a
+//     64-dim block) of positions 2c, 2c + 1, 2c + 8, 2c + 9; each byte goes
+//     through the table and prmt pairs the two positions of a dim into one
+//     B register, so n-tile jj of the block holds dims 8n + jj.
+//     The chunks combine through distributed shared memory,
+//     u~ = sum_r exp(m_r - M) u~_r / sum_r exp(m_r - M) l_r, written as f16
+//     hi/lo, one dim group at a time.
+// Every product uses hi*hi + lo*hi + hi*lo of the f16 splits.
+constexpr int SSTG = 3, VSTG = 4;
+template <int NT, int MT, int MTV, int NBW>
+__global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a) {
+    extern __shared__ __align__(16) unsigned char dsm[];
+    constexpr int HP = 16 * MTV, QROW = 72;
+    const int NCH = gridDim.x, chmax = a.chmax, nbg = a.nbg, DG = 64 * nbg;
+    const int SROW = chmax + 4, PROW = chmax + 8, UROW = DG + 4;
+    uint2 *lut = reinterpret_cast<uint2 *>(dsm);
+    unsigned char *ring = dsm + a.off_ring;
+    float *Ss = reinterpret_cast<float *>(dsm + a.off_S);        // [HP][SROW]
+    __half *Ph = reinterpret_cast<__half *>(dsm + a.off_P);      // [HP][PROW]
+    __half *Pl = Ph + HP * PROW;
+    float *part = reinterpret_cast<float *>(dsm + a.off_part);   // [HP][UROW]
+    float *mloc = reinterpret_cast<float *>(dsm + a.off_small);  // [HP]
+    float *lloc = mloc + HP;                                     // [HP]
+    float *wgt = lloc + HP;                                      // [NCH][HP]
+    float *kn_s = wgt + NCH * HP;                                // [chmax]
+    float *vn_s = kn_s + chmax;                                  // [chmax]
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int m = blockIdx.z;
+    const int tn = a.pos[m] + 1;
+    const int chl = ((tn + NCH - 1) / NCH + 15) / 16 * 16;
+    const int c0 = rank * chl, nloc = max(0, min(tn, c0 + chl) - c0);
+    const int nmt = (nloc + 15) / 16;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
-    const int pos = a.pos[m];
-    const int tn = pos + 1;
-    const int t0 = blockIdx.x * 64 + warp * 16;
-    if (t0 >= tn) return;
-    const int slot = a.slot[m];
-    const int64_t rowbase = ((int64_t)slot * a.L + a.layer) * a.B;
-    const uint8_t *codes = a.kcodes + rowbase * a.kpl;
-    const int r0 = min(t0 + g, tn - 1), r1 = min(t0 + g + 8, tn - 1);
-    const uint8_t *c0 = codes + (int64_t)r0 * a.kpl, *c1 = codes + (int64_t)r1 * a.kpl;
-    const __half *qt = a.qrot + (int64_t)m * a.nh * a.kvd;
-    const __half *ql = a.qrot_lo + (int64_t)m * a.nh * a.kvd;
-    float acc[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
+    const uint2 *lutl = lut + (lane & 15);
+    const int64_t rowbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+
+    // ---- A. scores
+    const uint8_t *kcodes = a.kcodes + rowbase * a.kpl;
+    const __half *qh = a.qrot + (int64_t)m * a.nh * a.kvd, *ql = a.qrot_lo + (int64_t)m * a.nh * a.kvd;
     const int nblk = a.kvd / 64;
-    for (int q = 0; q < nblk; ++q) {
-        const uint2 w0 = *reinterpret_cast<const uint2 *>(c0 + q * 32 + c * 8);
-        const uint2 w1 = *reinterpret_cast<const uint2 *>(c1 + q * 32 + c * 8);
-        uint32_t bq[NT][8], bl[NT][8];
+    int mg = 0;  // first m-tile of the current group of 4 * MT
+    auto sstage = [&](int q) {
+        unsigned char *st = ring + (q % SSTG) * a.sstage;
+        const int rows = min(4 * MT, nmt - mg) * 16;
+        for (int i = tid; i < rows * 2; i += 128) {  // code rows: 2 x 16 bytes each
+            const int r = i >> 1, h16 = i & 1;
+            const int t = min(c0 + mg * 16 + r, tn - 1);
+            cp_async16(smem_u32(st + r * 32 + h16 * 16), kcodes + (int64_t)t * a.kpl + q * 32 + h16 * 16, true);
+        }
+        __half *qs = reinterpret_cast<__half *>(st + 4 * MT * 16 * 32);
+        for (int i = tid; i < 2 * NT * 8 * 8; i += 128) {
+            const int hl = i / (NT * 8 * 8), r = (i / 8) % (NT * 8), ch = i % 8;
+            const bool ok = r < a.nh;
+            const __half *src = (hl ? ql : qh) + (int64_t)(ok ? r : 0) * a.kvd + q * 64 + ch * 8;
+            cp_async16(smem_u32(qs + (hl * NT * 8 + r) * QROW + ch * 8), src, ok);
+        }
+    };
+    auto prologue = [&]() {
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            const int h = j * 8 + g;
-            if (h < a.nh) {
-                const int64_t off = (int64_t)h * a.kvd + q * 64 + c * 16;
-                const uint4 *src = reinterpret_cast<const uint4 *>(qt + off);
-                const uint4 *srl = reinterpret_cast<const uint4 *>(ql + off);
-                uint4 u0 = src[0], u1 = src[1], v0 = srl[0], v1 = srl[1];
+        for (int s = 0; s < SSTG - 1; ++s) {
+            if (s < nblk) sstage(s);
+            cp_commit();
+        }
+    };
+    if (nmt > 0) {
+        for (int t = tid; t < nloc; t += 128) {
+            cp_async4(smem_u32(kn_s + t), a.knorm + rowbase + c0 + t);
+            cp_async4(smem_u32(vn_s + t), a.vnorm + rowbase + c0 + t);
+        }
+        prologue();
+    }
+    build_lut_rep(lut, a.kcent);
+    for (; mg < nmt; mg += 4 * MT) {
+        if (mg > 0) prologue();
+        const int gm = min(4 * MT, nmt - mg);
+        float acc[MT][NT][4];
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
+        for (int q = 0; q < nblk; ++q) {
+            cp_wait<SSTG - 2>();
+            __syncthreads();
+            if (q + SSTG - 1 < nblk) sstage(q + SSTG - 1);
+            cp_commit();
+            const unsigned char *st = ring + (q % SSTG) * a.sstage;
+            const __half *qs = reinterpret_cast<const __half *>(st + 4 * MT * 16 * 32);
+            uint32_t bq[NT][8], bl[NT][8];
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const uint4 *sh = reinterpret_cast<const uint4 *>(qs + (j * 8 + g) * QROW + c * 16);
+                const uint4 *sl = reinterpret_cast<const uint4 *>(qs + (NT * 8 + j * 8 + g) * QROW + c * 16);
+                const uint4 u0 = sh[0], u1 = sh[1], v0 = sl[0], v1 = sl[1];
                 bq[j][0] = u0.x; bq[j][1] = u0.y; bq[j][2] = u0.z; bq[j][3] = u0.w;
                 bq[j][4] = u1.x; bq[j][5] = u1.y; bq[j][6] = u1.z; bq[j][7] = u1.w;
                 bl[j][0] = v0.x; bl[j][1] = v0.y; bl[j][2] = v0.z; bl[j][3] = v0.w;
                 bl[j][4] = v1.x; bl[j][5] = v1.y; bl[j][6] = v1.z; bl[j][7] = v1.w;
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) bq[j][e] = bl[j][e] = 0u;
-            }
-        }
-#pragma unroll
-        for (int st = 0; st < 4; ++st) {
-            // step st uses bytes 2st (k-cols 2c,2c+1) and 2st+1 (k-cols 8+2c, 9+2c)
-            const uint32_t lo0 = st < 2 ? w0.x : w0.y, lo1 = st < 2 ? w1.x : w1.y;
-            const int sh = (st & 1) * 16;
-            const uint2 e0 = lut[(lo0 >> sh) & 0xff], e2 = lut[(lo0 >> (sh + 8)) & 0xff];
-            const uint2 e1 = lut[(lo1 >> sh) & 0xff], e3 = lut[(lo1 >> (sh + 8)) & 0xff];
-#pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                mma_f16(acc[j], e0.x, e1.x, e2.x, e3.x, bq[j][2 * st], bq[j][2 * st + 1]);
-                mma_f16(acc[j], e0.y, e1.y, e2.y, e3.y, bq[j][2 * st], bq[j][2 * st + 1]);
-                mma_f16(acc[j], e0.x, e1.x, e2.x, e3.x, bl[j][2 * st], bl[j][2 * st + 1]);
-            }
-        }
-    }
-    // epilogue: s = acc * norm_k[t] * scale; positions >= tn are -inf
-    const float *kn = a.knorm + rowbase;
-    float *S = a.S + (int64_t)m * a.nh * a.Tpad;
-#pragma unroll
-    for (int hrow = 0; hrow < 2; ++hrow) {
-        const int t = t0 + g + hrow * 8;
-        const float f = t < tn ? kn[t] * a.scale : 0.0f;
-#pragma unroll
-        for (int j = 0; j < NT; ++j)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int h = j * 8 + c * 2 + e;
-                if (h < a.nh && t < a.Tpad) S[(int64_t)h * a.Tpad + t] = t < tn ? acc[j][hrow * 2 + e] * f : -INFINITY;
-            }
-    }
-}
-
-// softmax over positions per (token, head); p = softmax(s) * norm_v as f16 hi/lo, zero-padded
-__global__ void softmax_kernel(const SoftmaxArgs a) {
-    __shared__ float red[32];
-    const int m = blockIdx.y, h = blockIdx.x;
-    const int tn = a.pos[m] + 1;
-    const float *s = a.S + ((int64_t)m * a.nh + h) * a.Tpad;
-    __half *p = a.P + ((int64_t)m * a.nhp + h) * a.Tpad;
-    __half *pl = a.P_lo + ((int64_t)m * a.nhp + h) * a.Tpad;
-    const int64_t rowbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
-    const float *vn = a.vnorm + rowbase;
-    float mx = -INFINITY;
-    for (int t = threadIdx.x; t < tn; t += blockDim.x) mx = fmaxf(mx, s[t]);
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    mx = -INFINITY;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
-    __syncthreads();
-    float sum = 0.0f;
-    for (int t = threadIdx.x; t < tn; t += blockDim.x) sum += expf(s[t] - mx);
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-    __syncthreads();
-    sum = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) sum += red[i];
-    const float inv = 1.0f / sum;
-    for (int t = threadIdx.x; t < a.Tpad; t += blockDim.x) {
-        const float v = t < tn ? expf(s[t] - mx) * inv * vn[t] : 0.0f;
-        const __half hv = __float2half_rn(v);
-        p[t] = hv;
-        pl[t] = __float2half_rn(v - __half2float(hv));
-    }
-}
-
-// zero the padded head rows of P (heads nh..nhp-1) once per call
-__global__ void zero_rows_kernel(__half *P, __half *P_lo, int nh, int nhp, int Tpad) {
-    const int m = blockIdx.y, h = nh + blockIdx.x;
-    __half *p = P + ((int64_t)m * nhp + h) * Tpad, *pl = P_lo + ((int64_t)m * nhp + h) * Tpad;
-    for (int t = threadIdx.x; t < Tpad; t += blockDim.x) p[t] = pl[t] = __float2half_rn(0.0f);
-}
-
-// ---------------------------------------------------------------------------
-// Decode values: u~[h, i] = sum_t p[h, t] * centroid(code_v[t, i]).
-// CTA = 64 dims x all heads; 4 warps x 16 dims; positions in tiles of 32.
-template <int MT>  // m-tiles of 16 heads
-__global__ void __launch_bounds__(128) values_kernel(const ValueArgs a) {
-    __shared__ uint2 lut[256];
-    __shared__ __align__(16) __half tile[2][32][72];  // hi / lo: 32 positions x 64 dims (+8 pad)
-    build_lut(lut, a.vcent);
-    const int m = blockIdx.y, d0 = blockIdx.x * 64;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, c = lane & 3;
-    const int tn = a.pos[m] + 1;
-    const int64_t rowbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
-    const uint8_t *codes = a.vcodes + rowbase * a.vpl + d0 / 2;
-    const __half *P = a.P + (int64_t)m * a.nhp * a.Tpad;
-    const __half *Pl = a.P_lo + (int64_t)m * a.nhp * a.Tpad;
-    float acc[MT][2][4];
-#pragma unroll
-    for (int i = 0; i < MT; ++i)
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
-    const int ntile = (tn + 31) / 32;
-    for (int tt = 0; tt < ntile; ++tt) {
-        __syncthreads();  // lut ready / previous tile consumed
-        {   // stage: thread -> (position tid/4, 8 bytes = 16 dims)
-            const int pr = threadIdx.x >> 2, part = threadIdx.x & 3;
-            const int t = tt * 32 + pr;
-            uint2 w = make_uint2(0u, 0u);
-            if (t < tn) w = *reinterpret_cast<const uint2 *>(codes + (int64_t)t * a.vpl + part * 8);
-            uint32_t oh[8], ol[8];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint2 e0 = lut[(w.x >> (8 * b)) & 0xff], e1 = lut[(w.y >> (8 * b)) & 0xff];
-                oh[b] = e0.x; ol[b] = e0.y;
-                oh[4 + b] = e1.x; ol[4 + b] = e1.y;
-            }
-            uint4 *dh = reinterpret_cast<uint4 *>(&tile[0][pr][part * 16]);
-            uint4 *dl = reinterpret_cast<uint4 *>(&tile[1][pr][part * 16]);
-            dh[0] = make_uint4(oh[0], oh[1], oh[2], oh[3]);
-            dh[1] = make_uint4(oh[4], oh[5], oh[6], oh[7]);
-            dl[0] = make_uint4(ol[0], ol[1], ol[2], ol[3]);
-            dl[1] = make_uint4(ol[4], ol[5], ol[6], ol[7]);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {  // two k16 steps (positions)
-            const int tk = tt * 32 + ks * 16;
-            uint32_t bh[4], bw[4];
-            {
-                const int r = ks * 16 + (lane & 15);
-                const int col = warp * 16 + ((lane >> 4) << 3);
-                ldsm_x4_t(smem_u32(&tile[0][r][col]), bh[0], bh[1], bh[2], bh[3]);
-                ldsm_x4_t(smem_u32(&tile[1][r][col]), bw[0], bw[1], bw[2], bw[3]);
             }
 #pragma unroll
             for (int i = 0; i < MT; ++i) {
-                const int64_t o0 = (int64_t)(i * 16 + g) * a.Tpad + tk, o1 = o0 + 8 * (int64_t)a.Tpad;
-                const uint32_t a0 = *reinterpret_cast<const uint32_t *>(P + o0 + 2 * c);
-                const uint32_t a1 = *reinterpret_cast<const uint32_t *>(P + o1 + 2 * c);
-                const uint32_t a2 = *reinterpret_cast<const uint32_t *>(P + o0 + 8 + 2 * c);
-                const uint32_t a3 = *reinterpret_cast<const uint32_t *>(P + o1 + 8 + 2 * c);
-                const uint32_t l0 = *reinterpret_cast<const uint32_t *>(Pl + o0 + 2 * c);
-                const uint32_t l1 = *reinterpret_cast<const uint32_t *>(Pl + o1 + 2 * c);
-                const uint32_t l2 = *reinterpret_cast<const uint32_t *>(Pl + o0 + 8 + 2 * c);
-                const uint32_t l3 = *reinterpret_cast<const uint32_t *>(Pl + o1 + 8 + 2 * c);
+                const int mt = warp + 4 * i;
+                if (mt < gm) {
+                    const uint2 w0 = *reinterpret_cast<const uint2 *>(st + (mt * 16 + g) * 32 + c * 8);
+                    const uint2 w1 = *reinterpret_cast<const uint2 *>(st + (mt * 16 + g + 8) * 32 + c * 8);
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    mma_f16(acc[i][j], a0, a1, a2, a3, bh[2 * j], bh[2 * j + 1]);
-                    mma_f16(acc[i][j], l0, l1, l2, l3, bh[2 * j], bh[2 * j + 1]);
-                    mma_f16(acc[i][j], a0, a1, a2, a3, bw[2 * j], bw[2 * j + 1]);
+                    for (int s4 = 0; s4 < 4; ++s4) {
+                        const uint32_t x0 = s4 < 2 ? w0.x : w0.y, x1 = s4 < 2 ? w1.x : w1.y;
+                        const int k = (s4 & 1) * 2;
+                        const uint2 e0 = lut_byte(lutl, x0, k), e2 = lut_byte(lutl, x0, k + 1);
+                        const uint2 e1 = lut_byte(lutl, x1, k), e3 = lut_byte(lutl, x1, k + 1);
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) {
+                            mma_f16(acc[i][j], e0.x, e1.x, e2.x, e3.x, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+                            mma_f16(acc[i][j], e0.y, e1.y, e2.y, e3.y, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+                            mma_f16(acc[i][j], e0.x, e1.x, e2.x, e3.x, bl[j][2 * s4], bl[j][2 * s4 + 1]);
+                        }
+                    }
+                }
+            }
+        }
+        cp_wait<0>();
+        __syncthreads();  // norms staged; the ring is free for the next group
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+            const int mt = warp + 4 * i;
+            if (mt < gm) {
+#pragma unroll
+                for (int hrow = 0; hrow < 2; ++hrow) {
+                    const int t = (mg + mt) * 16 + g + hrow * 8;
+                    const float f = t < nloc ? kn_s[t] * a.scale : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int h = j * 8 + c * 2 + e;
+                            if (h < HP) Ss[h * SROW + t] = acc[i][j][hrow * 2 + e] * f;
+                        }
                 }
             }
         }
     }
-    // write u~ as f16 hi/lo [m][h][kvd]
-    __half *U = a.U + (int64_t)m * a.nh * a.kvd, *Ul = a.U_lo + (int64_t)m * a.nh * a.kvd;
+    __syncthreads();
+
+    // ---- B. local softmax, one warp per head
+    for (int h = warp; h < HP; h += 4) {
+        __half *ph = Ph + h * PROW, *pl = Pl + h * PROW;
+        const float *srow = Ss + h * SROW;
+        const bool live = h < a.nh && nloc > 0;
+        float mx = -INFINITY, sum = 0.0f;
+        if (live) {
+            for (int t = lane; t < nloc; t += 32) mx = fmaxf(mx, srow[t]);
 #pragma unroll
-    for (int i = 0; i < MT; ++i)
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        for (int t = lane; t < nmt * 16; t += 32) {
+            float v = 0.0f;
+            if (live && t < nloc) {
+                const float e = expf(srow[t] - mx);
+                sum += e;
+                v = e * vn_s[t];
+            }
+            const __half hv = __float2half_rn(v);
+            ph[t] = hv;
+            pl[t] = __float2half_rn(v - __half2float(hv));
+        }
 #pragma unroll
-        for (int hrow = 0; hrow < 2; ++hrow) {
-            const int h = i * 16 + g + hrow * 8;
-            if (h >= a.nh) continue;
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            mloc[h] = mx;
+            lloc[h] = sum;
+        }
+    }
+    __syncthreads();  // scores phase done with the table
+    build_lut_rep(lut, a.vcent);
+
+    // ---- C. values and the cluster combine, one dim group at a time
+    const uint8_t *vcodes = a.vcodes + rowbase * a.vpl;
+    const int vchunks = DG / 32;  // 16-byte chunks per row of a tile (DG / 2 bytes)
+    for (int dg = 0; dg < a.ndg; ++dg) {
+        const uint8_t *vsrc = vcodes + dg * (DG / 2);
+        auto vstage = [&](int ks) {
+            unsigned char *st = ring + (ks % VSTG) * a.vstage;
+            for (int i = tid; i < 16 * vchunks; i += 128) {
+                const int r = i / vchunks, ch = i % vchunks;
+                const int t = min(c0 + ks * 16 + r, tn - 1);
+                cp_async16(smem_u32(st + r * a.vrow + ch * 16), vsrc + (int64_t)t * a.vpl + ch * 16, true);
+            }
+        };
+        __syncthreads();  // ring free (scores stages or the previous group's tiles)
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int d = d0 + warp * 16 + j * 8 + c * 2;
-                uint32_t hi, lo;
-                split_h2(acc[i][j][hrow * 2], acc[i][j][hrow * 2 + 1], hi, lo);
-                *reinterpret_cast<uint32_t *>(U + (int64_t)h * a.kvd + d) = hi;
-                *reinterpret_cast<uint32_t *>(Ul + (int64_t)h * a.kvd + d) = lo;
+        for (int s = 0; s < VSTG - 1; ++s) {
+            if (s < nmt) vstage(s);
+            cp_commit();
+        }
+        float acc[NBW][MTV][8][4];
+#pragma unroll
+        for (int b = 0; b < NBW; ++b)
+#pragma unroll
+            for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[b][i][j][e] = 0.0f;
+        for (int ks = 0; ks < nmt; ++ks) {
+            cp_wait<VSTG - 2>();
+            __syncthreads();
+            if (ks + VSTG - 1 < nmt) vstage(ks + VSTG - 1);
+            cp_commit();
+            const unsigned char *st = ring + (ks % VSTG) * a.vstage;
+            uint32_t ah[MTV][4], al[MTV][4];
+#pragma unroll
+            for (int i = 0; i < MTV; ++i) {
+                const int r = i * 16 + (lane & 15), col = ks * 16 + ((lane >> 4) << 3);
+                ldsm_x4(smem_u32(Ph + r * PROW + col), ah[i][0], ah[i][1], ah[i][2], ah[i][3]);
+                ldsm_x4(smem_u32(Pl + r * PROW + col), al[i][0], al[i][1], al[i][2], al[i][3]);
+            }
+#pragma unroll
+            for (int b = 0; b < NBW; ++b) {
+                if (warp + 4 * b >= nbg) continue;
+                const unsigned char *cb = st + (warp + 4 * b) * 32 + 4 * g;
+                const uint32_t x0 = *reinterpret_cast<const uint32_t *>(cb + (2 * c) * a.vrow);
+                const uint32_t x1 = *reinterpret_cast<const uint32_t *>(cb + (2 * c + 1) * a.vrow);
+                const uint32_t x2 = *reinterpret_cast<const uint32_t *>(cb + (2 * c + 8) * a.vrow);
+                const uint32_t x3 = *reinterpret_cast<const uint32_t *>(cb + (2 * c + 9) * a.vrow);
+#pragma unroll
+                uint32_t bh[8][2], bl[8][2];  // B registers of n-tile jj = 2by + hf (dim 8g + jj)
+#pragma unroll
+                for (int by = 0; by < 4; ++by) {
+                    const uint2 e0 = lut_byte(lutl, x0, by), e1 = lut_byte(lutl, x1, by);
+                    const uint2 e2 = lut_byte(lutl, x2, by), e3 = lut_byte(lutl, x3, by);
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const uint32_t sel = hf ? 0x7632u : 0x5410u;
+                        bh[2 * by + hf][0] = prmt(e0.x, e1.x, sel);
+                        bh[2 * by + hf][1] = prmt(e2.x, e3.x, sel);
+                        bl[2 * by + hf][0] = prmt(e0.y, e1.y, sel);
+                        bl[2 * by + hf][1] = prmt(e2.y, e3.y, sel);
+                    }
+                }
+                // term-major: consecutive MMAs go to different accumulators
+#pragma unroll
+                for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+                        mma_f16(acc[b][i][jj], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bh[jj][0], bh[jj][1]);
+#pragma unroll
+                for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+                        mma_f16(acc[b][i][jj], al[i][0], al[i][1], al[i][2], al[i][3], bh[jj][0], bh[jj][1]);
+#pragma unroll
+                for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+                        mma_f16(acc[b][i][jj], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bl[jj][0], bl[jj][1]);
             }
         }
+        cp_wait<0>();
+        __syncthreads();  // the partial tile may overlay the table and the ring
+        // accumulator (row h, col n = 2c + e) of n-tile jj is dim 8n + jj of block warp + 4b
+#pragma unroll
+        for (int b = 0; b < NBW; ++b)
+            if (warp + 4 * b < nbg)
+#pragma unroll
+            for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                for (int hrow = 0; hrow < 2; ++hrow)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            part[(i * 16 + g + hrow * 8) * UROW + (warp + 4 * b) * 64 + 8 * (2 * c + e) + jj] =
+                                acc[b][i][jj][hrow * 2 + e];
+        cluster.sync();
+        if (tid < HP) {
+            const int h = tid;
+            float M = -INFINITY;
+            for (int r = 0; r < NCH; ++r) M = fmaxf(M, *cluster.map_shared_rank(mloc + h, r));
+            float L = 0.0f;
+            for (int r = 0; r < NCH; ++r) {
+                const float mr = *cluster.map_shared_rank(mloc + h, r);
+                const float w = mr == -INFINITY ? 0.0f : expf(mr - M);
+                wgt[r * HP + h] = w;
+                L += w * *cluster.map_shared_rank(lloc + h, r);
+            }
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            for (int r = 0; r < NCH; ++r) wgt[r * HP + h] *= inv;
+        }
+        __syncthreads();
+        const int quads = a.nh * (DG / 4);
+        const int per = (quads + NCH - 1) / NCH;
+        const int q0 = rank * per, q1 = min(quads, q0 + per);
+        for (int qd = q0 + tid; qd < q1; qd += 128) {
+            const int h = qd / (DG / 4), d = (qd % (DG / 4)) * 4;
+            float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < NCH; ++r) {
+                const float w = wgt[r * HP + h];
+                if (w == 0.0f) continue;  // chunk without positions
+                const float4 v = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(part, r) + h * UROW + d);
+                u.x += w * v.x; u.y += w * v.y; u.z += w * v.z; u.w += w * v.w;
+            }
+            uint32_t h01, l01, h23, l23;
+            split_h2(u.x, u.y, h01, l01);
+            split_h2(u.z, u.w, h23, l23);
+            const int64_t o = ((int64_t)m * a.nh + h) * a.kvd + dg * DG + d;
+            *reinterpret_cast<uint2 *>(a.U + o) = make_uint2(h01, h23);
+            *reinterpret_cast<uint2 *>(a.U_lo + o) = make_uint2(l01, l23);
+        }
+        cluster.sync();  // peers are done reading this CTA's partial tile
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -470,36 +625,85 @@ __global__ void __launch_bounds__(128) fa_kernel(const FlashArgs a) {
 
 }  // namespace
 
-cudaError_t scores(const ScoreArgs &a, cudaStream_t s) {
-    dim3 grid((a.Tmax + 63) / 64, a.M);
+namespace {
+constexpr int ATTEND_CHUNKS = 8;  // CTAs per token (one thread-block cluster)
+int align16(int x) { return (x + 15) / 16 * 16; }
+}  // namespace
+
+template <int NT, int NBW>
+cudaError_t launch_decode_attn(DecodeAttnArgs a, cudaStream_t s) {
+    constexpr int MT = NT <= 2 ? 4 : 2, MTV = (NT * 8 + 15) / 16, HP = 16 * MTV;
+    const int NCH = ATTEND_CHUNKS;
+    const int DG = 64 * a.nbg;
+    a.chmax = ((a.B + NCH - 1) / NCH + 15) / 16 * 16;
+    a.sstage = 4 * MT * 16 * 32 + 2 * NT * 8 * 72 * 2;
+    a.vrow = DG / 2 + (16 - (DG / 2) % 128 + 128) % 128;  // row stride = 16 mod 128 bytes: conflict-free reads
+    a.vstage = 16 * a.vrow;
+    const int ring = std::max(SSTG * a.sstage, VSTG * a.vstage);
+    const int part = HP * (DG + 4) * 4;
+    a.off_ring = LUT_ENTRIES * (int)sizeof(uint2);
+    a.off_S = align16(a.off_ring + ring);
+    a.off_P = align16(a.off_S + HP * (a.chmax + 4) * 4);
+    a.off_small = align16(a.off_P + 2 * HP * (a.chmax + 8) * 2);
+    int end = align16(a.off_small + (2 * HP + NCH * HP + 2 * a.chmax) * 4);
+    if (a.ndg == 1 && part <= a.off_S) {
+        a.off_part = 0;  // the partial tile overlays the table and the ring once they are dead
+    } else {
+        a.off_part = end;
+        end = align16(end + part);
+    }
+    const int smem = end;
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    static int attr = 0;
+    if (smem > attr) {
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<NT, MT, MTV, NBW>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = smem;
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(NCH, 1, a.M);
+    lc.blockDim = dim3(128);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = NCH;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, decode_attn_kernel<NT, MT, MTV, NBW>, a);
+}
+
+template <int NT>
+cudaError_t decode_attn_nbw(DecodeAttnArgs &a, cudaStream_t s) {
+    switch ((a.nbg + 3) / 4) {
+        case 1: return launch_decode_attn<NT, 1>(a, s);
+        case 2: return launch_decode_attn<NT, 2>(a, s);
+        case 3: return launch_decode_attn<NT, 3>(a, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t decode_attn(const DecodeAttnArgs &a0, cudaStream_t s) {
+    DecodeAttnArgs a = a0;
+    if (a.M <= 0) return cudaSuccess;
+    if (a.kvd % 64 || a.nh < 1 || a.nh > 32) return cudaErrorInvalidValue;
+    // 64-dim blocks per dim group: the largest divisor of kv_dim / 64 up to 12
+    // (up to 8 with two head tiles, whose accumulators take twice the registers)
+    const int nblk = a.kvd / 64;
     const int nt = (a.nh + 7) / 8;
-    if (a.kvd % 64) return cudaErrorInvalidValue;
-    switch (nt) {
-        case 1: scores_kernel<1><<<grid, 128, 0, s>>>(a); break;
-        case 2: scores_kernel<2><<<grid, 128, 0, s>>>(a); break;
-        case 3: scores_kernel<3><<<grid, 128, 0, s>>>(a); break;
-        case 4: scores_kernel<4><<<grid, 128, 0, s>>>(a); break;
-        default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
-}
-
-cudaError_t softmax(const SoftmaxArgs &a, cudaStream_t s) {
-    softmax_kernel<<<dim3(a.nh, a.M), 256, 0, s>>>(a);
-    if (a.nhp > a.nh) zero_rows_kernel<<<dim3(a.nhp - a.nh, a.M), 128, 0, s>>>(a.P, a.P_lo, a.nh, a.nhp, a.Tpad);
-    return cudaGetLastError();
-}
-
-cudaError_t values(const ValueArgs &a, cudaStream_t s) {
-    if (a.kvd % 64) return cudaErrorInvalidValue;
-    dim3 grid(a.kvd / 64, a.M);
-    const int mt = a.nhp / 16;
-    switch (mt) {
-        case 1: values_kernel<1><<<grid, 128, 0, s>>>(a); break;
-        case 2: values_kernel<2><<<grid, 128, 0, s>>>(a); break;
-        default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
+    a.nbg = 1;
+    for (int d = nt > 2 ? 8 : 12; d >= 1; --d)
+        if (nblk % d == 0) {
+            a.nbg = d;
+            break;
+        }
+    a.ndg = nblk / a.nbg;
+    if (nt == 1) return decode_attn_nbw<1>(a, s);
+    if (nt == 2) return decode_attn_nbw<2>(a, s);
+    return decode_attn_nbw<4>(a, s);
 }
 
 cudaError_t centroids(const uint8_t *codes, int pl, const int32_t *slot, const int32_t *pos, int L, int B, int layer,

@@ -11,30 +11,20 @@ namespace attn {
 
 // Arena layout: codes [slot][layer][pos][pl], norms [slot][layer][pos].
 // Operands marked hi/lo are f16 splits of f32 values (x = hi + lo).
-struct ScoreArgs {
-    const uint8_t *kcodes;
-    const float *knorm;
-    const float *kcent;               // 16 key centroids (4-bit)
+// Decode attention of M single-token queries over the cached codes:
+// U[m, h] = u~ = sum_t softmax_t(s)[t] * norm_v[t] * centroid(code_v[t]) with
+// s[t] = norm_k[t] * scale * <centroid(code_k[t]), q~_h>, f16 hi/lo out.
+struct DecodeAttnArgs {
+    const uint8_t *kcodes, *vcodes;   // [slot][layer][pos][pl]
+    const float *knorm, *vnorm;       // [slot][layer][pos]
+    const float *kcent, *vcent;       // 16 centroids each
     const __half *qrot, *qrot_lo;     // [M][nh][kvd]
     const int32_t *slot, *pos;        // per token
-    float *S;                         // [M][nh][Tpad]
-    int M, nh, kvd, kpl, L, B, layer, Tpad, Tmax;
+    __half *U, *U_lo;                 // [M][nh][kvd]
+    int M, nh, kvd, kpl, vpl, L, B, layer;
     float scale;
-};
-struct SoftmaxArgs {
-    const float *S;
-    const float *vnorm;
-    const int32_t *slot, *pos;
-    __half *P, *P_lo;  // [M][nhp][Tpad]
-    int M, nh, nhp, L, B, layer, Tpad;
-};
-struct ValueArgs {
-    const uint8_t *vcodes;
-    const float *vcent;
-    const __half *P, *P_lo;  // [M][nhp][Tpad]
-    const int32_t *slot, *pos;
-    __half *U, *U_lo;        // [M][nh][kvd]
-    int M, nh, nhp, kvd, vpl, L, B, layer, Tpad;
+    // set by the launcher
+    int nbg, ndg, chmax, sstage, vrow, vstage, off_ring, off_S, off_P, off_small, off_part;
 };
 struct FlashArgs {
     const __half *Q, *Q_lo, *K, *K_lo, *V, *V_lo;  // rows = tokens (sequence-major, T per sequence)
@@ -44,9 +34,7 @@ struct FlashArgs {
     float scale;
 };
 
-cudaError_t scores(const ScoreArgs &a, cudaStream_t s);
-cudaError_t softmax(const SoftmaxArgs &a, cudaStream_t s);
-cudaError_t values(const ValueArgs &a, cudaStream_t s);
+cudaError_t decode_attn(const DecodeAttnArgs &a, cudaStream_t s);
 cudaError_t centroids(const uint8_t *codes, int pl, const int32_t *slot, const int32_t *pos, int L, int B, int layer,
                       const float *cent, int kvd, int M, __half *out, __half *out_lo, cudaStream_t s);
 cudaError_t gather_norms(const float *norms, const int32_t *slot, const int32_t *pos, int L, int B, int layer, int M,

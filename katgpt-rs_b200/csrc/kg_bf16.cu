@@ -9,13 +9,17 @@
 // XOR-swizzled shared memory and feed mma.sync m16n8k16 via ldmatrix.
 #include <algorithm>
 
+#include <cooperative_groups.h>
+
 #include "kg_bf16.cuh"
 
 namespace kg {
 namespace bf {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 4, THREADS = 256;
+namespace cg = cooperative_groups;
+
+constexpr int BK = 32, STAGES = 4;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -37,7 +41,7 @@ template <typename T>
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
 template <>
 __device__ __forceinline__ void mma16816<bf16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -45,7 +49,7 @@ __device__ __forceinline__ void mma16816<bf16>(float (&d)[4], const uint32_t (&a
 }
 template <>
 __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -68,45 +72,93 @@ __device__ __forceinline__ float from_t<__half>(__half v) { return __half2float(
 // swizzled so the 8 rows an ldmatrix reads fall in distinct banks.
 __device__ __forceinline__ int swz(int row, int c) { return row * 4 + (c ^ ((row >> 1) & 3)); }
 
-template <typename T, bool SA, bool SB>
-__global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
+// one output element through the epilogue; returns 1 when a ReLU output is alive
+template <typename T>
+__device__ __forceinline__ int epi_store(const Gemm &g, int z, int row, int cc, float v, float rs) {
+    switch (g.epi) {
+        case EPI_F32: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v; return 0;
+        case EPI_F32_RESID:
+            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
+            return 0;
+        case EPI_F32_ROWSCALE: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v * rs; return 0;
+        default: {
+            int alive = 0;
+            if (g.epi == EPI_RELU) {
+                alive = v > 0.0f ? 1 : 0;
+                v = v > 0.0f ? v : 0.0f;
+            } else if (g.epi == EPI_OUT_ROWSCALE) {
+                v = v * rs;
+            }
+            const int64_t ob = z * g.sCb + (int64_t)row * g.ldcb + cc;
+            const T hi = to_t<T>(v);
+            static_cast<T *>(g.Cb)[ob] = hi;
+            if (g.Cb2) static_cast<T *>(g.Cb2)[ob] = to_t<T>(v - from_t<T>(hi));
+            return alive;
+        }
+    }
+}
+
+// Tile shapes: 128 x 128 with 2 x 4 warps (warp tile 64 x 32) for prefill
+// shapes, 64 x 64 with 2 x 2 warps (warp tile 32 x 32) for decode shapes
+// (few rows: more tiles in flight over the weight stream).
+template <int BM_, int BN_, int WM_, int WN_>
+struct Tile {
+    static constexpr int BM = BM_, BN = BN_, WM = WM_, WN = WN_, THREADS = 32 * WM_ * WN_;
+    static constexpr int MI = BM_ / WM_ / 16, NJ = BN_ / WN_ / 8;
+};
+using TileL = Tile<128, 128, 2, 4>;
+using TileS = Tile<64, 64, 2, 2>;
+
+template <typename CF, bool SA, bool SB>
+constexpr int gemm_smem() {
+    return std::max(STAGES * (CF::BM * (SA ? 2 : 1) + CF::BN * (SB ? 2 : 1)) * BK * 2, CF::BM * (CF::BN + 4) * 4);
+}
+
+template <typename CF, typename T, bool SA, bool SB>
+__global__ void __launch_bounds__(CF::THREADS) gemm_kernel(const Gemm g) {
+    constexpr int BM_ = CF::BM, BN_ = CF::BN, NT_ = CF::THREADS, MI = CF::MI, NJ = CF::NJ;
     extern __shared__ uint4 sm[];
-    constexpr int TA = BM * 4, TB = BN * 4;  // 16-byte chunks per tile
+    constexpr int TA = BM_ * 4, TB = BN_ * 4;  // 16-byte chunks per tile
     constexpr int PER_STAGE = TA * (SA ? 2 : 1) + TB * (SB ? 2 : 1);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps, warp tile 64 x 32
-    const int bm = blockIdx.y * BM, bn = blockIdx.x * BN, z = blockIdx.z;
+    const int wm = warp / CF::WN, wn = warp % CF::WN;
+    const int bm = blockIdx.y * BM_, bn = blockIdx.x * BN_;
+    const int ks = blockIdx.z % g.ksplit, z = blockIdx.z / g.ksplit;
     const T *A = static_cast<const T *>(g.A) + z * g.sA;
     const T *A2 = SA ? static_cast<const T *>(g.A2) + z * g.sA : nullptr;
     const T *B = static_cast<const T *>(g.B) + z * g.sB;
     const T *B2 = SB ? static_cast<const T *>(g.B2) + z * g.sB : nullptr;
-    const int KT = g.K / BK;
+    const int KT_all = g.K / BK;
+    const int kt_per = (KT_all + g.ksplit - 1) / g.ksplit;
+    const int kt0 = ks * kt_per;
+    const int KT = max(0, min(KT_all, kt0 + kt_per) - kt0);
 
     auto tileA = [&](int st, int part) { return sm + st * PER_STAGE + part * TA; };
     auto tileB = [&](int st, int part) { return sm + st * PER_STAGE + TA * (SA ? 2 : 1) + part * TB; };
 
     auto load = [&](int stage, int kt) {
-        const int k0 = kt * BK;
+        const int k0 = (kt0 + kt) * BK;
 #pragma unroll
-        for (int it = 0; it < 2; ++it) {
-            int idx = tid + it * THREADS;  // 0..511
-            int row = idx >> 2, c = idx & 3;
-            int gr = bm + row;
+        for (int idx = tid; idx < TA; idx += NT_) {
+            const int row = idx >> 2, c = idx & 3, gr = bm + row;
             const int64_t ao = (int64_t)min(gr, g.M - 1) * g.lda + k0 + c * 8;
             cp_async16(smem_u32(tileA(stage, 0) + swz(row, c)), A + ao, gr < g.M);
             if (SA) cp_async16(smem_u32(tileA(stage, 1) + swz(row, c)), A2 + ao, gr < g.M);
-            int gn = bn + row;
+        }
+#pragma unroll
+        for (int idx = tid; idx < TB; idx += NT_) {
+            const int row = idx >> 2, c = idx & 3, gn = bn + row;
             const int64_t bo = (int64_t)min(gn, g.N - 1) * g.ldb + k0 + c * 8;
             cp_async16(smem_u32(tileB(stage, 0) + swz(row, c)), B + bo, gn < g.N);
             if (SB) cp_async16(smem_u32(tileB(stage, 1) + swz(row, c)), B2 + bo, gn < g.N);
         }
     };
 
-    float acc[4][4][4];
+    float acc[MI][NJ][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < MI; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < NJ; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
 
@@ -123,79 +175,118 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(const Gemm g) {
         const int st = kt % STAGES;
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {  // two k16 steps per BK = 32
-            uint32_t bfr[2][4][2];
+            uint32_t bfr[2][NJ][2];
 #pragma unroll
             for (int part = 0; part < (SB ? 2 : 1); ++part)
 #pragma unroll
-                for (int j2 = 0; j2 < 2; ++j2) {
-                    int row = wn * 32 + j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
-                    int c = kk * 2 + ((lane >> 3) & 1);
-                    uint32_t r0, r1, r2, r3;
-                    ldsm_x4(smem_u32(tileB(st, part) + swz(row, c)), r0, r1, r2, r3);
-                    bfr[part][j2 * 2][0] = r0;
-                    bfr[part][j2 * 2][1] = r1;
-                    bfr[part][j2 * 2 + 1][0] = r2;
-                    bfr[part][j2 * 2 + 1][1] = r3;
+                for (int j2 = 0; j2 < NJ / 2; ++j2) {
+                    const int row = wn * (BN_ / CF::WN) + j2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+                    const int c = kk * 2 + ((lane >> 3) & 1);
+                    ldsm_x4(smem_u32(tileB(st, part) + swz(row, c)), bfr[part][j2 * 2][0], bfr[part][j2 * 2][1],
+                            bfr[part][j2 * 2 + 1][0], bfr[part][j2 * 2 + 1][1]);
                 }
+            uint32_t af[2][MI][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                uint32_t af[4], af2[4];
-                {
-                    int row = wm * 64 + i * 16 + (lane & 15);
-                    int c = kk * 2 + (lane >> 4);
-                    ldsm_x4(smem_u32(tileA(st, 0) + swz(row, c)), af[0], af[1], af[2], af[3]);
-                    if (SA) ldsm_x4(smem_u32(tileA(st, 1) + swz(row, c)), af2[0], af2[1], af2[2], af2[3]);
-                }
+            for (int part = 0; part < (SA ? 2 : 1); ++part)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    mma16816<T>(acc[i][j], af, bfr[0][j][0], bfr[0][j][1]);
-                    if (SA) mma16816<T>(acc[i][j], af2, bfr[0][j][0], bfr[0][j][1]);
-                    if (SB) mma16816<T>(acc[i][j], af, bfr[1][j][0], bfr[1][j][1]);
+                for (int i = 0; i < MI; ++i) {
+                    const int row = wm * (BM_ / CF::WM) + i * 16 + (lane & 15);
+                    const int c = kk * 2 + (lane >> 4);
+                    ldsm_x4(smem_u32(tileA(st, part) + swz(row, c)), af[part][i][0], af[part][i][1], af[part][i][2],
+                            af[part][i][3]);
                 }
+            // term-major order: consecutive MMAs go to different accumulators
+#pragma unroll
+            for (int i = 0; i < MI; ++i)
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) mma16816<T>(acc[i][j], af[0][i], bfr[0][j][0], bfr[0][j][1]);
+            if (SA) {
+#pragma unroll
+                for (int i = 0; i < MI; ++i)
+#pragma unroll
+                    for (int j = 0; j < NJ; ++j) mma16816<T>(acc[i][j], af[SA ? 1 : 0][i], bfr[0][j][0], bfr[0][j][1]);
+            }
+            if (SB) {
+#pragma unroll
+                for (int i = 0; i < MI; ++i)
+#pragma unroll
+                    for (int j = 0; j < NJ; ++j) mma16816<T>(acc[i][j], af[0][i], bfr[SB ? 1 : 0][j][0], bfr[SB ? 1 : 0][j][1]);
             }
         }
     }
     cp_wait<0>();
+    const int g8 = lane >> 2, c4 = lane & 3;
+
+    if (g.ksplit > 1) {
+        // Split-K: the ksplit CTAs of one output tile form a thread-block
+        // cluster. Each parks its partial tile in its own shared memory, then
+        // each reduces a 1/ksplit slice of the tile over all peers' shared
+        // memory (in split order, so results are deterministic) and runs the
+        // epilogue on it.
+        cg::cluster_group cluster = cg::this_cluster();
+        constexpr int LDR = BN_ + 4;
+        float *red = reinterpret_cast<float *>(sm);
+        __syncthreads();  // every warp is done with the pipeline buffers
+#pragma unroll
+        for (int i = 0; i < MI; ++i)
+#pragma unroll
+            for (int hrow = 0; hrow < 2; ++hrow)
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) {
+                    const int r = wm * (BM_ / CF::WM) + i * 16 + g8 + hrow * 8;
+                    const int cl = wn * (BN_ / CF::WN) + j * 8 + c4 * 2;
+                    *reinterpret_cast<float2 *>(red + r * LDR + cl) =
+                        make_float2(acc[i][j][hrow * 2], acc[i][j][hrow * 2 + 1]);
+                }
+        cluster.sync();
+        const int rank = (int)cluster.block_rank();
+        const int mrows = min(BM_, g.M - bm);
+        const int quads = mrows * (BN_ / 4);  // float4 groups of the valid rows
+        const int per = (quads + g.ksplit - 1) / g.ksplit;
+        const int q0 = rank * per, q1 = min(quads, q0 + per);
+        for (int qd = q0 + tid; qd < q1; qd += NT_) {
+            const int r = qd / (BN_ / 4), cl = (qd % (BN_ / 4)) * 4;
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < g.ksplit; ++p) {
+                const float4 v = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(red, p) + r * LDR + cl);
+                sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+            }
+            const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+            const int row = bm + r;
+            float rs = 1.0f;
+            if (g.epi == EPI_F32_ROWSCALE || g.epi == EPI_OUT_ROWSCALE) rs = g.row_scale[z * g.sRs + row];
+            int alive = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (bn + cl + e < g.N) alive += epi_store<T>(g, z, row, bn + cl + e, vals[e], rs);
+            if (g.epi == EPI_RELU) {
+                // one atomic per row and warp: lanes of the same row pool their counts
+                const unsigned grp = __match_any_sync(__activemask(), row);
+                alive = __reduce_add_sync(grp, alive);
+                if (alive && lane == __ffs(grp) - 1) atomicAdd(&g.row_alive[row], alive);
+            }
+        }
+        cluster.sync();  // peers may still be reading this CTA's shared memory
+        return;
+    }
 
     // ---- epilogue
-    T *Cb = static_cast<T *>(g.Cb), *Cb2 = static_cast<T *>(g.Cb2);
-    const int g8 = lane >> 2, c4 = lane & 3;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < MI; ++i) {
 #pragma unroll
         for (int hrow = 0; hrow < 2; ++hrow) {
-            const int row = bm + wm * 64 + i * 16 + g8 + hrow * 8;
+            const int row = bm + wm * (BM_ / CF::WM) + i * 16 + g8 + hrow * 8;
             const bool rok = row < g.M;
             int alive = 0;
             float rs = 1.0f;
             if (rok && (g.epi == EPI_F32_ROWSCALE || g.epi == EPI_OUT_ROWSCALE)) rs = g.row_scale[z * g.sRs + row];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int col = bn + wn * 32 + j * 8 + c4 * 2;
+            for (int j = 0; j < NJ; ++j) {
+                const int col = bn + wn * (BN_ / CF::WN) + j * 8 + c4 * 2;
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int cc = col + e;
-                    if (!rok || cc >= g.N) continue;
-                    float v = acc[i][j][hrow * 2 + e];
-                    const int64_t ob = z * g.sCb + (int64_t)row * g.ldcb + cc;
-                    switch (g.epi) {
-                        case EPI_F32: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v; break;
-                        case EPI_F32_RESID:
-                            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
-                            break;
-                        case EPI_F32_ROWSCALE: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v * rs; break;
-                        default: {
-                            if (g.epi == EPI_RELU) {
-                                alive += v > 0.0f ? 1 : 0;
-                                v = v > 0.0f ? v : 0.0f;
-                            } else if (g.epi == EPI_OUT_ROWSCALE) {
-                                v = v * rs;
-                            }
-                            const T hi = to_t<T>(v);
-                            Cb[ob] = hi;
-                            if (Cb2) Cb2[ob] = to_t<T>(v - from_t<T>(hi));
-                        }
-                    }
+                    if (rok && cc < g.N) alive += epi_store<T>(g, z, row, cc, acc[i][j][hrow * 2 + e], rs);
                 }
             }
             if (g.epi == EPI_RELU) {
@@ -384,18 +475,47 @@ __global__ void softmax_kernel(const float *logits, float *probs, int V, float i
 
 }  // namespace
 
-template <typename T, bool SA, bool SB>
-cudaError_t launch_gemm(const Gemm &g, cudaStream_t s) {
-    const int smem = STAGES * (BM * (SA ? 2 : 1) + BN * (SB ? 2 : 1)) * BK * 2;
+template <typename CF, typename T, bool SA, bool SB>
+cudaError_t launch_gemm(Gemm g, cudaStream_t s) {
+    constexpr int smem = gemm_smem<CF, SA, SB>();
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<T, SA, SB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<CF, T, SA, SB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
-    gemm_kernel<T, SA, SB><<<grid, THREADS, smem, s>>>(g);
-    return cudaGetLastError();
+    const int64_t tiles = (int64_t)((g.N + CF::BN - 1) / CF::BN) * ((g.M + CF::BM - 1) / CF::BM) * g.batch;
+    if (g.ksplit == 0) {
+        // split K when the output has too few tiles to fill the GPU: at least
+        // 3 K tiles per split, at most 8 CTAs per cluster, stop at two waves
+        const int kt = g.K / BK;
+        g.ksplit = 1;
+        while (tiles * g.ksplit < 2 * 148 && g.ksplit * 2 * 3 <= kt && g.ksplit * 2 <= 8) g.ksplit *= 2;
+    }
+    if (g.ksplit > 8 || (g.ksplit & (g.ksplit - 1)) || (g.K / BK) < g.ksplit) return cudaErrorInvalidValue;
+    dim3 grid((g.N + CF::BN - 1) / CF::BN, (g.M + CF::BM - 1) / CF::BM, g.batch * g.ksplit);
+    if (g.ksplit == 1) {
+        gemm_kernel<CF, T, SA, SB><<<grid, CF::THREADS, smem, s>>>(g);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = dim3(CF::THREADS);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = g.ksplit;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, gemm_kernel<CF, T, SA, SB>, g);
+}
+
+template <typename T, bool SA, bool SB>
+cudaError_t launch_gemm_shape(const Gemm &g, cudaStream_t s) {
+    return g.M <= 64 ? launch_gemm<TileS, T, SA, SB>(g, s) : launch_gemm<TileL, T, SA, SB>(g, s);
 }
 
 cudaError_t gemm(const Gemm &g, cudaStream_t s) {
@@ -404,12 +524,12 @@ cudaError_t gemm(const Gemm &g, cudaStream_t s) {
     const bool sa = g.A2 != nullptr, sb = g.B2 != nullptr;
     if (g.dtype == DT_BF16) {
         if (sb) return cudaErrorInvalidValue;  // bf16 B operands are exact weights
-        return sa ? launch_gemm<bf16, true, false>(g, s) : launch_gemm<bf16, false, false>(g, s);
+        return sa ? launch_gemm_shape<bf16, true, false>(g, s) : launch_gemm_shape<bf16, false, false>(g, s);
     }
-    if (sa && sb) return launch_gemm<__half, true, true>(g, s);
-    if (sa) return launch_gemm<__half, true, false>(g, s);
-    if (sb) return launch_gemm<__half, false, true>(g, s);
-    return launch_gemm<__half, false, false>(g, s);
+    if (sa && sb) return launch_gemm_shape<__half, true, true>(g, s);
+    if (sa) return launch_gemm_shape<__half, true, false>(g, s);
+    if (sb) return launch_gemm_shape<__half, false, true>(g, s);
+    return launch_gemm_shape<__half, false, false>(g, s);
 }
 
 cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M, float *x,

@@ -44,6 +44,10 @@ struct Gemm {
     int *row_alive;
     const float *row_scale;
     int64_t sRs;
+    // split-K (1, 2, 4 or 8; 0 = chosen from the shape): the K range is cut
+    // into ksplit parts computed by the CTAs of one thread-block cluster and
+    // reduced through distributed shared memory in part order (deterministic)
+    int ksplit;
 };
 
 cudaError_t gemm(const Gemm &g, cudaStream_t s);

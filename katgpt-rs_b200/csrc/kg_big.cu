@@ -103,7 +103,6 @@ cudaError_t big_init(kg_ctx *ctx) {
     const int64_t n = ctx->n, kvd = ctx->kvd, m = ctx->m, V = ctx->V, L = ctx->L, B = ctx->B, S = c.max_seqs;
     g.ws_tokens = std::max<int64_t>(S, 8192);
     g.Tpad = (B + 31) / 32 * 32;
-    g.nhp = (ctx->nh + 15) / 16 * 16;
     auto &own = ctx->allocs;
     // weights (bf16), one block in the flat reference order
     g.nbf = V * n + B * n + L * (2 * n * n + 2 * kvd * n + 2 * m * n) + V * n;
@@ -160,9 +159,6 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.qrot2, S * ctx->nh * kvd, own));
     BIG_TRY(dalloc(&g.U, S * ctx->nh * kvd, own));
     BIG_TRY(dalloc(&g.U2, S * ctx->nh * kvd, own));
-    BIG_TRY(dalloc(&g.Sbuf, S * ctx->nh * g.Tpad, own));
-    BIG_TRY(dalloc(&g.P, S * g.nhp * g.Tpad, own));
-    BIG_TRY(dalloc(&g.P2, S * g.nhp * g.Tpad, own));
     // centroid tables
     BIG_TRY(dalloc(&g.kcent, 16, own));
     BIG_TRY(dalloc(&g.vcent, 16, own));
@@ -266,7 +262,15 @@ bf::Gemm gemm0() {
     bf::Gemm q;
     std::memset(&q, 0, sizeof(q));
     q.batch = 1;
+    q.ksplit = 1;
     return q;
+}
+
+// Launch a GEMM, splitting K when the output has too few tiles to fill the GPU
+// (the decode step's M is the number of sequences).
+cudaError_t gemm_split(bf::Gemm q, cudaStream_t s) {
+    q.ksplit = 0;
+    return bf::gemm(q, s);
 }
 
 // One pass over all layers for M tokens (rows of the workspace). Every GEMM
@@ -301,7 +305,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = wqkv; q.ldb = n; q.M = M; q.N = nqkv; q.K = n;
         q.epi = bf::EPI_F32; q.C = g.qkv; q.ldc = nqkv;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(bf::gemm(q, s));
+        BIG_TRY(gemm_split(q, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // TurboQuant encode of K and V into the arena (exact reference order)
         prof_mark(ctx, KG_PROF_ENCODE, 0, s);
@@ -332,7 +336,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
                 d.M = M; d.N = kvd; d.K = kvd;
                 d.epi = bf::EPI_OUT_ROWSCALE; d.Cb = kv ? g.vt : g.kt; d.Cb2 = kv ? g.vt2 : g.kt2; d.ldcb = kvd;
                 d.row_scale = g.nrm;
-                BIG_TRY(bf::gemm(d, s));
+                BIG_TRY(gemm_split(d, s));
             }
             attn::FlashArgs fa;
             fa.Q = g.qh; fa.Q_lo = g.ql; fa.K = g.kt; fa.K_lo = g.kt2; fa.V = g.vt; fa.V_lo = g.vt2; fa.O = g.attf;
@@ -347,23 +351,15 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             r.B = g.rot_h; r.B2 = g.rot_l; r.ldb = kvd; r.sB = hd;
             r.M = M; r.N = kvd; r.K = hd; r.batch = nh;
             r.epi = bf::EPI_OUT; r.Cb = g.qrot; r.Cb2 = g.qrot2; r.ldcb = (int64_t)nh * kvd; r.sCb = kvd;
-            BIG_TRY(bf::gemm(r, s));
-            attn::ScoreArgs sa;
-            sa.kcodes = g.kcodes; sa.knorm = g.knorm; sa.kcent = g.kcent; sa.qrot = g.qrot; sa.qrot_lo = g.qrot2;
-            sa.slot = g.slot_of; sa.pos = g.pos_of; sa.S = g.Sbuf;
-            sa.M = M; sa.nh = nh; sa.kvd = kvd; sa.kpl = (int)ctx->kpl; sa.L = L; sa.B = B; sa.layer = l;
-            sa.Tpad = (int)g.Tpad; sa.Tmax = B; sa.scale = scale;
+            BIG_TRY(gemm_split(r, s));
+            attn::DecodeAttnArgs da;
+            da.kcodes = g.kcodes; da.vcodes = g.vcodes; da.knorm = g.knorm; da.vnorm = g.vnorm;
+            da.kcent = g.kcent; da.vcent = g.vcent; da.qrot = g.qrot; da.qrot_lo = g.qrot2;
+            da.slot = g.slot_of; da.pos = g.pos_of; da.U = g.U; da.U_lo = g.U2;
+            da.M = M; da.nh = nh; da.kvd = kvd; da.kpl = (int)ctx->kpl; da.vpl = (int)ctx->vpl;
+            da.L = L; da.B = B; da.layer = l; da.scale = scale;
             prof_mark(ctx, KG_PROF_ATTN, 0, s);
-            BIG_TRY(attn::scores(sa, s));
-            attn::SoftmaxArgs sm;
-            sm.S = g.Sbuf; sm.vnorm = g.vnorm; sm.slot = g.slot_of; sm.pos = g.pos_of; sm.P = g.P; sm.P_lo = g.P2;
-            sm.M = M; sm.nh = nh; sm.nhp = (int)g.nhp; sm.L = L; sm.B = B; sm.layer = l; sm.Tpad = (int)g.Tpad;
-            BIG_TRY(attn::softmax(sm, s));
-            attn::ValueArgs va;
-            va.vcodes = g.vcodes; va.vcent = g.vcent; va.P = g.P; va.P_lo = g.P2; va.slot = g.slot_of;
-            va.pos = g.pos_of; va.U = g.U; va.U_lo = g.U2; va.M = M; va.nh = nh; va.nhp = (int)g.nhp; va.kvd = kvd;
-            va.vpl = (int)ctx->vpl; va.L = L; va.B = B; va.layer = l; va.Tpad = (int)g.Tpad;
-            BIG_TRY(attn::values(va, s));
+            BIG_TRY(attn::decode_attn(da, s));
             prof_mark(ctx, KG_PROF_ATTN, 1, s);
             // out_h = R[:, head cols]^T u~_h
             bf::Gemm o = gemm0();
@@ -372,7 +368,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             o.B = g.rot_th; o.B2 = g.rot_tl; o.ldb = kvd; o.sB = (int64_t)hd * kvd;
             o.M = M; o.N = hd; o.K = kvd; o.batch = nh;
             o.epi = bf::EPI_F32; o.C = g.attf; o.ldc = n; o.sC = hd;
-            BIG_TRY(bf::gemm(o, s));
+            BIG_TRY(gemm_split(o, s));
         }
         BIG_TRY(bf::to_bf16(g.attf, n, n, M, g.attb, g.attb2, n, s));
         // output projection + residual: x = Wo att + xr
@@ -380,7 +376,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
         w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(bf::gemm(w, s));
+        BIG_TRY(gemm_split(w, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // MLP
         BIG_TRY(cudaMemcpyAsync(g.xr2, g.x, (size_t)M * n * 4, cudaMemcpyDeviceToDevice, s));
@@ -390,13 +386,13 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
         u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(bf::gemm(u, s));
+        BIG_TRY(gemm_split(u, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         bf::Gemm dn = gemm0();
         dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
         dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(bf::gemm(dn, s));
+        BIG_TRY(gemm_split(dn, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
                                     c.sparse_threshold, s));
@@ -415,7 +411,7 @@ cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, cudaStream_
     q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = g.lm; q.ldb = n; q.M = M; q.N = V; q.K = n;
     q.epi = bf::EPI_F32; q.C = lo; q.ldc = V;
     prof_mark(ctx, KG_PROF_GEMM, 0, s);
-    BIG_TRY(bf::gemm(q, s));
+    BIG_TRY(gemm_split(q, s));
     prof_mark(ctx, KG_PROF_GEMM, 1, s);
     if (probs) BIG_TRY(bf::softmax_rows(lo, probs, V, M, 1.0f / ctx->cfg.temperature, s));
     return cudaSuccess;

@@ -75,15 +75,14 @@ struct BigState {
     float *kcent = nullptr, *vcent = nullptr;          // 16 centroids each
     uint8_t *kcodes = nullptr, *vcodes = nullptr;      // [slot][layer][pos][pl]
     float *knorm = nullptr, *vnorm = nullptr;          // [slot][layer][pos]
-    int64_t ws_tokens = 0, Tpad = 0, nhp = 0, nbf = 0;
+    int64_t ws_tokens = 0, Tpad = 0, nbf = 0;
     // workspace (hi/lo pairs are 16-bit splits of f32 values)
     float *x = nullptr, *xr = nullptr, *xr2 = nullptr, *delta = nullptr, *qkv = nullptr, *nrm = nullptr,
           *attf = nullptr;
     __nv_bfloat16 *xb = nullptr, *xb2 = nullptr, *attb = nullptr, *attb2 = nullptr, *hid = nullptr, *hid2 = nullptr;
     __half *qh = nullptr, *ql = nullptr, *cent = nullptr, *cent2 = nullptr, *kt = nullptr, *kt2 = nullptr,
-           *vt = nullptr, *vt2 = nullptr, *qrot = nullptr, *qrot2 = nullptr, *U = nullptr, *U2 = nullptr,
-           *P = nullptr, *P2 = nullptr;
-    float *Sbuf = nullptr, *xn = nullptr;  // xn: normalised K/V rows for the tiled encoder
+           *vt = nullptr, *vt2 = nullptr, *qrot = nullptr, *qrot2 = nullptr, *U = nullptr, *U2 = nullptr;
+    float *xn = nullptr;  // normalised K/V rows for the tiled encoder
     uint8_t *skip = nullptr;
     int *alive = nullptr;
     int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;

@@ -46,11 +46,20 @@ __device__ float warp_sum_sq(const float *x, int len, int stride) {
     const int lane = threadIdx.x & 31;
     const int c2 = len / 16;
     float acc = 0.0f;
-    if (lane < 16)
-        for (int c = 0; c < c2; ++c) {
+    if (lane < 16) {
+        int c = 0;
+        for (; c + 8 <= c2; c += 8) {  // loads first, then the chain in order
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = x[(int64_t)(16 * (c + u) + lane) * stride];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = fmaf(v[u], v[u], acc);
+        }
+        for (; c < c2; ++c) {
             float v = x[(int64_t)(16 * c + lane) * stride];
             acc = fmaf(v, v, acc);
         }
+    }
     // t[l] = a0[l] + a1[l] = chain l + chain l+8, then hsum8
     float t = acc + __shfl_down_sync(0xffffffffu, acc, 8);
     float sum = tree8(t);
@@ -104,8 +113,17 @@ __global__ void mgs_step(int dim, int j, float *V, float *Q) {
     const int i = j + 1 + blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= dim) return;
     float d = -0.0f;  // Iterator::<f32>::sum starts from -0.0
-    for (int k = 0; k < dim; ++k) d = d + qj[k] * V[(int64_t)k * dim + i];
-    for (int k = 0; k < dim; ++k) V[(int64_t)k * dim + i] = V[(int64_t)k * dim + i] - d * qj[k];
+    int k = 0;
+    for (; k + 16 <= dim; k += 16) {  // loads first, then the sequential sum in order
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = V[(int64_t)(k + u) * dim + i];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) d = d + qj[k + u] * v[u];
+    }
+    for (; k < dim; ++k) d = d + qj[k] * V[(int64_t)k * dim + i];
+#pragma unroll 8
+    for (int kk = 0; kk < dim; ++kk) V[(int64_t)kk * dim + i] = V[(int64_t)kk * dim + i] - d * qj[kk];
 }
 
 __global__ void transpose_sq(int dim, const float *a, float *t) {
@@ -222,7 +240,9 @@ __global__ void __launch_bounds__(256) rotate_kernel(int dim, int bits, int64_t 
     float *Rs = reinterpret_cast<float *>(esm);   // [2][ER][EK]
     float *Xs = Rs + 2 * ER * EK;                 // [2][EV][EK]
     __shared__ uint8_t codes[EV][ER];
+    __shared__ float s_bnd[256];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int b = tid; b < (1 << bits) - 1; b += blockDim.x) s_bnd[b] = bnd[b];
     const int wr = warp >> 1, wv = warp & 1;  // 4 x 2 warps: 16 rows x 8 vectors each
     const int r0 = blockIdx.x * ER;
     const int64_t v0 = (int64_t)blockIdx.y * EV;
@@ -271,21 +291,39 @@ __global__ void __launch_bounds__(256) rotate_kernel(int dim, int bits, int64_t 
         }
         __syncthreads();  // buffer reused by the stage after next
     }
-    // fixed-order reductions; the remaining-8-chunk and tail terms are empty (dim % 32 == 0),
-    // so sum = tree32 + hsum(0) = tree32 + 0
+    // Fixed-order reduction of all 128 outputs at once: a transposed butterfly
+    // over the lane masks 8, 16, 4, 1, 2 — the pairing order of the reference
+    // tree ((acc0+acc1)+(acc2+acc3), then horizontal_sum_256) — halves the
+    // values per lane at each step, so every output gets exactly that tree and
+    // each lane ends with 4 finished outputs. The remaining-8-chunk and tail
+    // terms are empty (dim % 32 == 0): sum = tree + hsum(0) = tree + 0.
+    float *v = &acc[0][0];  // flat view: output o = i * 8 + q lives in v[o]
+    int obase = 0;
+#define KG_BFLY(MASK, HALF)                                                        \
+    {                                                                              \
+        const bool hi = (lane & (MASK)) != 0;                                      \
+        _Pragma("unroll") for (int k = 0; k < (HALF); ++k) {                       \
+            const float send = hi ? v[k] : v[k + (HALF)];                          \
+            const float keep = hi ? v[k + (HALF)] : v[k];                          \
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, (MASK));              \
+        }                                                                          \
+        if (hi) obase += (HALF);                                                   \
+    }
+    KG_BFLY(8, 64)
+    KG_BFLY(16, 32)
+    KG_BFLY(4, 16)
+    KG_BFLY(1, 8)
+    KG_BFLY(2, 4)
+#undef KG_BFLY
     const int nb = (1 << bits) - 1;
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-            float r = tree32(acc[i][v]);
-            r = r + 0.0f;
-            if (lane == 0) {
-                int c = 0;
-                for (int b = 0; b < nb; ++b) c += (r >= bnd[b]) ? 1 : 0;
-                codes[wv * 8 + v][wr * 16 + i] = (uint8_t)c;
-            }
-        }
+    for (int k = 0; k < 4; ++k) {
+        const float r = v[k] + 0.0f;
+        int c = 0;
+        for (int b = 0; b < nb; ++b) c += (r >= s_bnd[b]) ? 1 : 0;
+        const int o = obase + k;  // o = i * 8 + q
+        codes[wv * 8 + (o & 7)][wr * 16 + (o >> 3)] = (uint8_t)c;
+    }
     __syncthreads();
     // pack 64 codes per vector: 32 bytes (3/4-bit) at byte offset r0/2
     for (int e = tid; e < EV * (ER / 2); e += 256) {
