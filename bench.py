@@ -223,11 +223,20 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
 
     # prefill (untimed setup of the decode benchmark; its device time is reported)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    be.profile_read()
+    be.profile(True)
     e0.record(stream)
     be.forward_batch_dev(n, C3_PREFILL, P(d_ids), P(d_pre), None, None, None, sp)
     e1.record(stream)
     torch.cuda.synchronize()
+    be.profile(False)
+    pf_ms, _ = be.profile_read()
     prefill_ms = e0.elapsed_time(e1)
+    # tensor FLOPs of the prefill weight GEMMs (QKV, Wo, W1, W2; activations as
+    # bf16 hi + lo: two products per multiply-add)
+    d, m = C3["n_embd"], C3["mlp_hidden"]
+    pf_flops = 2.0 * 2 * n * C3_PREFILL * C3["n_layer"] * (3 * d * d + d * d + 2 * d * m)
+    pf_gemm_tf = pf_flops / (float(pf_ms[2]) * 1e-3) / 1e12 if pf_ms[2] > 0 else None
 
     def step(s):
         be.forward_batch_dev(n, 1, P(d_ids), P(d_dec[s]), P(d_pos[s]), P(d_log), None, sp)
@@ -309,7 +318,12 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
         "phases_ms_per_step": {"kv_attention": float(ph_ms[0]) / args.steps, "tq_encode": float(ph_ms[1]) / args.steps,
                                "weight_gemms": float(ph_ms[2]) / args.steps},
         "weight_gemm_gbs": gemm_gbs,
-        "prefill": {"tokens": n * C3_PREFILL, "ms": prefill_ms, "tokens_per_s": n * C3_PREFILL / (prefill_ms / 1000.0)},
+        "prefill": {"tokens": n * C3_PREFILL, "ms": prefill_ms, "tokens_per_s": n * C3_PREFILL / (prefill_ms / 1000.0),
+                    "weight_gemm_ms": float(pf_ms[2]),
+                    "weight_gemm_tensor": {"achieved": pf_gemm_tf, "unit": "TFLOP/s",
+                                           "peak": peaks.get("bf16_tflops", 1590.0),
+                                           "frac": (pf_gemm_tf / peaks.get("bf16_tflops", 1590.0)) if pf_gemm_tf else None,
+                                           "kernel": "tcgen05 GEMM (QKV, Wo, W1, W2), bf16 hi+lo activations x bf16 weights"}},
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(n * 4 * 3), "d2h_bytes_per_step": int(n * V * 4)},
         "clocks": clk.summary(),
     }

@@ -513,6 +513,7 @@ int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const i
     int herr = 0;
     KG_CUDA(ctx, cudaMemcpyAsync(&herr, ctx->d_err, 4, cudaMemcpyDeviceToHost, s));
     KG_CUDA(ctx, cudaStreamSynchronize(s));
+    if (herr == KG_ERR_TIMEOUT) return fail(ctx, KG_ERR_TIMEOUT, "a device-side wait exceeded its limit");
     if (herr) return fail(ctx, KG_ERR_INVALID_ARG, "device rejected a token, position or slot");
     return KG_OK;
 }

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "kg_attn.cuh"
+#include "kg_umma.cuh"
 #include "kg_bf16.cuh"
 #include "kg_internal.h"
 
@@ -268,7 +269,10 @@ bf::Gemm gemm0() {
 
 // Launch a GEMM, splitting K when the output has too few tiles to fill the GPU
 // (the decode step's M is the number of sequences).
-cudaError_t gemm_split(bf::Gemm q, cudaStream_t s) {
+// Launch a GEMM: tcgen05 for prefill-sized M, otherwise the mma.sync kernel
+// (with K split across a cluster when the output has few tiles, as in decode).
+cudaError_t gemm_split(kg_ctx *ctx, bf::Gemm q, cudaStream_t s) {
+    if (q.M >= 256 && umma::supported(q)) return umma::gemm(q, s, ctx->d_err);
     q.ksplit = 0;
     return bf::gemm(q, s);
 }
@@ -305,7 +309,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = wqkv; q.ldb = n; q.M = M; q.N = nqkv; q.K = n;
         q.epi = bf::EPI_F32; q.C = g.qkv; q.ldc = nqkv;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(gemm_split(q, s));
+        BIG_TRY(gemm_split(ctx, q, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // TurboQuant encode of K and V into the arena (exact reference order)
         prof_mark(ctx, KG_PROF_ENCODE, 0, s);
@@ -336,7 +340,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
                 d.M = M; d.N = kvd; d.K = kvd;
                 d.epi = bf::EPI_OUT_ROWSCALE; d.Cb = kv ? g.vt : g.kt; d.Cb2 = kv ? g.vt2 : g.kt2; d.ldcb = kvd;
                 d.row_scale = g.nrm;
-                BIG_TRY(gemm_split(d, s));
+                BIG_TRY(gemm_split(ctx, d, s));
             }
             attn::FlashArgs fa;
             fa.Q = g.qh; fa.Q_lo = g.ql; fa.K = g.kt; fa.K_lo = g.kt2; fa.V = g.vt; fa.V_lo = g.vt2; fa.O = g.attf;
@@ -351,7 +355,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             r.B = g.rot_h; r.B2 = g.rot_l; r.ldb = kvd; r.sB = hd;
             r.M = M; r.N = kvd; r.K = hd; r.batch = nh;
             r.epi = bf::EPI_OUT; r.Cb = g.qrot; r.Cb2 = g.qrot2; r.ldcb = (int64_t)nh * kvd; r.sCb = kvd;
-            BIG_TRY(gemm_split(r, s));
+            BIG_TRY(gemm_split(ctx, r, s));
             attn::DecodeAttnArgs da;
             da.kcodes = g.kcodes; da.vcodes = g.vcodes; da.knorm = g.knorm; da.vnorm = g.vnorm;
             da.kcent = g.kcent; da.vcent = g.vcent; da.qrot = g.qrot; da.qrot_lo = g.qrot2;
@@ -368,7 +372,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             o.B = g.rot_th; o.B2 = g.rot_tl; o.ldb = kvd; o.sB = (int64_t)hd * kvd;
             o.M = M; o.N = hd; o.K = kvd; o.batch = nh;
             o.epi = bf::EPI_F32; o.C = g.attf; o.ldc = n; o.sC = hd;
-            BIG_TRY(gemm_split(o, s));
+            BIG_TRY(gemm_split(ctx, o, s));
         }
         BIG_TRY(bf::to_bf16(g.attf, n, n, M, g.attb, g.attb2, n, s));
         // output projection + residual: x = Wo att + xr
@@ -376,7 +380,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
         w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(gemm_split(w, s));
+        BIG_TRY(gemm_split(ctx, w, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // MLP
         BIG_TRY(cudaMemcpyAsync(g.xr2, g.x, (size_t)M * n * 4, cudaMemcpyDeviceToDevice, s));
@@ -386,13 +390,13 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
         u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(gemm_split(u, s));
+        BIG_TRY(gemm_split(ctx, u, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         bf::Gemm dn = gemm0();
         dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
         dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
-        BIG_TRY(gemm_split(dn, s));
+        BIG_TRY(gemm_split(ctx, dn, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
                                     c.sparse_threshold, s));
@@ -411,7 +415,7 @@ cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, cudaStream_
     q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = g.lm; q.ldb = n; q.M = M; q.N = V; q.K = n;
     q.epi = bf::EPI_F32; q.C = lo; q.ldc = V;
     prof_mark(ctx, KG_PROF_GEMM, 0, s);
-    BIG_TRY(gemm_split(q, s));
+    BIG_TRY(gemm_split(ctx, q, s));
     prof_mark(ctx, KG_PROF_GEMM, 1, s);
     if (probs) BIG_TRY(bf::softmax_rows(lo, probs, V, M, 1.0f / ctx->cfg.temperature, s));
     return cudaSuccess;

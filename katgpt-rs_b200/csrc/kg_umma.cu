@@ -1,0 +1,410 @@
+// kg_umma.cu — tcgen05 (5th-generation tensor core) GEMM for prefill shapes.
+//
+// C[M x N] = A[M x K] * B[N x K]^T with the split-operand products of
+// kg_bf16.cuh (A = hi + lo activations, B = exact bf16 weights, or f16 hi + lo
+// on both sides) and the same fused epilogues, for M in the thousands.
+//
+// Persistent, warp-specialised CTA (192 threads, one per SM):
+//   warp 0      TMA producer: 128B-swizzled A / A_lo / B / B_lo tiles of
+//               64 K-elements into a 3-stage shared-memory ring
+//               (cp.async.bulk.tensor, completion counted on mbarriers)
+//   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, M = 128,
+//               N = BN, K = 16, accumulating in tensor memory; tcgen05.commit
+//               releases a ring stage once the MMAs reading it are done and
+//               signals a finished accumulator
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32 (w % 4) ..), fused epilogue, stores to global
+// Two accumulator buffers of BN TMEM columns let the epilogue of one output
+// tile overlap the main loop of the next. Every mbarrier wait is bounded by a
+// clock limit; on expiry the kernel records KG_ERR_TIMEOUT in the error word,
+// stops issuing work and still releases its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/kg_abi.h"
+#include "kg_bf16.cuh"
+#include "kg_umma.cuh"
+
+namespace kg {
+namespace umma {
+namespace {
+
+constexpr int BM = 128, BK = 64, STG = 3, THREADS = 192;
+constexpr int STAGE_BYTES = 64 * 1024;
+constexpr long long WAIT_CYCLES = 4ll << 30;  // about 2 s at 2 GHz
+
+__device__ __forceinline__ uint32_t sa(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(sa(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(sa(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(sa(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(sa(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase of `parity` to complete. Returns false (and raises the
+// abort flag and the error word) when the clock limit passes or another
+// thread of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+    if (mbar_try(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(b, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > WAIT_CYCLES) {
+            *abort_flag = 1;
+            if (err) atomicExch(err, (int)KG_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(sa(dst)),
+        "l"(tm), "r"(x), "r"(y), "r"(sa(bar))
+        : "memory");
+}
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle (8-row x 128 B
+// atoms, 1024 B between atoms along M/N), descriptor version 1
+__device__ __forceinline__ uint64_t sdesc(const void *p) {
+    return (uint64_t)((sa(p) >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// instruction descriptor, kind::f16: f32 accumulator, A and B of `fmt`
+// (0 = f16, 1 = bf16), both K-major, shape 128 x BN
+__host__ __device__ constexpr uint32_t idesc(int fmt, int bn) {
+    return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)(bn >> 3) << 17) |
+           ((uint32_t)(BM >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(sa(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ T to_t(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_t<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half to_t<__half>(float v) { return __float2half_rn(v); }
+template <typename T>
+__device__ __forceinline__ float from_t(T v);
+template <>
+__device__ __forceinline__ float from_t<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float from_t<__half>(__half v) { return __half2float(v); }
+
+struct Maps {
+    CUtensorMap a, a2, b, b2;
+};
+
+template <typename T, bool SA, bool SB, int BN>
+__global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Maps maps, const bf::Gemm g,
+                                                              int *err) {
+    extern __shared__ uint8_t dsm_raw[];
+    // 1024-byte alignment for the 128B-swizzled tiles
+    uint8_t *dsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+    constexpr uint32_t TX = A_BYTES * (SA ? 2 : 1) + B_BYTES * (SB ? 2 : 1);
+    static_assert(TX <= STAGE_BYTES, "stage too large");
+    uint64_t *full = reinterpret_cast<uint64_t *>(dsm + STG * STAGE_BYTES);
+    uint64_t *empty = full + STG;
+    uint64_t *tfull = empty + STG;   // [2] accumulator ready
+    uint64_t *tempty = tfull + 2;    // [2] accumulator drained
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = (g.M + BM - 1) / BM, nt = (g.N + BN - 1) / BN, tiles = mt * nt;
+    const int kb_n = g.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STG; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {  // 2 x BN accumulator columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(sa(tslot)),
+                     "r"(2 * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            int it = 0;
+            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+                const int m0 = (t / nt) * BM, n0 = (t % nt) * BN;
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = it % STG;
+                    if (!mbar_wait(&empty[s], ((it / STG) & 1) ^ 1, abort_flag, err)) break;
+                    uint8_t *st = dsm + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], TX);
+                    tma_load_2d(st, &maps.a, kb * BK, m0, &full[s]);
+                    if (SA) tma_load_2d(st + A_BYTES, &maps.a2, kb * BK, m0, &full[s]);
+                    uint8_t *sb = st + A_BYTES * (SA ? 2 : 1);
+                    tma_load_2d(sb, &maps.b, kb * BK, n0, &full[s]);
+                    if (SB) tma_load_2d(sb + B_BYTES, &maps.b2, kb * BK, n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t ID = idesc(std::is_same<T, __half>::value ? 0 : 1, BN);
+            int it = 0, tl = 0;
+            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++tl) {
+                const int buf = tl & 1;
+                if (!mbar_wait(&tempty[buf], ((tl >> 1) & 1) ^ 1, abort_flag, err)) break;
+                tc_fence_after();
+                const uint32_t d = tbase + buf * BN;
+                bool ok = true;
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = it % STG;
+                    if (!mbar_wait(&full[s], (it / STG) & 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t *st = dsm + s * STAGE_BYTES;
+                    const uint64_t da = sdesc(st), db = sdesc(st + A_BYTES * (SA ? 2 : 1));
+                    const uint64_t da2 = sdesc(st + A_BYTES), db2 = sdesc(st + A_BYTES * (SA ? 2 : 1) + B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint64_t ko = (uint64_t)(k * 32 >> 4);  // 32 bytes per K step, in 16-byte units
+                        umma(d, da + ko, db + ko, ID, (kb | k) != 0);
+                        if (SA) umma(d, da2 + ko, db + ko, ID, 1);
+                        if (SB) umma(d, da + ko, db2 + ko, ID, 1);
+                    }
+                    umma_commit(&empty[s]);  // the stage is free once these MMAs are done
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);
+            }
+        }
+    } else {
+        // epilogue: warp w owns TMEM lanes 32 * (w % 4) .. +31 = tile rows
+        const int q = warp & 3;
+        int tl = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tl) {
+            const int buf = tl & 1;
+            if (!mbar_wait(&tfull[buf], (tl >> 1) & 1, abort_flag, err)) break;
+            tc_fence_after();
+            const int m0 = (t / nt) * BM, n0 = (t % nt) * BN;
+            const int row = m0 + q * 32 + lane;
+            const bool rok = row < g.M;
+            float rs = 1.0f;
+            if (rok && (g.epi == bf::EPI_F32_ROWSCALE || g.epi == bf::EPI_OUT_ROWSCALE)) rs = g.row_scale[row];
+            int alive = 0;
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(tbase + buf * BN + c0 + ((uint32_t)(q * 32) << 16), v);
+                const int col = n0 + c0;
+                if (!rok || col >= g.N) continue;
+                const bool full_row = col + 32 <= g.N;
+                switch (g.epi) {
+                    case bf::EPI_F32:
+                    case bf::EPI_F32_ROWSCALE:
+                    case bf::EPI_F32_RESID: {
+                        float *dst = g.C + (int64_t)row * g.ldc + col;
+                        const float *r = g.epi == bf::EPI_F32_RESID ? g.R + (int64_t)row * g.ldr + col : nullptr;
+                        if (full_row) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                float4 o = make_float4(v[i] * rs, v[i + 1] * rs, v[i + 2] * rs, v[i + 3] * rs);
+                                if (r) {
+                                    const float4 rr = *reinterpret_cast<const float4 *>(r + i);
+                                    o.x += rr.x; o.y += rr.y; o.z += rr.z; o.w += rr.w;
+                                }
+                                *reinterpret_cast<float4 *>(dst + i) = o;
+                            }
+                        } else {
+                            for (int i = 0; i < 32 && col + i < g.N; ++i) dst[i] = v[i] * rs + (r ? r[i] : 0.0f);
+                        }
+                        break;
+                    }
+                    default: {  // 16-bit hi / lo outputs
+                        T *hi = static_cast<T *>(g.Cb) + (int64_t)row * g.ldcb + col;
+                        T *lo = g.Cb2 ? static_cast<T *>(g.Cb2) + (int64_t)row * g.ldcb + col : nullptr;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            float x = v[i];
+                            if (g.epi == bf::EPI_RELU) {
+                                alive += x > 0.0f ? 1 : 0;
+                                x = x > 0.0f ? x : 0.0f;
+                            } else if (g.epi == bf::EPI_OUT_ROWSCALE) {
+                                x *= rs;
+                            }
+                            v[i] = x;
+                        }
+                        if (full_row) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                T h[8], l[8];
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) {
+                                    h[e] = to_t<T>(v[i + e]);
+                                    l[e] = to_t<T>(v[i + e] - from_t<T>(h[e]));
+                                }
+                                *reinterpret_cast<uint4 *>(hi + i) = *reinterpret_cast<const uint4 *>(h);
+                                if (lo) *reinterpret_cast<uint4 *>(lo + i) = *reinterpret_cast<const uint4 *>(l);
+                            }
+                        } else {
+                            for (int i = 0; i < 32 && col + i < g.N; ++i) {
+                                const T h = to_t<T>(v[i]);
+                                hi[i] = h;
+                                if (lo) lo[i] = to_t<T>(v[i] - from_t<T>(h));
+                            }
+                        }
+                    }
+                }
+            }
+            if (g.epi == bf::EPI_RELU && rok && alive) atomicAdd(&g.row_alive[row], alive);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(2 * BN));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D map over a row-major [rows x cols] 16-bit matrix with leading dimension
+// ld (elements); box = 64 columns x box_rows rows, 128-byte swizzle
+bool make_map(CUtensorMap *m, const void *base, int64_t rows, int64_t cols, int64_t ld, int box_rows, bool f16) {
+    auto fn = encode_fn();
+    if (!fn || !base) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, bool SA, bool SB>
+cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
+    constexpr int BN = SB ? 128 : 256;
+    const bool f16 = std::is_same<T, __half>::value;
+    Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if (!make_map(&maps.a, g.A, g.M, g.K, g.lda, BM, f16) || (SA && !make_map(&maps.a2, g.A2, g.M, g.K, g.lda, BM, f16)) ||
+        !make_map(&maps.b, g.B, g.N, g.K, g.ldb, BN, f16) || (SB && !make_map(&maps.b2, g.B2, g.N, g.K, g.ldb, BN, f16)))
+        return cudaErrorInvalidValue;
+    const int smem = 1024 + STG * STAGE_BYTES + 256;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(umma_gemm_kernel<T, SA, SB, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+    umma_gemm_kernel<T, SA, SB, BN><<<std::min(tiles, nsm), THREADS, smem, s>>>(maps, g, err);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool supported(const bf::Gemm &g) {
+    // one batch, K in whole 64-element blocks, 16-byte aligned rows and bases,
+    // and the hi-only B form only for bf16 weights
+    if (g.batch != 1 || g.K % BK || g.lda % 8 || g.ldb % 8) return false;
+    if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return false;
+    if (g.A2 && (reinterpret_cast<uintptr_t>(g.A2) & 15)) return false;
+    if (g.B2 && (reinterpret_cast<uintptr_t>(g.B2) & 15)) return false;
+    if (g.epi == bf::EPI_F32 || g.epi == bf::EPI_F32_RESID || g.epi == bf::EPI_F32_ROWSCALE) {
+        if (g.ldc % 4 || (g.epi == bf::EPI_F32_RESID && g.ldr % 4)) return false;
+        if (reinterpret_cast<uintptr_t>(g.C) & 15) return false;
+    } else if (g.ldcb % 8 || (reinterpret_cast<uintptr_t>(g.Cb) & 15)) {
+        return false;
+    }
+    return encode_fn() != nullptr;
+}
+
+cudaError_t gemm(const bf::Gemm &g, cudaStream_t s, int *err) {
+    if (g.M <= 0 || g.N <= 0) return cudaSuccess;
+    const bool sa = g.A2 != nullptr, sb = g.B2 != nullptr;
+    if (g.dtype == bf::DT_BF16) {
+        if (sb) return cudaErrorInvalidValue;
+        return sa ? launch<__nv_bfloat16, true, false>(g, s, err) : launch<__nv_bfloat16, false, false>(g, s, err);
+    }
+    if (sa && sb) return launch<__half, true, true>(g, s, err);
+    if (sa) return launch<__half, true, false>(g, s, err);
+    if (sb) return launch<__half, false, true>(g, s, err);
+    return launch<__half, false, false>(g, s, err);
+}
+
+}  // namespace umma
+}  // namespace kg

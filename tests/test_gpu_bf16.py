@@ -100,17 +100,19 @@ def test_random_weights_and_codes_readback(kg):
 
 
 def test_c3_width_long_context(kg, orc):
-    # several score tiles and multi-step attention chunks per token: a
-    # 160-token prefill then decode steps up to position 199 at C3 widths
+    # two 160-token prompts (320 prefill rows: the tcgen05 GEMM path) then
+    # decode steps up to position 199 at C3 widths: several score tiles and
+    # multi-step attention chunks per token
     cfg, be, w = make(kg, 1, vocab_size=512, block_size=256, n_embd=768, n_head=12, head_dim=64,
-                      n_kv_head=12, mlp_hidden=3072, n_layer=1, max_seqs=1)
-    toks = tokens(1, 200, cfg.vocab_size, seed=21)
+                      n_kv_head=12, mlp_hidden=3072, n_layer=1, max_seqs=2)
+    toks = tokens(2, 200, cfg.vocab_size, seed=21)
     pre = be.forward_batch(toks[:, :160])
-    dec = np.stack([be.forward_batch(toks[:, t:t + 1], start_pos=np.full(1, t))[:, 0] for t in range(160, 200)],
+    dec = np.stack([be.forward_batch(toks[:, t:t + 1], start_pos=np.full(2, t))[:, 0] for t in range(160, 200)],
                    axis=1)
-    got = np.concatenate([pre, dec], axis=1)[0]
-    ref = orc.run_sequence(orc.from_kg(cfg), 1, w, toks[0], key_bits=4, val_bits=4)[0]
-    err = rel_err(got, ref)
-    print("max rel err prefill %.2e decode %.2e" % (err[:160].max(), err[160:].max()))
-    assert err.max() <= REL_BF16
+    got = np.concatenate([pre, dec], axis=1)
+    for i in range(2):
+        ref = orc.run_sequence(orc.from_kg(cfg), 1, w, toks[i], key_bits=4, val_bits=4)[0]
+        err = rel_err(got[i], ref)
+        print("seq %d max rel err prefill %.2e decode %.2e" % (i, err[:160].max(), err[160:].max()))
+        assert err.max() <= REL_BF16
     be.close()
