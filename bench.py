@@ -204,7 +204,8 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     be = kgcuda.CudaBackend(cfg, device=local)
     be.random_weights(seed=SEED, std=0.02)
     n, V = C3_SEQS, C3["vocab_size"]
-    total_dec = args.warmup + args.steps
+    n_prof = min(args.steps, 8)
+    total_dec = args.warmup + args.steps + n_prof
     e_steps = min(max(3, args.steps // 4), 64)
     assert C3_PREFILL + total_dec + e_steps + 2 <= C3["block_size"], "too many steps for block_size 2048"
     rng = np.random.default_rng(1000 + rank)
@@ -241,11 +242,11 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     def step(s):
         be.forward_batch_dev(n, 1, P(d_ids), P(d_dec[s]), P(d_pos[s]), P(d_log), None, sp)
 
+    # warm-up: the first step of a batch shape runs eagerly, the second
+    # captures the decode step as a CUDA graph, later steps replay it
     for s in range(args.warmup):
         step(s)
     torch.cuda.synchronize()
-    be.profile_read()          # clear
-    be.profile(True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -253,11 +254,18 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     with ClockSampler(local) as clk:
         step_ms = timed_steps(torch, stream, args.steps, lambda s: step(args.warmup + s), flush)
     torch.cuda.nvtx.range_pop()
-    be.profile(False)
-    ph_ms, ph_cnt = be.profile_read()
-    ph_ms = [float(x) for x in ph_ms]
+    graph_kernels = be.graph_kernels()
     if world > 1:
         dist.barrier()
+    # phase breakdown: the same steps again, eagerly with CUDA events around
+    # each phase (attention, encode, GEMMs) on the launching stream
+    p0 = args.warmup + args.steps
+    be.profile_read()          # clear
+    be.profile(True)
+    prof_ms = timed_steps(torch, stream, n_prof, lambda s: step(p0 + s), flush)
+    be.profile(False)
+    ph_ms, ph_cnt = be.profile_read()
+    ph_ms = [float(x) / n_prof for x in ph_ms]
     my_ms = float(np.sum(step_ms))
     t = torch.tensor([my_ms], device=dev)
     if world > 1:
@@ -292,11 +300,11 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
 
     kpl = kvpl = C3["n_embd"] // 2
     L = C3["n_layer"]
-    positions = [C3_PREFILL + args.warmup + s for s in range(args.steps)]
-    attn_bytes = sum(n * L * (p + 1) * (kpl + kvpl + 8) for p in positions)
+    positions = [C3_PREFILL + p0 + s for s in range(n_prof)]
+    attn_bytes = sum(n * L * (p + 1) * (kpl + kvpl + 8) for p in positions) / n_prof  # per step
     attn_gbs = attn_bytes / (ph_ms[0] / 1000.0) / 1e9 if ph_ms[0] > 0 else None
     nbf = sum([V * 768, 2048 * 768, L * (4 * 768 * 768 + 2 * 768 * 3072), V * 768])
-    gemm_bytes = args.steps * (nbf - 2048 * 768 - V * 768) * 2  # streamed weights (wte/wpe gathered, not streamed)
+    gemm_bytes = (nbf - 2048 * 768 - V * 768) * 2  # per step: streamed weights (wte/wpe gathered, not streamed)
     gemm_gbs = gemm_bytes / (ph_ms[2] / 1000.0) / 1e9 if ph_ms[2] > 0 else None
     peaks = load_peaks()
     peak = peaks.get("hbm_gbs", 6650.0)
@@ -309,14 +317,16 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
                                "1024-token prefill then teacher-forced decode",
                    "global_batch": world * n, "seq_len": C3_PREFILL, "parallelism": f"dp{world} (sequence shards)",
                    "l2": "flushed between steps (256 MiB write, outside the timed events)"},
-        "gpu_launches": None,
+        "gpu_launches": int(graph_kernels * args.steps),
+        "decode_step": "one CUDA graph per step" if graph_kernels else "eager",
+        "kernels_per_step": int(graph_kernels),
         "roofline": {"bound": "hbm", "kernel": "decode KV attention (scores + softmax + values over 4-bit codes)",
                      "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
                      "frac": (attn_gbs / peak) if attn_gbs else None, "traffic": None,
-                     "algorithmic_bytes_per_step": attn_bytes / args.steps,
+                     "algorithmic_bytes_per_step": attn_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
-        "phases_ms_per_step": {"kv_attention": float(ph_ms[0]) / args.steps, "tq_encode": float(ph_ms[1]) / args.steps,
-                               "weight_gemms": float(ph_ms[2]) / args.steps},
+        "phases_ms_per_step": {"kv_attention": ph_ms[0], "tq_encode": ph_ms[1], "weight_gemms": ph_ms[2],
+                               "note": f"eager steps {p0}..{p0 + n_prof - 1} with CUDA events per phase"},
         "weight_gemm_gbs": gemm_gbs,
         "prefill": {"tokens": n * C3_PREFILL, "ms": prefill_ms, "tokens_per_s": n * C3_PREFILL / (prefill_ms / 1000.0),
                     "weight_gemm_ms": float(pf_ms[2]),

@@ -207,6 +207,10 @@ int kg_profile(kg_ctx *ctx, int enable);
  * of every phase since the last read (ms[KG_PROF_N]) and the number of timed
  * intervals (count[KG_PROF_N]); resets the sums. */
 int kg_profile_read(kg_ctx *ctx, float *ms, int64_t *count);
+/* Kernel launches replayed by the last kg_forward_batch(_dev) call when it ran
+ * as a captured CUDA graph (single-position decode of the bf16 path on a
+ * non-legacy stream, profiling off); 0 when that call ran eagerly. */
+int64_t kg_graph_kernels(const kg_ctx *ctx);
 
 #ifdef __cplusplus
 }

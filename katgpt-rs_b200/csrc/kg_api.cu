@@ -149,6 +149,10 @@ void kg_ctx_destroy(kg_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (auto &gr : ctx->graphs) {
+        if (gr.stream) cudaStreamSynchronize(gr.stream);
+        if (gr.exec) cudaGraphExecDestroy(gr.exec);
+    }
     for (void *p : ctx->allocs) cudaFree(p);
     if (ctx->stage) cudaFree(ctx->stage);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -436,6 +440,61 @@ int kg_seq_reset_all(kg_ctx *ctx) {
     return KG_OK;
 }
 
+namespace {
+// Single-position decode through a captured CUDA graph: one launch per step
+// instead of one per kernel. The caller's arrays are copied into fixed device
+// buffers first, so any arrays of the same batch shape replay the same graph.
+int forward_graph(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                  const int32_t *start_pos, float *logits, float *probs, cudaStream_t s) {
+    const int S = ctx->cfg.max_seqs;
+    if (!ctx->g_ids) {
+        int rc;
+        if ((rc = dalloc(ctx, &ctx->g_ids, S)) || (rc = dalloc(ctx, &ctx->g_tok, S)) || (rc = dalloc(ctx, &ctx->g_pos, S)))
+            return rc;
+    }
+    KG_CUDA(ctx, cudaMemcpyAsync(ctx->g_ids, seq_ids, n_seq * 4, cudaMemcpyDeviceToDevice, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(ctx->g_tok, tokens, n_seq * 4, cudaMemcpyDeviceToDevice, s));
+    if (start_pos) KG_CUDA(ctx, cudaMemcpyAsync(ctx->g_pos, start_pos, n_seq * 4, cudaMemcpyDeviceToDevice, s));
+    const int32_t *pos = start_pos ? ctx->g_pos : nullptr;
+    kg_ctx::DecodeGraph *gr = nullptr;
+    for (auto &x : ctx->graphs)
+        if (x.n_seq == n_seq && x.has_pos == (start_pos != nullptr) && x.logits == logits && x.probs == probs &&
+            x.stream == s)
+            gr = &x;
+    if (!gr) {  // first use of this key: eager
+        ctx->graphs.push_back({n_seq, start_pos != nullptr, logits, probs, s, nullptr, 0, false});
+        KG_CUDA(ctx, kg::big_forward(ctx, n_seq, ctx->g_ids, ctx->g_tok, pos, 1, logits, probs, s));
+        return KG_OK;
+    }
+    if (!gr->captured) {
+        cudaGraph_t graph = nullptr;
+        KG_CUDA(ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = kg::big_forward(ctx, n_seq, ctx->g_ids, ctx->g_tok, pos, 1, logits, probs, s);
+        cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+        if (e == cudaSuccess) e = e2;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&gr->exec, graph, 0);
+        if (e == cudaSuccess) {
+            size_t n = 0;
+            cudaGraphGetNodes(graph, nullptr, &n);
+            std::vector<cudaGraphNode_t> nodes(n);
+            cudaGraphGetNodes(graph, nodes.data(), &n);
+            int64_t k = 0;
+            for (auto nd : nodes) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+            }
+            gr->kernels = k;
+            gr->captured = true;
+        }
+        if (graph) cudaGraphDestroy(graph);
+        KG_CUDA(ctx, e);
+    }
+    KG_CUDA(ctx, cudaGraphLaunch(gr->exec, s));
+    ctx->last_graph_kernels = gr->kernels;
+    return KG_OK;
+}
+}  // namespace
+
 int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
                          const int32_t *start_pos, int32_t T, float *logits, float *probs, void *stream) {
     if (!ctx) return KG_ERR_INVALID_ARG;
@@ -444,10 +503,13 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
     if (n_seq < 0 || T < 1 || T > ctx->B || (ctx->micro && T > 16) || !seq_ids || !tokens)
         return fail(ctx, KG_ERR_INVALID_ARG, "bad batch shape");
     if (n_seq == 0) return KG_OK;
+    ctx->last_graph_kernels = 0;
     if (ctx->big_path) {
         KG_CUDA(ctx, cudaSetDevice(ctx->device));
-        cudaError_t e = kg::big_forward(ctx, n_seq, seq_ids, tokens, start_pos, T, logits, probs,
-                                        static_cast<cudaStream_t>(stream));
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (T == 1 && s != nullptr && !ctx->prof && n_seq <= std::min<int64_t>(ctx->big.ws_tokens, ctx->cfg.max_seqs))
+            return forward_graph(ctx, n_seq, seq_ids, tokens, start_pos, logits, probs, s);
+        cudaError_t e = kg::big_forward(ctx, n_seq, seq_ids, tokens, start_pos, T, logits, probs, s);
         if (e == cudaErrorNotSupported)
             return fail(ctx, KG_ERR_UNSUPPORTED, "bf16 path: a multi-position call must start at position 0");
         KG_CUDA(ctx, e);
@@ -649,3 +711,5 @@ void prof_mark(kg_ctx *ctx, int phase, int end, cudaStream_t s) {
     if (end) ctx->prof_used[phase] = i + 1;
 }
 }  // namespace kg
+
+int64_t kg_graph_kernels(const kg_ctx *ctx) { return ctx ? ctx->last_graph_kernels : 0; }

@@ -118,6 +118,22 @@ struct kg_ctx {
     int *d_err = nullptr;
     // host copies of the TurboQuant tables
     std::vector<float> h_rot, h_kc, h_kb, h_vc, h_vb, h_pred;
+    // decode step graphs (bf16 path, T == 1): inputs are copied into the
+    // g_* buffers, the graph replays the whole forward; keyed by batch shape
+    // and output pointers. A key runs eagerly once before it is captured (the
+    // first run sets kernel attributes, which capture cannot).
+    struct DecodeGraph {
+        int n_seq;
+        bool has_pos;
+        float *logits, *probs;
+        cudaStream_t stream;
+        cudaGraphExec_t exec;
+        int64_t kernels;
+        bool captured;
+    };
+    std::vector<DecodeGraph> graphs;
+    int32_t *g_ids = nullptr, *g_tok = nullptr, *g_pos = nullptr;
+    int64_t last_graph_kernels = 0;
     // staging for host-pointer calls
     void *stage = nullptr;
     size_t stage_bytes = 0;

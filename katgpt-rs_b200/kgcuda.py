@@ -86,6 +86,7 @@ def lib():
             "kg_spkv_utility": (ctypes.c_int, [P, I32, I32, I32, P]),
             "kg_profile": (ctypes.c_int, [P, ctypes.c_int]),
             "kg_profile_read": (ctypes.c_int, [P, P, P]),
+            "kg_graph_kernels": (I64, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -252,6 +253,10 @@ class CudaBackend:
         cnt = np.zeros(3, np.int64)
         self._check(lib().kg_profile_read(self._h, _ptr(ms), _ptr(cnt)))
         return ms, cnt
+
+    def graph_kernels(self):
+        """Kernel launches replayed by the last forward call's CUDA graph (0: eager)."""
+        return int(lib().kg_graph_kernels(self._h))
 
     def spkv_utility(self, seq, layer, pos):
         u = np.empty(1, np.float32)

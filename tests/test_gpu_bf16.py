@@ -116,3 +116,25 @@ def test_c3_width_long_context(kg, orc):
         print("seq %d max rel err prefill %.2e decode %.2e" % (i, err[:160].max(), err[160:].max()))
         assert err.max() <= REL_BF16
     be.close()
+
+
+def test_decode_graph_replay_matches_eager(kg):
+    # the decode step replays as a CUDA graph from its third call on; with
+    # phase profiling on every step runs eagerly: both must agree bitwise
+    cfg, be, w = make(kg, 1)
+    cfg2, be2, _ = make(kg, 1)
+    be2.profile(True)
+    toks = tokens(3, 20, cfg.vocab_size, seed=8)
+    a = be.forward_batch(toks[:, :8])
+    b = be2.forward_batch(toks[:, :8])
+    np.testing.assert_array_equal(a, b)
+    kernels = []
+    for t in range(8, 20):
+        x = be.forward_batch(toks[:, t:t + 1], start_pos=np.full(3, t))
+        kernels.append(be.graph_kernels())
+        y = be2.forward_batch(toks[:, t:t + 1], start_pos=np.full(3, t))
+        np.testing.assert_array_equal(x, y)
+    assert kernels[0] == 0 and kernels[1] > 0 and all(k == kernels[1] for k in kernels[1:])
+    be2.profile(False)
+    be.close()
+    be2.close()
