@@ -23,6 +23,7 @@
 
 #include <algorithm>
 
+#include "kg_async.cuh"
 #include "kg_attn.cuh"
 
 namespace kg {
@@ -37,7 +38,7 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 }
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -443,6 +444,396 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a
 }
 
 // ---------------------------------------------------------------------------
+// Decode attention with a TMA producer warp (kv_dim a multiple of 256). Same
+// arithmetic and fragment layouts as decode_attn_kernel; the staging differs:
+//   warp 4 (one thread) streams every tile through a ring of NS shared-memory
+//   stages with cp.async.bulk.tensor: per 64-dim block of the scores phase
+//   the chunk's key-code rows ([rows x 32 B], plain) and the q~ hi / lo rows
+//   ([heads x 128 B], 128-byte swizzle); per 16-position step of the values
+//   phase the value-code rows of the dim group ([16 x 128 B] boxes, 128-byte
+//   swizzle, which makes the 4-byte reads of the value step conflict-free).
+//   The replicated centroid tables come precomputed from global memory by
+//   bulk copy (key table first, value table once the scores are done).
+//   Warps 0..3 consume: wait on the stage's full barrier, compute, release it
+//   through its empty barrier; no CTA-wide barrier inside the loops.
+// Waits are bounded (kg_async.cuh): on a timeout the CTA keeps passing through
+// every barrier it owes (named, cluster) with the work skipped, and the
+// device error word reports KG_ERR_TIMEOUT.
+constexpr int NS = 4;                  // ring stages
+// 8 replicas of the byte table (16 KB): lane l reads replica l & 7, at most
+// two lanes of a warp share a bank pair (four wavefronts per lookup)
+constexpr int LUT8_ENTRIES = 256 * 8;
+__device__ __forceinline__ uint2 lut8_byte(const uint2 *lutl, uint32_t w, int k) {
+    return lutl[((w >> (8 * k)) & 0xffu) << 3];
+}
+constexpr int ATTEND_CHUNKS_TMA = 8;   // CTAs per token (one thread-block cluster)
+__device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+template <int NT, int MT, int MTV, int NBW>
+__global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_constant__ AttnMaps maps,
+                                                              const DecodeAttnArgs a) {
+    extern __shared__ __align__(1024) uint8_t dsm_raw[];
+    // 1024-byte alignment for the swizzled tiles, by offsetting the shared
+    // array itself (keeps every derived pointer in the shared address space)
+    uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
+    constexpr int HP = 16 * MTV, QB = NT * 8 * 128, ROWS_A = 4 * MT * 16;
+    constexpr int DG = 64 * 4 * NBW, NBOX = DG / 256;
+    constexpr int NCH = ATTEND_CHUNKS_TMA;
+    const int chmax = a.chmax;
+    const int SROW = chmax + 4, PROW = chmax + 8, UROW = DG + 4;
+    uint2 *lut = reinterpret_cast<uint2 *>(dsm);
+    uint8_t *ring = dsm + a.off_ring;
+    float *Ss = reinterpret_cast<float *>(dsm + a.off_S);
+    __half *Ph = reinterpret_cast<__half *>(dsm + a.off_P);
+    __half *Pl = Ph + HP * PROW;
+    float *part = reinterpret_cast<float *>(dsm + a.off_part);
+    float *mloc = reinterpret_cast<float *>(dsm + a.off_small);
+    float *lloc = mloc + HP;
+    float *wgt = lloc + HP;
+    float *kn_s = wgt + NCH * HP;
+    float *vn_s = kn_s + chmax;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(vn_s + chmax);  // 8-byte aligned: chmax % 16 == 0
+    uint64_t *full = bars, *empty = bars + NS, *lutfull = bars + 2 * NS, *lutfree = lutfull + 1;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(lutfree + 1);
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int m = blockIdx.z;
+    const int tn = a.pos[m] + 1;
+    const int chl = ((tn + NCH - 1) / NCH + 15) / 16 * 16;
+    const int c0 = rank * chl, nloc = max(0, min(tn, c0 + chl) - c0);
+    const int nmt = (nloc + 15) / 16;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, c = lane & 3;
+    const int64_t rowbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+    const int nblk = a.kvd / 64;
+    const int ngroups = (nmt + 4 * MT - 1) / (4 * MT);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            as::mbar_init(&full[s], 1);
+            as::mbar_init(&empty[s], 4);
+        }
+        as::mbar_init(lutfull, 1);
+        as::mbar_init(lutfree, 4);
+        *abort_flag = 0;
+        as::mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == 4) {
+        // ---- producer
+        if (lane == 0) {
+            as::mbar_expect_tx(lutfull, LUT8_ENTRIES * 8);
+            as::bulk_load(lut, a.lutk, LUT8_ENTRIES * 8, lutfull);
+            // the chunk's key and value code rows are contiguous: pull both into
+            // L2 now, so the ring's tile loads wait on L2 rather than on DRAM
+            if (nloc > 0) {
+                const uint32_t kb = (uint32_t)nloc * a.kpl, vb = (uint32_t)nloc * a.vpl;
+                as::prefetch_l2(a.kcodes + (rowbase + c0) * a.kpl, (kb + 15) & ~15u);
+                as::prefetch_l2(a.vcodes + (rowbase + c0) * a.vpl, (vb + 15) & ~15u);
+            }
+            int it = 0;
+            for (int mg = 0; mg < ngroups; ++mg)
+                for (int q = 0; q < nblk; ++q, ++it) {
+                    const int s = it % NS;
+                    if (!as::mbar_wait(&empty[s], ((it / NS) & 1) ^ 1, abort_flag, a.err)) continue;
+                    uint8_t *st = ring + s * a.sstage;
+                    as::mbar_expect_tx(&full[s], 2 * QB + ROWS_A * 32);
+                    as::tma_load_2d(st, &maps.qh, q * 64, m * a.nh, &full[s]);
+                    as::tma_load_2d(st + QB, &maps.ql, q * 64, m * a.nh, &full[s]);
+                    as::tma_load_2d(st + 2 * QB, &maps.kc, q * 32, (int)(rowbase + c0 + mg * ROWS_A), &full[s]);
+                }
+            if (as::mbar_wait(lutfree, 0, abort_flag, a.err)) {
+                as::mbar_expect_tx(lutfull, LUT8_ENTRIES * 8);
+                as::bulk_load(lut, a.lutv, LUT8_ENTRIES * 8, lutfull);
+            }
+        }
+        __syncwarp();
+        int it = ngroups * nblk;
+        for (int dg = 0; dg < a.ndg; ++dg) {
+            if (lane == 0) {
+                for (int ks = 0; ks < nmt; ++ks, ++it) {
+                    const int s = it % NS;
+                    if (!as::mbar_wait(&empty[s], ((it / NS) & 1) ^ 1, abort_flag, a.err)) continue;
+                    uint8_t *st = ring + s * a.sstage;
+                    as::mbar_expect_tx(&full[s], NBOX * 16 * 128);
+                    for (int b = 0; b < NBOX; ++b)
+                        as::tma_load_2d(st + b * 2048, &maps.vc, dg * (DG / 2) + b * 128, (int)(rowbase + c0 + ks * 16),
+                                        &full[s]);
+                }
+            }
+            __syncwarp();
+            cluster.sync();  // partial tiles written
+            cluster.sync();  // combine done
+        }
+        return;
+    }
+
+    // ---- consumers (warps 0..3)
+    for (int t = tid; t < nloc; t += 128) {
+        kn_s[t] = a.knorm[rowbase + c0 + t];
+        vn_s[t] = a.vnorm[rowbase + c0 + t];
+    }
+    const uint2 *lutl = lut + (lane & 7);
+    as::mbar_wait(lutfull, 0, abort_flag, a.err);
+    bar_consumers();  // norms staged
+    int it = 0;
+    for (int mg = 0; mg < ngroups; ++mg) {
+        const int gm = min(4 * MT, nmt - mg * 4 * MT);
+        float acc[MT][NT][4], acl[MT][NT][4];
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[i][j][e] = acl[i][j][e] = 0.0f;
+        for (int q = 0; q < nblk; ++q, ++it) {
+            const int s = it % NS;
+            const bool ok = as::mbar_wait(&full[s], (it / NS) & 1, abort_flag, a.err);
+            const uint8_t *st = ring + s * a.sstage;
+            if (ok) {
+                uint32_t bq[NT][8], bl[NT][8];
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    // q~ row j * 8 + g (row & 7 == g), dims 16c .. 16c + 15 = 16-byte chunks 2c, 2c + 1
+                    const uint8_t *rh = st + (j * 8 + g) * 128, *rl = st + QB + (j * 8 + g) * 128;
+                    const uint4 u0 = *reinterpret_cast<const uint4 *>(rh + (((2 * c) ^ g) << 4));
+                    const uint4 u1 = *reinterpret_cast<const uint4 *>(rh + (((2 * c + 1) ^ g) << 4));
+                    const uint4 v0 = *reinterpret_cast<const uint4 *>(rl + (((2 * c) ^ g) << 4));
+                    const uint4 v1 = *reinterpret_cast<const uint4 *>(rl + (((2 * c + 1) ^ g) << 4));
+                    bq[j][0] = u0.x; bq[j][1] = u0.y; bq[j][2] = u0.z; bq[j][3] = u0.w;
+                    bq[j][4] = u1.x; bq[j][5] = u1.y; bq[j][6] = u1.z; bq[j][7] = u1.w;
+                    bl[j][0] = v0.x; bl[j][1] = v0.y; bl[j][2] = v0.z; bl[j][3] = v0.w;
+                    bl[j][4] = v1.x; bl[j][5] = v1.y; bl[j][6] = v1.z; bl[j][7] = v1.w;
+                }
+                const uint8_t *kc = st + 2 * QB;
+#pragma unroll
+                for (int i = 0; i < MT; ++i) {
+                    const int mt = warp + 4 * i;
+                    if (mt < gm) {
+                        const uint2 w0 = *reinterpret_cast<const uint2 *>(kc + (mt * 16 + g) * 32 + c * 8);
+                        const uint2 w1 = *reinterpret_cast<const uint2 *>(kc + (mt * 16 + g + 8) * 32 + c * 8);
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {
+                            const uint32_t x0 = s4 < 2 ? w0.x : w0.y, x1 = s4 < 2 ? w1.x : w1.y;
+                            const int k = (s4 & 1) * 2;
+                            const uint2 e0 = lut8_byte(lutl, x0, k), e2 = lut8_byte(lutl, x0, k + 1);
+                            const uint2 e1 = lut8_byte(lutl, x1, k), e3 = lut8_byte(lutl, x1, k + 1);
+#pragma unroll
+                            for (int j = 0; j < NT; ++j)
+                                mma_f16(acc[i][j], e0.x, e1.x, e2.x, e3.x, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+#pragma unroll
+                            for (int j = 0; j < NT; ++j)
+                                mma_f16(acl[i][j], e0.y, e1.y, e2.y, e3.y, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+#pragma unroll
+                            for (int j = 0; j < NT; ++j)
+                                mma_f16(acl[i][j], e0.x, e1.x, e2.x, e3.x, bl[j][2 * s4], bl[j][2 * s4 + 1]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) as::mbar_arrive(&empty[s]);
+        }
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+            const int mt = warp + 4 * i;
+            if (mt < gm) {
+#pragma unroll
+                for (int hrow = 0; hrow < 2; ++hrow) {
+                    const int t = (mg * 4 * MT + mt) * 16 + g + hrow * 8;
+                    const float f = t < nloc ? kn_s[t] * a.scale : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int h = j * 8 + c * 2 + e;
+                            if (h < HP) Ss[h * SROW + t] = (acc[i][j][hrow * 2 + e] + acl[i][j][hrow * 2 + e]) * f;
+                        }
+                }
+            }
+        }
+    }
+    __syncwarp();
+    if (lane == 0) as::mbar_arrive(lutfree);  // the key table is no longer read
+    bar_consumers();                          // all scores in Ss
+
+    // local softmax, one warp per head
+    for (int h = warp; h < HP; h += 4) {
+        __half *ph = Ph + h * PROW, *pl = Pl + h * PROW;
+        const float *srow = Ss + h * SROW;
+        const bool live = h < a.nh && nloc > 0;
+        float mx = -INFINITY, sum = 0.0f;
+        if (live) {
+            for (int t = lane; t < nloc; t += 32) mx = fmaxf(mx, srow[t]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        for (int t = lane; t < nmt * 16; t += 32) {
+            float v = 0.0f;
+            if (live && t < nloc) {
+                const float e = expf(srow[t] - mx);
+                sum += e;
+                v = e * vn_s[t];
+            }
+            const __half hv = __float2half_rn(v);
+            ph[t] = hv;
+            pl[t] = __float2half_rn(v - __half2float(hv));
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            mloc[h] = mx;
+            lloc[h] = sum;
+        }
+    }
+    as::mbar_wait(lutfull, 1, abort_flag, a.err);  // value table in place
+    bar_consumers();                               // P and m / l complete
+
+    for (int dg = 0; dg < a.ndg; ++dg) {
+        float acc[NBW][MTV][8][4];
+#pragma unroll
+        for (int b = 0; b < NBW; ++b)
+#pragma unroll
+            for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[b][i][j][e] = 0.0f;
+        for (int ks = 0; ks < nmt; ++ks, ++it) {
+            const int s = it % NS;
+            const bool ok = as::mbar_wait(&full[s], (it / NS) & 1, abort_flag, a.err);
+            const uint8_t *st = ring + s * a.sstage;
+            if (ok) {
+                uint32_t ah[MTV][4], al[MTV][4];
+#pragma unroll
+                for (int i = 0; i < MTV; ++i) {
+                    const int r = i * 16 + (lane & 15), col = ks * 16 + ((lane >> 4) << 3);
+                    ldsm_x4(smem_u32(Ph + r * PROW + col), ah[i][0], ah[i][1], ah[i][2], ah[i][3]);
+                    ldsm_x4(smem_u32(Pl + r * PROW + col), al[i][0], al[i][1], al[i][2], al[i][3]);
+                }
+#pragma unroll
+                for (int b = 0; b < NBW; ++b) {
+                    // dim block db = warp + 4b: box db / 4, 32-byte column (db % 4); the thread's
+                    // word (dims 8g ..) sits in 16-byte chunk 2 (db % 4) + g / 4 of each row
+                    const int db = warp + 4 * b;
+                    const uint8_t *box = st + (db >> 2) * 2048;
+                    const int chunk = 2 * (db & 3) + (g >> 2), inb = 4 * (g & 3);
+                    auto word = [&](int r) {
+                        return *reinterpret_cast<const uint32_t *>(box + r * 128 + ((chunk ^ (r & 7)) << 4) + inb);
+                    };
+                    const uint32_t x0 = word(2 * c), x1 = word(2 * c + 1), x2 = word(2 * c + 8), x3 = word(2 * c + 9);
+                    uint32_t bh[8][2], bl[8][2];
+#pragma unroll
+                    for (int by = 0; by < 4; ++by) {
+                        const uint2 e0 = lut8_byte(lutl, x0, by), e1 = lut8_byte(lutl, x1, by);
+                        const uint2 e2 = lut8_byte(lutl, x2, by), e3 = lut8_byte(lutl, x3, by);
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const uint32_t sel = hf ? 0x7632u : 0x5410u;
+                            bh[2 * by + hf][0] = prmt(e0.x, e1.x, sel);
+                            bh[2 * by + hf][1] = prmt(e2.x, e3.x, sel);
+                            bl[2 * by + hf][0] = prmt(e0.y, e1.y, sel);
+                            bl[2 * by + hf][1] = prmt(e2.y, e3.y, sel);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj)
+                            mma_f16(acc[b][i][jj], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bh[jj][0], bh[jj][1]);
+#pragma unroll
+                    for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj)
+                            mma_f16(acc[b][i][jj], al[i][0], al[i][1], al[i][2], al[i][3], bh[jj][0], bh[jj][1]);
+#pragma unroll
+                    for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj)
+                            mma_f16(acc[b][i][jj], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bl[jj][0], bl[jj][1]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) as::mbar_arrive(&empty[s]);
+        }
+        bar_consumers();  // the partial tile may overlay the table and the ring (single dim group)
+#pragma unroll
+        for (int b = 0; b < NBW; ++b)
+#pragma unroll
+            for (int i = 0; i < MTV; ++i)
+#pragma unroll
+                for (int hrow = 0; hrow < 2; ++hrow)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            part[(i * 16 + g + hrow * 8) * UROW + (warp + 4 * b) * 64 + 8 * (2 * c + e) + jj] =
+                                acc[b][i][jj][hrow * 2 + e];
+        cluster.sync();
+        if (tid < HP) {
+            const int h = tid;
+            float mr[NCH], lr[NCH];
+#pragma unroll
+            for (int r = 0; r < NCH; ++r) {
+                mr[r] = *cluster.map_shared_rank(mloc + h, r);
+                lr[r] = *cluster.map_shared_rank(lloc + h, r);
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < NCH; ++r) M = fmaxf(M, mr[r]);
+            float L = 0.0f;
+#pragma unroll
+            for (int r = 0; r < NCH; ++r) {
+                mr[r] = mr[r] == -INFINITY ? 0.0f : expf(mr[r] - M);
+                L += mr[r] * lr[r];
+            }
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+            for (int r = 0; r < NCH; ++r) wgt[r * HP + h] = mr[r] * inv;
+        }
+        bar_consumers();
+        const int quads = a.nh * (DG / 4);
+        const int per = (quads + NCH - 1) / NCH;
+        const int q0 = rank * per, q1 = min(quads, q0 + per);
+        for (int qd = q0 + tid; qd < q1; qd += 128) {
+            const int h = qd / (DG / 4), d = (qd % (DG / 4)) * 4;
+            float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 v[NCH];
+#pragma unroll
+            for (int r = 0; r < NCH; ++r)  // a chunk without positions has weight 0 and an unwritten tile
+                v[r] = wgt[r * HP + h] != 0.0f
+                           ? *reinterpret_cast<const float4 *>(cluster.map_shared_rank(part, r) + h * UROW + d)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < NCH; ++r) {
+                const float w = wgt[r * HP + h];
+                u.x += w * v[r].x; u.y += w * v[r].y; u.z += w * v[r].z; u.w += w * v[r].w;
+            }
+            uint32_t h01, l01, h23, l23;
+            split_h2(u.x, u.y, h01, l01);
+            split_h2(u.z, u.w, h23, l23);
+            const int64_t o = ((int64_t)m * a.nh + h) * a.kvd + dg * DG + d;
+            *reinterpret_cast<uint2 *>(a.U + o) = make_uint2(h01, h23);
+            *reinterpret_cast<uint2 *>(a.U_lo + o) = make_uint2(l01, l23);
+        }
+        cluster.sync();  // peers are done reading this CTA's partial tile
+    }
+}
+
+// 8-replica byte tables of both codebooks (LUT8_ENTRIES uint2 each)
+__global__ void build_luts_kernel(const float *kcent, const float *vcent, uint2 *lutk, uint2 *lutv) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 2 * LUT8_ENTRIES) return;
+    const float *cent = i < LUT8_ENTRIES ? kcent : vcent;
+    const int b = (i % LUT8_ENTRIES) >> 3;
+    uint32_t hi, lo;
+    split_h2(cent[b & 15], cent[b >> 4], hi, lo);
+    (i < LUT8_ENTRIES ? lutk : lutv)[i % LUT8_ENTRIES] = make_uint2(hi, lo);
+}
+
+// ---------------------------------------------------------------------------
 // Prefill: dequantize codes of every prompt token to f16 hi/lo centroid vectors.
 __global__ void centroids_kernel(const uint8_t *codes, int pl, int64_t row_stride_codes, const int32_t *slot,
                                  const int32_t *pos, int L, int B, int layer, const float *cent, int kvd, int M,
@@ -686,10 +1077,73 @@ cudaError_t decode_attn_nbw(DecodeAttnArgs &a, cudaStream_t s) {
     }
 }
 
+template <int NT, int NBW>
+cudaError_t launch_decode_attn_tma(DecodeAttnArgs a, cudaStream_t s) {
+    constexpr int MT = NT <= 2 ? 4 : 2, MTV = (NT * 8 + 15) / 16, HP = 16 * MTV;
+    constexpr int DG = 64 * 4 * NBW;
+    const int NCH = ATTEND_CHUNKS_TMA;
+    a.nbg = DG / 64;
+    a.ndg = a.kvd / DG;
+    a.chmax = ((a.B + NCH - 1) / NCH + 15) / 16 * 16;
+    const int stage_a = 2 * NT * 8 * 128 + 4 * MT * 16 * 32, stage_c = (DG / 256) * 2048;
+    a.sstage = (std::max(stage_a, stage_c) + 1023) / 1024 * 1024;
+    const int part = HP * (DG + 4) * 4;
+    a.off_ring = LUT8_ENTRIES * (int)sizeof(uint2);
+    a.off_S = align16(a.off_ring + NS * a.sstage);
+    a.off_P = align16(a.off_S + HP * (a.chmax + 4) * 4);
+    a.off_small = align16(a.off_P + 2 * HP * (a.chmax + 8) * 2);
+    int end = align16(a.off_small + (2 * HP + NCH * HP + 2 * a.chmax) * 4 + (2 * NS + 2) * 8 + 16);
+    if (a.ndg == 1 && part <= a.off_S) {
+        a.off_part = 0;
+    } else {
+        a.off_part = end;
+        end = align16(end + part);
+    }
+    const int smem = end + 1024;  // slack for the 1024-byte alignment of the swizzled tiles
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    static int attr = 0;
+    if (smem > attr) {
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_tma_kernel<NT, MT, MTV, NBW>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = smem;
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(NCH, 1, a.M);
+    lc.blockDim = dim3(160);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = NCH;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, decode_attn_tma_kernel<NT, MT, MTV, NBW>, *a.maps, a);
+}
+
+template <int NT>
+cudaError_t decode_attn_tma_nbw(const DecodeAttnArgs &a, cudaStream_t s) {
+    // dim groups of 256 * NBW dims (NBW <= 2 with two head tiles)
+    const int n256 = a.kvd / 256;
+    if constexpr (NT <= 2) {
+        if (n256 % 3 == 0) return launch_decode_attn_tma<NT, 3>(a, s);
+    }
+    if (n256 % 2 == 0) return launch_decode_attn_tma<NT, 2>(a, s);
+    return launch_decode_attn_tma<NT, 1>(a, s);
+}
+
 cudaError_t decode_attn(const DecodeAttnArgs &a0, cudaStream_t s) {
     DecodeAttnArgs a = a0;
     if (a.M <= 0) return cudaSuccess;
     if (a.kvd % 64 || a.nh < 1 || a.nh > 32) return cudaErrorInvalidValue;
+    if (a.maps && a.lutk && a.lutv && a.kvd % 256 == 0) {
+        const int nt = (a.nh + 7) / 8;
+        if (nt == 1) return decode_attn_tma_nbw<1>(a, s);
+        if (nt == 2) return decode_attn_tma_nbw<2>(a, s);
+        return decode_attn_tma_nbw<4>(a, s);
+    }
     // 64-dim blocks per dim group: the largest divisor of kv_dim / 64 up to 12
     // (up to 8 with two head tiles, whose accumulators take twice the registers)
     const int nblk = a.kvd / 64;
@@ -738,6 +1192,22 @@ cudaError_t flash_prefill(const FlashArgs &a, cudaStream_t s) {
         case 128: return launch_fa<128>(a, s);
         default: return cudaErrorInvalidValue;
     }
+}
+
+bool decode_attn_maps(AttnMaps *maps, const uint8_t *kcodes, const uint8_t *vcodes, int64_t rows, int kpl, int vpl,
+                      const __half *qrot, const __half *qrot_lo, int64_t qrows, int kvd, int nh) {
+    if (kvd % 256 || nh < 1 || nh > 32) return false;
+    const int nt = (nh + 7) / 8 <= 2 ? (nh + 7) / 8 : 4;
+    const int rows_a = 4 * (nt <= 2 ? 4 : 2) * 16;
+    return make_tensor_map(&maps->kc, kcodes, rows, kpl, kpl, 1, 32, rows_a, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           make_tensor_map(&maps->vc, vcodes, rows, vpl, vpl, 1, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           make_tensor_map(&maps->qh, qrot, qrows, kvd, kvd, 2, 64, nt * 8, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           make_tensor_map(&maps->ql, qrot_lo, qrows, kvd, kvd, 2, 64, nt * 8, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+cudaError_t build_luts(const float *kcent, const float *vcent, uint2 *lutk, uint2 *lutv, cudaStream_t s) {
+    build_luts_kernel<<<(2 * LUT8_ENTRIES + 255) / 256, 256, 0, s>>>(kcent, vcent, lutk, lutv);
+    return cudaGetLastError();
 }
 
 }  // namespace attn

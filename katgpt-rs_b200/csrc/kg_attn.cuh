@@ -1,5 +1,6 @@
 // kg_attn.cuh — attention kernels over the TurboQuant KV cache (kg_attn.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -14,6 +15,17 @@ namespace attn {
 // Decode attention of M single-token queries over the cached codes:
 // U[m, h] = u~ = sum_t softmax_t(s)[t] * norm_v[t] * centroid(code_v[t]) with
 // s[t] = norm_k[t] * scale * <centroid(code_k[t]), q~_h>, f16 hi/lo out.
+// Tensor maps of the TMA decode kernel (kv_dim a multiple of 256), built once
+// per context: key / value code arenas as [rows x pl] bytes, q~ hi / lo as
+// [tokens * heads x kv_dim] f16.
+struct AttnMaps {
+    CUtensorMap kc, vc, qh, ql;
+};
+bool decode_attn_maps(AttnMaps *maps, const uint8_t *kcodes, const uint8_t *vcodes, int64_t rows, int kpl, int vpl,
+                      const __half *qrot, const __half *qrot_lo, int64_t qrows, int kvd, int nh);
+// the replicated byte tables of both codebooks (2048 uint2 each: 8 replicas)
+cudaError_t build_luts(const float *kcent, const float *vcent, uint2 *lutk, uint2 *lutv, cudaStream_t s);
+
 struct DecodeAttnArgs {
     const uint8_t *kcodes, *vcodes;   // [slot][layer][pos][pl]
     const float *knorm, *vnorm;       // [slot][layer][pos]
@@ -23,6 +35,9 @@ struct DecodeAttnArgs {
     __half *U, *U_lo;                 // [M][nh][kvd]
     int M, nh, kvd, kpl, vpl, L, B, layer;
     float scale;
+    const AttnMaps *maps;             // host copy; null: the cp.async kernel
+    const uint2 *lutk, *lutv;         // replicated tables (TMA kernel)
+    int *err;                         // device error word (timeouts)
     // set by the launcher
     int nbg, ndg, chmax, sstage, vrow, vstage, off_ring, off_S, off_P, off_small, off_part;
 };

@@ -168,6 +168,11 @@ cudaError_t big_init(kg_ctx *ctx) {
     std::copy(ctx->h_vc.begin(), ctx->h_vc.end(), vc.begin());
     BIG_TRY(cudaMemcpy(g.kcent, kc.data(), 64, cudaMemcpyHostToDevice));
     BIG_TRY(cudaMemcpy(g.vcent, vc.data(), 64, cudaMemcpyHostToDevice));
+    BIG_TRY(dalloc(&g.lutk, 4096, own));
+    BIG_TRY(dalloc(&g.lutv, 4096, own));
+    BIG_TRY(attn::build_luts(g.kcent, g.vcent, g.lutk, g.lutv, ctx->stream));
+    g.has_maps = attn::decode_attn_maps(&g.maps, g.kcodes, g.vcodes, (int64_t)S * L * B, (int)ctx->kpl, (int)ctx->vpl,
+                                        g.qrot, g.qrot2, (int64_t)S * ctx->nh, kvd, (int)ctx->nh);
     // f16 hi/lo splits of the rotation for the tensor-core GEMMs
     BIG_TRY(bf::f32_to_f16_split(ctx->rot, kvd * kvd, g.rot_h, g.rot_l, ctx->stream));
     BIG_TRY(bf::f32_to_f16_split(ctx->rot_t, kvd * kvd, g.rot_th, g.rot_tl, ctx->stream));
@@ -362,6 +367,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             da.slot = g.slot_of; da.pos = g.pos_of; da.U = g.U; da.U_lo = g.U2;
             da.M = M; da.nh = nh; da.kvd = kvd; da.kpl = (int)ctx->kpl; da.vpl = (int)ctx->vpl;
             da.L = L; da.B = B; da.layer = l; da.scale = scale;
+            da.maps = g.has_maps ? &g.maps : nullptr; da.lutk = g.lutk; da.lutv = g.lutv; da.err = ctx->d_err;
             prof_mark(ctx, KG_PROF_ATTN, 0, s);
             BIG_TRY(attn::decode_attn(da, s));
             prof_mark(ctx, KG_PROF_ATTN, 1, s);

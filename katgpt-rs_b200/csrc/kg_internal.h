@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "../../include/kg_abi.h"
+#include "kg_attn.cuh"
 
 namespace kg {
 
@@ -86,6 +87,11 @@ struct BigState {
     uint8_t *skip = nullptr;
     int *alive = nullptr;
     int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;
+    // TMA decode attention: tensor maps over the code arenas and q~, and the
+    // replicated centroid tables (has_maps false: the cp.async kernel runs)
+    attn::AttnMaps maps;
+    bool has_maps = false;
+    uint2 *lutk = nullptr, *lutv = nullptr;
 };
 int big_supported(const kg_config &c, std::string &why);
 }  // namespace kg

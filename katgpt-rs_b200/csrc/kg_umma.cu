@@ -26,7 +26,7 @@
 #include <mutex>
 #include <type_traits>
 
-#include "../../include/kg_abi.h"
+#include "kg_async.cuh"
 #include "kg_bf16.cuh"
 #include "kg_umma.cuh"
 
@@ -36,52 +36,7 @@ namespace {
 
 constexpr int BM = 128, BK = 64, STG = 3, THREADS = 192;
 constexpr int STAGE_BYTES = 64 * 1024;
-constexpr long long WAIT_CYCLES = 4ll << 30;  // about 2 s at 2 GHz
-
-__device__ __forceinline__ uint32_t sa(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(sa(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(sa(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(sa(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(sa(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Wait for the phase of `parity` to complete. Returns false (and raises the
-// abort flag and the error word) when the clock limit passes or another
-// thread of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
-    if (mbar_try(b, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try(b, parity)) {
-        if (*abort_flag) return false;
-        if (clock64() - t0 > WAIT_CYCLES) {
-            *abort_flag = 1;
-            if (err) atomicExch(err, (int)KG_ERR_TIMEOUT);
-            return false;
-        }
-    }
-    return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];\n" ::"r"(sa(dst)),
-        "l"(tm), "r"(x), "r"(y), "r"(sa(bar))
-        : "memory");
-}
+using namespace as;
 
 // shared-memory matrix descriptor: K-major, 128-byte swizzle (8-row x 128 B
 // atoms, 1024 B between atoms along M/N), descriptor version 1
@@ -143,9 +98,10 @@ struct Maps {
 template <typename T, bool SA, bool SB, int BN>
 __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Maps maps, const bf::Gemm g,
                                                               int *err) {
-    extern __shared__ uint8_t dsm_raw[];
-    // 1024-byte alignment for the 128B-swizzled tiles
-    uint8_t *dsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t dsm_raw[];
+    // 1024-byte alignment for the 128B-swizzled tiles (offsetting the shared
+    // array keeps derived pointers in the shared address space)
+    uint8_t *dsm = dsm_raw + ((1024u - (sa(dsm_raw) & 1023u)) & 1023u);
     constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
     constexpr uint32_t TX = A_BYTES * (SA ? 2 : 1) + B_BYTES * (SB ? 2 : 1);
     static_assert(TX <= STAGE_BYTES, "stage too large");
@@ -324,41 +280,18 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// 2-D map over a row-major [rows x cols] 16-bit matrix with leading dimension
-// ld (elements); box = 64 columns x box_rows rows, 128-byte swizzle
-bool make_map(CUtensorMap *m, const void *base, int64_t rows, int64_t cols, int64_t ld, int box_rows, bool f16) {
-    auto fn = encode_fn();
-    if (!fn || !base) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-    const cuuint32_t es[2] = {1, 1};
-    return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
-              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <typename T, bool SA, bool SB>
 cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
     constexpr int BN = SB ? 128 : 256;
     const bool f16 = std::is_same<T, __half>::value;
     Maps maps;
     std::memset(&maps, 0, sizeof(maps));
-    if (!make_map(&maps.a, g.A, g.M, g.K, g.lda, BM, f16) || (SA && !make_map(&maps.a2, g.A2, g.M, g.K, g.lda, BM, f16)) ||
-        !make_map(&maps.b, g.B, g.N, g.K, g.ldb, BN, f16) || (SB && !make_map(&maps.b2, g.B2, g.N, g.K, g.ldb, BN, f16)))
+    (void)f16;  // 16-bit elements either way: the map only moves bytes
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+    if (!make_tensor_map(&maps.a, g.A, g.M, g.K, g.lda, 2, BK, BM, SW) ||
+        (SA && !make_tensor_map(&maps.a2, g.A2, g.M, g.K, g.lda, 2, BK, BM, SW)) ||
+        !make_tensor_map(&maps.b, g.B, g.N, g.K, g.ldb, 2, BK, BN, SW) ||
+        (SB && !make_tensor_map(&maps.b2, g.B2, g.N, g.K, g.ldb, 2, BK, BN, SW)))
         return cudaErrorInvalidValue;
     const int smem = 1024 + STG * STAGE_BYTES + 256;
     static bool attr = false;
@@ -390,7 +323,7 @@ bool supported(const bf::Gemm &g) {
     } else if (g.ldcb % 8 || (reinterpret_cast<uintptr_t>(g.Cb) & 15)) {
         return false;
     }
-    return encode_fn() != nullptr;
+    return tensor_map_encoder() != nullptr;
 }
 
 cudaError_t gemm(const bf::Gemm &g, cudaStream_t s, int *err) {
@@ -407,4 +340,31 @@ cudaError_t gemm(const bf::Gemm &g, cudaStream_t s, int *err) {
 }
 
 }  // namespace umma
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool make_tensor_map(CUtensorMap *m, const void *base, int64_t rows, int64_t cols, int64_t ld, int elem,
+                     int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
+    auto fn = tensor_map_encoder();
+    if (!fn || !base) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld * elem)};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    const CUtensorMapDataType dt = elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace kg
