@@ -110,6 +110,18 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU legs: the oracle (C++ restatement of the reference's x86 AVX2 path)
 
+def profiled_traffic(name):
+    """DRAM bytes per launch recorded by the ncu capture summarised in profiles/."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as fh:
+            for line in fh:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
@@ -308,6 +320,7 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     gemm_gbs = gemm_bytes / (ph_ms[2] / 1000.0) / 1e9 if ph_ms[2] > 0 else None
     peaks = load_peaks()
     peak = peaks.get("hbm_gbs", 6650.0)
+    traffic = profiled_traffic("decode_attention_c3.txt")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -322,7 +335,9 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
         "kernels_per_step": int(graph_kernels),
         "roofline": {"bound": "hbm", "kernel": "decode KV attention (scores + softmax + values over 4-bit codes)",
                      "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
-                     "frac": (attn_gbs / peak) if attn_gbs else None, "traffic": None,
+                     "frac": (attn_gbs / peak) if attn_gbs else None, "traffic": traffic,
+                     "traffic_unit": "bytes per launch (one layer), ncu dram read+write",
+                     "algorithmic_bytes_per_launch": attn_bytes / L,
                      "algorithmic_bytes_per_step": attn_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
         "phases_ms_per_step": {"kv_attention": ph_ms[0], "tq_encode": ph_ms[1], "weight_gemms": ph_ms[2],
