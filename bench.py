@@ -169,6 +169,19 @@ def cpu_sample_c2(budget_s=10.0, threads=None):
     return done / el, threads, f"{done // C2_T} sequences x {C2_T} positions (forward_sp_kv_quant, {el:.1f} s)"
 
 
+def workload_config(workload, world):
+    """The `config` of a bench line (shared by both arms)."""
+    if workload == "c3":
+        return {"workload": "c3: n_layer 12, n_embd 768, 12 heads, mlp 3072, vocab 32000, block 2048, "
+                            "bf16 weights N(0,0.02), 4-bit TurboQuant KV (forward_quantized); 64 sequences, "
+                            "1024-token prefill then teacher-forced decode",
+                "global_batch": world * C3_SEQS, "seq_len": C3_PREFILL, "parallelism": f"dp{world} (sequence shards)",
+                "l2": "flushed between steps (256 MiB write, outside the timed events)"}
+    return {"workload": "c2: Config::micro + SpKvQuant + TurboQuant 3-bit, 65536 sequences x 16 positions",
+            "global_batch": world * C2_SEQS, "seq_len": C2_T, "parallelism": f"dp{world} (sequence shards)",
+            "l2": "flushed between steps (256 MiB write, outside the timed events)"}
+
+
 def run_reference(args):
     """The reference arm: the oracle on all host cores, rank 0 only."""
     if int(os.environ.get("RANK", "0")) != 0:
@@ -182,8 +195,9 @@ def run_reference(args):
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": len(vals),
             "warmup": 0, "ms_per_step": 1000.0 * (time.perf_counter() - t0) / len(vals), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": args.workload, "note": "reference = its x86 AVX2 CPU path restated in C++ "
-                       "(the Rust reference cannot be built here)"},
+            "config": dict(workload_config(args.workload, args.gpus),
+                           note="reference = its x86 AVX2 CPU path restated in C++ (the Rust reference cannot "
+                                "be built here), a bounded sample of the workload on the host cores"),
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -325,11 +339,7 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "c3: n_layer 12, n_embd 768, 12 heads, mlp 3072, vocab 32000, block 2048, "
-                               "bf16 weights N(0,0.02), 4-bit TurboQuant KV (forward_quantized); 64 sequences, "
-                               "1024-token prefill then teacher-forced decode",
-                   "global_batch": world * n, "seq_len": C3_PREFILL, "parallelism": f"dp{world} (sequence shards)",
-                   "l2": "flushed between steps (256 MiB write, outside the timed events)"},
+        "config": workload_config("c3", world),
         "gpu_launches": int(graph_kernels * args.steps),
         "decode_step": "one CUDA graph per step" if graph_kernels else "eager",
         "kernels_per_step": int(graph_kernels),
@@ -424,9 +434,7 @@ def bench_c2(args, torch, dist, kgcuda, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c2: Config::micro + SpKvQuant + TurboQuant 3-bit, 65536 sequences x 16 positions",
-                   "global_batch": world * n_seq, "seq_len": C2_T, "parallelism": f"dp{world} (sequence shards)",
-                   "l2": "flushed between steps (256 MiB write, outside the timed events)"},
+        "config": workload_config("c2", world),
         "gpu_launches": C2_T * args.steps,
         "roofline": {"bound": "hbm", "kernel": "micro_forward", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,
@@ -459,12 +467,13 @@ def main():
                                 device_id=torch.device("cuda", local))
     fn = bench_c3 if args.workload == "c3" else bench_c2
     line = fn(args, torch, dist, kgcuda, world, rank, local)
-    if rank == 0:
+    if rank == 0 and world == 1:
         try:
             v, cores, sample = (cpu_sample_c3 if args.workload == "c3" else cpu_sample_c2)()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
         except Exception as ex:  # the baseline must not break the bench line
             line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": 0, "kind": "port", "sample": f"failed: {ex}"}
+    if rank == 0:
         print(json.dumps(line, default=float), flush=True)
     if world > 1:
         dist.barrier()
