@@ -265,8 +265,14 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     pf_flops = 2.0 * 2 * n * C3_PREFILL * C3["n_layer"] * (3 * d * d + d * d + 2 * d * m)
     pf_gemm_tf = pf_flops / (float(pf_ms[2]) * 1e-3) / 1e12 if pf_ms[2] > 0 else None
 
+    # N > 1: each rank decodes its own sequences; NCCL gathers the logits of
+    # every rank after each step (the only collective on the path)
+    d_all = torch.empty((world, n, V), dtype=torch.float32, device=dev) if world > 1 else None
+
     def step(s):
         be.forward_batch_dev(n, 1, P(d_ids), P(d_dec[s]), P(d_pos[s]), P(d_log), None, sp)
+        if world > 1:
+            dist.all_gather_into_tensor(d_all, d_log)
 
     # warm-up: the first step of a batch shape runs eagerly, the second
     # captures the decode step as a CUDA graph, later steps replay it
@@ -340,6 +346,7 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config("c3", world),
+        "collective": (f"NCCL all_gather of each rank's logits ({n} x {V} f32) per step" if world > 1 else None),
         "gpu_launches": int(graph_kernels * args.steps),
         "decode_step": "one CUDA graph per step" if graph_kernels else "eager",
         "kernels_per_step": int(graph_kernels),

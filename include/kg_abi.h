@@ -132,6 +132,21 @@ int kg_download_weights(kg_ctx *ctx, float *host_out, int64_t count);
  * as MultiLayerKVCache::reset / TurboQuantKVCache::reset / SpKvQuantCache::reset. */
 int kg_seq_reset(kg_ctx *ctx, int32_t seq);
 int kg_seq_reset_all(kg_ctx *ctx);
+/* Sequence slots: kg_seq_alloc hands out a free slot id in [0, max_seqs)
+ * (reset, ready for position 0) or KG_ERR_OOM when all are taken;
+ * kg_seq_free returns one. Slots may also be addressed directly by id. */
+int kg_seq_alloc(kg_ctx *ctx, int32_t *seq_out);
+int kg_seq_free(kg_ctx *ctx, int32_t seq);
+
+/* ---- KV snapshot / restore (MultiLayerKVCache::snapshot / restore,
+ * crates/katgpt-transformer/src/kv_cache.rs:89-122): the device cache state of
+ * one sequence for positions [0, pos) of every layer, kept in caller-owned
+ * DEVICE memory of kg_kv_snapshot_bytes(ctx, pos) bytes. Restore writes it
+ * back and zeroes positions [pos, block_size) like the reference. Both are
+ * enqueued on `stream` (NULL = the legacy default stream). ---- */
+int64_t kg_kv_snapshot_bytes(const kg_ctx *ctx, int32_t pos);
+int kg_kv_snapshot(kg_ctx *ctx, int32_t seq, int32_t pos, void *dst_dev, void *stream);
+int kg_kv_restore(kg_ctx *ctx, int32_t seq, int32_t pos, const void *src_dev, void *stream);
 
 /* ---- forward ---- */
 

@@ -713,3 +713,100 @@ void prof_mark(kg_ctx *ctx, int phase, int end, cudaStream_t s) {
 }  // namespace kg
 
 int64_t kg_graph_kernels(const kg_ctx *ctx) { return ctx ? ctx->last_graph_kernels : 0; }
+
+// ---- sequence slots and KV snapshots ---------------------------------------
+
+int kg_seq_alloc(kg_ctx *ctx, int32_t *seq_out) {
+    if (!ctx || !seq_out) return KG_ERR_INVALID_ARG;
+    if (ctx->slot_used.size() != (size_t)ctx->cfg.max_seqs) ctx->slot_used.assign(ctx->cfg.max_seqs, 0);
+    for (int32_t i = 0; i < ctx->cfg.max_seqs; ++i)
+        if (!ctx->slot_used[i]) {
+            const int rc = kg_seq_reset(ctx, i);
+            if (rc) return rc;
+            ctx->slot_used[i] = 1;
+            *seq_out = i;
+            return KG_OK;
+        }
+    return fail(ctx, KG_ERR_OOM, "no free sequence slot");
+}
+
+int kg_seq_free(kg_ctx *ctx, int32_t seq) {
+    if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs) return KG_ERR_INVALID_ARG;
+    if (ctx->slot_used.size() == (size_t)ctx->cfg.max_seqs) ctx->slot_used[seq] = 0;
+    return KG_OK;
+}
+
+namespace {
+// One per-sequence cache array: `w` bytes per position, layer planes of
+// block_size positions, slot planes of L layers.
+struct KvArray {
+    uint8_t *base;
+    size_t w;
+};
+int kv_arrays(const kg_ctx *ctx, KvArray *out) {
+    int n = 0;
+    if (ctx->big_path) {
+        const kg::BigState &g = ctx->big;
+        out[n++] = {g.kcodes, (size_t)ctx->kpl};
+        out[n++] = {g.vcodes, (size_t)ctx->vpl};
+        out[n++] = {reinterpret_cast<uint8_t *>(g.knorm), 4};
+        out[n++] = {reinterpret_cast<uint8_t *>(g.vnorm), 4};
+    } else if (ctx->micro) {
+        out[n++] = {reinterpret_cast<uint8_t *>(ctx->Kf), (size_t)ctx->kvd * 4};
+        out[n++] = {reinterpret_cast<uint8_t *>(ctx->Vf), (size_t)ctx->kvd * 4};
+        if (ctx->kpl + ctx->vpl) out[n++] = {ctx->codes, (size_t)(ctx->kpl + ctx->vpl)};
+        out[n++] = {reinterpret_cast<uint8_t *>(ctx->norms), 8};
+        out[n++] = {reinterpret_cast<uint8_t *>(ctx->util), 4};
+    }
+    return n;
+}
+}  // namespace
+
+int64_t kg_kv_snapshot_bytes(const kg_ctx *ctx, int32_t pos) {
+    if (!ctx || pos < 0 || pos > ctx->B) return 0;
+    KvArray arr[8];
+    const int n = kv_arrays(ctx, arr);
+    int64_t b = 0;
+    for (int i = 0; i < n; ++i) b += (int64_t)pos * ctx->L * arr[i].w;
+    return b;
+}
+
+int kg_kv_snapshot(kg_ctx *ctx, int32_t seq, int32_t pos, void *dst_dev, void *stream) {
+    if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs || pos < 0 || pos > ctx->B || (pos > 0 && !dst_dev))
+        return KG_ERR_INVALID_ARG;
+    if (!ctx->big_path && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no device KV cache for this shape");
+    if (pos == 0) return KG_OK;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    KvArray arr[8];
+    const int n = kv_arrays(ctx, arr);
+    uint8_t *dst = static_cast<uint8_t *>(dst_dev);
+    for (int i = 0; i < n; ++i) {
+        const size_t pitch = (size_t)ctx->B * arr[i].w, width = (size_t)pos * arr[i].w;
+        const uint8_t *src = arr[i].base + (size_t)seq * ctx->L * pitch;
+        KG_CUDA(ctx, cudaMemcpy2DAsync(dst, width, src, pitch, width, ctx->L, cudaMemcpyDeviceToDevice, s));
+        dst += width * ctx->L;
+    }
+    return KG_OK;
+}
+
+int kg_kv_restore(kg_ctx *ctx, int32_t seq, int32_t pos, const void *src_dev, void *stream) {
+    if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs || pos < 0 || pos > ctx->B || (pos > 0 && !src_dev))
+        return KG_ERR_INVALID_ARG;
+    if (!ctx->big_path && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no device KV cache for this shape");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    KvArray arr[8];
+    const int n = kv_arrays(ctx, arr);
+    const uint8_t *src = static_cast<const uint8_t *>(src_dev);
+    for (int i = 0; i < n; ++i) {
+        const size_t pitch = (size_t)ctx->B * arr[i].w, width = (size_t)pos * arr[i].w;
+        uint8_t *dst = arr[i].base + (size_t)seq * ctx->L * pitch;
+        if (pos > 0) {
+            KG_CUDA(ctx, cudaMemcpy2DAsync(dst, pitch, src, width, width, ctx->L, cudaMemcpyDeviceToDevice, s));
+            src += width * ctx->L;
+        }
+        if (pos < ctx->B) KG_CUDA(ctx, cudaMemset2DAsync(dst + width, pitch, 0, pitch - width, ctx->L, s));
+    }
+    return KG_OK;
+}

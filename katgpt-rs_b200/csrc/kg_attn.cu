@@ -469,7 +469,7 @@ __device__ __forceinline__ uint2 lut8_byte(const uint2 *lutl, uint32_t w, int k)
 constexpr int ATTEND_CHUNKS_TMA = 8;   // CTAs per token (one thread-block cluster)
 __device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
 
-template <int NT, int MT, int MTV, int NBW>
+template <int NT, int MT, int MTV, int NBW, bool QRES>
 __global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_constant__ AttnMaps maps,
                                                               const DecodeAttnArgs a) {
     extern __shared__ __align__(1024) uint8_t dsm_raw[];
@@ -492,9 +492,12 @@ __global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_co
     float *wgt = lloc + HP;
     float *kn_s = wgt + NCH * HP;
     float *vn_s = kn_s + chmax;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(vn_s + chmax);  // 8-byte aligned: chmax % 16 == 0
+    float *hred = vn_s + chmax;                                    // [2][4][HP] per-warp head max / sum
+    uint64_t *bars = reinterpret_cast<uint64_t *>(hred + 8 * HP);  // 8-byte aligned: chmax, HP % 16 == 0
     uint64_t *full = bars, *empty = bars + NS, *lutfull = bars + 2 * NS, *lutfree = lutfull + 1;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(lutfree + 1);
+    uint64_t *fullA = lutfree + 1, *emptyA = fullA + 4, *qfull = emptyA + 4;  // resident-q~ scores phase
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(qfull + 1);
+    const uint8_t *qres = dsm + a.off_q;                           // [blocks][hi, lo][NT * 8][128 B]
 
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
@@ -516,6 +519,11 @@ __global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_co
         }
         as::mbar_init(lutfull, 1);
         as::mbar_init(lutfree, 4);
+        for (int w = 0; w < 4; ++w) {
+            as::mbar_init(&fullA[w], 1);
+            as::mbar_init(&emptyA[w], 1);
+        }
+        as::mbar_init(qfull, 1);
         *abort_flag = 0;
         as::mbar_fence_init();
     }
@@ -533,24 +541,43 @@ __global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_co
                 as::prefetch_l2(a.kcodes + (rowbase + c0) * a.kpl, (kb + 15) & ~15u);
                 as::prefetch_l2(a.vcodes + (rowbase + c0) * a.vpl, (vb + 15) & ~15u);
             }
-            int it = 0;
-            for (int mg = 0; mg < ngroups; ++mg)
-                for (int q = 0; q < nblk; ++q, ++it) {
-                    const int s = it % NS;
-                    if (!as::mbar_wait(&empty[s], ((it / NS) & 1) ^ 1, abort_flag, a.err)) continue;
-                    uint8_t *st = ring + s * a.sstage;
-                    as::mbar_expect_tx(&full[s], 2 * QB + ROWS_A * 32);
-                    as::tma_load_2d(st, &maps.qh, q * 64, m * a.nh, &full[s]);
-                    as::tma_load_2d(st + QB, &maps.ql, q * 64, m * a.nh, &full[s]);
-                    as::tma_load_2d(st + 2 * QB, &maps.kc, q * 32, (int)(rowbase + c0 + mg * ROWS_A), &full[s]);
+            if constexpr (QRES) {
+                // q~ of the token once, then one 16-position key tile (kpl bytes
+                // per row, 128-byte swizzled boxes) per m-tile into its warp's slot
+                as::mbar_expect_tx(qfull, 2 * nblk * QB);
+                for (int q = 0; q < nblk; ++q) {
+                    as::tma_load_2d(dsm + a.off_q + q * 2 * QB, &maps.qh, q * 64, m * a.nh, qfull);
+                    as::tma_load_2d(dsm + a.off_q + q * 2 * QB + QB, &maps.ql, q * 64, m * a.nh, qfull);
                 }
+                const int kb = a.kpl / 128;
+                for (int mt = 0; mt < nmt; ++mt) {
+                    const int w = mt & 3;
+                    if (!as::mbar_wait(&emptyA[w], ((mt >> 2) & 1) ^ 1, abort_flag, a.err)) continue;
+                    uint8_t *st = ring + w * a.sstage_a;
+                    as::mbar_expect_tx(&fullA[w], kb * 2048);
+                    for (int b = 0; b < kb; ++b)
+                        as::tma_load_2d(st + b * 2048, &maps.kt, b * 128, (int)(rowbase + c0 + mt * 16), &fullA[w]);
+                }
+            } else {
+                int it = 0;
+                for (int mg = 0; mg < ngroups; ++mg)
+                    for (int q = 0; q < nblk; ++q, ++it) {
+                        const int s = it % NS;
+                        if (!as::mbar_wait(&empty[s], ((it / NS) & 1) ^ 1, abort_flag, a.err)) continue;
+                        uint8_t *st = ring + s * a.sstage;
+                        as::mbar_expect_tx(&full[s], 2 * QB + ROWS_A * 32);
+                        as::tma_load_2d(st, &maps.qh, q * 64, m * a.nh, &full[s]);
+                        as::tma_load_2d(st + QB, &maps.ql, q * 64, m * a.nh, &full[s]);
+                        as::tma_load_2d(st + 2 * QB, &maps.kc, q * 32, (int)(rowbase + c0 + mg * ROWS_A), &full[s]);
+                    }
+            }
             if (as::mbar_wait(lutfree, 0, abort_flag, a.err)) {
                 as::mbar_expect_tx(lutfull, LUT8_ENTRIES * 8);
                 as::bulk_load(lut, a.lutv, LUT8_ENTRIES * 8, lutfull);
             }
         }
         __syncwarp();
-        int it = ngroups * nblk;
+        int it = QRES ? 0 : ngroups * nblk;
         for (int dg = 0; dg < a.ndg; ++dg) {
             if (lane == 0) {
                 for (int ks = 0; ks < nmt; ++ks, ++it) {
@@ -579,114 +606,266 @@ __global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_co
     as::mbar_wait(lutfull, 0, abort_flag, a.err);
     bar_consumers();  // norms staged
     int it = 0;
-    for (int mg = 0; mg < ngroups; ++mg) {
-        const int gm = min(4 * MT, nmt - mg * 4 * MT);
-        float acc[MT][NT][4], acl[MT][NT][4];
-#pragma unroll
-        for (int i = 0; i < MT; ++i)
-#pragma unroll
-            for (int j = 0; j < NT; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[i][j][e] = acl[i][j][e] = 0.0f;
-        for (int q = 0; q < nblk; ++q, ++it) {
-            const int s = it % NS;
-            const bool ok = as::mbar_wait(&full[s], (it / NS) & 1, abort_flag, a.err);
-            const uint8_t *st = ring + s * a.sstage;
-            if (ok) {
-                uint32_t bq[NT][8], bl[NT][8];
-#pragma unroll
-                for (int j = 0; j < NT; ++j) {
-                    // q~ row j * 8 + g (row & 7 == g), dims 16c .. 16c + 15 = 16-byte chunks 2c, 2c + 1
-                    const uint8_t *rh = st + (j * 8 + g) * 128, *rl = st + QB + (j * 8 + g) * 128;
-                    const uint4 u0 = *reinterpret_cast<const uint4 *>(rh + (((2 * c) ^ g) << 4));
-                    const uint4 u1 = *reinterpret_cast<const uint4 *>(rh + (((2 * c + 1) ^ g) << 4));
-                    const uint4 v0 = *reinterpret_cast<const uint4 *>(rl + (((2 * c) ^ g) << 4));
-                    const uint4 v1 = *reinterpret_cast<const uint4 *>(rl + (((2 * c + 1) ^ g) << 4));
-                    bq[j][0] = u0.x; bq[j][1] = u0.y; bq[j][2] = u0.z; bq[j][3] = u0.w;
-                    bq[j][4] = u1.x; bq[j][5] = u1.y; bq[j][6] = u1.z; bq[j][7] = u1.w;
-                    bl[j][0] = v0.x; bl[j][1] = v0.y; bl[j][2] = v0.z; bl[j][3] = v0.w;
-                    bl[j][4] = v1.x; bl[j][5] = v1.y; bl[j][6] = v1.z; bl[j][7] = v1.w;
-                }
-                const uint8_t *kc = st + 2 * QB;
-#pragma unroll
-                for (int i = 0; i < MT; ++i) {
-                    const int mt = warp + 4 * i;
-                    if (mt < gm) {
-                        const uint2 w0 = *reinterpret_cast<const uint2 *>(kc + (mt * 16 + g) * 32 + c * 8);
-                        const uint2 w1 = *reinterpret_cast<const uint2 *>(kc + (mt * 16 + g + 8) * 32 + c * 8);
-#pragma unroll
-                        for (int s4 = 0; s4 < 4; ++s4) {
-                            const uint32_t x0 = s4 < 2 ? w0.x : w0.y, x1 = s4 < 2 ? w1.x : w1.y;
-                            const int k = (s4 & 1) * 2;
-                            const uint2 e0 = lut8_byte(lutl, x0, k), e2 = lut8_byte(lutl, x0, k + 1);
-                            const uint2 e1 = lut8_byte(lutl, x1, k), e3 = lut8_byte(lutl, x1, k + 1);
-#pragma unroll
-                            for (int j = 0; j < NT; ++j)
-                                mma_f16(acc[i][j], e0.x, e1.x, e2.x, e3.x, bq[j][2 * s4], bq[j][2 * s4 + 1]);
-#pragma unroll
-                            for (int j = 0; j < NT; ++j)
-                                mma_f16(acl[i][j], e0.y, e1.y, e2.y, e3.y, bq[j][2 * s4], bq[j][2 * s4 + 1]);
-#pragma unroll
-                            for (int j = 0; j < NT; ++j)
-                                mma_f16(acl[i][j], e0.x, e1.x, e2.x, e3.x, bl[j][2 * s4], bl[j][2 * s4 + 1]);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) as::mbar_arrive(&empty[s]);
-        }
+    if constexpr (QRES) {
+        as::mbar_wait(qfull, 0, abort_flag, a.err);
+        // scores of this warp's m-tiles (mt = warp + 4i), kept in registers
+        float sc[MT][NT][4];
 #pragma unroll
         for (int i = 0; i < MT; ++i) {
             const int mt = warp + 4 * i;
-            if (mt < gm) {
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sc[i][j][e] = -INFINITY;
+            if (mt < nmt) {
+                const bool ok = as::mbar_wait(&fullA[warp], i & 1, abort_flag, a.err);
+                const uint8_t *st = ring + warp * a.sstage_a;
+                // hi*hi, lo*hi and hi*lo products in separate accumulators (independent MMA chains)
+                float s0[NT][4], s1[NT][4], s2[NT][4];
+#pragma unroll
+                for (int j = 0; j < NT; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s0[j][e] = s1[j][e] = s2[j][e] = 0.0f;
+                if (ok) {
+                    for (int q = 0; q < nblk; ++q) {
+                        const uint8_t *qh = qres + q * 2 * QB, *ql = qh + QB;
+                        uint32_t bq[NT][8], bl[NT][8];
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) {
+                            const uint8_t *rh = qh + (j * 8 + g) * 128, *rl = ql + (j * 8 + g) * 128;
+                            const uint4 u0 = *reinterpret_cast<const uint4 *>(rh + (((2 * c) ^ g) << 4));
+                            const uint4 u1 = *reinterpret_cast<const uint4 *>(rh + (((2 * c + 1) ^ g) << 4));
+                            const uint4 v0 = *reinterpret_cast<const uint4 *>(rl + (((2 * c) ^ g) << 4));
+                            const uint4 v1 = *reinterpret_cast<const uint4 *>(rl + (((2 * c + 1) ^ g) << 4));
+                            bq[j][0] = u0.x; bq[j][1] = u0.y; bq[j][2] = u0.z; bq[j][3] = u0.w;
+                            bq[j][4] = u1.x; bq[j][5] = u1.y; bq[j][6] = u1.z; bq[j][7] = u1.w;
+                            bl[j][0] = v0.x; bl[j][1] = v0.y; bl[j][2] = v0.z; bl[j][3] = v0.w;
+                            bl[j][4] = v1.x; bl[j][5] = v1.y; bl[j][6] = v1.z; bl[j][7] = v1.w;
+                        }
+                        // the thread's 8 code bytes of rows g and g + 8: bytes 32q + 8c of each row =
+                        // box q / 4, 16-byte chunk 2 (q % 4) + c / 2 (swizzled by row % 8 = g), half c % 2
+                        const uint8_t *box = st + (q >> 2) * 2048;
+                        const int co = ((((q & 3) << 1) | (c >> 1)) ^ g) << 4 | ((c & 1) << 3);
+                        const uint2 w0 = *reinterpret_cast<const uint2 *>(box + g * 128 + co);
+                        const uint2 w1 = *reinterpret_cast<const uint2 *>(box + (g + 8) * 128 + co);
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {
+                            const uint32_t x0 = s4 < 2 ? w0.x : w0.y, x1 = s4 < 2 ? w1.x : w1.y;
+                            const int kk = (s4 & 1) * 2;
+                            const uint2 e0 = lut8_byte(lutl, x0, kk), e2 = lut8_byte(lutl, x0, kk + 1);
+                            const uint2 e1 = lut8_byte(lutl, x1, kk), e3 = lut8_byte(lutl, x1, kk + 1);
+#pragma unroll
+                            for (int j = 0; j < NT; ++j)
+                                mma_f16(s0[j], e0.x, e1.x, e2.x, e3.x, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+#pragma unroll
+                            for (int j = 0; j < NT; ++j)
+                                mma_f16(s1[j], e0.y, e1.y, e2.y, e3.y, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+#pragma unroll
+                            for (int j = 0; j < NT; ++j)
+                                mma_f16(s2[j], e0.x, e1.x, e2.x, e3.x, bl[j][2 * s4], bl[j][2 * s4 + 1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) as::mbar_arrive(&emptyA[warp]);
 #pragma unroll
                 for (int hrow = 0; hrow < 2; ++hrow) {
-                    const int t = (mg * 4 * MT + mt) * 16 + g + hrow * 8;
+                    const int t = mt * 16 + g + hrow * 8;
                     const float f = t < nloc ? kn_s[t] * a.scale : 0.0f;
 #pragma unroll
                     for (int j = 0; j < NT; ++j)
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
-                            const int h = j * 8 + c * 2 + e;
-                            if (h < HP) Ss[h * SROW + t] = (acc[i][j][hrow * 2 + e] + acl[i][j][hrow * 2 + e]) * f;
+                            const int h = j * 8 + c * 2 + e, x = hrow * 2 + e;
+                            if (t < nloc && h < a.nh) sc[i][j][x] = (s0[j][x] + s1[j][x] + s2[j][x]) * f;
                         }
                 }
             }
         }
-    }
-    __syncwarp();
-    if (lane == 0) as::mbar_arrive(lutfree);  // the key table is no longer read
-    bar_consumers();                          // all scores in Ss
-
-    // local softmax, one warp per head
-    for (int h = warp; h < HP; h += 4) {
-        __half *ph = Ph + h * PROW, *pl = Pl + h * PROW;
-        const float *srow = Ss + h * SROW;
-        const bool live = h < a.nh && nloc > 0;
-        float mx = -INFINITY, sum = 0.0f;
-        if (live) {
-            for (int t = lane; t < nloc; t += 32) mx = fmaxf(mx, srow[t]);
+        __syncwarp();
+        if (lane == 0) as::mbar_arrive(lutfree);  // the key table is no longer read
+        // chunk-local softmax from registers: head h = 8j + 2c + e, rows over g
+        float mx[NT][2];
 #pragma unroll
-            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        }
-        for (int t = lane; t < nmt * 16; t += 32) {
-            float v = 0.0f;
-            if (live && t < nloc) {
-                const float e = expf(srow[t] - mx);
-                sum += e;
-                v = e * vn_s[t];
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float v = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < MT; ++i) v = fmaxf(v, fmaxf(sc[i][j][e], sc[i][j][2 + e]));
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+                mx[j][e] = v;
+                if (g == 0) hred[warp * HP + j * 8 + 2 * c + e] = v;
             }
-            const __half hv = __float2half_rn(v);
-            ph[t] = hv;
-            pl[t] = __float2half_rn(v - __half2float(hv));
+        bar_consumers();
+        float ls[NT][2];
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int h = j * 8 + 2 * c + e;
+                mx[j][e] = fmaxf(fmaxf(hred[h], hred[HP + h]), fmaxf(hred[2 * HP + h], hred[3 * HP + h]));
+                ls[j][e] = 0.0f;
+            }
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+            const int mt = warp + 4 * i;
+            if (mt < nmt) {
+#pragma unroll
+                for (int hrow = 0; hrow < 2; ++hrow) {
+                    const int t = mt * 16 + g + hrow * 8;
+                    const float vn = t < nloc ? vn_s[t] : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int h = j * 8 + 2 * c + e;
+                            const float sv = sc[i][j][hrow * 2 + e];
+                            const float pe = sv == -INFINITY ? 0.0f : expf(sv - mx[j][e]);
+                            ls[j][e] += pe;
+                            const float v = pe * vn;
+                            const __half hv = __float2half_rn(v);
+                            Ph[h * PROW + t] = hv;
+                            Pl[h * PROW + t] = __float2half_rn(v - __half2float(hv));
+                        }
+                }
+            }
+        }
+        if constexpr (NT * 8 < HP) {  // head rows past the MMA tiles stay zero
+            for (int x = tid; x < (HP - NT * 8) * nmt * 16; x += 128) {
+                const int h = NT * 8 + x / (nmt * 16), t = x % (nmt * 16);
+                Ph[h * PROW + t] = Pl[h * PROW + t] = __float2half_rn(0.0f);
+            }
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) {
-            mloc[h] = mx;
-            lloc[h] = sum;
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float v = ls[j][e];
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (g == 0) hred[4 * HP + warp * HP + j * 8 + 2 * c + e] = v;
+            }
+        bar_consumers();
+        if (tid < HP) {
+            const bool live = tid < a.nh && tid < NT * 8 && nloc > 0;
+            mloc[tid] = live ? fmaxf(fmaxf(hred[tid], hred[HP + tid]), fmaxf(hred[2 * HP + tid], hred[3 * HP + tid]))
+                             : -INFINITY;
+            lloc[tid] = live ? (hred[4 * HP + tid] + hred[5 * HP + tid]) + (hred[6 * HP + tid] + hred[7 * HP + tid])
+                             : 0.0f;
         }
+    } else {
+        for (int mg = 0; mg < ngroups; ++mg) {
+            const int gm = min(4 * MT, nmt - mg * 4 * MT);
+            float acc[MT][NT][4], acl[MT][NT][4];
+    #pragma unroll
+            for (int i = 0; i < MT; ++i)
+    #pragma unroll
+                for (int j = 0; j < NT; ++j)
+    #pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[i][j][e] = acl[i][j][e] = 0.0f;
+            for (int q = 0; q < nblk; ++q, ++it) {
+                const int s = it % NS;
+                const bool ok = as::mbar_wait(&full[s], (it / NS) & 1, abort_flag, a.err);
+                const uint8_t *st = ring + s * a.sstage;
+                if (ok) {
+                    uint32_t bq[NT][8], bl[NT][8];
+    #pragma unroll
+                    for (int j = 0; j < NT; ++j) {
+                        // q~ row j * 8 + g (row & 7 == g), dims 16c .. 16c + 15 = 16-byte chunks 2c, 2c + 1
+                        const uint8_t *rh = st + (j * 8 + g) * 128, *rl = st + QB + (j * 8 + g) * 128;
+                        const uint4 u0 = *reinterpret_cast<const uint4 *>(rh + (((2 * c) ^ g) << 4));
+                        const uint4 u1 = *reinterpret_cast<const uint4 *>(rh + (((2 * c + 1) ^ g) << 4));
+                        const uint4 v0 = *reinterpret_cast<const uint4 *>(rl + (((2 * c) ^ g) << 4));
+                        const uint4 v1 = *reinterpret_cast<const uint4 *>(rl + (((2 * c + 1) ^ g) << 4));
+                        bq[j][0] = u0.x; bq[j][1] = u0.y; bq[j][2] = u0.z; bq[j][3] = u0.w;
+                        bq[j][4] = u1.x; bq[j][5] = u1.y; bq[j][6] = u1.z; bq[j][7] = u1.w;
+                        bl[j][0] = v0.x; bl[j][1] = v0.y; bl[j][2] = v0.z; bl[j][3] = v0.w;
+                        bl[j][4] = v1.x; bl[j][5] = v1.y; bl[j][6] = v1.z; bl[j][7] = v1.w;
+                    }
+                    const uint8_t *kc = st + 2 * QB;
+    #pragma unroll
+                    for (int i = 0; i < MT; ++i) {
+                        const int mt = warp + 4 * i;
+                        if (mt < gm) {
+                            const uint2 w0 = *reinterpret_cast<const uint2 *>(kc + (mt * 16 + g) * 32 + c * 8);
+                            const uint2 w1 = *reinterpret_cast<const uint2 *>(kc + (mt * 16 + g + 8) * 32 + c * 8);
+    #pragma unroll
+                            for (int s4 = 0; s4 < 4; ++s4) {
+                                const uint32_t x0 = s4 < 2 ? w0.x : w0.y, x1 = s4 < 2 ? w1.x : w1.y;
+                                const int k = (s4 & 1) * 2;
+                                const uint2 e0 = lut8_byte(lutl, x0, k), e2 = lut8_byte(lutl, x0, k + 1);
+                                const uint2 e1 = lut8_byte(lutl, x1, k), e3 = lut8_byte(lutl, x1, k + 1);
+    #pragma unroll
+                                for (int j = 0; j < NT; ++j)
+                                    mma_f16(acc[i][j], e0.x, e1.x, e2.x, e3.x, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+    #pragma unroll
+                                for (int j = 0; j < NT; ++j)
+                                    mma_f16(acl[i][j], e0.y, e1.y, e2.y, e3.y, bq[j][2 * s4], bq[j][2 * s4 + 1]);
+    #pragma unroll
+                                for (int j = 0; j < NT; ++j)
+                                    mma_f16(acl[i][j], e0.x, e1.x, e2.x, e3.x, bl[j][2 * s4], bl[j][2 * s4 + 1]);
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) as::mbar_arrive(&empty[s]);
+            }
+    #pragma unroll
+            for (int i = 0; i < MT; ++i) {
+                const int mt = warp + 4 * i;
+                if (mt < gm) {
+    #pragma unroll
+                    for (int hrow = 0; hrow < 2; ++hrow) {
+                        const int t = (mg * 4 * MT + mt) * 16 + g + hrow * 8;
+                        const float f = t < nloc ? kn_s[t] * a.scale : 0.0f;
+    #pragma unroll
+                        for (int j = 0; j < NT; ++j)
+    #pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int h = j * 8 + c * 2 + e;
+                                if (h < HP) Ss[h * SROW + t] = (acc[i][j][hrow * 2 + e] + acl[i][j][hrow * 2 + e]) * f;
+                            }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) as::mbar_arrive(lutfree);  // the key table is no longer read
+        bar_consumers();                          // all scores in Ss
+
+        // local softmax, one warp per head
+        for (int h = warp; h < HP; h += 4) {
+            __half *ph = Ph + h * PROW, *pl = Pl + h * PROW;
+            const float *srow = Ss + h * SROW;
+            const bool live = h < a.nh && nloc > 0;
+            float mx = -INFINITY, sum = 0.0f;
+            if (live) {
+                for (int t = lane; t < nloc; t += 32) mx = fmaxf(mx, srow[t]);
+    #pragma unroll
+                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            }
+            for (int t = lane; t < nmt * 16; t += 32) {
+                float v = 0.0f;
+                if (live && t < nloc) {
+                    const float e = expf(srow[t] - mx);
+                    sum += e;
+                    v = e * vn_s[t];
+                }
+                const __half hv = __float2half_rn(v);
+                ph[t] = hv;
+                pl[t] = __float2half_rn(v - __half2float(hv));
+            }
+    #pragma unroll
+            for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                mloc[h] = mx;
+                lloc[h] = sum;
+            }
+        }
+
     }
     as::mbar_wait(lutfull, 1, abort_flag, a.err);  // value table in place
     bar_consumers();                               // P and m / l complete
@@ -1077,24 +1256,41 @@ cudaError_t decode_attn_nbw(DecodeAttnArgs &a, cudaStream_t s) {
     }
 }
 
-template <int NT, int NBW>
+template <int NT, int NBW, bool QRES>
 cudaError_t launch_decode_attn_tma(DecodeAttnArgs a, cudaStream_t s) {
     constexpr int MT = NT <= 2 ? 4 : 2, MTV = (NT * 8 + 15) / 16, HP = 16 * MTV;
-    constexpr int DG = 64 * 4 * NBW;
+    constexpr int DG = 64 * 4 * NBW, QB = NT * 8 * 128;
     const int NCH = ATTEND_CHUNKS_TMA;
     a.nbg = DG / 64;
     a.ndg = a.kvd / DG;
     a.chmax = ((a.B + NCH - 1) / NCH + 15) / 16 * 16;
-    const int stage_a = 2 * NT * 8 * 128 + 4 * MT * 16 * 32, stage_c = (DG / 256) * 2048;
-    a.sstage = (std::max(stage_a, stage_c) + 1023) / 1024 * 1024;
-    const int part = HP * (DG + 4) * 4;
+    const int nblk = a.kvd / 64;
+    const int stage_c = (DG / 256) * 2048;
+    int ring, end;
     a.off_ring = LUT8_ENTRIES * (int)sizeof(uint2);
-    a.off_S = align16(a.off_ring + NS * a.sstage);
-    a.off_P = align16(a.off_S + HP * (a.chmax + 4) * 4);
+    if (QRES) {
+        // lut | q~ (all blocks) | ring (one key tile slot per warp / value stages) | P | small
+        a.off_q = a.off_ring;
+        a.sstage_a = (a.kpl / 128) * 2048;
+        a.sstage = stage_c;
+        a.off_ring = a.off_q + 2 * nblk * QB;
+        ring = std::max(4 * a.sstage_a, NS * a.sstage);
+        a.off_S = a.off_ring + ring;  // no score buffer: scores stay in registers
+        a.off_P = align16(a.off_S);
+    } else {
+        const int stage_a = 2 * QB + 4 * MT * 16 * 32;
+        a.off_q = 0;
+        a.sstage_a = 0;
+        a.sstage = (std::max(stage_a, stage_c) + 1023) / 1024 * 1024;
+        ring = NS * a.sstage;
+        a.off_S = align16(a.off_ring + ring);
+        a.off_P = align16(a.off_S + HP * (a.chmax + 4) * 4);
+    }
     a.off_small = align16(a.off_P + 2 * HP * (a.chmax + 8) * 2);
-    int end = align16(a.off_small + (2 * HP + NCH * HP + 2 * a.chmax) * 4 + (2 * NS + 2) * 8 + 16);
-    if (a.ndg == 1 && part <= a.off_S) {
-        a.off_part = 0;
+    end = align16(a.off_small + (2 * HP + NCH * HP + 2 * a.chmax + 8 * HP) * 4 + (2 * NS + 2 + 9) * 8 + 16);
+    const int part = HP * (DG + 4) * 4;
+    if (a.ndg == 1 && part <= a.off_ring) {
+        a.off_part = 0;  // the partial tile overlays the table (and q~) once they are dead
     } else {
         a.off_part = end;
         end = align16(end + part);
@@ -1103,7 +1299,7 @@ cudaError_t launch_decode_attn_tma(DecodeAttnArgs a, cudaStream_t s) {
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     static int attr = 0;
     if (smem > attr) {
-        cudaError_t e = cudaFuncSetAttribute(decode_attn_tma_kernel<NT, MT, MTV, NBW>,
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_tma_kernel<NT, MT, MTV, NBW, QRES>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attr = smem;
@@ -1120,18 +1316,28 @@ cudaError_t launch_decode_attn_tma(DecodeAttnArgs a, cudaStream_t s) {
     at[0].val.clusterDim.z = 1;
     lc.attrs = at;
     lc.numAttrs = 1;
-    return cudaLaunchKernelEx(&lc, decode_attn_tma_kernel<NT, MT, MTV, NBW>, *a.maps, a);
+    return cudaLaunchKernelEx(&lc, decode_attn_tma_kernel<NT, MT, MTV, NBW, QRES>, *a.maps, a);
 }
 
-template <int NT>
+template <int NT, bool QRES>
 cudaError_t decode_attn_tma_nbw(const DecodeAttnArgs &a, cudaStream_t s) {
     // dim groups of 256 * NBW dims (NBW <= 2 with two head tiles)
     const int n256 = a.kvd / 256;
     if constexpr (NT <= 2) {
-        if (n256 % 3 == 0) return launch_decode_attn_tma<NT, 3>(a, s);
+        if (n256 % 3 == 0) return launch_decode_attn_tma<NT, 3, QRES>(a, s);
     }
-    if (n256 % 2 == 0) return launch_decode_attn_tma<NT, 2>(a, s);
-    return launch_decode_attn_tma<NT, 1>(a, s);
+    if (n256 % 2 == 0) return launch_decode_attn_tma<NT, 2, QRES>(a, s);
+    return launch_decode_attn_tma<NT, 1, QRES>(a, s);
+}
+
+template <int NT>
+cudaError_t decode_attn_tma_q(const DecodeAttnArgs &a, cudaStream_t s) {
+    // q~ resident in shared memory when all its blocks fit in 48 KB and a
+    // warp's m-tiles cover the longest chunk
+    constexpr int MT = NT <= 2 ? 4 : 2;
+    const int chmax = ((a.B + ATTEND_CHUNKS_TMA - 1) / ATTEND_CHUNKS_TMA + 15) / 16 * 16;
+    if ((a.kvd / 64) * 2 * NT * 8 * 128 <= 48 * 1024 && chmax <= 64 * MT) return decode_attn_tma_nbw<NT, true>(a, s);
+    return decode_attn_tma_nbw<NT, false>(a, s);
 }
 
 cudaError_t decode_attn(const DecodeAttnArgs &a0, cudaStream_t s) {
@@ -1140,9 +1346,9 @@ cudaError_t decode_attn(const DecodeAttnArgs &a0, cudaStream_t s) {
     if (a.kvd % 64 || a.nh < 1 || a.nh > 32) return cudaErrorInvalidValue;
     if (a.maps && a.lutk && a.lutv && a.kvd % 256 == 0) {
         const int nt = (a.nh + 7) / 8;
-        if (nt == 1) return decode_attn_tma_nbw<1>(a, s);
-        if (nt == 2) return decode_attn_tma_nbw<2>(a, s);
-        return decode_attn_tma_nbw<4>(a, s);
+        if (nt == 1) return decode_attn_tma_q<1>(a, s);
+        if (nt == 2) return decode_attn_tma_q<2>(a, s);
+        return decode_attn_tma_q<4>(a, s);
     }
     // 64-dim blocks per dim group: the largest divisor of kv_dim / 64 up to 12
     // (up to 8 with two head tiles, whose accumulators take twice the registers)
@@ -1200,6 +1406,7 @@ bool decode_attn_maps(AttnMaps *maps, const uint8_t *kcodes, const uint8_t *vcod
     const int nt = (nh + 7) / 8 <= 2 ? (nh + 7) / 8 : 4;
     const int rows_a = 4 * (nt <= 2 ? 4 : 2) * 16;
     return make_tensor_map(&maps->kc, kcodes, rows, kpl, kpl, 1, 32, rows_a, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           make_tensor_map(&maps->kt, kcodes, rows, kpl, kpl, 1, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) &&
            make_tensor_map(&maps->vc, vcodes, rows, vpl, vpl, 1, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) &&
            make_tensor_map(&maps->qh, qrot, qrows, kvd, kvd, 2, 64, nt * 8, CU_TENSOR_MAP_SWIZZLE_128B) &&
            make_tensor_map(&maps->ql, qrot_lo, qrows, kvd, kvd, 2, 64, nt * 8, CU_TENSOR_MAP_SWIZZLE_128B);

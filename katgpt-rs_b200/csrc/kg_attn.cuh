@@ -19,7 +19,7 @@ namespace attn {
 // per context: key / value code arenas as [rows x pl] bytes, q~ hi / lo as
 // [tokens * heads x kv_dim] f16.
 struct AttnMaps {
-    CUtensorMap kc, vc, qh, ql;
+    CUtensorMap kc, kt, vc, qh, ql;  // key codes as 32-byte columns and as 16-row tiles
 };
 bool decode_attn_maps(AttnMaps *maps, const uint8_t *kcodes, const uint8_t *vcodes, int64_t rows, int kpl, int vpl,
                       const __half *qrot, const __half *qrot_lo, int64_t qrows, int kvd, int nh);
@@ -40,6 +40,7 @@ struct DecodeAttnArgs {
     int *err;                         // device error word (timeouts)
     // set by the launcher
     int nbg, ndg, chmax, sstage, vrow, vstage, off_ring, off_S, off_P, off_small, off_part;
+    int off_q, sstage_a;              // resident-q~ variant: q~ region, per-warp key tile slot
 };
 struct FlashArgs {
     const __half *Q, *Q_lo, *K, *K_lo, *V, *V_lo;  // rows = tokens (sequence-major, T per sequence)

@@ -144,6 +144,7 @@ struct kg_ctx {
     void *stage = nullptr;
     size_t stage_bytes = 0;
     std::vector<void *> allocs;
+    std::vector<uint8_t> slot_used;  // kg_seq_alloc / kg_seq_free bookkeeping
 };
 
 namespace kg {

@@ -87,6 +87,11 @@ def lib():
             "kg_profile": (ctypes.c_int, [P, ctypes.c_int]),
             "kg_profile_read": (ctypes.c_int, [P, P, P]),
             "kg_graph_kernels": (I64, [P]),
+            "kg_seq_alloc": (ctypes.c_int, [P, P]),
+            "kg_seq_free": (ctypes.c_int, [P, I32]),
+            "kg_kv_snapshot_bytes": (I64, [P, I32]),
+            "kg_kv_snapshot": (ctypes.c_int, [P, I32, I32, P, P]),
+            "kg_kv_restore": (ctypes.c_int, [P, I32, I32, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -253,6 +258,25 @@ class CudaBackend:
         cnt = np.zeros(3, np.int64)
         self._check(lib().kg_profile_read(self._h, _ptr(ms), _ptr(cnt)))
         return ms, cnt
+
+    def seq_alloc(self):
+        """A free sequence slot (reset), as kg_seq_alloc."""
+        out = ctypes.c_int32(-1)
+        self._check(lib().kg_seq_alloc(self._h, ctypes.byref(out)))
+        return out.value
+
+    def seq_free(self, seq):
+        self._check(lib().kg_seq_free(self._h, seq))
+
+    def kv_snapshot_bytes(self, pos):
+        return int(lib().kg_kv_snapshot_bytes(self._h, pos))
+
+    def kv_snapshot(self, seq, pos, dst_dev, stream=None):
+        """Copy positions [0, pos) of `seq` into device memory at dst_dev (int address)."""
+        self._check(lib().kg_kv_snapshot(self._h, seq, pos, ctypes.c_void_p(dst_dev), stream))
+
+    def kv_restore(self, seq, pos, src_dev, stream=None):
+        self._check(lib().kg_kv_restore(self._h, seq, pos, ctypes.c_void_p(src_dev), stream))
 
     def graph_kernels(self):
         """Kernel launches replayed by the last forward call's CUDA graph (0: eager)."""
