@@ -13,6 +13,7 @@
 #include <string>
 #include <vector>
 
+#include "kg_bf16.cuh"
 #include "kg_internal.h"
 
 namespace kg {
@@ -619,11 +620,44 @@ int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint
     // codes of a zero-norm vector are left untouched: start from the caller's bytes
     KG_CUDA(ctx, cudaMemcpyAsync(dp, packed, n_vec * pl, cudaMemcpyHostToDevice, s));
     const float *bnd = which == 0 ? ctx->kb : ctx->vb;
-    if (kvd % 128 == 0 && (bits == 3 || bits == 4))
-        KG_CUDA(ctx, kg::tq_encode_tiled((int)kvd, bits, n_vec, dx, kvd, ctx->rot, bnd, dp, pl, dn, nullptr,
-                                         nullptr, 0, 0, 0, dxn, dskip, s));
-    else
+    if (kvd % 64 == 0 && (bits == 3 || bits == 4)) {
+        // tensor-core rotation with exact fix-up (the encoder of the forward path)
+        if (!ctx->big_path && !ctx->enc_rh) {
+            if ((rc = dalloc(ctx, &ctx->enc_rh, kvd * kvd)) || (rc = dalloc(ctx, &ctx->enc_rl, kvd * kvd))) return rc;
+            KG_CUDA(ctx, kg::bf::f32_to_f16_split(ctx->rot, kvd * kvd, ctx->enc_rh, ctx->enc_rl, s));
+        }
+        const size_t bh = align256(n_vec * kvd * 2);
+        rc = ensure_stage(ctx, 2 * bx + bp + bn + bs + 2 * bh + bx);
+        if (rc) return rc;
+        st = static_cast<char *>(ctx->stage);  // (re)allocated: recompute the carve-up
+        dx = reinterpret_cast<float *>(st);
+        dp = reinterpret_cast<uint8_t *>(st + bx);
+        dn = reinterpret_cast<float *>(st + bx + bp);
+        dxn = reinterpret_cast<float *>(st + bx + bp + bn);
+        dskip = reinterpret_cast<uint8_t *>(st + 2 * bx + bp + bn);
+        __half *dxh = reinterpret_cast<__half *>(st + 2 * bx + bp + bn + bs);
+        __half *dxl = reinterpret_cast<__half *>(st + 2 * bx + bp + bn + bs + bh);
+        float *dy = reinterpret_cast<float *>(st + 2 * bx + bp + bn + bs + 2 * bh);
+        KG_CUDA(ctx, cudaMemcpyAsync(dx, x, n_vec * kvd * 4, cudaMemcpyHostToDevice, s));
+        KG_CUDA(ctx, cudaMemcpyAsync(dp, packed, n_vec * pl, cudaMemcpyHostToDevice, s));
+        const int mk = which == 0 ? (int)n_vec : 0, mv = which == 1 ? (int)n_vec : 0;
+        KG_CUDA(ctx, kg::tq_norm_split((int)kvd, mk, mv, dx, kvd, 0, 0, dxn, dxh, dxl, dskip, dn, dn, nullptr, nullptr,
+                                       0, 0, 0, s));
+        kg::bf::Gemm g;
+        std::memset(&g, 0, sizeof(g));
+        g.dtype = kg::bf::DT_F16;
+        g.A = dxh; g.A2 = dxl; g.lda = kvd;
+        g.B = ctx->big_path ? ctx->big.rot_h : ctx->enc_rh;
+        g.B2 = ctx->big_path ? ctx->big.rot_l : ctx->enc_rl;
+        g.ldb = kvd;
+        g.M = (int)n_vec; g.N = (int)kvd; g.K = (int)kvd; g.batch = 1;
+        g.epi = kg::bf::EPI_F32; g.C = dy; g.ldc = kvd;
+        KG_CUDA(ctx, kg::gemm_auto(ctx, &g, s));
+        KG_CUDA(ctx, kg::tq_quantize_fixup((int)kvd, mk, mv, dy, dxn, dskip, ctx->rot, bnd, bnd, bits, bits, dp, dp,
+                                           pl, pl, nullptr, nullptr, 0, 0, 0, nullptr, s));
+    } else {
         KG_CUDA(ctx, kg::tq_encode_device((int)kvd, bits, n_vec, dx, ctx->rot, bnd, dp, pl, dn, 1, s));
+    }
     KG_CUDA(ctx, cudaMemcpyAsync(packed, dp, n_vec * pl, cudaMemcpyDeviceToHost, s));
     KG_CUDA(ctx, cudaMemcpyAsync(norms, dn, n_vec * 4, cudaMemcpyDeviceToHost, s));
     KG_CUDA(ctx, cudaStreamSynchronize(s));

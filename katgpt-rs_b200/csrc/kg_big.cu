@@ -153,8 +153,11 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.vt, W * kvd, own));
     BIG_TRY(dalloc(&g.vt2, W * kvd, own));
     BIG_TRY(dalloc(&g.nrm, W, own));
-    BIG_TRY(dalloc(&g.xn, W * kvd, own));
-    BIG_TRY(dalloc(&g.skip, W, own));
+    BIG_TRY(dalloc(&g.xn, 2 * W * kvd, own));
+    BIG_TRY(dalloc(&g.skip, 2 * W, own));
+    BIG_TRY(dalloc(&g.xnh, 2 * W * kvd, own));
+    BIG_TRY(dalloc(&g.xnl, 2 * W * kvd, own));
+    BIG_TRY(dalloc(&g.yrot, 2 * W * kvd, own));
     // decode attention scratch (max_seqs rows)
     BIG_TRY(dalloc(&g.qrot, S * ctx->nh * kvd, own));
     BIG_TRY(dalloc(&g.qrot2, S * ctx->nh * kvd, own));
@@ -318,7 +321,22 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // TurboQuant encode of K and V into the arena (exact reference order)
         prof_mark(ctx, KG_PROF_ENCODE, 0, s);
-        if (kvd % 128 == 0) {
+        if (M >= 256) {
+            // prefill-sized: K and V rows together, exact norms and xn, rotation
+            // on the tensor cores, codes with exact recomputation next to the
+            // boundaries
+            BIG_TRY(tq_norm_split(kvd, M, M, g.qkv, nqkv, n, n + kvd, g.xn, g.xnh, g.xnl, g.skip, g.knorm, g.vnorm,
+                                  g.slot_of, g.pos_of, L, B, l, s));
+            bf::Gemm rg = gemm0();
+            rg.dtype = bf::DT_F16;
+            rg.A = g.xnh; rg.A2 = g.xnl; rg.lda = kvd; rg.B = g.rot_h; rg.B2 = g.rot_l; rg.ldb = kvd;
+            rg.M = 2 * M; rg.N = kvd; rg.K = kvd;
+            rg.epi = bf::EPI_F32; rg.C = g.yrot; rg.ldc = kvd;
+            BIG_TRY(gemm_split(ctx, rg, s));
+            BIG_TRY(tq_quantize_fixup(kvd, M, M, g.yrot, g.xn, g.skip, ctx->rot, ctx->kb, ctx->vb, c.key_bits,
+                                      c.val_bits, g.kcodes, g.vcodes, ctx->kpl, ctx->vpl, g.slot_of, g.pos_of, L, B,
+                                      l, nullptr, s));
+        } else if (kvd % 128 == 0) {  // decode-sized: the exact tiled encoder is faster
             BIG_TRY(tq_encode_tiled(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
                                     g.knorm, g.slot_of, g.pos_of, L, B, l, g.xn, g.skip, s));
             BIG_TRY(tq_encode_tiled(kvd, c.val_bits, M, g.qkv + n + kvd, nqkv, ctx->rot, ctx->vb, g.vcodes,
@@ -465,6 +483,10 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
                         probs ? probs + (int64_t)i0 * T * V : nullptr, s));
     }
     return cudaGetLastError();
+}
+
+cudaError_t gemm_auto(kg_ctx *ctx, const void *gemm_args, cudaStream_t s) {
+    return gemm_split(ctx, *static_cast<const bf::Gemm *>(gemm_args), s);
 }
 
 }  // namespace kg

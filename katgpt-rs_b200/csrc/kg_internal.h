@@ -60,6 +60,20 @@ cudaError_t tq_encode_tiled(int dim, int bits, int64_t n_vec, const float *x, in
                             const int32_t *slot, const int32_t *pos, int L, int B, int layer, float *xn_scratch,
                             uint8_t *skip_scratch, cudaStream_t s);
 // Same, reading row v at x + v*ldx and writing arena row (slot[v]*L + layer)*B + pos[v].
+// Tensor-core encoder with exact fix-up (kg_tq.cu): norms + xn + f16 split of
+// the K and V rows of qkv (2M vectors), then after the caller's rotation GEMM
+// Y = xn R^T, codes from Y with exact recomputation near boundaries.
+float tq_fixup_eps(int dim);
+// Vectors v < Mk are K rows (x + t * ldx + koff), the next Mv are V rows.
+cudaError_t tq_norm_split(int dim, int Mk, int Mv, const float *qkv, int64_t ldx, int64_t koff, int64_t voff,
+                          float *xn, __half *xh, __half *xl, uint8_t *skip, float *knorm, float *vnorm,
+                          const int32_t *slot, const int32_t *pos, int L, int B, int layer, cudaStream_t s);
+cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
+                              const float *rot, const float *kb, const float *vb, int kbits, int vbits,
+                              uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl, const int32_t *slot,
+                              const int32_t *pos, int L, int B, int layer, int *nfix, cudaStream_t s);
+// the rotation GEMM of the fast encoder (tcgen05 or mma.sync by size)
+cudaError_t gemm_auto(kg_ctx *ctx, const void *gemm_args, cudaStream_t s);
 cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,
                               const float *bnd, uint8_t *packed, int64_t pstride, float *norms, int64_t nstride,
                               const int32_t *slot, const int32_t *pos, int L, int B, int layer, cudaStream_t s);
@@ -83,8 +97,10 @@ struct BigState {
     __nv_bfloat16 *xb = nullptr, *xb2 = nullptr, *attb = nullptr, *attb2 = nullptr, *hid = nullptr, *hid2 = nullptr;
     __half *qh = nullptr, *ql = nullptr, *cent = nullptr, *cent2 = nullptr, *kt = nullptr, *kt2 = nullptr,
            *vt = nullptr, *vt2 = nullptr, *qrot = nullptr, *qrot2 = nullptr, *U = nullptr, *U2 = nullptr;
-    float *xn = nullptr;  // normalised K/V rows for the tiled encoder
+    float *xn = nullptr;  // normalised K and V rows of a step [2 * ws_tokens][kv_dim]
     uint8_t *skip = nullptr;
+    __half *xnh = nullptr, *xnl = nullptr;  // their f16 hi / lo split (rotation GEMM operand)
+    float *yrot = nullptr;                  // rotated rows from the GEMM, before the fix-up
     int *alive = nullptr;
     int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;
     // TMA decode attention: tensor maps over the code arenas and q~, and the
@@ -145,6 +161,7 @@ struct kg_ctx {
     size_t stage_bytes = 0;
     std::vector<void *> allocs;
     std::vector<uint8_t> slot_used;  // kg_seq_alloc / kg_seq_free bookkeeping
+    __half *enc_rh = nullptr, *enc_rl = nullptr;  // f16 hi / lo of R for kg_tq_encode (codec contexts)
 };
 
 namespace kg {

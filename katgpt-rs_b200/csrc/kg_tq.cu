@@ -335,6 +335,133 @@ __global__ void __launch_bounds__(256) rotate_kernel(int dim, int bits, int64_t 
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core encoder with exact fix-up (bit-identical codes).
+//
+// The reference code of coordinate j is count(y_j >= b) over the sorted
+// boundaries b, with y_j = simd_dot(R[j, :], xn) in the AVX2 order. A
+// split-precision GEMM (xn and R as f16 hi + lo, three products, f32
+// accumulation) gives y'_j with |y'_j - y_j| <= eps, eps bounding both
+// roundings (the reference dot's and the tensor core's) for a unit vector
+// against a unit row: whenever every boundary is farther than eps from
+// y'_j, y'_j yields the reference code. The few coordinates closer than eps
+// are recomputed exactly (warp_dot, the same order as the exact encoder).
+// K and V rows of a step go through one norm launch, one GEMM and one
+// quantize launch: vector v < Mk is a K row, the rest V rows.
+
+// Per vector: norm (exact order) to the arena, xn = x * (1 / norm), and its
+// f16 hi / lo split (row v of xh / xl, zero for vectors the reference skips).
+__global__ void norm_split_kernel(int dim, int Mk, int Mv, const float *qkv, int64_t ldx, int64_t koff,
+                                  int64_t voff, float *xn, __half *xh, __half *xl, uint8_t *skip, float *knorm,
+                                  float *vnorm, const int32_t *slot, const int32_t *pos, int L, int B, int layer) {
+    const int lane = threadIdx.x & 31;
+    const int v = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (v >= Mk + Mv) return;
+    const int M = Mk;
+    const int t = v < M ? v : v - M;
+    const float *xv = qkv + (int64_t)t * ldx + (v < M ? koff : voff);
+    const float norm = sqrtf(warp_sum_sq(xv, dim, 1));
+    const int64_t drow = slot ? ((int64_t)slot[t] * L + layer) * B + pos[t] : t;
+    if (lane == 0) {
+        (v < M ? knorm : vnorm)[drow] = norm;
+        skip[v] = norm < 1e-8f ? 1 : 0;
+    }
+    const float inv = norm < 1e-8f ? 0.0f : 1.0f / norm;
+    for (int k = lane; k < dim; k += 32) {
+        const float y = xv[k] * inv;
+        xn[(int64_t)v * dim + k] = y;
+        const __half h = __float2half_rn(y);
+        xh[(int64_t)v * dim + k] = h;
+        xl[(int64_t)v * dim + k] = __float2half_rn(y - __half2float(h));
+    }
+}
+
+// One warp per vector: codes from y' where no boundary is within eps, exact
+// recomputation elsewhere, then 4-bit packing (two codes per byte, low first).
+__global__ void quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
+                                      const float *rot, const float *kb, const float *vb, int kbits, int vbits,
+                                      uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl,
+                                      const int32_t *slot, const int32_t *pos, int L, int B, int layer, float eps,
+                                      int *nfix) {
+    extern __shared__ uint8_t qsm[];
+    __shared__ float bnd[2][15];
+    const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (threadIdx.x < 15) {
+        bnd[0][threadIdx.x] = threadIdx.x < (1 << kbits) - 1 ? kb[threadIdx.x] : INFINITY;
+        bnd[1][threadIdx.x] = threadIdx.x < (1 << vbits) - 1 ? vb[threadIdx.x] : INFINITY;
+    }
+    __syncthreads();
+    const int v = blockIdx.x * warps + w;
+    if (v >= Mk + Mv || skip[v]) return;  // skipped vectors keep their codes (reference quirk)
+    uint8_t *cd = qsm + (size_t)w * dim;
+    const int which = v < Mk ? 0 : 1, t = which ? v - Mk : v;
+    const int nb = (1 << (which ? vbits : kbits)) - 1;
+    const float *b = bnd[which];
+    const float *yv = Y + (int64_t)v * dim;
+    int fixes = 0;
+    for (int j0 = 0; j0 < dim; j0 += 32) {
+        const int j = j0 + lane;
+        bool near = false;
+        if (j < dim) {
+            const float y = yv[j];
+            int c = 0;
+            for (int k = 0; k < nb; ++k) {
+                c += y >= b[k] ? 1 : 0;
+                near |= fabsf(y - b[k]) <= eps;
+            }
+            cd[j] = (uint8_t)c;
+        }
+        unsigned m = __ballot_sync(0xffffffffu, near);
+        while (m) {  // exact recomputation, one coordinate at a time by the whole warp
+            const int l = __ffs(m) - 1;
+            m &= m - 1;
+            const int jj = j0 + l;
+            const float r = warp_dot(rot + (int64_t)jj * dim, xn + (int64_t)v * dim, dim);
+            if (lane == 0) {
+                int c = 0;
+                for (int k = 0; k < nb; ++k) c += r >= b[k] ? 1 : 0;
+                cd[jj] = (uint8_t)c;
+            }
+            ++fixes;
+        }
+    }
+    __syncwarp();
+    const int64_t drow = slot ? ((int64_t)slot[t] * L + layer) * B + pos[t] : t;
+    uint8_t *out = (which ? vcodes : kcodes) + drow * (which ? vpl : kpl);
+    for (int k = lane; k < dim / 2; k += 32) out[k] = (uint8_t)((cd[2 * k] & 15) | ((cd[2 * k + 1] & 15) << 4));
+    if (nfix && lane == 0 && fixes) atomicAdd(nfix, fixes);
+}
+
+}  // namespace
+
+// Bound on |y' - y| for the fix-up: both roundings of a dim-term dot of a unit
+// vector with a unit row (the AVX2 order's ~dim/32 + 8 roundings and the
+// tensor core's per-k-step accumulation), with a 4x margin.
+float tq_fixup_eps(int dim) { return 4.0f * (16.0f + (float)dim / 16.0f) * 5.96e-8f; }
+
+cudaError_t tq_norm_split(int dim, int Mk, int Mv, const float *qkv, int64_t ldx, int64_t koff, int64_t voff,
+                          float *xn, __half *xh, __half *xl, uint8_t *skip, float *knorm, float *vnorm,
+                          const int32_t *slot, const int32_t *pos, int L, int B, int layer, cudaStream_t s) {
+    if (Mk + Mv <= 0) return cudaSuccess;
+    norm_split_kernel<<<(Mk + Mv + 7) / 8, 256, 0, s>>>(dim, Mk, Mv, qkv, ldx, koff, voff, xn, xh, xl, skip, knorm,
+                                                        vnorm, slot, pos, L, B, layer);
+    return cudaGetLastError();
+}
+
+cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
+                              const float *rot, const float *kb, const float *vb, int kbits, int vbits,
+                              uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl, const int32_t *slot,
+                              const int32_t *pos, int L, int B, int layer, int *nfix, cudaStream_t s) {
+    if (Mk + Mv <= 0) return cudaSuccess;
+    if (dim % 2 || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
+    const int warps = 8;
+    quantize_fixup_kernel<<<(Mk + Mv + warps - 1) / warps, warps * 32, (size_t)warps * dim, s>>>(
+        dim, Mk, Mv, Y, xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl, vpl, slot, pos, L, B, layer,
+        tq_fixup_eps(dim), nfix);
+    return cudaGetLastError();
+}
+
+namespace {
 }  // namespace
 
 cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t, float *work,

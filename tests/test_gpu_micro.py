@@ -217,3 +217,34 @@ def test_uncompiled_and_unsupported(kg):
         be2.compile(kg.reference_weights(big, 42))
     assert e.value.status == -6
     be2.close()
+
+
+@pytest.mark.parametrize("kvd,bits", [(768, 4), (1024, 3)])
+def test_encoder_near_boundaries(kg, orc, kvd, bits):
+    # rotated coordinates placed on (and within a few ulps of) the codebook
+    # boundaries: the tensor-core rotation cannot decide these, the exact
+    # recomputation must, and every code must match the reference encoder
+    nh = kvd // 64
+    cfg = kg.micro_config(kv_mode=kg.KG_KV_TQ, n_embd=kvd, n_head=nh, head_dim=64, n_kv_head=nh,
+                          key_bits=bits, val_bits=bits, mlp_hidden=4 * kvd, vocab_size=64)
+    be = kg.CudaBackend(cfg)
+    rot, kc, kb, vc, vb = be.tq_tables()
+    rng = np.random.default_rng(kvd * bits)
+    n = 48
+    ys = []
+    for i in range(n):
+        y = rng.standard_normal(kvd) / np.sqrt(kvd)
+        idx = rng.choice(kvd, size=48, replace=False)
+        y[idx] = kb[rng.integers(0, len(kb), size=48)].astype(np.float64) * (1.0 + rng.choice([0, 1e-7, -1e-7, 3e-7, -3e-7], size=48))
+        rest = np.setdiff1d(np.arange(kvd), idx)
+        y[rest] *= np.sqrt(max(1e-6, 1.0 - np.sum(y[idx] ** 2)) / np.sum(y[rest] ** 2))
+        ys.append(y)
+    x = (np.stack(ys) @ rot.astype(np.float64)).astype(np.float32) * 3.0  # x = R^T y (rows), any norm
+    for which, bnd in ((0, kb), (1, vb)):
+        init = np.zeros((n, orc.packed_len(kvd, bits)), np.uint8)
+        packed, norms = be.tq_encode(x, which=which, packed_init=init)
+        for i in range(n):
+            pk, nr = orc.tq_store(rot, bnd, bits, x[i], packed_init=init[i])
+            assert norms[i] == nr, i
+            np.testing.assert_array_equal(packed[i], pk, err_msg=f"which {which} vector {i}")
+    be.close()
