@@ -25,6 +25,7 @@
 
 #include "kg_async.cuh"
 #include "kg_attn.cuh"
+#include "kg_pdl.cuh"
 
 namespace kg {
 namespace attn {
@@ -137,6 +138,7 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 constexpr int SSTG = 3, VSTG = 4;
 template <int NT, int MT, int MTV, int NBW>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeAttnArgs a) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char dsm[];
     constexpr int HP = 16 * MTV, QROW = 72;
     const int NCH = gridDim.x, chmax = a.chmax, nbg = a.nbg, DG = 64 * nbg;
@@ -472,6 +474,7 @@ __device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, 128;
 template <int NT, int MT, int MTV, int NBW, bool QRES>
 __global__ void __launch_bounds__(160, 2) decode_attn_tma_kernel(const __grid_constant__ AttnMaps maps,
                                                               const DecodeAttnArgs a) {
+    pdl_wait();
     extern __shared__ __align__(1024) uint8_t dsm_raw[];
     // 1024-byte alignment for the swizzled tiles, by offsetting the shared
     // array itself (keeps every derived pointer in the shared address space)
@@ -1017,6 +1020,7 @@ __global__ void build_luts_kernel(const float *kcent, const float *vcent, uint2 
 __global__ void centroids_kernel(const uint8_t *codes, int pl, int64_t row_stride_codes, const int32_t *slot,
                                  const int32_t *pos, int L, int B, int layer, const float *cent, int kvd, int M,
                                  __half *out, __half *out_lo) {
+    pdl_wait();
     __shared__ uint2 lut[256];
     build_lut(lut, cent);
     __syncthreads();
@@ -1034,6 +1038,7 @@ __global__ void centroids_kernel(const uint8_t *codes, int pl, int64_t row_strid
 }
 __global__ void gather_norms_kernel(const float *norms, const int32_t *slot, const int32_t *pos, int L, int B,
                                     int layer, int M, float *out) {
+    pdl_wait();
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= M) return;
     out[m] = norms[((int64_t)slot[m] * L + layer) * B + pos[m]];
@@ -1044,6 +1049,7 @@ __global__ void gather_norms_kernel(const float *norms, const int32_t *slot, con
 // online softmax is f32, output f32. CTA = 64 queries x one head, 4 warps x 16.
 template <int HD>
 __global__ void __launch_bounds__(128) fa_kernel(const FlashArgs a) {
+    pdl_wait();
     constexpr int KT = 64, LD = HD + 8;
     extern __shared__ __align__(16) __half fsm[];
     __half *sKh = fsm, *sKl = fsm + KT * LD, *sVh = fsm + 2 * KT * LD, *sVl = fsm + 3 * KT * LD;
@@ -1236,13 +1242,15 @@ cudaError_t launch_decode_attn(DecodeAttnArgs a, cudaStream_t s) {
     lc.blockDim = dim3(128);
     lc.dynamicSmemBytes = smem;
     lc.stream = s;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = NCH;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = at;
-    lc.numAttrs = 1;
+    lc.numAttrs = 2;
     return cudaLaunchKernelEx(&lc, decode_attn_kernel<NT, MT, MTV, NBW>, a);
 }
 
@@ -1309,13 +1317,15 @@ cudaError_t launch_decode_attn_tma(DecodeAttnArgs a, cudaStream_t s) {
     lc.blockDim = dim3(160);
     lc.dynamicSmemBytes = smem;
     lc.stream = s;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = NCH;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = at;
-    lc.numAttrs = 1;
+    lc.numAttrs = 2;
     return cudaLaunchKernelEx(&lc, decode_attn_tma_kernel<NT, MT, MTV, NBW, QRES>, *a.maps, a);
 }
 

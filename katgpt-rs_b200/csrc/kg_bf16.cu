@@ -12,6 +12,7 @@
 #include <cooperative_groups.h>
 
 #include "kg_bf16.cuh"
+#include "kg_pdl.cuh"
 
 namespace kg {
 namespace bf {
@@ -77,9 +78,12 @@ template <typename T>
 __device__ __forceinline__ int epi_store(const Gemm &g, int z, int row, int cc, float v, float rs) {
     switch (g.epi) {
         case EPI_F32: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v; return 0;
-        case EPI_F32_RESID:
-            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
+        case EPI_F32_RESID: {
+            const float o = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
+            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = o;
+            if (g.C2) g.C2[z * g.sC + (int64_t)row * g.ldc + cc] = o;
             return 0;
+        }
         case EPI_F32_ROWSCALE: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v * rs; return 0;
         default: {
             int alive = 0;
@@ -116,6 +120,7 @@ constexpr int gemm_smem() {
 
 template <typename CF, typename T, bool SA, bool SB>
 __global__ void __launch_bounds__(CF::THREADS) gemm_kernel(const Gemm g) {
+    pdl_wait();
     constexpr int BM_ = CF::BM, BN_ = CF::BN, NT_ = CF::THREADS, MI = CF::MI, NJ = CF::NJ;
     extern __shared__ uint4 sm[];
     constexpr int TA = BM_ * 4, TB = BN_ * 4;  // 16-byte chunks per tile
@@ -301,12 +306,15 @@ __global__ void __launch_bounds__(CF::THREADS) gemm_kernel(const Gemm g) {
 // ---- small kernels ---------------------------------------------------------
 
 __global__ void embed_kernel(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n,
-                             int M, float *x) {
+                             int M, float *x, float *zero_rows) {
+    pdl_wait();
     const int m = blockIdx.x;
     if (m >= M) return;
     const bf16 *a = wte + (int64_t)tok[m] * n, *b = wpe + (int64_t)pos[m] * n;
-    for (int j = threadIdx.x; j < n; j += blockDim.x)
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
         x[(int64_t)m * n + j] = __bfloat162float(a[j]) + __bfloat162float(b[j]);
+        if (zero_rows) zero_rows[(int64_t)m * n + j] = 0.0f;
+    }
 }
 
 __device__ __forceinline__ float block_sum(float v, float *red) {
@@ -336,9 +344,12 @@ __device__ __forceinline__ void put_split(bf16 *yb, bf16 *yb2, int64_t i, float 
     if (yb2) yb2[i] = __float2bfloat16_rn(v - __bfloat162float(hi));
 }
 
-__global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, int twice) {
+__global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, int twice,
+                               int *zero_count) {
+    pdl_wait();
     __shared__ float red[32];
     const int m = blockIdx.x;
+    if (zero_count && threadIdx.x == 0) zero_count[m] = 0;
     const float *xr = x + (int64_t)m * n;
     float ss = 0.0f;
     for (int j = threadIdx.x; j < n; j += blockDim.x) ss += xr[j] * xr[j];
@@ -368,11 +379,13 @@ __global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb
 }
 
 __global__ void to_bf16_kernel(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy) {
+    pdl_wait();
     const int m = blockIdx.x;
     for (int j = threadIdx.x; j < n; j += blockDim.x) put_split(y, y2, (int64_t)m * ldy + j, x[(int64_t)m * ldx + j]);
 }
 
 __global__ void to_f16_kernel(const float *x, int64_t ldx, int n, __half *hi, __half *lo, int64_t ldy) {
+    pdl_wait();
     const int m = blockIdx.x;
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
         const float v = x[(int64_t)m * ldx + j];
@@ -398,6 +411,7 @@ __global__ void flat_bf16_kernel(const float *x, int64_t count, bf16 *y) {
 // delta routing for one token (one block per token)
 __global__ void delta_route_kernel(float *x, const float *xr, float *delta, const float *query, const float *normw,
                                    int n, int layer) {
+    pdl_wait();
     __shared__ float red[32];
     const int m = blockIdx.x;
     float *xm = x + (int64_t)m * n, *dm = delta + (int64_t)m * n;
@@ -431,6 +445,7 @@ __global__ void delta_route_kernel(float *x, const float *xr, float *delta, cons
 // TwELL sparse W2 for one token (one block per row); skips rows over threshold
 __global__ void twell_kernel(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t,
                              const float *resid, float *out, int n, int m, float threshold) {
+    pdl_wait();
     extern __shared__ int s_idx[];
     __shared__ int s_cnt;
     const int r = blockIdx.x;
@@ -460,6 +475,7 @@ __global__ void twell_kernel(const bf16 *hidden, const bf16 *hidden_lo, const in
 }
 
 __global__ void softmax_kernel(const float *logits, float *probs, int V, float inv_temp) {
+    pdl_wait();
     __shared__ float red[32];
     const int m = blockIdx.x;
     const float *l = logits + (int64_t)m * V;
@@ -495,22 +511,9 @@ cudaError_t launch_gemm(Gemm g, cudaStream_t s) {
     if (g.ksplit > 8 || (g.ksplit & (g.ksplit - 1)) || (g.K / BK) < g.ksplit) return cudaErrorInvalidValue;
     dim3 grid((g.N + CF::BN - 1) / CF::BN, (g.M + CF::BM - 1) / CF::BM, g.batch * g.ksplit);
     if (g.ksplit == 1) {
-        gemm_kernel<CF, T, SA, SB><<<grid, CF::THREADS, smem, s>>>(g);
-        return cudaGetLastError();
+        return launch_pdl(gemm_kernel<CF, T, SA, SB>, grid, dim3(CF::THREADS), smem, s, g);
     }
-    cudaLaunchConfig_t lc = {};
-    lc.gridDim = grid;
-    lc.blockDim = dim3(CF::THREADS);
-    lc.dynamicSmemBytes = smem;
-    lc.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = g.ksplit;
-    lc.attrs = at;
-    lc.numAttrs = 1;
-    return cudaLaunchKernelEx(&lc, gemm_kernel<CF, T, SA, SB>, g);
+    return launch_pdl_cluster(gemm_kernel<CF, T, SA, SB>, grid, dim3(CF::THREADS), smem, s, dim3(1, 1, g.ksplit), g);
 }
 
 template <typename T, bool SA, bool SB>
@@ -533,25 +536,22 @@ cudaError_t gemm(const Gemm &g, cudaStream_t s) {
 }
 
 cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M, float *x,
-                  cudaStream_t s) {
+                  cudaStream_t s, float *zero_rows) {
     if (M <= 0) return cudaSuccess;
-    embed_kernel<<<M, 256, 0, s>>>(tok, pos, wte, wpe, n, M, x);
-    return cudaGetLastError();
+    return launch_pdl(embed_kernel, dim3(M), dim3(256), 0, s, tok, pos, wte, wpe, n, M, x, zero_rows);
 }
-cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s) {
+cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s,
+                    int *zero_count) {
     if (M <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<M, 256, 0, s>>>(x, n, M, yf, yb, yb2, twice ? 1 : 0);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_kernel, dim3(M), dim3(256), 0, s, x, n, M, yf, yb, yb2, twice ? 1 : 0, zero_count);
 }
 cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    to_bf16_kernel<<<M, 256, 0, s>>>(x, ldx, n, M, y, y2, ldy);
-    return cudaGetLastError();
+    return launch_pdl(to_bf16_kernel, dim3(M), dim3(256), 0, s, x, ldx, n, M, y, y2, ldy);
 }
 cudaError_t to_f16(const float *x, int64_t ldx, int n, int M, __half *hi, __half *lo, int64_t ldy, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    to_f16_kernel<<<M, 256, 0, s>>>(x, ldx, n, hi, lo, ldy);
-    return cudaGetLastError();
+    return launch_pdl(to_f16_kernel, dim3(M), dim3(256), 0, s, x, ldx, n, hi, lo, ldy);
 }
 cudaError_t f32_to_f16_split(const float *x, int64_t count, __half *hi, __half *lo, cudaStream_t s) {
     if (count <= 0) return cudaSuccess;
@@ -566,8 +566,7 @@ cudaError_t f32_to_bf16_flat(const float *x, int64_t count, bf16 *y, cudaStream_
 cudaError_t delta_route(float *x, const float *xr, float *delta, const float *query, const float *normw, int n,
                         int M, int layer, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    delta_route_kernel<<<M, 256, 0, s>>>(x, xr, delta, query, normw, n, layer);
-    return cudaGetLastError();
+    return launch_pdl(delta_route_kernel, dim3(M), dim3(256), 0, s, x, xr, delta, query, normw, n, layer);
 }
 cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t,
                             const float *resid, float *out, int n, int m, int M, float threshold, cudaStream_t s) {
@@ -577,13 +576,11 @@ cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int
         cudaError_t e = cudaFuncSetAttribute(twell_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    twell_kernel<<<M, 256, smem, s>>>(hidden, hidden_lo, row_alive, w2t, resid, out, n, m, threshold);
-    return cudaGetLastError();
+    return launch_pdl(twell_kernel, dim3(M), dim3(256), smem, s, hidden, hidden_lo, row_alive, w2t, resid, out, n, m, threshold);
 }
 cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    softmax_kernel<<<M, 256, 0, s>>>(logits, probs, V, inv_temp);
-    return cudaGetLastError();
+    return launch_pdl(softmax_kernel, dim3(M), dim3(256), 0, s, logits, probs, V, inv_temp);
 }
 
 }  // namespace bf

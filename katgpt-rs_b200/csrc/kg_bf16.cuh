@@ -44,6 +44,7 @@ struct Gemm {
     int *row_alive;
     const float *row_scale;
     int64_t sRs;
+    float *C2;  // EPI_F32_RESID: optional second copy of C (same ldc / sC)
     // split-K (1, 2, 4 or 8; 0 = chosen from the shape): the K range is cut
     // into ksplit parts computed by the CTAs of one thread-block cluster and
     // reduced through distributed shared memory in part order (deterministic)
@@ -52,12 +53,15 @@ struct Gemm {
 
 cudaError_t gemm(const Gemm &g, cudaStream_t s);
 
-// x[m, :] = wte[tok[m], :] + wpe[pos[m], :] (bf16 tables, f32 out)
+// x[m, :] = wte[tok[m], :] + wpe[pos[m], :] (bf16 tables, f32 out); zero_rows
+// (optional, [M][n]) is cleared on the way
 cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const bf16 *wpe, int n, int M,
-                  float *x, cudaStream_t s);
+                  float *x, cudaStream_t s, float *zero_rows = nullptr);
 // per row: y = x / sqrt(mean(x^2) + 1e-5); `twice` applies it twice (sp_kv double norm).
 // Writes f32 (if yf) and the bf16 hi/lo split (if yb / yb2). In-place allowed (yf == x).
-cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s);
+// zero_count (optional, [M]) is cleared on the way (the next ReLU GEMM's alive counts).
+cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s,
+                    int *zero_count = nullptr);
 // f32 -> bf16 hi (+ lo) split (strided rows)
 cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy, cudaStream_t s);
 // f32 -> f16 hi + lo split (strided rows)

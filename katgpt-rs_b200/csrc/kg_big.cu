@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "kg_attn.cuh"
+#include "kg_pdl.cuh"
 #include "kg_umma.cuh"
 #include "kg_bf16.cuh"
 #include "kg_internal.h"
@@ -32,6 +33,7 @@ namespace {
 __global__ void expand_tokens_kernel(const int32_t *seq_ids, const int32_t *start_pos, int T, int n_seq, int B,
                                      int n_slots, int V, const int32_t *tokens, int32_t *slot_of, int32_t *pos_of,
                                      int *err) {
+    pdl_wait();
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= n_seq * T) return;
     const int i = m / T, t = m - i * T;
@@ -63,6 +65,7 @@ __global__ void transpose_bf16_kernel(const bf16 *a, int rows, int cols, bf16 *t
 }
 
 __global__ void sanitize_tokens_kernel(const int32_t *tokens, int M, int V, int32_t *out) {
+    pdl_wait();
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m < M) out[m] = min(max(tokens[m], 0), V - 1);
 }
@@ -299,7 +302,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
     const int64_t per_layer = 2 * (int64_t)n * n + 2 * (int64_t)kvd * n + 2 * (int64_t)m * n;
     const bool spkv = c.kv_mode == KG_KV_SPKV_TQ;
     const float scale = 1.0f / sqrtf((float)hd);
-    BIG_TRY(cudaMemsetAsync(g.delta, 0, (size_t)M * n * 4, s));
+    // g.delta (delta-routing accumulator) was cleared by the embedding kernel
     for (int l = 0; l < L; ++l) {
         const bf16 *wqkv = g.layers + l * per_layer;
         const bf16 *wo = wqkv + (int64_t)(n + 2 * kvd) * n;
@@ -337,10 +340,9 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
                                       c.val_bits, g.kcodes, g.vcodes, ctx->kpl, ctx->vpl, g.slot_of, g.pos_of, L, B,
                                       l, nullptr, s));
         } else if (kvd % 128 == 0) {  // decode-sized: the exact tiled encoder is faster
-            BIG_TRY(tq_encode_tiled(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
-                                    g.knorm, g.slot_of, g.pos_of, L, B, l, g.xn, g.skip, s));
-            BIG_TRY(tq_encode_tiled(kvd, c.val_bits, M, g.qkv + n + kvd, nqkv, ctx->rot, ctx->vb, g.vcodes,
-                                    ctx->vpl, g.vnorm, g.slot_of, g.pos_of, L, B, l, g.xn, g.skip, s));
+            BIG_TRY(tq_encode_tiled_kv(kvd, c.key_bits, c.val_bits, M, g.qkv, nqkv, n, n + kvd, ctx->rot, ctx->kb,
+                                       ctx->vb, g.kcodes, ctx->kpl, g.knorm, g.vcodes, ctx->vpl, g.vnorm, g.slot_of,
+                                       g.pos_of, L, B, l, g.xn, g.skip, s));
         } else {
             BIG_TRY(tq_encode_scatter(kvd, c.key_bits, M, g.qkv + n, nqkv, ctx->rot, ctx->kb, g.kcodes, ctx->kpl,
                                       g.knorm, 1, g.slot_of, g.pos_of, L, B, l, s));
@@ -402,14 +404,12 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         // output projection + residual: x = Wo att + xr
         bf::Gemm w = gemm0();
         w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
-        w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n;
+        w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n; w.C2 = g.xr2;  // xr2: MLP residual
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(gemm_split(ctx, w, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // MLP
-        BIG_TRY(cudaMemcpyAsync(g.xr2, g.x, (size_t)M * n * 4, cudaMemcpyDeviceToDevice, s));
-        BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s));
-        BIG_TRY(cudaMemsetAsync(g.alive, 0, (size_t)M * 4, s));
+        BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s, g.alive));  // also clears alive counts
         bf::Gemm u = gemm0();
         u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
         u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;
@@ -457,11 +457,12 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
         // decode: tokens of up to ws_tokens sequences per pass
         for (int i0 = 0; i0 < n_seq; i0 += (int)std::min<int64_t>(g.ws_tokens, ctx->cfg.max_seqs)) {
             const int cnt = std::min<int>(n_seq - i0, (int)std::min<int64_t>(g.ws_tokens, ctx->cfg.max_seqs));
-            expand_tokens_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(seq_ids + i0, start_pos ? start_pos + i0 : nullptr,
-                                                                  1, cnt, (int)ctx->B, ctx->cfg.max_seqs, (int)V,
-                                                                  tokens + i0, g.slot_of, g.pos_of, ctx->d_err);
-            sanitize_tokens_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(tokens + i0, cnt, (int)V, g.tok_of);
-            BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, cnt, g.x, s));
+            BIG_TRY(launch_pdl(expand_tokens_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s, seq_ids + i0,
+                               start_pos ? start_pos + i0 : nullptr, 1, cnt, (int)ctx->B, ctx->cfg.max_seqs, (int)V,
+                               tokens + i0, g.slot_of, g.pos_of, ctx->d_err));
+            BIG_TRY(launch_pdl(sanitize_tokens_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s, tokens + i0, cnt,
+                               (int)V, g.tok_of));
+            BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, cnt, g.x, s, g.delta));
             BIG_TRY(run_layers(ctx, cnt, false, cnt, 1, s));
             BIG_TRY(lm_head(ctx, cnt, logits ? logits + (int64_t)i0 * V : nullptr,
                             probs ? probs + (int64_t)i0 * V : nullptr, s));
@@ -477,7 +478,7 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
                                                             ctx->cfg.max_seqs, (int)V, tokens + (int64_t)i0 * T,
                                                             g.slot_of, g.pos_of, ctx->d_err);
         sanitize_tokens_kernel<<<(M + 255) / 256, 256, 0, s>>>(tokens + (int64_t)i0 * T, M, (int)V, g.tok_of);
-        BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, M, g.x, s));
+        BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, M, g.x, s, g.delta));
         BIG_TRY(run_layers(ctx, M, true, cnt, T, s));
         BIG_TRY(lm_head(ctx, M, logits ? logits + (int64_t)i0 * T * V : nullptr,
                         probs ? probs + (int64_t)i0 * T * V : nullptr, s));

@@ -72,6 +72,13 @@ cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const flo
                               const float *rot, const float *kb, const float *vb, int kbits, int vbits,
                               uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl, const int32_t *slot,
                               const int32_t *pos, int L, int B, int layer, int *nfix, cudaStream_t s);
+// exact tiled encoder for the K and V rows of qkv in one norm and one rotate
+// launch (kv_dim % 128 == 0); xn / skip scratch of 2M rows
+cudaError_t tq_encode_tiled_kv(int dim, int kbits, int vbits, int M, const float *qkv, int64_t ldx, int64_t koff,
+                               int64_t voff, const float *rot, const float *kb, const float *vb, uint8_t *kcodes,
+                               int64_t kpl, float *knorm, uint8_t *vcodes, int64_t vpl, float *vnorm,
+                               const int32_t *slot, const int32_t *pos, int L, int B, int layer, float *xn_scratch,
+                               uint8_t *skip_scratch, cudaStream_t s);
 // the rotation GEMM of the fast encoder (tcgen05 or mma.sync by size)
 cudaError_t gemm_auto(kg_ctx *ctx, const void *gemm_args, cudaStream_t s);
 cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,

@@ -20,6 +20,7 @@
 
 #include "kg_exact.cuh"
 #include "kg_internal.h"
+#include "kg_pdl.cuh"
 
 namespace kg {
 namespace {
@@ -213,6 +214,7 @@ constexpr int ER = 64, EV = 16, EK = 128;  // rows, vectors, columns per stage
 
 __global__ void norm_kernel(int dim, int64_t n_vec, const float *x, int64_t ldx, float *xn, uint8_t *skip,
                             float *norms, const int32_t *slot, const int32_t *pos, int L, int B, int layer) {
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t v = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (v >= n_vec) return;
@@ -232,10 +234,28 @@ __device__ __forceinline__ void cp16(void *dst, const void *src, bool pred) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(pred ? 16 : 0));
 }
 
+// blockIdx.z selects the second side (the V rows of a K + V launch): its xn
+// and flags follow the first side's n_vec rows, with its own codebook,
+// bit width and code arena.
+struct RotSide {
+    const float *bnd;
+    uint8_t *packed;
+    int64_t pstride;
+    int bits;
+};
 __global__ void __launch_bounds__(256) rotate_kernel(int dim, int bits, int64_t n_vec, const float *xn,
                                                      const uint8_t *skip, const float *rot, const float *bnd,
                                                      uint8_t *packed, int64_t pstride, const int32_t *slot,
-                                                     const int32_t *pos, int L, int B, int layer) {
+                                                     const int32_t *pos, int L, int B, int layer, RotSide side2) {
+    pdl_wait();
+    if (blockIdx.z) {
+        xn += n_vec * dim;
+        skip += n_vec;
+        bnd = side2.bnd;
+        packed = side2.packed;
+        pstride = side2.pstride;
+        bits = side2.bits;
+    }
     extern __shared__ float4 esm[];
     float *Rs = reinterpret_cast<float *>(esm);   // [2][ER][EK]
     float *Xs = Rs + 2 * ER * EK;                 // [2][EV][EK]
@@ -354,6 +374,7 @@ __global__ void __launch_bounds__(256) rotate_kernel(int dim, int bits, int64_t 
 __global__ void norm_split_kernel(int dim, int Mk, int Mv, const float *qkv, int64_t ldx, int64_t koff,
                                   int64_t voff, float *xn, __half *xh, __half *xl, uint8_t *skip, float *knorm,
                                   float *vnorm, const int32_t *slot, const int32_t *pos, int L, int B, int layer) {
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int v = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (v >= Mk + Mv) return;
@@ -370,9 +391,11 @@ __global__ void norm_split_kernel(int dim, int Mk, int Mv, const float *qkv, int
     for (int k = lane; k < dim; k += 32) {
         const float y = xv[k] * inv;
         xn[(int64_t)v * dim + k] = y;
-        const __half h = __float2half_rn(y);
-        xh[(int64_t)v * dim + k] = h;
-        xl[(int64_t)v * dim + k] = __float2half_rn(y - __half2float(h));
+        if (xh) {
+            const __half h = __float2half_rn(y);
+            xh[(int64_t)v * dim + k] = h;
+            xl[(int64_t)v * dim + k] = __float2half_rn(y - __half2float(h));
+        }
     }
 }
 
@@ -383,6 +406,7 @@ __global__ void quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, c
                                       uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl,
                                       const int32_t *slot, const int32_t *pos, int L, int B, int layer, float eps,
                                       int *nfix) {
+    pdl_wait();
     extern __shared__ uint8_t qsm[];
     __shared__ float bnd[2][15];
     const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -443,9 +467,8 @@ cudaError_t tq_norm_split(int dim, int Mk, int Mv, const float *qkv, int64_t ldx
                           float *xn, __half *xh, __half *xl, uint8_t *skip, float *knorm, float *vnorm,
                           const int32_t *slot, const int32_t *pos, int L, int B, int layer, cudaStream_t s) {
     if (Mk + Mv <= 0) return cudaSuccess;
-    norm_split_kernel<<<(Mk + Mv + 7) / 8, 256, 0, s>>>(dim, Mk, Mv, qkv, ldx, koff, voff, xn, xh, xl, skip, knorm,
-                                                        vnorm, slot, pos, L, B, layer);
-    return cudaGetLastError();
+    return launch_pdl(norm_split_kernel, dim3((Mk + Mv + 7) / 8), dim3(256), 0, s, dim, Mk, Mv, qkv, ldx, koff, voff,
+                      xn, xh, xl, skip, knorm, vnorm, slot, pos, L, B, layer);
 }
 
 cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
@@ -455,10 +478,9 @@ cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const flo
     if (Mk + Mv <= 0) return cudaSuccess;
     if (dim % 2 || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
     const int warps = 8;
-    quantize_fixup_kernel<<<(Mk + Mv + warps - 1) / warps, warps * 32, (size_t)warps * dim, s>>>(
-        dim, Mk, Mv, Y, xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl, vpl, slot, pos, L, B, layer,
-        tq_fixup_eps(dim), nfix);
-    return cudaGetLastError();
+    return launch_pdl(quantize_fixup_kernel, dim3((Mk + Mv + warps - 1) / warps), dim3(warps * 32),
+                      (size_t)warps * dim, s, dim, Mk, Mv, Y, xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl,
+                      vpl, slot, pos, L, B, layer, tq_fixup_eps(dim), nfix);
 }
 
 namespace {
@@ -515,8 +537,32 @@ cudaError_t tq_encode_tiled(int dim, int bits, int64_t n_vec, const float *x, in
     }
     dim3 grid(dim / ER, (unsigned)((n_vec + EV - 1) / EV));
     rotate_kernel<<<grid, 256, smem, s>>>(dim, bits, n_vec, xn_scratch, skip_scratch, rot, bnd, packed, pstride, slot,
-                                          pos, L, B, layer);
+                                          pos, L, B, layer, RotSide{});
     return cudaGetLastError();
+}
+
+cudaError_t tq_encode_tiled_kv(int dim, int kbits, int vbits, int M, const float *qkv, int64_t ldx, int64_t koff,
+                               int64_t voff, const float *rot, const float *kb, const float *vb, uint8_t *kcodes,
+                               int64_t kpl, float *knorm, uint8_t *vcodes, int64_t vpl, float *vnorm,
+                               const int32_t *slot, const int32_t *pos, int L, int B, int layer, float *xn_scratch,
+                               uint8_t *skip_scratch, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    if (dim % EK || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
+    cudaError_t e0 = launch_pdl(norm_split_kernel, dim3((2 * M + 7) / 8), dim3(256), 0, s, dim, M, M, qkv, ldx, koff,
+                                voff, xn_scratch, (__half *)nullptr, (__half *)nullptr, skip_scratch, knorm, vnorm,
+                                slot, pos, L, B, layer);
+    if (e0 != cudaSuccess) return e0;
+    const int smem = 2 * (ER + EV) * EK * 4;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    dim3 grid(dim / ER, (unsigned)((M + EV - 1) / EV), 2);
+    return launch_pdl(rotate_kernel, grid, dim3(256), smem, s, dim, kbits, (int64_t)M, (const float *)xn_scratch,
+                      (const uint8_t *)skip_scratch, rot, kb, kcodes, kpl, slot, pos, L, B, layer,
+                      RotSide{vb, vcodes, vpl, vbits});
 }
 
 cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, int64_t ldx, const float *rot,

@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                     case bf::EPI_F32_ROWSCALE:
                     case bf::EPI_F32_RESID: {
                         float *dst = g.C + (int64_t)row * g.ldc + col;
+                        float *dst2 = g.epi == bf::EPI_F32_RESID && g.C2 ? g.C2 + (int64_t)row * g.ldc + col : nullptr;
                         const float *r = g.epi == bf::EPI_F32_RESID ? g.R + (int64_t)row * g.ldr + col : nullptr;
                         if (full_row) {
 #pragma unroll
@@ -224,9 +225,13 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                                     o.x += rr.x; o.y += rr.y; o.z += rr.z; o.w += rr.w;
                                 }
                                 *reinterpret_cast<float4 *>(dst + i) = o;
+                                if (dst2) *reinterpret_cast<float4 *>(dst2 + i) = o;
                             }
                         } else {
-                            for (int i = 0; i < 32 && col + i < g.N; ++i) dst[i] = v[i] * rs + (r ? r[i] : 0.0f);
+                            for (int i = 0; i < 32 && col + i < g.N; ++i) {
+                                dst[i] = v[i] * rs + (r ? r[i] : 0.0f);
+                                if (dst2) dst2[i] = dst[i];
+                            }
                         }
                         break;
                     }
