@@ -779,7 +779,10 @@ struct KvArray {
 };
 int kv_arrays(const kg_ctx *ctx, KvArray *out) {
     int n = 0;
-    if (ctx->big_path) {
+    if (ctx->big_path && ctx->big.std_kv) {
+        out[n++] = {reinterpret_cast<uint8_t *>(ctx->big.kcache), (size_t)ctx->kvd * 2};
+        out[n++] = {reinterpret_cast<uint8_t *>(ctx->big.vcache), (size_t)ctx->kvd * 2};
+    } else if (ctx->big_path) {
         const kg::BigState &g = ctx->big;
         out[n++] = {g.kcodes, (size_t)ctx->kpl};
         out[n++] = {g.vcodes, (size_t)ctx->vpl};

@@ -1016,6 +1016,129 @@ __global__ void build_luts_kernel(const float *kcent, const float *vcent, uint2 
 }
 
 // ---------------------------------------------------------------------------
+// Standard attention over a bf16 K/V cache (AttentionMode::Standard,
+// attention_head, src/transformer.rs:333-389; cache layout of
+// MultiLayerKVCache, crates/katgpt-transformer/src/kv_cache.rs:8-124, kept as
+// [slot][layer][pos][kv_dim] bf16 on the device).
+
+// New K/V rows of a step into the bf16 cache; for prefill also the f16 hi/lo
+// split of the bf16-rounded rows (the flash kernel's operands), so prefill and
+// decode attend over the same cached values.
+__global__ void kv_store_std_kernel(const float *qkv, int64_t ldx, int64_t koff, int64_t voff, int kvd,
+                                    const int32_t *slot, const int32_t *pos, int L, int B, int layer, bf16 *kc,
+                                    bf16 *vc, __half *kt, __half *kt2, __half *vt, __half *vt2) {
+    pdl_wait();
+    const int m = blockIdx.x;
+    const int64_t row = ((int64_t)slot[m] * L + layer) * B + pos[m];
+    for (int j = threadIdx.x; j < kvd; j += blockDim.x) {
+        const bf16 k = __float2bfloat16_rn(qkv[(int64_t)m * ldx + koff + j]);
+        const bf16 v = __float2bfloat16_rn(qkv[(int64_t)m * ldx + voff + j]);
+        kc[row * kvd + j] = k;
+        vc[row * kvd + j] = v;
+        if (kt) {
+            const float kf = __bfloat162float(k), vf = __bfloat162float(v);
+            const __half kh = __float2half_rn(kf), vh = __float2half_rn(vf);
+            kt[(int64_t)m * kvd + j] = kh;
+            kt2[(int64_t)m * kvd + j] = __float2half_rn(kf - __half2float(kh));
+            vt[(int64_t)m * kvd + j] = vh;
+            vt2[(int64_t)m * kvd + j] = __float2half_rn(vf - __half2float(vh));
+        }
+    }
+}
+
+// Decode: one CTA per (kv head, token); each of 4 warps streams every 4th
+// position (4 positions in flight), lanes own HD / 32 dims, online softmax
+// per warp, then the warps combine through shared memory. Query heads that
+// share the kv head (GQA) run one after another.
+template <int HD>
+__global__ void __launch_bounds__(128) std_decode_kernel(const StdDecodeArgs a) {
+    pdl_wait();
+    constexpr int DPL = HD / 32, U = 4;
+    __shared__ float sm_m[4], sm_l[4], sm_o[4][HD];
+    const int kh = blockIdx.x, m = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tn = a.pos[m] + 1, G = a.nh / a.nkv;
+    const int64_t base = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+    const bf16 *K = a.kc + base * a.kvd + kh * HD + lane * DPL;
+    const bf16 *Vp = a.vc + base * a.kvd + kh * HD + lane * DPL;
+    auto load = [&](const bf16 *p, float (&f)[DPL]) {
+        if constexpr (DPL == 4) {
+            const uint2 w = *reinterpret_cast<const uint2 *>(p);
+            const __nv_bfloat162 x0 = *reinterpret_cast<const __nv_bfloat162 *>(&w.x);
+            const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162 *>(&w.y);
+            f[0] = __low2float(x0); f[1] = __high2float(x0); f[2] = __low2float(x1); f[3] = __high2float(x1);
+        } else {
+            const __nv_bfloat162 x0 = *reinterpret_cast<const __nv_bfloat162 *>(p);
+            f[0] = __low2float(x0); f[1] = __high2float(x0);
+        }
+    };
+    for (int qh = 0; qh < G; ++qh) {
+        const int h = kh * G + qh;
+        float q[DPL];
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) q[d] = a.Q[(int64_t)m * a.ldq + h * HD + lane * DPL + d] * a.scale;
+        float mx = -INFINITY, l = 0.0f, o[DPL];
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[d] = 0.0f;
+        for (int t0 = warp * U; t0 < tn; t0 += 4 * U) {
+            float kf[U][DPL], vf[U][DPL], s[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int t = min(t0 + u, tn - 1);
+                load(K + (int64_t)t * a.kvd, kf[u]);
+                load(Vp + (int64_t)t * a.kvd, vf[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float p = 0.0f;
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) p = fmaf(q[d], kf[u][d], p);
+                s[u] = p;
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1)
+#pragma unroll
+                for (int u = 0; u < U; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], off);
+            float mnew = mx;
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (t0 + u < tn) mnew = fmaxf(mnew, s[u]);
+            const float corr = expf(mx - mnew);
+            l *= corr;
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[d] *= corr;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float p = t0 + u < tn ? expf(s[u] - mnew) : 0.0f;
+                l += p;
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) o[d] = fmaf(p, vf[u][d], o[d]);
+            }
+            mx = mnew;
+        }
+        if (lane == 0) {
+            sm_m[warp] = mx;
+            sm_l[warp] = l;
+        }
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) sm_o[warp][lane * DPL + d] = o[d];
+        __syncthreads();
+        for (int d = threadIdx.x; d < HD; d += 128) {
+            float M = -INFINITY;
+            for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w]);
+            float L = 0.0f, acc = 0.0f;
+            for (int w = 0; w < 4; ++w) {
+                const float f = sm_m[w] == -INFINITY ? 0.0f : expf(sm_m[w] - M);
+                L += f * sm_l[w];
+                acc += f * sm_o[w][d];
+            }
+            a.O[(int64_t)m * a.ldo + h * HD + d] = acc / L;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Prefill: dequantize codes of every prompt token to f16 hi/lo centroid vectors.
 __global__ void centroids_kernel(const uint8_t *codes, int pl, int64_t row_stride_codes, const int32_t *slot,
                                  const int32_t *pos, int L, int B, int layer, const float *cent, int kvd, int M,
@@ -1425,6 +1548,25 @@ bool decode_attn_maps(AttnMaps *maps, const uint8_t *kcodes, const uint8_t *vcod
 cudaError_t build_luts(const float *kcent, const float *vcent, uint2 *lutk, uint2 *lutv, cudaStream_t s) {
     build_luts_kernel<<<(2 * LUT8_ENTRIES + 255) / 256, 256, 0, s>>>(kcent, vcent, lutk, lutv);
     return cudaGetLastError();
+}
+
+cudaError_t kv_store_std(const float *qkv, int64_t ldx, int64_t koff, int64_t voff, int kvd, int M,
+                         const int32_t *slot, const int32_t *pos, int L, int B, int layer, bf16 *kc, bf16 *vc,
+                         __half *kt, __half *kt2, __half *vt, __half *vt2, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    return launch_pdl(kv_store_std_kernel, dim3(M), dim3(256), 0, s, qkv, ldx, koff, voff, kvd, slot, pos, L, B, layer,
+                      kc, vc, kt, kt2, vt, vt2);
+}
+
+cudaError_t std_decode(const StdDecodeArgs &a, cudaStream_t s) {
+    if (a.M <= 0) return cudaSuccess;
+    if (a.nh % a.nkv) return cudaErrorInvalidValue;
+    const dim3 grid(a.nkv, a.M);
+    switch (a.hd) {
+        case 64: return launch_pdl(std_decode_kernel<64>, grid, dim3(128), 0, s, a);
+        case 128: return launch_pdl(std_decode_kernel<128>, grid, dim3(128), 0, s, a);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace attn

@@ -51,6 +51,24 @@ struct FlashArgs {
 };
 
 cudaError_t decode_attn(const DecodeAttnArgs &a, cudaStream_t s);
+
+// Standard attention over a bf16 K/V cache [slot][layer][pos][kvd].
+struct StdDecodeArgs {
+    const float *Q;              // f32 query rows (column 0 of qkv), scaled inside
+    int64_t ldq;
+    const __nv_bfloat16 *kc, *vc;
+    const int32_t *slot, *pos;
+    float *O;                    // [M][n] f32 attention output
+    int64_t ldo;
+    int M, nh, nkv, hd, kvd, L, B, layer;
+    float scale;
+};
+cudaError_t std_decode(const StdDecodeArgs &a, cudaStream_t s);
+// new K / V rows into the bf16 cache; kt.. (optional) receive the f16 hi / lo
+// split of the bf16-rounded rows for the prefill flash kernel
+cudaError_t kv_store_std(const float *qkv, int64_t ldx, int64_t koff, int64_t voff, int kvd, int M,
+                         const int32_t *slot, const int32_t *pos, int L, int B, int layer, __nv_bfloat16 *kc,
+                         __nv_bfloat16 *vc, __half *kt, __half *kt2, __half *vt, __half *vt2, cudaStream_t s);
 cudaError_t centroids(const uint8_t *codes, int pl, const int32_t *slot, const int32_t *pos, int L, int B, int layer,
                       const float *cent, int kvd, int M, __half *out, __half *out_lo, cudaStream_t s);
 cudaError_t gather_norms(const float *norms, const int32_t *slot, const int32_t *pos, int L, int B, int layer, int M,

@@ -89,9 +89,11 @@ cudaError_t dalloc(T **p, size_t count, std::vector<void *> &owned) {
 }  // namespace
 
 int big_supported(const kg_config &c, std::string &why) {
-    if (c.kv_mode == KG_KV_F32) return why = "the bf16 path needs a TurboQuant KV mode", -1;
-    for (int b : {c.key_bits, c.val_bits})
-        if (b != 3 && b != 4) return why = "the bf16 path packs 3/4-bit codes", -1;
+    if (c.weight_dtype != KG_W_BF16) return why = "the tensor-core path runs bf16 weights (KG_W_BF16)", -1;
+    if (c.kv_mode != KG_KV_F32)
+        for (int b : {c.key_bits, c.val_bits})
+            if (b != 3 && b != 4) return why = "the bf16 path packs 3/4-bit codes", -1;
+    if (c.n_kv_head < 1 || c.n_head % c.n_kv_head) return why = "n_head must be a multiple of n_kv_head", -1;
     const int kvd = c.n_kv_head * c.head_dim;
     if (kvd % 64) return why = "kv_dim must be a multiple of 64", -1;
     if (c.head_dim != 64 && c.head_dim != 128) return why = "head_dim must be 64 or 128", -1;
@@ -118,15 +120,21 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.w2t, L * m * n, own));
     BIG_TRY(dalloc(&g.dq, L * n, own));
     BIG_TRY(dalloc(&g.dn, L * n, own));
-    BIG_TRY(dalloc(&g.rot_h, kvd * kvd, own));
-    BIG_TRY(dalloc(&g.rot_l, kvd * kvd, own));
-    BIG_TRY(dalloc(&g.rot_th, kvd * kvd, own));
-    BIG_TRY(dalloc(&g.rot_tl, kvd * kvd, own));
-    // code arena
-    BIG_TRY(dalloc(&g.kcodes, (size_t)S * L * B * ctx->kpl, own));
-    BIG_TRY(dalloc(&g.vcodes, (size_t)S * L * B * ctx->vpl, own));
-    BIG_TRY(dalloc(&g.knorm, (size_t)S * L * B, own));
-    BIG_TRY(dalloc(&g.vnorm, (size_t)S * L * B, own));
+    g.std_kv = c.kv_mode == KG_KV_F32;
+    if (g.std_kv) {  // standard attention: bf16 K/V arena
+        BIG_TRY(dalloc(&g.kcache, (size_t)S * L * B * kvd, own));
+        BIG_TRY(dalloc(&g.vcache, (size_t)S * L * B * kvd, own));
+    } else {
+        BIG_TRY(dalloc(&g.rot_h, kvd * kvd, own));
+        BIG_TRY(dalloc(&g.rot_l, kvd * kvd, own));
+        BIG_TRY(dalloc(&g.rot_th, kvd * kvd, own));
+        BIG_TRY(dalloc(&g.rot_tl, kvd * kvd, own));
+        // code arena
+        BIG_TRY(dalloc(&g.kcodes, (size_t)S * L * B * ctx->kpl, own));
+        BIG_TRY(dalloc(&g.vcodes, (size_t)S * L * B * ctx->vpl, own));
+        BIG_TRY(dalloc(&g.knorm, (size_t)S * L * B, own));
+        BIG_TRY(dalloc(&g.vnorm, (size_t)S * L * B, own));
+    }
     // workspace (ws_tokens rows)
     const int64_t W = g.ws_tokens;
     const int64_t nqkv = n + 2 * kvd;
@@ -166,6 +174,10 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.qrot2, S * ctx->nh * kvd, own));
     BIG_TRY(dalloc(&g.U, S * ctx->nh * kvd, own));
     BIG_TRY(dalloc(&g.U2, S * ctx->nh * kvd, own));
+    if (g.std_kv) {
+        BIG_TRY(cudaStreamSynchronize(ctx->stream));
+        return cudaSuccess;
+    }
     // centroid tables
     BIG_TRY(dalloc(&g.kcent, 16, own));
     BIG_TRY(dalloc(&g.vcent, 16, own));
@@ -190,6 +202,12 @@ cudaError_t big_reset(kg_ctx *ctx, int64_t slot0, int64_t nslots) {
     BigState &g = ctx->big;
     const size_t rows = (size_t)ctx->L * ctx->B;
     cudaStream_t s = ctx->stream;
+    if (g.std_kv) {
+        const size_t e = rows * ctx->kvd;
+        BIG_TRY(cudaMemsetAsync(g.kcache + slot0 * e, 0, nslots * e * 2, s));
+        BIG_TRY(cudaMemsetAsync(g.vcache + slot0 * e, 0, nslots * e * 2, s));
+        return cudaStreamSynchronize(s);
+    }
     BIG_TRY(cudaMemsetAsync(g.kcodes + slot0 * rows * ctx->kpl, 0, nslots * rows * ctx->kpl, s));
     BIG_TRY(cudaMemsetAsync(g.vcodes + slot0 * rows * ctx->vpl, 0, nslots * rows * ctx->vpl, s));
     BIG_TRY(cudaMemsetAsync(g.knorm + slot0 * rows, 0, nslots * rows * 4, s));
@@ -324,7 +342,12 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // TurboQuant encode of K and V into the arena (exact reference order)
         prof_mark(ctx, KG_PROF_ENCODE, 0, s);
-        if (M >= 256) {
+        if (g.std_kv) {
+            // standard attention: K/V rows into the bf16 cache (and the prompt's
+            // f16 hi/lo copies for the flash kernel)
+            BIG_TRY(attn::kv_store_std(g.qkv, nqkv, n, n + kvd, kvd, M, g.slot_of, g.pos_of, L, B, l, g.kcache,
+                                       g.vcache, prefill ? g.kt : nullptr, g.kt2, g.vt, g.vt2, s));
+        } else if (M >= 256) {
             // prefill-sized: K and V rows together, exact norms and xn, rotation
             // on the tensor cores, codes with exact recomputation next to the
             // boundaries
@@ -350,10 +373,19 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
                                       ctx->vpl, g.vnorm, 1, g.slot_of, g.pos_of, L, B, l, s));
         }
         prof_mark(ctx, KG_PROF_ENCODE, 1, s);
-        BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
-        if (prefill) {
-            // dequantize the prompt's K and V: k~ = norm * (c R)
-            for (int kv = 0; kv < 2; ++kv) {
+        if (prefill || !g.std_kv) BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
+        if (g.std_kv && !prefill) {
+            attn::StdDecodeArgs sa;
+            sa.Q = g.qkv; sa.ldq = nqkv; sa.kc = g.kcache; sa.vc = g.vcache; sa.slot = g.slot_of; sa.pos = g.pos_of;
+            sa.O = g.attf; sa.ldo = n; sa.M = M; sa.nh = nh; sa.nkv = (int)ctx->nkv; sa.hd = hd; sa.kvd = kvd;
+            sa.L = L; sa.B = B; sa.layer = l; sa.scale = scale;
+            prof_mark(ctx, KG_PROF_ATTN, 0, s);
+            BIG_TRY(attn::std_decode(sa, s));
+            prof_mark(ctx, KG_PROF_ATTN, 1, s);
+        } else if (prefill) {
+            // dequantize the prompt's K and V: k~ = norm * (c R) (standard
+            // attention already has its f16 hi / lo rows from kv_store_std)
+            for (int kv = 0; kv < (g.std_kv ? 0 : 2); ++kv) {
                 const uint8_t *codes = kv ? g.vcodes : g.kcodes;
                 const int pl = (int)(kv ? ctx->vpl : ctx->kpl);
                 BIG_TRY(attn::centroids(codes, pl, g.slot_of, g.pos_of, L, B, l, kv ? g.vcent : g.kcent, kvd, M,

@@ -114,6 +114,9 @@ struct BigState {
     // replicated centroid tables (has_maps false: the cp.async kernel runs)
     attn::AttnMaps maps;
     bool has_maps = false;
+    // standard attention (kv_mode KG_KV_F32): bf16 K/V cache [slot][layer][pos][kv_dim]
+    bool std_kv = false;
+    __nv_bfloat16 *kcache = nullptr, *vcache = nullptr;
     uint2 *lutk = nullptr, *lutv = nullptr;
 };
 int big_supported(const kg_config &c, std::string &why);

@@ -138,3 +138,25 @@ def test_decode_graph_replay_matches_eager(kg):
     be2.profile(False)
     be.close()
     be2.close()
+
+
+@pytest.mark.parametrize("shape", [
+    dict(),                                                                   # 2 heads of 64
+    dict(n_embd=256, n_head=4, head_dim=64, n_kv_head=2, mlp_hidden=512),    # grouped-query attention
+    dict(vocab_size=256, n_embd=2048, n_head=16, head_dim=128, n_kv_head=16, mlp_hidden=8192, n_layer=1),  # C4 widths
+])
+def test_standard_attention_matches_oracle(kg, orc, shape):
+    # AttentionMode::Standard on the bf16 path: bf16 K/V cache, forward_base semantics
+    cfg, be, w = make(kg, 0, **shape)
+    n_seq, T0, T1 = 2, 24, 8
+    toks = tokens(n_seq, T0 + T1, cfg.vocab_size, seed=17)
+    pre = be.forward_batch(toks[:, :T0])
+    dec = [be.forward_batch(toks[:, t:t + 1], start_pos=np.full(n_seq, t))[:, 0] for t in range(T0, T0 + T1)]
+    got = np.concatenate([pre, np.stack(dec, axis=1)], axis=1)
+    for i in range(n_seq):
+        ref = orc.run_sequence(orc.from_kg(cfg), orc.MODE_BASE, w, toks[i])[0]
+        err = rel_err(got[i], ref)
+        print("standard %s seq %d: max rel err prefill %.2e decode %.2e" % (shape.get("n_embd", 128), i,
+                                                                          err[:T0].max(), err[T0:].max()))
+        assert err.max() <= REL_BF16
+    be.close()

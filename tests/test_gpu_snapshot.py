@@ -58,6 +58,14 @@ def test_snapshot_restore_bf16_path(kg):
     _roundtrip(kg, cfg, w, torch, exact=False)
 
 
+def test_snapshot_restore_standard_attention(kg):
+    torch = pytest.importorskip("torch")
+    cfg = kg.micro_config(vocab_size=96, block_size=64, n_embd=256, n_head=4, head_dim=64, n_kv_head=4,
+                          mlp_hidden=512, n_layer=2, kv_mode=kg.KG_KV_F32, weight_dtype=kg.KG_W_BF16, max_seqs=2)
+    w = kg.bf16_round(kg.reference_weights(cfg, seed=11, scale_mode=1, std=0.05))
+    _roundtrip(kg, cfg, w, torch, exact=False)
+
+
 def test_seq_alloc_free(kg):
     cfg = kg.micro_config(kv_mode=kg.KG_KV_TQ, max_seqs=2)
     be = kg.CudaBackend(cfg)
