@@ -37,6 +37,11 @@ SEED = 42
 C3 = dict(vocab_size=32000, block_size=2048, n_embd=768, n_head=12, head_dim=64, n_kv_head=12,
           mlp_hidden=3072, n_layer=12, key_bits=4, val_bits=4)
 C3_SEQS, C3_PREFILL = 64, 1024
+# c4: the wide-MLP TwELL model; vocab and decode steps are not given by the
+# workload and are taken as 32000 and up to 64 (block 512 + 64)
+C4 = dict(vocab_size=32000, block_size=576, n_embd=2048, n_head=16, head_dim=128, n_kv_head=16,
+          mlp_hidden=8192, n_layer=24)
+C4_SEQS, C4_PREFILL, C4_KEEP = 512, 512, 0.1
 C2_SEQS, C2_T = 65536, 16
 
 
@@ -46,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c3", choices=["c3", "c2"])
+    ap.add_argument("--workload", default="c3", choices=["c3", "c4", "c2"])
     return ap.parse_args()
 
 
@@ -129,6 +134,16 @@ def _oracle():
     return oracle
 
 
+_WEIGHTS = {}
+
+
+def _oracle_weights(oracle, name, cfg):
+    """Oracle weights of a workload, generated once per process (the c4 set is 5 GB of f32)."""
+    if name not in _WEIGHTS:
+        _WEIGHTS[name] = oracle.weights(cfg, SEED, 1, 0.02)
+    return _WEIGHTS[name]
+
+
 def cpu_sample_c3(budget_s=15.0, threads=None):
     """forward_quantized of the C3 model on host cores: one sequence per thread,
     positions 0.. until the budget is spent (short contexts: the attention part
@@ -137,7 +152,7 @@ def cpu_sample_c3(budget_s=15.0, threads=None):
     threads = threads or os.cpu_count() or 1
     cfg = oracle.config(vocab_size=C3["vocab_size"], block_size=C3["block_size"], n_embd=768, n_head=12,
                         head_dim=64, n_kv_head=12, mlp_hidden=3072, n_layer=12)
-    w = oracle.weights(cfg, SEED, 1, 0.02)
+    w = _oracle_weights(oracle, "c3", cfg)
     rng = np.random.default_rng(7)
     T = 8
     while True:
@@ -150,6 +165,27 @@ def cpu_sample_c3(budget_s=15.0, threads=None):
             break
         T *= 2
     return threads * T / el, threads, f"{threads} sequences x positions 0..{T - 1} (forward_quantized, {el:.1f} s)"
+
+
+def cpu_sample_c4(budget_s=15.0, threads=None):
+    """forward_base of the c4 model on host cores (dense hidden activations:
+    the hook is a device-side benchmark input), one sequence per thread."""
+    oracle = _oracle()
+    threads = threads or os.cpu_count() or 1
+    cfg = oracle.config(vocab_size=C4["vocab_size"], block_size=C4["block_size"], n_embd=2048, n_head=16,
+                        head_dim=128, n_kv_head=16, mlp_hidden=8192, n_layer=24)
+    w = _oracle_weights(oracle, "c4", cfg)
+    rng = np.random.default_rng(7)
+    T = 2
+    while True:
+        toks = rng.integers(0, C4["vocab_size"], size=(threads, T)).astype(np.int32)
+        t0 = time.perf_counter()
+        oracle.run_batch(cfg, oracle.MODE_BASE, w, toks, threads=threads, keep_logits=False)
+        el = time.perf_counter() - t0
+        if el > budget_s / 3 or T >= 64:
+            break
+        T *= 2
+    return threads * T / el, threads, f"{threads} sequences x positions 0..{T - 1} (forward_base, {el:.1f} s)"
 
 
 def cpu_sample_c2(budget_s=10.0, threads=None):
@@ -169,6 +205,9 @@ def cpu_sample_c2(budget_s=10.0, threads=None):
     return done / el, threads, f"{done // C2_T} sequences x {C2_T} positions (forward_sp_kv_quant, {el:.1f} s)"
 
 
+CPU_SAMPLE = {"c3": cpu_sample_c3, "c4": cpu_sample_c4, "c2": cpu_sample_c2}
+
+
 def workload_config(workload, world):
     """The `config` of a bench line (shared by both arms)."""
     if workload == "c3":
@@ -176,6 +215,13 @@ def workload_config(workload, world):
                             "bf16 weights N(0,0.02), 4-bit TurboQuant KV (forward_quantized); 64 sequences, "
                             "1024-token prefill then teacher-forced decode",
                 "global_batch": world * C3_SEQS, "seq_len": C3_PREFILL, "parallelism": f"dp{world} (sequence shards)",
+                "l2": "flushed between steps (256 MiB write, outside the timed events)"}
+    if workload == "c4":
+        return {"workload": "c4: n_layer 24, n_embd 2048, 16 heads, mlp 8192, vocab 32000 (assumed), bf16 weights "
+                            "N(0,0.02), standard attention with a bf16 KV cache, TwELL with ~90%-zero hidden "
+                            "activations (benchmark hook: per-token Bernoulli keep 0.1, N(0,1) survivors); "
+                            "512 sequences, 512-token prefill then teacher-forced decode",
+                "global_batch": world * C4_SEQS, "seq_len": C4_PREFILL, "parallelism": f"dp{world} (sequence shards)",
                 "l2": "flushed between steps (256 MiB write, outside the timed events)"}
     return {"workload": "c2: Config::micro + SpKvQuant + TurboQuant 3-bit, 65536 sequences x 16 positions",
             "global_batch": world * C2_SEQS, "seq_len": C2_T, "parallelism": f"dp{world} (sequence shards)",
@@ -189,7 +235,7 @@ def run_reference(args):
     t0 = time.perf_counter()
     vals = []
     for _ in range(max(1, min(args.steps, 3))):
-        v, cores, sample = (cpu_sample_c3 if args.workload == "c3" else cpu_sample_c2)(budget_s=8.0)
+        v, cores, sample = CPU_SAMPLE[args.workload](budget_s=8.0)
         vals.append(v)
     v = float(np.median(vals))
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": len(vals),
@@ -224,26 +270,48 @@ def timed_steps(torch, stream, steps, step_fn, flush):
     return [a.elapsed_time(b) for a, b in ev]
 
 
-def bench_c3(args, torch, dist, kgcuda, world, rank, local):
+def decode_spec(workload, kgcuda):
+    """Model, cache and roofline description of a decode workload."""
+    if workload == "c3":
+        c = C3
+        return dict(name="c3", cfg=c, seqs=C3_SEQS, prefill=C3_PREFILL, kv_mode=kgcuda.KG_KV_TQ, keep=0.0,
+                    kv_bytes_per_pos=c["n_embd"] // 2 + c["n_embd"] // 2 + 8,   # 4-bit K and V codes + two norms
+                    attn_kernel="decode KV attention (scores + softmax + values over 4-bit codes)",
+                    profile="decode_attention_c3.txt")
+    c = C4
+    kvd = c["n_kv_head"] * c["head_dim"]
+    return dict(name="c4", cfg=c, seqs=C4_SEQS, prefill=C4_PREFILL, kv_mode=kgcuda.KG_KV_F32, keep=C4_KEEP,
+                kv_bytes_per_pos=2 * kvd * 2,                                   # bf16 K and V rows
+                attn_kernel="decode KV attention (standard, bf16 K/V rows, GQA)",
+                profile="decode_attention_c4.txt")
+
+
+def bench_decode(args, torch, dist, kgcuda, world, rank, local):
+    """Prefill every sequence, then time teacher-forced decode steps (one
+    token per sequence per step) on the device."""
+    sp_ = decode_spec(args.workload, kgcuda)
+    C, n, PRE = sp_["cfg"], sp_["seqs"], sp_["prefill"]
     dev = torch.device("cuda", local)
-    cfg = kgcuda.micro_config(kv_mode=kgcuda.KG_KV_TQ, weight_dtype=kgcuda.KG_W_BF16, max_seqs=C3_SEQS, **C3)
+    cfg = kgcuda.micro_config(kv_mode=sp_["kv_mode"], weight_dtype=kgcuda.KG_W_BF16, max_seqs=n, **C)
     be = kgcuda.CudaBackend(cfg, device=local)
     be.random_weights(seed=SEED, std=0.02)
-    n, V = C3_SEQS, C3["vocab_size"]
+    if sp_["keep"] > 0:
+        be.set_mlp_hook(sp_["keep"], SEED + rank)
+    V = C["vocab_size"]
     n_prof = min(args.steps, 8)
     total_dec = args.warmup + args.steps + n_prof
     e_steps = min(max(3, args.steps // 4), 64)
-    assert C3_PREFILL + total_dec + e_steps + 2 <= C3["block_size"], "too many steps for block_size 2048"
+    assert PRE + total_dec + e_steps + 2 <= C["block_size"], f"too many steps for block_size {C['block_size']}"
     rng = np.random.default_rng(1000 + rank)
-    toks = rng.integers(0, V, size=(n, C3["block_size"])).astype(np.int32)
+    toks = rng.integers(0, V, size=(n, C["block_size"])).astype(np.int32)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     sp = ctypes.c_void_p(stream.cuda_stream)
     d_ids = torch.arange(n, dtype=torch.int32, device=dev)
-    d_pre = torch.from_numpy(np.ascontiguousarray(toks[:, :C3_PREFILL])).to(dev)
-    d_dec = torch.from_numpy(np.ascontiguousarray(toks[:, C3_PREFILL:].T)).to(dev)       # [pos][seq]
-    d_pos = (torch.arange(C3["block_size"] - C3_PREFILL, dtype=torch.int32, device=dev)[:, None]
-             + C3_PREFILL).expand(-1, n).contiguous()
+    d_pre = torch.from_numpy(np.ascontiguousarray(toks[:, :PRE])).to(dev)
+    d_dec = torch.from_numpy(np.ascontiguousarray(toks[:, PRE:].T)).to(dev)       # [pos][seq]
+    d_pos = (torch.arange(C["block_size"] - PRE, dtype=torch.int32, device=dev)[:, None]
+             + PRE).expand(-1, n).contiguous()
     d_log = torch.empty((n, V), dtype=torch.float32, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
@@ -253,7 +321,7 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     be.profile_read()
     be.profile(True)
     e0.record(stream)
-    be.forward_batch_dev(n, C3_PREFILL, P(d_ids), P(d_pre), None, None, None, sp)
+    be.forward_batch_dev(n, PRE, P(d_ids), P(d_pre), None, None, None, sp)
     e1.record(stream)
     torch.cuda.synchronize()
     be.profile(False)
@@ -261,8 +329,11 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     prefill_ms = e0.elapsed_time(e1)
     # tensor FLOPs of the prefill weight GEMMs (QKV, Wo, W1, W2; activations as
     # bf16 hi + lo: two products per multiply-add)
-    d, m = C3["n_embd"], C3["mlp_hidden"]
-    pf_flops = 2.0 * 2 * n * C3_PREFILL * C3["n_layer"] * (3 * d * d + d * d + 2 * d * m)
+    d, m, L = C["n_embd"], C["mlp_hidden"], C["n_layer"]
+    kvd = C["n_kv_head"] * C["head_dim"]
+    qd = C["n_head"] * C["head_dim"]
+    layer_w = qd * d + 2 * kvd * d + d * qd + 2 * d * m
+    pf_flops = 2.0 * 2 * n * PRE * L * layer_w
     pf_gemm_tf = pf_flops / (float(pf_ms[2]) * 1e-3) / 1e12 if pf_ms[2] > 0 else None
 
     # N > 1: each rank decodes its own sequences; NCCL gathers the logits of
@@ -282,7 +353,7 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    torch.cuda.nvtx.range_push("c3_decode")  # lets a profiler select the timed steps
+    torch.cuda.nvtx.range_push(f"{sp_['name']}_decode")  # lets a profiler select the timed steps
     with ClockSampler(local) as clk:
         step_ms = timed_steps(torch, stream, args.steps, lambda s: step(args.warmup + s), flush)
     torch.cuda.nvtx.range_pop()
@@ -306,7 +377,7 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
     value = world * n / (ms_per_step / 1000.0)
 
     # end to end through the public host API with pinned host buffers
-    base = C3_PREFILL + total_dec
+    base = PRE + total_dec
     h_tok = torch.from_numpy(np.ascontiguousarray(toks[:, base:base + e_steps].T)).pin_memory()
     h_ids = torch.arange(n, dtype=torch.int32).pin_memory()
     h_pos = (torch.arange(e_steps, dtype=torch.int32)[:, None] + base).expand(-1, n).contiguous().pin_memory()
@@ -330,37 +401,34 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_val = world * n * (e_steps - 1) / float(te.item())
 
-    kpl = kvpl = C3["n_embd"] // 2
-    L = C3["n_layer"]
-    positions = [C3_PREFILL + p0 + s for s in range(n_prof)]
-    attn_bytes = sum(n * L * (p + 1) * (kpl + kvpl + 8) for p in positions) / n_prof  # per step
+    positions = [PRE + p0 + s for s in range(n_prof)]
+    attn_bytes = sum(n * L * (p + 1) * sp_["kv_bytes_per_pos"] for p in positions) / n_prof  # per step
     attn_gbs = attn_bytes / (ph_ms[0] / 1000.0) / 1e9 if ph_ms[0] > 0 else None
-    nbf = sum([V * 768, 2048 * 768, L * (4 * 768 * 768 + 2 * 768 * 3072), V * 768])
-    gemm_bytes = (nbf - 2048 * 768 - V * 768) * 2  # per step: streamed weights (wte/wpe gathered, not streamed)
+    gemm_bytes = (L * layer_w + V * d) * 2  # per step: streamed weights (wte/wpe gathered, not streamed)
     gemm_gbs = gemm_bytes / (ph_ms[2] / 1000.0) / 1e9 if ph_ms[2] > 0 else None
     peaks = load_peaks()
     peak = peaks.get("hbm_gbs", 6650.0)
-    traffic = profiled_traffic("decode_attention_c3.txt")
+    traffic = profiled_traffic(sp_["profile"])
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config("c3", world),
+        "config": workload_config(sp_["name"], world),
         "collective": (f"NCCL all_gather of each rank's logits ({n} x {V} f32) per step" if world > 1 else None),
         "gpu_launches": int(graph_kernels * args.steps),
         "decode_step": "one CUDA graph per step" if graph_kernels else "eager",
         "kernels_per_step": int(graph_kernels),
-        "roofline": {"bound": "hbm", "kernel": "decode KV attention (scores + softmax + values over 4-bit codes)",
+        "roofline": {"bound": "hbm", "kernel": sp_["attn_kernel"],
                      "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
                      "frac": (attn_gbs / peak) if attn_gbs else None, "traffic": traffic,
                      "traffic_unit": "bytes per launch (one layer), ncu dram read+write",
                      "algorithmic_bytes_per_launch": attn_bytes / L,
                      "algorithmic_bytes_per_step": attn_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
-        "phases_ms_per_step": {"kv_attention": ph_ms[0], "tq_encode": ph_ms[1], "weight_gemms": ph_ms[2],
+        "phases_ms_per_step": {"kv_attention": ph_ms[0], "kv_encode": ph_ms[1], "weight_gemms": ph_ms[2],
                                "note": f"eager steps {p0}..{p0 + n_prof - 1} with CUDA events per phase"},
         "weight_gemm_gbs": gemm_gbs,
-        "prefill": {"tokens": n * C3_PREFILL, "ms": prefill_ms, "tokens_per_s": n * C3_PREFILL / (prefill_ms / 1000.0),
+        "prefill": {"tokens": n * PRE, "ms": prefill_ms, "tokens_per_s": n * PRE / (prefill_ms / 1000.0),
                     "weight_gemm_ms": float(pf_ms[2]),
                     "weight_gemm_tensor": {"achieved": pf_gemm_tf, "unit": "TFLOP/s",
                                            "peak": peaks.get("bf16_tflops", 1590.0),
@@ -369,6 +437,9 @@ def bench_c3(args, torch, dist, kgcuda, world, rank, local):
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(n * 4 * 3), "d2h_bytes_per_step": int(n * V * 4)},
         "clocks": clk.summary(),
     }
+    if sp_["keep"] > 0:
+        line["mlp_hook"] = {"keep": sp_["keep"], "note": "hidden activations after W1 replaced by Bernoulli(keep) "
+                                                          "N(0,1) values (the sparsity a trained TwELL model shows)"}
     be.close()
     return line
 
@@ -472,11 +543,11 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    fn = bench_c3 if args.workload == "c3" else bench_c2
+    fn = bench_c2 if args.workload == "c2" else bench_decode
     line = fn(args, torch, dist, kgcuda, world, rank, local)
     if rank == 0 and world == 1:
         try:
-            v, cores, sample = (cpu_sample_c3 if args.workload == "c3" else cpu_sample_c2)()
+            v, cores, sample = CPU_SAMPLE[args.workload]()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
         except Exception as ex:  # the baseline must not break the bench line
             line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": 0, "kind": "port", "sample": f"failed: {ex}"}

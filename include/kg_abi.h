@@ -222,6 +222,12 @@ int kg_profile(kg_ctx *ctx, int enable);
  * of every phase since the last read (ms[KG_PROF_N]) and the number of timed
  * intervals (count[KG_PROF_N]); resets the sums. */
 int kg_profile_read(kg_ctx *ctx, float *ms, int64_t *count);
+/* Benchmark input hook (no reference counterpart; the reference's TwELL
+ * benchmark forces sparse hidden activations): after W1 + ReLU of every layer
+ * the bf16 path replaces the hidden activations by a per-token Bernoulli(keep)
+ * mask with |N(0,1)| survivors, deterministic in (seed, layer, slot,
+ * position). keep <= 0 turns it off. Drops captured decode graphs. */
+int kg_set_mlp_hook(kg_ctx *ctx, float keep, uint64_t seed);
 /* Kernel launches replayed by the last kg_forward_batch(_dev) call when it ran
  * as a captured CUDA graph (single-position decode of the bf16 path on a
  * non-legacy stream, profiling off); 0 when that call ran eagerly. */

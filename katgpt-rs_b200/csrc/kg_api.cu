@@ -847,3 +847,17 @@ int kg_kv_restore(kg_ctx *ctx, int32_t seq, int32_t pos, const void *src_dev, vo
     }
     return KG_OK;
 }
+
+int kg_set_mlp_hook(kg_ctx *ctx, float keep, uint64_t seed) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (!ctx->big_path) return fail(ctx, KG_ERR_UNSUPPORTED, "the hook applies to the bf16 path");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    for (auto &gr : ctx->graphs) {  // captured with the previous setting
+        if (gr.stream) KG_CUDA(ctx, cudaStreamSynchronize(gr.stream));
+        if (gr.exec) cudaGraphExecDestroy(gr.exec);
+    }
+    ctx->graphs.clear();
+    ctx->hook_keep = keep > 0.0f ? std::min(keep, 1.0f) : 0.0f;
+    ctx->hook_seed = seed;
+    return KG_OK;
+}

@@ -447,31 +447,81 @@ __global__ void twell_kernel(const bf16 *hidden, const bf16 *hidden_lo, const in
                              const float *resid, float *out, int n, int m, float threshold) {
     pdl_wait();
     extern __shared__ int s_idx[];
-    __shared__ int s_cnt;
+    __shared__ int s_off[256];
     const int r = blockIdx.x;
     const int alive = row_alive[r];
     if (!((float)alive / (float)m <= 1.0f - threshold)) return;  // dense result stands
-    if (threadIdx.x == 0) s_cnt = 0;
-    __syncthreads();
     const bf16 *h = hidden + (int64_t)r * m;
     const bf16 *hl = hidden_lo ? hidden_lo + (int64_t)r * m : nullptr;
     float *s_val = reinterpret_cast<float *>(s_idx + m);
-    // pack alive indices (ascending order is not needed for an f32 sum)
-    for (int j = threadIdx.x; j < m; j += blockDim.x) {
-        float v = __bfloat162float(h[j]) + (hl ? __bfloat162float(hl[j]) : 0.0f);
+    // pack alive (> 0) indices in ascending order (simd_sparse_matmul_rows'
+    // packing): each thread scans a contiguous strip, a block scan places it
+    const int strip = (m + blockDim.x - 1) / blockDim.x, j0 = threadIdx.x * strip, j1 = min(m, j0 + strip);
+    int cnt = 0;
+    for (int j = j0; j < j1; ++j) cnt += (__bfloat162float(h[j]) + (hl ? __bfloat162float(hl[j]) : 0.0f)) > 0.0f;
+    s_off[threadIdx.x] = cnt;
+    __syncthreads();
+    for (int d = 1; d < (int)blockDim.x; d <<= 1) {  // inclusive scan of the strip counts
+        const int v = threadIdx.x >= d ? s_off[threadIdx.x - d] : 0;
+        __syncthreads();
+        s_off[threadIdx.x] += v;
+        __syncthreads();
+    }
+    int k = s_off[threadIdx.x] - cnt;
+    for (int j = j0; j < j1; ++j) {
+        const float v = __bfloat162float(h[j]) + (hl ? __bfloat162float(hl[j]) : 0.0f);
         if (v > 0.0f) {
-            int k = atomicAdd(&s_cnt, 1);
             s_idx[k] = j;
             s_val[k] = v;
+            ++k;
         }
     }
+    const int na = s_off[blockDim.x - 1];
     __syncthreads();
-    const int na = s_cnt;
     for (int c = threadIdx.x; c < n; c += blockDim.x) {
         float acc = 0.0f;
         for (int a = 0; a < na; ++a) acc += s_val[a] * __bfloat162float(w2t[(int64_t)s_idx[a] * n + c]);
         out[(int64_t)r * n + c] = acc + resid[(int64_t)r * n + c];
     }
+}
+
+// Benchmark hook: hidden activations after W1 replaced by a per-token
+// Bernoulli(keep) mask with |N(0, 1)| survivors (the c4 workload's ~90%-zero
+// hidden layer), deterministic in (seed, layer, slot, position, index); the
+// alive counts follow.
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {
+    x ^= x >> 30;
+    x *= 0xbf58476d1ce4e5b9ull;
+    x ^= x >> 27;
+    x *= 0x94d049bb133111ebull;
+    return x ^ (x >> 31);
+}
+__global__ void mlp_hook_kernel(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot, const int32_t *pos, int m,
+                                float keep, uint64_t seed, int layer) {
+    pdl_wait();
+    __shared__ int s_cnt;
+    const int r = blockIdx.x;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    const uint64_t key = mix64(seed ^ mix64(((uint64_t)layer << 48) ^ ((uint64_t)slot[r] << 24) ^ (uint64_t)pos[r]));
+    int cnt = 0;
+    for (int j = threadIdx.x; j < m; j += blockDim.x) {
+        const uint64_t a = mix64(key + 2 * (uint64_t)j), b = mix64(key + 2 * (uint64_t)j + 1);
+        const float u = (float)(a >> 40) * (1.0f / 16777216.0f);
+        float v = 0.0f;
+        if (u < keep) {  // Box-Muller on two more uniforms from b
+            const float u1 = ((float)(b >> 40) + 0.5f) * (1.0f / 16777216.0f);
+            const float u2 = (float)((b >> 16) & 0xffffff) * (1.0f / 16777216.0f);
+            v = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+            cnt += v != 0.0f;
+        }
+        const bf16 hv = __float2bfloat16_rn(v);
+        hid[(int64_t)r * m + j] = hv;
+        hid2[(int64_t)r * m + j] = __float2bfloat16_rn(v - __bfloat162float(hv));
+    }
+    atomicAdd(&s_cnt, cnt);
+    __syncthreads();
+    if (threadIdx.x == 0) row_alive[r] = s_cnt;
 }
 
 __global__ void softmax_kernel(const float *logits, float *probs, int V, float inv_temp) {
@@ -577,6 +627,11 @@ cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int
         if (e != cudaSuccess) return e;
     }
     return launch_pdl(twell_kernel, dim3(M), dim3(256), smem, s, hidden, hidden_lo, row_alive, w2t, resid, out, n, m, threshold);
+}
+cudaError_t mlp_hook(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot, const int32_t *pos, int m, int M,
+                     float keep, uint64_t seed, int layer, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    return launch_pdl(mlp_hook_kernel, dim3(M), dim3(256), 0, s, hid, hid2, row_alive, slot, pos, m, keep, seed, layer);
 }
 cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;

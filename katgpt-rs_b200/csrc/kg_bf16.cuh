@@ -76,6 +76,11 @@ cudaError_t delta_route(float *x, const float *xr, float *delta, const float *qu
                         int n, int M, int layer, cudaStream_t s);
 // TwELL (math.rs:315-355): for rows whose alive fraction <= 1 - threshold, recompute
 // out = sum over alive j of h[j] * W2[:, j] + resid (gather over W2^T rows) in f32.
+// Benchmark hook: replace post-ReLU hidden activations by a Bernoulli(keep)
+// mask with N(0,1) survivors (deterministic per layer, slot, position) and
+// recount alive entries.
+cudaError_t mlp_hook(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot, const int32_t *pos, int m, int M,
+                     float keep, uint64_t seed, int layer, cudaStream_t s);
 cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t, const float *resid,
                             float *out, int n, int m, int M, float threshold, cudaStream_t s);
 // softmax_scaled (math.rs:36-50) per row of logits [M x V]

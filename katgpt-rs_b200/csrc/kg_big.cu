@@ -288,6 +288,8 @@ cudaError_t big_download(kg_ctx *ctx, float *dst, int64_t offset, int64_t count)
 
 namespace {
 
+constexpr int kTwellMaxRows = 32;  // rows per call up to which sparse rows take the gather path
+
 bf::Gemm gemm0() {
     bf::Gemm q;
     std::memset(&q, 0, sizeof(q));
@@ -448,14 +450,23 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(gemm_split(ctx, u, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
+        if (ctx->hook_keep > 0.0f)  // benchmark hook: ~(1 - keep) of the hidden activations exactly zero
+            BIG_TRY(bf::mlp_hook(g.hid, g.hid2, g.alive, g.slot_of, g.pos_of, m, M, ctx->hook_keep, ctx->hook_seed, l,
+                                 s));
         bf::Gemm dn = gemm0();
         dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
         dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(gemm_split(ctx, dn, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
-        BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
-                                    c.sparse_threshold, s));
+        // TwELL (math.rs:315-355): rows at or under the alive threshold are
+        // recomputed as a compressed-index gather over W2^T rows. With many rows
+        // per call the dense product (one weight stream for all rows) stands:
+        // it is the same sum in another order, and cheaper than one gather of
+        // ~alive rows of W2^T per token.
+        if (M <= kTwellMaxRows)
+            BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
+                                        c.sparse_threshold, s));
         if (!spkv) BIG_TRY(bf::delta_route(g.x, g.xr, g.delta, g.dq + (int64_t)l * n, g.dn + (int64_t)l * n, n, M, l, s));
     }
     return cudaSuccess;

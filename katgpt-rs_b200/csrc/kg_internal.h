@@ -172,6 +172,8 @@ struct kg_ctx {
     std::vector<void *> allocs;
     std::vector<uint8_t> slot_used;  // kg_seq_alloc / kg_seq_free bookkeeping
     __half *enc_rh = nullptr, *enc_rl = nullptr;  // f16 hi / lo of R for kg_tq_encode (codec contexts)
+    float hook_keep = 0.0f;                       // kg_set_mlp_hook (benchmark input), 0 = off
+    uint64_t hook_seed = 0;
 };
 
 namespace kg {

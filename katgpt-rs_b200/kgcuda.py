@@ -92,6 +92,7 @@ def lib():
             "kg_kv_snapshot_bytes": (I64, [P, I32]),
             "kg_kv_snapshot": (ctypes.c_int, [P, I32, I32, P, P]),
             "kg_kv_restore": (ctypes.c_int, [P, I32, I32, P, P]),
+            "kg_set_mlp_hook": (ctypes.c_int, [P, F32, ctypes.c_uint64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -277,6 +278,10 @@ class CudaBackend:
 
     def kv_restore(self, seq, pos, src_dev, stream=None):
         self._check(lib().kg_kv_restore(self._h, seq, pos, ctypes.c_void_p(src_dev), stream))
+
+    def set_mlp_hook(self, keep, seed=0):
+        """Benchmark hook: Bernoulli(keep) sparse hidden activations after W1 (0 = off)."""
+        self._check(lib().kg_set_mlp_hook(self._h, keep, seed))
 
     def graph_kernels(self):
         """Kernel launches replayed by the last forward call's CUDA graph (0: eager)."""
