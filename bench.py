@@ -219,7 +219,7 @@ def workload_config(workload, world):
     if workload == "c4":
         return {"workload": "c4: n_layer 24, n_embd 2048, 16 heads, mlp 8192, vocab 32000 (assumed), bf16 weights "
                             "N(0,0.02), standard attention with a bf16 KV cache, TwELL with ~90%-zero hidden "
-                            "activations (benchmark hook: per-token Bernoulli keep 0.1, N(0,1) survivors); "
+                            "activations (benchmark hook: per-token Bernoulli keep 0.1, |N(0,1)| survivors (post-ReLU)); "
                             "512 sequences, 512-token prefill then teacher-forced decode",
                 "global_batch": world * C4_SEQS, "seq_len": C4_PREFILL, "parallelism": f"dp{world} (sequence shards)",
                 "l2": "flushed between steps (256 MiB write, outside the timed events)"}
@@ -439,7 +439,7 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
     }
     if sp_["keep"] > 0:
         line["mlp_hook"] = {"keep": sp_["keep"], "note": "hidden activations after W1 replaced by Bernoulli(keep) "
-                                                          "N(0,1) values (the sparsity a trained TwELL model shows)"}
+                                                          "|N(0,1)| values (post-ReLU activations are non-negative; the sparsity a trained TwELL model shows)"}
     be.close()
     return line
 

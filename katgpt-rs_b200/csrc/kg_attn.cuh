@@ -52,6 +52,28 @@ struct FlashArgs {
 
 cudaError_t decode_attn(const DecodeAttnArgs &a, cudaStream_t s);
 
+// Decode attention of M single-token queries over 4-bit / 3-bit codes as two
+// streaming kernels (kg_tqattn.cu): scores per 32-position unit, then values
+// per block of dims. E, cmax and csum are scratch of [M][nh][Sp] f16 and
+// [M][nc16][nh] f32 (one entry per 16 positions), Sp = tq_padded_len(B),
+// nc16 = Sp / 16.
+struct TqAttnArgs {
+    const uint8_t *kcodes, *vcodes;   // [slot][layer][pos][kvd / 2]
+    const float *knorm, *vnorm;       // [slot][layer][pos]
+    const float *kcent, *vcent;       // 16 centroids each (zero-padded)
+    const __half *qrot;               // q~ [M][nh][kvd] (f16)
+    const int32_t *slot, *pos;        // per token
+    __half *E;                        // exp(s - chunk max) * norm_v [M][nh][Sp]
+    float *cmax, *csum;               // chunk maxima and sums [M][nc16][nh]
+    __half *U, *U_lo;                 // u~ [M][nh][kvd], f16 hi / lo
+    int *err;                         // device error word (timeouts)
+    int M, nh, kvd, kpl, vpl, L, B, layer, Sp, nc16;
+    float scale;
+    int rsk;                          // set by the launcher
+};
+int tq_padded_len(int block_size);
+cudaError_t tq_decode_attn(const TqAttnArgs &a, cudaStream_t s);
+
 // Standard attention over a bf16 K/V cache [slot][layer][pos][kvd].
 struct StdDecodeArgs {
     const float *Q;              // f32 query rows (column 0 of qkv), scaled inside

@@ -512,8 +512,8 @@ __global__ void mlp_hook_kernel(bf16 *hid, bf16 *hid2, int *row_alive, const int
         if (u < keep) {  // Box-Muller on two more uniforms from b
             const float u1 = ((float)(b >> 40) + 0.5f) * (1.0f / 16777216.0f);
             const float u2 = (float)((b >> 16) & 0xffffff) * (1.0f / 16777216.0f);
-            v = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-            cnt += v != 0.0f;
+            v = fabsf(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));  // post-ReLU: non-negative
+            cnt += v > 0.0f;
         }
         const bf16 hv = __float2bfloat16_rn(v);
         hid[(int64_t)r * m + j] = hv;

@@ -77,7 +77,8 @@ cudaError_t delta_route(float *x, const float *xr, float *delta, const float *qu
 // TwELL (math.rs:315-355): for rows whose alive fraction <= 1 - threshold, recompute
 // out = sum over alive j of h[j] * W2[:, j] + resid (gather over W2^T rows) in f32.
 // Benchmark hook: replace post-ReLU hidden activations by a Bernoulli(keep)
-// mask with N(0,1) survivors (deterministic per layer, slot, position) and
+// mask with |N(0,1)| survivors (the hidden activation is post-ReLU, and the
+// gather counts only entries > 0; deterministic per layer, slot, position) and
 // recount alive entries.
 cudaError_t mlp_hook(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot, const int32_t *pos, int m, int M,
                      float keep, uint64_t seed, int layer, cudaStream_t s);

@@ -93,6 +93,7 @@ int big_supported(const kg_config &c, std::string &why) {
     if (c.kv_mode != KG_KV_F32)
         for (int b : {c.key_bits, c.val_bits})
             if (b != 3 && b != 4) return why = "the bf16 path packs 3/4-bit codes", -1;
+    if (c.kv_mode != KG_KV_F32 && c.block_size > 6144) return why = "quantized-KV decode attention: block_size <= 6144", -1;
     if (c.n_kv_head < 1 || c.n_head % c.n_kv_head) return why = "n_head must be a multiple of n_kv_head", -1;
     const int kvd = c.n_kv_head * c.head_dim;
     if (kvd % 64) return why = "kv_dim must be a multiple of 64", -1;
@@ -178,6 +179,10 @@ cudaError_t big_init(kg_ctx *ctx) {
         BIG_TRY(cudaStreamSynchronize(ctx->stream));
         return cudaSuccess;
     }
+    g.Sp = attn::tq_padded_len((int)B);
+    BIG_TRY(dalloc(&g.pe, S * ctx->nh * g.Sp, own));
+    BIG_TRY(dalloc(&g.pmax, S * (g.Sp / 16) * ctx->nh, own));
+    BIG_TRY(dalloc(&g.psum, S * (g.Sp / 16) * ctx->nh, own));
     // centroid tables
     BIG_TRY(dalloc(&g.kcent, 16, own));
     BIG_TRY(dalloc(&g.vcent, 16, own));
@@ -415,15 +420,16 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             r.M = M; r.N = kvd; r.K = hd; r.batch = nh;
             r.epi = bf::EPI_OUT; r.Cb = g.qrot; r.Cb2 = g.qrot2; r.ldcb = (int64_t)nh * kvd; r.sCb = kvd;
             BIG_TRY(gemm_split(ctx, r, s));
-            attn::DecodeAttnArgs da;
-            da.kcodes = g.kcodes; da.vcodes = g.vcodes; da.knorm = g.knorm; da.vnorm = g.vnorm;
-            da.kcent = g.kcent; da.vcent = g.vcent; da.qrot = g.qrot; da.qrot_lo = g.qrot2;
-            da.slot = g.slot_of; da.pos = g.pos_of; da.U = g.U; da.U_lo = g.U2;
-            da.M = M; da.nh = nh; da.kvd = kvd; da.kpl = (int)ctx->kpl; da.vpl = (int)ctx->vpl;
-            da.L = L; da.B = B; da.layer = l; da.scale = scale;
-            da.maps = g.has_maps ? &g.maps : nullptr; da.lutk = g.lutk; da.lutv = g.lutv; da.err = ctx->d_err;
+            attn::TqAttnArgs ta;
+            ta.kcodes = g.kcodes; ta.vcodes = g.vcodes; ta.knorm = g.knorm; ta.vnorm = g.vnorm;
+            ta.kcent = g.kcent; ta.vcent = g.vcent; ta.qrot = g.qrot;
+            ta.slot = g.slot_of; ta.pos = g.pos_of; ta.E = g.pe; ta.cmax = g.pmax; ta.csum = g.psum;
+            ta.U = g.U; ta.U_lo = g.U2;
+            ta.M = M; ta.nh = nh; ta.kvd = kvd; ta.kpl = (int)ctx->kpl; ta.vpl = (int)ctx->vpl;
+            ta.L = L; ta.B = B; ta.layer = l; ta.Sp = g.Sp; ta.nc16 = g.Sp / 16; ta.scale = scale;
+            ta.err = ctx->d_err;
             prof_mark(ctx, KG_PROF_ATTN, 0, s);
-            BIG_TRY(attn::decode_attn(da, s));
+            BIG_TRY(attn::tq_decode_attn(ta, s));
             prof_mark(ctx, KG_PROF_ATTN, 1, s);
             // out_h = R[:, head cols]^T u~_h
             bf::Gemm o = gemm0();

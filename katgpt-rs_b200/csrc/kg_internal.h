@@ -118,6 +118,11 @@ struct BigState {
     bool std_kv = false;
     __nv_bfloat16 *kcache = nullptr, *vcache = nullptr;
     uint2 *lutk = nullptr, *lutv = nullptr;
+    // two-kernel decode attention scratch: e rows [max_seqs][nh][Sp] and
+    // 16-position chunk maxima / sums [max_seqs][Sp / 16][nh]
+    __half *pe = nullptr;
+    float *pmax = nullptr, *psum = nullptr;
+    int Sp = 0;
 };
 int big_supported(const kg_config &c, std::string &why);
 }  // namespace kg

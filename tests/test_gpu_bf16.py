@@ -18,14 +18,14 @@ def rel_err(a, b):
     return np.abs(a - b).max(axis=-1) / den
 
 
-def make(kg, mode=1, **shape):
+def make(kg, mode=1, std=0.05, **shape):
     base = dict(vocab_size=96, block_size=64, n_embd=128, n_head=2, head_dim=64, n_kv_head=2,
                 mlp_hidden=256, n_layer=4, key_bits=4, val_bits=4, kv_mode=mode,
                 weight_dtype=kg.KG_W_BF16, max_seqs=4)
     base.update(shape)
     cfg = kg.micro_config(**base)
     be = kg.CudaBackend(cfg)
-    w = kg.bf16_round(kg.reference_weights(cfg, seed=11, scale_mode=1, std=0.05))
+    w = kg.bf16_round(kg.reference_weights(cfg, seed=11, scale_mode=1, std=std))
     be.compile(w)
     return cfg, be, w
 
@@ -158,5 +158,35 @@ def test_standard_attention_matches_oracle(kg, orc, shape):
         err = rel_err(got[i], ref)
         print("standard %s seq %d: max rel err prefill %.2e decode %.2e" % (shape.get("n_embd", 128), i,
                                                                           err[:T0].max(), err[T0:].max()))
+        assert err.max() <= REL_BF16
+    be.close()
+
+
+@pytest.mark.parametrize("shape", [
+    dict(n_embd=192, n_head=3, head_dim=64, n_kv_head=3, mlp_hidden=384),      # kv_dim 192: 64-dim value blocks
+    dict(n_embd=1024, n_head=16, head_dim=64, n_kv_head=16, mlp_hidden=1024),  # four warps per score unit
+    dict(n_embd=1280, n_head=20, head_dim=64, n_kv_head=20, mlp_hidden=1024),  # > 16 heads: streaming scores
+    dict(n_embd=768, n_head=12, head_dim=64, n_kv_head=12, mlp_hidden=768, key_bits=3, val_bits=3),  # 3-bit
+])
+def test_quantized_attention_shapes(kg, orc, shape):
+    # the decode attention kernels' shape variants against forward_quantized;
+    # 70 positions so a token spans three 32-position units. Weights N(0, 0.02):
+    # the device's f32 rounding differs from the reference's in the last bits,
+    # so a coordinate lying on a codebook boundary can take the neighbouring
+    # code (the encoder itself is bit-exact on equal inputs); wider weights
+    # make one such flip move the logits by up to a few percent
+    shape = dict(shape)
+    kb, vb = shape.pop("key_bits", 4), shape.pop("val_bits", 4)
+    cfg, be, w = make(kg, 1, std=0.02, vocab_size=128, block_size=96, n_layer=2, key_bits=kb, val_bits=vb, **shape)
+    n_seq, T0, T1 = 2, 60, 10
+    toks = tokens(n_seq, T0 + T1, cfg.vocab_size, seed=23)
+    pre = be.forward_batch(toks[:, :T0])
+    dec = [be.forward_batch(toks[:, t:t + 1], start_pos=np.full(n_seq, t))[:, 0] for t in range(T0, T0 + T1)]
+    got = np.concatenate([pre, np.stack(dec, axis=1)], axis=1)
+    for i in range(n_seq):
+        ref = orc.run_sequence(orc.from_kg(cfg), 1, w, toks[i], key_bits=kb, val_bits=vb)[0]
+        err = rel_err(got[i], ref)
+        print("quantized %d/%d heads seq %d: max rel err prefill %.2e decode %.2e" % (
+            cfg.n_head, cfg.n_embd, i, err[:T0].max(), err[T0:].max()))
         assert err.max() <= REL_BF16
     be.close()
