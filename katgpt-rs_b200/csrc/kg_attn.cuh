@@ -1,4 +1,4 @@
-// kg_attn.cuh — attention kernels over the TurboQuant KV cache (kg_attn.cu).
+// kg_attn.cuh — attention kernels (kg_attn.cu, kg_tqattn.cu).
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -12,36 +12,6 @@ namespace attn {
 
 // Arena layout: codes [slot][layer][pos][pl], norms [slot][layer][pos].
 // Operands marked hi/lo are f16 splits of f32 values (x = hi + lo).
-// Decode attention of M single-token queries over the cached codes:
-// U[m, h] = u~ = sum_t softmax_t(s)[t] * norm_v[t] * centroid(code_v[t]) with
-// s[t] = norm_k[t] * scale * <centroid(code_k[t]), q~_h>, f16 hi/lo out.
-// Tensor maps of the TMA decode kernel (kv_dim a multiple of 256), built once
-// per context: key / value code arenas as [rows x pl] bytes, q~ hi / lo as
-// [tokens * heads x kv_dim] f16.
-struct AttnMaps {
-    CUtensorMap kc, kt, vc, qh, ql;  // key codes as 32-byte columns and as 16-row tiles
-};
-bool decode_attn_maps(AttnMaps *maps, const uint8_t *kcodes, const uint8_t *vcodes, int64_t rows, int kpl, int vpl,
-                      const __half *qrot, const __half *qrot_lo, int64_t qrows, int kvd, int nh);
-// the replicated byte tables of both codebooks (2048 uint2 each: 8 replicas)
-cudaError_t build_luts(const float *kcent, const float *vcent, uint2 *lutk, uint2 *lutv, cudaStream_t s);
-
-struct DecodeAttnArgs {
-    const uint8_t *kcodes, *vcodes;   // [slot][layer][pos][pl]
-    const float *knorm, *vnorm;       // [slot][layer][pos]
-    const float *kcent, *vcent;       // 16 centroids each
-    const __half *qrot, *qrot_lo;     // [M][nh][kvd]
-    const int32_t *slot, *pos;        // per token
-    __half *U, *U_lo;                 // [M][nh][kvd]
-    int M, nh, kvd, kpl, vpl, L, B, layer;
-    float scale;
-    const AttnMaps *maps;             // host copy; null: the cp.async kernel
-    const uint2 *lutk, *lutv;         // replicated tables (TMA kernel)
-    int *err;                         // device error word (timeouts)
-    // set by the launcher
-    int nbg, ndg, chmax, sstage, vrow, vstage, off_ring, off_S, off_P, off_small, off_part;
-    int off_q, sstage_a;              // resident-q~ variant: q~ region, per-warp key tile slot
-};
 struct FlashArgs {
     const __half *Q, *Q_lo, *K, *K_lo, *V, *V_lo;  // rows = tokens (sequence-major, T per sequence)
     float *O;
@@ -49,8 +19,6 @@ struct FlashArgs {
     int n_seq, T, nh, nkv, hd;
     float scale;
 };
-
-cudaError_t decode_attn(const DecodeAttnArgs &a, cudaStream_t s);
 
 // Decode attention of M single-token queries over 4-bit / 3-bit codes as two
 // streaming kernels (kg_tqattn.cu): scores per 32-position unit, then values

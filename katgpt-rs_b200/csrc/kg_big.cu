@@ -191,11 +191,6 @@ cudaError_t big_init(kg_ctx *ctx) {
     std::copy(ctx->h_vc.begin(), ctx->h_vc.end(), vc.begin());
     BIG_TRY(cudaMemcpy(g.kcent, kc.data(), 64, cudaMemcpyHostToDevice));
     BIG_TRY(cudaMemcpy(g.vcent, vc.data(), 64, cudaMemcpyHostToDevice));
-    BIG_TRY(dalloc(&g.lutk, 4096, own));
-    BIG_TRY(dalloc(&g.lutv, 4096, own));
-    BIG_TRY(attn::build_luts(g.kcent, g.vcent, g.lutk, g.lutv, ctx->stream));
-    g.has_maps = attn::decode_attn_maps(&g.maps, g.kcodes, g.vcodes, (int64_t)S * L * B, (int)ctx->kpl, (int)ctx->vpl,
-                                        g.qrot, g.qrot2, (int64_t)S * ctx->nh, kvd, (int)ctx->nh);
     // f16 hi/lo splits of the rotation for the tensor-core GEMMs
     BIG_TRY(bf::f32_to_f16_split(ctx->rot, kvd * kvd, g.rot_h, g.rot_l, ctx->stream));
     BIG_TRY(bf::f32_to_f16_split(ctx->rot_t, kvd * kvd, g.rot_th, g.rot_tl, ctx->stream));

@@ -110,14 +110,9 @@ struct BigState {
     float *yrot = nullptr;                  // rotated rows from the GEMM, before the fix-up
     int *alive = nullptr;
     int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;
-    // TMA decode attention: tensor maps over the code arenas and q~, and the
-    // replicated centroid tables (has_maps false: the cp.async kernel runs)
-    attn::AttnMaps maps;
-    bool has_maps = false;
     // standard attention (kv_mode KG_KV_F32): bf16 K/V cache [slot][layer][pos][kv_dim]
     bool std_kv = false;
     __nv_bfloat16 *kcache = nullptr, *vcache = nullptr;
-    uint2 *lutk = nullptr, *lutv = nullptr;
     // two-kernel decode attention scratch: e rows [max_seqs][nh][Sp] and
     // 16-position chunk maxima / sums [max_seqs][Sp / 16][nh]
     __half *pe = nullptr;
