@@ -37,6 +37,7 @@ struct TqAttnArgs {
     int *err;                         // device error word (timeouts)
     int M, nh, kvd, kpl, vpl, L, B, layer, Sp, nc16;
     float scale;
+    int rsk;                          // set by the launcher
 };
 int tq_padded_len(int block_size);
 cudaError_t tq_decode_attn(const TqAttnArgs &a, cudaStream_t s);

@@ -13,11 +13,12 @@
 // mma.sync m16n8k16 runs with positions as M, heads as N and dims as K. Per
 // 16-position chunk c the kernel writes the head maxima c_h, the sums
 // l_h = sum_t exp(s - c_h) and e[h,t] = exp(s - c_h) * norm_v[t] (f16).
-//   tq_scores_kernel: CTA = (segment of a token's units, token) of G warps
-//     that split the 64-dim blocks and keep their q~ fragments in registers;
-//     each warp streams its columns of the unit's code rows through its own
-//     cp.async ring, the warps exchange partial sums through shared memory and
-//     each finalises its share of the (m-tile, head-tile) pieces.
+//   tq_scores_kernel: CTA = (segment of a token's units, token); two groups of
+//     G warps, each group owning two shared-memory unit buffers filled by
+//     bulk copies (one row per lane) on an mbarrier; the warps of a group split
+//     the 64-dim blocks and keep their q~ fragments in registers, exchange the
+//     partial sums through shared memory and each finalises its share of the
+//     (m-tile, head-tile) pieces.
 //   tq_scores_stream_kernel (shapes whose q~ does not fit in registers): CTA =
 //     (128-position chunk, token), every warp streams its 32 rows' code bytes
 //     into registers, q~ through L1.
@@ -87,9 +88,27 @@ __device__ __forceinline__ void build_lut32(uint32_t *lut, const float *cent) {
         reinterpret_cast<uint4 *>(lut)[i] = make_uint4(v, v, v, v);
     }
 }
-// table entry of byte k (0..3) of w for this lane (lutl = table + lane)
-__device__ __forceinline__ uint32_t lk(const uint32_t *lutl, uint32_t w, int k) {
-    return lutl[__byte_perm(w, 0u, 0x4440u | (uint32_t)k) << 5];
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t addr) { return __uint_as_float(lds32(addr)); }
+template <typename CW>
+__device__ __forceinline__ CW lds_cw(uint32_t addr);
+template <>
+__device__ __forceinline__ uint2 lds_cw<uint2>(uint32_t addr) { return lds64(addr); }
+template <>
+__device__ __forceinline__ uint32_t lds_cw<uint32_t>(uint32_t addr) { return lds32(addr); }
+// table entry of byte k (0..3) of w for this lane (lut_lane = shared address
+// of the table + 4 lane)
+__device__ __forceinline__ uint32_t lk(uint32_t lut_lane, uint32_t w, int k) {
+    return lds32(lut_lane + (__byte_perm(w, 0u, 0x4440u | (uint32_t)k) << 7));
 }
 __device__ __forceinline__ uint32_t word_of(const uint2 &v, int wi) { return wi == 0 ? v.x : v.y; }
 __device__ __forceinline__ uint32_t word_of(const uint32_t &v, int) { return v; }
@@ -145,33 +164,27 @@ __device__ __forceinline__ void finalize_piece(const TqAttnArgs &a, const float 
 }
 
 // ---------------------------------------------------------------------------
-// Scores, q~ resident in registers: a CTA of G warps walks units u0 .. u1 - 1
-// of one token; warp w owns the 64-dim blocks [w bpw, (w + 1) bpw), copies
-// just those columns of each unit's 32 code rows into its own ring of NBUF
-// slots (cp.async, rows of RSW bytes), and the warps exchange partial sums
-// through shared memory once per unit. Dynamic shared memory: table (32 KB) |
-// rings [G][NBUF][32 rows][rsw] | partial sums [2][G][8 NT][32 lanes] f32.
-template <int NT, int G, int MAXB, int NBUF>
-struct ScoresShape {
-    static constexpr int THREADS = 32 * G, NV = 8 * NT;
-    __host__ __device__ static int rsw(int bpw) { return 32 * bpw + (bpw % 2 == 0 ? 32 : 0); }  // 8 or 24 (mod 32) words
-    static size_t smem(int bpw) {
-        return (size_t)LUT32 * 4 + (size_t)G * NBUF * 32 * rsw(bpw) + (size_t)2 * G * NV * 32 * 4;
-    }
-};
-template <int NT, int G, int MAXB, int NBUF>
-__global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
-    using SS = ScoresShape<NT, G, MAXB, NBUF>;
-    constexpr int NV = SS::NV;  // accumulators per lane
+// Scores, q~ resident in registers. Dynamic shared memory: table (32 KB) |
+// unit buffers [2 groups][2][32 rows][rsk] | partial sums
+// [2 groups][2][G warps][8 NT][32 lanes] f32 | mbarriers [2][2].
+template <int NT, int G, int MAXB>
+__global__ void __launch_bounds__(64 * G) tq_scores_kernel(const TqAttnArgs a) {
+    constexpr int NV = 8 * NT;  // accumulators per lane
     extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ int s_abort;
     uint32_t *lut = reinterpret_cast<uint32_t *>(dsm);
-    const int tid = threadIdx.x, lane = tid & 31, wig = tid >> 5, g = lane >> 2, t = lane & 3;
-    const int nblk = a.kvd >> 6;
-    const int bpw = (nblk + G - 1) / G;
-    const int rsw = SS::rsw(bpw);
-    uint8_t *ring = dsm + LUT32 * 4 + wig * NBUF * 32 * rsw;
-    float *part = reinterpret_cast<float *>(dsm + LUT32 * 4 + G * NBUF * 32 * rsw);
+    const int rsk = a.rsk;
+    uint8_t *bufs = dsm + LUT32 * 4;
+    float *part = reinterpret_cast<float *>(bufs + 4 * 32 * rsk);
+    uint64_t *full = reinterpret_cast<uint64_t *>(part + 2 * 2 * G * NV * 32);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int grp = warp / G, wig = warp % G;
     build_lut32(lut, a.kcent);  // constant input: overlaps the previous kernel
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < 4; ++i) as::mbar_init(full + i, 1);
+        as::mbar_fence_init();
+    }
     pdl_wait();
     const int m = blockIdx.y;
     const int tn = a.pos[m] + 1;
@@ -180,8 +193,12 @@ __global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
     const int u0 = blockIdx.x * per, u1 = min(nu, u0 + per);
     if (u0 >= u1) return;  // whole CTA
     __syncthreads();
-    const int nj = u1 - u0;
+    const int nj = u1 - u0 > grp ? (u1 - u0 - grp + 1) >> 1 : 0;  // units u0 + grp + 2 j of this group
+    if (nj == 0) return;  // this group has no unit (its warps take no further barrier)
     const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+    const uint8_t *codes = a.kcodes + rbase * a.kpl;
+    const int nblk = a.kvd >> 6;
+    const int bpw = (nblk + G - 1) / G;
     const int b0 = wig * bpw, nbw = max(0, min(nblk, b0 + bpw) - b0);
     // q~ fragments of this warp's blocks: dims 64 b + 16 t .. + 15 of head 8 jj + g
     uint32_t qf[MAXB][NT][8];
@@ -203,38 +220,26 @@ __global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
                 }
             }
     }
-    const uint32_t *lutl = lut + lane;
-    // copy plan: the warp's nbw * 32 bytes of each of the unit's 32 rows,
-    // 2 * nbw 16-byte chunks per row
-    const int cpr = 2 * nbw, nch = 32 * cpr;
-    const uint8_t *src0 = a.kcodes + rbase * a.kpl + 32 * b0;
-    const uint32_t ring_s = as::sa(ring);
-    // chunk c = lane + 32 r of a unit: row c / cpr, 16-byte piece c % cpr
-    int c_row[2 * MAXB], c_piece[2 * MAXB];
-#pragma unroll
-    for (int r = 0; r < 2 * MAXB; ++r) {
-        const int c = lane + 32 * r;
-        c_row[r] = c < nch ? c / cpr : -1;
-        c_piece[r] = c < nch ? c - c_row[r] * cpr : 0;
-    }
+    const uint32_t lutl = as::sa(lut) + 4 * lane;
+    uint8_t *gbuf = bufs + grp * 2 * 32 * rsk;
+    const uint32_t gbuf_s = as::sa(gbuf) + g * rsk + 8 * t;  // row g, byte 8 t of buffer 0
+    uint64_t *gfull = full + 2 * grp;
+    float *gpart = part + grp * 2 * G * NV * 32;
+    // leader warp: bulk-copy the rows of unit j (one per lane) into buffer j & 1
     auto issue = [&](int j) {
-        const int p0 = 32 * (u0 + j);
-        const uint32_t so = ring_s + (uint32_t)(j % NBUF) * 32 * rsw;
-#pragma unroll
-        for (int r = 0; r < 2 * MAXB; ++r)
-            if (c_row[r] >= 0)
-                cp_async16(so + c_row[r] * rsw + 16 * c_piece[r],
-                           src0 + (int64_t)min(p0 + c_row[r], tn - 1) * a.kpl + 16 * c_piece[r]);
+        const int slot = j & 1, p0 = 32 * (u0 + grp + 2 * j), rows = min(32, tn - p0);
+        if (lane == 0) as::mbar_expect_tx(gfull + slot, (uint32_t)(rows * a.kpl));
+        __syncwarp();
+        if (lane < rows)
+            as::bulk_load(gbuf + (slot * 32 + lane) * rsk, codes + (int64_t)(p0 + lane) * a.kpl, (uint32_t)a.kpl,
+                          gfull + slot);
     };
-#pragma unroll
-    for (int j = 0; j < NBUF - 1; ++j) {
-        if (j < nj) issue(j);
-        cp_commit();
+    if (wig == 0) {
+        issue(0);
+        if (nj > 1) issue(1);
     }
     for (int j = 0; j < nj; ++j) {
-        const int p0 = 32 * (u0 + j);
-        if (j + NBUF - 1 < nj) issue(j + NBUF - 1);
-        cp_commit();
+        const int slot = j & 1, p0 = 32 * (u0 + grp + 2 * j);
         // norms of rows p0 + 8 i + g (i = 0..3), loaded while the unit computes
         float kn[4], vn[4];
 #pragma unroll
@@ -243,8 +248,6 @@ __global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
             kn[i] = __ldg(a.knorm + rbase + p) * a.scale;
             vn[i] = __ldg(a.vnorm + rbase + p);
         }
-        cp_wait<NBUF - 1>();
-        __syncwarp();
         // two accumulator sets (even / odd blocks) keep independent MMA chains in flight
         float acc[2][2][NT][4];
 #pragma unroll
@@ -255,38 +258,40 @@ __global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
                 for (int jj = 0; jj < NT; ++jj)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc[q][mt][jj][e] = 0.0f;
-        const uint8_t *st = ring + (j % NBUF) * 32 * rsw + g * rsw + 8 * t;
+        const bool ok = as::mbar_wait(gfull + slot, (uint32_t)((j >> 1) & 1), &s_abort, a.err);
+        if (__all_sync(0xffffffffu, ok)) {
+            const uint32_t st = gbuf_s + slot * 32 * rsk + 32 * b0;
 #pragma unroll
-        for (int bi = 0; bi < MAXB; ++bi) {
-            if (bi < nbw) {
-                uint2 c[4];
+            for (int bi = 0; bi < MAXB; ++bi) {
+                if (bi < nbw) {
+                    uint2 c[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) c[i] = *reinterpret_cast<const uint2 *>(st + 8 * i * rsw + 32 * bi);
+                    for (int i = 0; i < 4; ++i) c[i] = lds64(st + 8 * i * rsk + 32 * bi);
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const int k0 = (2 * s) & 3;
+                    for (int s = 0; s < 4; ++s) {
+                        const int k0 = (2 * s) & 3;
 #pragma unroll
-                    for (int mt = 0; mt < 2; ++mt) {
-                        const uint32_t wl = s < 2 ? c[2 * mt].x : c[2 * mt].y;
-                        const uint32_t wh = s < 2 ? c[2 * mt + 1].x : c[2 * mt + 1].y;
-                        const uint32_t a0 = lk(lutl, wl, k0), a2 = lk(lutl, wl, k0 + 1);
-                        const uint32_t a1 = lk(lutl, wh, k0), a3 = lk(lutl, wh, k0 + 1);
+                        for (int mt = 0; mt < 2; ++mt) {
+                            const uint32_t wl = s < 2 ? c[2 * mt].x : c[2 * mt].y;
+                            const uint32_t wh = s < 2 ? c[2 * mt + 1].x : c[2 * mt + 1].y;
+                            const uint32_t a0 = lk(lutl, wl, k0), a2 = lk(lutl, wl, k0 + 1);
+                            const uint32_t a1 = lk(lutl, wh, k0), a3 = lk(lutl, wh, k0 + 1);
 #pragma unroll
-                        for (int jj = 0; jj < NT; ++jj)
-                            mma16816(acc[bi & 1][mt][jj], a0, a1, a2, a3, qf[bi][jj][2 * s], qf[bi][jj][2 * s + 1]);
+                            for (int jj = 0; jj < NT; ++jj)
+                                mma16816(acc[bi & 1][mt][jj], a0, a1, a2, a3, qf[bi][jj][2 * s], qf[bi][jj][2 * s + 1]);
+                        }
                     }
                 }
             }
         }
-        __syncwarp();  // the slot is refilled by the next issue
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
             for (int jj = 0; jj < NT; ++jj)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[0][mt][jj][e] += acc[1][mt][jj][e];
-        // exchange partial sums (double-buffered by unit parity)
-        float *pp = part + (j & 1) * G * NV * 32;
+        // exchange partial sums, then refill the buffer
+        float *pp = gpart + (j & 1) * G * NV * 32;
         if (G > 1) {
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
@@ -294,8 +299,11 @@ __global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
                 for (int jj = 0; jj < NT; ++jj)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) pp[(wig * NV + (mt * NT + jj) * 4 + e) * 32 + lane] = acc[0][mt][jj][e];
-            __syncthreads();
+            bar_named(1 + grp, 32 * G);
+        } else {
+            __syncwarp();
         }
+        if (wig == 0 && j + 2 < nj && !__any_sync(0xffffffffu, s_abort != 0)) issue(j + 2);
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -315,7 +323,6 @@ __global__ void __launch_bounds__(32 * G) tq_scores_kernel(const TqAttnArgs a) {
                 finalize_piece(a, d, m, p0 + 16 * mt, jj, g, t, tn, knp, vnp);
             }
     }
-    cp_wait<0>();
 }
 
 // Scores for shapes whose q~ does not fit in registers: CTA = (128-position
@@ -333,7 +340,7 @@ __global__ void __launch_bounds__(128) tq_scores_stream_kernel(const TqAttnArgs 
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, g = lane >> 2, t = lane & 3;
     const int pw = p0 + 32 * w;
     if (pw >= tn) return;  // this warp (no barrier follows)
-    const uint32_t *lutl = lut + lane;
+    const uint32_t lutl = as::sa(lut) + 4 * lane;
     const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
     const int nblk = a.kvd >> 6;
     float acc[2][NT][4];
@@ -547,12 +554,12 @@ __global__ void __launch_bounds__(128, 3) tq_values_kernel(const TqAttnArgs a) {
         for (int j = 0; j < NJ; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.0f;
-    const uint32_t *lutl = lut + lane;
+    const uint32_t lutl = as::sa(lut) + 4 * lane;
     // ldmatrix row address: matrix lane >> 3 = (heads + 8 (q & 1), positions 8 (q >> 1))
     const int lq = lane >> 3, lr = lane & 7;
     const uint32_t ld_s = ring_s + 16 * RS + (lr + 8 * (lq & 1)) * ES + 16 * (lq >> 1);
-    const uint8_t *cw_p = wring + (2 * t) * RS + WB * g;
-    const float *f_p = s_f + g;
+    const uint32_t cw_s = ring_s + (2 * t) * RS + WB * g;
+    const uint32_t f_s = as::sa(s_f) + 4 * g;
     for (int i = 0; i < nmy; ++i) {
         if (i + D - 1 < nmy) issue(i + D - 1);
         cp_commit();
@@ -564,19 +571,18 @@ __global__ void __launch_bounds__(128, 3) tq_values_kernel(const TqAttnArgs a) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             ldsm_x4(ld_s + so + 16 * mt * ES, af[mt][0], af[mt][1], af[mt][2], af[mt][3]);
-            const float *fo = f_p + ks * HP + 16 * mt;
-            const __half2 fa = __float2half2_rn(fo[0]);
-            const __half2 fb = __float2half2_rn(fo[8]);
+            const uint32_t fo = f_s + 4 * (ks * HP + 16 * mt);
+            const __half2 fa = __float2half2_rn(ldsf(fo));
+            const __half2 fb = __float2half2_rn(ldsf(fo + 32));
             af[mt][0] = hmul2(af[mt][0], fa);
             af[mt][1] = hmul2(af[mt][1], fb);
             af[mt][2] = hmul2(af[mt][2], fa);
             af[mt][3] = hmul2(af[mt][3], fb);
         }
-        const uint8_t *cp = cw_p + so;
-        const CW v0 = *reinterpret_cast<const CW *>(cp);
-        const CW v1 = *reinterpret_cast<const CW *>(cp + RS);
-        const CW v2 = *reinterpret_cast<const CW *>(cp + 8 * RS);
-        const CW v3 = *reinterpret_cast<const CW *>(cp + 9 * RS);
+        const CW v0 = lds_cw<CW>(cw_s + so);
+        const CW v1 = lds_cw<CW>(cw_s + so + RS);
+        const CW v2 = lds_cw<CW>(cw_s + so + 8 * RS);
+        const CW v3 = lds_cw<CW>(cw_s + so + 9 * RS);
 #pragma unroll
         for (int wi = 0; wi < WB / 4; ++wi) {
             const uint32_t w0 = word_of(v0, wi), w1 = word_of(v1, wi), w2 = word_of(v2, wi), w3 = word_of(v3, wi);
@@ -659,24 +665,22 @@ int sm_count() {
 
 // Launch attributes are set (and the occupancy queried) on the first call of
 // each shape, which is an eager call; graph captures reuse them.
-template <int NT, int G, int MAXB, int NBUF>
+template <int NT, int G, int MAXB>
 cudaError_t launch_scores(const TqAttnArgs &a, cudaStream_t s) {
-    using SS = ScoresShape<NT, G, MAXB, NBUF>;
-    auto kern = tq_scores_kernel<NT, G, MAXB, NBUF>;
-    const int bpw = (a.kvd / 64 + G - 1) / G;
-    const size_t smem = SS::smem(bpw);
+    const size_t smem = (size_t)LUT32 * 4 + 4 * 32 * (size_t)a.rsk + 2 * 2 * G * 8 * NT * 32 * 4 + 4 * 8;
     static size_t smem_set = 0;
     static int occ = 0;
     if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(tq_scores_kernel<NT, G, MAXB>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SS::THREADS, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, tq_scores_kernel<NT, G, MAXB>, 64 * G, smem);
         if (e != cudaSuccess) return e;
         smem_set = smem;
     }
     const int nu_max = (a.B + 31) / 32;
     const int nseg = std::max(1, std::min(nu_max, std::max(1, occ) * sm_count() / a.M));
-    return launch_pdl(kern, dim3(nseg, a.M), dim3(SS::THREADS), smem, s, a);
+    return launch_pdl(tq_scores_kernel<NT, G, MAXB>, dim3(nseg, a.M), dim3(64 * G), smem, s, a);
 }
 
 template <int MT, int NJ>
@@ -703,16 +707,20 @@ cudaError_t tq_decode_attn(const TqAttnArgs &a0, cudaStream_t s) {
     if (a.kvd % 64 || a.nh < 1 || a.nh > 32 || a.Sp != tq_padded_len(a.B) || a.nc16 != a.Sp / 16 ||
         2 * a.kpl != a.kvd || 2 * a.vpl != a.kvd)
         return cudaErrorInvalidValue;
+    // unit-buffer row stride: 8 or 24 (mod 32) words, so the eight rows of a
+    // 64-bit read land in distinct banks
+    a.rsk = a.kpl + ((a.kpl / 32) % 2 == 0 ? 32 : 0);
     const int nt = (a.nh + 7) / 8;
     const int nblk = a.kvd / 64;
     cudaError_t e;
-    // q~ register budget: MAXB blocks x NT head tiles x 8 registers per warp
     if (nt == 1 && nblk <= 12)
-        e = launch_scores<1, 2, 6, 4>(a, s);
+        e = launch_scores<1, 1, 12>(a, s);
+    else if (nt == 2 && nblk <= 6)
+        e = launch_scores<2, 1, 6>(a, s);
     else if (nt == 2 && nblk <= 12)
-        e = launch_scores<2, 4, 3, 4>(a, s);
+        e = launch_scores<2, 2, 6>(a, s);
     else if (nt == 2 && nblk <= 24)
-        e = launch_scores<2, 4, 6, 4>(a, s);
+        e = launch_scores<2, 4, 6>(a, s);
     else if (nt == 1)
         e = launch_pdl(tq_scores_stream_kernel<1, 4>, dim3(a.Sp / TQ_CH, a.M), dim3(128), 0, s, a);
     else if (nt == 2)
