@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c3", choices=["c3", "c4", "c2"])
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="sequences per GPU for c3/c4 (0 = the workload's; smaller for profiler captures)")
     return ap.parse_args()
 
 
@@ -290,7 +292,7 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
     """Prefill every sequence, then time teacher-forced decode steps (one
     token per sequence per step) on the device."""
     sp_ = decode_spec(args.workload, kgcuda)
-    C, n, PRE = sp_["cfg"], sp_["seqs"], sp_["prefill"]
+    C, n, PRE = sp_["cfg"], (args.seqs or sp_["seqs"]), sp_["prefill"]
     dev = torch.device("cuda", local)
     cfg = kgcuda.micro_config(kv_mode=sp_["kv_mode"], weight_dtype=kgcuda.KG_W_BF16, max_seqs=n, **C)
     be = kgcuda.CudaBackend(cfg, device=local)
@@ -413,7 +415,7 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config(sp_["name"], world),
+        "config": dict(workload_config(sp_["name"], world), **({"global_batch": world * n} if args.seqs else {})),
         "collective": (f"NCCL all_gather of each rank's logits ({n} x {V} f32) per step" if world > 1 else None),
         "gpu_launches": int(graph_kernels * args.steps),
         "decode_step": "one CUDA graph per step" if graph_kernels else "eager",

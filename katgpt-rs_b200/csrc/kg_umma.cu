@@ -285,14 +285,11 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
     }
 }
 
-template <typename T, bool SA, bool SB>
-cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
-    constexpr int BN = SB ? 128 : 256;
-    const bool f16 = std::is_same<T, __half>::value;
+template <typename T, bool SA, bool SB, int BN>
+cudaError_t launch_bn(const bf::Gemm &g, cudaStream_t s, int *err, int nsm) {
     Maps maps;
     std::memset(&maps, 0, sizeof(maps));
-    (void)f16;  // 16-bit elements either way: the map only moves bytes
-    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;  // 16-bit elements either way: the map only moves bytes
     if (!make_tensor_map(&maps.a, g.A, g.M, g.K, g.lda, 2, BK, BM, SW) ||
         (SA && !make_tensor_map(&maps.a2, g.A2, g.M, g.K, g.lda, 2, BK, BM, SW)) ||
         !make_tensor_map(&maps.b, g.B, g.N, g.K, g.ldb, 2, BK, BN, SW) ||
@@ -305,12 +302,30 @@ cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    int dev = 0, nsm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
     umma_gemm_kernel<T, SA, SB, BN><<<std::min(tiles, nsm), THREADS, smem, s>>>(maps, g, err);
     return cudaGetLastError();
+}
+
+// Tile width: the widest of 256 (128 with split B) / 128 / 64 columns that
+// still gives every SM a tile (few-row GEMMs such as a 512-sequence decode
+// step would otherwise leave most SMs idle).
+template <typename T, bool SA, bool SB>
+cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
+    static int nsm = 0;
+    if (nsm == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 148;
+    }
+    const int mt = (g.M + BM - 1) / BM;
+    auto tiles = [&](int bn) { return mt * ((g.N + bn - 1) / bn); };
+    if constexpr (!SB) {
+        if (tiles(256) >= nsm) return launch_bn<T, SA, SB, 256>(g, s, err, nsm);
+    }
+    if (tiles(128) >= nsm) return launch_bn<T, SA, SB, 128>(g, s, err, nsm);
+    return launch_bn<T, SA, SB, 64>(g, s, err, nsm);
 }
 
 }  // namespace
