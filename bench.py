@@ -423,8 +423,8 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
         "roofline": {"bound": "hbm", "kernel": sp_["attn_kernel"],
                      "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
                      "frac": (attn_gbs / peak) if attn_gbs else None, "traffic": traffic,
-                     "traffic_unit": "bytes per launch (one layer), ncu dram read+write",
-                     "algorithmic_bytes_per_launch": attn_bytes / L,
+                     "traffic_unit": "bytes per layer (its attention launches), ncu dram read+write",
+                     "algorithmic_bytes_per_layer": attn_bytes / L,
                      "algorithmic_bytes_per_step": attn_bytes,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
         "phases_ms_per_step": {"kv_attention": ph_ms[0], "kv_encode": ph_ms[1], "weight_gemms": ph_ms[2],

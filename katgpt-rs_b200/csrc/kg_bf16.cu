@@ -496,6 +496,9 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
     x *= 0x94d049bb133111ebull;
     return x ^ (x >> 31);
 }
+// one block per row; a thread draws 8 consecutive entries (one hash each for
+// the Bernoulli draw, a second for a survivor's Box-Muller value) and stores
+// them as one 16-byte vector per half
 __global__ void mlp_hook_kernel(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot, const int32_t *pos, int m,
                                 float keep, uint64_t seed, int layer) {
     pdl_wait();
@@ -505,21 +508,35 @@ __global__ void mlp_hook_kernel(bf16 *hid, bf16 *hid2, int *row_alive, const int
     __syncthreads();
     const uint64_t key = mix64(seed ^ mix64(((uint64_t)layer << 48) ^ ((uint64_t)slot[r] << 24) ^ (uint64_t)pos[r]));
     int cnt = 0;
-    for (int j = threadIdx.x; j < m; j += blockDim.x) {
-        const uint64_t a = mix64(key + 2 * (uint64_t)j), b = mix64(key + 2 * (uint64_t)j + 1);
-        const float u = (float)(a >> 40) * (1.0f / 16777216.0f);
-        float v = 0.0f;
-        if (u < keep) {  // Box-Muller on two more uniforms from b
-            const float u1 = ((float)(b >> 40) + 0.5f) * (1.0f / 16777216.0f);
-            const float u2 = (float)((b >> 16) & 0xffffff) * (1.0f / 16777216.0f);
-            v = fabsf(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));  // post-ReLU: non-negative
-            cnt += v > 0.0f;
+    for (int j0 = 8 * threadIdx.x; j0 < m; j0 += 8 * blockDim.x) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            float v[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const uint64_t j = (uint64_t)(j0 + e + q);
+                const float u = (float)(mix64(key + 2 * j) >> 40) * (1.0f / 16777216.0f);
+                v[q] = 0.0f;
+                if (u < keep) {  // Box-Muller on two more uniforms
+                    const uint64_t b2 = mix64(key + 2 * j + 1);
+                    const float u1 = ((float)(b2 >> 40) + 0.5f) * (1.0f / 16777216.0f);
+                    const float u2 = (float)((b2 >> 16) & 0xffffff) * (1.0f / 16777216.0f);
+                    v[q] = fabsf(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));  // post-ReLU: non-negative
+                    cnt += v[q] > 0.0f;
+                }
+            }
+            const bf16 h0 = __float2bfloat16_rn(v[0]), h1 = __float2bfloat16_rn(v[1]);
+            const bf16 l0 = __float2bfloat16_rn(v[0] - __bfloat162float(h0)), l1 = __float2bfloat16_rn(v[1] - __bfloat162float(h1));
+            hv[e / 2] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+            lv[e / 2] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
         }
-        const bf16 hv = __float2bfloat16_rn(v);
-        hid[(int64_t)r * m + j] = hv;
-        hid2[(int64_t)r * m + j] = __float2bfloat16_rn(v - __bfloat162float(hv));
+        *reinterpret_cast<uint4 *>(hid + (int64_t)r * m + j0) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4 *>(hid2 + (int64_t)r * m + j0) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
     }
-    atomicAdd(&s_cnt, cnt);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&s_cnt, cnt);
     __syncthreads();
     if (threadIdx.x == 0) row_alive[r] = s_cnt;
 }
@@ -631,6 +648,7 @@ cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int
 cudaError_t mlp_hook(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot, const int32_t *pos, int m, int M,
                      float keep, uint64_t seed, int layer, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
+    if (m % 8) return cudaErrorInvalidValue;  // 16-byte row vectors
     return launch_pdl(mlp_hook_kernel, dim3(M), dim3(256), 0, s, hid, hid2, row_alive, slot, pos, m, keep, seed, layer);
 }
 cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s) {
