@@ -77,11 +77,28 @@ __device__ __forceinline__ int swz(int row, int c) { return row * 4 + (c ^ ((row
 template <typename T>
 __device__ __forceinline__ int epi_store(const Gemm &g, int z, int row, int cc, float v, float rs) {
     switch (g.epi) {
-        case EPI_F32: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v; return 0;
+        case EPI_F32: {
+            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v;
+            if (g.Qh && cc < g.qcols) {
+                const __half h = __float2half_rn(v);
+                g.Qh[(int64_t)row * g.ldq + cc] = h;
+                g.Ql[(int64_t)row * g.ldq + cc] = __float2half_rn(v - __half2float(h));
+            }
+            return 0;
+        }
         case EPI_F32_RESID: {
+            const int64_t i = z * g.sC + (int64_t)row * g.ldc + cc;
             const float o = v + g.R[z * g.sR + (int64_t)row * g.ldr + cc];
-            g.C[z * g.sC + (int64_t)row * g.ldc + cc] = o;
-            if (g.C2) g.C2[z * g.sC + (int64_t)row * g.ldc + cc] = o;
+            g.C[i] = o;
+            if (g.C2) g.C2[i] = o;
+            if (g.Dacc) g.Dacc[i] += o - g.R3[i];
+            return 0;
+        }
+        case EPI_BF16_SPLIT: {
+            const int64_t ob = z * g.sCb + (int64_t)row * g.ldcb + cc;
+            const bf16 hi = __float2bfloat16_rn(v);
+            static_cast<bf16 *>(g.Cb)[ob] = hi;
+            if (g.Cb2) static_cast<bf16 *>(g.Cb2)[ob] = __float2bfloat16_rn(v - __bfloat162float(hi));
             return 0;
         }
         case EPI_F32_ROWSCALE: g.C[z * g.sC + (int64_t)row * g.ldc + cc] = v * rs; return 0;

@@ -17,7 +17,8 @@ enum Epi : int {
     EPI_RELU = 2,          // Cb(+Cb2) = split(max(acc, 0)); row_alive[row] += #(acc > 0)
     EPI_OUT = 3,           // Cb(+Cb2) = split(acc)
     EPI_F32_ROWSCALE = 4,  // C = acc * row_scale[row]
-    EPI_OUT_ROWSCALE = 5   // Cb(+Cb2) = split(acc * row_scale[row])
+    EPI_OUT_ROWSCALE = 5,  // Cb(+Cb2) = split(acc * row_scale[row])
+    EPI_BF16_SPLIT = 6     // Cb(+Cb2) = bf16 hi / lo split of acc, whatever the operand type
 };
 enum DType : int { DT_BF16 = 0, DT_F16 = 1 };
 
@@ -45,6 +46,14 @@ struct Gemm {
     const float *row_scale;
     int64_t sRs;
     float *C2;  // EPI_F32_RESID: optional second copy of C (same ldc / sC)
+    // EPI_F32: optional f16 hi / lo copy of columns [0, qcols) into Qh / Ql
+    // (row stride ldq); EPI_F32_RESID: optional Dacc[i] += C[i] - R3[i] (same
+    // indexing as C). mma.sync path only (M < 256).
+    __half *Qh, *Ql;
+    int64_t ldq;
+    int qcols;
+    float *Dacc;
+    const float *R3;
     // split-K (1, 2, 4 or 8; 0 = chosen from the shape): the K range is cut
     // into ksplit parts computed by the CTAs of one thread-block cluster and
     // reduced through distributed shared memory in part order (deterministic)

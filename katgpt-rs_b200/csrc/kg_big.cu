@@ -335,10 +335,18 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         } else {
             BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, g.xb, g.xb2, false, s));
         }
+        // decode steps of fewer than 256 rows run the mma.sync GEMMs, whose
+        // epilogues also produce q's f16 split, the attention output's bf16
+        // split and the delta-routing accumulation (no separate kernels)
+        const bool fuse = !prefill && M < 256;
+        const bool fuse_q = fuse && !g.std_kv;
         // fused QKV projection
         bf::Gemm q = gemm0();
         q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = wqkv; q.ldb = n; q.M = M; q.N = nqkv; q.K = n;
         q.epi = bf::EPI_F32; q.C = g.qkv; q.ldc = nqkv;
+        if (fuse_q) {
+            q.Qh = g.qh; q.Ql = g.ql; q.ldq = n; q.qcols = n;
+        }
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(gemm_split(ctx, q, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
@@ -375,7 +383,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
                                       ctx->vpl, g.vnorm, 1, g.slot_of, g.pos_of, L, B, l, s));
         }
         prof_mark(ctx, KG_PROF_ENCODE, 1, s);
-        if (prefill || !g.std_kv) BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
+        if ((prefill || !g.std_kv) && !fuse_q) BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
         if (g.std_kv && !prefill) {
             attn::StdDecodeArgs sa;
             sa.Q = g.qkv; sa.ldq = nqkv; sa.kc = g.kcache; sa.vc = g.vcache; sa.slot = g.slot_of; sa.pos = g.pos_of;
@@ -432,10 +440,14 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             o.A = g.U; o.A2 = g.U2; o.lda = (int64_t)nh * kvd; o.sA = kvd;
             o.B = g.rot_th; o.B2 = g.rot_tl; o.ldb = kvd; o.sB = (int64_t)hd * kvd;
             o.M = M; o.N = hd; o.K = kvd; o.batch = nh;
-            o.epi = bf::EPI_F32; o.C = g.attf; o.ldc = n; o.sC = hd;
+            if (fuse) {  // straight to the Wo GEMM's bf16 hi / lo operand
+                o.epi = bf::EPI_BF16_SPLIT; o.Cb = g.attb; o.Cb2 = g.attb2; o.ldcb = n; o.sCb = hd;
+            } else {
+                o.epi = bf::EPI_F32; o.C = g.attf; o.ldc = n; o.sC = hd;
+            }
             BIG_TRY(gemm_split(ctx, o, s));
         }
-        BIG_TRY(bf::to_bf16(g.attf, n, n, M, g.attb, g.attb2, n, s));
+        if (!(fuse && !g.std_kv)) BIG_TRY(bf::to_bf16(g.attf, n, n, M, g.attb, g.attb2, n, s));
         // output projection + residual: x = Wo att + xr
         bf::Gemm w = gemm0();
         w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
@@ -457,6 +469,13 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         bf::Gemm dn = gemm0();
         dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
         dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
+        // delta routing's per-layer accumulation (delta += x - xr) in the
+        // epilogue, except at routing layers (3, 7, ..: the routing kernel
+        // accumulates) and when the TwELL gather may still rewrite x
+        const bool fuse_delta = fuse && !spkv && (l & 3) != 3 && M > kTwellMaxRows;
+        if (fuse_delta) {
+            dn.Dacc = g.delta; dn.R3 = g.xr;
+        }
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(gemm_split(ctx, dn, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
@@ -468,7 +487,8 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         if (M <= kTwellMaxRows)
             BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
                                         c.sparse_threshold, s));
-        if (!spkv) BIG_TRY(bf::delta_route(g.x, g.xr, g.delta, g.dq + (int64_t)l * n, g.dn + (int64_t)l * n, n, M, l, s));
+        if (!spkv && !fuse_delta)
+            BIG_TRY(bf::delta_route(g.x, g.xr, g.delta, g.dq + (int64_t)l * n, g.dn + (int64_t)l * n, n, M, l, s));
     }
     return cudaSuccess;
 }

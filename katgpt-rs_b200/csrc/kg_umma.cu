@@ -334,6 +334,7 @@ bool supported(const bf::Gemm &g) {
     // one batch, K in whole 64-element blocks, 16-byte aligned rows and bases,
     // and the hi-only B form only for bf16 weights
     if (g.batch != 1 || g.K % BK || g.lda % 8 || g.ldb % 8) return false;
+    if (g.Qh || g.Dacc || g.epi == bf::EPI_BF16_SPLIT) return false;  // fused extras: mma.sync epilogue only
     if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return false;
     if (g.A2 && (reinterpret_cast<uintptr_t>(g.A2) & 15)) return false;
     if (g.B2 && (reinterpret_cast<uintptr_t>(g.B2) & 15)) return false;
