@@ -108,7 +108,10 @@ cudaError_t big_init(kg_ctx *ctx) {
     BigState &g = ctx->big;
     const kg_config &c = ctx->cfg;
     const int64_t n = ctx->n, kvd = ctx->kvd, m = ctx->m, V = ctx->V, L = ctx->L, B = ctx->B, S = c.max_seqs;
-    g.ws_tokens = std::max<int64_t>(S, 8192);
+    // workspace rows: prefill runs in passes of whole sequences up to this many
+    // tokens (large passes keep the tcgen05 GEMMs' last wave small); about
+    // 75 KB per row at n_embd 768, 200 KB at 2048
+    g.ws_tokens = std::max<int64_t>(S, n <= 2048 ? 32768 : 16384);
     g.Tpad = (B + 31) / 32 * 32;
     auto &own = ctx->allocs;
     // weights (bf16), one block in the flat reference order

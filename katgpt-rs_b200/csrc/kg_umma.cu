@@ -307,9 +307,10 @@ cudaError_t launch_bn(const bf::Gemm &g, cudaStream_t s, int *err, int nsm) {
     return cudaGetLastError();
 }
 
-// Tile width: the widest of 256 (128 with split B) / 128 / 64 columns that
-// still gives every SM a tile (few-row GEMMs such as a 512-sequence decode
-// step would otherwise leave most SMs idle).
+// Tile width: 256 (128 with split B), 128 or 64 columns. Up to 2048 rows (a
+// 512-sequence decode step) the widest that still gives every SM a tile;
+// above, 128 when it raises the share of busy SMs over the launch's waves by
+// at least 10 points (a pass whose last wave would be mostly empty).
 template <typename T, bool SA, bool SB>
 cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
     static int nsm = 0;
@@ -320,11 +321,22 @@ cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
         if (nsm <= 0) nsm = 148;
     }
     const int mt = (g.M + BM - 1) / BM;
-    auto tiles = [&](int bn) { return mt * ((g.N + bn - 1) / bn); };
-    if constexpr (!SB) {
-        if (tiles(256) >= nsm) return launch_bn<T, SA, SB, 256>(g, s, err, nsm);
+    auto busy = [&](int bn) {
+        const int t = mt * ((g.N + bn - 1) / bn);
+        return (double)t / ((double)((t + nsm - 1) / nsm) * nsm);
+    };
+    int bn = SB ? 128 : 256;
+    if (g.M <= 2048) {  // few rows: the widest tile that still gives every SM a tile
+        auto tiles = [&](int w) { return mt * ((g.N + w - 1) / w); };
+        if (tiles(bn) < nsm) bn = 128;
+        if (tiles(bn) < nsm) bn = 64;
+    } else if (!SB && busy(128) >= busy(256) + 0.10) {  // many rows: a small last wave
+        bn = 128;
     }
-    if (tiles(128) >= nsm) return launch_bn<T, SA, SB, 128>(g, s, err, nsm);
+    if constexpr (!SB) {
+        if (bn == 256) return launch_bn<T, SA, SB, 256>(g, s, err, nsm);
+    }
+    if (bn == 128) return launch_bn<T, SA, SB, 128>(g, s, err, nsm);
     return launch_bn<T, SA, SB, 64>(g, s, err, nsm);
 }
 
