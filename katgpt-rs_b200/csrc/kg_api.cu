@@ -157,6 +157,9 @@ void kg_ctx_destroy(kg_ctx *ctx) {
     for (void *p : ctx->allocs) cudaFree(p);
     if (ctx->stage) cudaFree(ctx->stage);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    if (ctx->aux) cudaStreamSynchronize(ctx->aux), cudaStreamDestroy(ctx->aux);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     for (int p = 0; p < KG_PROF_N; ++p)
         for (int e = 0; e < 2; ++e)
             for (cudaEvent_t ev : ctx->prof_ev[p][e]) cudaEventDestroy(ev);
@@ -190,6 +193,10 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     ctx->dev_name = std::string("CUDA:") + prop.name;
     e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "cudaStreamCreate"));
+    e = cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming);
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "cudaStreamCreate (side stream)"));
 
     const kg_config &c = ctx->cfg;
     ctx->n = c.n_embd; ctx->nh = c.n_head; ctx->hd = c.head_dim; ctx->nkv = c.n_kv_head;

@@ -353,6 +353,24 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         prof_mark(ctx, KG_PROF_GEMM, 0, s);
         BIG_TRY(gemm_split(ctx, q, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
+        // decode over codes: q~_h = R[:, head cols] q_h (batched over heads) on the
+        // side stream while this stream encodes K and V; joined before attention
+        const bool fork = fuse_q && ctx->aux && !ctx->prof;
+        auto qrot_gemm = [&](cudaStream_t st) {
+            bf::Gemm r = gemm0();
+            r.dtype = bf::DT_F16;
+            r.A = g.qh; r.A2 = g.ql; r.lda = n; r.sA = hd;
+            r.B = g.rot_h; r.B2 = g.rot_l; r.ldb = kvd; r.sB = hd;
+            r.M = M; r.N = kvd; r.K = hd; r.batch = nh;
+            r.epi = bf::EPI_OUT; r.Cb = g.qrot; r.Cb2 = g.qrot2; r.ldcb = (int64_t)nh * kvd; r.sCb = kvd;
+            return gemm_split(ctx, r, st);
+        };
+        if (fork) {
+            BIG_TRY(cudaEventRecord(ctx->ev_fork, s));
+            BIG_TRY(cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
+            BIG_TRY(qrot_gemm(ctx->aux));
+            BIG_TRY(cudaEventRecord(ctx->ev_join, ctx->aux));
+        }
         // TurboQuant encode of K and V into the arena (exact reference order)
         prof_mark(ctx, KG_PROF_ENCODE, 0, s);
         if (g.std_kv) {
@@ -418,14 +436,10 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             fa.n_seq = n_seq; fa.T = T; fa.nh = nh; fa.nkv = (int)ctx->nkv; fa.hd = hd; fa.scale = scale;
             BIG_TRY(attn::flash_prefill(fa, s));
         } else {
-            // q~_h = R[:, head cols] q_h  (batched over heads)
-            bf::Gemm r = gemm0();
-            r.dtype = bf::DT_F16;
-            r.A = g.qh; r.A2 = g.ql; r.lda = n; r.sA = hd;
-            r.B = g.rot_h; r.B2 = g.rot_l; r.ldb = kvd; r.sB = hd;
-            r.M = M; r.N = kvd; r.K = hd; r.batch = nh;
-            r.epi = bf::EPI_OUT; r.Cb = g.qrot; r.Cb2 = g.qrot2; r.ldcb = (int64_t)nh * kvd; r.sCb = kvd;
-            BIG_TRY(gemm_split(ctx, r, s));
+            if (fork)
+                BIG_TRY(cudaStreamWaitEvent(s, ctx->ev_join, 0));
+            else
+                BIG_TRY(qrot_gemm(s));
             attn::TqAttnArgs ta;
             ta.kcodes = g.kcodes; ta.vcodes = g.vcodes; ta.knorm = g.knorm; ta.vnorm = g.vnorm;
             ta.kcent = g.kcent; ta.vcent = g.vcent; ta.qrot = g.qrot;

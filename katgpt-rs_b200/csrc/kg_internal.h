@@ -174,6 +174,10 @@ struct kg_ctx {
     __half *enc_rh = nullptr, *enc_rl = nullptr;  // f16 hi / lo of R for kg_tq_encode (codec contexts)
     float hook_keep = 0.0f;                       // kg_set_mlp_hook (benchmark input), 0 = off
     uint64_t hook_seed = 0;
+    // side stream of the decode layers (q~ GEMM alongside the K/V encoder),
+    // forked from and joined back to the calling stream through events
+    cudaStream_t aux = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 };
 
 namespace kg {
