@@ -1,5 +1,5 @@
 // kg_async.cuh — mbarrier, TMA and bulk-copy helpers shared by the tcgen05
-// GEMM (kg_umma.cu) and the decode attention (kg_attn.cu).
+// GEMM (kg_umma.cu) and the decode-attention scores kernel (kg_tqattn.cu).
 //
 // Every wait is bounded: mbar_wait gives up after `KG_WAIT_CYCLES` clock
 // cycles (about 2 s), raises the CTA's abort flag and writes KG_ERR_TIMEOUT to
@@ -70,11 +70,6 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(sa(dst)),
         "l"(src), "r"(bytes), "r"(sa(bar))
         : "memory");
-}
-
-// prefetch a contiguous range into L2 (16-byte aligned, size a multiple of 16)
-__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
 }
 
 }  // namespace as

@@ -13,7 +13,6 @@
 
 #include <algorithm>
 
-#include "kg_async.cuh"
 #include "kg_attn.cuh"
 #include "kg_pdl.cuh"
 

@@ -1,4 +1,4 @@
-// kg_bf16.cuh — interfaces of the BF16 tensor-core path (kg_bf16.cu, kg_attn.cu).
+// kg_bf16.cuh — interfaces of the BF16 tensor-core path (kg_bf16.cu: GEMMs, norms, TwELL, small kernels).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
