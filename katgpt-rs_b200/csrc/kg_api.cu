@@ -470,7 +470,19 @@ int forward_graph(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int3
             x.stream == s)
             gr = &x;
     if (!gr) {  // first use of this key: eager
-        ctx->graphs.push_back({n_seq, start_pos != nullptr, logits, probs, s, nullptr, 0, false});
+        // the cache holds at most kMaxDecodeGraphs keys (callers that pass a new
+        // output buffer every step would otherwise grow it without bound): evict
+        // the least recently used one
+        if (ctx->graphs.size() >= kg_ctx::kMaxDecodeGraphs) {
+            auto old = std::min_element(ctx->graphs.begin(), ctx->graphs.end(),
+                                        [](const kg_ctx::DecodeGraph &a, const kg_ctx::DecodeGraph &b) {
+                                            return a.last_use < b.last_use;
+                                        });
+            if (old->stream) KG_CUDA(ctx, cudaStreamSynchronize(old->stream));
+            if (old->exec) cudaGraphExecDestroy(old->exec);
+            ctx->graphs.erase(old);
+        }
+        ctx->graphs.push_back({n_seq, start_pos != nullptr, logits, probs, s, nullptr, 0, false, ++ctx->graph_clock});
         KG_CUDA(ctx, kg::big_forward(ctx, n_seq, ctx->g_ids, ctx->g_tok, pos, 1, logits, probs, s));
         return KG_OK;
     }
@@ -498,6 +510,7 @@ int forward_graph(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int3
         KG_CUDA(ctx, e);
     }
     KG_CUDA(ctx, cudaGraphLaunch(gr->exec, s));
+    gr->last_use = ++ctx->graph_clock;
     ctx->last_graph_kernels = gr->kernels;
     return KG_OK;
 }

@@ -14,6 +14,7 @@
 #include <algorithm>
 
 #include "kg_attn.cuh"
+#include "kg_dev.cuh"
 #include "kg_pdl.cuh"
 
 namespace kg {
@@ -389,11 +390,9 @@ cudaError_t gather_norms(const float *norms, const int32_t *slot, const int32_t 
 template <int HD>
 cudaError_t launch_fa(const FlashArgs &a, cudaStream_t s) {
     const int smem = 4 * 64 * (HD + 8) * 2;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(fa_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        cudaError_t e = dev::smem(fa_kernel<HD>, smem);
         if (e != cudaSuccess) return e;
-        attr = true;
     }
     dim3 grid((a.T + 63) / 64, a.nh, a.n_seq);
     fa_kernel<HD><<<grid, 128, smem, s>>>(a);

@@ -12,6 +12,7 @@
 #include <cooperative_groups.h>
 
 #include "kg_bf16.cuh"
+#include "kg_dev.cuh"
 #include "kg_pdl.cuh"
 
 namespace kg {
@@ -578,11 +579,9 @@ __global__ void softmax_kernel(const float *logits, float *probs, int V, float i
 template <typename CF, typename T, bool SA, bool SB>
 cudaError_t launch_gemm(Gemm g, cudaStream_t s) {
     constexpr int smem = gemm_smem<CF, SA, SB>();
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<CF, T, SA, SB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        cudaError_t e = dev::smem(gemm_kernel<CF, T, SA, SB>, smem);
         if (e != cudaSuccess) return e;
-        attr = true;
     }
     const int64_t tiles = (int64_t)((g.N + CF::BN - 1) / CF::BN) * ((g.M + CF::BM - 1) / CF::BM) * g.batch;
     if (g.ksplit == 0) {

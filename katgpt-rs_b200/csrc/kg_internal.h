@@ -162,8 +162,11 @@ struct kg_ctx {
         cudaGraphExec_t exec;
         int64_t kernels;
         bool captured;
+        uint64_t last_use;
     };
+    static constexpr size_t kMaxDecodeGraphs = 8;
     std::vector<DecodeGraph> graphs;
+    uint64_t graph_clock = 0;
     int32_t *g_ids = nullptr, *g_tok = nullptr, *g_pos = nullptr;
     int64_t last_graph_kernels = 0;
     // staging for host-pointer calls

@@ -25,6 +25,7 @@
 //   softmax_scaled        crates/katgpt-types/src/math.rs:36-50
 #include <algorithm>
 
+#include "kg_dev.cuh"
 #include "kg_exact.cuh"
 #include "kg_internal.h"
 
@@ -451,16 +452,9 @@ cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     const int blocks = (a.n_seq + SB - 1) / SB;
     const size_t smem = ((size_t)a.pack_floats + 128 * 17) * sizeof(float);
     auto kfn = micro_forward<16, 4, 4, 4, 64, 27, 16, MODE>;
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = dev::smem(kfn, smem);
     if (e != cudaSuccess) return e;
-    static int n_sm = 0, per_sm = 0;
-    if (!n_sm) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, 128, smem);
-        if (per_sm < 1) per_sm = 1;
-    }
+    const int n_sm = dev::sm_count(), per_sm = dev::occupancy(kfn, 128, smem);
     const int grid = std::min(blocks, n_sm * per_sm);
     kfn<<<grid, threads, smem, s>>>(a);
     return cudaGetLastError();

@@ -18,6 +18,7 @@
 #include <mutex>
 #include <string>
 
+#include "kg_dev.cuh"
 #include "kg_exact.cuh"
 #include "kg_internal.h"
 #include "kg_pdl.cuh"
@@ -529,11 +530,9 @@ cudaError_t tq_encode_tiled(int dim, int bits, int64_t n_vec, const float *x, in
     norm_kernel<<<(unsigned)((n_vec + 7) / 8), 256, 0, s>>>(dim, n_vec, x, ldx, xn_scratch, skip_scratch, norms, slot,
                                                              pos, L, B, layer);
     const int smem = 2 * (ER + EV) * EK * 4;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        cudaError_t e = dev::smem(rotate_kernel, smem);
         if (e != cudaSuccess) return e;
-        attr = true;
     }
     dim3 grid(dim / ER, (unsigned)((n_vec + EV - 1) / EV));
     rotate_kernel<<<grid, 256, smem, s>>>(dim, bits, n_vec, xn_scratch, skip_scratch, rot, bnd, packed, pstride, slot,
@@ -553,11 +552,9 @@ cudaError_t tq_encode_tiled_kv(int dim, int kbits, int vbits, int M, const float
                                 slot, pos, L, B, layer);
     if (e0 != cudaSuccess) return e0;
     const int smem = 2 * (ER + EV) * EK * 4;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        cudaError_t e = dev::smem(rotate_kernel, smem);
         if (e != cudaSuccess) return e;
-        attr = true;
     }
     dim3 grid(dim / ER, (unsigned)((M + EV - 1) / EV), 2);
     return launch_pdl(rotate_kernel, grid, dim3(256), smem, s, dim, kbits, (int64_t)M, (const float *)xn_scratch,
@@ -575,8 +572,7 @@ cudaError_t tq_encode_scatter(int dim, int bits, int64_t n_vec, const float *x, 
         warps /= 2;
         smem = (size_t)warps * dim * (sizeof(float) + 1);
     }
-    cudaError_t e = cudaFuncSetAttribute(tq_encode_warp, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = dev::smem(tq_encode_warp, smem);
     if (e != cudaSuccess) return e;
     int64_t blocks = (n_vec + warps - 1) / warps;
     if (blocks > 148 * 16) blocks = 148 * 16;
@@ -639,7 +635,8 @@ extern "C" int kg_tq_encode_noalloc(kg_ctx *ctx, int32_t which, int64_t n_vec, c
         return KG_ERR_INVALID_ARG;
     }
     const int64_t kvd = ctx->kvd;
-    if (n_vec * kvd > kg::kNoAllocMaxFloats || n_vec > kg::kNoAllocMaxVectors) {
+    // bound n_vec before forming n_vec * kv_dim (a huge n_vec would overflow the product)
+    if (n_vec > kg::kNoAllocMaxVectors || n_vec > kg::kNoAllocMaxFloats / kvd) {
         ctx->err = "kg_tq_encode_noalloc: n_vec * kv_dim exceeds the fixed scratch of " +
                    std::to_string(kg::kNoAllocMaxFloats) + " floats (at most " +
                    std::to_string(kg::kNoAllocMaxFloats / kvd) + " vectors at this kv_dim)";

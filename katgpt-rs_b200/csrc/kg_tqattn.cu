@@ -37,6 +37,7 @@
 
 #include "kg_async.cuh"
 #include "kg_attn.cuh"
+#include "kg_dev.cuh"
 #include "kg_pdl.cuh"
 
 namespace kg {
@@ -652,34 +653,16 @@ __global__ void __launch_bounds__(128, 3) tq_values_kernel(const TqAttnArgs a) {
     }
 }
 
-int sm_count() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
-// Launch attributes are set (and the occupancy queried) on the first call of
-// each shape, which is an eager call; graph captures reuse them.
+// Launch attributes are set (and the occupancy queried) per device on the
+// first call of each shape, which is an eager call; graph captures reuse them.
 template <int NT, int G, int MAXB>
 cudaError_t launch_scores(const TqAttnArgs &a, cudaStream_t s) {
     const size_t smem = (size_t)LUT32 * 4 + 4 * 32 * (size_t)a.rsk + 2 * 2 * G * 8 * NT * 32 * 4 + 4 * 8;
-    static size_t smem_set = 0;
-    static int occ = 0;
-    if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(tq_scores_kernel<NT, G, MAXB>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, tq_scores_kernel<NT, G, MAXB>, 64 * G, smem);
-        if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
+    cudaError_t e = dev::smem(tq_scores_kernel<NT, G, MAXB>, smem);
+    if (e != cudaSuccess) return e;
+    const int occ = dev::occupancy(tq_scores_kernel<NT, G, MAXB>, 64 * G, smem);
     const int nu_max = (a.B + 31) / 32;
-    const int nseg = std::max(1, std::min(nu_max, std::max(1, occ) * sm_count() / a.M));
+    const int nseg = std::max(1, std::min(nu_max, occ * dev::sm_count() / a.M));
     return launch_pdl(tq_scores_kernel<NT, G, MAXB>, dim3(nseg, a.M), dim3(64 * G), smem, s, a);
 }
 
@@ -687,13 +670,8 @@ template <int MT, int NJ>
 cudaError_t launch_values(const TqAttnArgs &a, cudaStream_t s) {
     constexpr int D = 4;
     const size_t smem = (size_t)LUT32 * 4 + 4 * D * ValuesShape<MT, NJ>::SLOT + (size_t)a.nc16 * 16 * MT * 4;
-    static size_t smem_set = 0;
-    if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(tq_values_kernel<MT, NJ, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
+    cudaError_t e = dev::smem(tq_values_kernel<MT, NJ, D>, smem);
+    if (e != cudaSuccess) return e;
     return launch_pdl(tq_values_kernel<MT, NJ, D>, dim3(a.kvd / (8 * NJ), a.M), dim3(128), smem, s, a);
 }
 

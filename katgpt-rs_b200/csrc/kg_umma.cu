@@ -28,6 +28,7 @@
 
 #include "kg_async.cuh"
 #include "kg_bf16.cuh"
+#include "kg_dev.cuh"
 #include "kg_umma.cuh"
 
 namespace kg {
@@ -296,11 +297,9 @@ cudaError_t launch_bn(const bf::Gemm &g, cudaStream_t s, int *err, int nsm) {
         (SB && !make_tensor_map(&maps.b2, g.B2, g.N, g.K, g.ldb, 2, BK, BN, SW)))
         return cudaErrorInvalidValue;
     const int smem = 1024 + STG * STAGE_BYTES + 256;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(umma_gemm_kernel<T, SA, SB, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        cudaError_t e = dev::smem(umma_gemm_kernel<T, SA, SB, BN>, smem);
         if (e != cudaSuccess) return e;
-        attr = true;
     }
     const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
     umma_gemm_kernel<T, SA, SB, BN><<<std::min(tiles, nsm), THREADS, smem, s>>>(maps, g, err);
@@ -313,13 +312,7 @@ cudaError_t launch_bn(const bf::Gemm &g, cudaStream_t s, int *err, int nsm) {
 // at least 10 points (a pass whose last wave would be mostly empty).
 template <typename T, bool SA, bool SB>
 cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
-    static int nsm = 0;
-    if (nsm == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-        if (nsm <= 0) nsm = 148;
-    }
+    const int nsm = dev::sm_count();
     const int mt = (g.M + BM - 1) / BM;
     auto busy = [&](int bn) {
         const int t = mt * ((g.N + bn - 1) / bn);

@@ -14,6 +14,7 @@
 #include <immintrin.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -642,18 +643,20 @@ static void rotation_from(int64_t dim, const float *mat, float *q) {
     // in the same sequence (and with the same operands) as the reference's
     // left-looking loop, so every value is bit-identical; it only lets the
     // columns be updated in parallel.
-    unsigned nt = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<float> qj(dim);  // column j of q, contiguous (same values, same order of use)
     for (int64_t j = 0; j < dim; ++j) {
         float *vj = &v[j * dim];
         float nrm = sqrtf(sum_sq(vj, dim));
+        std::fill(qj.begin(), qj.end(), 0.0f);
         if (nrm > 1e-8f)
-            for (int64_t k = 0; k < dim; ++k) q[k * dim + j] = vj[k] / nrm;
+            for (int64_t k = 0; k < dim; ++k) q[k * dim + j] = qj[k] = vj[k] / nrm;
         auto work = [&](int64_t i0, int64_t i1) {
             for (int64_t i = i0; i < i1; ++i) {
                 float *vi = &v[i * dim];
                 float d = -0.0f;  // Iterator::<f32>::sum starts at -0.0
-                for (int64_t k = 0; k < dim; ++k) d = d + q[k * dim + j] * vi[k];
-                for (int64_t k = 0; k < dim; ++k) vi[k] -= d * q[k * dim + j];
+                for (int64_t k = 0; k < dim; ++k) d = d + qj[k] * vi[k];
+                for (int64_t k = 0; k < dim; ++k) vi[k] -= d * qj[k];
             }
         };
         int64_t rem = dim - (j + 1);
@@ -682,25 +685,36 @@ struct TQ {
     int kbits, vbits;
     std::vector<float> rot, rot_t, kc, kb, vc, vb;
 };
-static const TQ &tq_tables(int64_t dim, int kbits, int vbits) {
+// `timing`: tables for the CPU-baseline timing harness only, whose rotation is
+// a scaled Gaussian matrix of the same size instead of the O(dim^3) MGS
+// orthogonalisation (the encode / dequant work per vector is the same dim^2
+// dot products either way).
+static const TQ &tq_tables(int64_t dim, int kbits, int vbits, bool timing = false) {
     // small process-wide cache (tables are deterministic in (dim, bits))
-    static std::vector<TQ *> cache;
+    static std::vector<std::pair<bool, TQ *>> cache;
     static std::mutex mu;
     std::lock_guard<std::mutex> lk(mu);
-    for (TQ *t : cache)
-        if (t->dim == dim && t->kbits == kbits && t->vbits == vbits) return *t;
+    for (auto &e : cache)
+        if (e.first == timing && e.second->dim == dim && e.second->kbits == kbits && e.second->vbits == vbits)
+            return *e.second;
     TQ *t = new TQ;
     t->dim = dim;
     t->kbits = kbits;
     t->vbits = vbits;
     t->rot.resize(dim * dim);
-    rotation(dim, 42, t->rot.data());  // kv_cache.rs:63-77: seed 42, shared by layers
+    if (timing) {
+        Rng g(42);
+        const float sc = 1.0f / sqrtf((float)dim);
+        for (auto &v : t->rot) v = g.uniform() * 2.0f * sc - sc;
+    } else {
+        rotation(dim, 42, t->rot.data());  // kv_cache.rs:63-77: seed 42, shared by layers
+    }
     t->rot_t.resize(dim * dim);
     for (int64_t i = 0; i < dim; ++i)
         for (int64_t j = 0; j < dim; ++j) t->rot_t[i * dim + j] = t->rot[j * dim + i];
     codebook(dim, kbits, t->kc, t->kb, nullptr);
     codebook(dim, vbits, t->vc, t->vb, nullptr);
-    cache.push_back(t);
+    cache.push_back({timing, t});
     return *t;
 }
 
@@ -1207,6 +1221,88 @@ int or_run_batch_tail(const or_config *c, int mode, int kb, int vb, const float 
     for (int r : rc)
         if (r) return r;
     return 0;
+}
+
+// CPU-baseline timing of forward_quantized (mode 1) or forward_base (mode 0)
+// decode at a long context, without running the prompt. Each worker thread owns one sequence (the reference's
+// generate_batch, src/transformer.rs:3588-3606). Positions [0, ctx) of its
+// cache hold synthetic codes and norms and are marked as already dequantized
+// (dequant_pos = ctx - 1, the reference's single shared flat buffer), so the
+// timed positions ctx .. ctx + n_pos - 1 run the reference's per-token work at
+// that context: QKV/Wo/W1/W2/lm_head matvecs, TurboQuant store of the new K
+// and V, incremental dequant of the new position, attention over ctx + 1
+// positions, delta routing. `w_one_layer` is the flat layout of the same
+// model with n_layer = 1; every layer reads that one layer's matrices (each
+// layer's matrices stream from DRAM either way, so the work per token is
+// unchanged). Returns tokens/s of the timed positions (all threads), or < 0.
+double or_time_decode(const or_config *c, int mode, int kb, int vb, const float *w_one_layer, int32_t ctx,
+                      int32_t n_pos, int n_threads) {
+    if (check_cfg(c, ctx + n_pos) || ctx < 1 || n_pos < 1) return -1.0;
+    if (mode != OR_MODE_BASE && mode != OR_MODE_QUANT) return -1.0;
+    Dims d = dims_of(c);
+    or_config c1 = *c;
+    c1.n_layer = 1;
+    Dims d1 = dims_of(&c1);
+    Weights W1 = view_weights(d1, w_one_layer);
+    Weights W = W1;
+    W.layers.assign(d.L, W1.layers[0]);
+    std::vector<float> dq(d.L * d.n, 0.0f), dn(d.L * d.n, 1.0f);  // weights.rs:161-176 init
+    W.dq = dq.data();
+    W.dn = dn.data();
+    if (mode == OR_MODE_QUANT) tq_tables(d.kvd, kb, vb, true);
+    if (n_threads < 1) n_threads = 1;
+    std::vector<double> secs(n_threads, 0.0);
+    std::vector<float> ones(d.n, 1.0f);
+    auto worker = [&](int tid) {
+        Seq s;
+        s.init(d, &W, mode, kb, vb);
+        s.sparse_threshold = c->sparse_threshold;
+        Rng rng(1000 + tid);
+        // synthetic cache contents: a cheap 64-bit counter hash per 8 bytes / value
+        uint64_t z = 0x9E3779B97F4A7C15ULL * (uint64_t)(tid + 1);
+        auto fill_bytes = [&](std::vector<uint8_t> &v) {
+            for (size_t i = 0; i + 8 <= v.size(); i += 8) {
+                z = z * 6364136223846793005ULL + 1442695040888963407ULL;
+                std::memcpy(&v[i], &z, 8);
+            }
+        };
+        auto fill_vals = [&](float *p, int64_t cnt) {
+            for (int64_t i = 0; i < cnt; ++i) {
+                z = z * 6364136223846793005ULL + 1442695040888963407ULL;
+                p[i] = (float)(int32_t)(z >> 40) * (0.01f / 8388608.0f);
+            }
+        };
+        if (mode == OR_MODE_QUANT) {
+            s.quant_shared_flat = true;
+            s.tq = &tq_tables(d.kvd, kb, vb, true);
+            fill_bytes(s.kcodes);
+            fill_bytes(s.vcodes);
+            std::fill(s.knorm.begin(), s.knorm.end(), 1.0f);
+            std::fill(s.vnorm.begin(), s.vnorm.end(), 1.0f);
+            fill_vals(s.flatK.data(), ctx * d.kvd);
+            fill_vals(s.flatV.data(), ctx * d.kvd);
+            std::fill(s.dequant_pos.begin(), s.dequant_pos.end(), (int64_t)ctx - 1);
+        } else {
+            for (int64_t l = 0; l < d.L; ++l) {
+                fill_vals(&s.Kc[l * d.B * d.kvd], ctx * d.kvd);
+                fill_vals(&s.Vc[l * d.B * d.kvd], ctx * d.kvd);
+            }
+        }
+        const auto t0 = std::chrono::steady_clock::now();
+        for (int32_t p = ctx; p < ctx + n_pos; ++p) {
+            const int64_t tok = (int64_t)(rng.next() % (uint64_t)d.V);
+            if (mode == OR_MODE_QUANT) s.forward_quant(tok, p);
+            else s.forward_base(tok, p, ones.data());
+        }
+        secs[tid] = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    };
+    std::vector<std::thread> th;
+    for (int t = 1; t < n_threads; ++t) th.emplace_back(worker, t);
+    worker(0);
+    for (auto &t : th) t.join();
+    double mx = 0.0;
+    for (double v : secs) mx = std::max(mx, v);
+    return mx > 0.0 ? (double)n_threads * n_pos / mx : -1.0;
 }
 
 int or_run_batch(const or_config *c, int mode, int kb, int vb, const float *weights,

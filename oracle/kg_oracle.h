@@ -119,6 +119,15 @@ int or_run_batch_tail(const or_config *c, int mode, int key_bits, int val_bits,
                       const float *weights, const int32_t *tokens, int32_t n_seq, int32_t T,
                       int32_t t0, float *logits, int n_threads);
 
+/* CPU-baseline timing harness (not a reference function): tokens/s of
+ * forward_quantized (mode 1) or forward_base (mode 0) decode at positions
+ * ctx .. ctx+n_pos-1, one sequence per thread, over a cache whose first ctx
+ * positions hold synthetic codes / rows.
+ * w_one_layer: the flat layout of the model with n_layer = 1, its layer
+ * shared by all c->n_layer layers. Returns < 0 on bad arguments. */
+double or_time_decode(const or_config *c, int mode, int key_bits, int val_bits, const float *w_one_layer,
+                      int32_t ctx, int32_t n_pos, int n_threads);
+
 #ifdef __cplusplus
 }
 #endif

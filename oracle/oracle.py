@@ -74,6 +74,7 @@ def lib():
             "or_run_sequence": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, P, P, P, P]),
             "or_run_batch": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, P, ctypes.c_int]),
             "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
+            "or_time_decode": (ctypes.c_double, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, I32, I32, ctypes.c_int]),
         }
         for k, (r, a) in sig.items():
             f = getattr(L, k)
@@ -283,3 +284,15 @@ def run_batch(cfg, mode, w, tokens, key_bits=3, val_bits=3, threads=None, keep_l
     if rc:
         raise RuntimeError(f"or_run_batch failed: {rc}")
     return logits
+
+
+def time_decode(cfg, w_one_layer, ctx, n_pos, mode=MODE_QUANT, key_bits=4, val_bits=4, threads=None):
+    """tokens/s of forward_quantized (MODE_QUANT) or forward_base (MODE_BASE)
+    decode at positions ctx.. (CPU-baseline timing; w_one_layer is the flat
+    weights of the model with n_layer = 1, shared by every layer)."""
+    threads = threads or os.cpu_count() or 1
+    v = lib().or_time_decode(ctypes.byref(cfg), mode, key_bits, val_bits, _p(f32(w_one_layer)), ctx, n_pos,
+                             threads)
+    if v < 0:
+        raise RuntimeError("or_time_decode: bad arguments")
+    return v

@@ -1,0 +1,44 @@
+"""GPU parity at the box-scale decode widths (n_embd 4096, 32 heads of 128,
+mlp 16384, vocab 32000 in the benchmark, 4-bit TurboQuant KV).
+
+The oracle runs forward_quantized in f32 on the same bf16-rounded weights
+(src/transformer.rs:4042-4233). Two layers keep the oracle to about a minute;
+every layer runs the same kernels, so depth adds no kernel shape. Bar (north
+star): logits within 2e-2 relative, per position max|gpu - ref| / max|ref|.
+Weights ~N(0, 0.02), the distribution the benchmark draws.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL_BF16 = 2e-2
+C5_WIDTHS = dict(n_embd=4096, n_head=32, head_dim=128, n_kv_head=32, mlp_hidden=16384, key_bits=4, val_bits=4)
+
+
+def rel_err(a, b):
+    den = np.maximum(np.abs(b).max(axis=-1), 1e-30)
+    return np.abs(a - b).max(axis=-1) / den
+
+
+def test_c5_widths_prefill_then_decode_match_oracle(kg, orc):
+    # 2 sequences: a 256-token prefill (512 rows: the tcgen05 GEMMs, the
+    # tensor-core encoder with exact fix-up, flash attention over dequantized
+    # rows), then single-token decode steps to position 299 (rotated-domain
+    # attention over the codes with 32 heads, the exact tiled encoder)
+    cfg = kg.micro_config(vocab_size=512, block_size=320, n_layer=2, kv_mode=kg.KG_KV_TQ,
+                          weight_dtype=kg.KG_W_BF16, max_seqs=2, **C5_WIDTHS)
+    be = kg.CudaBackend(cfg)
+    w = kg.bf16_round(kg.reference_weights(cfg, seed=13, scale_mode=1, std=0.02))
+    be.compile(w)
+    T0, T = 256, 300
+    toks = np.random.default_rng(29).integers(0, cfg.vocab_size, size=(2, T)).astype(np.int32)
+    pre = be.forward_batch(toks[:, :T0])
+    dec = np.stack([be.forward_batch(toks[:, t:t + 1], start_pos=np.full(2, t))[:, 0] for t in range(T0, T)], axis=1)
+    got = np.concatenate([pre, dec], axis=1)
+    ref = orc.run_batch(orc.from_kg(cfg), orc.MODE_QUANT, w, toks, key_bits=4, val_bits=4, threads=2)
+    for i in range(2):
+        err = rel_err(got[i], ref[i])
+        print("c5 widths seq %d: max rel err prefill %.2e decode %.2e" % (i, err[:T0].max(), err[T0:].max()))
+        assert err.max() <= REL_BF16, (i, int(np.argmax(err)), float(err.max()))
+    be.close()
