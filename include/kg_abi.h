@@ -99,8 +99,13 @@ const char *kg_device_name(const kg_ctx *ctx);
 
 /* Number of floats in the flat weight layout: wte[V*n], wpe[block*n], per
  * layer {wq[n*n], wk[kvd*n], wv[kvd*n], wo[n*n], w1[m*n], w2[n*m]},
- * lm_head[V*n], delta_routing_query[L*n], delta_routing_norm[L*n] — the
- * TransformerWeights field order (crates/katgpt-transformer/src/weights.rs:76-177). */
+ * lm_head[V*n], delta_routing_query[L*n], delta_routing_norm[L*n],
+ * attn_norm_gamma[L*n], mlp_norm_gamma[L*n] — the TransformerWeights field
+ * order (crates/katgpt-transformer/src/weights.rs:12-30, 76-177), the two
+ * kog_cpu_fusion gammas last. forward_base (KG_KV_F32) applies both gammas at
+ * run time (src/transformer.rs:1893-1895, 2023-2026); forward_quantized and
+ * forward_sp_kv_quant normalise without them, as the reference does. A model
+ * whose MLP gamma was folded into w1 (weights.rs:205-221) passes ones. */
 int64_t kg_weights_count(const kg_config *cfg);
 
 /* TransformerWeights::new(config, Rng::new(seed)) (weights.rs:76-177) into a

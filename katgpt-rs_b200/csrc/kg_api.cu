@@ -276,7 +276,9 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     a.off_lm = (int)(a.off_layers + L * a.layer_stride);
     a.off_dq = (int)(a.off_lm + V * n);
     a.off_dn = (int)(a.off_dq + L * n);
-    off = a.off_dn + L * n;  // == w_count
+    a.off_ag = (int)(a.off_dn + L * n);
+    a.off_mg = (int)(a.off_ag + L * n);
+    off = a.off_mg + L * n;  // == w_count
     a.off_rot = (int)off; off += tq ? kvd * kvd : 0;
     a.off_rot_t = (int)off; off += tq ? kvd * kvd : 0;
     a.off_kc = (int)off; off += (int64_t)kc.size();
@@ -400,6 +402,10 @@ int kg_download_weights(kg_ctx *ctx, float *out, int64_t count) {
     }
     KG_CUDA(ctx, cudaMemcpyAsync(out + nbf, ctx->big.dq, ctx->L * ctx->n * 4, cudaMemcpyDeviceToHost, ctx->stream));
     KG_CUDA(ctx, cudaMemcpyAsync(out + nbf + ctx->L * ctx->n, ctx->big.dn, ctx->L * ctx->n * 4,
+                                 cudaMemcpyDeviceToHost, ctx->stream));
+    KG_CUDA(ctx, cudaMemcpyAsync(out + nbf + 2 * ctx->L * ctx->n, ctx->big.ag, ctx->L * ctx->n * 4,
+                                 cudaMemcpyDeviceToHost, ctx->stream));
+    KG_CUDA(ctx, cudaMemcpyAsync(out + nbf + 3 * ctx->L * ctx->n, ctx->big.mg, ctx->L * ctx->n * 4,
                                  cudaMemcpyDeviceToHost, ctx->stream));
     KG_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     return KG_OK;

@@ -363,7 +363,7 @@ __device__ __forceinline__ void put_split(bf16 *yb, bf16 *yb2, int64_t i, float 
 }
 
 __global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, int twice,
-                               int *zero_count) {
+                               int *zero_count, const float *gamma) {
     pdl_wait();
     __shared__ float red[32];
     const int m = blockIdx.x;
@@ -391,6 +391,7 @@ __global__ void rmsnorm_kernel(const float *x, int n, int M, float *yf, bf16 *yb
     __syncthreads();
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
         float v = xr[j] * inv;
+        if (gamma) v = gamma[j] * v;
         if (yf) yf[(int64_t)m * n + j] = v;
         put_split(yb, yb2, (int64_t)m * n + j, v);
     }
@@ -624,9 +625,10 @@ cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const
     return launch_pdl(embed_kernel, dim3(M), dim3(256), 0, s, tok, pos, wte, wpe, n, M, x, zero_rows);
 }
 cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s,
-                    int *zero_count) {
+                    int *zero_count, const float *gamma) {
     if (M <= 0) return cudaSuccess;
-    return launch_pdl(rmsnorm_kernel, dim3(M), dim3(256), 0, s, x, n, M, yf, yb, yb2, twice ? 1 : 0, zero_count);
+    return launch_pdl(rmsnorm_kernel, dim3(M), dim3(256), 0, s, x, n, M, yf, yb, yb2, twice ? 1 : 0, zero_count,
+                      gamma);
 }
 cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;

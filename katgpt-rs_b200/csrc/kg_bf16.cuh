@@ -69,8 +69,9 @@ cudaError_t embed(const int32_t *tok, const int32_t *pos, const bf16 *wte, const
 // per row: y = x / sqrt(mean(x^2) + 1e-5); `twice` applies it twice (sp_kv double norm).
 // Writes f32 (if yf) and the bf16 hi/lo split (if yb / yb2). In-place allowed (yf == x).
 // zero_count (optional, [M]) is cleared on the way (the next ReLU GEMM's alive counts).
+// gamma (optional, [n]): rmsnorm_with_gamma, y = gamma * (x * inv_rms) (math.rs:218-233).
 cudaError_t rmsnorm(const float *x, int n, int M, float *yf, bf16 *yb, bf16 *yb2, bool twice, cudaStream_t s,
-                    int *zero_count = nullptr);
+                    int *zero_count = nullptr, const float *gamma = nullptr);
 // f32 -> bf16 hi (+ lo) split (strided rows)
 cudaError_t to_bf16(const float *x, int64_t ldx, int n, int M, bf16 *y, bf16 *y2, int64_t ldy, cudaStream_t s);
 // f32 -> f16 hi + lo split (strided rows)

@@ -124,6 +124,8 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.w2t, L * m * n, own));
     BIG_TRY(dalloc(&g.dq, L * n, own));
     BIG_TRY(dalloc(&g.dn, L * n, own));
+    BIG_TRY(dalloc(&g.ag, L * n, own));
+    BIG_TRY(dalloc(&g.mg, L * n, own));
     g.std_kv = c.kv_mode == KG_KV_F32;
     if (g.std_kv) {  // standard attention: bf16 K/V arena
         BIG_TRY(dalloc(&g.kcache, (size_t)S * L * B * kvd, own));
@@ -225,7 +227,8 @@ cudaError_t big_upload_chunk(kg_ctx *ctx, const float *dsrc, int64_t offset, int
     return bf::f32_to_bf16_flat(dsrc, count, g.wall + offset, ctx->stream);
 }
 
-// Delta-routing tables (f32, [2][L][n]) and W2^T for the TwELL gather.
+// The f32 tail of the flat layout (delta-routing query and norm, attention and
+// MLP norm gammas: [4][L][n]) and W2^T for the TwELL gather.
 cudaError_t big_finish_upload(kg_ctx *ctx, const float *dq_dn_dev) {
     BigState &g = ctx->big;
     const int64_t n = ctx->n, kvd = ctx->kvd, m = ctx->m, L = ctx->L;
@@ -234,6 +237,8 @@ cudaError_t big_finish_upload(kg_ctx *ctx, const float *dq_dn_dev) {
     if (dq_dn_dev) {
         BIG_TRY(cudaMemcpyAsync(g.dq, dq_dn_dev, L * n * 4, cudaMemcpyDeviceToDevice, s));
         BIG_TRY(cudaMemcpyAsync(g.dn, dq_dn_dev + L * n, L * n * 4, cudaMemcpyDeviceToDevice, s));
+        BIG_TRY(cudaMemcpyAsync(g.ag, dq_dn_dev + 2 * L * n, L * n * 4, cudaMemcpyDeviceToDevice, s));
+        BIG_TRY(cudaMemcpyAsync(g.mg, dq_dn_dev + 3 * L * n, L * n * 4, cudaMemcpyDeviceToDevice, s));
     }
     for (int64_t l = 0; l < L; ++l) {
         const bf16 *w2 = g.layers + l * per_layer + 2 * n * n + 2 * kvd * n + m * n;  // [n x m]
@@ -270,13 +275,15 @@ __global__ void bf16_to_f32_kernel(const bf16 *a, int64_t count, float *o) {
 }
 }  // namespace
 
-// Synthetic weights N(0, std) for every bf16 tensor; delta query 0, norm 1.
+// Synthetic weights N(0, std) for every bf16 tensor; delta query 0, norm and gammas 1.
 cudaError_t big_random_weights(kg_ctx *ctx, uint64_t seed, float std_) {
     BigState &g = ctx->big;
     cudaStream_t s = ctx->stream;
     random_bf16_kernel<<<2048, 256, 0, s>>>(g.wall, g.nbf, seed, std_);
     fill_kernel<<<64, 256, 0, s>>>(g.dq, ctx->L * ctx->n, 0.0f);
     fill_kernel<<<64, 256, 0, s>>>(g.dn, ctx->L * ctx->n, 1.0f);
+    fill_kernel<<<64, 256, 0, s>>>(g.ag, ctx->L * ctx->n, 1.0f);
+    fill_kernel<<<64, 256, 0, s>>>(g.mg, ctx->L * ctx->n, 1.0f);
     BIG_TRY(cudaGetLastError());
     return big_finish_upload(ctx, nullptr);
 }
@@ -332,11 +339,15 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         const bf16 *w1 = wo + (int64_t)n * n;
         const bf16 *w2 = w1 + (int64_t)m * n;
         // pre-attention norm: residual xr = norm(x); sp_kv normalises a second time
+        // forward_base (standard attention) applies attn_norm_gamma at run time
+        // (kog_cpu_fusion, src/transformer.rs:1893-1895); forward_quantized and
+        // forward_sp_kv_quant use plain rmsnorm (:4076, sp_kv/forward.rs:649-651)
         if (spkv) {
             BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, nullptr, nullptr, false, s));
             BIG_TRY(bf::rmsnorm(g.xr, n, M, nullptr, g.xb, g.xb2, false, s));
         } else {
-            BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, g.xb, g.xb2, false, s));
+            BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, g.xb, g.xb2, false, s, nullptr,
+                                g.std_kv ? g.ag + (int64_t)l * n : nullptr));
         }
         // decode steps of fewer than 256 rows run the mma.sync GEMMs, whose
         // epilogues also produce q's f16 split, the attention output's bf16
@@ -473,7 +484,9 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         BIG_TRY(gemm_split(ctx, w, s));
         prof_mark(ctx, KG_PROF_GEMM, 1, s);
         // MLP
-        BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s, g.alive));  // also clears alive counts
+        // also clears alive counts; mlp_norm_gamma for forward_base (src/transformer.rs:2023-2026)
+        BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s, g.alive,
+                            g.std_kv ? g.mg + (int64_t)l * n : nullptr));
         bf::Gemm u = gemm0();
         u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
         u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;

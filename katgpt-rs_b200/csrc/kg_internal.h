@@ -19,7 +19,7 @@ struct MicroArgs {
     // layout), TurboQuant tables, SP-KV predictor
     const float *pack;
     int pack_floats;
-    int off_wte, off_wpe, off_layers, layer_stride, off_lm, off_dq, off_dn;
+    int off_wte, off_wpe, off_layers, layer_stride, off_lm, off_dq, off_dn, off_ag, off_mg;
     int off_rot, off_rot_t, off_kc, off_kb, off_vc, off_vb;
     int off_pw1, off_pb1, off_pw2, off_pb2;
     int L;
@@ -93,6 +93,7 @@ struct BigState {
     __nv_bfloat16 *wall = nullptr;  // [wte | wpe | layers | lm_head] in flat reference order
     __nv_bfloat16 *wte = nullptr, *wpe = nullptr, *layers = nullptr, *lm = nullptr, *w2t = nullptr;
     float *dq = nullptr, *dn = nullptr;                // delta routing query / norm [L][n]
+    float *ag = nullptr, *mg = nullptr;                // attn_norm_gamma / mlp_norm_gamma [L][n]
     __half *rot_h = nullptr, *rot_l = nullptr, *rot_th = nullptr, *rot_tl = nullptr;  // f16 hi/lo of R, R^T
     float *kcent = nullptr, *vcent = nullptr;          // 16 centroids each
     uint8_t *kcodes = nullptr, *vcodes = nullptr;      // [slot][layer][pos][pl]

@@ -95,13 +95,23 @@ __device__ __forceinline__ void tq_roundtrip(const float (&vec)[KVD], const floa
     for (int i = 0; i < KVD; ++i) deq[i] = kgx::dot<KVD>(rot_t + i * KVD, c) * norm;
 }
 
-// rmsnorm / rmsnorm_with_gamma(gamma = 1): x * (1 / sqrt(sum_sq/n + 1e-5))
+// rmsnorm (math.rs:56-69): x * (1 / sqrt(sum_sq/n + 1e-5))
 template <int N>
 __device__ __forceinline__ void rmsnorm(float (&x)[N]) {
     float ss = kgx::sum_sq<N>(x);
     float inv = 1.0f / sqrtf(ss / (float)N + 1e-5f);
 #pragma unroll
     for (int i = 0; i < N; ++i) x[i] = x[i] * inv;
+}
+// rmsnorm_with_gamma (math.rs:218-233 -> simd_scale_mul_inplace, elementwise.rs:1249-1270):
+// g * (x * inv) over whole 8-lane chunks, (g * x) * inv in the scalar tail
+template <int N>
+__device__ __forceinline__ void rmsnorm_gamma(float (&x)[N], const float *g) {
+    float ss = kgx::sum_sq<N>(x);
+    float inv = 1.0f / sqrtf(ss / (float)N + 1e-5f);
+    constexpr int BODY = N / 8 * 8;
+#pragma unroll
+    for (int i = 0; i < N; ++i) x[i] = i < BODY ? g[i] * (x[i] * inv) : (g[i] * x[i]) * inv;
 }
 
 template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE>
@@ -150,7 +160,12 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         const float *w1 = wo + N * N, *w2 = w1 + M * N;
         const int64_t row = ((int64_t)slot * p.L + l) * BLK;  // [slot][layer] base (positions)
 
-        rmsnorm<N>(x);
+        // forward_base (kog_cpu_fusion) applies attn_norm_gamma at run time
+        // (src/transformer.rs:1893-1895); the quantized forwards use plain rmsnorm
+        if constexpr (MODE == MODE_BASE)
+            rmsnorm_gamma<N>(x, sm + p.off_ag + l * N);
+        else
+            rmsnorm<N>(x);
         float xr[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) xr[j] = x[j];
@@ -285,7 +300,10 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         float xr2[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) xr2[j] = x[j];
-        rmsnorm<N>(x);
+        if constexpr (MODE == MODE_BASE)
+            rmsnorm_gamma<N>(x, sm + p.off_mg + l * N);  // mlp_norm_gamma (src/transformer.rs:2023-2026)
+        else
+            rmsnorm<N>(x);
         float hid[M];
         int alive = 0;
 #pragma unroll

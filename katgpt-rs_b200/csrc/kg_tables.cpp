@@ -54,7 +54,7 @@ int64_t weights_count(const kg_config &c) {
     int64_t n = c.n_embd, kvd = (int64_t)c.n_kv_head * c.head_dim, m = c.mlp_hidden;
     int64_t per_layer = 2 * n * n + 2 * kvd * n + 2 * m * n;
     return (int64_t)c.vocab_size * n * 2 + (int64_t)c.block_size * n + c.n_layer * per_layer +
-           2 * (int64_t)c.n_layer * n;
+           4 * (int64_t)c.n_layer * n;
 }
 
 // crates/katgpt-transformer/src/weights.rs:76-177
@@ -74,6 +74,8 @@ void reference_weights(const kg_config &c, uint64_t seed, int scale_mode, float 
     for (int64_t i = 0; i < (int64_t)c.vocab_size * n; ++i) *p++ = rng.normal() * es;
     for (int64_t i = 0; i < (int64_t)c.n_layer * n; ++i) *p++ = 0.0f;  // delta_routing_query
     for (int64_t i = 0; i < (int64_t)c.n_layer * n; ++i) *p++ = 1.0f;  // delta_routing_norm
+    for (int64_t i = 0; i < (int64_t)c.n_layer * n; ++i) *p++ = 1.0f;  // attn_norm_gamma (weights.rs:142-143)
+    for (int64_t i = 0; i < (int64_t)c.n_layer * n; ++i) *p++ = 1.0f;  // mlp_norm_gamma (weights.rs:144-145)
 }
 
 // ---- Lloyd-Max codebook, src/turboquant/codebook.rs:20-198 ----

@@ -379,11 +379,12 @@ struct LayerW {
 };
 struct Weights {
     const float *wte, *wpe, *lm_head, *dq, *dn;
+    const float *ag, *mg;  // attn_norm_gamma / mlp_norm_gamma [L][n] (weights.rs:20-25, 142-145)
     std::vector<LayerW> layers;
 };
 static int64_t weights_count(const Dims &d) {
     int64_t per_layer = 2 * d.n * d.n + 2 * d.kvd * d.n + 2 * d.m * d.n;
-    return d.V * d.n + d.B * d.n + d.L * per_layer + d.V * d.n + 2 * d.L * d.n;
+    return d.V * d.n + d.B * d.n + d.L * per_layer + d.V * d.n + 4 * d.L * d.n;
 }
 static Weights view_weights(const Dims &d, const float *w) {
     Weights W;
@@ -402,7 +403,9 @@ static Weights view_weights(const Dims &d, const float *w) {
     }
     W.lm_head = p; p += d.V * d.n;
     W.dq = p; p += d.L * d.n;
-    W.dn = p;
+    W.dn = p; p += d.L * d.n;
+    W.ag = p; p += d.L * d.n;
+    W.mg = p;
     return W;
 }
 
@@ -850,9 +853,9 @@ struct Seq {
     }
 
     // MLP block shared by all three forwards: xr2=x; norm; relu(W1); sparse/dense W2; += xr2
-    void mlp(const LayerW &lw, bool gamma_norm, const float *ones) {
+    void mlp(const LayerW &lw, bool gamma_norm, const float *gamma) {
         xr2 = x;
-        if (gamma_norm) rmsnorm_gamma(x.data(), ones, d.n);
+        if (gamma_norm) rmsnorm_gamma(x.data(), gamma, d.n);
         else rmsnorm(x.data(), d.n);
         matmul_relu(hidden.data(), lw.w1, x.data(), d.m, d.n);
         int64_t alive = sparse_matmul(x.data(), lw.w2, hidden.data(), d.n, d.m, aidx.data(), aval.data());
@@ -870,13 +873,15 @@ struct Seq {
             depth_route(x.data(), deltas, bidx, W->dq + l * d.n, W->dn + l * d.n, d.n, scaled);
     }
 
-    // transformer.rs:1821-2200 (forward_base, default features, lora=None)
-    void forward_base(int64_t tok, int64_t pos, const float *ones) {
+    // transformer.rs:1821-2200 (forward_base, default features, lora=None);
+    // kog_cpu_fusion applies attn_norm_gamma (:1893-1895) and mlp_norm_gamma
+    // (:2023-2026) at run time through rmsnorm_with_gamma
+    void forward_base(int64_t tok, int64_t pos) {
         add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
         float scale = 1.0f / sqrtf((float)d.hd);
         for (int64_t l = 0; l < d.L; ++l) {
             const LayerW &lw = W->layers[l];
-            rmsnorm_gamma(x.data(), ones, d.n);
+            rmsnorm_gamma(x.data(), W->ag + l * d.n, d.n);
             xr = x;
             matmul(q.data(), lw.wq, x.data(), d.n, d.n);
             matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
@@ -891,7 +896,7 @@ struct Seq {
             }
             matmul(x.data(), lw.wo, att.data(), d.n, d.n);
             add_inplace(x.data(), xr.data(), d.n);
-            mlp(lw, true, ones);
+            mlp(lw, true, W->mg + l * d.n);
             delta_route(l);
         }
         matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
@@ -1010,8 +1015,7 @@ static const Predictor &predictor_for(int64_t n, int64_t nkv) {
 
 static int run_one(const or_config *c, int mode, int kb, int vb, const Weights &W, const Dims &d,
                    const int32_t *tokens, int32_t T, float *logits, int32_t t0, uint8_t *codes,
-                   float *norms, float *utilities, bool shared_flat, Seq &s,
-                   const std::vector<float> &ones) {
+                   float *norms, float *utilities, bool shared_flat, Seq &s) {
     s.init(d, &W, mode == 3 ? OR_MODE_QUANT : mode, kb, vb);
     s.sparse_threshold = c->sparse_threshold;
     s.quant_shared_flat = shared_flat;
@@ -1024,7 +1028,7 @@ static int run_one(const or_config *c, int mode, int kb, int vb, const Weights &
     for (int32_t p = 0; p < T; ++p) {
         int64_t tok = tokens[p];
         if (tok < 0 || tok >= d.V) return -2;
-        if (mode == OR_MODE_BASE) s.forward_base(tok, p, ones.data());
+        if (mode == OR_MODE_BASE) s.forward_base(tok, p);
         else if (mode == OR_MODE_SPKV_QUANT) s.forward_spkv(tok, p);
         else s.forward_quant(tok, p);
         if (logits && p >= t0) std::memcpy(logits + (int64_t)(p - t0) * d.V, s.logits.data(), d.V * 4);
@@ -1089,6 +1093,8 @@ void or_weights_init(const or_config *c, uint64_t seed, int scale_mode, float st
     for (int64_t i = 0; i < d.V * d.n; ++i) *p++ = rng.normal() * es;
     for (int64_t i = 0; i < d.L * d.n; ++i) *p++ = 0.0f;  // delta query: zeros (weights.rs:161-168)
     for (int64_t i = 0; i < d.L * d.n; ++i) *p++ = 1.0f;  // delta norm gamma: ones (:169-176)
+    for (int64_t i = 0; i < d.L * d.n; ++i) *p++ = 1.0f;  // attn_norm_gamma: ones (:142-143)
+    for (int64_t i = 0; i < d.L * d.n; ++i) *p++ = 1.0f;  // mlp_norm_gamma: ones (:144-145)
 }
 
 float or_dot(const float *a, const float *b, int64_t len) { return dot(a, b, len); }
@@ -1186,11 +1192,10 @@ int or_run_sequence(const or_config *c, int mode, int kb, int vb, const float *w
     if (mode < 0 || mode > 3) return -1;
     Dims d = dims_of(c);
     Weights W = view_weights(d, weights);
-    std::vector<float> ones(d.n, 1.0f);
     Seq s;
     // mode 3: forward_quantized with the reference's single shared flat buffer
     return run_one(c, mode, kb, vb, W, d, tokens, T, logits, 0, codes, norms, utilities, mode == 3,
-                   s, ones);
+                   s);
 }
 
 int or_run_batch_tail(const or_config *c, int mode, int kb, int vb, const float *weights,
@@ -1200,7 +1205,6 @@ int or_run_batch_tail(const or_config *c, int mode, int kb, int vb, const float 
     if (mode < 0 || mode > 3 || t0 < 0 || t0 > T) return -1;
     Dims d = dims_of(c);
     Weights W = view_weights(d, weights);
-    std::vector<float> ones(d.n, 1.0f);
     if (mode != OR_MODE_BASE) tq_tables(d.kvd, kb, vb);
     if (mode == OR_MODE_SPKV_QUANT) predictor_for(d.n, d.nkv);
     if (n_threads < 1) n_threads = 1;
@@ -1210,7 +1214,7 @@ int or_run_batch_tail(const or_config *c, int mode, int kb, int vb, const float 
         for (int32_t i = tid; i < n_seq; i += n_threads) {
             float *lo = logits ? logits + (int64_t)i * (T - t0) * d.V : nullptr;
             int r = run_one(c, mode, kb, vb, W, d, tokens + (int64_t)i * T, T, lo, t0, nullptr,
-                            nullptr, nullptr, mode == 3, s, ones);
+                            nullptr, nullptr, mode == 3, s);
             if (r) rc[tid] = r;
         }
     };
@@ -1246,13 +1250,14 @@ double or_time_decode(const or_config *c, int mode, int kb, int vb, const float 
     Weights W1 = view_weights(d1, w_one_layer);
     Weights W = W1;
     W.layers.assign(d.L, W1.layers[0]);
-    std::vector<float> dq(d.L * d.n, 0.0f), dn(d.L * d.n, 1.0f);  // weights.rs:161-176 init
+    std::vector<float> dq(d.L * d.n, 0.0f), dn(d.L * d.n, 1.0f);  // weights.rs:142-145, 161-176 init
     W.dq = dq.data();
     W.dn = dn.data();
+    W.ag = dn.data();
+    W.mg = dn.data();
     if (mode == OR_MODE_QUANT) tq_tables(d.kvd, kb, vb, true);
     if (n_threads < 1) n_threads = 1;
     std::vector<double> secs(n_threads, 0.0);
-    std::vector<float> ones(d.n, 1.0f);
     auto worker = [&](int tid) {
         Seq s;
         s.init(d, &W, mode, kb, vb);
@@ -1292,7 +1297,7 @@ double or_time_decode(const or_config *c, int mode, int kb, int vb, const float 
         for (int32_t p = ctx; p < ctx + n_pos; ++p) {
             const int64_t tok = (int64_t)(rng.next() % (uint64_t)d.V);
             if (mode == OR_MODE_QUANT) s.forward_quant(tok, p);
-            else s.forward_base(tok, p, ones.data());
+            else s.forward_base(tok, p);
         }
         secs[tid] = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     };
