@@ -175,6 +175,25 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids,
                          const int32_t *tokens, const int32_t *start_pos, int32_t T,
                          float *logits_out, float *probs_out, void *stream);
 
+/* ---- sampling (sample_token_into, crates/katgpt-types/src/math.rs:398-422) ---- */
+
+/* Seed sequence slot `seq`'s generator with Rng::new(seed)
+ * (crates/katgpt-types/src/rng.rs:34-49). Every slot starts as Rng::new(slot). */
+int kg_rng_seed(kg_ctx *ctx, int32_t seq, uint64_t seed);
+/* Current XorShift64 state of slot `seq`'s generator. */
+int kg_rng_state(kg_ctx *ctx, int32_t seq, uint64_t *state_out);
+/* For each row i < n_rows: r = Rng::uniform() of slot seq_ids[i]'s generator,
+ * redrawn while r == 0; tokens_out[i] = the first index whose running f32 sum
+ * of probs[i][0..vocab) (index order) exceeds r, at most vocab - 1 — the
+ * reference's CDF + partition_point. probs rows are ld_probs floats apart
+ * (e.g. the probs_out of kg_forward_batch_dev); seq_ids NULL means row i uses
+ * slot i. Device pointers, enqueued on `stream`; each row advances its slot's
+ * generator by the draws it took. */
+int kg_sample_dev(kg_ctx *ctx, int32_t n_rows, const int32_t *seq_ids, const float *probs, int64_t ld_probs,
+                  int32_t *tokens_out, void *stream);
+/* Host-pointer form (probs [n_rows][vocab]); synchronises. */
+int kg_sample(kg_ctx *ctx, int32_t n_rows, const int32_t *seq_ids, const float *probs, int32_t *tokens_out);
+
 /* ---- TurboQuant codec access (parity / inspection) ---- */
 
 /* Packed bytes per vector for `bits` at dimension `dim` (kv_cache.rs:499-509). */

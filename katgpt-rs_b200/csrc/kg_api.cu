@@ -216,6 +216,8 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     if ((rc = dalloc(ctx, &ctx->norms, rows * 2))) return bail(rc);
     if ((rc = dalloc(ctx, &ctx->util, rows))) return bail(rc);
     if ((rc = dalloc(ctx, &ctx->d_err, 1))) return bail(rc);
+    e = kg::sampler_init(ctx);
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "sampler init"));
 
     // ---- TurboQuant tables (TurboQuantKVCache::new, kv_cache.rs:56-99)
     const int64_t kvd = ctx->kvd;

@@ -38,9 +38,18 @@ struct TqAttnArgs {
     int M, nh, kvd, kpl, vpl, L, B, layer, Sp, nc16;
     float scale;
     int rsk;                          // set by the launcher
+    // tcgen05 path (kg_tcattn.cu): 32-position chunk statistics in cmax / csum
+    // ([M][nc32][nh]), 1 / softmax denominator per (token, head), arena slots
+    int nc32;
+    float *linv;                      // [M][nh]
+    int n_slots;
 };
 int tq_padded_len(int block_size);
 cudaError_t tq_decode_attn(const TqAttnArgs &a, cudaStream_t s);
+// The tcgen05 form (kg_tcattn.cu): 4-bit / nibble-packed codes, kv_dim a
+// multiple of 256, at most 32 heads, block_size <= 6144.
+bool tc_attn_supported(const TqAttnArgs &a);
+cudaError_t tc_decode_attn(const TqAttnArgs &a, cudaStream_t s);
 
 // Standard attention over a bf16 K/V cache [slot][layer][pos][kvd].
 struct StdDecodeArgs {

@@ -188,6 +188,7 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.pe, S * ctx->nh * g.Sp, own));
     BIG_TRY(dalloc(&g.pmax, S * (g.Sp / 16) * ctx->nh, own));
     BIG_TRY(dalloc(&g.psum, S * (g.Sp / 16) * ctx->nh, own));
+    BIG_TRY(dalloc(&g.linv, S * ctx->nh, own));
     // centroid tables
     BIG_TRY(dalloc(&g.kcent, 16, own));
     BIG_TRY(dalloc(&g.vcent, 16, own));
@@ -459,6 +460,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             ta.M = M; ta.nh = nh; ta.kvd = kvd; ta.kpl = (int)ctx->kpl; ta.vpl = (int)ctx->vpl;
             ta.L = L; ta.B = B; ta.layer = l; ta.Sp = g.Sp; ta.nc16 = g.Sp / 16; ta.scale = scale;
             ta.err = ctx->d_err;
+            ta.nc32 = g.Sp / 32; ta.linv = g.linv; ta.n_slots = c.max_seqs;
             prof_mark(ctx, KG_PROF_ATTN, 0, s);
             BIG_TRY(attn::tq_decode_attn(ta, s));
             prof_mark(ctx, KG_PROF_ATTN, 1, s);

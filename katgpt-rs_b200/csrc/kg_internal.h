@@ -117,7 +117,7 @@ struct BigState {
     // two-kernel decode attention scratch: e rows [max_seqs][nh][Sp] and
     // 16-position chunk maxima / sums [max_seqs][Sp / 16][nh]
     __half *pe = nullptr;
-    float *pmax = nullptr, *psum = nullptr;
+    float *pmax = nullptr, *psum = nullptr, *linv = nullptr;
     int Sp = 0;
 };
 int big_supported(const kg_config &c, std::string &why);
@@ -182,6 +182,8 @@ struct kg_ctx {
     // forked from and joined back to the calling stream through events
     cudaStream_t aux = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    // per-slot Rng state of sample_token_into on the device (kg_sample.cu)
+    uint64_t *rng = nullptr;
 };
 
 namespace kg {
@@ -194,4 +196,6 @@ cudaError_t big_random_weights(kg_ctx *ctx, uint64_t seed, float std_);
 cudaError_t big_download(kg_ctx *ctx, float *dst_dev, int64_t offset, int64_t count);
 cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const int32_t *tokens,
                         const int32_t *start_pos, int T, float *logits, float *probs, cudaStream_t s);
+// per-slot sampler generators, Rng::new(slot) (kg_sample.cu)
+cudaError_t sampler_init(kg_ctx *ctx);
 }  // namespace kg

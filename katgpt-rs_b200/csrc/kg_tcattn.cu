@@ -1,0 +1,480 @@
+// kg_tcattn.cu — decode attention over 4-bit / 3-bit TurboQuant codes on the
+// 5th-generation tensor cores (tcgen05), in the rotated domain.
+//
+// Math (forward_quantized attention, src/transformer.rs:4123-4141, softmax
+// :333-389; a stored vector is norm * R^T centroid(code),
+// src/turboquant/kv_cache.rs:279-317), per token m and head h:
+//   s[t,h] = norm_k[t] * scale * <centroid(code_k[t]), q~_h>
+//   u~_h   = sum_t softmax_t(s[., h])[t] * norm_v[t] * centroid(code_v[t])
+// Three launches per layer:
+//  * tc_scores_kernel — CTA = (two 128-position tiles, token). D[128 positions
+//    x NHP heads] += A[positions x 16 dims] B[16 dims x heads] with A in
+//    tensor memory: decoder thread r owns TMEM lane r (= position r of its
+//    tile), turns its row's 32 code bytes per 64-dim block into f16 centroid
+//    pairs through a 32-replica shared-memory table (entry (b, l) at word
+//    32 b + l, lane l reads replica l: conflict-free) and stores them with
+//    tcgen05.st; q~ arrives by TMA (128-byte swizzle) as the B operand. The
+//    epilogue scales by norm_k * scale, and per 32-position chunk writes the
+//    head maxima c, the sums sum exp(s - c) and e = exp(s - c) * norm_v (f16).
+//  * tc_softmax_kernel — per (token, head): the global max M over the chunks,
+//    l = sum_c csum_c exp(c - M), 1 / l, and e *= exp(c - M) in place, so the
+//    values kernel can load e by TMA as an operand.
+//  * tc_values_kernel — CTA = (256 dims, token). D[128 dims x NHP heads] +=
+//    A[dims x 16 positions] B[16 positions x heads] with A = the decoded value
+//    rows in shared memory as an MN-major operand (rows = positions, 64 dims
+//    per 128-byte swizzled row: the decode writes rows exactly as the codes
+//    lie) and B = e rows by TMA. The epilogue writes u~ = D / l as f16 hi / lo.
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (one
+// thread), warps 2..9 decoders and epilogue. Every mbarrier wait is bounded:
+// on expiry the CTA raises its abort flag, KG_ERR_TIMEOUT goes to the error
+// word, every warp still passes the barriers it owes and the tensor memory is
+// released.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "kg_async.cuh"
+#include "kg_attn.cuh"
+#include "kg_dev.cuh"
+#include "kg_pdl.cuh"
+#include "kg_tc.cuh"
+
+namespace kg {
+namespace attn {
+namespace {
+
+constexpr int TCW = 320;        // threads per CTA (10 warps)
+constexpr int LUTW = 256 * 32;  // words of the replicated code-byte -> centroid-pair table
+constexpr uint32_t FULLM = 0xffffffffu;
+
+// scores
+constexpr int S_STG = 3;
+constexpr int S_TILE = 128;                          // positions per tile (TMEM lanes)
+constexpr int S_KB = 64;                             // dims per K block: 32 code bytes per row
+constexpr int S_CODE = 2 * S_TILE * 32;              // two tiles of 128 rows x 32 B
+constexpr int S_Q = 32 * 128;                        // q~ block: up to 32 heads x 64 dims (f16)
+constexpr int S_STAGE = S_CODE + S_Q;                // 12 KB
+constexpr int S_CH = 33;                             // padded 32-position chunk in the transpose buffer
+constexpr int S_TCOLS = 256;                         // acc (2 x 32) + A (3 stages x 2 tiles x 32)
+// values
+constexpr int V_STG = 3;
+constexpr int V_KB = 64;                             // positions per K block
+constexpr int V_DG = 256;                            // dims per CTA (128 code bytes per row)
+constexpr int V_CODE = V_KB * (V_DG / 2);            // 8 KB
+constexpr int V_E = 32 * 128;                        // e block: up to 32 heads x 64 positions (f16)
+constexpr int V_STAGE = V_CODE + V_E;                // 12 KB
+constexpr int V_ATOM = V_KB * 128;                   // one 64-dim atom of A: 64 rows x 128 B
+constexpr int V_A = 4 * V_ATOM;                      // 32 KB
+
+struct ScoreMaps {
+    CUtensorMap codes, q;
+};
+struct ValueMaps {
+    CUtensorMap codes, e;
+};
+
+__device__ __forceinline__ uint32_t h2u(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+// byte b -> (centroid[b & 15], centroid[b >> 4]) as an f16 pair, 32 replicas
+__device__ __forceinline__ void lut_build(uint32_t *lut, const float *cent) {
+    for (int i = threadIdx.x; i < LUTW / 4; i += blockDim.x) {
+        const int b = i >> 3;
+        const uint32_t v = h2u(__ldg(cent + (b & 15)), __ldg(cent + (b >> 4)));
+        reinterpret_cast<uint4 *>(lut)[i] = make_uint4(v, v, v, v);
+    }
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(v) : "r"(addr));
+    return v;
+}
+// table entry of byte k (0..3) of w for this lane (lut_lane = table address + 4 lane)
+__device__ __forceinline__ uint32_t lk(uint32_t lut_lane, uint32_t w, int k) {
+    return lds32(lut_lane + (__byte_perm(w, 0u, 0x4440u | (uint32_t)k) << 7));
+}
+__device__ __forceinline__ void bar_named(int id, int threads) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
+// warp-uniform bounded wait
+__device__ __forceinline__ bool wait_all(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+    const bool ok = as::mbar_wait(b, parity, abort_flag, err);
+    return __all_sync(FULLM, ok);
+}
+
+// ---------------------------------------------------------------------------
+template <int NHP>
+__global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant__ ScoreMaps maps, const TqAttnArgs a) {
+    extern __shared__ __align__(1024) uint8_t dsm_raw[];
+    uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
+    uint8_t *stages = dsm;
+    uint32_t *lut = reinterpret_cast<uint32_t *>(dsm + S_STG * S_STAGE);
+    float *sT = reinterpret_cast<float *>(lut + LUTW);  // [2 tiles][NHP][4 chunks][33]
+    uint64_t *full = reinterpret_cast<uint64_t *>(sT + 2 * NHP * 4 * S_CH);
+    uint64_t *afull = full + S_STG, *empty = afull + S_STG, *accfull = empty + S_STG;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    lut_build(lut, a.kcent);  // a constant input: overlaps the previous kernel
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_STG; ++s) {
+            as::mbar_init(&full[s], 1);
+            as::mbar_init(&afull[s], 8);
+            as::mbar_init(&empty[s], 1);
+        }
+        as::mbar_init(accfull, 1);
+        *abort_flag = 0;
+        as::mbar_fence_init();
+    }
+    if (warp == 0) tc::alloc(tslot, S_TCOLS);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = *tslot;
+    pdl_wait();
+
+    const int m = blockIdx.y;
+    const int tn = a.pos[m] + 1;
+    const int p0 = blockIdx.x * 2 * S_TILE;
+    const int ntile = p0 >= tn ? 0 : min(2, (tn - p0 + S_TILE - 1) / S_TILE);  // CTA-uniform
+    const int nkb = a.kvd / S_KB;
+    const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+    const uint32_t acc_col = 0, a_col = 64;  // acc of tile p at p * 32; A of (stage s, tile p) at 64 + (2s + p) * 32
+
+    if (ntile > 0) {
+        if (warp == 0) {
+            if (lane == 0) {  // TMA producer
+                for (int kb = 0; kb < nkb; ++kb) {
+                    const int s = kb % S_STG;
+                    if (!as::mbar_wait(&empty[s], ((kb / S_STG) & 1) ^ 1, abort_flag, a.err)) break;
+                    uint8_t *st = stages + s * S_STAGE;
+                    as::mbar_expect_tx(&full[s], (uint32_t)(ntile * S_TILE * 32 + NHP * 128));
+                    for (int p = 0; p < ntile; ++p)
+                        as::tma_load_2d(st + p * S_TILE * 32, &maps.codes, 32 * kb, (int)(rbase + p0 + p * S_TILE),
+                                        &full[s]);
+                    as::tma_load_2d(st + S_CODE, &maps.q, S_KB * kb, m * a.nh, &full[s]);
+                }
+            }
+        } else if (warp == 1) {
+            if (lane == 0) {  // MMA issuer
+                constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP);
+                for (int kb = 0; kb < nkb; ++kb) {
+                    const int s = kb % S_STG;
+                    const uint32_t ph = (kb / S_STG) & 1;
+                    if (!as::mbar_wait(&full[s], ph, abort_flag, a.err)) break;
+                    if (!as::mbar_wait(&afull[s], ph, abort_flag, a.err)) break;
+                    tc::fence_after();
+                    const uint64_t qd = tc::sdesc_k(stages + s * S_STAGE + S_CODE);
+                    for (int p = 0; p < ntile; ++p)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            tc::mma_ts(tbase + acc_col + p * 32, tbase + a_col + (2 * s + p) * 32 + 8 * k,
+                                       qd + (uint64_t)(2 * k), ID, (kb | k) != 0);
+                    tc::commit(&empty[s]);  // stage s (codes, q~, A) is free once these MMAs are done
+                }
+                tc::commit(accfull);
+            }
+        } else {
+            // decoders: warp w handles tile (w - 2) / 4, TMEM lanes 32 (w % 4) .. +31
+            const int p = (warp - 2) >> 2, quad = warp & 3, r = quad * 32 + lane;
+            const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+            const uint32_t lutl = as::sa(lut) + 4 * lane;
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S_STG;
+                const uint32_t ph = (kb / S_STG) & 1;
+                ok = wait_all(&full[s], ph, abort_flag, a.err) && wait_all(&empty[s], ph ^ 1, abort_flag, a.err);
+                if (!ok) break;
+                tc::fence_after();
+                if (p < ntile) {
+                    const uint8_t *row = stages + s * S_STAGE + p * S_TILE * 32 + r * 32;
+                    const uint4 c0 = *reinterpret_cast<const uint4 *>(row);
+                    const uint4 c1 = *reinterpret_cast<const uint4 *>(row + 16);
+                    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    uint32_t v[32];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) v[4 * i + k] = lk(lutl, w[i], k);
+                    tc::st32(tbase + lane_off + a_col + (2 * s + p) * 32, v);
+                    tc::st_wait();
+                }
+                tc::fence_before();
+                __syncwarp();
+                if (lane == 0) as::mbar_arrive(&afull[s]);
+            }
+            // epilogue: scaled scores of this lane's position into the transpose buffer
+            if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
+            tc::fence_after();
+            if (ok && p < ntile) {
+                float v[NHP];
+                if constexpr (NHP == 32) {
+                    tc::ld32f(tbase + lane_off + acc_col + p * 32, v);
+                } else {
+                    tc::ld16f(tbase + lane_off + acc_col + p * 32, v);
+                }
+                const int pos = p0 + p * S_TILE + r;
+                const bool valid = pos < tn;
+                const float kn = valid ? __ldg(a.knorm + rbase + pos) * a.scale : 0.0f;
+                float *col = sT + (p * NHP) * 4 * S_CH + (r >> 5) * S_CH + (r & 31);
+#pragma unroll
+                for (int h = 0; h < NHP; ++h) col[h * 4 * S_CH] = valid ? v[h] * kn : -INFINITY;
+            }
+            bar_named(1, 256);
+            // per (tile, head, 32-position chunk): max, sum of exp, e = exp(s - max) * norm_v (f16)
+            const int t = threadIdx.x - 64;
+            const int pt = t / (NHP * 4), h = (t / 4) % NHP, c = t & 3;
+            if (ok && pt < ntile && h < a.nh) {
+                const int q0 = p0 + pt * S_TILE + c * 32;
+                const float *row = sT + (pt * NHP + h) * 4 * S_CH + c * S_CH;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, row[i]);
+                float sum = 0.0f;
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float s0 = row[i], s1 = row[i + 1];
+                    const float e0 = s0 == -INFINITY ? 0.0f : __expf(s0 - mx);
+                    const float e1 = s1 == -INFINITY ? 0.0f : __expf(s1 - mx);
+                    sum += e0;
+                    sum += e1;
+                    const float vn0 = e0 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i) : 0.0f;
+                    const float vn1 = e1 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i + 1) : 0.0f;
+                    pk[i >> 1] = h2u(e0 * vn0, e1 * vn1);
+                }
+                uint4 *dst = reinterpret_cast<uint4 *>(a.E + ((int64_t)m * a.nh + h) * a.Sp + q0);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                const int64_t ci = ((int64_t)m * a.nc32 + (q0 >> 5)) * a.nh + h;
+                a.cmax[ci] = mx;
+                a.csum[ci] = sum;
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::dealloc(tbase, S_TCOLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// per (head, token): global max, denominator, e rescaled in place
+__global__ void __launch_bounds__(128) tc_softmax_kernel(const TqAttnArgs a) {
+    pdl_wait();
+    __shared__ float red[128];
+    __shared__ float fac[6144 / 32];
+    const int h = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+    const int tn = a.pos[m] + 1, nc = (tn + 31) >> 5;
+    const float *cm = a.cmax + (int64_t)m * a.nc32 * a.nh + h;
+    const float *cs = a.csum + (int64_t)m * a.nc32 * a.nh + h;
+    float mx = -INFINITY;
+    for (int c = tid; c < nc; c += 128) mx = fmaxf(mx, cm[(int64_t)c * a.nh]);
+    red[tid] = mx;
+    __syncthreads();
+    for (int w = 64; w > 0; w >>= 1) {
+        if (tid < w) red[tid] = fmaxf(red[tid], red[tid + w]);
+        __syncthreads();
+    }
+    const float M = red[0];
+    __syncthreads();
+    float l = 0.0f;
+    for (int c = tid; c < nc; c += 128) {
+        const float cmv = cm[(int64_t)c * a.nh];
+        const float f = cmv == -INFINITY ? 0.0f : __expf(cmv - M);
+        fac[c] = f;
+        l += cs[(int64_t)c * a.nh] * f;
+    }
+    red[tid] = l;
+    __syncthreads();
+    for (int w = 64; w > 0; w >>= 1) {
+        if (tid < w) red[tid] += red[tid + w];
+        __syncthreads();
+    }
+    if (tid == 0) a.linv[(int64_t)m * a.nh + h] = 1.0f / red[0];
+    __half2 *e = reinterpret_cast<__half2 *>(a.E + ((int64_t)m * a.nh + h) * a.Sp);
+    for (int i = tid; i < nc * 16; i += 128) {
+        const float f = fac[i >> 4];
+        const float2 x = __half22float2(e[i]);
+        e[i] = __floats2half2_rn(x.x * f, x.y * f);
+    }
+}
+
+// ---------------------------------------------------------------------------
+template <int NHP>
+__global__ void __launch_bounds__(TCW, 1) tc_values_kernel(const __grid_constant__ ValueMaps maps, const TqAttnArgs a) {
+    extern __shared__ __align__(1024) uint8_t dsm_raw[];
+    uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
+    uint8_t *stages = dsm;
+    uint8_t *abuf = dsm + V_STG * V_STAGE;  // [2][4 atoms][64 rows][128 B]
+    uint32_t *lut = reinterpret_cast<uint32_t *>(abuf + 2 * V_A);
+    uint64_t *full = reinterpret_cast<uint64_t *>(lut + LUTW);
+    uint64_t *empty = full + V_STG, *afull = empty + V_STG, *aempty = afull + 2, *accfull = aempty + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
+    constexpr uint32_t TCOLS = 2 * NHP < 32 ? 32 : 2 * NHP;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    lut_build(lut, a.vcent);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < V_STG; ++s) {
+            as::mbar_init(&full[s], 1);
+            as::mbar_init(&empty[s], 9);  // 8 decoder warps (codes read) + the MMA commit (e read)
+        }
+        for (int b = 0; b < 2; ++b) {
+            as::mbar_init(&afull[b], 8);
+            as::mbar_init(&aempty[b], 1);
+        }
+        as::mbar_init(accfull, 1);
+        *abort_flag = 0;
+        as::mbar_fence_init();
+    }
+    if (warp == 0) tc::alloc(tslot, TCOLS);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = *tslot;
+    pdl_wait();
+
+    const int g = blockIdx.x, m = blockIdx.y;
+    const int tn = a.pos[m] + 1;
+    const int nkb = (tn + V_KB - 1) / V_KB;
+    const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % V_STG;
+                if (!as::mbar_wait(&empty[s], ((kb / V_STG) & 1) ^ 1, abort_flag, a.err)) break;
+                uint8_t *st = stages + s * V_STAGE;
+                as::mbar_expect_tx(&full[s], (uint32_t)(V_CODE + NHP * 128));
+                as::tma_load_2d(st, &maps.codes, g * (V_DG / 2), (int)(rbase + kb * V_KB), &full[s]);
+                as::tma_load_2d(st + V_CODE, &maps.e, kb * V_KB, m * a.nh, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP, /*a_mn=*/1, /*b_mn=*/0);
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % V_STG, ab = kb & 1;
+                if (!as::mbar_wait(&full[s], (kb / V_STG) & 1, abort_flag, a.err)) break;
+                if (!as::mbar_wait(&afull[ab], (kb >> 1) & 1, abort_flag, a.err)) break;
+                tc::fence_after();
+                const uint64_t ed = tc::sdesc_k(stages + s * V_STAGE + V_CODE);
+                const uint32_t a0 = as::sa(abuf + ab * V_A);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        tc::mma_ss(tbase + hh * NHP, tc::sdesc_sw128(a0 + hh * 2 * V_ATOM + k * 2048, V_ATOM, 1024),
+                                   ed + (uint64_t)(2 * k), ID, (kb | k) != 0);
+                tc::commit(&empty[s]);
+                tc::commit(&aempty[ab]);
+            }
+            tc::commit(accfull);
+        }
+    } else {
+        // decoders: value rows of the K block into the MN-major A buffer
+        const int t = threadIdx.x - 64;
+        const uint32_t lutl = as::sa(lut) + 4 * lane;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int s = kb % V_STG, ab = kb & 1;
+            ok = wait_all(&full[s], (kb / V_STG) & 1, abort_flag, a.err) &&
+                 wait_all(&aempty[ab], ((kb >> 1) & 1) ^ 1, abort_flag, a.err);
+            if (!ok) break;
+            const uint8_t *codes = stages + s * V_STAGE;
+            uint8_t *A = abuf + ab * V_A;
+#pragma unroll 2
+            for (int c = t; c < V_KB * 32; c += 256) {
+                const int r = c >> 5, w = c & 31, da = w >> 3, j = w & 7;
+                const uint32_t cw = *reinterpret_cast<const uint32_t *>(codes + r * 128 + 4 * w);
+                const uint4 o = make_uint4(lk(lutl, cw, 0), lk(lutl, cw, 1), lk(lutl, cw, 2), lk(lutl, cw, 3));
+                *reinterpret_cast<uint4 *>(A + da * V_ATOM + r * 128 + ((j ^ (r & 7)) << 4)) = o;
+            }
+            tc::fence_proxy_async();  // the MMA reads A through the async proxy
+            __syncwarp();
+            if (lane == 0) {
+                as::mbar_arrive(&afull[ab]);
+                as::mbar_arrive(&empty[s]);
+            }
+        }
+        // epilogue: warp w reads accumulator (w - 2) / 4 (dims 128 of them), TMEM lanes 32 (w % 4) ..
+        if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
+        tc::fence_after();
+        if (ok) {
+            const int hh = (warp - 2) >> 2, quad = warp & 3;
+            float v[NHP];
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + hh * NHP;
+            if constexpr (NHP == 32) {
+                tc::ld32f(taddr, v);
+            } else {
+                tc::ld16f(taddr, v);
+            }
+            const int d = g * V_DG + hh * 128 + quad * 32 + lane;
+#pragma unroll
+            for (int h = 0; h < NHP; ++h) {
+                if (h < a.nh) {
+                    const float u = v[h] * a.linv[(int64_t)m * a.nh + h];
+                    const __half hi = __float2half_rn(u);
+                    const int64_t o = ((int64_t)m * a.nh + h) * a.kvd + d;
+                    a.U[o] = hi;
+                    a.U_lo[o] = __float2half_rn(u - __half2float(hi));
+                }
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::dealloc(tbase, TCOLS);
+    }
+}
+
+template <int NHP>
+cudaError_t launch_tc(const TqAttnArgs &a, cudaStream_t s) {
+    ScoreMaps sm;
+    ValueMaps vm;
+    std::memset(&sm, 0, sizeof(sm));
+    std::memset(&vm, 0, sizeof(vm));
+    const int64_t rows = (int64_t)a.n_slots * a.L * a.B;
+    if (!make_tensor_map(&sm.codes, a.kcodes, rows, a.kpl, a.kpl, 1, 32, S_TILE, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_tensor_map(&sm.q, a.qrot, (int64_t)a.M * a.nh, a.kvd, a.kvd, 2, S_KB, NHP, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tensor_map(&vm.codes, a.vcodes, rows, a.vpl, a.vpl, 1, V_DG / 2, V_KB, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_tensor_map(&vm.e, a.E, (int64_t)a.M * a.nh, a.Sp, a.Sp, 2, V_KB, NHP, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    const size_t ssm = 1024 + (size_t)S_STG * S_STAGE + LUTW * 4 + (size_t)2 * NHP * 4 * S_CH * 4 + 256;
+    const size_t vsm = 1024 + (size_t)V_STG * V_STAGE + 2 * V_A + LUTW * 4 + 256;
+    cudaError_t e = dev::smem(tc_scores_kernel<NHP>, ssm);
+    if (e == cudaSuccess) e = dev::smem(tc_values_kernel<NHP>, vsm);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(tc_scores_kernel<NHP>, dim3((a.Sp + 2 * S_TILE - 1) / (2 * S_TILE), a.M), dim3(TCW), ssm, s, sm, a);
+    if (e == cudaSuccess) e = launch_pdl(tc_softmax_kernel, dim3(a.nh, a.M), dim3(128), 0, s, a);
+    if (e == cudaSuccess)
+        e = launch_pdl(tc_values_kernel<NHP>, dim3(a.kvd / V_DG, a.M), dim3(TCW), vsm, s, vm, a);
+    return e;
+}
+
+}  // namespace
+
+bool tc_attn_supported(const TqAttnArgs &a) {
+    return a.kvd % V_DG == 0 && a.nh >= 1 && a.nh <= 32 && 2 * a.kpl == a.kvd && 2 * a.vpl == a.kvd &&
+           a.Sp % S_TILE == 0 && a.Sp <= 6144 && a.nc32 == a.Sp / 32 && a.linv && a.n_slots > 0 &&
+           tensor_map_encoder() != nullptr;
+}
+
+cudaError_t tc_decode_attn(const TqAttnArgs &a, cudaStream_t s) {
+    if (a.M <= 0) return cudaSuccess;
+    return a.nh <= 16 ? launch_tc<16>(a, s) : launch_tc<32>(a, s);
+}
+
+}  // namespace attn
+}  // namespace kg

@@ -400,15 +400,17 @@ __global__ void norm_split_kernel(int dim, int Mk, int Mv, const float *qkv, int
     }
 }
 
-// One warp per vector: codes from y' where no boundary is within eps, exact
-// recomputation elsewhere, then 4-bit packing (two codes per byte, low first).
+// One warp per (vector, 32-coordinate segment): codes from y' where no
+// boundary is within eps, exact recomputation of the others (the whole warp
+// computes each such dot in the reference order), then 4-bit packing (two
+// codes per byte, low first). Spreading a vector's segments over warps keeps
+// the recomputations (about 4% of the coordinates at kv_dim 4096) parallel.
 __global__ void quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
                                       const float *rot, const float *kb, const float *vb, int kbits, int vbits,
                                       uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl,
                                       const int32_t *slot, const int32_t *pos, int L, int B, int layer, float eps,
                                       int *nfix) {
     pdl_wait();
-    extern __shared__ uint8_t qsm[];
     __shared__ float bnd[2][15];
     const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x & 31;
     if (threadIdx.x < 15) {
@@ -416,44 +418,37 @@ __global__ void quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, c
         bnd[1][threadIdx.x] = threadIdx.x < (1 << vbits) - 1 ? vb[threadIdx.x] : INFINITY;
     }
     __syncthreads();
-    const int v = blockIdx.x * warps + w;
-    if (v >= Mk + Mv || skip[v]) return;  // skipped vectors keep their codes (reference quirk)
-    uint8_t *cd = qsm + (size_t)w * dim;
-    const int which = v < Mk ? 0 : 1, t = which ? v - Mk : v;
+    const int nseg = dim / 32;
+    const int64_t gw = (int64_t)blockIdx.x * warps + w;
+    const int64_t v = gw / nseg;
+    const int j0 = (int)(gw - v * nseg) * 32;
+    if (v >= Mk + Mv || skip[v]) return;  // skipped vectors keep their codes (reference quirk); warp-uniform
+    const int which = v < Mk ? 0 : 1;
+    const int64_t t = which ? v - Mk : v;
     const int nb = (1 << (which ? vbits : kbits)) - 1;
     const float *b = bnd[which];
-    const float *yv = Y + (int64_t)v * dim;
-    int fixes = 0;
-    for (int j0 = 0; j0 < dim; j0 += 32) {
-        const int j = j0 + lane;
-        bool near = false;
-        if (j < dim) {
-            const float y = yv[j];
-            int c = 0;
-            for (int k = 0; k < nb; ++k) {
-                c += y >= b[k] ? 1 : 0;
-                near |= fabsf(y - b[k]) <= eps;
-            }
-            cd[j] = (uint8_t)c;
-        }
-        unsigned m = __ballot_sync(0xffffffffu, near);
-        while (m) {  // exact recomputation, one coordinate at a time by the whole warp
-            const int l = __ffs(m) - 1;
-            m &= m - 1;
-            const int jj = j0 + l;
-            const float r = warp_dot(rot + (int64_t)jj * dim, xn + (int64_t)v * dim, dim);
-            if (lane == 0) {
-                int c = 0;
-                for (int k = 0; k < nb; ++k) c += r >= b[k] ? 1 : 0;
-                cd[jj] = (uint8_t)c;
-            }
-            ++fixes;
+    const float y = Y[v * dim + j0 + lane];
+    int c = 0;
+    bool near = false;
+    for (int k = 0; k < nb; ++k) {
+        c += y >= b[k] ? 1 : 0;
+        near |= fabsf(y - b[k]) <= eps;
+    }
+    unsigned m = __ballot_sync(0xffffffffu, near);
+    const int fixes = __popc(m);
+    while (m) {  // exact recomputation, one coordinate at a time by the whole warp
+        const int l = __ffs(m) - 1;
+        m &= m - 1;
+        const float r = warp_dot(rot + (int64_t)(j0 + l) * dim, xn + v * dim, dim);  // all lanes get r
+        if (lane == l) {
+            c = 0;
+            for (int k = 0; k < nb; ++k) c += r >= b[k] ? 1 : 0;
         }
     }
-    __syncwarp();
+    const int c_hi = __shfl_down_sync(0xffffffffu, c, 1);
     const int64_t drow = slot ? ((int64_t)slot[t] * L + layer) * B + pos[t] : t;
-    uint8_t *out = (which ? vcodes : kcodes) + drow * (which ? vpl : kpl);
-    for (int k = lane; k < dim / 2; k += 32) out[k] = (uint8_t)((cd[2 * k] & 15) | ((cd[2 * k + 1] & 15) << 4));
+    uint8_t *out = (which ? vcodes : kcodes) + drow * (which ? vpl : kpl) + j0 / 2;
+    if ((lane & 1) == 0) out[lane >> 1] = (uint8_t)((c & 15) | ((c_hi & 15) << 4));
     if (nfix && lane == 0 && fixes) atomicAdd(nfix, fixes);
 }
 
@@ -477,11 +472,12 @@ cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const flo
                               uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl, const int32_t *slot,
                               const int32_t *pos, int L, int B, int layer, int *nfix, cudaStream_t s) {
     if (Mk + Mv <= 0) return cudaSuccess;
-    if (dim % 2 || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
+    if (dim % 32 || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
     const int warps = 8;
-    return launch_pdl(quantize_fixup_kernel, dim3((Mk + Mv + warps - 1) / warps), dim3(warps * 32),
-                      (size_t)warps * dim, s, dim, Mk, Mv, Y, xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl,
-                      vpl, slot, pos, L, B, layer, tq_fixup_eps(dim), nfix);
+    const int64_t nwarps = (int64_t)(Mk + Mv) * (dim / 32);
+    return launch_pdl(quantize_fixup_kernel, dim3((unsigned)((nwarps + warps - 1) / warps)), dim3(warps * 32), 0, s,
+                      dim, Mk, Mv, Y, xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl, vpl, slot, pos, L, B,
+                      layer, tq_fixup_eps(dim), nfix);
 }
 
 namespace {

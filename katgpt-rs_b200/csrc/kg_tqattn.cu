@@ -681,6 +681,7 @@ int tq_padded_len(int block_size) { return (block_size + TQ_CH - 1) / TQ_CH * TQ
 
 cudaError_t tq_decode_attn(const TqAttnArgs &a0, cudaStream_t s) {
     if (a0.M <= 0) return cudaSuccess;
+    if (tc_attn_supported(a0)) return tc_decode_attn(a0, s);  // tcgen05 scores and values
     TqAttnArgs a = a0;
     if (a.kvd % 64 || a.nh < 1 || a.nh > 32 || a.Sp != tq_padded_len(a.B) || a.nc16 != a.Sp / 16 ||
         2 * a.kpl != a.kvd || 2 * a.vpl != a.kvd)

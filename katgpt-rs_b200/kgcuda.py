@@ -93,6 +93,10 @@ def lib():
             "kg_kv_snapshot": (ctypes.c_int, [P, I32, I32, P, P]),
             "kg_kv_restore": (ctypes.c_int, [P, I32, I32, P, P]),
             "kg_set_mlp_hook": (ctypes.c_int, [P, F32, ctypes.c_uint64]),
+            "kg_rng_seed": (ctypes.c_int, [P, I32, ctypes.c_uint64]),
+            "kg_rng_state": (ctypes.c_int, [P, I32, P]),
+            "kg_sample_dev": (ctypes.c_int, [P, I32, P, P, I64, P, P]),
+            "kg_sample": (ctypes.c_int, [P, I32, P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -286,6 +290,24 @@ class CudaBackend:
     def graph_kernels(self):
         """Kernel launches replayed by the last forward call's CUDA graph (0: eager)."""
         return int(lib().kg_graph_kernels(self._h))
+
+    # ---- sampling (sample_token_into on the device)
+    def rng_seed(self, seq, seed):
+        self._check(lib().kg_rng_seed(self._h, seq, seed))
+
+    def rng_state(self, seq):
+        out = ctypes.c_uint64(0)
+        self._check(lib().kg_rng_state(self._h, seq, ctypes.byref(out)))
+        return out.value
+
+    def sample(self, probs, seq_ids=None):
+        """Token ids drawn from probs [n_rows][vocab] with each row's slot generator."""
+        probs = np.ascontiguousarray(probs, dtype=np.float32)
+        n = probs.shape[0]
+        ids = np.arange(n, dtype=np.int32) if seq_ids is None else np.ascontiguousarray(seq_ids, np.int32)
+        out = np.empty(n, np.int32)
+        self._check(lib().kg_sample(self._h, n, _ptr(ids), _ptr(probs), _ptr(out)))
+        return out
 
     def spkv_utility(self, seq, layer, pos):
         u = np.empty(1, np.float32)

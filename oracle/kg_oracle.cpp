@@ -1126,6 +1126,25 @@ int64_t or_sample_token(const float *probs, int64_t n, uint64_t seed) {
     return std::min(idx, n - 1);
 }
 
+// sample_token_into called k times with one generator (math.rs:398-422):
+// row j of probs [k][n] gets the j-th draw of Rng::new(seed)
+void or_sample_tokens(const float *probs, int64_t n, int64_t k, uint64_t seed, int64_t *out) {
+    Rng rng(seed);
+    std::vector<float> cdf(n);
+    for (int64_t j = 0; j < k; ++j) {
+        float r = rng.uniform();
+        while (r == 0.0f) r = rng.uniform();
+        const float *p = probs + j * n;
+        float s = 0.0f;
+        for (int64_t i = 0; i < n; ++i) {
+            s += p[i];
+            cdf[i] = s;
+        }
+        int64_t idx = std::partition_point(cdf.begin(), cdf.end(), [&](float c) { return c <= r; }) - cdf.begin();
+        out[j] = n == 0 ? 0 : std::min(idx, n - 1);
+    }
+}
+
 int64_t or_tq_packed_len(int64_t dim, int bits) { return packed_len(dim, bits); }
 
 void or_tq_codebook(int64_t dim, int bits, float *centroids, float *boundaries, float *mse) {

@@ -69,6 +69,9 @@ float or_exp_sum_inplace(float *x, int64_t len);
 float or_sparse_dot(const float *w_row, const int64_t *idx, const float *val, int64_t alive);
 void or_softmax_scaled(float *x, int64_t len, float inv_temp);
 int64_t or_sample_token(const float *probs, int64_t n, uint64_t seed);
+/* k successive sample_token_into draws from one Rng::new(seed): row j of
+ * probs[k][n] -> out[j] */
+void or_sample_tokens(const float *probs, int64_t n, int64_t k, uint64_t seed, int64_t *out);
 /* scalar (non-SIMD) restatements used to cross-check the AVX2 ones */
 float or_scalar_exp(float x);
 

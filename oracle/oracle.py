@@ -60,6 +60,7 @@ def lib():
             "or_sparse_dot": (F32, [P, P, P, I64]),
             "or_softmax_scaled": (None, [P, I64, F32]),
             "or_sample_token": (I64, [P, I64, U64]),
+            "or_sample_tokens": (None, [P, I64, I64, U64, P]),
             "or_scalar_exp": (F32, [F32]),
             "or_tq_packed_len": (I64, [I64, ctypes.c_int]),
             "or_tq_codebook": (None, [I64, ctypes.c_int, P, P, P]),
@@ -175,6 +176,14 @@ def softmax_scaled(x, inv_temp):
 def sample_token(probs, seed):
     p = f32(probs)
     return lib().or_sample_token(_p(p), p.size, seed)
+
+
+def sample_tokens(probs, seed):
+    """Successive draws of one Rng::new(seed): one token per row of probs [k][n]."""
+    p = f32(probs)
+    out = np.empty(p.shape[0], np.int64)
+    lib().or_sample_tokens(_p(p), p.shape[1], p.shape[0], seed, _p(out))
+    return out
 
 
 def packed_len(dim, bits):
