@@ -194,6 +194,30 @@ int kg_sample_dev(kg_ctx *ctx, int32_t n_rows, const int32_t *seq_ids, const flo
 /* Host-pointer form (probs [n_rows][vocab]); synchronises. */
 int kg_sample(kg_ctx *ctx, int32_t n_rows, const int32_t *seq_ids, const float *probs, int32_t *tokens_out);
 
+/* ---- multi-GPU sequence shards (one context per GPU) ----
+ * Sequences shard across GPUs with replicated weights; the one exchange is an
+ * all-gather of every shard's decode outputs, done here over NCCL on the
+ * caller's stream (the reference has no multi-device path: its batch path is a
+ * per-sequence par_iter on one host, src/transformer.rs:3588-3606). NCCL is
+ * loaded at run time; without it these return KG_ERR_UNSUPPORTED. */
+
+/* A 128-byte NCCL unique id, made on one rank and handed to every rank by the
+ * caller's own channel (a store, a broadcast, a file). */
+int kg_comm_unique_id(uint8_t *id_out);
+/* Join the `world`-rank communicator as `rank` (collective over all ranks). */
+int kg_comm_init(kg_ctx *ctx, const uint8_t *id, int32_t world, int32_t rank);
+/* Leave it (also done by kg_ctx_destroy). */
+int kg_comm_destroy(kg_ctx *ctx);
+/* One decode step of this rank's n_seq sequences (seq_ids, tokens, positions
+ * as in kg_forward_batch_dev with T = 1), then the all-gather: logits_all
+ * [world][n_seq][vocab] f32 and/or tokens_all [world][n_seq] int32 (tokens
+ * sampled on the device from softmax_scaled probabilities, as kg_sample_dev)
+ * receive every rank's rows, this rank's at offset rank. Every rank passes the
+ * same n_seq and the same choice of outputs. Device pointers, enqueued on
+ * `stream`; without a communicator it is the local step only. */
+int kg_decode_gather_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
+                         const int32_t *positions, float *logits_all, int32_t *tokens_all, void *stream);
+
 /* ---- TurboQuant codec access (parity / inspection) ---- */
 
 /* Packed bytes per vector for `bits` at dimension `dim` (kv_cache.rs:499-509). */

@@ -150,6 +150,7 @@ void kg_ctx_destroy(kg_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    kg_comm_destroy(ctx);
     for (auto &gr : ctx->graphs) {
         if (gr.stream) cudaStreamSynchronize(gr.stream);
         if (gr.exec) cudaGraphExecDestroy(gr.exec);

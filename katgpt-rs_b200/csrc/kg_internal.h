@@ -184,6 +184,11 @@ struct kg_ctx {
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     // per-slot Rng state of sample_token_into on the device (kg_sample.cu)
     uint64_t *rng = nullptr;
+    // multi-GPU sequence shards (kg_comm.cu): NCCL communicator, this rank,
+    // and the probabilities buffer of the sampled-token gather
+    void *comm = nullptr;
+    int world = 1, rank = 0;
+    float *probs_buf = nullptr;
 };
 
 namespace kg {

@@ -97,6 +97,10 @@ def lib():
             "kg_rng_state": (ctypes.c_int, [P, I32, P]),
             "kg_sample_dev": (ctypes.c_int, [P, I32, P, P, I64, P, P]),
             "kg_sample": (ctypes.c_int, [P, I32, P, P, P]),
+            "kg_comm_unique_id": (ctypes.c_int, [P]),
+            "kg_comm_init": (ctypes.c_int, [P, P, I32, I32]),
+            "kg_comm_destroy": (ctypes.c_int, [P]),
+            "kg_decode_gather_dev": (ctypes.c_int, [P, I32, P, P, P, P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -110,6 +114,15 @@ def exported_symbols():
     """Names of every kg_* function the header declares (for ABI checks)."""
     lib()
     return sorted(n for n in dir(_lib) if n.startswith("kg_"))
+
+
+def comm_unique_id():
+    """A 128-byte NCCL unique id (bytes) for kg_comm_init."""
+    buf = (ctypes.c_uint8 * 128)()
+    rc = lib().kg_comm_unique_id(buf)
+    if rc:
+        raise KgError(rc, "kg_comm_unique_id")
+    return bytes(buf)
 
 
 def bf16_round(a):
@@ -308,6 +321,20 @@ class CudaBackend:
         out = np.empty(n, np.int32)
         self._check(lib().kg_sample(self._h, n, _ptr(ids), _ptr(probs), _ptr(out)))
         return out
+
+    # ---- multi-GPU sequence shards
+    def comm_init(self, uid, world, rank):
+        """Join the NCCL communicator `uid` (bytes from comm_unique_id()) as `rank`."""
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(bytes(uid))
+        self._check(lib().kg_comm_init(self._h, buf, world, rank))
+
+    def comm_destroy(self):
+        self._check(lib().kg_comm_destroy(self._h))
+
+    def decode_gather_dev(self, n_seq, ids_ptr, tok_ptr, pos_ptr, logits_all_ptr, tokens_all_ptr, stream_ptr):
+        """One decode step of this rank's sequences, then the all-gather (device pointers)."""
+        self._check(lib().kg_decode_gather_dev(self._h, n_seq, ids_ptr, tok_ptr, pos_ptr, logits_all_ptr,
+                                               tokens_all_ptr, stream_ptr))
 
     def spkv_utility(self, seq, layer, pos):
         u = np.empty(1, np.float32)
