@@ -194,6 +194,29 @@ int kg_sample_dev(kg_ctx *ctx, int32_t n_rows, const int32_t *seq_ids, const flo
 /* Host-pointer form (probs [n_rows][vocab]); synchronises. */
 int kg_sample(kg_ctx *ctx, int32_t n_rows, const int32_t *seq_ids, const float *probs, int32_t *tokens_out);
 
+/* Speculative verification of one draft path per sequence on the device —
+ * speculative_step_rollback's loop (src/speculative/step.rs:150-222) with
+ * Leviathan acceptance and residual resampling
+ * (crates/katgpt-core/src/speculative/sampling.rs:26-116). Sequence i stands at
+ * start_pos[i] with its current token tokens[i] and k draft tokens
+ * drafts[i][0..k) whose draft-model probabilities are draft_probs[i][k][vocab].
+ * One multi-position forward scores the path (tokens[i], d_0 .. d_{k-2} at
+ * positions start_pos[i] ..); then for j < k, with u = Rng::uniform() of the
+ * slot's generator, d_j is accepted while u <= min(p(d_j) / q(d_j), 1) (1 when
+ * q(d_j) = 0), p being the target's softmax_scaled distribution at the path's
+ * current position; the first rejection draws from normalize(max(0, p - q))
+ * (p itself when that is all zero) and ends the path; a fully accepted path
+ * adds a bonus draw from the last distribution used. accepted[i][0..k] receives
+ * the emitted tokens, n_accepted[i] their count (1..k+1). The KV cache then
+ * holds the path's forwarded positions; positions past the accepted ones are
+ * rewritten by the next call before any read. Device pointers on `stream`. */
+int kg_verify_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *start_pos,
+                  const int32_t *tokens, const int32_t *drafts, int32_t k, const float *draft_probs, int32_t *accepted,
+                  int32_t *n_accepted, void *stream);
+/* Host-pointer form; synchronises. */
+int kg_verify(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *start_pos, const int32_t *tokens,
+              const int32_t *drafts, int32_t k, const float *draft_probs, int32_t *accepted, int32_t *n_accepted);
+
 /* ---- multi-GPU sequence shards (one context per GPU) ----
  * Sequences shard across GPUs with replicated weights; the one exchange is an
  * all-gather of every shard's decode outputs, done here over NCCL on the

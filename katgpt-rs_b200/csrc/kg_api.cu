@@ -157,6 +157,8 @@ void kg_ctx_destroy(kg_ctx *ctx) {
     }
     for (void *p : ctx->allocs) cudaFree(p);
     if (ctx->stage) cudaFree(ctx->stage);
+    if (ctx->verify_probs) cudaFree(ctx->verify_probs);
+    if (ctx->verify_tok) cudaFree(ctx->verify_tok);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     if (ctx->aux) cudaStreamSynchronize(ctx->aux), cudaStreamDestroy(ctx->aux);
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
@@ -540,8 +542,8 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
         if (T == 1 && s != nullptr && !ctx->prof && n_seq <= std::min<int64_t>(ctx->big.ws_tokens, ctx->cfg.max_seqs))
             return forward_graph(ctx, n_seq, seq_ids, tokens, start_pos, logits, probs, s);
         cudaError_t e = kg::big_forward(ctx, n_seq, seq_ids, tokens, start_pos, T, logits, probs, s);
-        if (e == cudaErrorNotSupported)
-            return fail(ctx, KG_ERR_UNSUPPORTED, "bf16 path: a multi-position call must start at position 0");
+        if (e == cudaErrorInvalidValue && T > 1 && start_pos)
+            return fail(ctx, KG_ERR_INVALID_ARG, "multi-position call from arbitrary positions: n_seq > max_seqs");
         KG_CUDA(ctx, e);
         return KG_OK;
     }
@@ -575,10 +577,10 @@ int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const i
     for (int64_t i = 0; i < (int64_t)n_seq * T; ++i)
         if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, KG_ERR_INVALID_ARG, "token out of range");
     if (ctx->big_path && T > 1 && start_pos) {
-        for (int32_t i = 0; i < n_seq; ++i)
-            if (start_pos[i] != 0)
-                return fail(ctx, KG_ERR_UNSUPPORTED, "bf16 path: a multi-position call must start at position 0");
-        start_pos = nullptr;
+        // all sequences from position 0: the prefill path (flash attention over the prompt)
+        bool all0 = true;
+        for (int32_t i = 0; i < n_seq; ++i) all0 = all0 && start_pos[i] == 0;
+        if (all0) start_pos = nullptr;
     }
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t b_ids = align256(n_seq * 4), b_tok = align256((size_t)n_seq * T * 4);

@@ -560,11 +560,11 @@ __global__ void mlp_hook_kernel(bf16 *hid, bf16 *hid2, int *row_alive, const int
     if (threadIdx.x == 0) row_alive[r] = s_cnt;
 }
 
-__global__ void softmax_kernel(const float *logits, float *probs, int V, float inv_temp) {
+__global__ void softmax_kernel(const float *logits, float *probs, int V, int64_t ld, float inv_temp) {
     pdl_wait();
     __shared__ float red[32];
     const int m = blockIdx.x;
-    const float *l = logits + (int64_t)m * V;
+    const float *l = logits + (int64_t)m * ld;
     float mx = -INFINITY;
     for (int j = threadIdx.x; j < V; j += blockDim.x) mx = fmaxf(mx, l[j]);
     mx = block_max(mx, red);
@@ -572,7 +572,7 @@ __global__ void softmax_kernel(const float *logits, float *probs, int V, float i
     for (int j = threadIdx.x; j < V; j += blockDim.x) s += expf((l[j] - mx) * inv_temp);
     s = block_sum(s, red);
     const float inv = 1.0f / s;
-    for (int j = threadIdx.x; j < V; j += blockDim.x) probs[(int64_t)m * V + j] = expf((l[j] - mx) * inv_temp) * inv;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) probs[(int64_t)m * ld + j] = expf((l[j] - mx) * inv_temp) * inv;
 }
 
 }  // namespace
@@ -669,9 +669,9 @@ cudaError_t mlp_hook(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot,
     if (m % 8) return cudaErrorInvalidValue;  // 16-byte row vectors
     return launch_pdl(mlp_hook_kernel, dim3(M), dim3(256), 0, s, hid, hid2, row_alive, slot, pos, m, keep, seed, layer);
 }
-cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s) {
+cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, int64_t ld, float inv_temp, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    return launch_pdl(softmax_kernel, dim3(M), dim3(256), 0, s, logits, probs, V, inv_temp);
+    return launch_pdl(softmax_kernel, dim3(M), dim3(256), 0, s, logits, probs, V, ld, inv_temp);
 }
 
 }  // namespace bf

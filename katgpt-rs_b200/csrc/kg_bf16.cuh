@@ -94,8 +94,8 @@ cudaError_t mlp_hook(bf16 *hid, bf16 *hid2, int *row_alive, const int32_t *slot,
                      float keep, uint64_t seed, int layer, cudaStream_t s);
 cudaError_t twell_sparse_w2(const bf16 *hidden, const bf16 *hidden_lo, const int *row_alive, const bf16 *w2t, const float *resid,
                             float *out, int n, int m, int M, float threshold, cudaStream_t s);
-// softmax_scaled (math.rs:36-50) per row of logits [M x V]
-cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, float inv_temp, cudaStream_t s);
+// softmax_scaled (math.rs:36-50) per row of logits [M x V], rows `ld` floats apart
+cudaError_t softmax_rows(const float *logits, float *probs, int V, int M, int64_t ld, float inv_temp, cudaStream_t s);
 
 }  // namespace bf
 }  // namespace kg

@@ -10,7 +10,7 @@
 //   recomputed by gather) -> delta routing; then lm_head GEMM (+ softmax).
 // Decode (T = 1) attends in the rotated domain straight from the codes;
 // prefill (T > 1 from position 0) dequantizes the prompt's K/V once and runs
-// causal flash attention.
+// causal flash attention; T > 1 from other positions runs decode rows.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -62,6 +62,27 @@ __global__ void transpose_bf16_kernel(const bf16 *a, int rows, int cols, bf16 *t
         const int row = bx + r, col = by + threadIdx.x;
         if (row < cols && col < rows) t[(int64_t)row * rows + col] = tile[threadIdx.x][r];
     }
+}
+
+// One position offset t of a multi-position call from arbitrary start
+// positions: row i = (sequence i, position start_pos[i] + t, token i*T + t).
+__global__ void expand_offset_kernel(const int32_t *seq_ids, const int32_t *start_pos, int T, int t, int n_seq, int B,
+                                     int n_slots, int V, const int32_t *tokens, int32_t *slot_of, int32_t *pos_of,
+                                     int32_t *tok_of, int *err) {
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_seq) return;
+    const int s = seq_ids[i], p = start_pos[i] + t, tok = tokens[(int64_t)i * T + t];
+    if (s < 0 || s >= n_slots || p < 0 || p >= B || tok < 0 || tok >= V) {
+        atomicExch(err, 1);
+        slot_of[i] = 0;
+        pos_of[i] = 0;
+        tok_of[i] = 0;
+        return;
+    }
+    slot_of[i] = s;
+    pos_of[i] = p;
+    tok_of[i] = tok;
 }
 
 __global__ void sanitize_tokens_kernel(const int32_t *tokens, int M, int V, int32_t *out) {
@@ -525,7 +546,9 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
     return cudaSuccess;
 }
 
-cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, cudaStream_t s) {
+// lm_head + softmax_scaled; output rows are `ld` floats apart (V unless a
+// pass writes every T-th row of a [n_seq][T][V] output)
+cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, int64_t ld, cudaStream_t s) {
     BigState &g = ctx->big;
     const int n = (int)ctx->n, V = (int)ctx->V;
     if (!logits && !probs) return cudaSuccess;
@@ -533,11 +556,11 @@ cudaError_t lm_head(kg_ctx *ctx, int M, float *logits, float *probs, cudaStream_
     float *lo = logits ? logits : probs;  // logits land in the probs buffer when only probs are wanted
     bf::Gemm q = gemm0();
     q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = g.lm; q.ldb = n; q.M = M; q.N = V; q.K = n;
-    q.epi = bf::EPI_F32; q.C = lo; q.ldc = V;
+    q.epi = bf::EPI_F32; q.C = lo; q.ldc = ld;
     prof_mark(ctx, KG_PROF_GEMM, 0, s);
     BIG_TRY(gemm_split(ctx, q, s));
     prof_mark(ctx, KG_PROF_GEMM, 1, s);
-    if (probs) BIG_TRY(bf::softmax_rows(lo, probs, V, M, 1.0f / ctx->cfg.temperature, s));
+    if (probs) BIG_TRY(bf::softmax_rows(lo, probs, V, M, ld, 1.0f / ctx->cfg.temperature, s));
     return cudaSuccess;
 }
 
@@ -547,8 +570,40 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
                         const int32_t *start_pos, int T, float *logits, float *probs, cudaStream_t s) {
     BigState &g = ctx->big;
     const int n = (int)ctx->n;
-    if (T > 1 && start_pos) return cudaErrorNotSupported;  // prefill starts at position 0
     const int64_t V = ctx->V;
+    if (T > 1 && start_pos) {
+        // T positions per sequence from arbitrary start positions (chunked
+        // prefill, batched verification of a speculative path; the semantics
+        // of forward_batched, src/transformer.rs:461-517): every (sequence,
+        // offset) is a decode row. Each layer encodes all rows' K/V into the
+        // arena before its attention runs and a row attends positions up to
+        // its own, so a row sees exactly the cache of T sequential calls.
+        // Decode scratch holds max_seqs rows: larger calls run one offset per
+        // pass, in offset order.
+        const int S = (int)std::min<int64_t>(g.ws_tokens, ctx->cfg.max_seqs);
+        if ((int64_t)n_seq * T <= S) {
+            const int M = n_seq * T;
+            BIG_TRY(launch_pdl(expand_tokens_kernel, dim3((M + 255) / 256), dim3(256), 0, s, seq_ids, start_pos, T,
+                               n_seq, (int)ctx->B, ctx->cfg.max_seqs, (int)V, tokens, g.slot_of, g.pos_of,
+                               ctx->d_err));
+            BIG_TRY(launch_pdl(sanitize_tokens_kernel, dim3((M + 255) / 256), dim3(256), 0, s, tokens, M, (int)V,
+                               g.tok_of));
+            BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, M, g.x, s, g.delta));
+            BIG_TRY(run_layers(ctx, M, false, M, 1, s));
+            BIG_TRY(lm_head(ctx, M, logits, probs, V, s));
+            return cudaGetLastError();
+        }
+        if (n_seq > S) return cudaErrorInvalidValue;
+        for (int t = 0; t < T; ++t) {
+            BIG_TRY(launch_pdl(expand_offset_kernel, dim3((n_seq + 255) / 256), dim3(256), 0, s, seq_ids, start_pos,
+                               T, t, n_seq, (int)ctx->B, ctx->cfg.max_seqs, (int)V, tokens, g.slot_of, g.pos_of,
+                               g.tok_of, ctx->d_err));
+            BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, n_seq, g.x, s, g.delta));
+            BIG_TRY(run_layers(ctx, n_seq, false, n_seq, 1, s));
+            BIG_TRY(lm_head(ctx, n_seq, logits ? logits + t * V : nullptr, probs ? probs + t * V : nullptr, T * V, s));
+        }
+        return cudaGetLastError();
+    }
     if (T == 1) {
         // decode: tokens of up to ws_tokens sequences per pass
         for (int i0 = 0; i0 < n_seq; i0 += (int)std::min<int64_t>(g.ws_tokens, ctx->cfg.max_seqs)) {
@@ -561,7 +616,7 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
             BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, cnt, g.x, s, g.delta));
             BIG_TRY(run_layers(ctx, cnt, false, cnt, 1, s));
             BIG_TRY(lm_head(ctx, cnt, logits ? logits + (int64_t)i0 * V : nullptr,
-                            probs ? probs + (int64_t)i0 * V : nullptr, s));
+                            probs ? probs + (int64_t)i0 * V : nullptr, V, s));
         }
         return cudaGetLastError();
     }
@@ -577,7 +632,7 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
         BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, M, g.x, s, g.delta));
         BIG_TRY(run_layers(ctx, M, true, cnt, T, s));
         BIG_TRY(lm_head(ctx, M, logits ? logits + (int64_t)i0 * T * V : nullptr,
-                        probs ? probs + (int64_t)i0 * T * V : nullptr, s));
+                        probs ? probs + (int64_t)i0 * T * V : nullptr, V, s));
     }
     return cudaGetLastError();
 }

@@ -189,6 +189,11 @@ struct kg_ctx {
     void *comm = nullptr;
     int world = 1, rank = 0;
     float *probs_buf = nullptr;
+    // speculative verification scratch (kg_verify_dev): the path's target
+    // probabilities and forward tokens, grown to the largest n_seq * k seen
+    float *verify_probs = nullptr;
+    int32_t *verify_tok = nullptr;
+    int64_t verify_rows = 0;
 };
 
 namespace kg {

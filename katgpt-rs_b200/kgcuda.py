@@ -97,6 +97,8 @@ def lib():
             "kg_rng_state": (ctypes.c_int, [P, I32, P]),
             "kg_sample_dev": (ctypes.c_int, [P, I32, P, P, I64, P, P]),
             "kg_sample": (ctypes.c_int, [P, I32, P, P, P]),
+            "kg_verify_dev": (ctypes.c_int, [P, I32, P, P, P, P, I32, P, P, P, P]),
+            "kg_verify": (ctypes.c_int, [P, I32, P, P, P, P, I32, P, P, P]),
             "kg_comm_unique_id": (ctypes.c_int, [P]),
             "kg_comm_init": (ctypes.c_int, [P, P, I32, I32]),
             "kg_comm_destroy": (ctypes.c_int, [P]),
@@ -321,6 +323,21 @@ class CudaBackend:
         out = np.empty(n, np.int32)
         self._check(lib().kg_sample(self._h, n, _ptr(ids), _ptr(probs), _ptr(out)))
         return out
+
+    def verify(self, tokens, drafts, draft_probs, start_pos, seq_ids=None):
+        """Speculative verification of one draft path per sequence (kg_verify):
+        returns (accepted [n][k+1], n_accepted [n])."""
+        drafts = np.ascontiguousarray(drafts, np.int32)
+        n, k = drafts.shape
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        start_pos = np.ascontiguousarray(start_pos, np.int32)
+        q = np.ascontiguousarray(draft_probs, np.float32)
+        ids = np.arange(n, dtype=np.int32) if seq_ids is None else np.ascontiguousarray(seq_ids, np.int32)
+        acc = np.zeros((n, k + 1), np.int32)
+        cnt = np.zeros(n, np.int32)
+        self._check(lib().kg_verify(self._h, n, _ptr(ids), _ptr(start_pos), _ptr(tokens), _ptr(drafts), k, _ptr(q),
+                                    _ptr(acc), _ptr(cnt)))
+        return acc, cnt
 
     # ---- multi-GPU sequence shards
     def comm_init(self, uid, world, rank):

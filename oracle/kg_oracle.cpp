@@ -1145,6 +1145,70 @@ void or_sample_tokens(const float *probs, int64_t n, int64_t k, uint64_t seed, i
     }
 }
 
+// crates/katgpt-core/src/speculative/sampling.rs:26-40 (sample_from_distribution)
+static int64_t sample_dist(const float *probs, int64_t n, Rng &rng) {
+    float r = rng.uniform();
+    while (r == 0.0f) r = rng.uniform();
+    float cdf = 0.0f;
+    for (int64_t i = 0; i < n; ++i) {
+        cdf += probs[i];
+        if (r < cdf) return i;
+    }
+    return n > 0 ? n - 1 : 0;
+}
+// sampling.rs:50-116 (sample_residual_distribution_into)
+static int64_t sample_residual(const float *p, const float *q, int64_t n, Rng &rng) {
+    std::vector<float> scratch(n);
+    const int64_t chunks = n / 4;
+    float sum = 0.0f;
+    for (int64_t c = 0; c < chunks; ++c) {
+        const int64_t i = c * 4;
+        const float r0 = fmax_rs(p[i] - q[i], 0.0f), r1 = fmax_rs(p[i + 1] - q[i + 1], 0.0f);
+        const float r2 = fmax_rs(p[i + 2] - q[i + 2], 0.0f), r3 = fmax_rs(p[i + 3] - q[i + 3], 0.0f);
+        scratch[i] = r0; scratch[i + 1] = r1; scratch[i + 2] = r2; scratch[i + 3] = r3;
+        sum += (r0 + r1) + (r2 + r3);
+    }
+    for (int64_t i = chunks * 4; i < n; ++i) {
+        const float r = fmax_rs(p[i] - q[i], 0.0f);
+        scratch[i] = r;
+        sum += r;
+    }
+    if (sum > 0.0f) {
+        const float inv = 1.0f / sum;
+        for (int64_t i = 0; i < n; ++i) scratch[i] *= inv;
+        return sample_dist(scratch.data(), n, rng);
+    }
+    return sample_dist(p, n, rng);
+}
+
+// speculative_step_rollback's acceptance loop for one path (src/speculative/step.rs:150-222):
+// p [k][n] = the target's softmax_scaled distributions at the path's positions,
+// q [k][n] = the draft marginals, drafts [k]; out [k+1], returns the count
+int32_t or_verify_path(const float *p, const float *q, const int32_t *drafts, int32_t k, int64_t n, uint64_t seed,
+                       int32_t *out) {
+    Rng rng(seed);
+    int32_t count = 0;
+    int64_t cur = 0;
+    bool all = true;
+    for (int32_t i = 0; i < k; ++i) {
+        const int64_t d = drafts[i];
+        const bool inr = d >= 0 && d < n;
+        const float qi = inr ? q[i * n + d] : 0.0f;
+        const float pi = inr ? p[cur * n + d] : 0.0f;
+        const float acc = qi > 0.0f ? std::min(pi / qi, 1.0f) : 1.0f;
+        if (rng.uniform() <= acc) {
+            out[count++] = (int32_t)d;
+            if (i + 1 < k) cur = i + 1;
+        } else {
+            out[count++] = (int32_t)sample_residual(p + cur * n, q + i * n, n, rng);
+            all = false;
+            break;
+        }
+    }
+    if (all && k > 0) out[count++] = (int32_t)sample_dist(p + cur * n, n, rng);
+    return count;
+}
+
 int64_t or_tq_packed_len(int64_t dim, int bits) { return packed_len(dim, bits); }
 
 void or_tq_codebook(int64_t dim, int bits, float *centroids, float *boundaries, float *mse) {

@@ -72,6 +72,11 @@ int64_t or_sample_token(const float *probs, int64_t n, uint64_t seed);
 /* k successive sample_token_into draws from one Rng::new(seed): row j of
  * probs[k][n] -> out[j] */
 void or_sample_tokens(const float *probs, int64_t n, int64_t k, uint64_t seed, int64_t *out);
+/* speculative_step_rollback's acceptance loop (src/speculative/step.rs:150-222)
+ * for one path with Rng::new(seed): p [k][n] target distributions, q [k][n]
+ * draft marginals, drafts [k]; writes out [k+1], returns the count */
+int32_t or_verify_path(const float *p, const float *q, const int32_t *drafts, int32_t k, int64_t n, uint64_t seed,
+                       int32_t *out);
 /* scalar (non-SIMD) restatements used to cross-check the AVX2 ones */
 float or_scalar_exp(float x);
 

@@ -61,6 +61,7 @@ def lib():
             "or_softmax_scaled": (None, [P, I64, F32]),
             "or_sample_token": (I64, [P, I64, U64]),
             "or_sample_tokens": (None, [P, I64, I64, U64, P]),
+            "or_verify_path": (I32, [P, P, P, I32, I64, U64, P]),
             "or_scalar_exp": (F32, [F32]),
             "or_tq_packed_len": (I64, [I64, ctypes.c_int]),
             "or_tq_codebook": (None, [I64, ctypes.c_int, P, P, P]),
@@ -184,6 +185,16 @@ def sample_tokens(probs, seed):
     out = np.empty(p.shape[0], np.int64)
     lib().or_sample_tokens(_p(p), p.shape[1], p.shape[0], seed, _p(out))
     return out
+
+
+def verify_path(p, q, drafts, seed):
+    """The speculative acceptance loop for one path: (tokens, count)."""
+    p, q = f32(p), f32(q)
+    drafts = np.ascontiguousarray(drafts, np.int32)
+    k = drafts.size
+    out = np.zeros(k + 1, np.int32)
+    cnt = lib().or_verify_path(_p(p), _p(q), _p(drafts), k, p.shape[-1], seed, _p(out))
+    return out[:cnt], cnt
 
 
 def packed_len(dim, bits):

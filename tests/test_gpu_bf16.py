@@ -190,3 +190,30 @@ def test_quantized_attention_shapes(kg, orc, shape):
             cfg.n_head, cfg.n_embd, i, err[:T0].max(), err[T0:].max()))
         assert err.max() <= REL_BF16
     be.close()
+
+
+@pytest.mark.parametrize("max_seqs", [16, 2])
+def test_multi_position_call_from_nonzero_position(kg, orc, max_seqs):
+    # prefill 64, then one 6-token call from position 64 (chunked prefill /
+    # batched verification, forward_batched semantics): matches the oracle's
+    # 70 sequential positions and 70 single-token calls; max_seqs 2 forces one
+    # pass per position offset (2 x 6 rows > 2 decode rows)
+    cfg, be, w = make(kg, 1, std=0.02, vocab_size=128, block_size=96, n_embd=256, n_head=4, head_dim=64,
+                      n_kv_head=4, mlp_hidden=512, n_layer=2, max_seqs=max_seqs)
+    cfg2, be2, _ = make(kg, 1, std=0.02, vocab_size=128, block_size=96, n_embd=256, n_head=4, head_dim=64,
+                        n_kv_head=4, mlp_hidden=512, n_layer=2, max_seqs=max_seqs)
+    toks = tokens(2, 70, cfg.vocab_size, seed=31)
+    pre = be.forward_batch(toks[:, :64])
+    chunk = be.forward_batch(toks[:, 64:70], start_pos=np.full(2, 64))
+    got = np.concatenate([pre, chunk], axis=1)
+    singles = np.stack([be2.forward_batch(toks[:, t:t + 1], start_pos=np.full(2, t))[:, 0] for t in range(70)], axis=1)
+    for i in range(2):
+        ref = orc.run_sequence(orc.from_kg(cfg), 1, w, toks[i], key_bits=4, val_bits=4)[0]
+        assert rel_err(got[i], ref).max() <= REL_BF16
+        assert rel_err(chunk[i], singles[i, 64:]).max() <= 1e-3
+        # the chunk's codes equal the sequential calls' codes except near codebook boundaries
+        kp, vp, _ = be.kv_codes(i, 1, 67)
+        kp2, vp2, _ = be2.kv_codes(i, 1, 67)
+        assert (kp != kp2).mean() < 0.02 and (vp != vp2).mean() < 0.02
+    be.close()
+    be2.close()
