@@ -372,15 +372,18 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
     pf_flops = 2.0 * n * PRE * L * layer_w
     pf_gemm_tf = pf_flops / (float(pf_ms[2]) * 1e-3) / 1e12 if pf_ms[2] > 0 else None
 
-    # N > 1: each rank decodes its own sequences; NCCL gathers the logits of
-    # every rank after each step (the only collective on the path)
-    d_all = torch.empty((world, n, V), dtype=torch.float32, device=dev) if world > 1 else None
+    # N > 1: each rank decodes its own sequences; the library's NCCL
+    # all-gather (kg_decode_gather_dev, on the decode stream right after the
+    # step) collects every rank's logits (the only collective on the path)
+    d_all = torch.empty((world, n, V), dtype=torch.float32, device=dev)
+    if world > 1:
+        obj = [kgcuda.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        be.comm_init(obj[0], world, rank)
 
     def step(s):
         k = slot(s)
-        be.forward_batch_dev(n, 1, P(d_ids), P(d_dec[k]), P(d_pos[k]), P(d_log), None, sp)
-        if world > 1:
-            dist.all_gather_into_tensor(d_all, d_log)
+        be.decode_gather_dev(n, P(d_ids), P(d_dec[k]), P(d_pos[k]), P(d_all), None, sp)
 
     # warm-up: the first step of a batch shape runs eagerly, the second
     # captures the decode step as a CUDA graph, later steps replay it
@@ -459,7 +462,8 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": spec["scaling"],
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(args.workload, world, args.seqs, args.layers),
-        "collective": (f"NCCL all_gather of each rank's logits ({n} x {V} f32) per step" if world > 1 else None),
+        "collective": (f"NCCL all-gather of each rank's logits ({n} x {V} f32) per step inside the library "
+                       f"(kg_decode_gather_dev)" if world > 1 else None),
         "gpu_launches": int(graph_kernels * args.steps),
         "decode_step": "one CUDA graph per step" if graph_kernels else "eager",
         "kernels_per_step": int(graph_kernels),
@@ -490,6 +494,8 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
         line["mlp_hook"] = {"keep": spec["keep"], "note": "hidden activations after W1 replaced by Bernoulli(keep) "
                                                           "|N(0,1)| values (post-ReLU activations are non-negative; the "
                                                           "sparsity a trained TwELL model shows)"}
+    if world > 1:
+        be.comm_destroy()
     be.close()
     return line
 
