@@ -47,7 +47,7 @@ struct TqAttnArgs {
 int tq_padded_len(int block_size);
 cudaError_t tq_decode_attn(const TqAttnArgs &a, cudaStream_t s);
 // The tcgen05 form (kg_tcattn.cu): 4-bit / nibble-packed codes, kv_dim a
-// multiple of 256, at most 32 heads, block_size <= 6144.
+// multiple of 256 and at least 2048, at most 32 heads, block_size <= 6144.
 bool tc_attn_supported(const TqAttnArgs &a);
 cudaError_t tc_decode_attn(const TqAttnArgs &a, cudaStream_t s);
 

@@ -167,6 +167,8 @@ def test_standard_attention_matches_oracle(kg, orc, shape):
     dict(n_embd=1024, n_head=16, head_dim=64, n_kv_head=16, mlp_hidden=1024),  # four warps per score unit
     dict(n_embd=1280, n_head=20, head_dim=64, n_kv_head=20, mlp_hidden=1024),  # > 16 heads: streaming scores
     dict(n_embd=768, n_head=12, head_dim=64, n_kv_head=12, mlp_hidden=768, key_bits=3, val_bits=3),  # 3-bit
+    dict(n_embd=2048, n_head=16, head_dim=128, n_kv_head=16, mlp_hidden=1024),  # tcgen05 attention, 16-head tile
+    dict(n_embd=2048, n_head=16, head_dim=128, n_kv_head=16, mlp_hidden=1024, key_bits=3, val_bits=3),  # and 3-bit
 ])
 def test_quantized_attention_shapes(kg, orc, shape):
     # the decode attention kernels' shape variants against forward_quantized;
