@@ -834,12 +834,18 @@ struct Seq {
         }
     }
 
+    // optional copy of the rotated unit coordinates each store quantizes
+    // ([L][rot_T][2][kvd]; untouched for zero-norm vectors), for parity tests
+    float *rot_out = nullptr;
+    int64_t rot_T = 0;
     void store_kv(int64_t l, int64_t pos) {
         int64_t at = l * d.B + pos;
         tq_store(tq->rot.data(), tq->kb.data(), kbits, d.kvd, k.data(), &kcodes[at * kpl],
                  &knorm[at], sn.data(), sr.data(), si.data());
+        if (rot_out) std::memcpy(rot_out + ((l * rot_T + pos) * 2 + 0) * d.kvd, sr.data(), d.kvd * 4);
         tq_store(tq->rot.data(), tq->vb.data(), vbits, d.kvd, v.data(), &vcodes[at * vpl],
                  &vnorm[at], sn.data(), sr.data(), si.data());
+        if (rot_out) std::memcpy(rot_out + ((l * rot_T + pos) * 2 + 1) * d.kvd, sr.data(), d.kvd * 4);
     }
     void deq_key(int64_t l, int64_t t, float *out) {
         int64_t at = l * d.B + t;
@@ -1015,8 +1021,10 @@ static const Predictor &predictor_for(int64_t n, int64_t nkv) {
 
 static int run_one(const or_config *c, int mode, int kb, int vb, const Weights &W, const Dims &d,
                    const int32_t *tokens, int32_t T, float *logits, int32_t t0, uint8_t *codes,
-                   float *norms, float *utilities, bool shared_flat, Seq &s) {
+                   float *norms, float *utilities, bool shared_flat, Seq &s, float *rot_out = nullptr) {
     s.init(d, &W, mode == 3 ? OR_MODE_QUANT : mode, kb, vb);
+    s.rot_out = rot_out;
+    s.rot_T = T;
     s.sparse_threshold = c->sparse_threshold;
     s.quant_shared_flat = shared_flat;
     if (mode != OR_MODE_BASE) s.tq = &tq_tables(d.kvd, kb, vb);
@@ -1279,6 +1287,16 @@ int or_run_sequence(const or_config *c, int mode, int kb, int vb, const float *w
     // mode 3: forward_quantized with the reference's single shared flat buffer
     return run_one(c, mode, kb, vb, W, d, tokens, T, logits, 0, codes, norms, utilities, mode == 3,
                    s);
+}
+
+int or_run_sequence_rot(const or_config *c, int mode, int kb, int vb, const float *weights, const int32_t *tokens,
+                        int32_t T, float *logits, uint8_t *codes, float *norms, float *rot_out) {
+    if (check_cfg(c, T)) return -1;
+    if (mode != OR_MODE_QUANT && mode != OR_MODE_SPKV_QUANT) return -1;
+    Dims d = dims_of(c);
+    Weights W = view_weights(d, weights);
+    Seq s;
+    return run_one(c, mode, kb, vb, W, d, tokens, T, logits, 0, codes, norms, nullptr, false, s, rot_out);
 }
 
 int or_run_batch_tail(const or_config *c, int mode, int kb, int vb, const float *weights,

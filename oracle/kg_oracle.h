@@ -114,6 +114,13 @@ int or_run_sequence(const or_config *c, int mode, int key_bits, int val_bits,
                     const float *weights, const int32_t *tokens, int32_t T,
                     float *logits, uint8_t *codes, float *norms, float *utilities);
 
+/* Same for the quantized modes, also writing the rotated unit coordinates
+ * each TurboQuant store quantizes: rot_out[L][T][2][kvd] (K then V; rows of
+ * zero-norm vectors untouched). */
+int or_run_sequence_rot(const or_config *c, int mode, int key_bits, int val_bits, const float *weights,
+                        const int32_t *tokens, int32_t T, float *logits, uint8_t *codes, float *norms,
+                        float *rot_out);
+
 /* Multi-sequence runner: n_seq sequences of T tokens each (row-major),
  * spread over n_threads std::threads (one per core, as the reference's rayon
  * generate_batch). logits may be NULL (discarded) for timing runs. */

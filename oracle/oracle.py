@@ -75,6 +75,7 @@ def lib():
             "or_cosine": (F32, [P, P, I64]),
             "or_run_sequence": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, P, P, P, P]),
             "or_run_batch": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, P, ctypes.c_int]),
+            "or_run_sequence_rot": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, P, P, P, P]),
             "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
             "or_time_decode": (ctypes.c_double, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, I32, I32, ctypes.c_int]),
         }
@@ -292,6 +293,24 @@ def run_sequence(cfg, mode, w, tokens, key_bits=3, val_bits=3):
     if rc:
         raise RuntimeError(f"or_run_sequence failed: {rc}")
     return logits, codes, norms, util
+
+
+def run_sequence_rot(cfg, mode, w, tokens, key_bits=3, val_bits=3):
+    """run_sequence for the quantized modes plus the rotated unit coordinates of
+    every stored K/V vector: (logits[T,V], codes, norms, rot[L,T,2,kvd])."""
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    T = tokens.size
+    kvd = cfg.n_kv_head * cfg.head_dim
+    logits = np.empty((T, cfg.vocab_size), np.float32)
+    pl = packed_len(kvd, key_bits) + packed_len(kvd, val_bits)
+    codes = np.zeros((cfg.n_layer, T, pl), np.uint8)
+    norms = np.zeros((cfg.n_layer, T, 2), np.float32)
+    rot = np.zeros((cfg.n_layer, T, 2, kvd), np.float32)
+    rc = lib().or_run_sequence_rot(ctypes.byref(cfg), mode, key_bits, val_bits, _p(f32(w)), _p(tokens), T,
+                                   _p(logits), _p(codes), _p(norms), _p(rot))
+    if rc:
+        raise RuntimeError(f"or_run_sequence_rot failed: {rc}")
+    return logits, codes, norms, rot
 
 
 def run_batch(cfg, mode, w, tokens, key_bits=3, val_bits=3, threads=None, keep_logits=True, t0=0):
