@@ -241,6 +241,21 @@ int kg_comm_destroy(kg_ctx *ctx);
 int kg_decode_gather_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
                          const int32_t *positions, float *logits_all, int32_t *tokens_all, void *stream);
 
+/* ---- forward_prefill (src/transformer.rs:2606-3004) ----
+ * The reference's prefill variant: over the prompt tokens[i][0..T) of each
+ * sequence (from position 0) every layer normalises twice (rmsnorm without
+ * gammas), writes K/V of every position into the cache, lets every position
+ * attend the WHOLE prompt (bidirectional), and runs delta routing with one
+ * block-delta accumulator shared by the prompt's positions in order. Writes
+ * the last position's logits, logits_out [n_seq][vocab]; the cache then holds
+ * positions 0..T-1, and decoding continues with kg_forward_batch at position T
+ * (generate_with_prefill, :3010-3106). Contexts with kv_mode KG_KV_F32. */
+int kg_forward_prefill(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, int32_t T,
+                       float *logits_out);
+/* Device-pointer form, enqueued on `stream`. */
+int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, int32_t T,
+                           float *logits_out, void *stream);
+
 /* ---- TurboQuant codec access (parity / inspection) ---- */
 
 /* Packed bytes per vector for `bits` at dimension `dim` (kv_cache.rs:499-509). */

@@ -612,6 +612,69 @@ int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const i
     return KG_OK;
 }
 
+int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, int32_t T,
+                           float *logits_out, void *stream) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (!ctx->compiled) return fail(ctx, KG_ERR_NOT_COMPILED, "weights not uploaded");
+    if (ctx->cfg.kv_mode != KG_KV_F32)
+        return fail(ctx, KG_ERR_UNSUPPORTED, "forward_prefill runs over the f32 / bf16 K/V cache (kv_mode F32)");
+    if (n_seq < 0 || T < 1 || T > ctx->B || (ctx->micro && T > 16) || !seq_ids || !tokens || !logits_out)
+        return fail(ctx, KG_ERR_INVALID_ARG, "bad batch shape");
+    if (n_seq == 0) return KG_OK;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (ctx->big_path) {
+        KG_CUDA(ctx, kg::big_forward_prefill(ctx, n_seq, seq_ids, tokens, T, logits_out, s));
+        return KG_OK;
+    }
+    if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no forward kernel for this model shape");
+    kg::MicroArgs a = ctx->margs;
+    a.n_seq = n_seq;
+    a.T = T;
+    a.seq_ids = seq_ids;
+    a.tokens = tokens;
+    a.start_pos = nullptr;
+    a.logits = logits_out;
+    a.probs = nullptr;
+    KG_CUDA(ctx, kg::launch_micro_prefill(ctx->cfg, a, s));
+    return KG_OK;
+}
+
+int kg_forward_prefill(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, int32_t T,
+                       float *logits_out) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (n_seq < 0 || T < 1 || T > ctx->B || !seq_ids || !tokens || !logits_out)
+        return fail(ctx, KG_ERR_INVALID_ARG, "bad batch shape");
+    if (n_seq == 0) return KG_OK;
+    for (int32_t i = 0; i < n_seq; ++i)
+        if (seq_ids[i] < 0 || seq_ids[i] >= ctx->cfg.max_seqs)
+            return fail(ctx, KG_ERR_INVALID_ARG, "sequence id out of range");
+    for (int64_t i = 0; i < (int64_t)n_seq * T; ++i)
+        if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, KG_ERR_INVALID_ARG, "token out of range");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t b_ids = align256(n_seq * 4), b_tok = align256((size_t)n_seq * T * 4);
+    const size_t b_out = align256((size_t)n_seq * ctx->V * 4);
+    int rc = ensure_stage(ctx, b_ids + b_tok + b_out);
+    if (rc) return rc;
+    char *st = static_cast<char *>(ctx->stage);
+    int32_t *d_ids = reinterpret_cast<int32_t *>(st);
+    int32_t *d_tok = reinterpret_cast<int32_t *>(st + b_ids);
+    float *d_log = reinterpret_cast<float *>(st + b_ids + b_tok);
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemcpyAsync(d_ids, seq_ids, n_seq * 4, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(d_tok, tokens, (size_t)n_seq * T * 4, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, cudaMemsetAsync(ctx->d_err, 0, 4, s));
+    rc = kg_forward_prefill_dev(ctx, n_seq, d_ids, d_tok, T, d_log, s);
+    if (rc) return rc;
+    KG_CUDA(ctx, cudaMemcpyAsync(logits_out, d_log, (size_t)n_seq * ctx->V * 4, cudaMemcpyDeviceToHost, s));
+    int herr = 0;
+    KG_CUDA(ctx, cudaMemcpyAsync(&herr, ctx->d_err, 4, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    if (herr == KG_ERR_TIMEOUT) return fail(ctx, KG_ERR_TIMEOUT, "a device-side wait exceeded its limit");
+    if (herr) return fail(ctx, KG_ERR_INVALID_ARG, "device rejected a token, position or slot");
+    return KG_OK;
+}
+
 int kg_forward_token(kg_ctx *ctx, int32_t seq, int32_t token, int32_t pos, float *logits_out) {
     return kg_forward_batch(ctx, 1, &seq, &token, &pos, 1, logits_out, nullptr);
 }

@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(128) fa_kernel(const FlashArgs a) {
         for (int e = 0; e < 4; ++e) o[j][e] = 0.0f;
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
     const float sl2 = a.scale * 1.4426950408889634f;
-    const int kend = min(T, qt0 + 64);
+    const int kend = a.bidir ? T : min(T, qt0 + 64);
     for (int k0 = 0; k0 < kend; k0 += KT) {
         __syncthreads();
         for (int e = threadIdx.x; e < KT * HD / 8; e += blockDim.x) {
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(128) fa_kernel(const FlashArgs a) {
             *reinterpret_cast<uint4 *>(sVl + r * LD + cc) = vl;
         }
         __syncthreads();
-        if (k0 > q0 + 15) continue;  // whole tile in the future for this warp
+        if (!a.bidir && k0 > q0 + 15) continue;  // whole tile in the future for this warp
         float s[KT / 8][4];
 #pragma unroll
         for (int j = 0; j < KT / 8; ++j)
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(128) fa_kernel(const FlashArgs a) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int kj = k0 + j * 8 + 2 * c + e;
-                    float v = (kj <= qi && kj < T) ? s[j][hr * 2 + e] * sl2 : -INFINITY;
+                    float v = ((a.bidir || kj <= qi) && kj < T) ? s[j][hr * 2 + e] * sl2 : -INFINITY;
                     s[j][hr * 2 + e] = v;
                     mx = fmaxf(mx, v);
                 }

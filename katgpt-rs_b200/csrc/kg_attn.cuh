@@ -18,6 +18,7 @@ struct FlashArgs {
     int64_t ldq, ldk, ldo;
     int n_seq, T, nh, nkv, hd;
     float scale;
+    int bidir;  // 1: every query attends all T keys (forward_prefill); 0: causal
 };
 
 // Decode attention of M single-token queries over 4-bit / 3-bit codes as two

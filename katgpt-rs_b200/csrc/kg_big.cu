@@ -147,6 +147,7 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.dn, L * n, own));
     BIG_TRY(dalloc(&g.ag, L * n, own));
     BIG_TRY(dalloc(&g.mg, L * n, own));
+    BIG_TRY(dalloc(&g.pdelta, S * n, own));
     g.std_kv = c.kv_mode == KG_KV_F32;
     if (g.std_kv) {  // standard attention: bf16 K/V arena
         BIG_TRY(dalloc(&g.kcache, (size_t)S * L * B * kvd, own));
@@ -467,6 +468,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             fa.Q = g.qh; fa.Q_lo = g.ql; fa.K = g.kt; fa.K_lo = g.kt2; fa.V = g.vt; fa.V_lo = g.vt2; fa.O = g.attf;
             fa.ldq = n; fa.ldk = kvd; fa.ldo = n;
             fa.n_seq = n_seq; fa.T = T; fa.nh = nh; fa.nkv = (int)ctx->nkv; fa.hd = hd; fa.scale = scale;
+            fa.bidir = 0;
             BIG_TRY(attn::flash_prefill(fa, s));
         } else {
             if (fork)
@@ -633,6 +635,133 @@ cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const in
         BIG_TRY(run_layers(ctx, M, true, cnt, T, s));
         BIG_TRY(lm_head(ctx, M, logits ? logits + (int64_t)i0 * T * V : nullptr,
                         probs ? probs + (int64_t)i0 * T * V : nullptr, V, s));
+    }
+    return cudaGetLastError();
+}
+
+namespace {
+
+__device__ __forceinline__ float block_sum_f(float v, float *red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    return t;
+}
+
+// forward_prefill's delta routing for one layer (src/transformer.rs:2954-2982):
+// one CTA per sequence keeps the sequence's block-delta accumulator D and walks
+// the positions in order: D += x_p - xr_p; at a routing layer (l % 4 == 3) the
+// position routes with D as it stands (blocks 0..b-1 are zero by then, the
+// routing softmax over them and D, transformer.rs:1707-1765) and D is zeroed.
+__global__ void prefill_route_kernel(float *x, const float *xr, float *D, const float *query, const float *normw,
+                                     int n, int T, int layer) {
+    pdl_wait();
+    __shared__ float red[32];
+    const int seq = blockIdx.x, tid = threadIdx.x;
+    float *d = D + (int64_t)seq * n;
+    const bool routing = (layer & 3) == 3;
+    const int b = layer >> 2;
+    for (int p = 0; p < T; ++p) {
+        float *xp = x + ((int64_t)seq * T + p) * n;
+        const float *rp = xr + ((int64_t)seq * T + p) * n;
+        for (int j = tid; j < n; j += blockDim.x) d[j] = d[j] + (xp[j] - rp[j]);
+        if (!routing) continue;  // no cross-thread reads this round: each thread owns its j
+        __syncthreads();
+        float ss = 0.0f;
+        for (int j = tid; j < n; j += blockDim.x) ss += d[j] * d[j];
+        ss = block_sum_f(ss, red);
+        const float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
+        float dt = 0.0f;
+        for (int j = tid; j < n; j += blockDim.x) dt += normw[j] * (d[j] * inv) * query[j];
+        const float own = block_sum_f(dt, red);
+        // b zero sources with logit 0 and the accumulator with logit `own`
+        const float mx = b > 0 ? fmaxf(0.0f, own) : own;
+        const float ez = expf(-mx), eo = expf(own - mx);
+        const float w = eo / ((float)b * ez + eo);
+        for (int j = tid; j < n; j += blockDim.x) {
+            xp[j] = xp[j] + w * d[j];
+            d[j] = 0.0f;
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+// forward_prefill (src/transformer.rs:2606-3004) on the bf16 path, standard
+// attention: per layer a double rmsnorm (no gamma), the fused QKV GEMM, K/V
+// into the bf16 cache, attention of every position over the whole prompt
+// (bidirectional), Wo + residual, rmsnorm, W1 / W2 + residual, then the
+// position-ordered delta routing. Writes the last position's logits per
+// sequence (logits [n_seq][V]) and leaves positions 0..T-1 in the cache.
+cudaError_t big_forward_prefill(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const int32_t *tokens, int T,
+                                float *logits, cudaStream_t s) {
+    BigState &g = ctx->big;
+    if (!g.std_kv) return cudaErrorNotSupported;
+    const int n = (int)ctx->n, kvd = (int)ctx->kvd, m = (int)ctx->m, L = (int)ctx->L, B = (int)ctx->B;
+    const int nh = (int)ctx->nh, hd = (int)ctx->hd, V = (int)ctx->V, nqkv = n + 2 * kvd;
+    const int64_t per_layer = 2 * (int64_t)n * n + 2 * (int64_t)kvd * n + 2 * (int64_t)m * n;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const int per = (int)std::max<int64_t>(1, std::min<int64_t>(g.ws_tokens / T, ctx->cfg.max_seqs));
+    for (int i0 = 0; i0 < n_seq; i0 += per) {
+        const int cnt = std::min(per, n_seq - i0), M = cnt * T;
+        BIG_TRY(launch_pdl(expand_tokens_kernel, dim3((M + 255) / 256), dim3(256), 0, s, seq_ids + i0,
+                           (const int32_t *)nullptr, T, cnt, B, ctx->cfg.max_seqs, V, tokens + (int64_t)i0 * T,
+                           g.slot_of, g.pos_of, ctx->d_err));
+        BIG_TRY(launch_pdl(sanitize_tokens_kernel, dim3((M + 255) / 256), dim3(256), 0, s, tokens + (int64_t)i0 * T,
+                           M, V, g.tok_of));
+        BIG_TRY(bf::embed(g.tok_of, g.pos_of, g.wte, g.wpe, n, M, g.x, s));
+        BIG_TRY(cudaMemsetAsync(g.pdelta, 0, (size_t)cnt * n * sizeof(float), s));
+        for (int l = 0; l < L; ++l) {
+            const bf16 *wqkv = g.layers + l * per_layer;
+            const bf16 *wo = wqkv + (int64_t)nqkv * n, *w1 = wo + (int64_t)n * n, *w2 = w1 + (int64_t)m * n;
+            // phase A: xr = rmsnorm(x); the projections read rmsnorm(xr) (:2674-2677)
+            BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, nullptr, nullptr, false, s));
+            BIG_TRY(bf::rmsnorm(g.xr, n, M, nullptr, g.xb, g.xb2, false, s));
+            bf::Gemm q = gemm0();
+            q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = wqkv; q.ldb = n; q.M = M; q.N = nqkv; q.K = n;
+            q.epi = bf::EPI_F32; q.C = g.qkv; q.ldc = nqkv;
+            BIG_TRY(gemm_split(ctx, q, s));
+            BIG_TRY(attn::kv_store_std(g.qkv, nqkv, n, n + kvd, kvd, M, g.slot_of, g.pos_of, L, B, l, g.kcache,
+                                       g.vcache, g.kt, g.kt2, g.vt, g.vt2, s));
+            BIG_TRY(bf::to_f16(g.qkv, nqkv, n, M, g.qh, g.ql, n, s));
+            // phase B: every position attends the whole prompt (:2863, :2892)
+            attn::FlashArgs fa;
+            fa.Q = g.qh; fa.Q_lo = g.ql; fa.K = g.kt; fa.K_lo = g.kt2; fa.V = g.vt; fa.V_lo = g.vt2; fa.O = g.attf;
+            fa.ldq = n; fa.ldk = kvd; fa.ldo = n;
+            fa.n_seq = cnt; fa.T = T; fa.nh = nh; fa.nkv = (int)ctx->nkv; fa.hd = hd; fa.scale = scale; fa.bidir = 1;
+            BIG_TRY(attn::flash_prefill(fa, s));
+            BIG_TRY(bf::to_bf16(g.attf, n, n, M, g.attb, g.attb2, n, s));
+            bf::Gemm w = gemm0();
+            w.A = g.attb; w.A2 = g.attb2; w.lda = n; w.B = wo; w.ldb = n; w.M = M; w.N = n; w.K = n;
+            w.epi = bf::EPI_F32_RESID; w.C = g.x; w.ldc = n; w.R = g.xr; w.ldr = n; w.C2 = g.xr2;
+            BIG_TRY(gemm_split(ctx, w, s));
+            BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s, g.alive));
+            bf::Gemm u = gemm0();
+            u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
+            u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;
+            BIG_TRY(gemm_split(ctx, u, s));
+            bf::Gemm dn = gemm0();
+            dn.A = g.hid; dn.A2 = g.hid2; dn.lda = m; dn.B = w2; dn.ldb = m; dn.M = M; dn.N = n; dn.K = m;
+            dn.epi = bf::EPI_F32_RESID; dn.C = g.x; dn.ldc = n; dn.R = g.xr2; dn.ldr = n;
+            BIG_TRY(gemm_split(ctx, dn, s));
+            if (M <= kTwellMaxRows)
+                BIG_TRY(bf::twell_sparse_w2(g.hid, g.hid2, g.alive, g.w2t + (int64_t)l * m * n, g.xr2, g.x, n, m, M,
+                                            ctx->cfg.sparse_threshold, s));
+            BIG_TRY(launch_pdl(prefill_route_kernel, dim3(cnt), dim3(256), 0, s, g.x, (const float *)g.xr, g.pdelta,
+                               (const float *)(g.dq + (int64_t)l * n), (const float *)(g.dn + (int64_t)l * n), n, T,
+                               l));
+        }
+        // lm_head of each sequence's last position
+        BIG_TRY(bf::to_bf16(g.x + (int64_t)(T - 1) * n, (int64_t)T * n, n, cnt, g.xb, g.xb2, n, s));
+        bf::Gemm q = gemm0();
+        q.A = g.xb; q.A2 = g.xb2; q.lda = n; q.B = g.lm; q.ldb = n; q.M = cnt; q.N = V; q.K = n;
+        q.epi = bf::EPI_F32; q.C = logits + (int64_t)i0 * V; q.ldc = V;
+        BIG_TRY(gemm_split(ctx, q, s));
     }
     return cudaGetLastError();
 }

@@ -41,6 +41,9 @@ struct MicroArgs {
 // Returns 0 if the model shape has a compiled micro kernel.
 int micro_supported(const kg_config &c);
 cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s);
+// forward_prefill (bidirectional, src/transformer.rs:2606-3004) of positions
+// 0..T-1; writes one logits row per sequence (the last position's)
+cudaError_t launch_micro_prefill(const kg_config &c, const MicroArgs &a, cudaStream_t s);
 
 // TurboQuant device helpers (kg_tq.cu)
 // Modified Gram-Schmidt of a row-major dim x dim Gaussian matrix `g`
@@ -94,6 +97,7 @@ struct BigState {
     __nv_bfloat16 *wte = nullptr, *wpe = nullptr, *layers = nullptr, *lm = nullptr, *w2t = nullptr;
     float *dq = nullptr, *dn = nullptr;                // delta routing query / norm [L][n]
     float *ag = nullptr, *mg = nullptr;                // attn_norm_gamma / mlp_norm_gamma [L][n]
+    float *pdelta = nullptr;                           // forward_prefill block-delta accumulator [max_seqs][n]
     __half *rot_h = nullptr, *rot_l = nullptr, *rot_th = nullptr, *rot_tl = nullptr;  // f16 hi/lo of R, R^T
     float *kcent = nullptr, *vcent = nullptr;          // 16 centroids each
     uint8_t *kcodes = nullptr, *vcodes = nullptr;      // [slot][layer][pos][pl]
@@ -206,6 +210,8 @@ cudaError_t big_random_weights(kg_ctx *ctx, uint64_t seed, float std_);
 cudaError_t big_download(kg_ctx *ctx, float *dst_dev, int64_t offset, int64_t count);
 cudaError_t big_forward(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const int32_t *tokens,
                         const int32_t *start_pos, int T, float *logits, float *probs, cudaStream_t s);
+cudaError_t big_forward_prefill(kg_ctx *ctx, int n_seq, const int32_t *seq_ids, const int32_t *tokens, int T,
+                                float *logits, cudaStream_t s);
 // per-slot sampler generators, Rng::new(slot) (kg_sample.cu)
 cudaError_t sampler_init(kg_ctx *ctx);
 }  // namespace kg

@@ -32,7 +32,7 @@
 namespace kg {
 namespace {
 
-constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2;
+constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2, MODE_PREFILL = 3;
 
 template <int KVD>
 __device__ __forceinline__ uint8_t quantize(float r, const float *bnd, int nb) {
@@ -114,6 +114,62 @@ __device__ __forceinline__ void rmsnorm_gamma(float (&x)[N], const float *g) {
     for (int i = 0; i < N; ++i) x[i] = i < BODY ? g[i] * (x[i] * inv) : (g[i] * x[i]) * inv;
 }
 
+// Delta routing at a routing layer l (l % 4 == 3; transformer.rs:1707-1765,
+// :287-320): sources are blocks 0..b-1 (already zeroed) and block b = `delta`;
+// softmax over the logits dot(gamma * rmsnorm(source), query) with the Cephes
+// exp, then x += w_s * source.
+template <int N>
+__device__ __forceinline__ void route_block(float (&x)[N], const float (&delta)[N], int l, const float *qw,
+                                            const float *nw) {
+    const int b = l >> 2;
+    float lg[16];
+    float zero_logit;
+    {
+        float z[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) z[j] = 0.0f;
+        float rms = sqrtf(kgx::sum_sq<N>(z) / (float)N + 1e-5f);
+        float inv = 1.0f / rms;
+#pragma unroll
+        for (int j = 0; j < N; ++j) z[j] = (j < N / 8 * 8) ? nw[j] * (z[j] * inv) : nw[j] * z[j] * inv;
+        zero_logit = kgx::dot<N>(z, qw);
+    }
+    float own_logit;
+    {
+        float sd[N];
+        float rms = sqrtf(kgx::sum_sq<N>(delta) / (float)N + 1e-5f);
+        float inv = 1.0f / rms;
+#pragma unroll
+        for (int j = 0; j < N; ++j) sd[j] = (j < N / 8 * 8) ? nw[j] * (delta[j] * inv) : nw[j] * delta[j] * inv;
+        own_logit = kgx::dot<N>(sd, qw);
+    }
+    const int ns = b + 1;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < 16; ++s) {
+        lg[s] = s < b ? zero_logit : own_logit;
+        if (s < ns) mx = kgx::fmax_rs(mx, lg[s]);
+    }
+    const int body = ns / 8 * 8;
+#pragma unroll
+    for (int s = 0; s < 16; ++s) {
+        float e = lg[s] + (-mx);
+        lg[s] = s < body ? kgx::cephes_lane(e, true) : kgx::cephes_scalar(e);
+    }
+    float se = kgx::sum_rt<16>(lg, ns);
+    float inv_sum = 1.0f / se;
+#pragma unroll
+    for (int s = 0; s < 16; ++s)
+        if (s < ns) {
+            float w = lg[s] * inv_sum;
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                float src = s < b ? 0.0f : delta[j];
+                x[j] = (j < N / 8 * 8) ? fmaf(w, src, x[j]) : x[j] + w * src;
+            }
+        }
+}
+
 template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE>
 __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     constexpr int KVD = NKV * HD;
@@ -131,6 +187,8 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     const int sl = threadIdx.x / T, tl = threadIdx.x - sl * T;
     const int n_groups = (p.n_seq + SB - 1) / SB;
     float *scs = sm + p.pack_floats + threadIdx.x * (BLK + 1);  // per-thread score row
+    // forward_prefill: this sequence's block-delta accumulator
+    float *dacc = sm + p.pack_floats + blockDim.x * (BLK + 1) + (threadIdx.x / p.T) * N;
     for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
     __syncthreads();  // previous group's attention reads are done
     const int i = grp * SB + sl;
@@ -144,6 +202,11 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
             atomicExch(p.err, 1);
             active = false;
         }
+    }
+    if constexpr (MODE == MODE_PREFILL) {
+        if (tl == 0)
+#pragma unroll
+            for (int j = 0; j < N; ++j) dacc[j] = 0.0f;
     }
     const float *wte = sm + p.off_wte, *wpe = sm + p.off_wpe;
     float x[N];
@@ -169,6 +232,7 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         float xr[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) xr[j] = x[j];
+        if constexpr (MODE == MODE_PREFILL) rmsnorm<N>(x);  // forward_prefill's double norm (:2674-2677)
         float util = 0.0f;
         if constexpr (MODE == MODE_SPKV) {
             rmsnorm<N>(x);  // double norm (sp_kv/forward.rs:648-651)
@@ -196,7 +260,7 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
 
         if (active) {
             float *kd = p.Kf + (row + pos) * KVD, *vd = p.Vf + (row + pos) * KVD;
-            if constexpr (MODE == MODE_BASE) {
+            if constexpr (MODE == MODE_BASE || MODE == MODE_PREFILL) {
 #pragma unroll
                 for (int j = 0; j < KVD; ++j) {
                     kd[j] = k[j];
@@ -222,7 +286,8 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
 
         // ---- attention over positions 0..pos
         float att[N];
-        const int tn = pos + 1;
+        // forward_prefill attends every prompt position (bidirectional, :2863)
+        const int tn = MODE == MODE_PREFILL ? T : pos + 1;
         const float *Kb = p.Kf + row * KVD, *Vb = p.Vf + row * KVD;
 #pragma unroll 1
         for (int h = 0; h < NH; ++h) {
@@ -350,73 +415,49 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         for (int j = 0; j < N; ++j) x[j] = x[j] + xr2[j];
 
         // ---- delta routing (not in the sp_kv path)
-        if constexpr (MODE != MODE_SPKV) {
+        if constexpr (MODE == MODE_PREFILL) {
+            // forward_prefill keeps one set of block deltas for the whole
+            // prompt (src/transformer.rs:2954-2982): positions add their delta
+            // in order, and at a routing layer each position routes with the
+            // accumulator as it stands and zeroes it. One barrier round per
+            // position, the sequence's accumulator in shared memory.
+            const float *qw = sm + p.off_dq + l * N, *nw = sm + p.off_dn + l * N;
+            for (int rnd = 0; rnd < T; ++rnd) {
+                if (active && tl == rnd) {
+#pragma unroll
+                    for (int j = 0; j < N; ++j) dacc[j] = dacc[j] + (x[j] - xr[j]);
+                    if ((l & 3) == 3) {
+                        float dl[N];
+#pragma unroll
+                        for (int j = 0; j < N; ++j) dl[j] = dacc[j];
+                        route_block<N>(x, dl, l, qw, nw);
+#pragma unroll
+                        for (int j = 0; j < N; ++j) dacc[j] = 0.0f;
+                    }
+                }
+                __syncthreads();
+            }
+        } else if constexpr (MODE != MODE_SPKV) {
 #pragma unroll
             for (int j = 0; j < N; ++j) delta[j] = delta[j] + (x[j] - xr[j]);
             if ((l & 3) == 3) {
-                const int b = l >> 2;  // sources: blocks 0..b-1 (already zeroed) and b
-                const float *qw = sm + p.off_dq + l * N, *nw = sm + p.off_dn + l * N;
-                float lg[16];
-                float zero_logit;
-                {
-                    float z[N];
-#pragma unroll
-                    for (int j = 0; j < N; ++j) z[j] = 0.0f;
-                    float rms = sqrtf(kgx::sum_sq<N>(z) / (float)N + 1e-5f);
-                    float inv = 1.0f / rms;
-#pragma unroll
-                    for (int j = 0; j < N; ++j)
-                        z[j] = (j < N / 8 * 8) ? nw[j] * (z[j] * inv) : nw[j] * z[j] * inv;
-                    zero_logit = kgx::dot<N>(z, qw);
-                }
-                float own_logit;
-                {
-                    float sd[N];
-                    float rms = sqrtf(kgx::sum_sq<N>(delta) / (float)N + 1e-5f);
-                    float inv = 1.0f / rms;
-#pragma unroll
-                    for (int j = 0; j < N; ++j)
-                        sd[j] = (j < N / 8 * 8) ? nw[j] * (delta[j] * inv) : nw[j] * delta[j] * inv;
-                    own_logit = kgx::dot<N>(sd, qw);
-                }
-                const int ns = b + 1;
-                float mx = -INFINITY;
-#pragma unroll
-                for (int s = 0; s < 16; ++s) {
-                    lg[s] = s < b ? zero_logit : own_logit;
-                    if (s < ns) mx = kgx::fmax_rs(mx, lg[s]);
-                }
-                const int body = ns / 8 * 8;
-#pragma unroll
-                for (int s = 0; s < 16; ++s) {
-                    float e = lg[s] + (-mx);
-                    lg[s] = s < body ? kgx::cephes_lane(e, true) : kgx::cephes_scalar(e);
-                }
-                float se = kgx::sum_rt<16>(lg, ns);
-                float inv_sum = 1.0f / se;
-#pragma unroll
-                for (int s = 0; s < 16; ++s)
-                    if (s < ns) {
-                        float w = lg[s] * inv_sum;
-#pragma unroll
-                        for (int j = 0; j < N; ++j) {
-                            float src = s < b ? 0.0f : delta[j];
-                            x[j] = (j < N / 8 * 8) ? fmaf(w, src, x[j]) : x[j] + w * src;
-                        }
-                    }
+                route_block<N>(x, delta, l, sm + p.off_dq + l * N, sm + p.off_dn + l * N);
 #pragma unroll
                 for (int j = 0; j < N; ++j) delta[j] = 0.0f;
             }
         }
     }
 
-    // ---- lm_head (+ softmax_scaled)
+    // ---- lm_head (+ softmax_scaled); forward_prefill returns the last position's
     if (!active) continue;
+    if constexpr (MODE == MODE_PREFILL) {
+        if (tl != T - 1) continue;
+    }
     const float *lm = sm + p.off_lm;
     float lg[VOC];
 #pragma unroll
     for (int r = 0; r < VOC; ++r) lg[r] = kgx::dot<N>(lm + r * N, x);
-    const int64_t orow = ((int64_t)i * T + tl) * VOC;
+    const int64_t orow = (MODE == MODE_PREFILL ? (int64_t)i : (int64_t)i * T + tl) * VOC;
     if (p.logits) {
 #pragma unroll
         for (int r = 0; r < VOC; ++r) p.logits[orow + r] = lg[r];
@@ -468,7 +509,7 @@ cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     const int SB = 128 / T;
     const int threads = SB * T;
     const int blocks = (a.n_seq + SB - 1) / SB;
-    const size_t smem = ((size_t)a.pack_floats + 128 * 17) * sizeof(float);
+    const size_t smem = ((size_t)a.pack_floats + 128 * 17 + (MODE == MODE_PREFILL ? 128 * 16 : 0)) * sizeof(float);
     auto kfn = micro_forward<16, 4, 4, 4, 64, 27, 16, MODE>;
     cudaError_t e = dev::smem(kfn, smem);
     if (e != cudaSuccess) return e;
@@ -487,6 +528,13 @@ int micro_supported(const kg_config &c) {
               c.weight_dtype == KG_W_F32 && c.n_layer >= 1 && c.n_layer <= 60;
     if (c.kv_mode == KG_KV_SPKV_TQ) ok = ok && c.spkv_window >= c.block_size;
     return ok ? 0 : -1;
+}
+
+// forward_prefill over positions 0..T-1 of each sequence (forward_base family: f32 K/V)
+cudaError_t launch_micro_prefill(const kg_config &c, const MicroArgs &a, cudaStream_t s) {
+    if (a.n_seq <= 0) return cudaSuccess;
+    if (a.T < 1 || a.T > 16 || c.kv_mode != KG_KV_F32 || a.start_pos) return cudaErrorInvalidValue;
+    return launch_mode<MODE_PREFILL>(a, s);
 }
 
 cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s) {

@@ -9,23 +9,24 @@
 // Three launches per layer:
 //  * tc_scores_kernel — CTA = (two 128-position tiles, token). D[128 positions
 //    x NHP heads] += A[positions x 16 dims] B[16 dims x heads] with A in
-//    tensor memory: decoder thread r owns TMEM lane r (= position r of its
-//    tile), turns its row's 32 code bytes per 64-dim block into f16 centroid
-//    pairs through a 32-replica shared-memory table (entry (b, l) at word
-//    32 b + l, lane l reads replica l: conflict-free) and stores them with
-//    tcgen05.st; q~ arrives by TMA (128-byte swizzle) as the B operand. The
+//    tensor memory: two decoder threads own TMEM lane r (= position r of its
+//    tile), each turning 16 of its row's 32 code bytes per 64-dim block into
+//    f16 centroid pairs through a 32-replica shared-memory table (entry (b, l)
+//    at word 32 b + l, lane l reads replica l: conflict-free) and storing them
+//    with tcgen05.st; q~ arrives by TMA (128-byte swizzle) as the B operand. The
 //    epilogue scales by norm_k * scale, and per 32-position chunk writes the
 //    head maxima c, the sums sum exp(s - c) and e = exp(s - c) * norm_v (f16).
 //  * tc_softmax_kernel — per (token, head): the global max M over the chunks,
 //    l = sum_c csum_c exp(c - M), 1 / l, and e *= exp(c - M) in place, so the
 //    values kernel can load e by TMA as an operand.
-//  * tc_values_kernel — CTA = (256 dims, token). D[128 dims x NHP heads] +=
+//  * tc_values_kernel — CTA = (128 dims, token). D[128 dims x NHP heads] +=
 //    A[dims x 16 positions] B[16 positions x heads] with A = the decoded value
 //    rows in shared memory as an MN-major operand (rows = positions, 64 dims
 //    per 128-byte swizzled row: the decode writes rows exactly as the codes
 //    lie) and B = e rows by TMA. The epilogue writes u~ = D / l as f16 hi / lo.
-// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (one
-// thread), warps 2..9 decoders and epilogue. Every mbarrier wait is bounded:
+// Warp roles: warp 0 TMA producer, warp 1 MMA issuer (one thread), the rest
+// (16 warps in the scores kernel, 8 in the values kernel) decoders and
+// epilogue; two CTAs per SM for both. Every mbarrier wait is bounded:
 // on expiry the CTA raises its abort flag, KG_ERR_TIMEOUT goes to the error
 // word, every warp still passes the barriers it owes and the tensor memory is
 // released.
@@ -46,7 +47,8 @@ namespace kg {
 namespace attn {
 namespace {
 
-constexpr int TCW = 320;        // threads per CTA (10 warps)
+constexpr int SCW = 576;        // scores threads per CTA: TMA, MMA and 16 decoder warps
+constexpr int TCW = 320;        // values threads per CTA: TMA, MMA and 8 decoder warps
 constexpr int LUTW = 256 * 32;  // words of the replicated code-byte -> centroid-pair table
 constexpr uint32_t FULLM = 0xffffffffu;
 
@@ -62,12 +64,12 @@ constexpr int S_TCOLS = 256;                         // acc (2 x 32) + A (3 stag
 // values
 constexpr int V_STG = 3;
 constexpr int V_KB = 64;                             // positions per K block
-constexpr int V_DG = 256;                            // dims per CTA (128 code bytes per row)
-constexpr int V_CODE = V_KB * (V_DG / 2);            // 8 KB
+constexpr int V_DG = 128;                            // dims per CTA (64 code bytes per row)
+constexpr int V_CODE = V_KB * (V_DG / 2);            // 4 KB
 constexpr int V_E = 32 * 128;                        // e block: up to 32 heads x 64 positions (f16)
-constexpr int V_STAGE = V_CODE + V_E;                // 12 KB
+constexpr int V_STAGE = V_CODE + V_E;                // 8 KB
 constexpr int V_ATOM = V_KB * 128;                   // one 64-dim atom of A: 64 rows x 128 B
-constexpr int V_A = 4 * V_ATOM;                      // 32 KB
+constexpr int V_A = 2 * V_ATOM;                      // 16 KB: the 128 dims (M) of one accumulator
 
 struct ScoreMaps {
     CUtensorMap codes, q;
@@ -108,7 +110,7 @@ __device__ __forceinline__ bool wait_all(uint64_t *b, uint32_t parity, volatile 
 
 // ---------------------------------------------------------------------------
 template <int NHP>
-__global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant__ ScoreMaps maps, const TqAttnArgs a) {
+__global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant__ ScoreMaps maps, const TqAttnArgs a) {
     extern __shared__ __align__(1024) uint8_t dsm_raw[];
     uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
     uint8_t *stages = dsm;
@@ -124,7 +126,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int s = 0; s < S_STG; ++s) {
             as::mbar_init(&full[s], 1);
-            as::mbar_init(&afull[s], 8);
+            as::mbar_init(&afull[s], 16);
             as::mbar_init(&empty[s], 1);
         }
         as::mbar_init(accfull, 1);
@@ -180,8 +182,9 @@ __global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant
                 tc::commit(accfull);
             }
         } else {
-            // decoders: warp w handles tile (w - 2) / 4, TMEM lanes 32 (w % 4) .. +31
-            const int p = (warp - 2) >> 2, quad = warp & 3, r = quad * 32 + lane;
+            // decoders: warp w handles tile (w - 2) / 8, column half ((w - 2) / 4) % 2 of
+            // each K block (16 of its 32 code bytes), TMEM lanes 32 (w % 4) .. +31
+            const int p = (warp - 2) >> 3, half = ((warp - 2) >> 2) & 1, quad = warp & 3, r = quad * 32 + lane;
             const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
             const uint32_t lutl = as::sa(lut) + 4 * lane;
             bool ok = true;
@@ -192,16 +195,15 @@ __global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant
                 if (!ok) break;
                 tc::fence_after();
                 if (p < ntile) {
-                    const uint8_t *row = stages + s * S_STAGE + p * S_TILE * 32 + r * 32;
+                    const uint8_t *row = stages + s * S_STAGE + p * S_TILE * 32 + r * 32 + 16 * half;
                     const uint4 c0 = *reinterpret_cast<const uint4 *>(row);
-                    const uint4 c1 = *reinterpret_cast<const uint4 *>(row + 16);
-                    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    uint32_t v[32];
+                    const uint32_t w[4] = {c0.x, c0.y, c0.z, c0.w};
+                    uint32_t v[16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
+                    for (int i = 0; i < 4; ++i)
 #pragma unroll
                         for (int k = 0; k < 4; ++k) v[4 * i + k] = lk(lutl, w[i], k);
-                    tc::st32(tbase + lane_off + a_col + (2 * s + p) * 32, v);
+                    tc::st16(tbase + lane_off + a_col + (2 * s + p) * 32 + 16 * half, v);
                     tc::st_wait();
                 }
                 tc::fence_before();
@@ -211,21 +213,17 @@ __global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant
             // epilogue: scaled scores of this lane's position into the transpose buffer
             if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
             tc::fence_after();
-            if (ok && p < ntile) {
-                float v[NHP];
-                if constexpr (NHP == 32) {
-                    tc::ld32f(tbase + lane_off + acc_col + p * 32, v);
-                } else {
-                    tc::ld16f(tbase + lane_off + acc_col + p * 32, v);
-                }
+            if (ok && p < ntile && 16 * half < NHP) {  // heads 16 half .. +15 of this lane's position
+                float v[16];
+                tc::ld16f(tbase + lane_off + acc_col + p * 32 + 16 * half, v);
                 const int pos = p0 + p * S_TILE + r;
                 const bool valid = pos < tn;
                 const float kn = valid ? __ldg(a.knorm + rbase + pos) * a.scale : 0.0f;
-                float *col = sT + (p * NHP) * 4 * S_CH + (r >> 5) * S_CH + (r & 31);
+                float *col = sT + (p * NHP + 16 * half) * 4 * S_CH + (r >> 5) * S_CH + (r & 31);
 #pragma unroll
-                for (int h = 0; h < NHP; ++h) col[h * 4 * S_CH] = valid ? v[h] * kn : -INFINITY;
+                for (int h = 0; h < 16; ++h) col[h * 4 * S_CH] = valid ? v[h] * kn : -INFINITY;
             }
-            bar_named(1, 256);
+            bar_named(1, 512);
             // per (tile, head, 32-position chunk): max, sum of exp, e = exp(s - max) * norm_v (f16)
             const int t = threadIdx.x - 64;
             const int pt = t / (NHP * 4), h = (t / 4) % NHP, c = t & 3;
@@ -236,21 +234,23 @@ __global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant
 #pragma unroll
                 for (int i = 0; i < 32; ++i) mx = fmaxf(mx, row[i]);
                 float sum = 0.0f;
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float s0 = row[i], s1 = row[i + 1];
-                    const float e0 = s0 == -INFINITY ? 0.0f : __expf(s0 - mx);
-                    const float e1 = s1 == -INFINITY ? 0.0f : __expf(s1 - mx);
-                    sum += e0;
-                    sum += e1;
-                    const float vn0 = e0 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i) : 0.0f;
-                    const float vn1 = e1 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i + 1) : 0.0f;
-                    pk[i >> 1] = h2u(e0 * vn0, e1 * vn1);
-                }
                 uint4 *dst = reinterpret_cast<uint4 *>(a.E + ((int64_t)m * a.nh + h) * a.Sp + q0);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                for (int j = 0; j < 4; ++j) {  // 8 positions -> one 16-byte store
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int i = 8 * j; i < 8 * j + 8; i += 2) {
+                        const float s0 = row[i], s1 = row[i + 1];
+                        const float e0 = s0 == -INFINITY ? 0.0f : __expf(s0 - mx);
+                        const float e1 = s1 == -INFINITY ? 0.0f : __expf(s1 - mx);
+                        sum += e0;
+                        sum += e1;
+                        const float vn0 = e0 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i) : 0.0f;
+                        const float vn1 = e1 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i + 1) : 0.0f;
+                        pk[(i >> 1) & 3] = h2u(e0 * vn0, e1 * vn1);
+                    }
+                    dst[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
                 const int64_t ci = ((int64_t)m * a.nc32 + (q0 >> 5)) * a.nh + h;
                 a.cmax[ci] = mx;
                 a.csum[ci] = sum;
@@ -264,6 +264,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_scores_kernel(const __grid_constant
         tc::dealloc(tbase, S_TCOLS);
     }
 }
+
 
 // ---------------------------------------------------------------------------
 // per (head, token): global max, denominator, e rescaled in place
@@ -309,17 +310,17 @@ __global__ void __launch_bounds__(128) tc_softmax_kernel(const TqAttnArgs a) {
 
 // ---------------------------------------------------------------------------
 template <int NHP>
-__global__ void __launch_bounds__(TCW, 1) tc_values_kernel(const __grid_constant__ ValueMaps maps, const TqAttnArgs a) {
+__global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant__ ValueMaps maps, const TqAttnArgs a) {
     extern __shared__ __align__(1024) uint8_t dsm_raw[];
     uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
     uint8_t *stages = dsm;
-    uint8_t *abuf = dsm + V_STG * V_STAGE;  // [2][4 atoms][64 rows][128 B]
+    uint8_t *abuf = dsm + V_STG * V_STAGE;  // [2 buffers][2 atoms][64 rows][128 B]
     uint32_t *lut = reinterpret_cast<uint32_t *>(abuf + 2 * V_A);
     uint64_t *full = reinterpret_cast<uint64_t *>(lut + LUTW);
     uint64_t *empty = full + V_STG, *afull = empty + V_STG, *aempty = afull + 2, *accfull = aempty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
-    constexpr uint32_t TCOLS = 2 * NHP < 32 ? 32 : 2 * NHP;
+    constexpr uint32_t TCOLS = 32;  // one NHP-column accumulator
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     lut_build(lut, a.vcent);
@@ -370,11 +371,9 @@ __global__ void __launch_bounds__(TCW, 1) tc_values_kernel(const __grid_constant
                 const uint64_t ed = tc::sdesc_k(stages + s * V_STAGE + V_CODE);
                 const uint32_t a0 = as::sa(abuf + ab * V_A);
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        tc::mma_ss(tbase + hh * NHP, tc::sdesc_sw128(a0 + hh * 2 * V_ATOM + k * 2048, V_ATOM, 1024),
-                                   ed + (uint64_t)(2 * k), ID, (kb | k) != 0);
+                for (int k = 0; k < 4; ++k)
+                    tc::mma_ss(tbase, tc::sdesc_sw128(a0 + k * 2048, V_ATOM, 1024), ed + (uint64_t)(2 * k), ID,
+                               (kb | k) != 0);
                 tc::commit(&empty[s]);
                 tc::commit(&aempty[ab]);
             }
@@ -392,10 +391,10 @@ __global__ void __launch_bounds__(TCW, 1) tc_values_kernel(const __grid_constant
             if (!ok) break;
             const uint8_t *codes = stages + s * V_STAGE;
             uint8_t *A = abuf + ab * V_A;
-#pragma unroll 2
-            for (int c = t; c < V_KB * 32; c += 256) {
-                const int r = c >> 5, w = c & 31, da = w >> 3, j = w & 7;
-                const uint32_t cw = *reinterpret_cast<const uint32_t *>(codes + r * 128 + 4 * w);
+#pragma unroll
+            for (int c = t; c < V_KB * 16; c += 256) {  // 64 rows x 16 words (8 dims each)
+                const int r = c >> 4, w = c & 15, da = w >> 3, j = w & 7;
+                const uint32_t cw = *reinterpret_cast<const uint32_t *>(codes + r * 64 + 4 * w);
                 const uint4 o = make_uint4(lk(lutl, cw, 0), lk(lutl, cw, 1), lk(lutl, cw, 2), lk(lutl, cw, 3));
                 *reinterpret_cast<uint4 *>(A + da * V_ATOM + r * 128 + ((j ^ (r & 7)) << 4)) = o;
             }
@@ -406,19 +405,19 @@ __global__ void __launch_bounds__(TCW, 1) tc_values_kernel(const __grid_constant
                 as::mbar_arrive(&empty[s]);
             }
         }
-        // epilogue: warp w reads accumulator (w - 2) / 4 (dims 128 of them), TMEM lanes 32 (w % 4) ..
+        // epilogue: warps 2..5 read the accumulator, TMEM lanes 32 (w % 4) .. (dims)
         if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
         tc::fence_after();
-        if (ok) {
-            const int hh = (warp - 2) >> 2, quad = warp & 3;
+        if (ok && warp < 6) {
+            const int quad = warp & 3;
             float v[NHP];
-            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + hh * NHP;
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16);
             if constexpr (NHP == 32) {
                 tc::ld32f(taddr, v);
             } else {
                 tc::ld16f(taddr, v);
             }
-            const int d = g * V_DG + hh * 128 + quad * 32 + lane;
+            const int d = g * V_DG + quad * 32 + lane;
 #pragma unroll
             for (int h = 0; h < NHP; ++h) {
                 if (h < a.nh) {
@@ -456,7 +455,7 @@ cudaError_t launch_tc(const TqAttnArgs &a, cudaStream_t s) {
     cudaError_t e = dev::smem(tc_scores_kernel<NHP>, ssm);
     if (e == cudaSuccess) e = dev::smem(tc_values_kernel<NHP>, vsm);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(tc_scores_kernel<NHP>, dim3((a.Sp + 2 * S_TILE - 1) / (2 * S_TILE), a.M), dim3(TCW), ssm, s, sm, a);
+    e = launch_pdl(tc_scores_kernel<NHP>, dim3((a.Sp + 2 * S_TILE - 1) / (2 * S_TILE), a.M), dim3(SCW), ssm, s, sm, a);
     if (e == cudaSuccess) e = launch_pdl(tc_softmax_kernel, dim3(a.nh, a.M), dim3(128), 0, s, a);
     if (e == cudaSuccess)
         e = launch_pdl(tc_values_kernel<NHP>, dim3(a.kvd / V_DG, a.M), dim3(TCW), vsm, s, vm, a);

@@ -98,6 +98,8 @@ def lib():
             "kg_sample_dev": (ctypes.c_int, [P, I32, P, P, I64, P, P]),
             "kg_sample": (ctypes.c_int, [P, I32, P, P, P]),
             "kg_verify_dev": (ctypes.c_int, [P, I32, P, P, P, P, I32, P, P, P, P]),
+            "kg_forward_prefill": (ctypes.c_int, [P, I32, P, P, I32, P]),
+            "kg_forward_prefill_dev": (ctypes.c_int, [P, I32, P, P, I32, P, P]),
             "kg_verify": (ctypes.c_int, [P, I32, P, P, P, P, I32, P, P, P]),
             "kg_comm_unique_id": (ctypes.c_int, [P]),
             "kg_comm_init": (ctypes.c_int, [P, P, I32, I32]),
@@ -236,6 +238,16 @@ class CudaBackend:
             return lo, pr
         return lo if logits else pr
 
+    def forward_prefill(self, tokens, seq_ids=None):
+        """forward_prefill (bidirectional) over each row of tokens from position 0:
+        the last position's logits [n_seq][vocab]."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        n_seq, T = tokens.shape
+        ids = np.arange(n_seq, dtype=np.int32) if seq_ids is None else np.ascontiguousarray(seq_ids, np.int32)
+        out = np.empty((n_seq, self.cfg.vocab_size), np.float32)
+        self._check(lib().kg_forward_prefill(self._h, n_seq, _ptr(ids), _ptr(tokens), T, _ptr(out)))
+        return out
+
     def forward_batch_dev(self, n_seq, T, ids_ptr, tok_ptr, pos_ptr, logits_ptr, probs_ptr, stream_ptr):
         """Device-pointer form (integers are raw device addresses)."""
         self._check(lib().kg_forward_batch_dev(self._h, n_seq, ids_ptr, tok_ptr, pos_ptr, T,
@@ -268,6 +280,15 @@ class CudaBackend:
         nr = np.empty(2, np.float32)
         self._check(lib().kg_kv_codes(self._h, seq, layer, pos, _ptr(kp), _ptr(vp), _ptr(nr)))
         return kp, vp, nr
+
+    def kv_codes_all(self, seq, T):
+        """Every stored code of one sequence, positions 0..T-1: [n_layer][T][kpl + vpl] (K then V)."""
+        rows = []
+        for layer in range(self.cfg.n_layer):
+            for pos in range(T):
+                kp, vp, _ = self.kv_codes(seq, layer, pos)
+                rows.append(np.concatenate([kp, vp]))
+        return np.stack(rows).reshape(self.cfg.n_layer, T, -1)
 
     def profile(self, enable=True):
         self._check(lib().kg_profile(self._h, 1 if enable else 0))

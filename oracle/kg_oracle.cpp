@@ -838,6 +838,10 @@ struct Seq {
     // ([L][rot_T][2][kvd]; untouched for zero-norm vectors), for parity tests
     float *rot_out = nullptr;
     int64_t rot_T = 0;
+    // codes imposed on every store ([L][force_T][kpl + vpl], K then V): the
+    // quantization decisions of another implementation, replayed
+    const uint8_t *force = nullptr;
+    int64_t force_T = 0;
     void store_kv(int64_t l, int64_t pos) {
         int64_t at = l * d.B + pos;
         tq_store(tq->rot.data(), tq->kb.data(), kbits, d.kvd, k.data(), &kcodes[at * kpl],
@@ -846,6 +850,11 @@ struct Seq {
         tq_store(tq->rot.data(), tq->vb.data(), vbits, d.kvd, v.data(), &vcodes[at * vpl],
                  &vnorm[at], sn.data(), sr.data(), si.data());
         if (rot_out) std::memcpy(rot_out + ((l * rot_T + pos) * 2 + 1) * d.kvd, sr.data(), d.kvd * 4);
+        if (force) {  // the norms stay this store's own
+            const uint8_t *f = force + (l * force_T + pos) * (kpl + vpl);
+            std::memcpy(&kcodes[at * kpl], f, kpl);
+            std::memcpy(&vcodes[at * vpl], f + kpl, vpl);
+        }
     }
     void deq_key(int64_t l, int64_t t, float *out) {
         int64_t at = l * d.B + t;
@@ -906,6 +915,54 @@ struct Seq {
             delta_route(l);
         }
         matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
+    }
+
+    // transformer.rs:2606-3004 (forward_prefill, default features, lora None):
+    // per layer, phase A over every prompt position (double rmsnorm, K/V into
+    // the f32 cache, Q and the residual kept), then phase B over every
+    // position: attention over ALL prompt positions (bidirectional), Wo +
+    // residual, MLP with the TwELL switch, delta routing with the context's
+    // block deltas accumulating across positions. Returns the last position's
+    // hidden state in x; the caller computes lm_head.
+    void forward_prefill(const int32_t *toks, int64_t P) {
+        std::vector<float> hidden(P * d.n), queries(P * d.n), residuals(P * d.n);
+        if (d.L > 1)
+            for (int64_t p = 0; p < P; ++p)
+                add_into(&hidden[p * d.n], W->wte + (int64_t)toks[p] * d.n, W->wpe + p * d.n, d.n);
+        const float scale = 1.0f / sqrtf((float)d.hd);
+        for (int64_t l = 0; l < d.L; ++l) {
+            const LayerW &lw = W->layers[l];
+            float *K = &Kc[l * d.B * d.kvd], *Vv = &Vc[l * d.B * d.kvd];
+            for (int64_t p = 0; p < P; ++p) {  // phase A (:2657-2757)
+                if (d.L > 1) std::memcpy(x.data(), &hidden[p * d.n], d.n * 4);
+                else add_into(x.data(), W->wte + (int64_t)toks[p] * d.n, W->wpe + p * d.n, d.n);
+                rmsnorm(x.data(), d.n);
+                xr = x;
+                rmsnorm(x.data(), d.n);
+                matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+                matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+                std::memcpy(K + p * d.kvd, k.data(), d.kvd * 4);
+                std::memcpy(Vv + p * d.kvd, v.data(), d.kvd * 4);
+                matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+                std::memcpy(&queries[p * d.n], q.data(), d.n * 4);
+                std::memcpy(&residuals[p * d.n], xr.data(), d.n * 4);
+            }
+            for (int64_t p = 0; p < P; ++p) {  // phase B (:2797-2987)
+                std::memcpy(xr.data(), &residuals[p * d.n], d.n * 4);
+                std::fill(att.begin(), att.end(), 0.0f);
+                std::memcpy(q.data(), &queries[p * d.n], d.n * 4);
+                for (int64_t h = 0; h < d.nh; ++h) {
+                    int64_t g = h * d.nkv / d.nh;
+                    attention_head(q.data(), K, Vv, att.data(), scores.data(), h * d.hd, g * d.hd, d.kvd, d.hd, P,
+                                   scale);
+                }
+                matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+                add_inplace(x.data(), xr.data(), d.n);
+                mlp(lw, false, nullptr);
+                delta_route(l);
+                if (d.L > 1) std::memcpy(&hidden[p * d.n], x.data(), d.n * 4);
+            }
+        }
     }
 
     // transformer.rs:4042-4233 (forward_quantized<TurboQuantKVCache>)
@@ -1287,6 +1344,43 @@ int or_run_sequence(const or_config *c, int mode, int kb, int vb, const float *w
     // mode 3: forward_quantized with the reference's single shared flat buffer
     return run_one(c, mode, kb, vb, W, d, tokens, T, logits, 0, codes, norms, utilities, mode == 3,
                    s);
+}
+
+// forward_prefill over prompt[0..P) (src/transformer.rs:2606-3004), then
+// forward_base of cont[0..n_cont) at positions P.. over the prefill's cache
+// (the decode half of generate_with_prefill, :3010-3106). logits_out rows:
+// the prefill's last position, then one per continuation token.
+int or_run_sequence_forced(const or_config *c, int key_bits, int val_bits, const float *weights,
+                           const int32_t *tokens, int32_t T, const uint8_t *codes_in, float *logits) {
+    if (check_cfg(c, T) || !codes_in) return -1;
+    Dims d = dims_of(c);
+    Weights W = view_weights(d, weights);
+    Seq s;
+    s.force = codes_in;
+    s.force_T = T;
+    return run_one(c, OR_MODE_QUANT, key_bits, val_bits, W, d, tokens, T, logits, 0, nullptr, nullptr, nullptr, false,
+                   s);
+}
+
+int or_prefill_then_decode(const or_config *c, const float *weights, const int32_t *prompt, int32_t P,
+                           const int32_t *cont, int32_t n_cont, float *logits_out) {
+    if (check_cfg(c, P + n_cont) || P < 1 || n_cont < 0) return -1;
+    Dims d = dims_of(c);
+    Weights W = view_weights(d, weights);
+    for (int32_t i = 0; i < P; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d.V) return -2;
+    for (int32_t i = 0; i < n_cont; ++i)
+        if (cont[i] < 0 || cont[i] >= d.V) return -2;
+    Seq s;
+    s.init(d, &W, OR_MODE_BASE, 4, 4);
+    s.sparse_threshold = c->sparse_threshold;
+    s.forward_prefill(prompt, P);
+    matmul(logits_out, W.lm_head, s.x.data(), d.V, d.n);  // matmul_parallel: the same row dots
+    for (int32_t i = 0; i < n_cont; ++i) {
+        s.forward_base(cont[i], P + i);
+        std::memcpy(logits_out + (int64_t)(i + 1) * d.V, s.logits.data(), d.V * 4);
+    }
+    return 0;
 }
 
 int or_run_sequence_rot(const or_config *c, int mode, int kb, int vb, const float *weights, const int32_t *tokens,

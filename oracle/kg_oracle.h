@@ -121,6 +121,23 @@ int or_run_sequence_rot(const or_config *c, int mode, int key_bits, int val_bits
                         const int32_t *tokens, int32_t T, float *logits, uint8_t *codes, float *norms,
                         float *rot_out);
 
+/* forward_quantized with the K/V codes imposed: every TurboQuant store keeps
+ * its own norm but takes its codes from codes_in[L][T][kpl + vpl] (K then V,
+ * the layout `codes` has above). Replays another implementation's
+ * quantization decisions, so the continuous arithmetic of the two can be
+ * compared where a rounding difference next to a codebook boundary would
+ * otherwise pick a different code. */
+int or_run_sequence_forced(const or_config *c, int key_bits, int val_bits, const float *weights,
+                           const int32_t *tokens, int32_t T, const uint8_t *codes_in, float *logits);
+
+/* forward_prefill (src/transformer.rs:2606-3004: bidirectional attention over
+ * the prompt, double rmsnorm, delta-routing state across positions) over
+ * prompt[0..P), then forward_base of cont[0..n_cont) at positions P.. on the
+ * prefill's f32 cache. logits_out [1 + n_cont][V]: the prefill's (last
+ * position) logits, then each continuation token's. */
+int or_prefill_then_decode(const or_config *c, const float *weights, const int32_t *prompt, int32_t P,
+                           const int32_t *cont, int32_t n_cont, float *logits_out);
+
 /* Multi-sequence runner: n_seq sequences of T tokens each (row-major),
  * spread over n_threads std::threads (one per core, as the reference's rayon
  * generate_batch). logits may be NULL (discarded) for timing runs. */

@@ -76,6 +76,8 @@ def lib():
             "or_run_sequence": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, P, P, P, P]),
             "or_run_batch": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, P, ctypes.c_int]),
             "or_run_sequence_rot": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, P, P, P, P]),
+            "or_prefill_then_decode": (ctypes.c_int, [cp, P, P, I32, P, I32, P]),
+            "or_run_sequence_forced": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, P, P, I32, P, P]),
             "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
             "or_time_decode": (ctypes.c_double, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, I32, I32, ctypes.c_int]),
         }
@@ -311,6 +313,37 @@ def run_sequence_rot(cfg, mode, w, tokens, key_bits=3, val_bits=3):
     if rc:
         raise RuntimeError(f"or_run_sequence_rot failed: {rc}")
     return logits, codes, norms, rot
+
+
+def run_sequence_forced(cfg, w, tokens, codes, key_bits=3, val_bits=3):
+    """forward_quantized of one sequence with every store's codes taken from
+    codes[L][T][kpl + vpl] (norms computed as usual): logits [T][V]."""
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    T = tokens.size
+    kvd = cfg.n_kv_head * cfg.head_dim
+    pl = packed_len(kvd, key_bits) + packed_len(kvd, val_bits)
+    codes = np.ascontiguousarray(codes, np.uint8)
+    if codes.shape != (cfg.n_layer, T, pl):
+        raise ValueError(f"codes shape {codes.shape}, expected {(cfg.n_layer, T, pl)}")
+    logits = np.empty((T, cfg.vocab_size), np.float32)
+    rc = lib().or_run_sequence_forced(ctypes.byref(cfg), key_bits, val_bits, _p(f32(w)), _p(tokens), T, _p(codes),
+                                      _p(logits))
+    if rc:
+        raise RuntimeError(f"or_run_sequence_forced failed: {rc}")
+    return logits
+
+
+def prefill_then_decode(cfg, w, prompt, cont=()):
+    """forward_prefill of the prompt then forward_base of the continuation:
+    logits [1 + len(cont)][V] (the prefill's last position first)."""
+    prompt = np.ascontiguousarray(prompt, np.int32)
+    cont = np.ascontiguousarray(cont, np.int32)
+    out = np.empty((1 + cont.size, cfg.vocab_size), np.float32)
+    rc = lib().or_prefill_then_decode(ctypes.byref(cfg), _p(f32(w)), _p(prompt), prompt.size,
+                                      _p(cont) if cont.size else None, cont.size, _p(out))
+    if rc:
+        raise RuntimeError(f"or_prefill_then_decode failed: {rc}")
+    return out
 
 
 def run_batch(cfg, mode, w, tokens, key_bits=3, val_bits=3, threads=None, keep_logits=True, t0=0):

@@ -4,7 +4,11 @@ mlp 16384, vocab 32000 in the benchmark, 4-bit TurboQuant KV).
 The oracle runs forward_quantized in f32 on the same bf16-rounded weights
 (src/transformer.rs:4042-4233). Two layers keep the oracle to about a minute;
 every layer runs the same kernels, so depth adds no kernel shape. Bar (north
-star): logits within 2e-2 relative, per position max|gpu - ref| / max|ref|.
+star): logits within 2e-2 relative, per position max|gpu - ref| / max|ref|,
+at every position against the oracle replaying the device's K/V codes (the
+forced_oracle fixture) and from position 64 on against the oracle's own
+codes (where few positions are attended one code flipped next to a codebook
+boundary weighs too much for a fixed bar).
 Weights ~N(0, 0.02), the distribution the benchmark draws.
 """
 import numpy as np
@@ -21,7 +25,7 @@ def rel_err(a, b):
     return np.abs(a - b).max(axis=-1) / den
 
 
-def test_c5_widths_prefill_then_decode_match_oracle(kg, orc):
+def test_c5_widths_prefill_then_decode_match_oracle(kg, orc, forced_oracle):
     # 2 sequences: a 256-token prefill (512 rows: the tcgen05 GEMMs, the
     # tensor-core encoder with exact fix-up, flash attention over dequantized
     # rows), then single-token decode steps to position 299 (rotated-domain
@@ -37,8 +41,13 @@ def test_c5_widths_prefill_then_decode_match_oracle(kg, orc):
     dec = np.stack([be.forward_batch(toks[:, t:t + 1], start_pos=np.full(2, t))[:, 0] for t in range(T0, T)], axis=1)
     got = np.concatenate([pre, dec], axis=1)
     ref = orc.run_batch(orc.from_kg(cfg), orc.MODE_QUANT, w, toks, key_bits=4, val_bits=4, threads=2)
+    forced = forced_oracle(be, cfg, w, toks, 4, 4)
     for i in range(2):
         err = rel_err(got[i], ref[i])
-        print("c5 widths seq %d: max rel err prefill %.2e decode %.2e" % (i, err[:T0].max(), err[T0:].max()))
-        assert err.max() <= REL_BF16, (i, int(np.argmax(err)), float(err.max()))
+        errf = rel_err(got[i], forced[i])
+        print("c5 widths seq %d: replayed codes: max rel err prefill %.2e decode %.2e | own codes: prefill %.2e "
+              "(positions 0..63), %.2e (64..), decode %.2e" %
+              (i, errf[:T0].max(), errf[T0:].max(), err[:64].max(), err[64:T0].max(), err[T0:].max()))
+        assert errf.max() <= REL_BF16, (i, int(np.argmax(errf)))
+        assert err[64:].max() <= REL_BF16
     be.close()

@@ -1,7 +1,12 @@
 """GPU parity at the benchmark configurations' own shapes (bf16 path).
 
 The oracle runs the reference forward in f32 on the same bf16-rounded
-weights. Bars (north star): logits within 2e-2 relative per position;
+weights. Bars (north star): logits within 2e-2 relative per position; for the
+quantized forward at every position against the oracle replaying the
+device's codes (the forced_oracle fixture), and from position 64 on also
+against the oracle's own codes (before that a single code flipped next to a
+boundary weighs too much: a 1e-5 relative perturbation of the weights moves
+the oracle's own logits by up to 2.8e-2 there);
 TurboQuant codes bit-exact on equal inputs (tested in test_gpu_micro.py and
 test_zz_no_alloc.py). End to end the K/V rows a device layer produces differ
 from the reference's in the last bits (different GEMM summation order), so a
@@ -29,7 +34,7 @@ def _prefill_decode(be, toks, T0):
     return np.concatenate([pre, np.stack(dec, axis=1)], axis=1) if dec else pre
 
 
-def test_c3_full_depth(kg, orc):
+def test_c3_full_depth(kg, orc, forced_oracle):
     # n_layer 12, n_embd 768, 12 heads, mlp 3072, vocab 32000, 4-bit KV:
     # 2 sequences, 1024-token prefill then 8 decode steps
     cfg = kg.micro_config(vocab_size=32000, block_size=1040, n_embd=768, n_head=12, head_dim=64, n_kv_head=12,
@@ -41,10 +46,15 @@ def test_c3_full_depth(kg, orc):
     toks = np.random.default_rng(301).integers(0, 32000, size=(2, 1032)).astype(np.int32)
     got = _prefill_decode(be, toks, 1024)
     ref = orc.run_batch(orc.from_kg(cfg), orc.MODE_QUANT, w, toks, key_bits=4, val_bits=4, threads=2)
+    forced = forced_oracle(be, cfg, w, toks, 4, 4)
     for i in range(2):
         err = rel_err(got[i], ref[i])
-        print("c3 full depth seq %d: max rel err prefill %.2e decode %.2e" % (i, err[:1024].max(), err[1024:].max()))
-        assert err.max() <= REL_BF16
+        errf = rel_err(got[i], forced[i])
+        print("c3 full depth seq %d: replayed codes: max rel err prefill %.2e decode %.2e | own codes: prefill "
+              "%.2e (positions 0..63), %.2e (64..1023), decode %.2e" %
+              (i, errf[:1024].max(), errf[1024:].max(), err[:64].max(), err[64:1024].max(), err[1024:].max()))
+        assert errf.max() <= REL_BF16
+        assert err[64:].max() <= REL_BF16
     be.close()
 
 

@@ -281,3 +281,19 @@ def test_batch_runner_matches_sequence_runner(orc):
         batch = orc.run_batch(cfg, mode, w, toks, threads=3)
         for i in range(6):
             assert np.array_equal(batch[i], orc.run_sequence(cfg, mode, w, toks[i])[0])
+
+
+def test_forced_codes_replay(orc):
+    # the replay entry behind the GPU parity at the configurations' shapes:
+    # the oracle's own codes reproduce its logits bit for bit, and one changed
+    # code byte (layer 0, position 5) changes nothing before position 5
+    cfg = orc.config()
+    w = orc.weights(cfg, 42)
+    toks = np.random.default_rng(8).integers(1, 27, size=16).astype(np.int32)
+    lo, codes, _, _ = orc.run_sequence_rot(cfg, orc.MODE_QUANT, w, toks, key_bits=3, val_bits=3)
+    assert np.array_equal(orc.run_sequence_forced(cfg, w, toks, codes, 3, 3), lo)
+    c2 = codes.copy()
+    c2[0, 5, 0] ^= 0x07
+    lf = orc.run_sequence_forced(cfg, w, toks, c2, 3, 3)
+    assert np.array_equal(lf[:5], lo[:5])
+    assert not np.array_equal(lf[5], lo[5])
