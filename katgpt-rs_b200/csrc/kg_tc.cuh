@@ -105,6 +105,12 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
         "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+// store 8 consecutive 32-bit columns of this thread's lane (warp-wide, 32x32b shape)
+__device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
 // store 16 consecutive 32-bit columns of this thread's lane (warp-wide, 32x32b shape)
 __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
@@ -113,6 +119,14 @@ __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+// store a 16-lane x 8-column block (warp-wide, 16x256b shape, lanes from the
+// lane field of taddr): thread t writes r0, r1 to lane + t/4 and r2, r3 to
+// lane + t/4 + 8, at columns col + 2 (t % 4) and col + 2 (t % 4) + 1
+__device__ __forceinline__ void st16x256(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
 }
 __device__ __forceinline__ void st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 

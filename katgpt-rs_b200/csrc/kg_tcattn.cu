@@ -20,13 +20,16 @@
 //    l = sum_c csum_c exp(c - M), 1 / l, and e *= exp(c - M) in place, so the
 //    values kernel can load e by TMA as an operand.
 //  * tc_values_kernel — CTA = (128 dims, token). D[128 dims x NHP heads] +=
-//    A[dims x 16 positions] B[16 positions x heads] with A = the decoded value
-//    rows in shared memory as an MN-major operand (rows = positions, 64 dims
-//    per 128-byte swizzled row: the decode writes rows exactly as the codes
-//    lie) and B = e rows by TMA. The epilogue writes u~ = D / l as f16 hi / lo.
+//    A[dims x 16 positions] B[16 positions x heads] with A in tensor memory
+//    (lanes = dims, in a fixed permutation the epilogue undoes; columns =
+//    position pairs): a decoder thread gathers one code byte of four
+//    consecutive rows, and each nibble pair of consecutive positions indexes
+//    the same byte -> f16 pair table, stored with tcgen05.st 16x256b. B = e
+//    rows by TMA. The epilogue writes u~ = D / l as f16 hi / lo.
 // Warp roles: warp 0 TMA producer, warp 1 MMA issuer (one thread), the rest
 // (16 warps in the scores kernel, 8 in the values kernel) decoders and
-// epilogue; two CTAs per SM for both. Every mbarrier wait is bounded:
+// epilogue; two CTAs per SM for both. Shared-memory stages (TMA) and tensor-
+// memory A buffers (decoders) run as separate rings. Every mbarrier wait is bounded:
 // on expiry the CTA raises its abort flag, KG_ERR_TIMEOUT goes to the error
 // word, every warp still passes the barriers it owes and the tensor memory is
 // released.
@@ -53,23 +56,25 @@ constexpr int LUTW = 256 * 32;  // words of the replicated code-byte -> centroid
 constexpr uint32_t FULLM = 0xffffffffu;
 
 // scores
-constexpr int S_STG = 3;
+constexpr int S_STG = 6;                             // shared-memory stages (codes + q~)
+constexpr int S_AB = 3;                              // A buffers in tensor memory
 constexpr int S_TILE = 128;                          // positions per tile (TMEM lanes)
 constexpr int S_KB = 64;                             // dims per K block: 32 code bytes per row
 constexpr int S_CODE = 2 * S_TILE * 32;              // two tiles of 128 rows x 32 B
 constexpr int S_Q = 32 * 128;                        // q~ block: up to 32 heads x 64 dims (f16)
 constexpr int S_STAGE = S_CODE + S_Q;                // 12 KB
 constexpr int S_CH = 33;                             // padded 32-position chunk in the transpose buffer
-constexpr int S_TCOLS = 256;                         // acc (2 x 32) + A (3 stages x 2 tiles x 32)
+constexpr int S_TCOLS = 256;                         // acc (2 x 32) + A (3 buffers x 2 tiles x 32)
+static_assert(S_STG * S_STAGE >= 2 * 32 * 4 * S_CH * 4, "the transpose buffer reuses the drained stages");
 // values
-constexpr int V_STG = 3;
-constexpr int V_KB = 64;                             // positions per K block
+constexpr int V_STG = 4;
+constexpr int V_AB = 3;                              // A buffers in tensor memory
+constexpr int V_KB = 128;                            // positions per K block (8 MMA K-steps of 16)
 constexpr int V_DG = 128;                            // dims per CTA (64 code bytes per row)
-constexpr int V_CODE = V_KB * (V_DG / 2);            // 4 KB
-constexpr int V_E = 32 * 128;                        // e block: up to 32 heads x 64 positions (f16)
-constexpr int V_STAGE = V_CODE + V_E;                // 8 KB
-constexpr int V_ATOM = V_KB * 128;                   // one 64-dim atom of A: 64 rows x 128 B
-constexpr int V_A = 2 * V_ATOM;                      // 16 KB: the 128 dims (M) of one accumulator
+constexpr int V_CODE = V_KB * (V_DG / 2);            // 8 KB, rows in the 64-byte swizzle
+constexpr int V_E = 2 * 32 * 128;                    // e block: two 64-position atoms of up to 32 heads (f16)
+constexpr int V_STAGE = V_CODE + V_E;                // 16 KB
+constexpr int V_TCOLS = 256;                         // acc (32) + A (3 buffers x 64 columns)
 
 struct ScoreMaps {
     CUtensorMap codes, q;
@@ -114,10 +119,10 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
     extern __shared__ __align__(1024) uint8_t dsm_raw[];
     uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
     uint8_t *stages = dsm;
+    float *sT = reinterpret_cast<float *>(dsm);  // [2 tiles][NHP][4 chunks][33], over the drained stages
     uint32_t *lut = reinterpret_cast<uint32_t *>(dsm + S_STG * S_STAGE);
-    float *sT = reinterpret_cast<float *>(lut + LUTW);  // [2 tiles][NHP][4 chunks][33]
-    uint64_t *full = reinterpret_cast<uint64_t *>(sT + 2 * NHP * 4 * S_CH);
-    uint64_t *afull = full + S_STG, *empty = afull + S_STG, *accfull = empty + S_STG;
+    uint64_t *full = reinterpret_cast<uint64_t *>(lut + LUTW);
+    uint64_t *empty = full + S_STG, *afull = empty + S_STG, *aempty = afull + S_AB, *accfull = aempty + S_AB;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -126,8 +131,11 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int s = 0; s < S_STG; ++s) {
             as::mbar_init(&full[s], 1);
-            as::mbar_init(&afull[s], 16);
-            as::mbar_init(&empty[s], 1);
+            as::mbar_init(&empty[s], 17);  // 16 decoder warps (codes read) + the MMA commit (q~ read)
+        }
+        for (int b = 0; b < S_AB; ++b) {
+            as::mbar_init(&afull[b], 16);
+            as::mbar_init(&aempty[b], 1);
         }
         as::mbar_init(accfull, 1);
         *abort_flag = 0;
@@ -146,7 +154,7 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
     const int ntile = p0 >= tn ? 0 : min(2, (tn - p0 + S_TILE - 1) / S_TILE);  // CTA-uniform
     const int nkb = a.kvd / S_KB;
     const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
-    const uint32_t acc_col = 0, a_col = 64;  // acc of tile p at p * 32; A of (stage s, tile p) at 64 + (2s + p) * 32
+    const uint32_t acc_col = 0, a_col = 64;  // acc of tile p at p * 32; A of (buffer b, tile p) at 64 + (2b + p) * 32
 
     if (ntile > 0) {
         if (warp == 0) {
@@ -166,18 +174,18 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
             if (lane == 0) {  // MMA issuer
                 constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP);
                 for (int kb = 0; kb < nkb; ++kb) {
-                    const int s = kb % S_STG;
-                    const uint32_t ph = (kb / S_STG) & 1;
-                    if (!as::mbar_wait(&full[s], ph, abort_flag, a.err)) break;
-                    if (!as::mbar_wait(&afull[s], ph, abort_flag, a.err)) break;
+                    const int s = kb % S_STG, b = kb % S_AB;
+                    if (!as::mbar_wait(&full[s], (kb / S_STG) & 1, abort_flag, a.err)) break;
+                    if (!as::mbar_wait(&afull[b], (kb / S_AB) & 1, abort_flag, a.err)) break;
                     tc::fence_after();
                     const uint64_t qd = tc::sdesc_k(stages + s * S_STAGE + S_CODE);
                     for (int p = 0; p < ntile; ++p)
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            tc::mma_ts(tbase + acc_col + p * 32, tbase + a_col + (2 * s + p) * 32 + 8 * k,
+                            tc::mma_ts(tbase + acc_col + p * 32, tbase + a_col + (2 * b + p) * 32 + 8 * k,
                                        qd + (uint64_t)(2 * k), ID, (kb | k) != 0);
-                    tc::commit(&empty[s]);  // stage s (codes, q~, A) is free once these MMAs are done
+                    tc::commit(&empty[s]);   // q~ of stage s read
+                    tc::commit(&aempty[b]);  // A buffer b read
                 }
                 tc::commit(accfull);
             }
@@ -189,9 +197,9 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
             const uint32_t lutl = as::sa(lut) + 4 * lane;
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % S_STG;
-                const uint32_t ph = (kb / S_STG) & 1;
-                ok = wait_all(&full[s], ph, abort_flag, a.err) && wait_all(&empty[s], ph ^ 1, abort_flag, a.err);
+                const int s = kb % S_STG, b = kb % S_AB;
+                ok = wait_all(&full[s], (kb / S_STG) & 1, abort_flag, a.err) &&
+                     wait_all(&aempty[b], ((kb / S_AB) & 1) ^ 1, abort_flag, a.err);
                 if (!ok) break;
                 tc::fence_after();
                 if (p < ntile) {
@@ -203,12 +211,15 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
                     for (int i = 0; i < 4; ++i)
 #pragma unroll
                         for (int k = 0; k < 4; ++k) v[4 * i + k] = lk(lutl, w[i], k);
-                    tc::st16(tbase + lane_off + a_col + (2 * s + p) * 32 + 16 * half, v);
+                    tc::st16(tbase + lane_off + a_col + (2 * b + p) * 32 + 16 * half, v);
                     tc::st_wait();
                 }
                 tc::fence_before();
                 __syncwarp();
-                if (lane == 0) as::mbar_arrive(&afull[s]);
+                if (lane == 0) {
+                    as::mbar_arrive(&afull[b]);
+                    as::mbar_arrive(&empty[s]);
+                }
             }
             // epilogue: scaled scores of this lane's position into the transpose buffer
             if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
@@ -309,18 +320,27 @@ __global__ void __launch_bounds__(128) tc_softmax_kernel(const TqAttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// One code byte column over four consecutive positions (byte k of w =
+// position k) into a 16x256b tensor-memory store: its low nibbles go to lane
+// t/4 of the block and its high nibbles to lane t/4 + 8, two positions per
+// column. The table index of a column is (nibble of position 2c) | (nibble of
+// position 2c + 1) << 4: the same byte -> f16 pair table the rows use.
+__device__ __forceinline__ void decode_column(uint32_t w, uint32_t lutl, uint32_t taddr) {
+    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+    const uint32_t il = lo | (lo >> 4), ih = hi | (hi >> 4);  // indices in bytes 0 and 2
+    tc::st16x256(taddr, lk(lutl, il, 0), lk(lutl, il, 2), lk(lutl, ih, 0), lk(lutl, ih, 2));
+}
+
 template <int NHP>
 __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant__ ValueMaps maps, const TqAttnArgs a) {
     extern __shared__ __align__(1024) uint8_t dsm_raw[];
     uint8_t *dsm = dsm_raw + ((1024u - (as::sa(dsm_raw) & 1023u)) & 1023u);
     uint8_t *stages = dsm;
-    uint8_t *abuf = dsm + V_STG * V_STAGE;  // [2 buffers][2 atoms][64 rows][128 B]
-    uint32_t *lut = reinterpret_cast<uint32_t *>(abuf + 2 * V_A);
+    uint32_t *lut = reinterpret_cast<uint32_t *>(dsm + V_STG * V_STAGE);
     uint64_t *full = reinterpret_cast<uint64_t *>(lut + LUTW);
-    uint64_t *empty = full + V_STG, *afull = empty + V_STG, *aempty = afull + 2, *accfull = aempty + 2;
+    uint64_t *empty = full + V_STG, *afull = empty + V_STG, *aempty = afull + V_AB, *accfull = aempty + V_AB;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
-    constexpr uint32_t TCOLS = 32;  // one NHP-column accumulator
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     lut_build(lut, a.vcent);
@@ -329,7 +349,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
             as::mbar_init(&full[s], 1);
             as::mbar_init(&empty[s], 9);  // 8 decoder warps (codes read) + the MMA commit (e read)
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < V_AB; ++b) {
             as::mbar_init(&afull[b], 8);
             as::mbar_init(&aempty[b], 1);
         }
@@ -337,7 +357,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
         *abort_flag = 0;
         as::mbar_fence_init();
     }
-    if (warp == 0) tc::alloc(tslot, TCOLS);
+    if (warp == 0) tc::alloc(tslot, V_TCOLS);
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -348,6 +368,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
     const int tn = a.pos[m] + 1;
     const int nkb = (tn + V_KB - 1) / V_KB;
     const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
+    constexpr uint32_t a_col = 32;  // accumulator at columns 0 .. NHP-1; A buffer b at 32 + 64 b
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
@@ -355,69 +376,84 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
                 const int s = kb % V_STG;
                 if (!as::mbar_wait(&empty[s], ((kb / V_STG) & 1) ^ 1, abort_flag, a.err)) break;
                 uint8_t *st = stages + s * V_STAGE;
-                as::mbar_expect_tx(&full[s], (uint32_t)(V_CODE + NHP * 128));
+                as::mbar_expect_tx(&full[s], (uint32_t)(V_CODE + 2 * NHP * 128));
                 as::tma_load_2d(st, &maps.codes, g * (V_DG / 2), (int)(rbase + kb * V_KB), &full[s]);
                 as::tma_load_2d(st + V_CODE, &maps.e, kb * V_KB, m * a.nh, &full[s]);
+                as::tma_load_2d(st + V_CODE + NHP * 128, &maps.e, kb * V_KB + 64, m * a.nh, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP, /*a_mn=*/1, /*b_mn=*/0);
+            constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP);
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % V_STG, ab = kb & 1;
+                const int s = kb % V_STG, b = kb % V_AB;
                 if (!as::mbar_wait(&full[s], (kb / V_STG) & 1, abort_flag, a.err)) break;
-                if (!as::mbar_wait(&afull[ab], (kb >> 1) & 1, abort_flag, a.err)) break;
+                if (!as::mbar_wait(&afull[b], (kb / V_AB) & 1, abort_flag, a.err)) break;
                 tc::fence_after();
                 const uint64_t ed = tc::sdesc_k(stages + s * V_STAGE + V_CODE);
-                const uint32_t a0 = as::sa(abuf + ab * V_A);
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    tc::mma_ss(tbase, tc::sdesc_sw128(a0 + k * 2048, V_ATOM, 1024), ed + (uint64_t)(2 * k), ID,
-                               (kb | k) != 0);
+                for (int ks = 0; ks < V_KB / 16; ++ks)  // 16 positions: 32 B into one of the two e atoms
+                    tc::mma_ts(tbase, tbase + a_col + b * 64 + 8 * ks,
+                               ed + (uint64_t)((ks >> 2) * (NHP * 128 / 16) + 2 * (ks & 3)), ID, (kb | ks) != 0);
                 tc::commit(&empty[s]);
-                tc::commit(&aempty[ab]);
+                tc::commit(&aempty[b]);
             }
             tc::commit(accfull);
         }
     } else {
-        // decoders: value rows of the K block into the MN-major A buffer
-        const int t = threadIdx.x - 64;
+        // decoders: warp w writes TMEM lanes 32 q .. +31 (q = w % 4: code bytes
+        // 16 q .. 16 q + 15 of each row), K-steps 4 ((w - 2) / 4) .. +3 of each
+        // block. Thread t = 4 j + i takes byte pair 16 q + 2 j, 2 j + 1 of rows
+        // 16 ks + 4 i .. +3 (positions), in an order rotated by i / 2 so that the
+        // four rows one load instruction touches lie in distinct banks of the
+        // 64-byte swizzle; byte 2 j fills lanes j, j + 8 and byte 2 j + 1 lanes
+        // j + 16, j + 24 of the warp's quarter (dims 4 j + 0, 1, 2, 3).
+        const int q = warp & 3, sub = (warp - 2) >> 2, i = lane & 3, j = lane >> 2;
+        const int rot = i >> 1;
+        const uint32_t selA = rot ? 0x4206u : 0x6420u, selB = rot ? 0x5317u : 0x7531u;
         const uint32_t lutl = as::sa(lut) + 4 * lane;
+        const uint32_t lane_off = (uint32_t)(32 * q) << 16;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % V_STG, ab = kb & 1;
+            const int s = kb % V_STG, b = kb % V_AB;
             ok = wait_all(&full[s], (kb / V_STG) & 1, abort_flag, a.err) &&
-                 wait_all(&aempty[ab], ((kb >> 1) & 1) ^ 1, abort_flag, a.err);
+                 wait_all(&aempty[b], ((kb / V_AB) & 1) ^ 1, abort_flag, a.err);
             if (!ok) break;
+            tc::fence_after();
             const uint8_t *codes = stages + s * V_STAGE;
-            uint8_t *A = abuf + ab * V_A;
 #pragma unroll
-            for (int c = t; c < V_KB * 16; c += 256) {  // 64 rows x 16 words (8 dims each)
-                const int r = c >> 4, w = c & 15, da = w >> 3, j = w & 7;
-                const uint32_t cw = *reinterpret_cast<const uint32_t *>(codes + r * 64 + 4 * w);
-                const uint4 o = make_uint4(lk(lutl, cw, 0), lk(lutl, cw, 1), lk(lutl, cw, 2), lk(lutl, cw, 3));
-                *reinterpret_cast<uint4 *>(A + da * V_ATOM + r * 128 + ((j ^ (r & 7)) << 4)) = o;
+            for (int u = 0; u < 4; ++u) {
+                const int ks = 4 * sub + u;
+                uint32_t h[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int R = 16 * ks + 4 * i + ((r + rot) & 3);
+                    h[r] = *reinterpret_cast<const uint16_t *>(codes + R * 64 + ((q ^ ((R >> 1) & 3)) << 4) + 2 * j);
+                }
+                const uint32_t x = __byte_perm(h[0], h[1], 0x5410), y = __byte_perm(h[2], h[3], 0x5410);
+                const uint32_t taddr = tbase + lane_off + a_col + b * 64 + 8 * ks;
+                decode_column(__byte_perm(x, y, selA), lutl, taddr);
+                decode_column(__byte_perm(x, y, selB), lutl, taddr + (16u << 16));
             }
-            tc::fence_proxy_async();  // the MMA reads A through the async proxy
+            tc::st_wait();
+            tc::fence_before();
             __syncwarp();
             if (lane == 0) {
-                as::mbar_arrive(&afull[ab]);
+                as::mbar_arrive(&afull[b]);
                 as::mbar_arrive(&empty[s]);
             }
         }
-        // epilogue: warps 2..5 read the accumulator, TMEM lanes 32 (w % 4) .. (dims)
+        // epilogue: warps 2..5 read the accumulator, TMEM lanes 32 q .. +31 (dims, in the decoders' order)
         if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
         tc::fence_after();
         if (ok && warp < 6) {
-            const int quad = warp & 3;
             float v[NHP];
-            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16);
             if constexpr (NHP == 32) {
-                tc::ld32f(taddr, v);
+                tc::ld32f(tbase + lane_off, v);
             } else {
-                tc::ld16f(taddr, v);
+                tc::ld16f(tbase + lane_off, v);
             }
-            const int d = g * V_DG + quad * 32 + lane;
+            const int d = g * V_DG + 32 * q + 4 * (lane & 7) + 2 * (lane >> 4) + ((lane >> 3) & 1);
 #pragma unroll
             for (int h = 0; h < NHP; ++h) {
                 if (h < a.nh) {
@@ -434,7 +470,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
     __syncthreads();
     if (warp == 0) {
         tc::fence_after();
-        tc::dealloc(tbase, TCOLS);
+        tc::dealloc(tbase, V_TCOLS);
     }
 }
 
@@ -447,11 +483,11 @@ cudaError_t launch_tc(const TqAttnArgs &a, cudaStream_t s) {
     const int64_t rows = (int64_t)a.n_slots * a.L * a.B;
     if (!make_tensor_map(&sm.codes, a.kcodes, rows, a.kpl, a.kpl, 1, 32, S_TILE, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_tensor_map(&sm.q, a.qrot, (int64_t)a.M * a.nh, a.kvd, a.kvd, 2, S_KB, NHP, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tensor_map(&vm.codes, a.vcodes, rows, a.vpl, a.vpl, 1, V_DG / 2, V_KB, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_tensor_map(&vm.e, a.E, (int64_t)a.M * a.nh, a.Sp, a.Sp, 2, V_KB, NHP, CU_TENSOR_MAP_SWIZZLE_128B))
+        !make_tensor_map(&vm.codes, a.vcodes, rows, a.vpl, a.vpl, 1, V_DG / 2, V_KB, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_tensor_map(&vm.e, a.E, (int64_t)a.M * a.nh, a.Sp, a.Sp, 2, 64, NHP, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    const size_t ssm = 1024 + (size_t)S_STG * S_STAGE + LUTW * 4 + (size_t)2 * NHP * 4 * S_CH * 4 + 256;
-    const size_t vsm = 1024 + (size_t)V_STG * V_STAGE + 2 * V_A + LUTW * 4 + 256;
+    const size_t ssm = 1024 + (size_t)S_STG * S_STAGE + LUTW * 4 + 256;
+    const size_t vsm = 1024 + (size_t)V_STG * V_STAGE + LUTW * 4 + 256;
     cudaError_t e = dev::smem(tc_scores_kernel<NHP>, ssm);
     if (e == cudaSuccess) e = dev::smem(tc_values_kernel<NHP>, vsm);
     if (e != cudaSuccess) return e;
