@@ -9,11 +9,11 @@
 // Three launches per layer:
 //  * tc_scores_kernel — CTA = (two 128-position tiles, token). D[128 positions
 //    x NHP heads] += A[positions x 16 dims] B[16 dims x heads] with A in
-//    tensor memory: two decoder threads own TMEM lane r (= position r of its
-//    tile), each turning 16 of its row's 32 code bytes per 64-dim block into
-//    f16 centroid pairs through a 32-replica shared-memory table (entry (b, l)
-//    at word 32 b + l, lane l reads replica l: conflict-free) and storing them
-//    with tcgen05.st; q~ arrives by TMA (128-byte swizzle) as the B operand. The
+//    tensor memory: decoder thread r owns TMEM lane r (= position r of its
+//    tile), turns its row's 32 code bytes per 64-dim block into f16 centroid
+//    pairs through a 32-replica shared-memory table (entry (b, l) at word
+//    32 b + l, lane l reads replica l: conflict-free) and stores them with
+//    tcgen05.st; q~ arrives by TMA (128-byte swizzle) as the B operand. The
 //    epilogue scales by norm_k * scale, and per 32-position chunk writes the
 //    head maxima c, the sums sum exp(s - c) and e = exp(s - c) * norm_v (f16).
 //  * tc_softmax_kernel — per (token, head): the global max M over the chunks,
@@ -26,10 +26,12 @@
 //    consecutive rows, and each nibble pair of consecutive positions indexes
 //    the same byte -> f16 pair table, stored with tcgen05.st 16x256b. B = e
 //    rows by TMA. The epilogue writes u~ = D / l as f16 hi / lo.
-// Warp roles: warp 0 TMA producer, warp 1 MMA issuer (one thread), the rest
-// (16 warps in the scores kernel, 8 in the values kernel) decoders and
-// epilogue; two CTAs per SM for both. Shared-memory stages (TMA) and tensor-
-// memory A buffers (decoders) run as separate rings. Every mbarrier wait is bounded:
+// Warp roles (352 threads): warp 0 TMA producer; warps 1 and 2 MMA issuers
+// (one thread each: a single thread issues one tcgen05.mma per ~50 ns, so two
+// independent MMA streams per CTA, per tile in the scores kernel and per half
+// of each K block in the values kernel); warps 3..10 decoders and epilogue.
+// Two CTAs per SM. Shared-memory stages (TMA) and tensor-memory A buffers
+// (decoders) run as separate rings. Every mbarrier wait is bounded:
 // on expiry the CTA raises its abort flag, KG_ERR_TIMEOUT goes to the error
 // word, every warp still passes the barriers it owes and the tensor memory is
 // released.
@@ -50,8 +52,8 @@ namespace kg {
 namespace attn {
 namespace {
 
-constexpr int SCW = 576;        // scores threads per CTA: TMA, MMA and 16 decoder warps
-constexpr int TCW = 320;        // values threads per CTA: TMA, MMA and 8 decoder warps
+constexpr int SCW = 352;        // scores threads per CTA: TMA, two MMA issuers, 8 decoder warps
+constexpr int TCW = 352;        // values threads per CTA: TMA, two MMA issuers, 8 decoder warps
 constexpr int LUTW = 256 * 32;  // words of the replicated code-byte -> centroid-pair table
 constexpr uint32_t FULLM = 0xffffffffu;
 
@@ -74,7 +76,7 @@ constexpr int V_DG = 128;                            // dims per CTA (64 code by
 constexpr int V_CODE = V_KB * (V_DG / 2);            // 8 KB, rows in the 64-byte swizzle
 constexpr int V_E = 2 * 32 * 128;                    // e block: two 64-position atoms of up to 32 heads (f16)
 constexpr int V_STAGE = V_CODE + V_E;                // 16 KB
-constexpr int V_TCOLS = 256;                         // acc (32) + A (3 buffers x 64 columns)
+constexpr int V_TCOLS = 256;                         // acc (2 x 32) + A (3 buffers x 64 columns)
 
 struct ScoreMaps {
     CUtensorMap codes, q;
@@ -122,36 +124,39 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
     float *sT = reinterpret_cast<float *>(dsm);  // [2 tiles][NHP][4 chunks][33], over the drained stages
     uint32_t *lut = reinterpret_cast<uint32_t *>(dsm + S_STG * S_STAGE);
     uint64_t *full = reinterpret_cast<uint64_t *>(lut + LUTW);
-    uint64_t *empty = full + S_STG, *afull = empty + S_STG, *aempty = afull + S_AB, *accfull = aempty + S_AB;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
+    uint64_t *empty = full + S_STG;
+    uint64_t *afull = empty + S_STG;     // [S_AB][2 tiles]
+    uint64_t *aempty = afull + 2 * S_AB;  // [S_AB][2 tiles]
+    uint64_t *accfull = aempty + 2 * S_AB;  // [2 tiles]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     lut_build(lut, a.kcent);  // a constant input: overlaps the previous kernel
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S_STG; ++s) {
-            as::mbar_init(&full[s], 1);
-            as::mbar_init(&empty[s], 17);  // 16 decoder warps (codes read) + the MMA commit (q~ read)
-        }
-        for (int b = 0; b < S_AB; ++b) {
-            as::mbar_init(&afull[b], 16);
-            as::mbar_init(&aempty[b], 1);
-        }
-        as::mbar_init(accfull, 1);
-        *abort_flag = 0;
-        as::mbar_fence_init();
-    }
     if (warp == 0) tc::alloc(tslot, S_TCOLS);
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
-    const uint32_t tbase = *tslot;
     pdl_wait();
-
     const int m = blockIdx.y;
     const int tn = a.pos[m] + 1;
     const int p0 = blockIdx.x * 2 * S_TILE;
     const int ntile = p0 >= tn ? 0 : min(2, (tn - p0 + S_TILE - 1) / S_TILE);  // CTA-uniform
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_STG; ++s) {
+            as::mbar_init(&full[s], 1);
+            as::mbar_init(&empty[s], 5 * ntile + (ntile == 0));  // per live tile: 4 decoder warps + its MMA commit
+        }
+        for (int i = 0; i < 2 * S_AB; ++i) {
+            as::mbar_init(&afull[i], 4);
+            as::mbar_init(&aempty[i], 1);
+        }
+        as::mbar_init(&accfull[0], 1);
+        as::mbar_init(&accfull[1], 1);
+        *abort_flag = 0;
+        as::mbar_fence_init();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = *tslot;
     const int nkb = a.kvd / S_KB;
     const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
     const uint32_t acc_col = 0, a_col = 64;  // acc of tile p at p * 32; A of (buffer b, tile p) at 64 + (2b + p) * 32
@@ -170,73 +175,102 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
                     as::tma_load_2d(st + S_CODE, &maps.q, S_KB * kb, m * a.nh, &full[s]);
                 }
             }
-        } else if (warp == 1) {
-            if (lane == 0) {  // MMA issuer
+        } else if (warp <= 2) {
+            // MMA issuers: warp 1 + p drives tile p (one accumulator each), so the
+            // two tiles' MMA streams issue concurrently
+            // (the A barrier also covers the stage's TMA: the decoders waited for it before arriving)
+            const int p = warp - 1;
+            if (lane == 0 && p < ntile) {
                 constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP);
+                int s = 0, b = 0;
+                uint32_t bph = 0;
                 for (int kb = 0; kb < nkb; ++kb) {
-                    const int s = kb % S_STG, b = kb % S_AB;
-                    if (!as::mbar_wait(&full[s], (kb / S_STG) & 1, abort_flag, a.err)) break;
-                    if (!as::mbar_wait(&afull[b], (kb / S_AB) & 1, abort_flag, a.err)) break;
+                    if (!as::mbar_wait(&afull[2 * b + p], bph, abort_flag, a.err)) break;
                     tc::fence_after();
                     const uint64_t qd = tc::sdesc_k(stages + s * S_STAGE + S_CODE);
-                    for (int p = 0; p < ntile; ++p)
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            tc::mma_ts(tbase + acc_col + p * 32, tbase + a_col + (2 * b + p) * 32 + 8 * k,
-                                       qd + (uint64_t)(2 * k), ID, (kb | k) != 0);
-                    tc::commit(&empty[s]);   // q~ of stage s read
-                    tc::commit(&aempty[b]);  // A buffer b read
+                    for (int k = 0; k < 4; ++k)
+                        tc::mma_ts(tbase + acc_col + p * 32, tbase + a_col + (2 * b + p) * 32 + 8 * k,
+                                   qd + (uint64_t)(2 * k), ID, (kb | k) != 0);
+                    tc::commit(&empty[s]);          // q~ of stage s read
+                    tc::commit(&aempty[2 * b + p]);  // A of tile p in buffer b read
+                    if (++s == S_STG) s = 0;
+                    if (++b == S_AB) {
+                        b = 0;
+                        bph ^= 1;
+                    }
                 }
-                tc::commit(accfull);
+                tc::commit(&accfull[p]);
             }
         } else {
-            // decoders: warp w handles tile (w - 2) / 8, column half ((w - 2) / 4) % 2 of
-            // each K block (16 of its 32 code bytes), TMEM lanes 32 (w % 4) .. +31
-            const int p = (warp - 2) >> 3, half = ((warp - 2) >> 2) & 1, quad = warp & 3, r = quad * 32 + lane;
+            // decoders: warp w handles tile (w - 3) / 4, TMEM lanes 32 (w % 4) .. +31:
+            // each thread turns its row's 32 code bytes of the K block into 32 columns
+            const int p = (warp - 3) >> 2, quad = warp & 3, r = quad * 32 + lane;
             const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
             const uint32_t lutl = as::sa(lut) + 4 * lane;
             bool ok = true;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % S_STG, b = kb % S_AB;
-                ok = wait_all(&full[s], (kb / S_STG) & 1, abort_flag, a.err) &&
-                     wait_all(&aempty[b], ((kb / S_AB) & 1) ^ 1, abort_flag, a.err);
-                if (!ok) break;
-                tc::fence_after();
-                if (p < ntile) {
-                    const uint8_t *row = stages + s * S_STAGE + p * S_TILE * 32 + r * 32 + 16 * half;
-                    const uint4 c0 = *reinterpret_cast<const uint4 *>(row);
-                    const uint32_t w[4] = {c0.x, c0.y, c0.z, c0.w};
-                    uint32_t v[16];
+            if (p < ntile) {
+                const uint8_t *row0 = stages + p * S_TILE * 32 + r * 32;
+                int s = 0, b = 0;
+                uint32_t sph = 0, bph = 0;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    ok = wait_all(&full[s], sph, abort_flag, a.err) &&
+                         wait_all(&aempty[2 * b + p], bph ^ 1, abort_flag, a.err);
+                    if (!ok) break;
+                    tc::fence_after();
+                    const uint8_t *row = row0 + s * S_STAGE;
+                    const uint32_t taddr = tbase + lane_off + a_col + (2 * b + p) * 32;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const uint4 c0 = *reinterpret_cast<const uint4 *>(row + 16 * hf);
+                        uint32_t v[16];
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) v[4 * i + k] = lk(lutl, w[i], k);
-                    tc::st16(tbase + lane_off + a_col + (2 * b + p) * 32 + 16 * half, v);
+                        for (int k = 0; k < 4; ++k) {
+                            v[k] = lk(lutl, c0.x, k);
+                            v[4 + k] = lk(lutl, c0.y, k);
+                            v[8 + k] = lk(lutl, c0.z, k);
+                            v[12 + k] = lk(lutl, c0.w, k);
+                        }
+                        tc::st16(taddr + 16 * hf, v);
+                    }
                     tc::st_wait();
+                    tc::fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        as::mbar_arrive(&afull[2 * b + p]);
+                        as::mbar_arrive(&empty[s]);
+                    }
+                    if (++s == S_STG) {
+                        s = 0;
+                        sph ^= 1;
+                    }
+                    if (++b == S_AB) {
+                        b = 0;
+                        bph ^= 1;
+                    }
                 }
-                tc::fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    as::mbar_arrive(&afull[b]);
-                    as::mbar_arrive(&empty[s]);
-                }
-            }
-            // epilogue: scaled scores of this lane's position into the transpose buffer
-            if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
-            tc::fence_after();
-            if (ok && p < ntile && 16 * half < NHP) {  // heads 16 half .. +15 of this lane's position
-                float v[16];
-                tc::ld16f(tbase + lane_off + acc_col + p * 32 + 16 * half, v);
-                const int pos = p0 + p * S_TILE + r;
-                const bool valid = pos < tn;
-                const float kn = valid ? __ldg(a.knorm + rbase + pos) * a.scale : 0.0f;
-                float *col = sT + (p * NHP + 16 * half) * 4 * S_CH + (r >> 5) * S_CH + (r & 31);
+                // epilogue: scaled scores of this lane's position into the transpose buffer
+                if (ok) ok = wait_all(&accfull[p], 0, abort_flag, a.err);
+                tc::fence_after();
+                if (ok) {  // the heads of this lane's position
+                    float v[NHP];
+                    if constexpr (NHP == 32) {
+                        tc::ld32f(tbase + lane_off + acc_col + p * 32, v);
+                    } else {
+                        tc::ld16f(tbase + lane_off + acc_col + p * 32, v);
+                    }
+                    const int pos = p0 + p * S_TILE + r;
+                    const bool valid = pos < tn;
+                    const float kn = valid ? __ldg(a.knorm + rbase + pos) * a.scale : 0.0f;
+                    float *col = sT + (p * NHP) * 4 * S_CH + (r >> 5) * S_CH + (r & 31);
 #pragma unroll
-                for (int h = 0; h < 16; ++h) col[h * 4 * S_CH] = valid ? v[h] * kn : -INFINITY;
+                    for (int h = 0; h < NHP; ++h) col[h * 4 * S_CH] = valid ? v[h] * kn : -INFINITY;
+                }
             }
-            bar_named(1, 512);
+            bar_named(1, 256);
+            ok = ok && !*abort_flag;  // every decoder warp skips the chunks once any wait gave up
             // per (tile, head, 32-position chunk): max, sum of exp, e = exp(s - max) * norm_v (f16)
-            const int t = threadIdx.x - 64;
+            const int t = threadIdx.x - 96;  // 0 .. 255 >= 2 tiles x NHP heads x 4 chunks
             const int pt = t / (NHP * 4), h = (t / 4) % NHP, c = t & 3;
             if (ok && pt < ntile && h < a.nh) {
                 const int q0 = p0 + pt * S_TILE + c * 32;
@@ -256,8 +290,8 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
                         const float e1 = s1 == -INFINITY ? 0.0f : __expf(s1 - mx);
                         sum += e0;
                         sum += e1;
-                        const float vn0 = e0 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i) : 0.0f;
-                        const float vn1 = e1 != 0.0f ? __ldg(a.vnorm + rbase + q0 + i + 1) : 0.0f;
+                        const float vn0 = e0 != 0.0f && q0 + i < tn ? __ldg(a.vnorm + rbase + q0 + i) : 0.0f;
+                        const float vn1 = e1 != 0.0f && q0 + i + 1 < tn ? __ldg(a.vnorm + rbase + q0 + i + 1) : 0.0f;
                         pk[(i >> 1) & 3] = h2u(e0 * vn0, e1 * vn1);
                     }
                     dst[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -275,7 +309,6 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
         tc::dealloc(tbase, S_TCOLS);
     }
 }
-
 
 // ---------------------------------------------------------------------------
 // per (head, token): global max, denominator, e rescaled in place
@@ -338,8 +371,11 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
     uint8_t *stages = dsm;
     uint32_t *lut = reinterpret_cast<uint32_t *>(dsm + V_STG * V_STAGE);
     uint64_t *full = reinterpret_cast<uint64_t *>(lut + LUTW);
-    uint64_t *empty = full + V_STG, *afull = empty + V_STG, *aempty = afull + V_AB, *accfull = aempty + V_AB;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 1);
+    uint64_t *empty = full + V_STG;
+    uint64_t *afull = empty + V_STG;      // [V_AB][2 halves of the K block]
+    uint64_t *aempty = afull + 2 * V_AB;  // [V_AB][2 halves]
+    uint64_t *accfull = aempty + 2 * V_AB;  // [2 halves]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(accfull + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -347,13 +383,14 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int s = 0; s < V_STG; ++s) {
             as::mbar_init(&full[s], 1);
-            as::mbar_init(&empty[s], 9);  // 8 decoder warps (codes read) + the MMA commit (e read)
+            as::mbar_init(&empty[s], 10);  // 8 decoder warps (codes read) + the two MMA commits (e read)
         }
-        for (int b = 0; b < V_AB; ++b) {
-            as::mbar_init(&afull[b], 8);
-            as::mbar_init(&aempty[b], 1);
+        for (int i = 0; i < 2 * V_AB; ++i) {
+            as::mbar_init(&afull[i], 4);
+            as::mbar_init(&aempty[i], 1);
         }
-        as::mbar_init(accfull, 1);
+        as::mbar_init(&accfull[0], 1);
+        as::mbar_init(&accfull[1], 1);
         *abort_flag = 0;
         as::mbar_fence_init();
     }
@@ -368,7 +405,8 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
     const int tn = a.pos[m] + 1;
     const int nkb = (tn + V_KB - 1) / V_KB;
     const int64_t rbase = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
-    constexpr uint32_t a_col = 32;  // accumulator at columns 0 .. NHP-1; A buffer b at 32 + 64 b
+    // accumulator of half hh at columns 32 hh; A buffer b at 64 + 64 b (K-steps 0..7, 8 columns each)
+    constexpr uint32_t a_col = 64;
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
@@ -382,56 +420,71 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
                 as::tma_load_2d(st + V_CODE + NHP * 128, &maps.e, kb * V_KB + 64, m * a.nh, &full[s]);
             }
         }
-    } else if (warp == 1) {
-        if (lane == 0) {  // MMA issuer
+    } else if (warp <= 2) {
+        // MMA issuers: warp 1 + hh takes positions 64 hh .. 64 hh + 63 of every
+        // K block (K-steps 4 hh .. +3, e atom hh) into its own accumulator, so the
+        // two halves' MMA streams issue concurrently; the epilogue adds them
+        // (the A barrier also covers the stage's TMA: the decoders waited for it before arriving)
+        const int hh = warp - 1;
+        if (lane == 0) {
             constexpr uint32_t ID = tc::idesc_f16(0, 128, NHP);
+            int s = 0, b = 0;
+            uint32_t bph = 0;
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % V_STG, b = kb % V_AB;
-                if (!as::mbar_wait(&full[s], (kb / V_STG) & 1, abort_flag, a.err)) break;
-                if (!as::mbar_wait(&afull[b], (kb / V_AB) & 1, abort_flag, a.err)) break;
+                if (!as::mbar_wait(&afull[2 * b + hh], bph, abort_flag, a.err)) break;
                 tc::fence_after();
-                const uint64_t ed = tc::sdesc_k(stages + s * V_STAGE + V_CODE);
+                const uint64_t ed = tc::sdesc_k(stages + s * V_STAGE + V_CODE + hh * NHP * 128);
 #pragma unroll
-                for (int ks = 0; ks < V_KB / 16; ++ks)  // 16 positions: 32 B into one of the two e atoms
-                    tc::mma_ts(tbase, tbase + a_col + b * 64 + 8 * ks,
-                               ed + (uint64_t)((ks >> 2) * (NHP * 128 / 16) + 2 * (ks & 3)), ID, (kb | ks) != 0);
+                for (int k = 0; k < 4; ++k)  // 16 positions: 32 B into the e atom
+                    tc::mma_ts(tbase + 32 * hh, tbase + a_col + b * 64 + 8 * (4 * hh + k), ed + (uint64_t)(2 * k), ID,
+                               (kb | k) != 0);
                 tc::commit(&empty[s]);
-                tc::commit(&aempty[b]);
+                tc::commit(&aempty[2 * b + hh]);
+                if (++s == V_STG) s = 0;
+                if (++b == V_AB) {
+                    b = 0;
+                    bph ^= 1;
+                }
             }
-            tc::commit(accfull);
+            tc::commit(&accfull[hh]);
         }
     } else {
         // decoders: warp w writes TMEM lanes 32 q .. +31 (q = w % 4: code bytes
-        // 16 q .. 16 q + 15 of each row), K-steps 4 ((w - 2) / 4) .. +3 of each
-        // block. Thread t = 4 j + i takes byte pair 16 q + 2 j, 2 j + 1 of rows
-        // 16 ks + 4 i .. +3 (positions), in an order rotated by i / 2 so that the
-        // four rows one load instruction touches lie in distinct banks of the
-        // 64-byte swizzle; byte 2 j fills lanes j, j + 8 and byte 2 j + 1 lanes
-        // j + 16, j + 24 of the warp's quarter (dims 4 j + 0, 1, 2, 3).
-        const int q = warp & 3, sub = (warp - 2) >> 2, i = lane & 3, j = lane >> 2;
+        // 16 q .. 16 q + 15 of each row), K-steps 4 hh .. +3 of each block
+        // (hh = (w - 3) / 4). Thread t = 4 j + i takes byte pair 16 q + 2 j,
+        // 2 j + 1 of rows 16 ks + 4 i .. +3 (positions), in an order rotated by
+        // i / 2 so that the four rows one load instruction touches lie in
+        // distinct banks of the 64-byte swizzle; byte 2 j fills lanes j, j + 8
+        // and byte 2 j + 1 lanes j + 16, j + 24 of the warp's quarter (dims
+        // 4 j + 0, 1, 2, 3).
+        const int q = warp & 3, hh = (warp - 3) >> 2, i = lane & 3, j = lane >> 2;
         const int rot = i >> 1;
         const uint32_t selA = rot ? 0x4206u : 0x6420u, selB = rot ? 0x5317u : 0x7531u;
         const uint32_t lutl = as::sa(lut) + 4 * lane;
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+        // byte offsets of this thread's four rows (the K-step adds 16 rows = 1024 B, a
+        // whole number of swizzle periods): row 4 i + ((r + rot) & 3) of K-step 4 hh
+        int off[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int R = 64 * hh + 4 * i + ((r + rot) & 3);
+            off[r] = R * 64 + ((q ^ ((R >> 1) & 3)) << 4) + 2 * j;
+        }
         bool ok = true;
+        int s = 0, b = 0;
+        uint32_t sph = 0, bph = 0;
         for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % V_STG, b = kb % V_AB;
-            ok = wait_all(&full[s], (kb / V_STG) & 1, abort_flag, a.err) &&
-                 wait_all(&aempty[b], ((kb / V_AB) & 1) ^ 1, abort_flag, a.err);
+            ok = wait_all(&full[s], sph, abort_flag, a.err) && wait_all(&aempty[2 * b + hh], bph ^ 1, abort_flag, a.err);
             if (!ok) break;
             tc::fence_after();
             const uint8_t *codes = stages + s * V_STAGE;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const int ks = 4 * sub + u;
                 uint32_t h[4];
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int R = 16 * ks + 4 * i + ((r + rot) & 3);
-                    h[r] = *reinterpret_cast<const uint16_t *>(codes + R * 64 + ((q ^ ((R >> 1) & 3)) << 4) + 2 * j);
-                }
+                for (int r = 0; r < 4; ++r) h[r] = *reinterpret_cast<const uint16_t *>(codes + off[r] + 1024 * u);
                 const uint32_t x = __byte_perm(h[0], h[1], 0x5410), y = __byte_perm(h[2], h[3], 0x5410);
-                const uint32_t taddr = tbase + lane_off + a_col + b * 64 + 8 * ks;
+                const uint32_t taddr = tbase + lane_off + a_col + b * 64 + 8 * (4 * hh + u);
                 decode_column(__byte_perm(x, y, selA), lutl, taddr);
                 decode_column(__byte_perm(x, y, selB), lutl, taddr + (16u << 16));
             }
@@ -439,25 +492,36 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
             tc::fence_before();
             __syncwarp();
             if (lane == 0) {
-                as::mbar_arrive(&afull[b]);
+                as::mbar_arrive(&afull[2 * b + hh]);
                 as::mbar_arrive(&empty[s]);
             }
+            if (++s == V_STG) {
+                s = 0;
+                sph ^= 1;
+            }
+            if (++b == V_AB) {
+                b = 0;
+                bph ^= 1;
+            }
         }
-        // epilogue: warps 2..5 read the accumulator, TMEM lanes 32 q .. +31 (dims, in the decoders' order)
-        if (ok) ok = wait_all(accfull, 0, abort_flag, a.err);
+        // epilogue: warps 3..6 (one per lane quarter) add the two accumulators,
+        // TMEM lanes 32 q .. +31 (dims, in the decoders' order)
+        if (ok) ok = wait_all(&accfull[0], 0, abort_flag, a.err) && wait_all(&accfull[1], 0, abort_flag, a.err);
         tc::fence_after();
-        if (ok && warp < 6) {
-            float v[NHP];
+        if (ok && warp < 7) {
+            float v[NHP], w[NHP];
             if constexpr (NHP == 32) {
                 tc::ld32f(tbase + lane_off, v);
+                tc::ld32f(tbase + lane_off + 32, w);
             } else {
                 tc::ld16f(tbase + lane_off, v);
+                tc::ld16f(tbase + lane_off + 32, w);
             }
             const int d = g * V_DG + 32 * q + 4 * (lane & 7) + 2 * (lane >> 4) + ((lane >> 3) & 1);
 #pragma unroll
             for (int h = 0; h < NHP; ++h) {
                 if (h < a.nh) {
-                    const float u = v[h] * a.linv[(int64_t)m * a.nh + h];
+                    const float u = (v[h] + w[h]) * a.linv[(int64_t)m * a.nh + h];
                     const __half hi = __float2half_rn(u);
                     const int64_t o = ((int64_t)m * a.nh + h) * a.kvd + d;
                     a.U[o] = hi;
