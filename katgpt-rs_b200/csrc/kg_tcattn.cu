@@ -210,7 +210,10 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
             const uint32_t lutl = as::sa(lut) + 4 * lane;
             bool ok = true;
             if (p < ntile) {
+                // rows arrive in the 32-byte swizzle: 16-byte half h of row r sits at
+                // r * 32 + 16 (h ^ (r / 4 % 2)), so 8 lanes' 16-byte loads cover all banks
                 const uint8_t *row0 = stages + p * S_TILE * 32 + r * 32;
+                const int hsw = (r >> 2) & 1;
                 int s = 0, b = 0;
                 uint32_t sph = 0, bph = 0;
                 for (int kb = 0; kb < nkb; ++kb) {
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
                     const uint32_t taddr = tbase + lane_off + a_col + (2 * b + p) * 32;
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
-                        const uint4 c0 = *reinterpret_cast<const uint4 *>(row + 16 * hf);
+                        const uint4 c0 = *reinterpret_cast<const uint4 *>(row + 16 * (hf ^ hsw));
                         uint32_t v[16];
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
@@ -545,7 +548,7 @@ cudaError_t launch_tc(const TqAttnArgs &a, cudaStream_t s) {
     std::memset(&sm, 0, sizeof(sm));
     std::memset(&vm, 0, sizeof(vm));
     const int64_t rows = (int64_t)a.n_slots * a.L * a.B;
-    if (!make_tensor_map(&sm.codes, a.kcodes, rows, a.kpl, a.kpl, 1, 32, S_TILE, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+    if (!make_tensor_map(&sm.codes, a.kcodes, rows, a.kpl, a.kpl, 1, 32, S_TILE, CU_TENSOR_MAP_SWIZZLE_32B) ||
         !make_tensor_map(&sm.q, a.qrot, (int64_t)a.M * a.nh, a.kvd, a.kvd, 2, S_KB, NHP, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tensor_map(&vm.codes, a.vcodes, rows, a.vpl, a.vpl, 1, V_DG / 2, V_KB, CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_tensor_map(&vm.e, a.E, (int64_t)a.M * a.nh, a.Sp, a.Sp, 2, 64, NHP, CU_TENSOR_MAP_SWIZZLE_128B))
