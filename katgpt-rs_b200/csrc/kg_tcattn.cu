@@ -78,22 +78,31 @@ constexpr int V_E = 2 * 32 * 128;                    // e block: two 64-position
 constexpr int V_STAGE = V_CODE + V_E;                // 16 KB
 constexpr int V_TCOLS = 256;                         // acc (2 x 32) + A (3 buffers x 64 columns)
 
+// mul128 = 128 and mul4097 = 4097 arrive as kernel parameters: multiplying by
+// a value the compiler cannot see keeps the table-address and index arithmetic
+// on the multiply-add pipe (IMAD) instead of shifts on the integer pipe, which
+// the decoders otherwise saturate
 struct ScoreMaps {
     CUtensorMap codes, q;
+    uint32_t mul128;
 };
 struct ValueMaps {
     CUtensorMap codes, e;
+    uint32_t mul128, mul4097;
 };
 
 __device__ __forceinline__ uint32_t h2u(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
 }
-// byte b -> (centroid[b & 15], centroid[b >> 4]) as an f16 pair, 32 replicas
+// byte b -> (centroid[b & 15], centroid[b >> 4]) as an f16 pair, 32 replicas;
+// SWAP: (centroid[b >> 4], centroid[b & 15])
+template <bool SWAP = false>
 __device__ __forceinline__ void lut_build(uint32_t *lut, const float *cent) {
     for (int i = threadIdx.x; i < LUTW / 4; i += blockDim.x) {
         const int b = i >> 3;
-        const uint32_t v = h2u(__ldg(cent + (b & 15)), __ldg(cent + (b >> 4)));
+        const int lo = SWAP ? b >> 4 : b & 15, hi = SWAP ? b & 15 : b >> 4;
+        const uint32_t v = h2u(__ldg(cent + lo), __ldg(cent + hi));
         reinterpret_cast<uint4 *>(lut)[i] = make_uint4(v, v, v, v);
     }
 }
@@ -102,9 +111,10 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
     asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(v) : "r"(addr));
     return v;
 }
-// table entry of byte k (0..3) of w for this lane (lut_lane = table address + 4 lane)
-__device__ __forceinline__ uint32_t lk(uint32_t lut_lane, uint32_t w, int k) {
-    return lds32(lut_lane + (__byte_perm(w, 0u, 0x4440u | (uint32_t)k) << 7));
+// table entry of byte k (0..3) of w for this lane (lut_lane = table address + 4 lane,
+// m128 = 128: one table entry spans 32 words)
+__device__ __forceinline__ uint32_t lk(uint32_t lut_lane, uint32_t w, int k, uint32_t m128) {
+    return lds32(lut_lane + __byte_perm(w, 0u, 0x4440u | (uint32_t)k) * m128);
 }
 __device__ __forceinline__ void bar_named(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
@@ -208,6 +218,7 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
             const int p = (warp - 3) >> 2, quad = warp & 3, r = quad * 32 + lane;
             const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
             const uint32_t lutl = as::sa(lut) + 4 * lane;
+            const uint32_t m128 = maps.mul128;
             bool ok = true;
             if (p < ntile) {
                 // rows arrive in the 32-byte swizzle: 16-byte half h of row r sits at
@@ -229,10 +240,10 @@ __global__ void __launch_bounds__(SCW, 2) tc_scores_kernel(const __grid_constant
                         uint32_t v[16];
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
-                            v[k] = lk(lutl, c0.x, k);
-                            v[4 + k] = lk(lutl, c0.y, k);
-                            v[8 + k] = lk(lutl, c0.z, k);
-                            v[12 + k] = lk(lutl, c0.w, k);
+                            v[k] = lk(lutl, c0.x, k, m128);
+                            v[4 + k] = lk(lutl, c0.y, k, m128);
+                            v[8 + k] = lk(lutl, c0.z, k, m128);
+                            v[12 + k] = lk(lutl, c0.w, k, m128);
                         }
                         tc::st16(taddr + 16 * hf, v);
                     }
@@ -359,12 +370,13 @@ __global__ void __launch_bounds__(128) tc_softmax_kernel(const TqAttnArgs a) {
 // One code byte column over four consecutive positions (byte k of w =
 // position k) into a 16x256b tensor-memory store: its low nibbles go to lane
 // t/4 of the block and its high nibbles to lane t/4 + 8, two positions per
-// column. The table index of a column is (nibble of position 2c) | (nibble of
-// position 2c + 1) << 4: the same byte -> f16 pair table the rows use.
-__device__ __forceinline__ void decode_column(uint32_t w, uint32_t lutl, uint32_t taddr) {
-    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-    const uint32_t il = lo | (lo >> 4), ih = hi | (hi >> 4);  // indices in bytes 0 and 2
-    tc::st16x256(taddr, lk(lutl, il, 0), lk(lutl, il, 2), lk(lutl, ih, 0), lk(lutl, ih, 2));
+// column. x * 4097 = x + (x << 12) (no overlapping bits) puts (nibble of
+// position 2c + 1) | (nibble of position 2c) << 4 in byte 2c + 1 (c = 0, 1):
+// indices into the half-swapped byte -> f16 pair table, whose entry is
+// (centroid of position 2c, centroid of position 2c + 1).
+__device__ __forceinline__ void decode_column(uint32_t w, uint32_t lutl, uint32_t taddr, uint32_t m128, uint32_t m4097) {
+    const uint32_t il = (w & 0x0F0F0F0Fu) * m4097, ih = ((w >> 4) & 0x0F0F0F0Fu) * m4097;
+    tc::st16x256(taddr, lk(lutl, il, 1, m128), lk(lutl, il, 3, m128), lk(lutl, ih, 1, m128), lk(lutl, ih, 3, m128));
 }
 
 template <int NHP>
@@ -382,7 +394,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    lut_build(lut, a.vcent);
+    lut_build<true>(lut, a.vcent);
     if (threadIdx.x == 0) {
         for (int s = 0; s < V_STG; ++s) {
             as::mbar_init(&full[s], 1);
@@ -465,6 +477,7 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
         const uint32_t selA = rot ? 0x4206u : 0x6420u, selB = rot ? 0x5317u : 0x7531u;
         const uint32_t lutl = as::sa(lut) + 4 * lane;
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+        const uint32_t m128 = maps.mul128, m4097 = maps.mul4097;
         // byte offsets of this thread's four rows (the K-step adds 16 rows = 1024 B, a
         // whole number of swizzle periods): row 4 i + ((r + rot) & 3) of K-step 4 hh
         int off[4];
@@ -488,8 +501,8 @@ __global__ void __launch_bounds__(TCW, 2) tc_values_kernel(const __grid_constant
                 for (int r = 0; r < 4; ++r) h[r] = *reinterpret_cast<const uint16_t *>(codes + off[r] + 1024 * u);
                 const uint32_t x = __byte_perm(h[0], h[1], 0x5410), y = __byte_perm(h[2], h[3], 0x5410);
                 const uint32_t taddr = tbase + lane_off + a_col + b * 64 + 8 * (4 * hh + u);
-                decode_column(__byte_perm(x, y, selA), lutl, taddr);
-                decode_column(__byte_perm(x, y, selB), lutl, taddr + (16u << 16));
+                decode_column(__byte_perm(x, y, selA), lutl, taddr, m128, m4097);
+                decode_column(__byte_perm(x, y, selB), lutl, taddr + (16u << 16), m128, m4097);
             }
             tc::st_wait();
             tc::fence_before();
@@ -547,6 +560,8 @@ cudaError_t launch_tc(const TqAttnArgs &a, cudaStream_t s) {
     ValueMaps vm;
     std::memset(&sm, 0, sizeof(sm));
     std::memset(&vm, 0, sizeof(vm));
+    sm.mul128 = vm.mul128 = 128;
+    vm.mul4097 = 4097;
     const int64_t rows = (int64_t)a.n_slots * a.L * a.B;
     if (!make_tensor_map(&sm.codes, a.kcodes, rows, a.kpl, a.kpl, 1, 32, S_TILE, CU_TENSOR_MAP_SWIZZLE_32B) ||
         !make_tensor_map(&sm.q, a.qrot, (int64_t)a.M * a.nh, a.kvd, a.kvd, 2, S_KB, NHP, CU_TENSOR_MAP_SWIZZLE_128B) ||
