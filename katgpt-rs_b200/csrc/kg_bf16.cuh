@@ -58,6 +58,10 @@ struct Gemm {
     // into ksplit parts computed by the CTAs of one thread-block cluster and
     // reduced through distributed shared memory in part order (deterministic)
     int ksplit;
+    // tcgen05 decode-sized GEMMs: f32 workspace for split-K partials (null: no
+    // split), ws_bytes its size
+    float *ws;
+    int64_t ws_bytes;
 };
 
 cudaError_t gemm(const Gemm &g, cudaStream_t s);

@@ -211,6 +211,11 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.pmax, S * (g.Sp / 16) * ctx->nh, own));
     BIG_TRY(dalloc(&g.psum, S * (g.Sp / 16) * ctx->nh, own));
     BIG_TRY(dalloc(&g.linv, S * ctx->nh, own));
+    {
+        constexpr size_t kSplitWsFloats = (size_t)8 << 20;  // 32 MiB: split-K partials of decode GEMMs
+        BIG_TRY(dalloc(&g.splitk_ws, kSplitWsFloats, own));
+        g.splitk_ws_bytes = (int64_t)kSplitWsFloats * 4;
+    }
     // centroid tables
     BIG_TRY(dalloc(&g.kcent, 16, own));
     BIG_TRY(dalloc(&g.vcent, 16, own));
@@ -331,12 +336,27 @@ bf::Gemm gemm0() {
     return q;
 }
 
-// Launch a GEMM, splitting K when the output has too few tiles to fill the GPU
-// (the decode step's M is the number of sequences).
-// Launch a GEMM: tcgen05 for prefill-sized M, otherwise the mma.sync kernel
-// (with K split across a cluster when the output has few tiles, as in decode).
+// Weight matrices of at least this many elements take the tcgen05 GEMM from
+// kMinUmmaRows rows on (decode steps of a wide model); smaller ones keep the
+// mma.sync cluster kernel below 256 rows (its fused decode epilogues win
+// there).
+constexpr int64_t kWideGemm = (int64_t)8 << 20;
+constexpr int kMinUmmaRows = 32;
+
+// Launch a GEMM: tcgen05 for prefill-sized M and for decode-sized M over wide
+// weights (the decode variant splits K across CTAs through the context's
+// workspace: main-stream calls only, one GEMM at a time), otherwise the
+// mma.sync kernel (with K split across a cluster when the output has few
+// tiles).
 cudaError_t gemm_split(kg_ctx *ctx, bf::Gemm q, cudaStream_t s) {
-    if (q.M >= 256 && umma::supported(q)) return umma::gemm(q, s, ctx->d_err);
+    const bool wide = (int64_t)q.N * q.K >= kWideGemm;
+    if ((q.M >= 256 || (q.M >= kMinUmmaRows && wide)) && umma::supported(q)) {
+        if (s != ctx->aux) {
+            q.ws = ctx->big.splitk_ws;
+            q.ws_bytes = ctx->big.splitk_ws_bytes;
+        }
+        return umma::gemm(q, s, ctx->d_err);
+    }
     q.ksplit = 0;
     return bf::gemm(q, s);
 }
@@ -372,10 +392,11 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, g.xb, g.xb2, false, s, nullptr,
                                 g.std_kv ? g.ag + (int64_t)l * n : nullptr));
         }
-        // decode steps of fewer than 256 rows run the mma.sync GEMMs, whose
-        // epilogues also produce q's f16 split, the attention output's bf16
-        // split and the delta-routing accumulation (no separate kernels)
-        const bool fuse = !prefill && M < 256;
+        // decode steps of fewer than 256 rows over narrow weights run the
+        // mma.sync GEMMs, whose epilogues also produce q's f16 split, the
+        // attention output's bf16 split and the delta-routing accumulation (no
+        // separate kernels); wide models take the tcgen05 GEMMs instead
+        const bool fuse = !prefill && M < 256 && (M < kMinUmmaRows || (int64_t)n * n < kWideGemm);
         const bool fuse_q = fuse && !g.std_kv;
         // fused QKV projection
         bf::Gemm q = gemm0();

@@ -122,6 +122,8 @@ struct BigState {
     // 16-position chunk maxima / sums [max_seqs][Sp / 16][nh]
     __half *pe = nullptr;
     float *pmax = nullptr, *psum = nullptr, *linv = nullptr;
+    float *splitk_ws = nullptr;  // f32 split-K partials of decode-sized tcgen05 GEMMs
+    int64_t splitk_ws_bytes = 0;
     int Sp = 0;
 };
 int big_supported(const kg_config &c, std::string &why);

@@ -96,6 +96,76 @@ struct Maps {
     CUtensorMap a, a2, b, b2;
 };
 
+// The fused epilogue of one output row's 32 columns starting at col (row < M
+// and col < N checked by the caller): f32 out (row scale, residual, second
+// copy) or 16-bit hi / lo out (ReLU with the alive count, row scale)
+template <typename T>
+__device__ __forceinline__ void epi_chunk(const bf::Gemm &g, int row, int col, float (&v)[32], float rs, int &alive) {
+    const bool full_row = col + 32 <= g.N;
+    switch (g.epi) {
+        case bf::EPI_F32:
+        case bf::EPI_F32_ROWSCALE:
+        case bf::EPI_F32_RESID: {
+            float *dst = g.C + (int64_t)row * g.ldc + col;
+            float *dst2 = g.epi == bf::EPI_F32_RESID && g.C2 ? g.C2 + (int64_t)row * g.ldc + col : nullptr;
+            const float *r = g.epi == bf::EPI_F32_RESID ? g.R + (int64_t)row * g.ldr + col : nullptr;
+            if (full_row) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    float4 o = make_float4(v[i] * rs, v[i + 1] * rs, v[i + 2] * rs, v[i + 3] * rs);
+                    if (r) {
+                        const float4 rr = *reinterpret_cast<const float4 *>(r + i);
+                        o.x += rr.x; o.y += rr.y; o.z += rr.z; o.w += rr.w;
+                    }
+                    *reinterpret_cast<float4 *>(dst + i) = o;
+                    if (dst2) *reinterpret_cast<float4 *>(dst2 + i) = o;
+                }
+            } else {
+                for (int i = 0; i < 32 && col + i < g.N; ++i) {
+                    dst[i] = v[i] * rs + (r ? r[i] : 0.0f);
+                    if (dst2) dst2[i] = dst[i];
+                }
+            }
+            break;
+        }
+        default: {  // 16-bit hi / lo outputs
+            T *hi = static_cast<T *>(g.Cb) + (int64_t)row * g.ldcb + col;
+            T *lo = g.Cb2 ? static_cast<T *>(g.Cb2) + (int64_t)row * g.ldcb + col : nullptr;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                float x = v[i];
+                if (g.epi == bf::EPI_RELU) {
+                    alive += x > 0.0f ? 1 : 0;
+                    x = x > 0.0f ? x : 0.0f;
+                } else if (g.epi == bf::EPI_OUT_ROWSCALE) {
+                    x *= rs;
+                }
+                v[i] = x;
+            }
+            if (full_row) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 8) {
+                    T h[8], l[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        h[e] = to_t<T>(v[i + e]);
+                        l[e] = to_t<T>(v[i + e] - from_t<T>(h[e]));
+                    }
+                    *reinterpret_cast<uint4 *>(hi + i) = *reinterpret_cast<const uint4 *>(h);
+                    if (lo) *reinterpret_cast<uint4 *>(lo + i) = *reinterpret_cast<const uint4 *>(l);
+                }
+            } else {
+                for (int i = 0; i < 32 && col + i < g.N; ++i) {
+                    const T h = to_t<T>(v[i]);
+                    hi[i] = h;
+                    if (lo) lo[i] = to_t<T>(v[i] - from_t<T>(h));
+                }
+            }
+        }
+    }
+}
+
+
 template <typename T, bool SA, bool SB, int BN>
 __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_constant__ Maps maps, const bf::Gemm g,
                                                               int *err) {
@@ -209,68 +279,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
                 tmem_ld32(tbase + buf * BN + c0 + ((uint32_t)(q * 32) << 16), v);
                 const int col = n0 + c0;
                 if (!rok || col >= g.N) continue;
-                const bool full_row = col + 32 <= g.N;
-                switch (g.epi) {
-                    case bf::EPI_F32:
-                    case bf::EPI_F32_ROWSCALE:
-                    case bf::EPI_F32_RESID: {
-                        float *dst = g.C + (int64_t)row * g.ldc + col;
-                        float *dst2 = g.epi == bf::EPI_F32_RESID && g.C2 ? g.C2 + (int64_t)row * g.ldc + col : nullptr;
-                        const float *r = g.epi == bf::EPI_F32_RESID ? g.R + (int64_t)row * g.ldr + col : nullptr;
-                        if (full_row) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 4) {
-                                float4 o = make_float4(v[i] * rs, v[i + 1] * rs, v[i + 2] * rs, v[i + 3] * rs);
-                                if (r) {
-                                    const float4 rr = *reinterpret_cast<const float4 *>(r + i);
-                                    o.x += rr.x; o.y += rr.y; o.z += rr.z; o.w += rr.w;
-                                }
-                                *reinterpret_cast<float4 *>(dst + i) = o;
-                                if (dst2) *reinterpret_cast<float4 *>(dst2 + i) = o;
-                            }
-                        } else {
-                            for (int i = 0; i < 32 && col + i < g.N; ++i) {
-                                dst[i] = v[i] * rs + (r ? r[i] : 0.0f);
-                                if (dst2) dst2[i] = dst[i];
-                            }
-                        }
-                        break;
-                    }
-                    default: {  // 16-bit hi / lo outputs
-                        T *hi = static_cast<T *>(g.Cb) + (int64_t)row * g.ldcb + col;
-                        T *lo = g.Cb2 ? static_cast<T *>(g.Cb2) + (int64_t)row * g.ldcb + col : nullptr;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            float x = v[i];
-                            if (g.epi == bf::EPI_RELU) {
-                                alive += x > 0.0f ? 1 : 0;
-                                x = x > 0.0f ? x : 0.0f;
-                            } else if (g.epi == bf::EPI_OUT_ROWSCALE) {
-                                x *= rs;
-                            }
-                            v[i] = x;
-                        }
-                        if (full_row) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 8) {
-                                T h[8], l[8];
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) {
-                                    h[e] = to_t<T>(v[i + e]);
-                                    l[e] = to_t<T>(v[i + e] - from_t<T>(h[e]));
-                                }
-                                *reinterpret_cast<uint4 *>(hi + i) = *reinterpret_cast<const uint4 *>(h);
-                                if (lo) *reinterpret_cast<uint4 *>(lo + i) = *reinterpret_cast<const uint4 *>(l);
-                            }
-                        } else {
-                            for (int i = 0; i < 32 && col + i < g.N; ++i) {
-                                const T h = to_t<T>(v[i]);
-                                hi[i] = h;
-                                if (lo) lo[i] = to_t<T>(v[i] - from_t<T>(h));
-                            }
-                        }
-                    }
-                }
+                epi_chunk<T>(g, row, col, v, rs, alive);
             }
             if (g.epi == bf::EPI_RELU && rok && alive) atomicAdd(&g.row_alive[row], alive);
             tc_fence_before();
@@ -284,6 +293,195 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(2 * BN));
     }
+}
+
+// ---------------------------------------------------------------------------
+// Decode-sized GEMMs (M <= 512 rows): the same operands and epilogues, built
+// for few output tiles. One thread issues at most one tcgen05.mma per ~50-90 ns
+// (measured on B200), so at these shapes the issue rate, not the tensor pipe,
+// bounds a single-issuer CTA: two MMA warps take alternate K blocks of the
+// tile into their own accumulators (summed by the epilogue), tiles are 256
+// columns wide when B has no lo half (4x the work per instruction of a
+// 64-column tile), and the K range is split across CTAs (ks parts, a power
+// of two dividing the K blocks) when the tiles alone leave SMs idle; split
+// parts write f32 partials that splitk_reduce_kernel sums in part order
+// before the fused epilogue (deterministic).
+// Warps: 0 TMA producer, 1..2 MMA issuers, 3..6 epilogue.
+constexpr int DTHREADS = 224;
+
+template <typename T, bool SA, bool SB, int BN>
+__global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_constant__ Maps maps, const bf::Gemm g,
+                                                              int ks, float *ws, int *err) {
+    extern __shared__ __align__(1024) uint8_t dsm_raw[];
+    uint8_t *dsm = dsm_raw + ((1024u - (sa(dsm_raw) & 1023u)) & 1023u);
+    constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+    constexpr uint32_t TX = A_BYTES * (SA ? 2 : 1) + B_BYTES * (SB ? 2 : 1);
+    static_assert(TX <= STAGE_BYTES, "stage too large");
+    uint64_t *full = reinterpret_cast<uint64_t *>(dsm + STG * STAGE_BYTES);
+    uint64_t *empty = full + STG;
+    uint64_t *tfull = empty + STG;  // accumulators ready (one commit per issuer)
+    uint64_t *tempty = tfull + 1;   // accumulators drained (one arrival per epilogue warp)
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nt = (g.N + BN - 1) / BN, tiles = ((g.M + BM - 1) / BM) * nt * ks;
+    const int kbs = (g.K / BK) / ks;  // K blocks per part (>= 2)
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STG; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 2);
+        mbar_init(tempty, 4);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {  // one BN-column accumulator per issuer
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(sa(tslot)),
+                     "r"(2 * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer: the tile's K part, block by block
+            int it = 0;
+            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+                const int part = t % ks, rest = t / ks;
+                const int m0 = (rest / nt) * BM, n0 = (rest % nt) * BN;
+                for (int j = 0; j < kbs; ++j, ++it) {
+                    const int s = it % STG, kb = part * kbs + j;
+                    if (!mbar_wait(&empty[s], ((it / STG) & 1) ^ 1, abort_flag, err)) break;
+                    uint8_t *st = dsm + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], TX);
+                    tma_load_2d(st, &maps.a, kb * BK, m0, &full[s]);
+                    if (SA) tma_load_2d(st + A_BYTES, &maps.a2, kb * BK, m0, &full[s]);
+                    uint8_t *sb = st + A_BYTES * (SA ? 2 : 1);
+                    tma_load_2d(sb, &maps.b, kb * BK, n0, &full[s]);
+                    if (SB) tma_load_2d(sb + B_BYTES, &maps.b2, kb * BK, n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp <= 2) {
+        if (lane == 0) {  // MMA issuer i: K blocks i, i + 2, ... of each part into accumulator i
+            const int i = warp - 1;
+            constexpr uint32_t ID = idesc(std::is_same<T, __half>::value ? 0 : 1, BN);
+            const uint32_t d = tbase + i * BN;
+            int base = 0, tl = 0;
+            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++tl, base += kbs) {
+                if (!mbar_wait(tempty, (tl & 1) ^ 1, abort_flag, err)) break;
+                tc_fence_after();
+                bool ok = true;
+                for (int j = i; j < kbs; j += 2) {
+                    const int it = base + j, s = it % STG;
+                    if (!mbar_wait(&full[s], (it / STG) & 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t *st = dsm + s * STAGE_BYTES;
+                    const uint64_t da = sdesc(st), db = sdesc(st + A_BYTES * (SA ? 2 : 1));
+                    const uint64_t da2 = sdesc(st + A_BYTES), db2 = sdesc(st + A_BYTES * (SA ? 2 : 1) + B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint64_t ko = (uint64_t)(k * 32 >> 4);
+                        umma(d, da + ko, db + ko, ID, (j != i || k != 0) ? 1u : 0u);
+                        if (SA) umma(d, da2 + ko, db + ko, ID, 1);
+                        if (SB) umma(d, da + ko, db2 + ko, ID, 1);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                umma_commit(tfull);
+            }
+        }
+    } else {
+        // epilogue: warp w owns TMEM lanes 32 (w % 4) .. +31 = tile rows
+        const int q = warp & 3;
+        int tl = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tl) {
+            if (!mbar_wait(tfull, tl & 1, abort_flag, err)) break;
+            tc_fence_after();
+            const int part = t % ks, rest = t / ks;
+            const int m0 = (rest / nt) * BM, n0 = (rest % nt) * BN;
+            const int row = m0 + q * 32 + lane;
+            const bool rok = row < g.M;
+            float rs = 1.0f;
+            if (ks == 1 && rok && (g.epi == bf::EPI_F32_ROWSCALE || g.epi == bf::EPI_OUT_ROWSCALE))
+                rs = g.row_scale[row];
+            int alive = 0;
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32], w[32];
+                const uint32_t ta = tbase + c0 + ((uint32_t)(q * 32) << 16);
+                tmem_ld32(ta, v);
+                tmem_ld32(ta + BN, w);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] += w[e];
+                const int col = n0 + c0;
+                if (!rok || col >= g.N) continue;
+                if (ks > 1) {  // f32 partial of this part
+                    float *dst = ws + ((int64_t)part * g.M + row) * g.N + col;
+                    if (col + 32 <= g.N) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 4)
+                            *reinterpret_cast<float4 *>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                    } else {
+                        for (int e = 0; e < 32 && col + e < g.N; ++e) dst[e] = v[e];
+                    }
+                } else {
+                    epi_chunk<T>(g, row, col, v, rs, alive);
+                }
+            }
+            if (g.epi == bf::EPI_RELU && rok && alive) atomicAdd(&g.row_alive[row], alive);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(2 * BN));
+    }
+}
+
+// sum of the ks partials (part order) + the fused epilogue; one thread per
+// (row, 32-column chunk)
+template <typename T>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const bf::Gemm g, int ks, const float *ws) {
+    const int chunks = (g.N + 31) / 32;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)g.M * chunks) return;
+    const int row = (int)(idx / chunks), col = (int)(idx % chunks) * 32;
+    float v[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = 0.0f;
+    const bool full_row = col + 32 <= g.N;
+    for (int p = 0; p < ks; ++p) {
+        const float *src = ws + ((int64_t)p * g.M + row) * g.N + col;
+        if (full_row) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+                const float4 x = *reinterpret_cast<const float4 *>(src + e);
+                v[e] += x.x;
+                v[e + 1] += x.y;
+                v[e + 2] += x.z;
+                v[e + 3] += x.w;
+            }
+        } else {
+            for (int e = 0; e < 32 && col + e < g.N; ++e) v[e] += src[e];
+        }
+    }
+    const float rs = (g.epi == bf::EPI_F32_ROWSCALE || g.epi == bf::EPI_OUT_ROWSCALE) ? g.row_scale[row] : 1.0f;
+    int alive = 0;
+    epi_chunk<T>(g, row, col, v, rs, alive);
+    if (g.epi == bf::EPI_RELU && alive) atomicAdd(&g.row_alive[row], alive);
 }
 
 template <typename T, bool SA, bool SB, int BN>
@@ -306,6 +504,30 @@ cudaError_t launch_bn(const bf::Gemm &g, cudaStream_t s, int *err, int nsm) {
     return cudaGetLastError();
 }
 
+template <typename T, bool SA, bool SB, int BN>
+cudaError_t launch_dec(const bf::Gemm &g, cudaStream_t s, int *err, int nsm, int ks) {
+    Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+    if (!make_tensor_map(&maps.a, g.A, g.M, g.K, g.lda, 2, BK, BM, SW) ||
+        (SA && !make_tensor_map(&maps.a2, g.A2, g.M, g.K, g.lda, 2, BK, BM, SW)) ||
+        !make_tensor_map(&maps.b, g.B, g.N, g.K, g.ldb, 2, BK, BN, SW) ||
+        (SB && !make_tensor_map(&maps.b2, g.B2, g.N, g.K, g.ldb, 2, BK, BN, SW)))
+        return cudaErrorInvalidValue;
+    const int smem = 1024 + STG * STAGE_BYTES + 256;
+    {
+        cudaError_t e = dev::smem(umma_dec_kernel<T, SA, SB, BN>, smem);
+        if (e != cudaSuccess) return e;
+    }
+    const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) * ks;
+    umma_dec_kernel<T, SA, SB, BN><<<std::min(tiles, nsm), DTHREADS, smem, s>>>(maps, g, ks, g.ws, err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || ks == 1) return e;
+    const int64_t work = (int64_t)g.M * ((g.N + 31) / 32);
+    splitk_reduce_kernel<T><<<(unsigned)((work + 255) / 256), 256, 0, s>>>(g, ks, g.ws);
+    return cudaGetLastError();
+}
+
 // Tile width: 256 (128 with split B), 128 or 64 columns. Up to 2048 rows (a
 // 512-sequence decode step) the widest that still gives every SM a tile;
 // above, 128 when it raises the share of busy SMs over the launch's waves by
@@ -314,6 +536,15 @@ template <typename T, bool SA, bool SB>
 cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
     const int nsm = dev::sm_count();
     const int mt = (g.M + BM - 1) / BM;
+    if (g.M <= 512 && g.K / BK >= 2) {  // decode-sized: two issuers, wide tiles, split K
+        constexpr int DBN = SB ? 128 : 256;
+        const int kb_n = g.K / BK, tiles = mt * ((g.N + DBN - 1) / DBN);
+        int ks = 1;
+        while (tiles * ks * 2 <= nsm && kb_n % (ks * 2) == 0 && kb_n / (ks * 2) >= 4 && g.ws &&
+               (int64_t)ks * 2 * g.M * g.N * 4 <= g.ws_bytes)
+            ks *= 2;
+        return launch_dec<T, SA, SB, DBN>(g, s, err, nsm, ks);
+    }
     auto busy = [&](int bn) {
         const int t = mt * ((g.N + bn - 1) / bn);
         return (double)t / ((double)((t + nsm - 1) / nsm) * nsm);

@@ -51,3 +51,29 @@ def test_c5_widths_prefill_then_decode_match_oracle(kg, orc, forced_oracle):
         assert errf.max() <= REL_BF16, (i, int(np.argmax(errf)))
         assert err[64:].max() <= REL_BF16
     be.close()
+
+
+def test_c5_widths_decode_batch_of_64_matches_oracle(kg, orc):
+    # 64 sequences decoding together: M = 64 rows over n_embd 4096 weights take
+    # the tcgen05 decode GEMM with K split across CTAs (Wo and W2 in 8 parts,
+    # QKV and W1 in 2) and the partial-sum reduction; 16-token prefill (1024
+    # rows), then 4 decode steps, against the oracle replaying the device's codes
+    n = 64
+    cfg = kg.micro_config(vocab_size=512, block_size=32, n_layer=2, kv_mode=kg.KG_KV_TQ, weight_dtype=kg.KG_W_BF16,
+                          max_seqs=n, **C5_WIDTHS)
+    be = kg.CudaBackend(cfg)
+    w = kg.bf16_round(kg.reference_weights(cfg, seed=17, scale_mode=1, std=0.02))
+    be.compile(w)
+    T0, T = 16, 20
+    toks = np.random.default_rng(31).integers(0, cfg.vocab_size, size=(n, T)).astype(np.int32)
+    pre = be.forward_batch(toks[:, :T0])
+    dec = np.stack([be.forward_batch(toks[:, t:t + 1], start_pos=np.full(n, t))[:, 0] for t in range(T0, T)], axis=1)
+    got = np.concatenate([pre, dec], axis=1)
+    check = list(range(0, n, 8))  # every 8th sequence against the oracle
+    codes = [be.kv_codes_all(i, T) for i in check]
+    c = orc.from_kg(cfg)
+    for k, i in enumerate(check):
+        ref = orc.run_sequence_forced(c, w, toks[i], codes[k], 4, 4)
+        err = rel_err(got[i], ref)
+        assert err.max() <= REL_BF16, (i, int(np.argmax(err)), float(err.max()))
+    be.close()
