@@ -15,10 +15,12 @@ Workloads (`--workload`):
       scaling).
   c4: n_layer 24, n_embd 2048, mlp 8192, standard bf16 KV, TwELL with ~90%-zero
       hidden activations; 512 sequences per GPU, 512-token prefill (weak).
+  c1: Config::micro with AttentionMode::Standard (forward_base, f32): 4,096
+      sequences x [BOS + 15 tokens] per GPU, teacher-forced (weak).
   c2: Config::micro with AttentionMode::SpKvQuant and the 3-bit codec;
       65,536 sequences x 16 positions per GPU (weak).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c3|c4|c2]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c3|c4|c2|c1]
 
 Prints one JSON line on rank 0.
 """
@@ -64,6 +66,16 @@ WORKLOADS = {
                     "per GPU, 512-token prefill then teacher-forced decode"),
 }
 C2_SEQS, C2_T = 65536, 16
+C1_SEQS = 4096
+# the micro-model workloads (Config::micro, BOS + 15 teacher-forced tokens):
+# sequences per GPU, attention mode, the reference forward they time
+MICRO = {
+    "c1": dict(seqs=C1_SEQS, kv="f32", fwd="forward_base",
+               text="c1: Config::micro + AttentionMode::Standard (forward_base, f32), 4096 sequences x 16 positions "
+                    "per GPU"),
+    "c2": dict(seqs=C2_SEQS, kv="spkv", fwd="forward_sp_kv_quant",
+               text="c2: Config::micro + SpKvQuant + TurboQuant 3-bit, 65536 sequences x 16 positions per GPU"),
+}
 E2E_STEPS = 20
 
 
@@ -73,7 +85,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c5", choices=["c5", "c3", "c4", "c2"])
+    ap.add_argument("--workload", default="c5", choices=["c5", "c3", "c4", "c2", "c1"])
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU (0 = the workload's; smaller for profiler captures)")
     ap.add_argument("--layers", type=int, default=0,
@@ -214,27 +226,30 @@ class CpuDecode:
                    f"{self.prefill} ({self.fwd}, {el:.1f} s of decode; one f32 layer shared by all layers)")
 
 
-def cpu_sample_c2(budget_s=10.0, threads=None):
+def cpu_sample_micro(workload, budget_s=10.0, threads=None):
+    """tokens/s of the oracle's micro-model forward on the host cores."""
     oracle = _oracle()
     threads = threads or os.cpu_count() or 1
     cfg = oracle.config()
     w = oracle.weights(cfg, SEED)
-    toks = c2_tokens(0, C2_SEQS)
+    spec = MICRO[workload]
+    mode = oracle.MODE_SPKV if spec["kv"] == "spkv" else oracle.MODE_BASE
+    toks = c2_tokens(0, spec["seqs"])
     n, done, t0 = 1024, 0, time.perf_counter()
     while True:
-        oracle.run_batch(cfg, oracle.MODE_SPKV, w, toks[:n], threads=threads, keep_logits=False)
+        oracle.run_batch(cfg, mode, w, toks[:n], threads=threads, keep_logits=False)
         done += n * C2_T
         el = time.perf_counter() - t0
         if el > budget_s:
             break
-        n = min(C2_SEQS, n * 2)
-    return done / el, threads, f"{done // C2_T} sequences x {C2_T} positions (forward_sp_kv_quant, {el:.1f} s)"
+        n = min(spec["seqs"], n * 2)
+    return done / el, threads, f"{done // C2_T} sequences x {C2_T} positions ({spec['fwd']}, {el:.1f} s)"
 
 
 def per_rank_seqs(workload, world, seqs_arg):
     """(sequences on this rank, sequences in the whole job)."""
-    if workload == "c2":
-        return C2_SEQS, C2_SEQS * world
+    if workload in MICRO:
+        return MICRO[workload]["seqs"], MICRO[workload]["seqs"] * world
     spec = WORKLOADS[workload]
     if seqs_arg:
         return seqs_arg, seqs_arg * world
@@ -248,10 +263,9 @@ def per_rank_seqs(workload, world, seqs_arg):
 def workload_config(workload, world, seqs_arg=0, layers=0):
     """The `config` of a bench line (identical in both arms)."""
     l2 = "inputs larger than L2 (KV cache and weights); L2 also flushed between steps (256 MiB write)"
-    if workload == "c2":
-        return {"workload": "c2: Config::micro + SpKvQuant + TurboQuant 3-bit, 65536 sequences x 16 positions per GPU",
-                "global_batch": world * C2_SEQS, "seq_len": C2_T, "parallelism": f"dp{world} (sequence shards)",
-                "l2": l2}
+    if workload in MICRO:
+        return {"workload": MICRO[workload]["text"], "global_batch": world * MICRO[workload]["seqs"],
+                "seq_len": C2_T, "parallelism": f"dp{world} (sequence shards)", "l2": l2}
     spec = WORKLOADS[workload]
     n, tot = per_rank_seqs(workload, world, seqs_arg)
     text = spec["text"] + (f" [n_layer {layers}]" if layers else "")
@@ -266,13 +280,13 @@ def run_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
     config = workload_config(args.workload, args.gpus, args.seqs)
-    if args.workload == "c2":
+    if args.workload in MICRO:
         vals = []
         for _ in range(args.warmup + args.steps):
-            v, cores, sample = cpu_sample_c2(budget_s=3.0)
+            v, cores, sample = cpu_sample_micro(args.workload, budget_s=3.0)
             vals.append(v)
         v = float(np.median(vals[args.warmup:]))
-        ms = 1000.0 * C2_SEQS * C2_T / v
+        ms = 1000.0 * MICRO[args.workload]["seqs"] * C2_T / v
     else:
         cpu = CpuDecode(args.workload)
         spec = WORKLOADS[args.workload]
@@ -289,7 +303,7 @@ def run_reference(args):
                   f"{spec['prefill']}+step ({cpu.fwd}; one f32 layer shared by all layers)")
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": WORKLOADS[args.workload]["scaling"] if args.workload != "c2" else "weak",
+            "scaling": WORKLOADS[args.workload]["scaling"] if args.workload not in MICRO else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference", "config": config,
             "note": "reference = its x86 AVX2 CPU path restated in C++ (the Rust reference cannot be built here), "
                     "timed on the host cores",
@@ -500,10 +514,14 @@ def bench_decode(args, torch, dist, kgcuda, world, rank, local):
     return line
 
 
-def bench_c2(args, torch, dist, kgcuda, world, rank, local):
+def bench_micro(args, torch, dist, kgcuda, world, rank, local):
+    """c1 / c2: teacher-forced forward of the micro model, one position per call
+    for every sequence (the exact-order kernel)."""
     dev = torch.device("cuda", local)
-    n_seq = C2_SEQS
-    cfg = kgcuda.micro_config(kv_mode=kgcuda.KG_KV_SPKV_TQ, max_seqs=n_seq)
+    spec = MICRO[args.workload]
+    n_seq = spec["seqs"]
+    kv_mode = kgcuda.KG_KV_SPKV_TQ if spec["kv"] == "spkv" else kgcuda.KG_KV_F32
+    cfg = kgcuda.micro_config(kv_mode=kv_mode, max_seqs=n_seq)
     be = kgcuda.CudaBackend(cfg, device=local)
     be.compile(kgcuda.reference_weights(cfg, SEED))
     toks = c2_tokens(rank, n_seq)
@@ -559,8 +577,12 @@ def bench_c2(args, torch, dist, kgcuda, world, rank, local):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_val = world * n_seq * C2_T * e_steps / float(te.item())
     self_diff = float(np.abs(h_log[:, :64].permute(1, 0, 2).numpy() - lo_dec).max())
-    code_b = 2 * 12 + 2 * 4
-    bytes_per_step = n_seq * sum(4 + t * code_b + code_b + 4 + 27 * 4 for t in range(C2_T))
+    # per position read / written: token, the cached K/V rows (c2: 3-bit codes of
+    # K and V + two norms; c1: f32 K and V rows), the new row, (c2) its
+    # utility, the logits
+    row_b = 2 * 12 + 2 * 4 if spec["kv"] == "spkv" else 2 * 16 * 4
+    util_b = 4 if spec["kv"] == "spkv" else 0
+    bytes_per_step = n_seq * sum(4 + t * row_b + row_b + util_b + 27 * 4 for t in range(C2_T))
     achieved = bytes_per_step / (ms_per_step / 1000.0) / 1e9
     peaks = load_peaks()
     peak = peaks.get("hbm_gbs", 6650.0)
@@ -568,7 +590,7 @@ def bench_c2(args, torch, dist, kgcuda, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config("c2", world),
+        "config": workload_config(args.workload, world),
         "gpu_launches": C2_T * args.steps,
         "roofline": {"bound": "hbm", "kernel": "micro_forward", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,
@@ -599,12 +621,12 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    fn = bench_c2 if args.workload == "c2" else bench_decode
+    fn = bench_micro if args.workload in MICRO else bench_decode
     line = fn(args, torch, dist, kgcuda, world, rank, local)
     if rank == 0 and world == 1:
         try:
-            if args.workload == "c2":
-                v, cores, sample = cpu_sample_c2()
+            if args.workload in MICRO:
+                v, cores, sample = cpu_sample_micro(args.workload)
             else:
                 cpu = CpuDecode(args.workload)
                 v, sample = cpu.sample()
