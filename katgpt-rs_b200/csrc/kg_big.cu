@@ -349,7 +349,7 @@ constexpr int kMinUmmaRows = 32;
 // mma.sync kernel (with K split across a cluster when the output has few
 // tiles).
 cudaError_t gemm_split(kg_ctx *ctx, bf::Gemm q, cudaStream_t s) {
-    const bool wide = (int64_t)q.N * q.K >= kWideGemm;
+    const bool wide = (int64_t)q.batch * q.N * q.K >= kWideGemm;  // all batches' weights
     if ((q.M >= 256 || (q.M >= kMinUmmaRows && wide)) && umma::supported(q)) {
         if (s != ctx->aux) {
             q.ws = ctx->big.splitk_ws;

@@ -99,16 +99,18 @@ struct Maps {
 // The fused epilogue of one output row's 32 columns starting at col (row < M
 // and col < N checked by the caller): f32 out (row scale, residual, second
 // copy) or 16-bit hi / lo out (ReLU with the alive count, row scale)
+// zb: batch index (outputs at z * sC / z * sCb, residual at z * sR).
 template <typename T>
-__device__ __forceinline__ void epi_chunk(const bf::Gemm &g, int row, int col, float (&v)[32], float rs, int &alive) {
+__device__ __forceinline__ void epi_chunk(const bf::Gemm &g, int row, int col, float (&v)[32], float rs, int &alive,
+                                          int zb = 0) {
     const bool full_row = col + 32 <= g.N;
     switch (g.epi) {
         case bf::EPI_F32:
         case bf::EPI_F32_ROWSCALE:
         case bf::EPI_F32_RESID: {
-            float *dst = g.C + (int64_t)row * g.ldc + col;
-            float *dst2 = g.epi == bf::EPI_F32_RESID && g.C2 ? g.C2 + (int64_t)row * g.ldc + col : nullptr;
-            const float *r = g.epi == bf::EPI_F32_RESID ? g.R + (int64_t)row * g.ldr + col : nullptr;
+            float *dst = g.C + zb * g.sC + (int64_t)row * g.ldc + col;
+            float *dst2 = g.epi == bf::EPI_F32_RESID && g.C2 ? g.C2 + zb * g.sC + (int64_t)row * g.ldc + col : nullptr;
+            const float *r = g.epi == bf::EPI_F32_RESID ? g.R + zb * g.sR + (int64_t)row * g.ldr + col : nullptr;
             if (full_row) {
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
@@ -129,8 +131,8 @@ __device__ __forceinline__ void epi_chunk(const bf::Gemm &g, int row, int col, f
             break;
         }
         default: {  // 16-bit hi / lo outputs
-            T *hi = static_cast<T *>(g.Cb) + (int64_t)row * g.ldcb + col;
-            T *lo = g.Cb2 ? static_cast<T *>(g.Cb2) + (int64_t)row * g.ldcb + col : nullptr;
+            T *hi = static_cast<T *>(g.Cb) + zb * g.sCb + (int64_t)row * g.ldcb + col;
+            T *lo = g.Cb2 ? static_cast<T *>(g.Cb2) + zb * g.sCb + (int64_t)row * g.ldcb + col : nullptr;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 float x = v[i];
@@ -299,13 +301,17 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
 // Decode-sized GEMMs (M <= 512 rows): the same operands and epilogues, built
 // for few output tiles. One thread issues at most one tcgen05.mma per ~50-90 ns
 // (measured on B200), so at these shapes the issue rate, not the tensor pipe,
-// bounds a single-issuer CTA: two MMA warps take alternate K blocks of the
-// tile into their own accumulators (summed by the epilogue), tiles are 256
-// columns wide when B has no lo half (4x the work per instruction of a
-// 64-column tile), and the K range is split across CTAs (ks parts, a power
-// of two dividing the K blocks) when the tiles alone leave SMs idle; split
+// bounds a single-issuer CTA: two MMA warps each compute one half of the
+// tile's columns over every K block (both consume every stage of the ring in
+// order, so their barrier waits never run ahead of a phase), tiles are 256
+// columns wide when B has no lo half, and the K range is split across CTAs
+// (ks parts, a power of two dividing the K blocks) when the tiles alone leave
+// SMs idle; split
 // parts write f32 partials that splitk_reduce_kernel sums in part order
-// before the fused epilogue (deterministic).
+// before the fused epilogue (deterministic). Batched calls (the per-head
+// rotations of the decode attention) are tiles of the same 2-D matrices at
+// per-batch row or column offsets (b * sA, b * sB within the maps, b * sC /
+// sCb at the output).
 // Warps: 0 TMA producer, 1..2 MMA issuers, 3..6 epilogue.
 constexpr int DTHREADS = 224;
 
@@ -318,27 +324,38 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
     constexpr uint32_t TX = A_BYTES * (SA ? 2 : 1) + B_BYTES * (SB ? 2 : 1);
     static_assert(TX <= STAGE_BYTES, "stage too large");
     uint64_t *full = reinterpret_cast<uint64_t *>(dsm + STG * STAGE_BYTES);
-    uint64_t *empty = full + STG;
-    uint64_t *tfull = empty + STG;  // accumulators ready (one commit per issuer)
-    uint64_t *tempty = tfull + 1;   // accumulators drained (one arrival per epilogue warp)
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + 1);
+    uint64_t *empty = full + STG;   // one commit per issuer
+    uint64_t *tfull = empty + STG;  // [2] accumulator ready (one commit per issuer)
+    uint64_t *tempty = tfull + 2;   // [2] accumulator drained (one arrival per epilogue warp)
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nt = (g.N + BN - 1) / BN, tiles = ((g.M + BM - 1) / BM) * nt * ks;
-    const int kbs = (g.K / BK) / ks;  // K blocks per part (>= 2)
+    const int nt = (g.N + BN - 1) / BN, mt = (g.M + BM - 1) / BM, tiles = g.batch * mt * nt * ks;
+    const int kbs = (g.K / BK) / ks;  // K blocks per part
+    // tile t -> (batch zb, row tile, column tile, K part): part fastest
+    auto decode_tile = [&](int t, int &zb, int &part, int &m0, int &n0) {
+        part = t % ks;
+        const int r1 = t / ks;
+        n0 = (r1 % nt) * BN;
+        const int r2 = r1 / nt;
+        m0 = (r2 % mt) * BM;
+        zb = r2 / mt;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STG; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], 2);
         }
-        mbar_init(tfull, 2);
-        mbar_init(tempty, 4);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 2);
+            mbar_init(&tempty[b], 4);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (warp == 0) {  // one BN-column accumulator per issuer
+    if (warp == 0) {  // two BN-column accumulator buffers (issuer i writes columns i BN/2 .. of each)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(sa(tslot)),
                      "r"(2 * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
@@ -352,52 +369,60 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
         if (lane == 0) {  // TMA producer: the tile's K part, block by block
             int it = 0;
             for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-                const int part = t % ks, rest = t / ks;
-                const int m0 = (rest / nt) * BM, n0 = (rest % nt) * BN;
+                int zb, part, m0, n0;
+                decode_tile(t, zb, part, m0, n0);
+                // batch offsets inside the 2-D maps: whole rows or a column shift
+                const int64_t ao = zb * g.sA, bo = zb * g.sB;
+                const int ay = m0 + (int)(ao / g.lda), ax = (int)(ao % g.lda);
+                const int by = n0 + (int)(bo / g.ldb), bx = (int)(bo % g.ldb);
                 for (int j = 0; j < kbs; ++j, ++it) {
                     const int s = it % STG, kb = part * kbs + j;
                     if (!mbar_wait(&empty[s], ((it / STG) & 1) ^ 1, abort_flag, err)) break;
                     uint8_t *st = dsm + s * STAGE_BYTES;
                     mbar_expect_tx(&full[s], TX);
-                    tma_load_2d(st, &maps.a, kb * BK, m0, &full[s]);
-                    if (SA) tma_load_2d(st + A_BYTES, &maps.a2, kb * BK, m0, &full[s]);
+                    tma_load_2d(st, &maps.a, ax + kb * BK, ay, &full[s]);
+                    if (SA) tma_load_2d(st + A_BYTES, &maps.a2, ax + kb * BK, ay, &full[s]);
                     uint8_t *sb = st + A_BYTES * (SA ? 2 : 1);
-                    tma_load_2d(sb, &maps.b, kb * BK, n0, &full[s]);
-                    if (SB) tma_load_2d(sb + B_BYTES, &maps.b2, kb * BK, n0, &full[s]);
+                    tma_load_2d(sb, &maps.b, bx + kb * BK, by, &full[s]);
+                    if (SB) tma_load_2d(sb + B_BYTES, &maps.b2, bx + kb * BK, by, &full[s]);
                 }
             }
         }
     } else if (warp <= 2) {
-        if (lane == 0) {  // MMA issuer i: K blocks i, i + 2, ... of each part into accumulator i
+        if (lane == 0) {  // MMA issuer i: columns i BN/2 .. (i + 1) BN/2 of the tile, every K block
             const int i = warp - 1;
-            constexpr uint32_t ID = idesc(std::is_same<T, __half>::value ? 0 : 1, BN);
-            const uint32_t d = tbase + i * BN;
-            int base = 0, tl = 0;
-            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++tl, base += kbs) {
-                if (!mbar_wait(tempty, (tl & 1) ^ 1, abort_flag, err)) break;
+            constexpr int HN = BN / 2;
+            constexpr uint32_t ID = idesc(std::is_same<T, __half>::value ? 0 : 1, HN);
+            // the B tile's rows HN i .. (K-major, 128-byte rows; 8-row atoms of 1024 B)
+            const uint64_t bofs = (uint64_t)(i * HN * 128 >> 4);
+            int it = 0, tl = 0;
+            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++tl) {
+                const int buf = tl & 1;
+                if (!mbar_wait(&tempty[buf], ((tl >> 1) & 1) ^ 1, abort_flag, err)) break;
                 tc_fence_after();
+                const uint32_t d = tbase + buf * BN + i * HN;
                 bool ok = true;
-                for (int j = i; j < kbs; j += 2) {
-                    const int it = base + j, s = it % STG;
+                for (int j = 0; j < kbs; ++j, ++it) {
+                    const int s = it % STG;
                     if (!mbar_wait(&full[s], (it / STG) & 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     uint8_t *st = dsm + s * STAGE_BYTES;
-                    const uint64_t da = sdesc(st), db = sdesc(st + A_BYTES * (SA ? 2 : 1));
-                    const uint64_t da2 = sdesc(st + A_BYTES), db2 = sdesc(st + A_BYTES * (SA ? 2 : 1) + B_BYTES);
+                    const uint64_t da = sdesc(st), db = sdesc(st + A_BYTES * (SA ? 2 : 1)) + bofs;
+                    const uint64_t da2 = sdesc(st + A_BYTES), db2 = sdesc(st + A_BYTES * (SA ? 2 : 1) + B_BYTES) + bofs;
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint64_t ko = (uint64_t)(k * 32 >> 4);
-                        umma(d, da + ko, db + ko, ID, (j != i || k != 0) ? 1u : 0u);
+                        umma(d, da + ko, db + ko, ID, (j | k) != 0);
                         if (SA) umma(d, da2 + ko, db + ko, ID, 1);
                         if (SB) umma(d, da + ko, db2 + ko, ID, 1);
                     }
                     umma_commit(&empty[s]);
                 }
                 if (!ok) break;
-                umma_commit(tfull);
+                umma_commit(&tfull[buf]);
             }
         }
     } else {
@@ -405,10 +430,11 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
         const int q = warp & 3;
         int tl = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tl) {
-            if (!mbar_wait(tfull, tl & 1, abort_flag, err)) break;
+            const int buf = tl & 1;
+            if (!mbar_wait(&tfull[buf], (tl >> 1) & 1, abort_flag, err)) break;
             tc_fence_after();
-            const int part = t % ks, rest = t / ks;
-            const int m0 = (rest / nt) * BM, n0 = (rest % nt) * BN;
+            int zb, part, m0, n0;
+            decode_tile(t, zb, part, m0, n0);
             const int row = m0 + q * 32 + lane;
             const bool rok = row < g.M;
             float rs = 1.0f;
@@ -416,16 +442,12 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
                 rs = g.row_scale[row];
             int alive = 0;
             for (int c0 = 0; c0 < BN; c0 += 32) {
-                float v[32], w[32];
-                const uint32_t ta = tbase + c0 + ((uint32_t)(q * 32) << 16);
-                tmem_ld32(ta, v);
-                tmem_ld32(ta + BN, w);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] += w[e];
+                float v[32];
+                tmem_ld32(tbase + buf * BN + c0 + ((uint32_t)(q * 32) << 16), v);
                 const int col = n0 + c0;
                 if (!rok || col >= g.N) continue;
-                if (ks > 1) {  // f32 partial of this part
-                    float *dst = ws + ((int64_t)part * g.M + row) * g.N + col;
+                if (ks > 1) {  // f32 partial of this part: ws[batch][part][row][col]
+                    float *dst = ws + (((int64_t)zb * ks + part) * g.M + row) * g.N + col;
                     if (col + 32 <= g.N) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 4)
@@ -434,13 +456,13 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
                         for (int e = 0; e < 32 && col + e < g.N; ++e) dst[e] = v[e];
                     }
                 } else {
-                    epi_chunk<T>(g, row, col, v, rs, alive);
+                    epi_chunk<T>(g, row, col, v, rs, alive, zb);
                 }
             }
             if (g.epi == bf::EPI_RELU && rok && alive) atomicAdd(&g.row_alive[row], alive);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty);
+            if (lane == 0) mbar_arrive(&tempty[buf]);
         }
     }
     tc_fence_before();
@@ -452,19 +474,21 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
 }
 
 // sum of the ks partials (part order) + the fused epilogue; one thread per
-// (row, 32-column chunk)
+// (batch, row, 32-column chunk)
 template <typename T>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const bf::Gemm g, int ks, const float *ws) {
     const int chunks = (g.N + 31) / 32;
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (int64_t)g.M * chunks) return;
-    const int row = (int)(idx / chunks), col = (int)(idx % chunks) * 32;
+    if (idx >= (int64_t)g.batch * g.M * chunks) return;
+    const int zb = (int)(idx / ((int64_t)g.M * chunks));
+    const int64_t rc = idx - (int64_t)zb * g.M * chunks;
+    const int row = (int)(rc / chunks), col = (int)(rc % chunks) * 32;
     float v[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] = 0.0f;
     const bool full_row = col + 32 <= g.N;
     for (int p = 0; p < ks; ++p) {
-        const float *src = ws + ((int64_t)p * g.M + row) * g.N + col;
+        const float *src = ws + (((int64_t)zb * ks + p) * g.M + row) * g.N + col;
         if (full_row) {
 #pragma unroll
             for (int e = 0; e < 32; e += 4) {
@@ -480,7 +504,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const bf::Gemm g, in
     }
     const float rs = (g.epi == bf::EPI_F32_ROWSCALE || g.epi == bf::EPI_OUT_ROWSCALE) ? g.row_scale[row] : 1.0f;
     int alive = 0;
-    epi_chunk<T>(g, row, col, v, rs, alive);
+    epi_chunk<T>(g, row, col, v, rs, alive, zb);
     if (g.epi == bf::EPI_RELU && alive) atomicAdd(&g.row_alive[row], alive);
 }
 
@@ -509,21 +533,25 @@ cudaError_t launch_dec(const bf::Gemm &g, cudaStream_t s, int *err, int nsm, int
     Maps maps;
     std::memset(&maps, 0, sizeof(maps));
     const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
-    if (!make_tensor_map(&maps.a, g.A, g.M, g.K, g.lda, 2, BK, BM, SW) ||
-        (SA && !make_tensor_map(&maps.a2, g.A2, g.M, g.K, g.lda, 2, BK, BM, SW)) ||
-        !make_tensor_map(&maps.b, g.B, g.N, g.K, g.ldb, 2, BK, BN, SW) ||
-        (SB && !make_tensor_map(&maps.b2, g.B2, g.N, g.K, g.ldb, 2, BK, BN, SW)))
+    // batched calls: the maps cover every batch's rows / columns of the 2-D matrices
+    const int64_t arows = g.M + (g.batch > 1 ? (int64_t)(g.batch - 1) * g.sA / g.lda : 0);
+    const int64_t brows = g.N + (g.batch > 1 ? (int64_t)(g.batch - 1) * g.sB / g.ldb : 0);
+    const int64_t acols = g.batch > 1 ? g.lda : g.K, bcols = g.batch > 1 ? g.ldb : g.K;
+    if (!make_tensor_map(&maps.a, g.A, arows, acols, g.lda, 2, BK, BM, SW) ||
+        (SA && !make_tensor_map(&maps.a2, g.A2, arows, acols, g.lda, 2, BK, BM, SW)) ||
+        !make_tensor_map(&maps.b, g.B, brows, bcols, g.ldb, 2, BK, BN, SW) ||
+        (SB && !make_tensor_map(&maps.b2, g.B2, brows, bcols, g.ldb, 2, BK, BN, SW)))
         return cudaErrorInvalidValue;
     const int smem = 1024 + STG * STAGE_BYTES + 256;
     {
         cudaError_t e = dev::smem(umma_dec_kernel<T, SA, SB, BN>, smem);
         if (e != cudaSuccess) return e;
     }
-    const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) * ks;
+    const int tiles = g.batch * ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) * ks;
     umma_dec_kernel<T, SA, SB, BN><<<std::min(tiles, nsm), DTHREADS, smem, s>>>(maps, g, ks, g.ws, err);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || ks == 1) return e;
-    const int64_t work = (int64_t)g.M * ((g.N + 31) / 32);
+    const int64_t work = (int64_t)g.batch * g.M * ((g.N + 31) / 32);
     splitk_reduce_kernel<T><<<(unsigned)((work + 255) / 256), 256, 0, s>>>(g, ks, g.ws);
     return cudaGetLastError();
 }
@@ -538,10 +566,10 @@ cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
     const int mt = (g.M + BM - 1) / BM;
     if (g.M <= 512 && g.K / BK >= 2) {  // decode-sized: two issuers, wide tiles, split K
         constexpr int DBN = SB ? 128 : 256;
-        const int kb_n = g.K / BK, tiles = mt * ((g.N + DBN - 1) / DBN);
+        const int kb_n = g.K / BK, tiles = g.batch * mt * ((g.N + DBN - 1) / DBN);
         int ks = 1;
         while (tiles * ks * 2 <= nsm && kb_n % (ks * 2) == 0 && kb_n / (ks * 2) >= 4 && g.ws &&
-               (int64_t)ks * 2 * g.M * g.N * 4 <= g.ws_bytes)
+               (int64_t)ks * 2 * g.batch * g.M * g.N * 4 <= g.ws_bytes)
             ks *= 2;
         return launch_dec<T, SA, SB, DBN>(g, s, err, nsm, ks);
     }
@@ -567,9 +595,21 @@ cudaError_t launch(const bf::Gemm &g, cudaStream_t s, int *err) {
 }  // namespace
 
 bool supported(const bf::Gemm &g) {
-    // one batch, K in whole 64-element blocks, 16-byte aligned rows and bases,
-    // and the hi-only B form only for bf16 weights
-    if (g.batch != 1 || g.K % BK || g.lda % 8 || g.ldb % 8) return false;
+    // K in whole 64-element blocks, 16-byte aligned rows and bases, and the
+    // hi-only B form only for bf16 weights; batches only in the decode-sized
+    // GEMM (M <= 512, at least 2 K blocks), as whole-row or in-row column
+    // shifts (16-byte aligned) of the 2-D operands
+    if (g.batch < 1 || g.K % BK || g.lda % 8 || g.ldb % 8) return false;
+    if (g.batch > 1) {
+        if (g.M > 512 || g.K / BK < 2) return false;
+        auto shift_ok = [&](int64_t s, int64_t ld) {
+            return s >= 0 && (s % ld == 0 || ((int64_t)(g.batch - 1) * s + g.K <= ld && s % 8 == 0));
+        };
+        if (!shift_ok(g.sA, g.lda) || !shift_ok(g.sB, g.ldb)) return false;
+        const bool f32_out = g.epi == bf::EPI_F32 || g.epi == bf::EPI_F32_RESID || g.epi == bf::EPI_F32_ROWSCALE;
+        if (f32_out ? (g.sC % 4 != 0 || g.sR % 4 != 0) : (g.sCb % 8 != 0)) return false;
+        if (g.epi == bf::EPI_RELU || g.epi == bf::EPI_F32_ROWSCALE || g.epi == bf::EPI_OUT_ROWSCALE) return false;
+    }
     if (g.Qh || g.Dacc || g.epi == bf::EPI_BF16_SPLIT) return false;  // fused extras: mma.sync epilogue only
     if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return false;
     if (g.A2 && (reinterpret_cast<uintptr_t>(g.A2) & 15)) return false;
