@@ -48,7 +48,9 @@ typedef enum {
 typedef enum {
     KG_KV_F32 = 0,     /* transformer::forward -> forward_base, f32 KV (src/transformer.rs:398-429,1821-2200) */
     KG_KV_TQ = 1,      /* transformer::forward_quantized<TurboQuantKVCache> (src/transformer.rs:4042-4233) */
-    KG_KV_SPKV_TQ = 2  /* sp_kv::forward::forward_sp_kv_quant, SpKvGateMode::Hard (src/sp_kv/forward.rs:610-822) */
+    KG_KV_SPKV_TQ = 2, /* sp_kv::forward::forward_sp_kv_quant, SpKvGateMode::Hard (src/sp_kv/forward.rs:610-822) */
+    KG_KV_PAGED = 3    /* transformer::forward_paged over a PagedKVCache (src/transformer.rs:3305-3504,
+                          crates/katgpt-transformer/src/kv_cache.rs:187-420); see the paged section */
 } kg_kv_mode;
 
 typedef enum {
@@ -255,6 +257,53 @@ int kg_forward_prefill(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const
 /* Device-pointer form, enqueued on `stream`. */
 int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, int32_t T,
                            float *logits_out, void *stream);
+
+/* ---- PagedKVCache + forward_paged (contexts with kv_mode KG_KV_PAGED) ----
+ * The reference's copy-on-write page store for DDTree branch exploration
+ * (crates/katgpt-transformer/src/kv_cache.rs:187-420): f32 K/V in pages of 16
+ * positions, [K 16 x kv_dim | V 16 x kv_dim] per page, per-layer page lists per
+ * sequence, a LIFO free list and per-page reference counts. The bookkeeping
+ * lives on the host inside the context (the same integer state as the
+ * reference: page indices, counts and free-list order match it call for call);
+ * the pages live in a device pool of max(initial, 2 * max_seqs * n_layer *
+ * (block_size/16 + 1)) pages, and an allocation past it returns KG_ERR_OOM
+ * (the reference grows its Vec instead). A page taken from the free list is
+ * zeroed, as alloc_page does. Sequence indices run from 0 to the paged
+ * sequence count (grown by ensure and fork), at most max_seqs.
+ * kg_forward_batch / kg_forward_token on such a context are forward_paged
+ * (src/transformer.rs:3305-3504): rmsnorm, residual, rmsnorm (no gammas),
+ * write_kv at the position, attention over positions 0..pos read back from
+ * the pages, the MLP and delta routing as forward; for each sequence in batch
+ * order they call ensure_pages(seq, p) for every position p of the call
+ * first. kg_forward_batch_dev expects the caller to have done those ensures
+ * with kg_paged_ensure. Micro widths (Config::micro()), block_size 16 or 64. */
+
+/* PagedKVCache::new(config, max_sequences) (:215-238): drop every page and
+ * sequence, then max_sequences empty sequences and (block_size/16 + 1) *
+ * n_layer free pages. Contexts start as kg_paged_init(ctx, 1). */
+int kg_paged_init(kg_ctx *ctx, int32_t max_sequences);
+/* PagedKVCache::ensure_pages (:268-296): pages for positions 0..pos of every layer. */
+int kg_paged_ensure(kg_ctx *ctx, int32_t seq, int32_t pos);
+/* PagedKVCache::fork (:334-350): a new sequence sharing seq's first
+ * fork_at_pos/16 pages of each layer; its index goes to *new_seq. */
+int kg_paged_fork(kg_ctx *ctx, int32_t seq, int32_t fork_at_pos, int32_t *new_seq);
+/* PagedKVCache::rollback (:360-378): keep pages covering [0, pos/16*16), free
+ * the pages whose reference count drops to zero. */
+int kg_paged_rollback(kg_ctx *ctx, int32_t seq, int32_t pos);
+/* PagedKVCache::reset (:381-390): every sequence's pages back to the free list. */
+int kg_paged_reset(kg_ctx *ctx);
+/* write_kv / read_kv (:298-329): kv_dim floats of K and V at (layer, seq, pos),
+ * host pointers; the page must exist (kg_paged_ensure). Synchronises. */
+int kg_paged_write_kv(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, const float *k, const float *v);
+int kg_paged_read_kv(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, float *k, float *v);
+/* The page list of (layer, seq): up to cap indices into pages_out, its length
+ * into *len_out (layer_page_tables[layer][seq]). */
+int kg_paged_table(const kg_ctx *ctx, int32_t layer, int32_t seq, int32_t *pages_out, int32_t cap,
+                   int32_t *len_out);
+/* total_pages, free_pages.len(), the sequence count, and (when refs is not
+ * NULL) page_ref_counts[0 .. min(total_pages, refs_cap)). */
+int kg_paged_stats(const kg_ctx *ctx, int64_t *total_pages, int64_t *free_pages, int32_t *n_sequences,
+                   int32_t *refs, int64_t refs_cap);
 
 /* ---- TurboQuant codec access (parity / inspection) ---- */
 

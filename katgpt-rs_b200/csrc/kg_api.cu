@@ -22,6 +22,9 @@ int64_t weights_count(const kg_config &c);
 void reference_weights(const kg_config &c, uint64_t seed, int scale_mode, float std_, float *out);
 void lloyd_max(int64_t dim, int bits, std::vector<float> &cent, std::vector<float> &bnd);
 void predictor_weights(int64_t n, int64_t hidden, int64_t nkv, float init_bias, std::vector<float> &out);
+cudaError_t paged_alloc(kg_ctx *ctx);
+cudaError_t paged_flush(kg_ctx *ctx, cudaStream_t s);
+int paged_ensure_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *start_pos, int32_t T);
 }  // namespace kg
 
 namespace {
@@ -82,8 +85,8 @@ int validate(const kg_config *c, std::string &why) {
     if ((int64_t)c->n_head * c->head_dim != c->n_embd) return why = "n_head*head_dim != n_embd", -1;
     if (c->n_head % c->n_kv_head) return why = "n_head not a multiple of n_kv_head", -1;
     if (c->max_seqs <= 0) return why = "max_seqs must be positive", -1;
-    if (c->kv_mode < KG_KV_F32 || c->kv_mode > KG_KV_SPKV_TQ) return why = "bad kv_mode", -1;
-    if (c->kv_mode != KG_KV_F32) {
+    if (c->kv_mode < KG_KV_F32 || c->kv_mode > KG_KV_PAGED) return why = "bad kv_mode", -1;
+    if (kg::kv_is_tq(c->kv_mode)) {
         for (int b : {c->key_bits, c->val_bits})
             if (b < 2 || b > 8) return why = "TurboQuant bits must be in [2, 8]", -1;
         if ((int64_t)c->n_kv_head * c->head_dim < 3) return why = "kv_dim must be >= 3", -1;
@@ -206,13 +209,16 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     ctx->kvd = ctx->nkv * ctx->hd; ctx->m = c.mlp_hidden; ctx->V = c.vocab_size;
     ctx->L = c.n_layer; ctx->B = c.block_size;
     ctx->w_count = kg::weights_count(c);
-    const bool tq = c.kv_mode != KG_KV_F32;
+    const bool tq = kg::kv_is_tq(c.kv_mode);
+    const bool paged = c.kv_mode == KG_KV_PAGED;
+    if (paged && !ctx->micro)
+        return bail(fail(ctx, KG_ERR_UNSUPPORTED, "forward_paged runs the micro widths at block_size 16 or 64"));
     ctx->kpl = tq ? packed_len(ctx->kvd, c.key_bits) : 0;
     ctx->vpl = tq ? packed_len(ctx->kvd, c.val_bits) : 0;
     ctx->ph = std::max<int64_t>(ctx->n / 4, 16);
 
     // ---- KV arena (exact micro path: f32 K/V or dequantized cache + codes)
-    const size_t S = (size_t)c.max_seqs, rows = ctx->micro ? S * ctx->L * ctx->B : 0;
+    const size_t S = (size_t)c.max_seqs, rows = ctx->micro && !paged ? S * ctx->L * ctx->B : 0;
     if ((rc = dalloc(ctx, &ctx->Kf, rows * ctx->kvd))) return bail(rc);
     if ((rc = dalloc(ctx, &ctx->Vf, rows * ctx->kvd))) return bail(rc);
     if ((rc = dalloc(ctx, &ctx->codes, rows * (ctx->kpl + ctx->vpl)))) return bail(rc);
@@ -322,6 +328,11 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     a.Kf = ctx->Kf; a.Vf = ctx->Vf; a.codes = ctx->codes; a.norms = ctx->norms; a.util = ctx->util;
     a.n_slots = c.max_seqs;
     a.err = ctx->d_err;
+    if (paged) {  // PagedKVCache::new(config, 1)
+        e = kg::paged_alloc(ctx);
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "paged KV pool"));
+        if ((rc = kg_paged_init(ctx, 1))) return bail(rc);
+    }
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "context init"));
     if ((rc = kg_seq_reset_all(ctx))) return bail(rc);
@@ -424,6 +435,7 @@ int kg_seq_reset(kg_ctx *ctx, int32_t seq) {
         return KG_OK;
     }
     if (!ctx->micro) return KG_OK;
+    if (ctx->cfg.kv_mode == KG_KV_PAGED) return kg_paged_rollback(ctx, seq, 0);  // the sequence's pages back
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t rows = (size_t)ctx->L * ctx->B, r0 = (size_t)seq * rows;
     cudaStream_t s = ctx->stream;
@@ -446,6 +458,11 @@ int kg_seq_reset_all(kg_ctx *ctx) {
         return KG_OK;
     }
     if (!ctx->micro) return KG_OK;
+    if (ctx->cfg.kv_mode == KG_KV_PAGED) {
+        KG_CUDA(ctx, cudaSetDevice(ctx->device));
+        KG_CUDA(ctx, cudaMemset(ctx->d_err, 0, 4));
+        return kg_paged_reset(ctx);
+    }
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t rows = (size_t)ctx->cfg.max_seqs * ctx->L * ctx->B;
     cudaStream_t s = ctx->stream;
@@ -557,6 +574,7 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
     a.logits = logits;
     a.probs = probs;
     // `stream` is used as given: NULL is the CUDA legacy default stream.
+    if (ctx->cfg.kv_mode == KG_KV_PAGED) KG_CUDA(ctx, kg::paged_flush(ctx, static_cast<cudaStream_t>(stream)));
     KG_CUDA(ctx, kg::launch_micro(ctx->cfg, a, static_cast<cudaStream_t>(stream)));
     return KG_OK;
 }
@@ -576,6 +594,10 @@ int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const i
     }
     for (int64_t i = 0; i < (int64_t)n_seq * T; ++i)
         if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, KG_ERR_INVALID_ARG, "token out of range");
+    if (ctx->micro && ctx->cfg.kv_mode == KG_KV_PAGED) {  // forward_paged's ensure_pages, per call in order
+        int rc = kg::paged_ensure_batch(ctx, n_seq, seq_ids, start_pos, T);
+        if (rc) return rc;
+    }
     if (ctx->big_path && T > 1 && start_pos) {
         // all sequences from position 0: the prefill path (flash attention over the prompt)
         bool all0 = true;
@@ -681,7 +703,7 @@ int kg_forward_token(kg_ctx *ctx, int32_t seq, int32_t token, int32_t pos, float
 
 int kg_tq_tables(const kg_ctx *ctx, float *rot, float *kc, float *kb, float *vc, float *vb) {
     if (!ctx) return KG_ERR_INVALID_ARG;
-    if (ctx->cfg.kv_mode == KG_KV_F32) return KG_ERR_INVALID_ARG;
+    if (!kg::kv_is_tq(ctx->cfg.kv_mode)) return KG_ERR_INVALID_ARG;
     if (rot) std::memcpy(rot, ctx->h_rot.data(), ctx->h_rot.size() * 4);
     if (kc) std::memcpy(kc, ctx->h_kc.data(), ctx->h_kc.size() * 4);
     if (kb) std::memcpy(kb, ctx->h_kb.data(), ctx->h_kb.size() * 4);
@@ -693,7 +715,7 @@ int kg_tq_tables(const kg_ctx *ctx, float *rot, float *kc, float *kb, float *vc,
 int kg_tq_encode(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed, float *norms) {
     if (!ctx || !x || !packed || !norms || n_vec < 0 || (which != 0 && which != 1))
         return KG_ERR_INVALID_ARG;
-    if (ctx->cfg.kv_mode == KG_KV_F32) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
+    if (!kg::kv_is_tq(ctx->cfg.kv_mode)) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
     if (n_vec == 0) return KG_OK;
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const int64_t kvd = ctx->kvd;
@@ -776,7 +798,7 @@ int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *k
         return KG_OK;
     }
     if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no KV arena for this model shape");
-    if (ctx->cfg.kv_mode == KG_KV_F32) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
+    if (!kg::kv_is_tq(ctx->cfg.kv_mode)) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const int64_t row = ((int64_t)seq * ctx->L + layer) * ctx->B + pos;
     cudaStream_t s = ctx->stream;
@@ -882,7 +904,7 @@ int kv_arrays(const kg_ctx *ctx, KvArray *out) {
         out[n++] = {g.vcodes, (size_t)ctx->vpl};
         out[n++] = {reinterpret_cast<uint8_t *>(g.knorm), 4};
         out[n++] = {reinterpret_cast<uint8_t *>(g.vnorm), 4};
-    } else if (ctx->micro) {
+    } else if (ctx->micro && ctx->cfg.kv_mode != KG_KV_PAGED) {  // paged contexts roll back by page tables
         out[n++] = {reinterpret_cast<uint8_t *>(ctx->Kf), (size_t)ctx->kvd * 4};
         out[n++] = {reinterpret_cast<uint8_t *>(ctx->Vf), (size_t)ctx->kvd * 4};
         if (ctx->kpl + ctx->vpl) out[n++] = {ctx->codes, (size_t)(ctx->kpl + ctx->vpl)};
@@ -906,6 +928,8 @@ int kg_kv_snapshot(kg_ctx *ctx, int32_t seq, int32_t pos, void *dst_dev, void *s
     if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs || pos < 0 || pos > ctx->B || (pos > 0 && !dst_dev))
         return KG_ERR_INVALID_ARG;
     if (!ctx->big_path && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no device KV cache for this shape");
+    if (ctx->cfg.kv_mode == KG_KV_PAGED)
+        return fail(ctx, KG_ERR_UNSUPPORTED, "a paged context rolls back with kg_paged_rollback / kg_paged_fork");
     if (pos == 0) return KG_OK;
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -925,6 +949,8 @@ int kg_kv_restore(kg_ctx *ctx, int32_t seq, int32_t pos, const void *src_dev, vo
     if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs || pos < 0 || pos > ctx->B || (pos > 0 && !src_dev))
         return KG_ERR_INVALID_ARG;
     if (!ctx->big_path && !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no device KV cache for this shape");
+    if (ctx->cfg.kv_mode == KG_KV_PAGED)
+        return fail(ctx, KG_ERR_UNSUPPORTED, "a paged context rolls back with kg_paged_rollback / kg_paged_fork");
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     KvArray arr[8];

@@ -36,7 +36,31 @@ struct MicroArgs {
     float *util;             // [.. ]
     int n_slots;
     int *err;                // set to a nonzero code on an invalid token/position/slot
+    // forward_paged: page pool [n_pages][2][16][kvd] and page tables [L][n_slots][maxp]
+    float *pool;
+    const int32_t *ptab;
+    int maxp, n_pages;
 };
+
+inline bool kv_is_tq(int kv_mode) { return kv_mode == KG_KV_TQ || kv_mode == KG_KV_SPKV_TQ; }
+
+// PagedKVCache bookkeeping (crates/katgpt-transformer/src/kv_cache.rs:187-420)
+// on the host, pages in a device pool.
+struct PagedState {
+    std::vector<std::vector<std::vector<int32_t>>> tables;  // [layer][seq] -> page list
+    std::vector<int32_t> free_pages;                        // LIFO
+    std::vector<int32_t> refs;                              // per page index < total
+    int64_t total = 0;                                      // pages ever handed out
+    int64_t cap = 0;                                        // device pool capacity (pages)
+    int maxp = 0;                                           // device table width (pages per list)
+    float *pool = nullptr;                                  // [cap][2][16][kvd]
+    int32_t *d_tab = nullptr;                               // [L][max_seqs][maxp], -1 = none
+    std::vector<int32_t> h_tab;
+    std::vector<int32_t> zero_list;                         // reused pages to zero before the next use
+    int32_t *d_zero = nullptr;                              // [cap]
+    bool dirty = true;
+};
+cudaError_t zero_pages(float *pool, const int32_t *idx, int n, int64_t page_floats, cudaStream_t s);
 
 // Returns 0 if the model shape has a compiled micro kernel.
 int micro_supported(const kg_config &c);
@@ -200,6 +224,8 @@ struct kg_ctx {
     float *verify_probs = nullptr;
     int32_t *verify_tok = nullptr;
     int64_t verify_rows = 0;
+    // kv_mode KG_KV_PAGED: PagedKVCache state (kg_paged.cu)
+    kg::PagedState paged;
 };
 
 namespace kg {

@@ -32,7 +32,7 @@
 namespace kg {
 namespace {
 
-constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2, MODE_PREFILL = 3;
+constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2, MODE_PREFILL = 3, MODE_PAGED = 4;
 
 template <int KVD>
 __device__ __forceinline__ uint8_t quantize(float r, const float *bnd, int nb) {
@@ -203,6 +203,20 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
             active = false;
         }
     }
+    if constexpr (MODE == MODE_PAGED) {
+        // every page this position reads or writes must exist (ensure_pages ran)
+        for (int l = 0; active && l < p.L; ++l) {
+            const int32_t *tab = p.ptab + ((int64_t)l * p.n_slots + slot) * p.maxp;
+            for (int q = 0; q <= pos / 16; ++q) {
+                const int pg = q < p.maxp ? tab[q] : -1;
+                if (pg < 0 || pg >= p.n_pages) {
+                    atomicExch(p.err, 1);
+                    active = false;
+                    break;
+                }
+            }
+        }
+    }
     if constexpr (MODE == MODE_PREFILL) {
         if (tl == 0)
 #pragma unroll
@@ -232,7 +246,8 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         float xr[N];
 #pragma unroll
         for (int j = 0; j < N; ++j) xr[j] = x[j];
-        if constexpr (MODE == MODE_PREFILL) rmsnorm<N>(x);  // forward_prefill's double norm (:2674-2677)
+        // forward_prefill's double norm (:2674-2677), forward_paged's (:3361-3364)
+        if constexpr (MODE == MODE_PREFILL || MODE == MODE_PAGED) rmsnorm<N>(x);
         float util = 0.0f;
         if constexpr (MODE == MODE_SPKV) {
             rmsnorm<N>(x);  // double norm (sp_kv/forward.rs:648-651)
@@ -258,9 +273,19 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
 #pragma unroll
         for (int r = 0; r < KVD; ++r) v[r] = kgx::dot<N>(wv + r * N, x);
 
+        // forward_paged: this layer's page list of the sequence; a position's K
+        // row sits at page * 32 + pos % 16 rows of the pool, its V row 16 rows on
+        const int32_t *ptab_l = MODE == MODE_PAGED ? p.ptab + ((int64_t)l * p.n_slots + slot) * p.maxp : nullptr;
         if (active) {
-            float *kd = p.Kf + (row + pos) * KVD, *vd = p.Vf + (row + pos) * KVD;
-            if constexpr (MODE == MODE_BASE || MODE == MODE_PREFILL) {
+            float *kd, *vd;
+            if constexpr (MODE == MODE_PAGED) {
+                kd = p.pool + ((int64_t)ptab_l[pos >> 4] * 32 + (pos & 15)) * KVD;  // write_kv (:298-309)
+                vd = kd + 16 * KVD;
+            } else {
+                kd = p.Kf + (row + pos) * KVD;
+                vd = p.Vf + (row + pos) * KVD;
+            }
+            if constexpr (MODE == MODE_BASE || MODE == MODE_PREFILL || MODE == MODE_PAGED) {
 #pragma unroll
                 for (int j = 0; j < KVD; ++j) {
                     kd[j] = k[j];
@@ -289,6 +314,14 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         // forward_prefill attends every prompt position (bidirectional, :2863)
         const int tn = MODE == MODE_PREFILL ? T : pos + 1;
         const float *Kb = p.Kf + row * KVD, *Vb = p.Vf + row * KVD;
+        auto krow = [&](int t) -> const float * {
+            if constexpr (MODE == MODE_PAGED) return p.pool + ((int64_t)ptab_l[t >> 4] * 32 + (t & 15)) * KVD;
+            else return Kb + t * KVD;
+        };
+        auto vrow = [&](int t) -> const float * {
+            if constexpr (MODE == MODE_PAGED) return p.pool + ((int64_t)ptab_l[t >> 4] * 32 + 16 + (t & 15)) * KVD;
+            else return Vb + t * KVD;
+        };
 #pragma unroll 1
         for (int h = 0; h < NH; ++h) {
             const int g = h * NKV / NH;
@@ -304,7 +337,7 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
                     float mx = 0.0f;
 #pragma unroll 1
                     for (int t = 0; t < tn; ++t) {
-                        float sv = kgx::dot<HD>(qh, Kb + t * KVD + g * HD) * scale;
+                        float sv = kgx::dot<HD>(qh, krow(t) + g * HD) * scale;
                         scs[t] = sv;
                         mx = (t == 0 || sv > mx) ? sv : mx;
                     }
@@ -314,11 +347,14 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
                         float e = scs[t] + (-mx);
                         scs[t] = t < body ? kgx::cephes_lane(e, true) : kgx::cephes_scalar(e);
                     }
-                    float inv = 1.0f / kgx::sum_small<BLK>(scs, tn);
+                    float ssum;
+                    if constexpr (BLK < 32) ssum = kgx::sum_small<BLK>(scs, tn);
+                    else ssum = kgx::sum_rt<BLK>(*reinterpret_cast<const float(*)[BLK]>(scs), tn);
+                    float inv = 1.0f / ssum;
 #pragma unroll 1
                     for (int t = 0; t < tn; ++t) {
                         const float pt = scs[t] * inv;
-                        const float *vr = Vb + t * KVD + g * HD;
+                        const float *vr = vrow(t) + g * HD;
 #pragma unroll
                         for (int d = 0; d < HD; ++d)  // fused_scale_acc: fma body, mul+add tail
                             o[d] = (d < HD / 8 * 8) ? fmaf(pt, vr[d], o[d]) : o[d] + pt * vr[d];
@@ -503,14 +539,15 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     }  // sequence groups
 }
 
-template <int MODE>
+template <int MODE, int BLK = 16>
 cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     const int T = a.T;
     const int SB = 128 / T;
     const int threads = SB * T;
     const int blocks = (a.n_seq + SB - 1) / SB;
-    const size_t smem = ((size_t)a.pack_floats + 128 * 17 + (MODE == MODE_PREFILL ? 128 * 16 : 0)) * sizeof(float);
-    auto kfn = micro_forward<16, 4, 4, 4, 64, 27, 16, MODE>;
+    const size_t smem =
+        ((size_t)a.pack_floats + 128 * (BLK + 1) + (MODE == MODE_PREFILL ? 128 * 16 : 0)) * sizeof(float);
+    auto kfn = micro_forward<16, 4, 4, 4, 64, 27, BLK, MODE>;
     cudaError_t e = dev::smem(kfn, smem);
     if (e != cudaSuccess) return e;
     const int n_sm = dev::sm_count(), per_sm = dev::occupancy(kfn, 128, smem);
@@ -519,12 +556,27 @@ cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+__global__ void zero_pages_kernel(float *pool, const int32_t *idx, int64_t page_floats) {
+    float4 *pg = reinterpret_cast<float4 *>(pool + (int64_t)idx[blockIdx.x] * page_floats);
+    for (int64_t e = threadIdx.x; e < page_floats / 4; e += blockDim.x) pg[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 }  // namespace
+
+// alloc_page's fill(0.0) of reused pages (kv_cache.rs:244-247), batched: one
+// CTA per listed page (page_floats is a multiple of 4).
+cudaError_t zero_pages(float *pool, const int32_t *idx, int n, int64_t page_floats, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    zero_pages_kernel<<<n, 128, 0, s>>>(pool, idx, page_floats);
+    return cudaGetLastError();
+}
 
 int micro_supported(const kg_config &c) {
     // Instantiated shape: Config::micro() widths (any n_layer).
+    // forward_paged also at block_size 64, so page lists of several pages run
+    const bool blk_ok = c.block_size == 16 || (c.kv_mode == KG_KV_PAGED && c.block_size == 64);
     bool ok = c.n_embd == 16 && c.n_head == 4 && c.head_dim == 4 && c.n_kv_head == 4 &&
-              c.mlp_hidden == 64 && c.vocab_size == 27 && c.block_size == 16 &&
+              c.mlp_hidden == 64 && c.vocab_size == 27 && blk_ok &&
               c.weight_dtype == KG_W_F32 && c.n_layer >= 1 && c.n_layer <= 60;
     if (c.kv_mode == KG_KV_SPKV_TQ) ok = ok && c.spkv_window >= c.block_size;
     return ok ? 0 : -1;
@@ -544,6 +596,8 @@ cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s)
         case KG_KV_F32: return launch_mode<MODE_BASE>(a, s);
         case KG_KV_TQ: return launch_mode<MODE_QUANT>(a, s);
         case KG_KV_SPKV_TQ: return launch_mode<MODE_SPKV>(a, s);
+        case KG_KV_PAGED:
+            return c.block_size == 64 ? launch_mode<MODE_PAGED, 64>(a, s) : launch_mode<MODE_PAGED, 16>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -400,56 +400,89 @@ __global__ void norm_split_kernel(int dim, int Mk, int Mv, const float *qkv, int
     }
 }
 
-// One warp per (vector, 32-coordinate segment): codes from y' where no
-// boundary is within eps, exact recomputation of the others (the whole warp
-// computes each such dot in the reference order), then 4-bit packing (two
-// codes per byte, low first). Spreading a vector's segments over warps keeps
-// the recomputations (about 4% of the coordinates at kv_dim 4096) parallel.
-__global__ void quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
-                                      const float *rot, const float *kb, const float *vb, int kbits, int vbits,
-                                      uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl,
-                                      const int32_t *slot, const int32_t *pos, int L, int B, int layer, float eps,
-                                      int *nfix) {
+// One CTA per vector (K or V row): codes from y' where no boundary is within
+// eps, then exact recomputation of the others, then 4-bit packing (two codes
+// per byte, low first). The vector's xn is staged in shared memory once; the
+// near-boundary coordinates (about 4% of them at kv_dim 4096, so ~160 per
+// vector) go to a shared list that the CTA's warps drain, so each warp
+// streams rotation rows with many loads in flight and no warp idles while
+// another holds a long run of recomputations.
+constexpr int kFixWarps = 8;
+
+// simd_dot_f32(row, xs, dim) by one warp with xs in shared memory: lane l
+// accumulates elements l + 32c in order (the AVX2 body's 32 lanes), the row
+// loaded 32 deep per lane before the FMA chain consumes it. dim % 32 == 0.
+__device__ __forceinline__ float warp_dot_row(const float *__restrict__ row, const float *xs, int dim) {
+    const int lane = threadIdx.x & 31;
+    const int c4 = dim / 32;
+    float acc = 0.0f;
+    int c = 0;
+    for (; c + 32 <= c4; c += 32) {
+        float ra[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) ra[u] = __ldg(row + 32 * (c + u) + lane);
+        asm volatile("" ::: "memory");  // all 32 loads issue before the chain's first shared read
+#pragma unroll
+        for (int u = 0; u < 32; ++u) acc = fmaf(ra[u], xs[32 * (c + u) + lane], acc);
+    }
+#pragma unroll 8
+    for (; c < c4; ++c) acc = fmaf(__ldg(row + 32 * c + lane), xs[32 * c + lane], acc);
+    const float sum = tree32(acc);
+    return sum + 0.0f;  // warp_dot adds the (here empty) 8-chunk remainder
+}
+
+__global__ void __launch_bounds__(kFixWarps * 32, 4)
+quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, const float *xn, const uint8_t *skip,
+                      const float *rot, const float *kb, const float *vb, int kbits, int vbits, uint8_t *kcodes,
+                      uint8_t *vcodes, int64_t kpl, int64_t vpl, const int32_t *slot, const int32_t *pos, int L,
+                      int B, int layer, float eps, int *nfix) {
     pdl_wait();
-    __shared__ float bnd[2][15];
-    const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x & 31;
-    if (threadIdx.x < 15) {
-        bnd[0][threadIdx.x] = threadIdx.x < (1 << kbits) - 1 ? kb[threadIdx.x] : INFINITY;
-        bnd[1][threadIdx.x] = threadIdx.x < (1 << vbits) - 1 ? vb[threadIdx.x] : INFINITY;
+    extern __shared__ float4 fix_sm4[];
+    float *xs = reinterpret_cast<float *>(fix_sm4);                 // [dim]
+    uint16_t *list = reinterpret_cast<uint16_t *>(xs + dim);       // [dim] near-boundary coordinates
+    uint8_t *cbuf = reinterpret_cast<uint8_t *>(list + dim);       // [dim] codes
+    __shared__ float bnd[15];
+    __shared__ int nlist;
+    const int64_t v = blockIdx.x;
+    if (v >= Mk + Mv || skip[v]) return;  // skipped vectors keep their codes (reference quirk); CTA-uniform
+    const int which = v < Mk ? 0 : 1;
+    const int bits = which ? vbits : kbits;
+    const int nb = (1 << bits) - 1;
+    if (threadIdx.x < 15) bnd[threadIdx.x] = threadIdx.x < nb ? (which ? vb : kb)[threadIdx.x] : INFINITY;
+    if (threadIdx.x == 0) nlist = 0;
+    __syncthreads();
+    const float *yv = Y + v * dim, *xv = xn + v * dim;
+    for (int j = threadIdx.x; j < dim; j += blockDim.x) {
+        xs[j] = xv[j];
+        const float y = yv[j];
+        int c = 0;
+        bool near = false;
+        for (int k = 0; k < nb; ++k) {
+            c += y >= bnd[k] ? 1 : 0;
+            near |= fabsf(y - bnd[k]) <= eps;
+        }
+        cbuf[j] = (uint8_t)c;
+        if (near) list[atomicAdd(&nlist, 1)] = (uint16_t)j;
     }
     __syncthreads();
-    const int nseg = dim / 32;
-    const int64_t gw = (int64_t)blockIdx.x * warps + w;
-    const int64_t v = gw / nseg;
-    const int j0 = (int)(gw - v * nseg) * 32;
-    if (v >= Mk + Mv || skip[v]) return;  // skipped vectors keep their codes (reference quirk); warp-uniform
-    const int which = v < Mk ? 0 : 1;
-    const int64_t t = which ? v - Mk : v;
-    const int nb = (1 << (which ? vbits : kbits)) - 1;
-    const float *b = bnd[which];
-    const float y = Y[v * dim + j0 + lane];
-    int c = 0;
-    bool near = false;
-    for (int k = 0; k < nb; ++k) {
-        c += y >= b[k] ? 1 : 0;
-        near |= fabsf(y - b[k]) <= eps;
-    }
-    unsigned m = __ballot_sync(0xffffffffu, near);
-    const int fixes = __popc(m);
-    while (m) {  // exact recomputation, one coordinate at a time by the whole warp
-        const int l = __ffs(m) - 1;
-        m &= m - 1;
-        const float r = warp_dot(rot + (int64_t)(j0 + l) * dim, xn + v * dim, dim);  // all lanes get r
-        if (lane == l) {
-            c = 0;
-            for (int k = 0; k < nb; ++k) c += r >= b[k] ? 1 : 0;
+    const int n_near = nlist;
+    const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
+    for (int f = w; f < n_near; f += kFixWarps) {  // exact recomputation in the reference order
+        const int j = list[f];
+        const float r = warp_dot_row(rot + (int64_t)j * dim, xs, dim);
+        if (lane == 0) {
+            int c = 0;
+            for (int k = 0; k < nb; ++k) c += r >= bnd[k] ? 1 : 0;
+            cbuf[j] = (uint8_t)c;
         }
     }
-    const int c_hi = __shfl_down_sync(0xffffffffu, c, 1);
+    __syncthreads();
+    const int64_t t = which ? v - Mk : v;
     const int64_t drow = slot ? ((int64_t)slot[t] * L + layer) * B + pos[t] : t;
-    uint8_t *out = (which ? vcodes : kcodes) + drow * (which ? vpl : kpl) + j0 / 2;
-    if ((lane & 1) == 0) out[lane >> 1] = (uint8_t)((c & 15) | ((c_hi & 15) << 4));
-    if (nfix && lane == 0 && fixes) atomicAdd(nfix, fixes);
+    uint8_t *out = (which ? vcodes : kcodes) + drow * (which ? vpl : kpl);
+    for (int b = threadIdx.x; b < dim / 2; b += blockDim.x)
+        out[b] = (uint8_t)((cbuf[2 * b] & 15) | ((cbuf[2 * b + 1] & 15) << 4));
+    if (nfix && threadIdx.x == 0 && n_near) atomicAdd(nfix, n_near);
 }
 
 }  // namespace
@@ -472,12 +505,13 @@ cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const flo
                               uint8_t *kcodes, uint8_t *vcodes, int64_t kpl, int64_t vpl, const int32_t *slot,
                               const int32_t *pos, int L, int B, int layer, int *nfix, cudaStream_t s) {
     if (Mk + Mv <= 0) return cudaSuccess;
-    if (dim % 32 || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
-    const int warps = 8;
-    const int64_t nwarps = (int64_t)(Mk + Mv) * (dim / 32);
-    return launch_pdl(quantize_fixup_kernel, dim3((unsigned)((nwarps + warps - 1) / warps)), dim3(warps * 32), 0, s,
-                      dim, Mk, Mv, Y, xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl, vpl, slot, pos, L, B,
-                      layer, tq_fixup_eps(dim), nfix);
+    if (dim % 32 || dim > 32768 || kbits < 3 || kbits > 4 || vbits < 3 || vbits > 4) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)dim * (sizeof(float) + sizeof(uint16_t) + 1);
+    const cudaError_t e = dev::smem(quantize_fixup_kernel, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(quantize_fixup_kernel, dim3((unsigned)(Mk + Mv)), dim3(kFixWarps * 32), smem, s, dim, Mk, Mv, Y,
+                      xn, skip, rot, kb, vb, kbits, vbits, kcodes, vcodes, kpl, vpl, slot, pos, L, B, layer,
+                      tq_fixup_eps(dim), nfix);
 }
 
 namespace {
@@ -626,7 +660,7 @@ cudaError_t noalloc_scratch(int device, float **xn, uint8_t **skip) {
 extern "C" int kg_tq_encode_noalloc(kg_ctx *ctx, int32_t which, int64_t n_vec, const float *x, uint8_t *packed,
                                     float *norms, void *stream) {
     if (!ctx || !x || !packed || !norms || n_vec < 0 || (which != 0 && which != 1)) return KG_ERR_INVALID_ARG;
-    if (ctx->cfg.kv_mode == KG_KV_F32) {
+    if (!kg::kv_is_tq(ctx->cfg.kv_mode)) {
         ctx->err = "context has no TurboQuant codec";
         return KG_ERR_INVALID_ARG;
     }

@@ -14,7 +14,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIBPATH = os.path.join(HERE, "lib", "libkgcuda.so")
 
-KG_KV_F32, KG_KV_TQ, KG_KV_SPKV_TQ = 0, 1, 2
+KG_KV_F32, KG_KV_TQ, KG_KV_SPKV_TQ, KG_KV_PAGED = 0, 1, 2, 3
 KG_W_F32, KG_W_BF16 = 0, 1
 
 STATUS = {0: "ok", -1: "invalid argument", -2: "device out of memory", -3: "CUDA error",
@@ -105,6 +105,15 @@ def lib():
             "kg_comm_init": (ctypes.c_int, [P, P, I32, I32]),
             "kg_comm_destroy": (ctypes.c_int, [P]),
             "kg_decode_gather_dev": (ctypes.c_int, [P, I32, P, P, P, P, P, P]),
+            "kg_paged_init": (ctypes.c_int, [P, I32]),
+            "kg_paged_ensure": (ctypes.c_int, [P, I32, I32]),
+            "kg_paged_fork": (ctypes.c_int, [P, I32, I32, P]),
+            "kg_paged_rollback": (ctypes.c_int, [P, I32, I32]),
+            "kg_paged_reset": (ctypes.c_int, [P]),
+            "kg_paged_write_kv": (ctypes.c_int, [P, I32, I32, I32, P, P]),
+            "kg_paged_read_kv": (ctypes.c_int, [P, I32, I32, I32, P, P]),
+            "kg_paged_table": (ctypes.c_int, [P, I32, I32, P, I32, P]),
+            "kg_paged_stats": (ctypes.c_int, [P, P, P, P, P, I64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -378,3 +387,50 @@ class CudaBackend:
         u = np.empty(1, np.float32)
         self._check(lib().kg_spkv_utility(self._h, seq, layer, pos, _ptr(u)))
         return float(u[0])
+
+    # ---- PagedKVCache (kv_mode KG_KV_PAGED; crates/katgpt-transformer/src/kv_cache.rs:187-420)
+
+    def paged_init(self, max_sequences):
+        """PagedKVCache::new(config, max_sequences)."""
+        self._check(lib().kg_paged_init(self._h, max_sequences))
+
+    def paged_ensure(self, seq, pos):
+        self._check(lib().kg_paged_ensure(self._h, seq, pos))
+
+    def paged_fork(self, seq, fork_at_pos):
+        out = ctypes.c_int32(-1)
+        self._check(lib().kg_paged_fork(self._h, seq, fork_at_pos, ctypes.byref(out)))
+        return out.value
+
+    def paged_rollback(self, seq, pos):
+        self._check(lib().kg_paged_rollback(self._h, seq, pos))
+
+    def paged_reset(self):
+        self._check(lib().kg_paged_reset(self._h))
+
+    def paged_write_kv(self, layer, seq, pos, k, v):
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        self._check(lib().kg_paged_write_kv(self._h, layer, seq, pos, _ptr(k), _ptr(v)))
+
+    def paged_read_kv(self, layer, seq, pos):
+        kvd = self.cfg.kvd()
+        k = np.empty(kvd, np.float32)
+        v = np.empty(kvd, np.float32)
+        self._check(lib().kg_paged_read_kv(self._h, layer, seq, pos, _ptr(k), _ptr(v)))
+        return k, v
+
+    def paged_table(self, layer, seq):
+        n = ctypes.c_int32(0)
+        self._check(lib().kg_paged_table(self._h, layer, seq, None, 0, ctypes.byref(n)))
+        out = np.empty(n.value, np.int32)
+        self._check(lib().kg_paged_table(self._h, layer, seq, _ptr(out), n.value, ctypes.byref(n)))
+        return [int(x) for x in out]
+
+    def paged_stats(self):
+        """(total_pages, free_pages, n_sequences, page_ref_counts)."""
+        tot, free, ns = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int32(0)
+        self._check(lib().kg_paged_stats(self._h, ctypes.byref(tot), ctypes.byref(free), ctypes.byref(ns), None, 0))
+        refs = np.zeros(tot.value, np.int32)
+        self._check(lib().kg_paged_stats(self._h, None, None, None, _ptr(refs), tot.value))
+        return tot.value, free.value, ns.value, [int(r) for r in refs]

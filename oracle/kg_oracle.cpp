@@ -965,6 +965,51 @@ struct Seq {
         }
     }
 
+    // transformer.rs:3305-3504 (forward_paged, default features): forward
+    // with K/V in PagedKVCache pages (crates/katgpt-transformer/src/kv_cache.rs:
+    // 187-420). Per layer: rmsnorm, save the residual, rmsnorm again (no
+    // gammas), separate Q/K/V matmuls, write_kv into the page that holds pos,
+    // read_kv of positions 0..pos into a flat buffer, attention_head per head,
+    // Wo + residual, the MLP with the TwELL switch, delta routing; lm_head.
+    // pool: pages of [K: 16 x kvd | V: 16 x kvd] floats; table: this
+    // sequence's page list per layer, [L][maxp] page indices.
+    void forward_paged(int64_t tok, int64_t pos, float *pool, const int64_t *table, int64_t maxp) {
+        const int64_t PS = 16;  // PAGE_SIZE (kv_cache.rs:189)
+        add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
+        const float scale = 1.0f / sqrtf((float)d.hd);
+        const int64_t tn = pos + 1;
+        std::vector<float> fk(tn * d.kvd), fv(tn * d.kvd);
+        auto page_row = [&](int64_t l, int64_t t, int which) {
+            const int64_t pg = table[l * maxp + t / PS];
+            return pool + ((pg * 2 + which) * PS + t % PS) * d.kvd;
+        };
+        for (int64_t l = 0; l < d.L; ++l) {
+            const LayerW &lw = W->layers[l];
+            rmsnorm(x.data(), d.n);
+            xr = x;
+            rmsnorm(x.data(), d.n);
+            matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+            matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+            matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+            std::memcpy(page_row(l, pos, 0), k.data(), d.kvd * 4);  // write_kv (:298-309)
+            std::memcpy(page_row(l, pos, 1), v.data(), d.kvd * 4);
+            for (int64_t t = 0; t < tn; ++t) {  // read_kv into the flat buffers (:3390-3398)
+                std::memcpy(&fk[t * d.kvd], page_row(l, t, 0), d.kvd * 4);
+                std::memcpy(&fv[t * d.kvd], page_row(l, t, 1), d.kvd * 4);
+            }
+            for (int64_t h = 0; h < d.nh; ++h) {
+                int64_t g = h * d.nkv / d.nh;
+                attention_head(q.data(), fk.data(), fv.data(), att.data(), scores.data(), h * d.hd, g * d.hd,
+                               d.kvd, d.hd, tn, scale);
+            }
+            matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+            add_inplace(x.data(), xr.data(), d.n);
+            mlp(lw, false, nullptr);
+            delta_route(l);
+        }
+        matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
+    }
+
     // transformer.rs:4042-4233 (forward_quantized<TurboQuantKVCache>)
     void forward_quant(int64_t tok, int64_t pos) {
         add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
@@ -1380,6 +1425,25 @@ int or_prefill_then_decode(const or_config *c, const float *weights, const int32
         s.forward_base(cont[i], P + i);
         std::memcpy(logits_out + (int64_t)(i + 1) * d.V, s.logits.data(), d.V * 4);
     }
+    return 0;
+}
+
+// One forward_paged token (src/transformer.rs:3305-3504) of a sequence whose
+// pages the caller has ensured (PagedKVCache::ensure_pages): writes K/V of
+// `pos` into `pool` and vocab_size logits. table [L][maxp] is the sequence's
+// page list per layer (entries past its length unused).
+int or_forward_paged(const or_config *c, const float *weights, float *pool, const int64_t *table, int64_t maxp,
+                     int32_t token, int32_t pos, float *logits) {
+    if (check_cfg(c, 0) || !pool || !table || maxp < 1 || pos < 0 || pos >= c->block_size || pos / 16 >= maxp)
+        return -1;
+    Dims d = dims_of(c);
+    if (token < 0 || token >= d.V) return -2;
+    Weights W = view_weights(d, weights);
+    Seq s;
+    s.init(d, &W, OR_MODE_BASE, 4, 4);
+    s.sparse_threshold = c->sparse_threshold;
+    s.forward_paged(token, pos, pool, table, maxp);
+    std::memcpy(logits, s.logits.data(), d.V * 4);
     return 0;
 }
 

@@ -117,6 +117,11 @@ int or_run_sequence(const or_config *c, int mode, int key_bits, int val_bits,
 /* Same for the quantized modes, also writing the rotated unit coordinates
  * each TurboQuant store quantizes: rot_out[L][T][2][kvd] (K then V; rows of
  * zero-norm vectors untouched). */
+/* One forward_paged token (src/transformer.rs:3305-3504) over caller-ensured
+ * PagedKVCache pages: pool = pages of [K 16 x kvd | V 16 x kvd] f32, table =
+ * the sequence's [n_layer][maxp] page indices. */
+int or_forward_paged(const or_config *c, const float *weights, float *pool, const int64_t *table, int64_t maxp,
+                     int32_t token, int32_t pos, float *logits);
 int or_run_sequence_rot(const or_config *c, int mode, int key_bits, int val_bits, const float *weights,
                         const int32_t *tokens, int32_t T, float *logits, uint8_t *codes, float *norms,
                         float *rot_out);

@@ -79,6 +79,7 @@ def lib():
             "or_prefill_then_decode": (ctypes.c_int, [cp, P, P, I32, P, I32, P]),
             "or_run_sequence_forced": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, P, P, I32, P, P]),
             "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
+            "or_forward_paged": (ctypes.c_int, [cp, P, P, P, I64, I32, I32, P]),
             "or_time_decode": (ctypes.c_double, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, I32, I32, ctypes.c_int]),
         }
         for k, (r, a) in sig.items():
@@ -368,3 +369,106 @@ def time_decode(cfg, w_one_layer, ctx, n_pos, mode=MODE_QUANT, key_bits=4, val_b
     if v < 0:
         raise RuntimeError("or_time_decode: bad arguments")
     return v
+
+
+PAGE_SIZE = 16  # crates/katgpt-transformer/src/kv_cache.rs:189
+
+
+class PagedKVCache:
+    """PagedKVCache (crates/katgpt-transformer/src/kv_cache.rs:187-420),
+    restated: a pool of pages [K: PAGE_SIZE x kvd | V: PAGE_SIZE x kvd] f32,
+    per-layer page tables per sequence, a LIFO free list and per-page
+    reference counts. Integer bookkeeping only; the page data is a numpy
+    array that grows like the reference's Vec<Vec<f32>>."""
+
+    def __init__(self, cfg, max_sequences):  # :215-238
+        self.kv_dim = cfg.n_kv_head * cfg.head_dim
+        self.n_layer = cfg.n_layer
+        initial = (cfg.block_size // PAGE_SIZE + 1) * cfg.n_layer
+        self.pages = np.zeros((initial, 2, PAGE_SIZE, self.kv_dim), np.float32)
+        self.layer_page_tables = [[[] for _ in range(max_sequences)] for _ in range(cfg.n_layer)]
+        self.free_pages = list(range(initial))
+        self.page_ref_counts = [0] * initial
+        self.total_pages = initial
+
+    def _alloc_page(self):  # :241-262
+        if self.free_pages:
+            idx = self.free_pages.pop()
+            self.pages[idx] = 0.0
+        else:
+            self.pages = np.concatenate([self.pages, np.zeros((1, 2, PAGE_SIZE, self.kv_dim), np.float32)])
+            idx = self.total_pages
+            self.total_pages += 1
+            self.page_ref_counts.append(0)
+        self.page_ref_counts[idx] += 1
+        return idx
+
+    def ensure_pages(self, seq, pos):  # :268-296
+        need = pos // PAGE_SIZE + 1
+        for tables in self.layer_page_tables:
+            while seq >= len(tables):
+                tables.append([])
+        deficits = [max(0, need - len(t[seq])) for t in self.layer_page_tables]
+        new = [[self._alloc_page() for _ in range(df)] for df in deficits]
+        for tables, pages in zip(self.layer_page_tables, new):
+            tables[seq].extend(pages)
+
+    def write_kv(self, layer, seq, pos, k, v):  # :298-309
+        pg = self.layer_page_tables[layer][seq][pos // PAGE_SIZE]
+        self.pages[pg, 0, pos % PAGE_SIZE] = k
+        self.pages[pg, 1, pos % PAGE_SIZE] = v
+
+    def read_kv(self, layer, seq, pos):  # :312-329
+        pg = self.layer_page_tables[layer][seq][pos // PAGE_SIZE]
+        return self.pages[pg, 0, pos % PAGE_SIZE].copy(), self.pages[pg, 1, pos % PAGE_SIZE].copy()
+
+    def fork(self, seq, fork_at_pos):  # :334-350
+        fork_page = fork_at_pos // PAGE_SIZE
+        new_seq = len(self.layer_page_tables[0])
+        for tables in self.layer_page_tables:
+            shared = tables[seq][:min(fork_page, len(tables[seq]))]
+            for pg in shared:
+                self.page_ref_counts[pg] += 1
+            tables.append(list(shared))
+        return new_seq
+
+    def rollback(self, seq, pos):  # :360-378
+        keep = pos // PAGE_SIZE
+        for tables in self.layer_page_tables:
+            if seq >= len(tables):
+                continue
+            removed = tables[seq][keep:]
+            del tables[seq][keep:]
+            for pg in removed:
+                self.page_ref_counts[pg] -= 1
+                if self.page_ref_counts[pg] == 0:
+                    self.free_pages.append(pg)
+
+    def reset(self):  # :381-390
+        for tables in self.layer_page_tables:
+            for t in tables:
+                self.free_pages.extend(t)
+                t.clear()
+        self.page_ref_counts = [0] * len(self.page_ref_counts)
+
+    def table(self, seq, maxp):
+        """The sequence's page lists as an int64 [n_layer][maxp] array (-1 past the end)."""
+        out = np.full((self.n_layer, maxp), -1, np.int64)
+        for l, tables in enumerate(self.layer_page_tables):
+            t = tables[seq] if seq < len(tables) else []
+            out[l, :len(t)] = t
+        return out
+
+
+def forward_paged(cfg, w, cache, seq, token, pos):
+    """transformer::forward_paged (src/transformer.rs:3305-3504) of one token:
+    ensure_pages, then the forward over `cache`'s pages; returns the logits."""
+    cache.ensure_pages(seq, pos)
+    maxp = max(len(t[seq]) for t in cache.layer_page_tables)
+    tab = cache.table(seq, maxp)
+    logits = np.empty(cfg.vocab_size, np.float32)
+    rc = lib().or_forward_paged(ctypes.byref(cfg), _p(f32(w)), _p(cache.pages), _p(tab), maxp, token, pos,
+                                _p(logits))
+    if rc:
+        raise RuntimeError(f"or_forward_paged failed: {rc}")
+    return logits
