@@ -49,8 +49,10 @@ typedef enum {
     KG_KV_F32 = 0,     /* transformer::forward -> forward_base, f32 KV (src/transformer.rs:398-429,1821-2200) */
     KG_KV_TQ = 1,      /* transformer::forward_quantized<TurboQuantKVCache> (src/transformer.rs:4042-4233) */
     KG_KV_SPKV_TQ = 2, /* sp_kv::forward::forward_sp_kv_quant, SpKvGateMode::Hard (src/sp_kv/forward.rs:610-822) */
-    KG_KV_PAGED = 3    /* transformer::forward_paged over a PagedKVCache (src/transformer.rs:3305-3504,
+    KG_KV_PAGED = 3,   /* transformer::forward_paged over a PagedKVCache (src/transformer.rs:3305-3504,
                           crates/katgpt-transformer/src/kv_cache.rs:187-420); see the paged section */
+    KG_KV_SQ = 4       /* transformer::forward_quantized<SpectralQuantKVCache> (src/transformer.rs:4042-4233,
+                          src/spectralquant/spectral_kv_cache.rs); see the SpectralQuant section */
 } kg_kv_mode;
 
 typedef enum {
@@ -304,6 +306,61 @@ int kg_paged_table(const kg_ctx *ctx, int32_t layer, int32_t seq, int32_t *pages
  * NULL) page_ref_counts[0 .. min(total_pages, refs_cap)). */
 int kg_paged_stats(const kg_ctx *ctx, int64_t *total_pages, int64_t *free_pages, int32_t *n_sequences,
                    int32_t *refs, int64_t refs_cap);
+
+/* ---- SpectralQuant (contexts with kv_mode KG_KV_SQ) ----
+ * The calibrated-eigenbasis KV codec (src/spectralquant/): each K/V vector is
+ * normalised, rotated by the layer's eigenvectors (V^T x), quantized per
+ * dimension with Lloyd-Max codebooks (b_high bits on the first d_eff
+ * "semantic" dimensions, or water-filled widths, b_low on the tail), and
+ * packed LSB-first at those widths; keys and values share the layer's tables,
+ * as the reference does. kg_kv_codes returns the pack at the front of a
+ * kv_dim-byte row. A KG_KV_SQ context needs one of the two calibration calls
+ * before its first forward (KG_ERR_NOT_COMPILED otherwise). Micro widths
+ * (Config::micro()); codebooks of at most 64 centroids (6 bits) per dimension. */
+
+/* SpectralQuantKVCacheConfig (src/spectralquant/types.rs:97-126), the fields
+ * the codec build reads. */
+typedef struct {
+    uint64_t seed;
+    int32_t lloyd_max_iter;
+    int32_t calibration_samples;
+    float avg_bits;
+    int32_t min_tail_bits;
+    int32_t max_bits;
+    int32_t wf_min_bits;
+    int32_t wf_max_bits;
+    int32_t use_water_fill;
+} kg_sq_params;
+
+/* The reference's test configuration (spectral_kv_cache.rs:1214-1234): seed
+ * 42, 30 Lloyd-Max iterations, 100 calibration samples, 3 bits on average,
+ * tail >= 1, at most 8, water-fill off (1..6 when on). */
+void kg_sq_params_default(kg_sq_params *p);
+/* SpectralQuantKVCache::from_keys (spectral_kv_cache.rs:349-385): calibrate
+ * the eigenbasis from key_samples [n_samples][kv_dim] (calibrate_eigenbasis,
+ * spectral.rs:226-278) and build every layer's tables from it. */
+int kg_sq_calibrate(kg_ctx *ctx, const kg_sq_params *p, const float *key_samples, int64_t n_samples);
+/* SpectralQuantKVCache::from_calibration (spectral_kv_cache.rs:99-347): per
+ * layer calibrations, eigenvectors [n_layer][kv_dim*kv_dim] (row-major,
+ * columns = eigenvectors; an identity matrix selects a seeded random
+ * rotation), eigenvalues [n_layer][kv_dim], d_eff [n_layer]. */
+int kg_sq_calibrate_from(kg_ctx *ctx, const kg_sq_params *p, const float *eigenvectors, const float *eigenvalues,
+                         const float *d_eff);
+/* Host-only forms (no context, no device): calibrate_eigenbasis of samples
+ * [n_samples][dim] (eigenvectors [dim*dim], eigenvalues [dim], d_eff), and the
+ * tables kg_sq_calibrate_from would install for n_layers calibrations (outputs
+ * laid out as kg_sq_tables, one layer after another), e.g. to store them with
+ * a model. KG_ERR_UNSUPPORTED when a codebook exceeds 64 centroids. */
+int kg_sq_calibrate_eigenbasis(const float *samples, int64_t n_samples, int64_t dim, float *eigenvectors,
+                               float *eigenvalues, float *d_eff);
+int kg_sq_build_tables(const kg_sq_params *p, int64_t kv_dim, int32_t n_layers, const float *eigenvectors,
+                       const float *eigenvalues, const float *d_eff, float *eig_out, uint8_t *bits_out,
+                       float *centroids_out, int32_t *n_levels_out, int32_t *d_eff_out);
+/* One layer's tables as the device holds them: eigenvectors [kv_dim*kv_dim],
+ * bits [kv_dim], centroids [kv_dim][64] (dimension j's codebook first
+ * n_levels[j] entries), n_levels [kv_dim], d_eff. Any pointer may be NULL. */
+int kg_sq_tables(const kg_ctx *ctx, int32_t layer, float *eigenvectors, uint8_t *bits, float *centroids,
+                 int32_t *n_levels, int32_t *d_eff);
 
 /* ---- TurboQuant codec access (parity / inspection) ---- */
 

@@ -25,6 +25,11 @@ void predictor_weights(int64_t n, int64_t hidden, int64_t nkv, float init_bias, 
 cudaError_t paged_alloc(kg_ctx *ctx);
 cudaError_t paged_flush(kg_ctx *ctx, cudaStream_t s);
 int paged_ensure_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *start_pos, int32_t T);
+void sq_calibrate(const float *samples, int64_t n, int64_t dim, std::vector<float> &vecs, std::vector<float> &vals,
+                  float &d_eff);
+bool sq_build_layer(const kg_sq_params &P, int64_t kvd, int64_t layer, const float *eig, const float *eval,
+                    float d_eff_in, float *eig_out, uint8_t *bits_out, float *cent_out, int32_t *lev_out,
+                    int32_t *d_eff_out);
 }  // namespace kg
 
 namespace {
@@ -85,7 +90,7 @@ int validate(const kg_config *c, std::string &why) {
     if ((int64_t)c->n_head * c->head_dim != c->n_embd) return why = "n_head*head_dim != n_embd", -1;
     if (c->n_head % c->n_kv_head) return why = "n_head not a multiple of n_kv_head", -1;
     if (c->max_seqs <= 0) return why = "max_seqs must be positive", -1;
-    if (c->kv_mode < KG_KV_F32 || c->kv_mode > KG_KV_PAGED) return why = "bad kv_mode", -1;
+    if (c->kv_mode < KG_KV_F32 || c->kv_mode > KG_KV_SQ) return why = "bad kv_mode", -1;
     if (kg::kv_is_tq(c->kv_mode)) {
         for (int b : {c->key_bits, c->val_bits})
             if (b < 2 || b > 8) return why = "TurboQuant bits must be in [2, 8]", -1;
@@ -210,11 +215,14 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     ctx->L = c.n_layer; ctx->B = c.block_size;
     ctx->w_count = kg::weights_count(c);
     const bool tq = kg::kv_is_tq(c.kv_mode);
-    const bool paged = c.kv_mode == KG_KV_PAGED;
+    const bool paged = c.kv_mode == KG_KV_PAGED, sqm = c.kv_mode == KG_KV_SQ;
     if (paged && !ctx->micro)
         return bail(fail(ctx, KG_ERR_UNSUPPORTED, "forward_paged runs the micro widths at block_size 16 or 64"));
+    if (sqm && !ctx->micro)
+        return bail(fail(ctx, KG_ERR_UNSUPPORTED, "the SpectralQuant codec runs the micro widths (Config::micro())"));
     ctx->kpl = tq ? packed_len(ctx->kvd, c.key_bits) : 0;
     ctx->vpl = tq ? packed_len(ctx->kvd, c.val_bits) : 0;
+    if (sqm) ctx->kpl = ctx->vpl = ctx->kvd;  // variable-width pack, at most one byte per dimension
     ctx->ph = std::max<int64_t>(ctx->n / 4, 16);
 
     // ---- KV arena (exact micro path: f32 K/V or dequantized cache + codes)
@@ -300,6 +308,9 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     a.off_pb1 = (int)off; off += ctx->ph;
     a.off_pw2 = (int)off; off += ctx->nkv * ctx->ph;
     a.off_pb2 = (int)off; off += ctx->nkv;
+    a.off_sq_eig = (int)off; off += sqm ? L * kvd * kvd : 0;
+    a.off_sq_cent = (int)off; off += sqm ? L * kvd * kg::kSqLevels : 0;
+    a.off_sq_meta = (int)off; off += sqm ? L * kvd : 0;
     off = (off + 3) / 4 * 4;
     ctx->pack_floats = off;
     if (off * 4 > 200 * 1024) return bail(fail(ctx, KG_ERR_UNSUPPORTED, "micro weights exceed shared memory"));
@@ -564,6 +575,8 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
         KG_CUDA(ctx, e);
         return KG_OK;
     }
+    if (ctx->cfg.kv_mode == KG_KV_SQ && !ctx->sq_ready)
+        return fail(ctx, KG_ERR_NOT_COMPILED, "SpectralQuant tables not built (kg_sq_calibrate / kg_sq_calibrate_from)");
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     kg::MicroArgs a = ctx->margs;
     a.n_seq = n_seq;
@@ -798,7 +811,7 @@ int kg_kv_codes(kg_ctx *ctx, int32_t seq, int32_t layer, int32_t pos, uint8_t *k
         return KG_OK;
     }
     if (!ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "no KV arena for this model shape");
-    if (!kg::kv_is_tq(ctx->cfg.kv_mode)) return fail(ctx, KG_ERR_INVALID_ARG, "context has no TurboQuant codec");
+    if (!kg::kv_has_codes(ctx->cfg.kv_mode)) return fail(ctx, KG_ERR_INVALID_ARG, "context has no KV codec");
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const int64_t row = ((int64_t)seq * ctx->L + layer) * ctx->B + pos;
     cudaStream_t s = ctx->stream;
@@ -979,5 +992,112 @@ int kg_set_mlp_hook(kg_ctx *ctx, float keep, uint64_t seed) {
     ctx->graphs.clear();
     ctx->hook_keep = keep > 0.0f ? std::min(keep, 1.0f) : 0.0f;
     ctx->hook_seed = seed;
+    return KG_OK;
+}
+
+// ---- SpectralQuant calibration (kg_sq.cpp builds the tables on the host) ----
+
+namespace {
+int sq_install(kg_ctx *ctx, const kg_sq_params *p, const float *eig, const float *eval, const float *deff,
+               bool per_layer) {
+    const int64_t kvd = ctx->kvd, L = ctx->L;
+    std::vector<float> E(L * kvd * kvd), C(L * kvd * kg::kSqLevels), meta(L * kvd);
+    std::vector<uint8_t> bits(L * kvd);
+    std::vector<int32_t> lev(L * kvd), de(L);
+    for (int64_t l = 0; l < L; ++l) {
+        const int64_t o = per_layer ? l : 0;
+        if (!kg::sq_build_layer(*p, kvd, l, eig + o * kvd * kvd, eval + o * kvd, deff[o], &E[l * kvd * kvd],
+                                &bits[l * kvd], &C[l * kvd * kg::kSqLevels], &lev[l * kvd], &de[l]))
+            return fail(ctx, KG_ERR_UNSUPPORTED, "SpectralQuant codebook wider than 64 centroids (6 bits)");
+        for (int64_t j = 0; j < kvd; ++j) {
+            const int32_t m = (int32_t)bits[l * kvd + j] | (lev[l * kvd + j] << 8);
+            std::memcpy(&meta[l * kvd + j], &m, 4);
+        }
+    }
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const kg::MicroArgs &a = ctx->margs;
+    KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_eig, E.data(), E.size() * 4, cudaMemcpyHostToDevice));
+    KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_cent, C.data(), C.size() * 4, cudaMemcpyHostToDevice));
+    KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice));
+    ctx->h_sq_eig = std::move(E);
+    ctx->h_sq_cent = std::move(C);
+    ctx->h_sq_bits = std::move(bits);
+    ctx->h_sq_lev = std::move(lev);
+    ctx->h_sq_deff = std::move(de);
+    ctx->sq_ready = true;
+    return KG_OK;
+}
+int sq_check(kg_ctx *ctx, const kg_sq_params *p) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (ctx->cfg.kv_mode != KG_KV_SQ || !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "context is not kv_mode KG_KV_SQ");
+    if (!p || p->max_bits < 1 || p->max_bits > 8 || p->lloyd_max_iter < 0 || p->wf_min_bits < 1 ||
+        p->wf_max_bits < p->wf_min_bits || p->wf_max_bits > 8)
+        return fail(ctx, KG_ERR_INVALID_ARG, "bad SpectralQuant parameters");
+    return KG_OK;
+}
+}  // namespace
+
+void kg_sq_params_default(kg_sq_params *p) {
+    if (!p) return;
+    p->seed = 42;
+    p->lloyd_max_iter = 30;
+    p->calibration_samples = 100;
+    p->avg_bits = 3.0f;
+    p->min_tail_bits = 1;
+    p->max_bits = 8;
+    p->wf_min_bits = 1;
+    p->wf_max_bits = 6;
+    p->use_water_fill = 0;
+}
+
+int kg_sq_calibrate(kg_ctx *ctx, const kg_sq_params *p, const float *key_samples, int64_t n_samples) {
+    if (int rc = sq_check(ctx, p)) return rc;
+    if (!key_samples || n_samples < 1) return fail(ctx, KG_ERR_INVALID_ARG, "need at least one calibration sample");
+    std::vector<float> vecs, vals;
+    float d_eff = 0.0f;
+    kg::sq_calibrate(key_samples, n_samples, ctx->kvd, vecs, vals, d_eff);
+    return sq_install(ctx, p, vecs.data(), vals.data(), &d_eff, false);
+}
+
+int kg_sq_calibrate_from(kg_ctx *ctx, const kg_sq_params *p, const float *eigenvectors, const float *eigenvalues,
+                         const float *d_eff) {
+    if (int rc = sq_check(ctx, p)) return rc;
+    if (!eigenvectors || !eigenvalues || !d_eff) return fail(ctx, KG_ERR_INVALID_ARG, "null calibration");
+    return sq_install(ctx, p, eigenvectors, eigenvalues, d_eff, true);
+}
+
+int kg_sq_tables(const kg_ctx *ctx, int32_t layer, float *eig, uint8_t *bits, float *cent, int32_t *lev,
+                 int32_t *d_eff) {
+    if (!ctx || !ctx->sq_ready || layer < 0 || layer >= ctx->L) return KG_ERR_INVALID_ARG;
+    const int64_t kvd = ctx->kvd;
+    if (eig) std::memcpy(eig, &ctx->h_sq_eig[layer * kvd * kvd], kvd * kvd * 4);
+    if (bits) std::memcpy(bits, &ctx->h_sq_bits[layer * kvd], kvd);
+    if (cent) std::memcpy(cent, &ctx->h_sq_cent[layer * kvd * kg::kSqLevels], kvd * kg::kSqLevels * 4);
+    if (lev) std::memcpy(lev, &ctx->h_sq_lev[layer * kvd], kvd * 4);
+    if (d_eff) *d_eff = ctx->h_sq_deff[layer];
+    return KG_OK;
+}
+
+int kg_sq_calibrate_eigenbasis(const float *samples, int64_t n_samples, int64_t dim, float *eigenvectors,
+                               float *eigenvalues, float *d_eff) {
+    if (!samples || n_samples < 1 || dim < 2 || !eigenvectors || !eigenvalues || !d_eff) return KG_ERR_INVALID_ARG;
+    std::vector<float> vecs, vals;
+    kg::sq_calibrate(samples, n_samples, dim, vecs, vals, *d_eff);
+    std::memcpy(eigenvectors, vecs.data(), dim * dim * 4);
+    std::memcpy(eigenvalues, vals.data(), dim * 4);
+    return KG_OK;
+}
+
+int kg_sq_build_tables(const kg_sq_params *p, int64_t kv_dim, int32_t n_layers, const float *eigenvectors,
+                       const float *eigenvalues, const float *d_eff, float *eig_out, uint8_t *bits_out,
+                       float *centroids_out, int32_t *n_levels_out, int32_t *d_eff_out) {
+    if (!p || kv_dim < 2 || n_layers < 1 || !eigenvectors || !eigenvalues || !d_eff || !eig_out || !bits_out ||
+        !centroids_out || !n_levels_out || !d_eff_out || p->max_bits < 1 || p->max_bits > 8)
+        return KG_ERR_INVALID_ARG;
+    for (int32_t l = 0; l < n_layers; ++l)
+        if (!kg::sq_build_layer(*p, kv_dim, l, eigenvectors + l * kv_dim * kv_dim, eigenvalues + l * kv_dim, d_eff[l],
+                                eig_out + l * kv_dim * kv_dim, bits_out + l * kv_dim,
+                                centroids_out + l * kv_dim * kg::kSqLevels, n_levels_out + l * kv_dim, d_eff_out + l))
+            return KG_ERR_UNSUPPORTED;
     return KG_OK;
 }

@@ -22,6 +22,7 @@ struct MicroArgs {
     int off_wte, off_wpe, off_layers, layer_stride, off_lm, off_dq, off_dn, off_ag, off_mg;
     int off_rot, off_rot_t, off_kc, off_kb, off_vc, off_vb;
     int off_pw1, off_pb1, off_pw2, off_pb2;
+    int off_sq_eig, off_sq_cent, off_sq_meta;  // SpectralQuant: [L][kvd*kvd], [L][kvd][64], [L][kvd] (bits | levels << 8)
     int L;
     int kbits, vbits, kpl, vpl;
     float sparse_threshold, inv_temp;
@@ -43,6 +44,9 @@ struct MicroArgs {
 };
 
 inline bool kv_is_tq(int kv_mode) { return kv_mode == KG_KV_TQ || kv_mode == KG_KV_SPKV_TQ; }
+// modes that keep packed codes and norms per (layer, position)
+inline bool kv_has_codes(int kv_mode) { return kv_is_tq(kv_mode) || kv_mode == KG_KV_SQ; }
+constexpr int kSqLevels = 64;  // centroids per dimension in the SpectralQuant tables
 
 // PagedKVCache bookkeeping (crates/katgpt-transformer/src/kv_cache.rs:187-420)
 // on the host, pages in a device pool.
@@ -226,6 +230,11 @@ struct kg_ctx {
     int64_t verify_rows = 0;
     // kv_mode KG_KV_PAGED: PagedKVCache state (kg_paged.cu)
     kg::PagedState paged;
+    // kv_mode KG_KV_SQ: host copies of the SpectralQuant tables (kg_sq.cpp), set by calibration
+    bool sq_ready = false;
+    std::vector<float> h_sq_eig, h_sq_cent;
+    std::vector<uint8_t> h_sq_bits;
+    std::vector<int32_t> h_sq_lev, h_sq_deff;
 };
 
 namespace kg {

@@ -32,7 +32,7 @@
 namespace kg {
 namespace {
 
-constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2, MODE_PREFILL = 3, MODE_PAGED = 4;
+constexpr int MODE_BASE = 0, MODE_QUANT = 1, MODE_SPKV = 2, MODE_PREFILL = 3, MODE_PAGED = 4, MODE_SQ = 5;
 
 template <int KVD>
 __device__ __forceinline__ uint8_t quantize(float r, const float *bnd, int nb) {
@@ -93,6 +93,75 @@ __device__ __forceinline__ void tq_roundtrip(const float (&vec)[KVD], const floa
     for (int i = 0; i < KVD; ++i) c[i] = cent[cd[i]];
 #pragma unroll
     for (int i = 0; i < KVD; ++i) deq[i] = kgx::dot<KVD>(rot_t + i * KVD, c) * norm;
+}
+
+// SpectralQuantKVCache store_vector then dequantize_*_into for one vector
+// (src/spectralquant/spectral_kv_cache.rs:399-470, 567-672): norm, x / norm,
+// rotation y_j = sum_i V[i][j] x_i accumulated in i order (rotate_into), per
+// dimension the nearest centroid by bisection (quantize_to_idx), LSB-first
+// packing at the dimension's width; then centroids, V c (row dots) and * norm.
+// A vector with norm < 1e-8 stores norm 0 and keeps its old codes.
+// meta[j] = bits | levels << 8; cent: 64 centroids per dimension.
+template <int KVD>
+__device__ __forceinline__ void sq_roundtrip(const float (&vec)[KVD], const float *eig, const float *cent,
+                                             const float *meta, uint8_t *codes, float *norm_out, float (&deq)[KVD]) {
+    const float norm = sqrtf(kgx::sum_sq<KVD>(vec));
+    if (norm < 1e-8f) {
+        *norm_out = 0.0f;
+#pragma unroll
+        for (int i = 0; i < KVD; ++i) deq[i] = 0.0f;
+        return;
+    }
+    *norm_out = norm;
+    const float inv = 1.0f / norm;
+    float xn[KVD], y[KVD];
+#pragma unroll
+    for (int i = 0; i < KVD; ++i) xn[i] = vec[i] * inv;
+#pragma unroll
+    for (int j = 0; j < KVD; ++j) y[j] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < KVD; ++i)
+#pragma unroll
+        for (int j = 0; j < KVD; ++j) y[j] = y[j] + eig[i * KVD + j] * xn[i];
+    uint8_t idx[KVD];
+    uint64_t buf = 0;
+    uint32_t have = 0;
+    int w = 0;
+#pragma unroll
+    for (int j = 0; j < KVD; ++j) {
+        const int m = __float_as_int(meta[j]);
+        const int bits = m & 255, n = m >> 8;
+        const float *c = cent + j * kSqLevels;
+        int q = 0;
+        if (n > 1) {
+            int lo = 0, hi = n - 1;
+            const float v = y[j];
+            if (v <= c[lo]) q = lo;
+            else if (v >= c[hi]) q = hi;
+            else {
+                while (lo + 1 < hi) {
+                    const int mid = lo + (hi - lo) / 2;
+                    if (c[mid] <= v) lo = mid;
+                    else hi = mid;
+                }
+                q = fabsf(v - c[lo]) <= fabsf(c[hi] - v) ? lo : hi;
+            }
+        }
+        idx[j] = (uint8_t)q;
+        buf |= (uint64_t)q << have;  // pack_variable_bits (:1125-1164)
+        have += bits;
+        while (have >= 8) {
+            codes[w++] = (uint8_t)(buf & 0xFF);
+            buf >>= 8;
+            have -= 8;
+        }
+    }
+    if (have > 0) codes[w++] = (uint8_t)(buf & 0xFF);
+    float cv[KVD];
+#pragma unroll
+    for (int j = 0; j < KVD; ++j) cv[j] = idx[j] < (__float_as_int(meta[j]) >> 8) ? cent[j * kSqLevels + idx[j]] : 0.0f;
+#pragma unroll
+    for (int i = 0; i < KVD; ++i) deq[i] = kgx::dot<KVD>(eig + i * KVD, cv) * norm;
 }
 
 // rmsnorm (math.rs:56-69): x * (1 / sqrt(sum_sq/n + 1e-5))
@@ -290,6 +359,19 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
                 for (int j = 0; j < KVD; ++j) {
                     kd[j] = k[j];
                     vd[j] = v[j];
+                }
+            } else if constexpr (MODE == MODE_SQ) {
+                uint8_t *cb = p.codes + (row + pos) * (p.kpl + p.vpl);
+                float *nb = p.norms + (row + pos) * 2;
+                const float *eig = sm + p.off_sq_eig + l * KVD * KVD, *cent = sm + p.off_sq_cent + l * KVD * kSqLevels;
+                const float *meta = sm + p.off_sq_meta + l * KVD;
+                float dk[KVD], dv[KVD];
+                sq_roundtrip<KVD>(k, eig, cent, meta, cb, nb, dk);  // keys and values share the layer's tables
+                sq_roundtrip<KVD>(v, eig, cent, meta, cb + p.kpl, nb + 1, dv);
+#pragma unroll
+                for (int j = 0; j < KVD; ++j) {
+                    kd[j] = dk[j];
+                    vd[j] = dv[j];
                 }
             } else {
                 uint8_t *cb = p.codes + (row + pos) * (p.kpl + p.vpl);
@@ -598,6 +680,7 @@ cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s)
         case KG_KV_SPKV_TQ: return launch_mode<MODE_SPKV>(a, s);
         case KG_KV_PAGED:
             return c.block_size == 64 ? launch_mode<MODE_PAGED, 64>(a, s) : launch_mode<MODE_PAGED, 16>(a, s);
+        case KG_KV_SQ: return launch_mode<MODE_SQ>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

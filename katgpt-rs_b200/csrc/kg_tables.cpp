@@ -45,6 +45,22 @@ struct HostRng {
     }
 };
 
+uint64_t host_rng_seed_state(uint64_t seed) { return HostRng(seed).s; }
+uint64_t host_rng_next_state(uint64_t &state) {
+    HostRng r(0);
+    r.s = state;
+    const uint64_t v = r.next();
+    state = r.s;
+    return v;
+}
+float host_rng_normal(uint64_t &state) {
+    HostRng r(0);
+    r.s = state;
+    const float v = r.normal();
+    state = r.s;
+    return v;
+}
+
 void host_normals(uint64_t seed, int64_t n, float *out) {
     HostRng r(seed);
     for (int64_t i = 0; i < n; ++i) out[i] = r.normal();

@@ -14,7 +14,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIBPATH = os.path.join(HERE, "lib", "libkgcuda.so")
 
-KG_KV_F32, KG_KV_TQ, KG_KV_SPKV_TQ, KG_KV_PAGED = 0, 1, 2, 3
+KG_KV_F32, KG_KV_TQ, KG_KV_SPKV_TQ, KG_KV_PAGED, KG_KV_SQ = 0, 1, 2, 3, 4
 KG_W_F32, KG_W_BF16 = 0, 1
 
 STATUS = {0: "ok", -1: "invalid argument", -2: "device out of memory", -3: "CUDA error",
@@ -39,6 +39,18 @@ class KgConfig(ctypes.Structure):
 
     def kvd(self):
         return self.n_kv_head * self.head_dim
+
+
+class KgSqParams(ctypes.Structure):
+    """Mirror of kg_sq_params (SpectralQuantKVCacheConfig fields, include/kg_abi.h)."""
+    _fields_ = [("seed", ctypes.c_uint64), ("lloyd_max_iter", ctypes.c_int32),
+                ("calibration_samples", ctypes.c_int32), ("avg_bits", ctypes.c_float),
+                ("min_tail_bits", ctypes.c_int32), ("max_bits", ctypes.c_int32),
+                ("wf_min_bits", ctypes.c_int32), ("wf_max_bits", ctypes.c_int32),
+                ("use_water_fill", ctypes.c_int32)]
+
+
+SQ_LEVELS = 64
 
 
 class KgError(RuntimeError):
@@ -105,6 +117,12 @@ def lib():
             "kg_comm_init": (ctypes.c_int, [P, P, I32, I32]),
             "kg_comm_destroy": (ctypes.c_int, [P]),
             "kg_decode_gather_dev": (ctypes.c_int, [P, I32, P, P, P, P, P, P]),
+            "kg_sq_params_default": (None, [ctypes.POINTER(KgSqParams)]),
+            "kg_sq_calibrate": (ctypes.c_int, [P, ctypes.POINTER(KgSqParams), P, I64]),
+            "kg_sq_calibrate_from": (ctypes.c_int, [P, ctypes.POINTER(KgSqParams), P, P, P]),
+            "kg_sq_tables": (ctypes.c_int, [P, I32, P, P, P, P, P]),
+            "kg_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
+            "kg_sq_build_tables": (ctypes.c_int, [ctypes.POINTER(KgSqParams), I64, I32, P, P, P, P, P, P, P, P]),
             "kg_paged_init": (ctypes.c_int, [P, I32]),
             "kg_paged_ensure": (ctypes.c_int, [P, I32, I32]),
             "kg_paged_fork": (ctypes.c_int, [P, I32, I32, P]),
@@ -284,8 +302,9 @@ class CudaBackend:
 
     def kv_codes(self, seq, layer, pos):
         kvd = self.cfg.kvd()
-        kp = np.empty(lib().kg_tq_packed_len(kvd, self.cfg.key_bits), np.uint8)
-        vp = np.empty(lib().kg_tq_packed_len(kvd, self.cfg.val_bits), np.uint8)
+        sq = self.cfg.kv_mode == KG_KV_SQ  # SpectralQuant: kv_dim-byte rows, the pack in front
+        kp = np.empty(kvd if sq else lib().kg_tq_packed_len(kvd, self.cfg.key_bits), np.uint8)
+        vp = np.empty(kvd if sq else lib().kg_tq_packed_len(kvd, self.cfg.val_bits), np.uint8)
         nr = np.empty(2, np.float32)
         self._check(lib().kg_kv_codes(self._h, seq, layer, pos, _ptr(kp), _ptr(vp), _ptr(nr)))
         return kp, vp, nr
@@ -434,3 +453,69 @@ class CudaBackend:
         refs = np.zeros(tot.value, np.int32)
         self._check(lib().kg_paged_stats(self._h, None, None, None, _ptr(refs), tot.value))
         return tot.value, free.value, ns.value, [int(r) for r in refs]
+
+    # ---- SpectralQuant (kv_mode KG_KV_SQ; src/spectralquant/)
+
+    def sq_calibrate(self, key_samples, params=None):
+        """SpectralQuantKVCache::from_keys on key_samples [n][kv_dim]."""
+        x = np.ascontiguousarray(key_samples, np.float32)
+        p = params or sq_params()
+        self._check(lib().kg_sq_calibrate(self._h, ctypes.byref(p), _ptr(x), x.shape[0]))
+
+    def sq_calibrate_from(self, eigenvectors, eigenvalues, d_eff, params=None):
+        """SpectralQuantKVCache::from_calibration: per layer [L][kvd*kvd], [L][kvd], [L]."""
+        e = np.ascontiguousarray(eigenvectors, np.float32)
+        v = np.ascontiguousarray(eigenvalues, np.float32)
+        d = np.ascontiguousarray(d_eff, np.float32)
+        p = params or sq_params()
+        self._check(lib().kg_sq_calibrate_from(self._h, ctypes.byref(p), _ptr(e), _ptr(v), _ptr(d)))
+
+    def sq_tables(self, layer):
+        """(eigenvectors [kvd*kvd], bits [kvd], centroids [kvd][64], n_levels [kvd], d_eff) of one layer."""
+        kvd = self.cfg.kvd()
+        e = np.empty(kvd * kvd, np.float32)
+        b = np.empty(kvd, np.uint8)
+        c = np.empty((kvd, SQ_LEVELS), np.float32)
+        n = np.empty(kvd, np.int32)
+        d = ctypes.c_int32(0)
+        self._check(lib().kg_sq_tables(self._h, layer, _ptr(e), _ptr(b), _ptr(c), _ptr(n), ctypes.byref(d)))
+        return e, b, c, n, d.value
+
+
+def sq_params(**kw):
+    """kg_sq_params_default (the reference's test configuration) with overrides."""
+    p = KgSqParams()
+    lib().kg_sq_params_default(ctypes.byref(p))
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+def sq_calibrate_eigenbasis(samples):
+    """kg_sq_calibrate_eigenbasis (host): (eigenvectors [dim*dim], eigenvalues [dim], d_eff)."""
+    x = np.ascontiguousarray(samples, np.float32)
+    n, dim = x.shape
+    vec = np.empty(dim * dim, np.float32)
+    val = np.empty(dim, np.float32)
+    de = ctypes.c_float(0)
+    rc = lib().kg_sq_calibrate_eigenbasis(_ptr(x), n, dim, _ptr(vec), _ptr(val), ctypes.byref(de))
+    if rc:
+        raise KgError(rc, "kg_sq_calibrate_eigenbasis")
+    return vec, val, de.value
+
+
+def sq_build_tables(params, kvd, eig, evals, d_eff):
+    """kg_sq_build_tables (host): dict of eig, bits, cent, nlev, d_eff per layer."""
+    eig = np.ascontiguousarray(eig, np.float32).reshape(-1, kvd * kvd)
+    L = eig.shape[0]
+    evals = np.ascontiguousarray(evals, np.float32).reshape(L, kvd)
+    d_eff = np.ascontiguousarray(d_eff, np.float32).reshape(L)
+    out = dict(eig=np.empty((L, kvd * kvd), np.float32), bits=np.empty((L, kvd), np.uint8),
+               cent=np.empty((L, kvd, SQ_LEVELS), np.float32), nlev=np.empty((L, kvd), np.int32),
+               d_eff=np.empty(L, np.int32))
+    rc = lib().kg_sq_build_tables(ctypes.byref(params), kvd, L, _ptr(eig), _ptr(evals), _ptr(d_eff),
+                                  _ptr(out["eig"]), _ptr(out["bits"]), _ptr(out["cent"]), _ptr(out["nlev"]),
+                                  _ptr(out["d_eff"]))
+    if rc:
+        raise KgError(rc, "kg_sq_build_tables")
+    return out

@@ -751,6 +751,355 @@ static void tq_dequant(const float *rot_t, const float *cent, int bits, int64_t 
     scale_inplace(out, dim, norm);
 }
 
+// ---- SpectralQuant (src/spectralquant/spectral.rs, spectral_kv_cache.rs) ----
+// Calibration (Jacobi eigenbasis of the sample covariance, participation
+// ratio), the per-layer build of SpectralQuantKVCache::from_calibration (bit
+// allocation, optional water-fill, identity -> random rotation, Lloyd-Max
+// codebooks fitted on synthetic rotated unit vectors) and the codec
+// (store_vector / dequantize_*_into). Tables use a fixed [kvd][64] centroid
+// layout: dimension j's codebook is cent[j*64 .. j*64 + nlev[j]).
+constexpr int kSqLevels = 64;
+
+// jacobi_eigendecompose (spectral.rs:73-158): at most 50 single rotations of
+// the largest off-diagonal element, f64, then a stable descending sort.
+static void sq_jacobi(const std::vector<double> &m, int64_t d, std::vector<float> &evals, std::vector<float> &evecs) {
+    std::vector<double> a = m, v(d * d, 0.0);
+    for (int64_t i = 0; i < d; ++i) v[i * d + i] = 1.0;
+    for (int sweep = 0; sweep < 50; ++sweep) {
+        double max_val = 0.0;
+        int64_t p = 0, q = 1;
+        for (int64_t i = 0; i < d; ++i)
+            for (int64_t j = i + 1; j < d; ++j) {
+                const double val = std::fabs(a[i * d + j]);
+                if (val > max_val) max_val = val, p = i, q = j;
+            }
+        if (max_val < 1e-10) break;
+        const double app = a[p * d + p], aqq = a[q * d + q], apq = a[p * d + q];
+        const double theta = 0.5 * std::atan2(2.0 * apq, app - aqq);
+        const double c = std::cos(theta), s = std::sin(theta);
+        for (int64_t i = 0; i < d; ++i) {
+            if (i == p || i == q) continue;
+            const double aip = a[i * d + p], aiq = a[i * d + q];
+            a[i * d + p] = c * aip + s * aiq;
+            a[p * d + i] = a[i * d + p];
+            a[i * d + q] = -s * aip + c * aiq;
+            a[q * d + i] = a[i * d + q];
+        }
+        const double npp = c * c * app + 2.0 * s * c * apq + s * s * aqq;
+        const double nqq = s * s * app - 2.0 * s * c * apq + c * c * aqq;
+        a[p * d + p] = npp;
+        a[q * d + q] = nqq;
+        a[p * d + q] = 0.0;
+        a[q * d + p] = 0.0;
+        for (int64_t i = 0; i < d; ++i) {
+            const double vip = v[i * d + p], viq = v[i * d + q];
+            v[i * d + p] = c * vip + s * viq;
+            v[i * d + q] = -s * vip + c * viq;
+        }
+    }
+    std::vector<float> ev(d), vec(d * d);
+    for (int64_t i = 0; i < d; ++i) ev[i] = (float)a[i * d + i];
+    for (int64_t i = 0; i < d * d; ++i) vec[i] = (float)v[i];
+    std::vector<int64_t> order(d);
+    for (int64_t i = 0; i < d; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int64_t x, int64_t y) { return ev[x] > ev[y]; });
+    evals.resize(d);
+    evecs.assign(d * d, 0.0f);
+    for (int64_t nc = 0; nc < d; ++nc) {
+        evals[nc] = ev[order[nc]];
+        for (int64_t r = 0; r < d; ++r) evecs[r * d + nc] = vec[r * d + order[nc]];
+    }
+}
+
+// participation_ratio (spectral.rs:11-24): (sum)^2 / sum of squares, f64 with mul_add.
+static float sq_participation_ratio(const float *ev, int64_t n) {
+    double sum = 0.0, sq = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        const double x = (double)ev[i];
+        sum += x;
+        sq = std::fma(x, x, sq);
+    }
+    if (sq < 1e-12) return 0.0f;
+    return (float)((sum * sum) / sq);
+}
+
+// slice::partition_point(|c| c < x), the binary search of Rust >= 1.82
+// (identical to any search when the centroids are sorted)
+static size_t sq_partition_point(const float *c, size_t n, float x) {
+    if (n == 0) return 0;
+    size_t base = 0, size = n;
+    while (size > 1) {
+        const size_t half = size / 2, mid = base + half;
+        if (c[mid] < x) base = mid;
+        size -= half;
+    }
+    return base + (c[base] < x ? 1 : 0);
+}
+
+// LloydMaxQuantizer::nearest_centroid (spectral.rs:711-733)
+static size_t sq_nearest(float x, const std::vector<float> &c) {
+    if (c.size() <= 1) return 0;
+    const size_t idx = sq_partition_point(c.data(), c.size(), x);
+    if (idx == 0) return 0;
+    if (idx >= c.size()) return c.size() - 1;
+    const float dl = std::fabs(x - c[idx - 1]), dr = std::fabs(c[idx] - x);
+    return dl <= dr ? idx - 1 : idx;
+}
+
+// LloydMaxQuantizer::fit (spectral.rs:523-589): quantile start, mean updates
+// in f64, empty cells reseeded from the data with Rng(seed), stop below 1e-6.
+static std::vector<float> sq_lloyd_fit(const std::vector<float> &data, int bits, int max_iter, uint64_t seed) {
+    const size_t nl = (size_t)1 << bits;
+    if (data.empty()) return std::vector<float>(nl, 0.0f);
+    std::vector<float> sorted = data;
+    std::stable_sort(sorted.begin(), sorted.end(), [](float x, float y) { return x < y; });
+    std::vector<float> c(nl);
+    for (size_t i = 0; i < nl; ++i) {
+        const float f = ((float)i + 0.5f) / (float)nl * (float)sorted.size();
+        size_t idx = f >= 1.8446744e19f ? SIZE_MAX : (f > 0.0f ? (size_t)f : 0);
+        c[i] = sorted[std::min(idx, sorted.size() - 1)];
+    }
+    Rng rng(seed);
+    for (int it = 0; it < max_iter; ++it) {
+        std::vector<double> sums(nl, 0.0);
+        std::vector<size_t> counts(nl, 0);
+        for (float x : data) {
+            const size_t k = sq_nearest(x, c);
+            sums[k] += (double)x;
+            counts[k] += 1;
+        }
+        std::vector<float> nc(nl);
+        for (size_t i = 0; i < nl; ++i)
+            nc[i] = counts[i] ? (float)(sums[i] / (double)counts[i]) : data[(size_t)(rng.next() % data.size())];
+        float md = 0.0f;
+        for (size_t i = 0; i < nl; ++i) md = fmax_rs(md, std::fabs(c[i] - nc[i]));
+        c = nc;
+        if (md < 1e-6f) break;
+    }
+    return c;
+}
+
+// waterfill_bits (spectral.rs:443-478): +1 bit at a time to the highest
+// lambda / 4^(b+1), lowest index on ties, capped at max_bits.
+static std::vector<uint8_t> sq_waterfill(const std::vector<double> &ev, size_t total, int min_bits, int max_bits) {
+    const size_t d = ev.size();
+    std::vector<uint8_t> bits(d, (uint8_t)min_bits);
+    size_t allocated = d * (size_t)min_bits;
+    while (allocated < total) {
+        size_t best = 0;
+        double best_gain = 0.0;
+        for (size_t i = 0; i < d; ++i) {
+            if (bits[i] >= max_bits) continue;
+            double p4 = 1.0;
+            for (int e = 0; e < bits[i] + 1; ++e) p4 *= 4.0;
+            const double gain = ev[i] / p4;
+            if (gain > best_gain || (gain == best_gain && i < best)) best_gain = gain, best = i;
+        }
+        if (best_gain <= 0.0) break;
+        bits[best] += 1;
+        allocated += 1;
+    }
+    return bits;
+}
+
+// generate_random_rotation (spectral_kv_cache.rs:1034-1077): Gram-Schmidt on
+// Rng(seed) normals, sequential f32 sums.
+static std::vector<float> sq_random_rotation(int64_t d, uint64_t seed) {
+    Rng rng(seed);
+    std::vector<float> m(d * d);
+    for (auto &x : m) x = rng.normal();
+    for (int64_t col = 0; col < d; ++col) {
+        for (int64_t prev = 0; prev < col; ++prev) {
+            float dot = 0.0f;
+            for (int64_t r = 0; r < d; ++r) dot += m[r * d + col] * m[r * d + prev];
+            for (int64_t r = 0; r < d; ++r) m[r * d + col] -= dot * m[r * d + prev];
+        }
+        float ns = 0.0f;
+        for (int64_t r = 0; r < d; ++r) ns += m[r * d + col] * m[r * d + col];
+        const float nrm = sqrtf(ns);
+        if (nrm > 1e-8f) {
+            const float inv = 1.0f / nrm;
+            for (int64_t r = 0; r < d; ++r) m[r * d + col] *= inv;
+        } else {
+            m[col * d + col] = 1.0f;
+        }
+    }
+    return m;
+}
+
+// rotate_into (spectral_kv_cache.rs:993-1005): out[j] = sum over i in order of V[i][j] * x[i]
+static void sq_rotate(const float *V, int64_t d, const float *x, float *out) {
+    for (int64_t j = 0; j < d; ++j) out[j] = 0.0f;
+    for (int64_t i = 0; i < d; ++i)
+        for (int64_t j = 0; j < d; ++j) out[j] += V[i * d + j] * x[i];
+}
+
+struct SqTab {
+    std::vector<float> eig;    // [kvd*kvd]
+    std::vector<uint8_t> bits;  // [kvd]
+    std::vector<int32_t> nlev;  // [kvd]
+    std::vector<float> cent;    // [kvd][kSqLevels]
+    int32_t d_eff = 0;
+};
+
+// One layer of SpectralQuantKVCache::from_calibration (spectral_kv_cache.rs:99-347).
+static int sq_build_layer(const or_sq_params &P, int64_t kvd, int64_t layer, const float *eig_in, const float *eval_in,
+                          float d_eff_f, SqTab &T) {
+    auto ceil_to_size = [](float f) -> size_t {  // `f.ceil() as usize` (saturating)
+        const float c = ceilf(f);
+        if (!(c > 0.0f)) return 0;
+        return c >= 1.8446744e19f ? SIZE_MAX : (size_t)c;
+    };
+    const size_t d_eff = std::min<size_t>(std::max<size_t>(ceil_to_size(d_eff_f), 1), (size_t)kvd);
+    // BitAllocator::allocate (spectral.rs:420-436)
+    float bl = roundf(P.avg_bits - (float)d_eff / (float)kvd);
+    bl = fmax_rs(bl, 1.0f);
+    bl = bl < (float)P.max_bits ? bl : (float)P.max_bits;
+    const int b_low = (int)bl;
+    const int b_high = std::min(b_low + 1, P.max_bits);
+    std::vector<uint8_t> sem_bits;
+    const bool wf = P.use_water_fill && b_high > 0;
+    if (wf) {
+        std::vector<double> ev(d_eff);
+        for (size_t i = 0; i < d_eff; ++i) ev[i] = (double)eval_in[i];
+        sem_bits = sq_waterfill(ev, (size_t)b_high * d_eff, P.wf_min_bits, P.wf_max_bits);
+    }
+    const int tail_bits = std::max(b_low, 1);
+    T.bits.assign(kvd, (uint8_t)tail_bits);
+    for (size_t i = 0; i < d_eff; ++i) T.bits[i] = wf ? sem_bits[i] : (uint8_t)b_high;
+    T.d_eff = (int32_t)d_eff;
+    T.eig.assign(eig_in, eig_in + kvd * kvd);
+    bool ident = true;
+    for (int64_t i = 0; i < kvd && ident; ++i)
+        for (int64_t j = 0; j < kvd; ++j)
+            if (std::fabs(T.eig[i * kvd + j] - (i == j ? 1.0f : 0.0f)) > 1e-4f) {
+                ident = false;
+                break;
+            }
+    if (ident) T.eig = sq_random_rotation(kvd, P.seed + (uint64_t)layer * 7919);
+    // synthetic unit vectors rotated by V^T
+    const size_t nsyn = std::max<size_t>((size_t)std::max(P.calibration_samples, 0), 256);
+    Rng rng(P.seed + (uint64_t)layer * 31);
+    std::vector<float> syn(nsyn * kvd), x(kvd);
+    for (size_t s = 0; s < nsyn; ++s) {
+        for (auto &v : x) v = rng.normal();
+        const float nrm = fmax_rs(sqrtf(sum_sq(x.data(), kvd)), 1e-8f);
+        scale_inplace(x.data(), kvd, 1.0f / nrm);
+        sq_rotate(T.eig.data(), kvd, x.data(), &syn[s * kvd]);
+    }
+    auto column_block = [&](size_t j0, size_t j1) {
+        std::vector<float> out;
+        out.reserve(nsyn * (j1 - j0));
+        for (size_t s = 0; s < nsyn; ++s)
+            for (size_t j = j0; j < j1; ++j) out.push_back(syn[s * kvd + j]);
+        return out;
+    };
+    T.nlev.assign(kvd, 0);
+    T.cent.assign(kvd * kSqLevels, 0.0f);
+    auto put = [&](size_t j, const std::vector<float> &c) {
+        if (c.size() > (size_t)kSqLevels) return false;
+        T.nlev[j] = (int32_t)c.size();
+        std::copy(c.begin(), c.end(), &T.cent[j * kSqLevels]);
+        return true;
+    };
+    const std::vector<float> tail = sq_lloyd_fit(column_block(d_eff, kvd), tail_bits, P.lloyd_max_iter,
+                                                 P.seed + (uint64_t)layer * 51 + 1);
+    for (size_t j = d_eff; j < (size_t)kvd; ++j)
+        if (!put(j, tail)) return -3;
+    if (!wf) {
+        const std::vector<float> sem = sq_lloyd_fit(column_block(0, d_eff), std::max(b_high, 1), P.lloyd_max_iter,
+                                                    P.seed + (uint64_t)layer * 51 + 2);
+        for (size_t j = 0; j < d_eff; ++j)
+            if (!put(j, sem)) return -3;
+    } else {
+        for (size_t j = 0; j < d_eff; ++j) {
+            const std::vector<float> cj = sq_lloyd_fit(column_block(j, j + 1), std::max<int>(sem_bits[j], 1),
+                                                       P.lloyd_max_iter, P.seed + (uint64_t)(j + 10));
+            if (!put(j, cj)) return -3;
+        }
+    }
+    return 0;
+}
+
+// quantize_to_idx (spectral_kv_cache.rs:1079-1111): nearest centroid by
+// bisection, ties to the lower index.
+static uint8_t sq_quantize(float v, const float *c, int n) {
+    if (n <= 1) return 0;
+    int lo = 0, hi = n - 1;
+    if (v <= c[lo]) return (uint8_t)lo;
+    if (v >= c[hi]) return (uint8_t)hi;
+    while (lo + 1 < hi) {
+        const int mid = lo + (hi - lo) / 2;
+        if (c[mid] <= v) lo = mid;
+        else hi = mid;
+    }
+    return std::fabs(v - c[lo]) <= std::fabs(c[hi] - v) ? (uint8_t)lo : (uint8_t)hi;
+}
+
+// pack_variable_bits (:1125-1164), LSB first; returns the byte count
+static int64_t sq_pack(const uint8_t *idx, const uint8_t *bits, int64_t n, uint8_t *out) {
+    uint64_t buf = 0;
+    uint32_t have = 0;
+    int64_t w = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        buf |= (uint64_t)idx[i] << have;
+        have += bits[i];
+        while (have >= 8) {
+            out[w++] = (uint8_t)(buf & 0xFF);
+            buf >>= 8;
+            have -= 8;
+        }
+    }
+    if (have > 0) out[w++] = (uint8_t)(buf & 0xFF);
+    return w;
+}
+
+// unpack_variable_bits (:1167-1187)
+static void sq_unpack(const uint8_t *p, int64_t plen, const uint8_t *bits, int64_t n, uint8_t *out) {
+    uint64_t buf = 0;
+    uint32_t have = 0;
+    int64_t b = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        while (have < bits[i] && b < plen) {
+            buf |= (uint64_t)p[b++] << have;
+            have += 8;
+        }
+        out[i] = (uint8_t)(buf & ((1ULL << bits[i]) - 1));
+        buf >>= bits[i];
+        have -= bits[i];
+    }
+}
+
+// store_vector (spectral_kv_cache.rs:399-470): zero-norm vectors store norm 0
+// and leave their codes as they were.
+static void sq_store(const SqTab &T, int64_t kvd, const float *x, uint8_t *packed, float *norm_out,
+                     std::vector<float> &xn, std::vector<float> &r, std::vector<uint8_t> &idx) {
+    const float nrm = sqrtf(sum_sq(x, kvd));
+    if (nrm < 1e-8f) {
+        *norm_out = 0.0f;
+        return;
+    }
+    *norm_out = nrm;
+    std::copy(x, x + kvd, xn.begin());
+    scale_inplace(xn.data(), kvd, 1.0f / nrm);
+    sq_rotate(T.eig.data(), kvd, xn.data(), r.data());
+    for (int64_t j = 0; j < kvd; ++j) idx[j] = sq_quantize(r[j], &T.cent[j * kSqLevels], T.nlev[j]);
+    sq_pack(idx.data(), T.bits.data(), kvd, packed);
+}
+
+// dequantize_*_into (:567-672): unpack, centroid lookup, V x (simd_matmul_rows), * norm
+static void sq_dequant(const SqTab &T, int64_t kvd, const uint8_t *packed, float nrm, float *out,
+                       std::vector<float> &r, std::vector<uint8_t> &idx) {
+    if (nrm < 1e-8f) {
+        std::fill(out, out + kvd, 0.0f);
+        return;
+    }
+    sq_unpack(packed, kvd, T.bits.data(), kvd, idx.data());
+    for (int64_t j = 0; j < kvd; ++j) r[j] = idx[j] < T.nlev[j] ? T.cent[j * kSqLevels + idx[j]] : 0.0f;
+    matmul(out, T.eig.data(), r.data(), kvd, kvd);
+    scale_inplace(out, kvd, nrm);
+}
+
 // utility predictor — src/sp_kv/utility_predictor.rs:16-87, weights types.rs:224-258
 struct Predictor {
     int64_t hidden;
@@ -796,6 +1145,9 @@ struct Seq {
     std::vector<int64_t> dequant_pos;
     std::vector<float> sn, sr;
     std::vector<uint8_t> si;
+    // SpectralQuant codec (tables per layer); null = TurboQuant
+    const std::vector<SqTab> *sqt = nullptr;
+    std::vector<uint8_t> sq_idx;
     // SP-KV
     const Predictor *pred = nullptr;
     std::vector<float> pbuf, hu, util, bias;
@@ -844,6 +1196,11 @@ struct Seq {
     int64_t force_T = 0;
     void store_kv(int64_t l, int64_t pos) {
         int64_t at = l * d.B + pos;
+        if (sqt) {  // SpectralQuantKVCache::store_key / store_value: one table for K and V
+            sq_store((*sqt)[l], d.kvd, k.data(), &kcodes[at * kpl], &knorm[at], sn, sr, sq_idx);
+            sq_store((*sqt)[l], d.kvd, v.data(), &vcodes[at * vpl], &vnorm[at], sn, sr, sq_idx);
+            return;
+        }
         tq_store(tq->rot.data(), tq->kb.data(), kbits, d.kvd, k.data(), &kcodes[at * kpl],
                  &knorm[at], sn.data(), sr.data(), si.data());
         if (rot_out) std::memcpy(rot_out + ((l * rot_T + pos) * 2 + 0) * d.kvd, sr.data(), d.kvd * 4);
@@ -858,11 +1215,13 @@ struct Seq {
     }
     void deq_key(int64_t l, int64_t t, float *out) {
         int64_t at = l * d.B + t;
+        if (sqt) return sq_dequant((*sqt)[l], d.kvd, &kcodes[at * kpl], knorm[at], out, sr, sq_idx);
         tq_dequant(tq->rot_t.data(), tq->kc.data(), kbits, d.kvd, &kcodes[at * kpl], knorm[at], out,
                    sr.data(), si.data());
     }
     void deq_val(int64_t l, int64_t t, float *out) {
         int64_t at = l * d.B + t;
+        if (sqt) return sq_dequant((*sqt)[l], d.kvd, &vcodes[at * vpl], vnorm[at], out, sr, sq_idx);
         tq_dequant(tq->rot_t.data(), tq->vc.data(), vbits, d.kvd, &vcodes[at * vpl], vnorm[at], out,
                    sr.data(), si.data());
     }
@@ -1444,6 +1803,111 @@ int or_forward_paged(const or_config *c, const float *weights, float *pool, cons
     s.sparse_threshold = c->sparse_threshold;
     s.forward_paged(token, pos, pool, table, maxp);
     std::memcpy(logits, s.logits.data(), d.V * 4);
+    return 0;
+}
+
+// ---- SpectralQuant ----
+static int sq_tables_from(int64_t kvd, int32_t L, const float *eig, const uint8_t *bits, const float *cent,
+                          const int32_t *nlev, std::vector<SqTab> &T) {
+    T.assign(L, SqTab());
+    for (int32_t l = 0; l < L; ++l) {
+        T[l].eig.assign(eig + l * kvd * kvd, eig + (l + 1) * kvd * kvd);
+        T[l].bits.assign(bits + l * kvd, bits + (l + 1) * kvd);
+        T[l].cent.assign(cent + l * kvd * kSqLevels, cent + (l + 1) * kvd * kSqLevels);
+        T[l].nlev.assign(nlev + l * kvd, nlev + (l + 1) * kvd);
+        for (int64_t j = 0; j < kvd; ++j)
+            if (T[l].bits[j] < 1 || T[l].bits[j] > 8 || T[l].nlev[j] > kSqLevels) return -1;
+    }
+    return 0;
+}
+
+// calibrate_eigenbasis (spectral.rs:226-278): covariance (1/N) sum x x^T in f64,
+// Jacobi, participation ratio. samples [n][dim].
+int or_sq_calibrate_eigenbasis(const float *samples, int64_t n, int64_t dim, float *eigvecs, float *eigvals,
+                               float *d_eff) {
+    if (!samples || n < 1 || dim < 2) return -1;
+    std::vector<double> cov(dim * dim, 0.0);
+    for (int64_t s = 0; s < n; ++s) {
+        const float *x = samples + s * dim;
+        for (int64_t i = 0; i < dim; ++i)
+            for (int64_t j = 0; j < dim; ++j) cov[i * dim + j] += (double)x[i] * (double)x[j];
+    }
+    const double scale = 1.0 / (double)n;
+    for (auto &v : cov) v *= scale;
+    std::vector<float> ev, vec;
+    sq_jacobi(cov, dim, ev, vec);
+    std::memcpy(eigvecs, vec.data(), dim * dim * 4);
+    std::memcpy(eigvals, ev.data(), dim * 4);
+    *d_eff = sq_participation_ratio(ev.data(), dim);
+    return 0;
+}
+
+// SpectralQuantKVCache::from_calibration per layer: tables as [L][kvd*kvd]
+// eigenvectors, [L][kvd] bits, [L][kvd][64] centroids, [L][kvd] level counts,
+// [L] d_eff. Returns -3 if a codebook exceeds 64 levels.
+int or_sq_build(const or_sq_params *P, int64_t kvd, int32_t L, const float *eig_in, const float *eval_in,
+                const float *deff_in, float *eig_out, uint8_t *bits_out, float *cent_out, int32_t *nlev_out,
+                int32_t *deff_out) {
+    if (!P || kvd < 2 || L < 1 || P->max_bits < 1) return -1;
+    for (int32_t l = 0; l < L; ++l) {
+        SqTab T;
+        int rc = sq_build_layer(*P, kvd, l, eig_in + l * kvd * kvd, eval_in + l * kvd, deff_in[l], T);
+        if (rc) return rc;
+        std::memcpy(eig_out + l * kvd * kvd, T.eig.data(), kvd * kvd * 4);
+        std::memcpy(bits_out + l * kvd, T.bits.data(), kvd);
+        std::memcpy(cent_out + l * kvd * kSqLevels, T.cent.data(), kvd * kSqLevels * 4);
+        std::memcpy(nlev_out + l * kvd, T.nlev.data(), kvd * 4);
+        deff_out[l] = T.d_eff;
+    }
+    return 0;
+}
+
+// store_vector then dequantize_*_into of one vector with one layer's tables
+// (packed gets the pack's byte count, returned; -1 on bad tables).
+int64_t or_sq_roundtrip(int64_t kvd, const float *eig, const uint8_t *bits, const float *cent, const int32_t *nlev,
+                        const float *x, uint8_t *packed, float *norm, float *deq) {
+    std::vector<SqTab> T;
+    if (sq_tables_from(kvd, 1, eig, bits, cent, nlev, T)) return -1;
+    std::vector<float> xn(kvd), r(kvd);
+    std::vector<uint8_t> idx(kvd);
+    sq_store(T[0], kvd, x, packed, norm, xn, r, idx);
+    if (deq) sq_dequant(T[0], kvd, packed, *norm, deq, r, idx);
+    int64_t tb = 0;
+    for (int64_t j = 0; j < kvd; ++j) tb += bits[j];
+    return (tb + 7) / 8;
+}
+
+// forward_quantized<SpectralQuantKVCache> (src/transformer.rs:4042-4233 with
+// the codec of src/spectralquant/spectral_kv_cache.rs) of one sequence:
+// logits [T][V], codes [L][T][2*kvd] (K row then V row, kvd bytes each, the
+// pack in front), norms [L][T][2].
+int or_run_sequence_sq(const or_config *c, const float *weights, const float *eig, const uint8_t *bits,
+                       const float *cent, const int32_t *nlev, const int32_t *tokens, int32_t T, float *logits,
+                       uint8_t *codes, float *norms) {
+    if (check_cfg(c, T)) return -1;
+    Dims d = dims_of(c);
+    Weights W = view_weights(d, weights);
+    std::vector<SqTab> tabs;
+    if (sq_tables_from(d.kvd, (int32_t)d.L, eig, bits, cent, nlev, tabs)) return -1;
+    Seq s;
+    s.init(d, &W, OR_MODE_QUANT, 8, 8);  // 8-bit packed rows: kvd bytes per vector
+    s.sparse_threshold = c->sparse_threshold;
+    s.sqt = &tabs;
+    s.sq_idx.assign(d.kvd, 0);
+    for (int32_t p = 0; p < T; ++p) {
+        if (tokens[p] < 0 || tokens[p] >= d.V) return -2;
+        s.forward_quant(tokens[p], p);
+        if (logits) std::memcpy(logits + (int64_t)p * d.V, s.logits.data(), d.V * 4);
+    }
+    for (int64_t l = 0; l < d.L; ++l)
+        for (int64_t p = 0; p < T; ++p) {
+            const int64_t at = l * d.B + p, o = l * T + p;
+            if (codes) {
+                std::memcpy(codes + o * 2 * d.kvd, &s.kcodes[at * s.kpl], d.kvd);
+                std::memcpy(codes + o * 2 * d.kvd + d.kvd, &s.vcodes[at * s.vpl], d.kvd);
+            }
+            if (norms) norms[o * 2] = s.knorm[at], norms[o * 2 + 1] = s.vnorm[at];
+        }
     return 0;
 }
 

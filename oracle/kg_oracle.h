@@ -40,6 +40,20 @@ typedef struct {
     float sparse_threshold;
 } or_config;
 
+/* SpectralQuantKVCacheConfig fields the codec build reads
+ * (src/spectralquant/types.rs:97-126). */
+typedef struct {
+    uint64_t seed;
+    int32_t lloyd_max_iter;
+    int32_t calibration_samples;
+    float avg_bits;
+    int32_t min_tail_bits;
+    int32_t max_bits;
+    int32_t wf_min_bits;
+    int32_t wf_max_bits;
+    int32_t use_water_fill;
+} or_sq_params;
+
 /* Forward flavours (one per reference entry point). */
 enum {
     OR_MODE_BASE = 0,      /* transformer::forward -> forward_base (src/transformer.rs:398-429,1821-2200) */
@@ -122,6 +136,20 @@ int or_run_sequence(const or_config *c, int mode, int key_bits, int val_bits,
  * the sequence's [n_layer][maxp] page indices. */
 int or_forward_paged(const or_config *c, const float *weights, float *pool, const int64_t *table, int64_t maxp,
                      int32_t token, int32_t pos, float *logits);
+/* SpectralQuant (src/spectralquant/): calibrate_eigenbasis, the per-layer
+ * tables of SpectralQuantKVCache::from_calibration ([L][kvd*kvd] eigenvectors,
+ * [L][kvd] bits, [L][kvd][64] centroids, [L][kvd] level counts, [L] d_eff),
+ * one store+dequantize round trip, and forward_quantized over the codec. */
+int or_sq_calibrate_eigenbasis(const float *samples, int64_t n, int64_t dim, float *eigvecs, float *eigvals,
+                               float *d_eff);
+int or_sq_build(const or_sq_params *P, int64_t kvd, int32_t L, const float *eig_in, const float *eval_in,
+                const float *deff_in, float *eig_out, uint8_t *bits_out, float *cent_out, int32_t *nlev_out,
+                int32_t *deff_out);
+int64_t or_sq_roundtrip(int64_t kvd, const float *eig, const uint8_t *bits, const float *cent, const int32_t *nlev,
+                        const float *x, uint8_t *packed, float *norm, float *deq);
+int or_run_sequence_sq(const or_config *c, const float *weights, const float *eig, const uint8_t *bits,
+                       const float *cent, const int32_t *nlev, const int32_t *tokens, int32_t T, float *logits,
+                       uint8_t *codes, float *norms);
 int or_run_sequence_rot(const or_config *c, int mode, int key_bits, int val_bits, const float *weights,
                         const int32_t *tokens, int32_t T, float *logits, uint8_t *codes, float *norms,
                         float *rot_out);

@@ -29,6 +29,25 @@ class OrConfig(ctypes.Structure):
                 ("sparse_threshold", ctypes.c_float)]
 
 
+class OrSqParams(ctypes.Structure):
+    """SpectralQuantKVCacheConfig fields (src/spectralquant/types.rs:97-126)."""
+    _fields_ = [("seed", ctypes.c_uint64), ("lloyd_max_iter", ctypes.c_int32),
+                ("calibration_samples", ctypes.c_int32), ("avg_bits", ctypes.c_float),
+                ("min_tail_bits", ctypes.c_int32), ("max_bits", ctypes.c_int32),
+                ("wf_min_bits", ctypes.c_int32), ("wf_max_bits", ctypes.c_int32),
+                ("use_water_fill", ctypes.c_int32)]
+
+
+def sq_params(avg_bits=3.0, min_tail_bits=1, max_bits=8, lloyd_max_iter=30, calibration_samples=100, seed=42,
+              use_water_fill=False, wf_min_bits=1, wf_max_bits=6):
+    """The reference's test configuration (spectral_kv_cache.rs:1214-1234) by default."""
+    return OrSqParams(seed, lloyd_max_iter, calibration_samples, avg_bits, min_tail_bits, max_bits, wf_min_bits,
+                      wf_max_bits, int(use_water_fill))
+
+
+SQ_LEVELS = 64
+
+
 def build():
     subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIBPATH
@@ -80,6 +99,10 @@ def lib():
             "or_run_sequence_forced": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, P, P, I32, P, P]),
             "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
             "or_forward_paged": (ctypes.c_int, [cp, P, P, P, I64, I32, I32, P]),
+            "or_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
+            "or_sq_build": (ctypes.c_int, [ctypes.POINTER(OrSqParams), I64, I32, P, P, P, P, P, P, P, P]),
+            "or_sq_roundtrip": (I64, [I64, P, P, P, P, P, P, P, P]),
+            "or_run_sequence_sq": (ctypes.c_int, [cp, P, P, P, P, P, P, I32, P, P, P]),
             "or_time_decode": (ctypes.c_double, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, I32, I32, ctypes.c_int]),
         }
         for k, (r, a) in sig.items():
@@ -472,3 +495,64 @@ def forward_paged(cfg, w, cache, seq, token, pos):
     if rc:
         raise RuntimeError(f"or_forward_paged failed: {rc}")
     return logits
+
+
+def sq_calibrate_eigenbasis(samples):
+    """calibrate_eigenbasis (src/spectralquant/spectral.rs:226-278) of samples [n][dim]:
+    (eigenvectors [dim*dim] row-major, eigenvalues [dim], d_eff)."""
+    x = f32(samples)
+    n, dim = x.shape
+    vec = np.empty(dim * dim, np.float32)
+    val = np.empty(dim, np.float32)
+    de = ctypes.c_float(0)
+    rc = lib().or_sq_calibrate_eigenbasis(_p(x), n, dim, _p(vec), _p(val), ctypes.byref(de))
+    if rc:
+        raise RuntimeError(f"or_sq_calibrate_eigenbasis failed: {rc}")
+    return vec, val, de.value
+
+
+def sq_build(params, kvd, eig, evals, d_eff):
+    """SpectralQuantKVCache::from_calibration tables for L layers (inputs [L][...]):
+    dict of eig [L][kvd*kvd], bits [L][kvd] u8, cent [L][kvd][64], nlev [L][kvd], d_eff [L]."""
+    eig = f32(eig).reshape(-1, kvd * kvd)
+    L = eig.shape[0]
+    evals = f32(evals).reshape(L, kvd)
+    d_eff = f32(d_eff).reshape(L)
+    out = dict(eig=np.empty((L, kvd * kvd), np.float32), bits=np.empty((L, kvd), np.uint8),
+               cent=np.empty((L, kvd, SQ_LEVELS), np.float32), nlev=np.empty((L, kvd), np.int32),
+               d_eff=np.empty(L, np.int32))
+    rc = lib().or_sq_build(ctypes.byref(params), kvd, L, _p(eig), _p(evals), _p(d_eff), _p(out["eig"]),
+                           _p(out["bits"]), _p(out["cent"]), _p(out["nlev"]), _p(out["d_eff"]))
+    if rc:
+        raise RuntimeError(f"or_sq_build failed: {rc}")
+    return out
+
+
+def sq_roundtrip(tabs, layer, x):
+    """store_vector + dequantize_*_into of x with one layer's tables: (packed bytes, norm, dequantized)."""
+    kvd = tabs["bits"].shape[1]
+    x = f32(x)
+    packed = np.zeros(kvd, np.uint8)
+    norm = ctypes.c_float(0)
+    deq = np.empty(kvd, np.float32)
+    nb = lib().or_sq_roundtrip(kvd, _p(tabs["eig"][layer]), _p(tabs["bits"][layer]), _p(tabs["cent"][layer]),
+                               _p(tabs["nlev"][layer]), _p(x), _p(packed), ctypes.byref(norm), _p(deq))
+    if nb < 0:
+        raise RuntimeError("or_sq_roundtrip: bad tables")
+    return packed[:nb], norm.value, deq
+
+
+def run_sequence_sq(cfg, w, tabs, tokens):
+    """forward_quantized over SpectralQuantKVCache: (logits [T][V], codes [L][T][2*kvd], norms [L][T][2])."""
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    T = tokens.size
+    kvd = cfg.n_kv_head * cfg.head_dim
+    logits = np.empty((T, cfg.vocab_size), np.float32)
+    codes = np.zeros((cfg.n_layer, T, 2 * kvd), np.uint8)
+    norms = np.zeros((cfg.n_layer, T, 2), np.float32)
+    rc = lib().or_run_sequence_sq(ctypes.byref(cfg), _p(f32(w)), _p(tabs["eig"]), _p(tabs["bits"]),
+                                  _p(tabs["cent"]), _p(tabs["nlev"]), _p(tokens), T, _p(logits), _p(codes),
+                                  _p(norms))
+    if rc:
+        raise RuntimeError(f"or_run_sequence_sq failed: {rc}")
+    return logits, codes, norms
