@@ -420,6 +420,12 @@ int kg_profile_read(kg_ctx *ctx, float *ms, int64_t *count);
  * mask with |N(0,1)| survivors, deterministic in (seed, layer, slot,
  * position). keep <= 0 turns it off. Drops captured decode graphs. */
 int kg_set_mlp_hook(kg_ctx *ctx, float keep, uint64_t seed);
+/* Diagnostics (no reference counterpart): run the bounded-wait path the
+ * pipelined kernels use, on purpose — one thread waits on an mbarrier that
+ * nothing arrives on, with a limit of limit_cycles SM clocks (at most 2^32).
+ * Returns KG_ERR_TIMEOUT (the status a lost arrival inside a GEMM or
+ * attention kernel produces); the context stays usable afterwards. */
+int kg_selftest_wait_timeout(kg_ctx *ctx, int64_t limit_cycles);
 /* Kernel launches replayed by the last kg_forward_batch(_dev) call when it ran
  * as a captured CUDA graph (single-position decode of the bf16 path on a
  * non-legacy stream, profiling off); 0 when that call ran eagerly. */

@@ -19,7 +19,7 @@ NVCC_COMMON = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                       "-Xcompiler", "-ffp-contract=off", "-Xptxas", "-v"]
 EXACT = {"kg_micro.cu", "kg_tq.cu"}
 CU_FILES = ["kg_micro.cu", "kg_tq.cu", "kg_api.cu", "kg_bf16.cu", "kg_attn.cu", "kg_tqattn.cu", "kg_big.cu", "kg_umma.cu",
-            "kg_sample.cu", "kg_tcattn.cu", "kg_comm.cu", "kg_paged.cu"]
+            "kg_sample.cu", "kg_tcattn.cu", "kg_comm.cu", "kg_paged.cu", "kg_selftest.cu"]
 CPP_FILES = ["kg_tables.cpp", "kg_sq.cpp"]
 
 

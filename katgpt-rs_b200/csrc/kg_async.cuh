@@ -42,18 +42,22 @@ __device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
 }
 // Wait for the phase of `parity` to complete; false when the clock limit
 // passed (the abort flag and *err are set) or another thread already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err,
+                                              long long limit_cycles) {
     if (mbar_try(b, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(b, parity)) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > KG_WAIT_CYCLES) {
+        if (clock64() - t0 > limit_cycles) {
             *abort_flag = 1;
             if (err) atomicExch(err, (int)KG_ERR_TIMEOUT);
             return false;
         }
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+    return mbar_wait_for(b, parity, abort_flag, err, KG_WAIT_CYCLES);
 }
 
 // 2-D tiled TMA load of one box into shared memory, completion on `bar`

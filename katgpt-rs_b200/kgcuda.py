@@ -123,6 +123,7 @@ def lib():
             "kg_sq_tables": (ctypes.c_int, [P, I32, P, P, P, P, P]),
             "kg_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
             "kg_sq_build_tables": (ctypes.c_int, [ctypes.POINTER(KgSqParams), I64, I32, P, P, P, P, P, P, P, P]),
+            "kg_selftest_wait_timeout": (ctypes.c_int, [P, I64]),
             "kg_paged_init": (ctypes.c_int, [P, I32]),
             "kg_paged_ensure": (ctypes.c_int, [P, I32, I32]),
             "kg_paged_fork": (ctypes.c_int, [P, I32, I32, P]),
