@@ -68,6 +68,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
         "l"(tm), "r"(x), "r"(y), "r"(sa(bar))
         : "memory");
 }
+// Prefetch one box of a 2-D tiled tensor map into L2 (no shared memory, no
+// barrier): a producer issues it a few stages ahead of its ring so that the
+// stage's own TMA load finds the bytes in L2 instead of waiting on HBM.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *tm, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n" ::"l"(tm), "r"(x), "r"(y)
+                 : "memory");
+}
 // contiguous bulk copy global -> shared (16-byte aligned, size a multiple of 16)
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(

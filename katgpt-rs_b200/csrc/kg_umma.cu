@@ -314,6 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1) umma_gemm_kernel(const __grid_cons
 // sCb at the output).
 // Warps: 0 TMA producer, 1..2 MMA issuers, 3..6 epilogue.
 constexpr int DTHREADS = 224;
+constexpr int DPF = STG + 3;  // L2 prefetch distance of the weight tiles, in K blocks
 
 template <typename T, bool SA, bool SB, int BN>
 __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_constant__ Maps maps, const bf::Gemm g,
@@ -377,6 +378,12 @@ __global__ void __launch_bounds__(DTHREADS, 1) umma_dec_kernel(const __grid_cons
                 const int by = n0 + (int)(bo / g.ldb), bx = (int)(bo % g.ldb);
                 for (int j = 0; j < kbs; ++j, ++it) {
                     const int s = it % STG, kb = part * kbs + j;
+                    // weight tiles DPF blocks ahead into L2 (the ring holds STG of them)
+                    for (int pj = (j == 0 ? STG : DPF); pj <= DPF; ++pj)
+                        if (j + pj < kbs) {
+                            tma_prefetch_2d(&maps.b, bx + (kb + pj) * BK, by);
+                            if (SB) tma_prefetch_2d(&maps.b2, bx + (kb + pj) * BK, by);
+                        }
                     if (!mbar_wait(&empty[s], ((it / STG) & 1) ^ 1, abort_flag, err)) break;
                     uint8_t *st = dsm + s * STAGE_BYTES;
                     mbar_expect_tx(&full[s], TX);
