@@ -315,8 +315,9 @@ int kg_paged_stats(const kg_ctx *ctx, int64_t *total_pages, int64_t *free_pages,
  * packed LSB-first at those widths; keys and values share the layer's tables,
  * as the reference does. kg_kv_codes returns the pack at the front of a
  * kv_dim-byte row. A KG_KV_SQ context needs one of the two calibration calls
- * before its first forward (KG_ERR_NOT_COMPILED otherwise). Micro widths
- * (Config::micro()); codebooks of at most 64 centroids (6 bits) per dimension. */
+ * before its first forward or codec call (KG_ERR_NOT_COMPILED otherwise). The
+ * forward runs the micro widths (Config::micro()); kg_sq_encode / kg_sq_decode
+ * run any kv_dim. Codebooks of at most 64 centroids (6 bits) per dimension. */
 
 /* SpectralQuantKVCacheConfig (src/spectralquant/types.rs:97-126), the fields
  * the codec build reads. */
@@ -356,6 +357,15 @@ int kg_sq_calibrate_eigenbasis(const float *samples, int64_t n_samples, int64_t 
 int kg_sq_build_tables(const kg_sq_params *p, int64_t kv_dim, int32_t n_layers, const float *eigenvectors,
                        const float *eigenvalues, const float *d_eff, float *eig_out, uint8_t *bits_out,
                        float *centroids_out, int32_t *n_levels_out, int32_t *d_eff_out);
+/* The codec at any kv_dim (a KG_KV_SQ context whose shape has no forward
+ * kernel is a codec context, like a TurboQuant one): store_vector of n_vec host
+ * vectors x [n_vec][kv_dim] with layer `layer`'s tables into packed
+ * [n_vec][kv_dim] (the pack at the front of each row; its other bytes, and
+ * every byte of a row whose norm is < 1e-8, keep the caller's contents) and
+ * norms [n_vec]; and dequantize_*_into of such rows into out [n_vec][kv_dim].
+ * Keys and values use the same tables. Synchronous. */
+int kg_sq_encode(kg_ctx *ctx, int32_t layer, int64_t n_vec, const float *x, uint8_t *packed, float *norms);
+int kg_sq_decode(kg_ctx *ctx, int32_t layer, int64_t n_vec, const uint8_t *packed, const float *norms, float *out);
 /* One layer's tables as the device holds them: eigenvectors [kv_dim*kv_dim],
  * bits [kv_dim], centroids [kv_dim][64] (dimension j's codebook first
  * n_levels[j] entries), n_levels [kv_dim], d_eff. Any pointer may be NULL. */

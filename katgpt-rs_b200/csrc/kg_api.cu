@@ -218,8 +218,6 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     const bool paged = c.kv_mode == KG_KV_PAGED, sqm = c.kv_mode == KG_KV_SQ;
     if (paged && !ctx->micro)
         return bail(fail(ctx, KG_ERR_UNSUPPORTED, "forward_paged runs the micro widths at block_size 16 or 64"));
-    if (sqm && !ctx->micro)
-        return bail(fail(ctx, KG_ERR_UNSUPPORTED, "the SpectralQuant codec runs the micro widths (Config::micro())"));
     ctx->kpl = tq ? packed_len(ctx->kvd, c.key_bits) : 0;
     ctx->vpl = tq ? packed_len(ctx->kvd, c.val_bits) : 0;
     if (sqm) ctx->kpl = ctx->vpl = ctx->kvd;  // variable-width pack, at most one byte per dimension
@@ -1015,10 +1013,33 @@ int sq_install(kg_ctx *ctx, const kg_sq_params *p, const float *eig, const float
         }
     }
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
-    const kg::MicroArgs &a = ctx->margs;
-    KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_eig, E.data(), E.size() * 4, cudaMemcpyHostToDevice));
-    KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_cent, C.data(), C.size() * 4, cudaMemcpyHostToDevice));
-    KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice));
+    if (ctx->micro) {  // the micro forward's shared-memory pack
+        const kg::MicroArgs &a = ctx->margs;
+        KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_eig, E.data(), E.size() * 4, cudaMemcpyHostToDevice));
+        KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_cent, C.data(), C.size() * 4, cudaMemcpyHostToDevice));
+        KG_CUDA(ctx, cudaMemcpy(ctx->pack + a.off_sq_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice));
+    }
+    // the codec entry points' tables: width | levels << 8 and bit offsets per dimension
+    std::vector<int32_t> imeta(L * kvd), offs(L * kvd);
+    ctx->sq_nbytes.assign(L, 0);
+    for (int64_t l = 0; l < L; ++l) {
+        int64_t o = 0;
+        for (int64_t j = 0; j < kvd; ++j) {
+            imeta[l * kvd + j] = (int32_t)bits[l * kvd + j] | (lev[l * kvd + j] << 8);
+            offs[l * kvd + j] = (int32_t)o;
+            o += bits[l * kvd + j];
+        }
+        ctx->sq_nbytes[l] = (int)((o + 7) / 8);
+    }
+    int rc = 0;
+    if (!ctx->sq_eig_d && ((rc = dalloc(ctx, &ctx->sq_eig_d, E.size())) || (rc = dalloc(ctx, &ctx->sq_cent_d, C.size())) ||
+                           (rc = dalloc(ctx, &ctx->sq_meta_d, imeta.size())) ||
+                           (rc = dalloc(ctx, &ctx->sq_offs_d, offs.size()))))
+        return rc;
+    KG_CUDA(ctx, cudaMemcpy(ctx->sq_eig_d, E.data(), E.size() * 4, cudaMemcpyHostToDevice));
+    KG_CUDA(ctx, cudaMemcpy(ctx->sq_cent_d, C.data(), C.size() * 4, cudaMemcpyHostToDevice));
+    KG_CUDA(ctx, cudaMemcpy(ctx->sq_meta_d, imeta.data(), imeta.size() * 4, cudaMemcpyHostToDevice));
+    KG_CUDA(ctx, cudaMemcpy(ctx->sq_offs_d, offs.data(), offs.size() * 4, cudaMemcpyHostToDevice));
     ctx->h_sq_eig = std::move(E);
     ctx->h_sq_cent = std::move(C);
     ctx->h_sq_bits = std::move(bits);
@@ -1029,7 +1050,7 @@ int sq_install(kg_ctx *ctx, const kg_sq_params *p, const float *eig, const float
 }
 int sq_check(kg_ctx *ctx, const kg_sq_params *p) {
     if (!ctx) return KG_ERR_INVALID_ARG;
-    if (ctx->cfg.kv_mode != KG_KV_SQ || !ctx->micro) return fail(ctx, KG_ERR_UNSUPPORTED, "context is not kv_mode KG_KV_SQ");
+    if (ctx->cfg.kv_mode != KG_KV_SQ) return fail(ctx, KG_ERR_UNSUPPORTED, "context is not kv_mode KG_KV_SQ");
     if (!p || p->max_bits < 1 || p->max_bits > 8 || p->lloyd_max_iter < 0 || p->wf_min_bits < 1 ||
         p->wf_max_bits < p->wf_min_bits || p->wf_max_bits > 8)
         return fail(ctx, KG_ERR_INVALID_ARG, "bad SpectralQuant parameters");
@@ -1099,5 +1120,60 @@ int kg_sq_build_tables(const kg_sq_params *p, int64_t kv_dim, int32_t n_layers, 
                                 eig_out + l * kv_dim * kv_dim, bits_out + l * kv_dim,
                                 centroids_out + l * kv_dim * kg::kSqLevels, n_levels_out + l * kv_dim, d_eff_out + l))
             return KG_ERR_UNSUPPORTED;
+    return KG_OK;
+}
+
+// ---- SpectralQuant codec at any kv_dim (host pointers; synchronous) ----
+
+int kg_sq_encode(kg_ctx *ctx, int32_t layer, int64_t n_vec, const float *x, uint8_t *packed, float *norms) {
+    if (!ctx || !x || !packed || !norms || n_vec < 0) return KG_ERR_INVALID_ARG;
+    if (!ctx->sq_ready) return fail(ctx, KG_ERR_NOT_COMPILED, "SpectralQuant tables not built");
+    if (layer < 0 || layer >= ctx->L) return fail(ctx, KG_ERR_INVALID_ARG, "layer out of range");
+    if (n_vec == 0) return KG_OK;
+    if (n_vec > INT32_MAX) return fail(ctx, KG_ERR_INVALID_ARG, "too many vectors in one call");
+    const int64_t kvd = ctx->kvd;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t bx = align256(n_vec * kvd * 4), bp = align256(n_vec * kvd), bn = align256(n_vec * 4);
+    int rc = ensure_stage(ctx, bx + bp + bn);
+    if (rc) return rc;
+    char *st = static_cast<char *>(ctx->stage);
+    float *dx = reinterpret_cast<float *>(st);
+    uint8_t *dp = reinterpret_cast<uint8_t *>(st + bx);
+    float *dn = reinterpret_cast<float *>(st + bx + bp);
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemcpyAsync(dx, x, n_vec * kvd * 4, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(dp, packed, n_vec * kvd, cudaMemcpyHostToDevice, s));  // zero-norm rows keep theirs
+    KG_CUDA(ctx, kg::sq_encode_device((int)kvd, n_vec, dx, ctx->sq_eig_d + layer * kvd * kvd, ctx->sq_meta_d + layer * kvd,
+                                      ctx->sq_cent_d + layer * kvd * kg::kSqLevels, ctx->sq_offs_d + layer * kvd,
+                                      ctx->sq_nbytes[layer], dp, kvd, dn, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(packed, dp, n_vec * kvd, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(norms, dn, n_vec * 4, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
+    return KG_OK;
+}
+
+int kg_sq_decode(kg_ctx *ctx, int32_t layer, int64_t n_vec, const uint8_t *packed, const float *norms, float *out) {
+    if (!ctx || !packed || !norms || !out || n_vec < 0) return KG_ERR_INVALID_ARG;
+    if (!ctx->sq_ready) return fail(ctx, KG_ERR_NOT_COMPILED, "SpectralQuant tables not built");
+    if (layer < 0 || layer >= ctx->L) return fail(ctx, KG_ERR_INVALID_ARG, "layer out of range");
+    if (n_vec == 0) return KG_OK;
+    if (n_vec > INT32_MAX) return fail(ctx, KG_ERR_INVALID_ARG, "too many vectors in one call");
+    const int64_t kvd = ctx->kvd;
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t bx = align256(n_vec * kvd * 4), bp = align256(n_vec * kvd), bn = align256(n_vec * 4);
+    int rc = ensure_stage(ctx, bx + bp + bn);
+    if (rc) return rc;
+    char *st = static_cast<char *>(ctx->stage);
+    float *dx = reinterpret_cast<float *>(st);
+    uint8_t *dp = reinterpret_cast<uint8_t *>(st + bx);
+    float *dn = reinterpret_cast<float *>(st + bx + bp);
+    cudaStream_t s = ctx->stream;
+    KG_CUDA(ctx, cudaMemcpyAsync(dp, packed, n_vec * kvd, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(dn, norms, n_vec * 4, cudaMemcpyHostToDevice, s));
+    KG_CUDA(ctx, kg::sq_decode_device((int)kvd, n_vec, dp, kvd, dn, ctx->sq_eig_d + layer * kvd * kvd,
+                                      ctx->sq_meta_d + layer * kvd, ctx->sq_cent_d + layer * kvd * kg::kSqLevels,
+                                      ctx->sq_offs_d + layer * kvd, ctx->sq_nbytes[layer], dx, s));
+    KG_CUDA(ctx, cudaMemcpyAsync(out, dx, n_vec * kvd * 4, cudaMemcpyDeviceToHost, s));
+    KG_CUDA(ctx, cudaStreamSynchronize(s));
     return KG_OK;
 }

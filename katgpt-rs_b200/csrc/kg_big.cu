@@ -112,6 +112,7 @@ cudaError_t dalloc(T **p, size_t count, std::vector<void *> &owned) {
 int big_supported(const kg_config &c, std::string &why) {
     if (c.weight_dtype != KG_W_BF16) return why = "the tensor-core path runs bf16 weights (KG_W_BF16)", -1;
     if (c.kv_mode == KG_KV_PAGED) return why = "forward_paged runs on the exact micro path", -1;
+    if (c.kv_mode == KG_KV_SQ) return why = "the SpectralQuant forward runs on the exact micro path", -1;
     if (c.kv_mode != KG_KV_F32)
         for (int b : {c.key_bits, c.val_bits})
             if (b != 3 && b != 4) return why = "the bf16 path packs 3/4-bit codes", -1;

@@ -95,6 +95,15 @@ cudaError_t tq_encode_tiled(int dim, int bits, int64_t n_vec, const float *x, in
 // the K and V rows of qkv (2M vectors), then after the caller's rotation GEMM
 // Y = xn R^T, codes from Y with exact recomputation near boundaries.
 float tq_fixup_eps(int dim);
+// SpectralQuant store / dequantize at any kv_dim with one layer's device tables
+// (eig [kvd*kvd], meta [kvd] = width | levels << 8, cent [kvd][64], offs [kvd]
+// bit offsets, nbytes = the pack's length); packed rows pstride bytes apart.
+cudaError_t sq_encode_device(int kvd, int64_t n_vec, const float *x, const float *eig, const int *meta,
+                             const float *cent, const int *offs, int nbytes, uint8_t *packed, int64_t pstride,
+                             float *norms, cudaStream_t s);
+cudaError_t sq_decode_device(int kvd, int64_t n_vec, const uint8_t *packed, int64_t pstride, const float *norms,
+                             const float *eig, const int *meta, const float *cent, const int *offs, int nbytes,
+                             float *out, cudaStream_t s);
 // Vectors v < Mk are K rows (x + t * ldx + koff), the next Mv are V rows.
 cudaError_t tq_norm_split(int dim, int Mk, int Mv, const float *qkv, int64_t ldx, int64_t koff, int64_t voff,
                           float *xn, __half *xh, __half *xl, uint8_t *skip, float *knorm, float *vnorm,
@@ -235,6 +244,11 @@ struct kg_ctx {
     std::vector<float> h_sq_eig, h_sq_cent;
     std::vector<uint8_t> h_sq_bits;
     std::vector<int32_t> h_sq_lev, h_sq_deff;
+    // the same tables for the codec entry points at any kv_dim: [L] layers of
+    // eig [kvd*kvd], meta [kvd], cent [kvd][64], bit offsets [kvd]; pack bytes per layer
+    float *sq_eig_d = nullptr, *sq_cent_d = nullptr;
+    int *sq_meta_d = nullptr, *sq_offs_d = nullptr;
+    std::vector<int> sq_nbytes;
 };
 
 namespace kg {

@@ -485,6 +485,103 @@ quantize_fixup_kernel(int dim, int Mk, int Mv, const float *Y, const float *xn, 
     if (nfix && threadIdx.x == 0 && n_near) atomicAdd(nfix, n_near);
 }
 
+// ---- SpectralQuant codec at any kv_dim (store_vector / dequantize_*_into,
+// src/spectralquant/spectral_kv_cache.rs:399-470, 567-672). A layer's tables:
+// eig [kvd*kvd] (V[i][j] at i*kvd + j, columns = eigenvectors), meta [kvd]
+// (width | levels << 8), cent [kvd][64], offs [kvd] (bit offset of dimension j
+// in the pack: the prefix sum of the widths), and the pack's byte count.
+
+// One CTA per vector: norm (simd_sum_sq order), x / norm, y_j = sum over i in
+// order of V[i][j] x_i (rotate_into: one thread per output, separate multiply
+// and add), the nearest centroid by the reference's bisection, and the index
+// ORed into the pack at its bit offset (LSB-first stream). A vector with norm
+// < 1e-8 stores norm 0 and leaves its bytes as they were.
+__global__ void sq_encode_kernel(int kvd, const float *x, const float *eig, const int *meta, const float *cent,
+                                 const int *offs, int nbytes, uint8_t *packed, int64_t pstride, float *norms) {
+    extern __shared__ float sq_sm[];
+    float *xn = sq_sm;                                          // [kvd]
+    uint32_t *words = reinterpret_cast<uint32_t *>(xn + kvd);  // [nbytes / 4 + 2]
+    __shared__ float s_norm;
+    const int64_t v = blockIdx.x;
+    const float *xv = x + v * kvd;
+    if (threadIdx.x < 32) {
+        const float ss = warp_sum_sq(xv, kvd, 1);
+        if (threadIdx.x == 0) s_norm = sqrtf(ss);
+    }
+    for (int w = threadIdx.x; w < nbytes / 4 + 2; w += blockDim.x) words[w] = 0u;
+    __syncthreads();
+    const float norm = s_norm;
+    if (norm < 1e-8f) {  // CTA-uniform
+        if (threadIdx.x == 0) norms[v] = 0.0f;
+        return;
+    }
+    if (threadIdx.x == 0) norms[v] = norm;
+    const float inv = 1.0f / norm;
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) xn[i] = xv[i] * inv;
+    __syncthreads();
+    for (int j = threadIdx.x; j < kvd; j += blockDim.x) {
+        float y = 0.0f;
+        for (int i = 0; i < kvd; ++i) y = y + eig[(int64_t)i * kvd + j] * xn[i];
+        const int n = meta[j] >> 8;
+        const float *c = cent + (int64_t)j * 64;
+        int q = 0;  // quantize_to_idx (spectral_kv_cache.rs:1079-1111)
+        if (n > 1) {
+            int lo = 0, hi = n - 1;
+            if (y <= c[lo]) q = lo;
+            else if (y >= c[hi]) q = hi;
+            else {
+                while (lo + 1 < hi) {
+                    const int mid = lo + (hi - lo) / 2;
+                    if (c[mid] <= y) lo = mid;
+                    else hi = mid;
+                }
+                q = fabsf(y - c[lo]) <= fabsf(c[hi] - y) ? lo : hi;
+            }
+        }
+        const int o = offs[j];
+        const uint64_t sh = (uint64_t)q << (o & 31);  // pack_variable_bits (:1125-1164)
+        atomicOr(&words[o >> 5], (uint32_t)sh);
+        if (sh >> 32) atomicOr(&words[(o >> 5) + 1], (uint32_t)(sh >> 32));
+    }
+    __syncthreads();
+    const uint8_t *wb = reinterpret_cast<const uint8_t *>(words);
+    uint8_t *out = packed + v * pstride;
+    for (int b = threadIdx.x; b < nbytes; b += blockDim.x) out[b] = wb[b];
+}
+
+// One CTA per vector: unpack (unpack_variable_bits, :1167-1187), centroids,
+// out_i = simd_dot(V row i, c) (simd_matmul_rows: one warp per row, the AVX2
+// order) * norm; zeros when norm < 1e-8.
+__global__ void sq_decode_kernel(int kvd, const uint8_t *packed, int64_t pstride, const float *norms, const float *eig,
+                                 const int *meta, const float *cent, const int *offs, int nbytes, float *out) {
+    extern __shared__ float sq_sm[];
+    float *c = sq_sm;  // [kvd]
+    const int64_t v = blockIdx.x;
+    const float norm = norms[v];
+    float *ov = out + v * kvd;
+    if (norm < 1e-8f) {
+        for (int i = threadIdx.x; i < kvd; i += blockDim.x) ov[i] = 0.0f;
+        return;
+    }
+    const uint8_t *p = packed + v * pstride;
+    for (int j = threadIdx.x; j < kvd; j += blockDim.x) {
+        const int m = meta[j], bits = m & 255, n = m >> 8, o = offs[j];
+        uint32_t w = 0;
+        for (int b = 0; b < 3; ++b) {
+            const int bi = (o >> 3) + b;
+            if (bi < nbytes) w |= (uint32_t)p[bi] << (8 * b);
+        }
+        const int idx = (int)((w >> (o & 7)) & ((1u << bits) - 1u));
+        c[j] = idx < n ? cent[(int64_t)j * 64 + idx] : 0.0f;
+    }
+    __syncthreads();
+    const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int i = wp; i < kvd; i += nw) {
+        const float r = warp_dot(eig + (int64_t)i * kvd, c, kvd);
+        if (lane == 0) ov[i] = r * norm;
+    }
+}
+
 }  // namespace
 
 // Bound on |y' - y| for the fix-up: both roundings of a dim-term dot of a unit
@@ -516,6 +613,30 @@ cudaError_t tq_quantize_fixup(int dim, int Mk, int Mv, const float *Y, const flo
 
 namespace {
 }  // namespace
+
+cudaError_t sq_encode_device(int kvd, int64_t n_vec, const float *x, const float *eig, const int *meta,
+                             const float *cent, const int *offs, int nbytes, uint8_t *packed, int64_t pstride,
+                             float *norms, cudaStream_t s) {
+    if (n_vec <= 0) return cudaSuccess;
+    if (kvd < 2 || nbytes < 1 || nbytes > kvd) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kvd * 4 + (size_t)(nbytes / 4 + 2) * 4;
+    cudaError_t e = dev::smem(sq_encode_kernel, smem);
+    if (e != cudaSuccess) return e;
+    sq_encode_kernel<<<(unsigned)n_vec, 256, smem, s>>>(kvd, x, eig, meta, cent, offs, nbytes, packed, pstride, norms);
+    return cudaGetLastError();
+}
+
+cudaError_t sq_decode_device(int kvd, int64_t n_vec, const uint8_t *packed, int64_t pstride, const float *norms,
+                             const float *eig, const int *meta, const float *cent, const int *offs, int nbytes,
+                             float *out, cudaStream_t s) {
+    if (n_vec <= 0) return cudaSuccess;
+    if (kvd < 2 || nbytes < 1 || nbytes > kvd) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kvd * 4;
+    cudaError_t e = dev::smem(sq_decode_kernel, smem);
+    if (e != cudaSuccess) return e;
+    sq_decode_kernel<<<(unsigned)n_vec, 256, smem, s>>>(kvd, packed, pstride, norms, eig, meta, cent, offs, nbytes, out);
+    return cudaGetLastError();
+}
 
 cudaError_t tq_rotation_device(int dim, const float *g, float *rot, float *rot_t, float *work,
                                cudaStream_t s) {

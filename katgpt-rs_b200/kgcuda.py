@@ -122,6 +122,8 @@ def lib():
             "kg_sq_calibrate_from": (ctypes.c_int, [P, ctypes.POINTER(KgSqParams), P, P, P]),
             "kg_sq_tables": (ctypes.c_int, [P, I32, P, P, P, P, P]),
             "kg_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
+            "kg_sq_encode": (ctypes.c_int, [P, I32, I64, P, P, P]),
+            "kg_sq_decode": (ctypes.c_int, [P, I32, I64, P, P, P]),
             "kg_sq_build_tables": (ctypes.c_int, [ctypes.POINTER(KgSqParams), I64, I32, P, P, P, P, P, P, P, P]),
             "kg_selftest_wait_timeout": (ctypes.c_int, [P, I64]),
             "kg_paged_init": (ctypes.c_int, [P, I32]),
@@ -470,6 +472,23 @@ class CudaBackend:
         d = np.ascontiguousarray(d_eff, np.float32)
         p = params or sq_params()
         self._check(lib().kg_sq_calibrate_from(self._h, ctypes.byref(p), _ptr(e), _ptr(v), _ptr(d)))
+
+    def sq_encode(self, x, layer=0, packed_init=None):
+        """store_vector of x [n][kv_dim]: (packed [n][kv_dim], norms [n])."""
+        x = np.ascontiguousarray(x, np.float32)
+        n, kvd = x.shape
+        packed = np.zeros((n, kvd), np.uint8) if packed_init is None else np.array(packed_init, np.uint8, copy=True)
+        norms = np.empty(n, np.float32)
+        self._check(lib().kg_sq_encode(self._h, layer, n, _ptr(x), _ptr(packed), _ptr(norms)))
+        return packed, norms
+
+    def sq_decode(self, packed, norms, layer=0):
+        """dequantize_*_into of packed rows [n][kv_dim] with norms [n]: [n][kv_dim] f32."""
+        packed = np.ascontiguousarray(packed, np.uint8)
+        norms = np.ascontiguousarray(norms, np.float32)
+        out = np.empty((packed.shape[0], self.cfg.kvd()), np.float32)
+        self._check(lib().kg_sq_decode(self._h, layer, packed.shape[0], _ptr(packed), _ptr(norms), _ptr(out)))
+        return out
 
     def sq_tables(self, layer):
         """(eigenvectors [kvd*kvd], bits [kvd], centroids [kvd][64], n_levels [kvd], d_eff) of one layer."""

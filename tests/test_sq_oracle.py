@@ -82,11 +82,11 @@ def test_identity_calibration_takes_random_rotation(orc):
     assert np.abs(V0.T @ V0 - np.eye(16)).max() < 1e-4
 
 
+@pytest.mark.parametrize("kvd", [16, 128])
 @pytest.mark.parametrize("water_fill", [False, True])
 @pytest.mark.parametrize("avg_bits", [2.0, 3.0, 4.0])
-def test_library_tables_match_oracle(kg, orc, water_fill, avg_bits):
+def test_library_tables_match_oracle(kg, orc, water_fill, avg_bits, kvd):
     rng = np.random.default_rng(int(avg_bits * 10) + water_fill)
-    kvd = 16
     A = (rng.standard_normal((kvd, kvd)) * 0.3).astype(np.float32)
     scale = (2.0 ** -np.arange(kvd)).astype(np.float32)
     X = ((rng.standard_normal((300, kvd)).astype(np.float32) * scale) @ A).astype(np.float32)
