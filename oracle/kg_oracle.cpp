@@ -1821,6 +1821,48 @@ static int sq_tables_from(int64_t kvd, int32_t L, const float *eig, const uint8_
     return 0;
 }
 
+// Pieces of the SpectralQuant build, exposed for the reference's own unit
+// tests (spectral.rs:845-1183, spectral_kv_cache.rs:1243-1274).
+int or_sq_jacobi(const double *m, int64_t dim, float *evals, float *evecs) {
+    if (!m || dim < 1) return -1;
+    std::vector<float> ev, vec;
+    sq_jacobi(std::vector<double>(m, m + dim * dim), dim, ev, vec);
+    std::memcpy(evals, ev.data(), dim * 4);
+    std::memcpy(evecs, vec.data(), dim * dim * 4);
+    return 0;
+}
+// BitAllocator::new(_, max_bits).allocate(d_eff, avg_bits, head_dim) (spectral.rs:420-436)
+void or_sq_allocate(float d_eff, float avg_bits, int64_t head_dim, int max_bits, int32_t *b_high, int32_t *b_low) {
+    const float c = ceilf(d_eff);
+    int64_t d = c > 0.0f ? (int64_t)c : 0;
+    d = std::min<int64_t>(std::max<int64_t>(d, 1), head_dim);
+    float bl = roundf(avg_bits - (float)d / (float)head_dim);
+    bl = fmax_rs(bl, 1.0f);
+    bl = bl < (float)max_bits ? bl : (float)max_bits;
+    *b_low = (int32_t)bl;
+    *b_high = std::min(*b_low + 1, max_bits);
+}
+// waterfill_bits (spectral.rs:443-478); max_bits < 0 means None
+void or_sq_waterfill(const double *ev, int64_t d, int64_t total, int min_bits, int max_bits, uint8_t *out) {
+    const std::vector<uint8_t> b =
+        sq_waterfill(std::vector<double>(ev, ev + d), (size_t)total, min_bits, max_bits < 0 ? 1 << 30 : max_bits);
+    std::memcpy(out, b.data(), d);
+}
+// LloydMaxQuantizer::new(bits, max_iter, seed).fit(data) centroids (spectral.rs:523-589)
+void or_sq_lloyd_fit(const float *data, int64_t n, int bits, int max_iter, uint64_t seed, float *centroids) {
+    const std::vector<float> c = sq_lloyd_fit(std::vector<float>(data, data + n), bits, max_iter, seed);
+    std::memcpy(centroids, c.data(), c.size() * 4);
+}
+// LloydMaxQuantizer::quantize's nearest_centroid (spectral.rs:711-733)
+int64_t or_sq_nearest(float x, const float *centroids, int64_t n) {
+    return (int64_t)sq_nearest(x, std::vector<float>(centroids, centroids + n));
+}
+// pack_variable_bits / unpack_variable_bits (spectral_kv_cache.rs:1125-1187)
+int64_t or_sq_pack(const uint8_t *idx, const uint8_t *bits, int64_t n, uint8_t *out) { return sq_pack(idx, bits, n, out); }
+void or_sq_unpack(const uint8_t *p, int64_t plen, const uint8_t *bits, int64_t n, uint8_t *out) {
+    sq_unpack(p, plen, bits, n, out);
+}
+
 // calibrate_eigenbasis (spectral.rs:226-278): covariance (1/N) sum x x^T in f64,
 // Jacobi, participation ratio. samples [n][dim].
 int or_sq_calibrate_eigenbasis(const float *samples, int64_t n, int64_t dim, float *eigvecs, float *eigvals,

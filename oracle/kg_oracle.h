@@ -140,6 +140,13 @@ int or_forward_paged(const or_config *c, const float *weights, float *pool, cons
  * tables of SpectralQuantKVCache::from_calibration ([L][kvd*kvd] eigenvectors,
  * [L][kvd] bits, [L][kvd][64] centroids, [L][kvd] level counts, [L] d_eff),
  * one store+dequantize round trip, and forward_quantized over the codec. */
+int or_sq_jacobi(const double *m, int64_t dim, float *evals, float *evecs);
+void or_sq_allocate(float d_eff, float avg_bits, int64_t head_dim, int max_bits, int32_t *b_high, int32_t *b_low);
+void or_sq_waterfill(const double *ev, int64_t d, int64_t total, int min_bits, int max_bits, uint8_t *out);
+void or_sq_lloyd_fit(const float *data, int64_t n, int bits, int max_iter, uint64_t seed, float *centroids);
+int64_t or_sq_nearest(float x, const float *centroids, int64_t n);
+int64_t or_sq_pack(const uint8_t *idx, const uint8_t *bits, int64_t n, uint8_t *out);
+void or_sq_unpack(const uint8_t *p, int64_t plen, const uint8_t *bits, int64_t n, uint8_t *out);
 int or_sq_calibrate_eigenbasis(const float *samples, int64_t n, int64_t dim, float *eigvecs, float *eigvals,
                                float *d_eff);
 int or_sq_build(const or_sq_params *P, int64_t kvd, int32_t L, const float *eig_in, const float *eval_in,

@@ -100,6 +100,13 @@ def lib():
             "or_run_batch_tail": (ctypes.c_int, [cp, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, I32, I32, I32, P, ctypes.c_int]),
             "or_forward_paged": (ctypes.c_int, [cp, P, P, P, I64, I32, I32, P]),
             "or_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
+            "or_sq_jacobi": (ctypes.c_int, [P, I64, P, P]),
+            "or_sq_allocate": (None, [F32, F32, I64, ctypes.c_int, P, P]),
+            "or_sq_waterfill": (None, [P, I64, I64, ctypes.c_int, ctypes.c_int, P]),
+            "or_sq_lloyd_fit": (None, [P, I64, ctypes.c_int, ctypes.c_int, U64, P]),
+            "or_sq_nearest": (I64, [F32, P, I64]),
+            "or_sq_pack": (I64, [P, P, I64, P]),
+            "or_sq_unpack": (None, [P, I64, P, I64, P]),
             "or_sq_build": (ctypes.c_int, [ctypes.POINTER(OrSqParams), I64, I32, P, P, P, P, P, P, P, P]),
             "or_sq_roundtrip": (I64, [I64, P, P, P, P, P, P, P, P]),
             "or_run_sequence_sq": (ctypes.c_int, [cp, P, P, P, P, P, P, I32, P, P, P]),
@@ -556,3 +563,54 @@ def run_sequence_sq(cfg, w, tabs, tokens):
     if rc:
         raise RuntimeError(f"or_run_sequence_sq failed: {rc}")
     return logits, codes, norms
+
+
+def sq_jacobi(m):
+    """jacobi_eigendecompose (spectral.rs:73-158) of a symmetric f64 matrix: (eigenvalues, eigenvectors row-major)."""
+    m = np.ascontiguousarray(m, np.float64)
+    d = m.shape[0]
+    ev, vec = np.empty(d, np.float32), np.empty(d * d, np.float32)
+    lib().or_sq_jacobi(_p(m), d, _p(ev), _p(vec))
+    return ev, vec.reshape(d, d)
+
+
+def sq_allocate(d_eff, avg_bits, head_dim, max_bits=8):
+    """BitAllocator::allocate: (b_high, b_low)."""
+    bh, bl = ctypes.c_int32(0), ctypes.c_int32(0)
+    lib().or_sq_allocate(d_eff, avg_bits, head_dim, max_bits, ctypes.byref(bh), ctypes.byref(bl))
+    return bh.value, bl.value
+
+
+def sq_waterfill(ev, total, min_bits, max_bits=None):
+    ev = np.ascontiguousarray(ev, np.float64)
+    out = np.empty(ev.size, np.uint8)
+    lib().or_sq_waterfill(_p(ev), ev.size, total, min_bits, -1 if max_bits is None else max_bits, _p(out))
+    return out
+
+
+def sq_lloyd_fit(data, bits, max_iter, seed):
+    data = f32(data)
+    out = np.empty(1 << bits, np.float32)
+    lib().or_sq_lloyd_fit(_p(data) if data.size else None, data.size, bits, max_iter, seed, _p(out))
+    return out
+
+
+def sq_nearest(x, centroids):
+    c = f32(centroids)
+    return int(lib().or_sq_nearest(np.float32(x), _p(c), c.size))
+
+
+def sq_pack(idx, bits):
+    idx = np.ascontiguousarray(idx, np.uint8)
+    bits = np.ascontiguousarray(bits, np.uint8)
+    out = np.zeros(idx.size, np.uint8)
+    n = lib().or_sq_pack(_p(idx), _p(bits), idx.size, _p(out))
+    return out[:n]
+
+
+def sq_unpack(packed, bits, n):
+    packed = np.ascontiguousarray(packed, np.uint8)
+    bits = np.ascontiguousarray(bits, np.uint8)
+    out = np.empty(n, np.uint8)
+    lib().or_sq_unpack(_p(packed), packed.size, _p(bits), n, _p(out))
+    return out

@@ -113,3 +113,62 @@ def test_forward_quantized_over_spectralquant_runs(orc):
     # the quantized forward stays close to forward_base on this model
     base = orc.run_sequence(cfg, orc.MODE_BASE, w, toks)[0]
     assert np.abs(logits - base).max() < 0.5 * np.abs(base).max()
+
+
+# ---- the reference's unit tests of the building blocks (spectral.rs:845-1183,
+# spectral_kv_cache.rs:1243-1274), on the oracle's restatement
+
+def test_jacobi_reference_cases(orc):
+    ev, V = orc.sq_jacobi(np.eye(4))                                  # identity
+    assert np.all(np.abs(ev - 1) < 0.01) and np.all(np.abs(V - np.eye(4)) < 0.1)
+    ev, _ = orc.sq_jacobi(np.diag([3.0, 1.0, 2.0]))                   # diagonal, sorted descending
+    assert np.all(np.abs(ev - [3, 2, 1]) < 0.01)
+    ev, V = orc.sq_jacobi(np.array([[2.0, 1.0], [1.0, 3.0]]))         # 2x2
+    assert abs(ev.sum() - 5.0) < 0.01 and abs(V[0, 0] * V[0, 1] + V[1, 0] * V[1, 1]) < 0.01
+    A = np.array([[4.0, 1, 2], [1, 3, 1], [2, 1, 5]])                 # known symmetric 3x3
+    ev, V = orc.sq_jacobi(A)
+    assert abs(ev.sum() - 12.0) < 0.01 and abs(np.prod(ev) - 43.0) < 0.5
+    assert np.abs(V.T @ V - np.eye(3)).max() < 0.01
+    D = V.T @ A.astype(np.float32) @ V
+    assert np.abs(np.diag(D) - ev).max() < 0.1 and np.abs(D - np.diag(np.diag(D))).max() < 0.05
+
+
+def test_bit_allocator_reference_cases(orc):
+    bh, bl = orc.sq_allocate(6.0, 3.0, 128)
+    assert bh >= bl and bh >= 1
+    bh, bl = orc.sq_allocate(10.0, 3.0, 128)
+    assert (bh, bl) == (4, 3)                                         # b_low = round(3 - 10/128)
+    bh, bl = orc.sq_allocate(2.0, 4.0, 128)
+    assert bh >= bl and bl >= 2
+
+
+def test_waterfill_reference_cases(orc):
+    b = orc.sq_waterfill([10.0, 5.0, 1.0, 0.5], 16, 2)
+    assert b.size == 4 and int(b.sum()) == 16 and b[0] >= b[1]
+    b = orc.sq_waterfill([5.0, 3.0, 1.0], 15, 3)
+    assert np.all(b >= 3) and int(b.sum()) == 15
+    b = orc.sq_waterfill([10.0, 1.0], 10, 2, 4)
+    assert np.all(b <= 4)
+
+
+def test_lloyd_max_reference_cases(orc):
+    data = (np.arange(100, dtype=np.float32) - np.float32(50.0)) / np.float32(50.0)
+    c = orc.sq_lloyd_fit(data, 2, 50, 42)
+    assert c.size == 4
+    for x in (-0.8, -0.2, 0.2, 0.8):
+        assert abs(x - c[orc.sq_nearest(x, c)]) < 0.5
+    s = np.sin(np.arange(200, dtype=np.float32) / np.float32(200.0)).astype(np.float32)
+    def mse(c):
+        return np.mean([(float(v) - float(c[orc.sq_nearest(v, c)])) ** 2 for v in s])
+    assert mse(orc.sq_lloyd_fit(s, 4, 50, 42)) < mse(orc.sq_lloyd_fit(s, 2, 50, 42))
+    d = np.arange(50, dtype=np.float32) * np.float32(0.1)
+    assert np.array_equal(orc.sq_lloyd_fit(d, 3, 20, 99), orc.sq_lloyd_fit(d, 3, 20, 99))
+    assert np.array_equal(orc.sq_lloyd_fit(np.zeros(0, np.float32), 2, 10, 42), np.zeros(4, np.float32))
+
+
+@pytest.mark.parametrize("idx,bits", [([0, 1, 2, 3, 0, 2, 1, 3], [2] * 8), ([3, 7, 15, 1, 0], [2, 3, 4, 1, 1]),
+                                      ([1, 0, 1, 1, 0, 0, 1, 0], [1] * 8)])
+def test_pack_unpack_reference_cases(orc, idx, bits):
+    p = orc.sq_pack(idx, bits)
+    assert p.size == (sum(bits) + 7) // 8
+    assert list(orc.sq_unpack(p, bits, len(idx))) == [i & ((1 << b) - 1) for i, b in zip(idx, bits)]
