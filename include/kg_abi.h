@@ -278,7 +278,10 @@ int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, c
  * the pages, the MLP and delta routing as forward; for each sequence in batch
  * order they call ensure_pages(seq, p) for every position p of the call
  * first. kg_forward_batch_dev expects the caller to have done those ensures
- * with kg_paged_ensure. Micro widths (Config::micro()), block_size 16 or 64. */
+ * with kg_paged_ensure. Two device forms: the exact f32 path at the micro
+ * widths (Config::micro(), block_size 16 or 64; f32 pages, logits
+ * bit-identical to the reference order), and the bf16 tensor-core path at
+ * model widths (KG_W_BF16 weights, standard attention over bf16 pages). */
 
 /* PagedKVCache::new(config, max_sequences) (:215-238): drop every page and
  * sequence, then max_sequences empty sequences and (block_size/16 + 1) *

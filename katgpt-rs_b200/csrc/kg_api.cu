@@ -216,8 +216,11 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     ctx->w_count = kg::weights_count(c);
     const bool tq = kg::kv_is_tq(c.kv_mode);
     const bool paged = c.kv_mode == KG_KV_PAGED, sqm = c.kv_mode == KG_KV_SQ;
-    if (paged && !ctx->micro)
-        return bail(fail(ctx, KG_ERR_UNSUPPORTED, "forward_paged runs the micro widths at block_size 16 or 64"));
+    if (paged && !ctx->micro) {
+        std::string bwhy;
+        if (kg::big_supported(c, bwhy) != 0)
+            return bail(fail(ctx, KG_ERR_UNSUPPORTED, "forward_paged: no device forward for this shape (" + bwhy + ")"));
+    }
     ctx->kpl = tq ? packed_len(ctx->kvd, c.key_bits) : 0;
     ctx->vpl = tq ? packed_len(ctx->kvd, c.val_bits) : 0;
     if (sqm) ctx->kpl = ctx->vpl = ctx->kvd;  // variable-width pack, at most one byte per dimension
@@ -275,6 +278,11 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
             ctx->big_path = true;
             e = kg::big_init(ctx);
             if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "bf16 path init"));
+            if (paged) {  // PagedKVCache::new(config, 1), bf16 pages
+                e = kg::paged_alloc(ctx);
+                if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "paged KV pool"));
+                if ((rc = kg_paged_init(ctx, 1))) return bail(rc);
+            }
             if ((rc = kg_seq_reset_all(ctx))) return bail(rc);
         }
         // Otherwise a codec-only context: TurboQuant tables and the encoder
@@ -438,13 +446,14 @@ int kg_download_weights(kg_ctx *ctx, float *out, int64_t count) {
 
 int kg_seq_reset(kg_ctx *ctx, int32_t seq) {
     if (!ctx || seq < 0 || seq >= ctx->cfg.max_seqs) return KG_ERR_INVALID_ARG;
+    if (ctx->cfg.kv_mode == KG_KV_PAGED && (ctx->micro || ctx->big_path))
+        return kg_paged_rollback(ctx, seq, 0);  // the sequence's pages back
     if (ctx->big_path) {
         KG_CUDA(ctx, cudaSetDevice(ctx->device));
         KG_CUDA(ctx, kg::big_reset(ctx, seq, 1));
         return KG_OK;
     }
     if (!ctx->micro) return KG_OK;
-    if (ctx->cfg.kv_mode == KG_KV_PAGED) return kg_paged_rollback(ctx, seq, 0);  // the sequence's pages back
     KG_CUDA(ctx, cudaSetDevice(ctx->device));
     const size_t rows = (size_t)ctx->L * ctx->B, r0 = (size_t)seq * rows;
     cudaStream_t s = ctx->stream;
@@ -464,7 +473,7 @@ int kg_seq_reset_all(kg_ctx *ctx) {
         KG_CUDA(ctx, cudaSetDevice(ctx->device));
         KG_CUDA(ctx, kg::big_reset(ctx, 0, ctx->cfg.max_seqs));
         KG_CUDA(ctx, cudaMemset(ctx->d_err, 0, 4));
-        return KG_OK;
+        return ctx->cfg.kv_mode == KG_KV_PAGED ? kg_paged_reset(ctx) : KG_OK;
     }
     if (!ctx->micro) return KG_OK;
     if (ctx->cfg.kv_mode == KG_KV_PAGED) {
@@ -565,6 +574,7 @@ int kg_forward_batch_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
     if (ctx->big_path) {
         KG_CUDA(ctx, cudaSetDevice(ctx->device));
         cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (ctx->cfg.kv_mode == KG_KV_PAGED) KG_CUDA(ctx, kg::paged_flush(ctx, s));  // tables and reused pages first
         if (T == 1 && s != nullptr && !ctx->prof && n_seq <= std::min<int64_t>(ctx->big.ws_tokens, ctx->cfg.max_seqs))
             return forward_graph(ctx, n_seq, seq_ids, tokens, start_pos, logits, probs, s);
         cudaError_t e = kg::big_forward(ctx, n_seq, seq_ids, tokens, start_pos, T, logits, probs, s);
@@ -605,7 +615,7 @@ int kg_forward_batch(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const i
     }
     for (int64_t i = 0; i < (int64_t)n_seq * T; ++i)
         if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, KG_ERR_INVALID_ARG, "token out of range");
-    if (ctx->micro && ctx->cfg.kv_mode == KG_KV_PAGED) {  // forward_paged's ensure_pages, per call in order
+    if ((ctx->micro || ctx->big_path) && ctx->cfg.kv_mode == KG_KV_PAGED) {  // forward_paged's ensure_pages, in order
         int rc = kg::paged_ensure_batch(ctx, n_seq, seq_ids, start_pos, T);
         if (rc) return rc;
     }

@@ -77,15 +77,25 @@ __device__ __forceinline__ void build_lut(uint2 *lut, const float *cent) {
 // decode attend over the same cached values.
 __global__ void kv_store_std_kernel(const float *qkv, int64_t ldx, int64_t koff, int64_t voff, int kvd,
                                     const int32_t *slot, const int32_t *pos, int L, int B, int layer, bf16 *kc,
-                                    bf16 *vc, __half *kt, __half *kt2, __half *vt, __half *vt2) {
+                                    bf16 *vc, __half *kt, __half *kt2, __half *vt, __half *vt2, const int32_t *ptab,
+                                    int maxp, int S, int n_pages, int *err) {
     pdl_wait();
     const int m = blockIdx.x;
-    const int64_t row = ((int64_t)slot[m] * L + layer) * B + pos[m];
+    int64_t krow = ((int64_t)slot[m] * L + layer) * B + pos[m], vrow = krow;
+    if (ptab) {  // PagedKVCache::write_kv (kv_cache.rs:298-309): the page that holds pos
+        const int pg = ptab[((int64_t)layer * S + slot[m]) * maxp + (pos[m] >> 4)];
+        if (pg < 0 || pg >= n_pages) {  // no page: nothing is written, the call reports it
+            if (threadIdx.x == 0 && err) atomicExch(err, 1);
+            return;
+        }
+        krow = (int64_t)pg * 32 + (pos[m] & 15);
+        vrow = krow + 16;
+    }
     for (int j = threadIdx.x; j < kvd; j += blockDim.x) {
         const bf16 k = __float2bfloat16_rn(qkv[(int64_t)m * ldx + koff + j]);
         const bf16 v = __float2bfloat16_rn(qkv[(int64_t)m * ldx + voff + j]);
-        kc[row * kvd + j] = k;
-        vc[row * kvd + j] = v;
+        kc[krow * kvd + j] = k;
+        vc[vrow * kvd + j] = v;
         if (kt) {
             const float kf = __bfloat162float(k), vf = __bfloat162float(v);
             const __half kh = __float2half_rn(kf), vh = __float2half_rn(vf);
@@ -112,6 +122,25 @@ __global__ void __launch_bounds__(128) std_decode_kernel(const StdDecodeArgs a) 
     const int64_t base = ((int64_t)a.slot[m] * a.L + a.layer) * a.B;
     const bf16 *K = a.kc + base * a.kvd + kh * HD + lane * DPL;
     const bf16 *Vp = a.vc + base * a.kvd + kh * HD + lane * DPL;
+    // paged cache: row t of this sequence's layer lives at page tab[t / 16]
+    const int32_t *tab = a.ptab ? a.ptab + ((int64_t)a.layer * a.S + a.slot[m]) * a.maxp : nullptr;
+    if (tab) {
+        bool bad = false;
+        for (int q = threadIdx.x; q <= (tn - 1) >> 4; q += blockDim.x)
+            bad |= q >= a.maxp || tab[q] < 0 || tab[q] >= a.n_pages;
+        if (__syncthreads_or(bad)) {  // CTA-uniform: no page to read, the call reports it
+            if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
+            return;
+        }
+    }
+    auto krow = [&](int t) -> const bf16 * {
+        if (tab) return a.kc + ((int64_t)tab[t >> 4] * 32 + (t & 15)) * a.kvd + kh * HD + lane * DPL;
+        return K + (int64_t)t * a.kvd;
+    };
+    auto vrow = [&](int t) -> const bf16 * {
+        if (tab) return a.vc + ((int64_t)tab[t >> 4] * 32 + 16 + (t & 15)) * a.kvd + kh * HD + lane * DPL;
+        return Vp + (int64_t)t * a.kvd;
+    };
     auto load = [&](const bf16 *p, float (&f)[DPL]) {
         if constexpr (DPL == 4) {
             const uint2 w = *reinterpret_cast<const uint2 *>(p);
@@ -136,8 +165,8 @@ __global__ void __launch_bounds__(128) std_decode_kernel(const StdDecodeArgs a) 
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int t = min(t0 + u, tn - 1);
-                load(K + (int64_t)t * a.kvd, kf[u]);
-                load(Vp + (int64_t)t * a.kvd, vf[u]);
+                load(krow(t), kf[u]);
+                load(vrow(t), vf[u]);
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
@@ -409,10 +438,11 @@ cudaError_t flash_prefill(const FlashArgs &a, cudaStream_t s) {
 
 cudaError_t kv_store_std(const float *qkv, int64_t ldx, int64_t koff, int64_t voff, int kvd, int M,
                          const int32_t *slot, const int32_t *pos, int L, int B, int layer, bf16 *kc, bf16 *vc,
-                         __half *kt, __half *kt2, __half *vt, __half *vt2, cudaStream_t s) {
+                         __half *kt, __half *kt2, __half *vt, __half *vt2, cudaStream_t s, const int32_t *ptab,
+                         int maxp, int S, int n_pages, int *err) {
     if (M <= 0) return cudaSuccess;
     return launch_pdl(kv_store_std_kernel, dim3(M), dim3(256), 0, s, qkv, ldx, koff, voff, kvd, slot, pos, L, B, layer,
-                      kc, vc, kt, kt2, vt, vt2);
+                      kc, vc, kt, kt2, vt, vt2, ptab, maxp, S, n_pages, err);
 }
 
 cudaError_t std_decode(const StdDecodeArgs &a, cudaStream_t s) {

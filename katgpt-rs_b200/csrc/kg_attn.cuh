@@ -62,13 +62,19 @@ struct StdDecodeArgs {
     int64_t ldo;
     int M, nh, nkv, hd, kvd, L, B, layer;
     float scale;
+    // paged cache (forward_paged): kc = vc = the page pool [page][K 16 rows |
+    // V 16 rows][kv_dim]; ptab [L][S][maxp] page indices; a missing page sets *err
+    const int32_t *ptab = nullptr;
+    int maxp = 0, S = 0, n_pages = 0;
+    int *err = nullptr;
 };
 cudaError_t std_decode(const StdDecodeArgs &a, cudaStream_t s);
 // new K / V rows into the bf16 cache; kt.. (optional) receive the f16 hi / lo
 // split of the bf16-rounded rows for the prefill flash kernel
 cudaError_t kv_store_std(const float *qkv, int64_t ldx, int64_t koff, int64_t voff, int kvd, int M,
                          const int32_t *slot, const int32_t *pos, int L, int B, int layer, __nv_bfloat16 *kc,
-                         __nv_bfloat16 *vc, __half *kt, __half *kt2, __half *vt, __half *vt2, cudaStream_t s);
+                         __nv_bfloat16 *vc, __half *kt, __half *kt2, __half *vt, __half *vt2, cudaStream_t s,
+                         const int32_t *ptab = nullptr, int maxp = 0, int S = 0, int n_pages = 0, int *err = nullptr);
 cudaError_t centroids(const uint8_t *codes, int pl, const int32_t *slot, const int32_t *pos, int L, int B, int layer,
                       const float *cent, int kvd, int M, __half *out, __half *out_lo, cudaStream_t s);
 cudaError_t gather_norms(const float *norms, const int32_t *slot, const int32_t *pos, int L, int B, int layer, int M,

@@ -111,7 +111,6 @@ cudaError_t dalloc(T **p, size_t count, std::vector<void *> &owned) {
 
 int big_supported(const kg_config &c, std::string &why) {
     if (c.weight_dtype != KG_W_BF16) return why = "the tensor-core path runs bf16 weights (KG_W_BF16)", -1;
-    if (c.kv_mode == KG_KV_PAGED) return why = "forward_paged runs on the exact micro path", -1;
     if (c.kv_mode == KG_KV_SQ) return why = "the SpectralQuant forward runs on the exact micro path", -1;
     if (c.kv_mode != KG_KV_F32)
         for (int b : {c.key_bits, c.val_bits})
@@ -150,8 +149,9 @@ cudaError_t big_init(kg_ctx *ctx) {
     BIG_TRY(dalloc(&g.ag, L * n, own));
     BIG_TRY(dalloc(&g.mg, L * n, own));
     BIG_TRY(dalloc(&g.pdelta, S * n, own));
-    g.std_kv = c.kv_mode == KG_KV_F32;
-    if (g.std_kv) {  // standard attention: bf16 K/V arena
+    g.std_kv = c.kv_mode == KG_KV_F32 || c.kv_mode == KG_KV_PAGED;
+    g.paged = c.kv_mode == KG_KV_PAGED;  // K/V rows in the page pool instead (kg_paged.cu)
+    if (g.std_kv && !g.paged) {  // standard attention: bf16 K/V arena
         BIG_TRY(dalloc(&g.kcache, (size_t)S * L * B * kvd, own));
         BIG_TRY(dalloc(&g.vcache, (size_t)S * L * B * kvd, own));
     } else {
@@ -237,6 +237,7 @@ cudaError_t big_reset(kg_ctx *ctx, int64_t slot0, int64_t nslots) {
     BigState &g = ctx->big;
     const size_t rows = (size_t)ctx->L * ctx->B;
     cudaStream_t s = ctx->stream;
+    if (g.paged) return cudaSuccess;  // pages are zeroed when they are handed out
     if (g.std_kv) {
         const size_t e = rows * ctx->kvd;
         BIG_TRY(cudaMemsetAsync(g.kcache + slot0 * e, 0, nslots * e * 2, s));
@@ -387,7 +388,8 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         // forward_base (standard attention) applies attn_norm_gamma at run time
         // (kog_cpu_fusion, src/transformer.rs:1893-1895); forward_quantized and
         // forward_sp_kv_quant use plain rmsnorm (:4076, sp_kv/forward.rs:649-651)
-        if (spkv) {
+        // forward_paged normalises twice too, without gammas (src/transformer.rs:3361-3364)
+        if (spkv || g.paged) {
             BIG_TRY(bf::rmsnorm(g.x, n, M, g.xr, nullptr, nullptr, false, s));
             BIG_TRY(bf::rmsnorm(g.xr, n, M, nullptr, g.xb, g.xb2, false, s));
         } else {
@@ -433,8 +435,15 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         if (g.std_kv) {
             // standard attention: K/V rows into the bf16 cache (and the prompt's
             // f16 hi/lo copies for the flash kernel)
-            BIG_TRY(attn::kv_store_std(g.qkv, nqkv, n, n + kvd, kvd, M, g.slot_of, g.pos_of, L, B, l, g.kcache,
-                                       g.vcache, prefill ? g.kt : nullptr, g.kt2, g.vt, g.vt2, s));
+            if (g.paged) {  // write_kv into the sequence's page (kv_cache.rs:298-309)
+                bf16 *pool = static_cast<bf16 *>(ctx->paged.pool);
+                BIG_TRY(attn::kv_store_std(g.qkv, nqkv, n, n + kvd, kvd, M, g.slot_of, g.pos_of, L, B, l, pool, pool,
+                                           prefill ? g.kt : nullptr, g.kt2, g.vt, g.vt2, s, ctx->paged.d_tab,
+                                           ctx->paged.maxp, c.max_seqs, (int)ctx->paged.cap, ctx->d_err));
+            } else {
+                BIG_TRY(attn::kv_store_std(g.qkv, nqkv, n, n + kvd, kvd, M, g.slot_of, g.pos_of, L, B, l, g.kcache,
+                                           g.vcache, prefill ? g.kt : nullptr, g.kt2, g.vt, g.vt2, s));
+            }
         } else if (M >= 256) {
             // prefill-sized: K and V rows together, exact norms and xn, rotation
             // on the tensor cores, codes with exact recomputation next to the
@@ -467,6 +476,11 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
             sa.Q = g.qkv; sa.ldq = nqkv; sa.kc = g.kcache; sa.vc = g.vcache; sa.slot = g.slot_of; sa.pos = g.pos_of;
             sa.O = g.attf; sa.ldo = n; sa.M = M; sa.nh = nh; sa.nkv = (int)ctx->nkv; sa.hd = hd; sa.kvd = kvd;
             sa.L = L; sa.B = B; sa.layer = l; sa.scale = scale;
+            if (g.paged) {  // read_kv of positions 0..pos through the page table
+                sa.kc = sa.vc = static_cast<const bf16 *>(ctx->paged.pool);
+                sa.ptab = ctx->paged.d_tab; sa.maxp = ctx->paged.maxp; sa.S = c.max_seqs;
+                sa.n_pages = (int)ctx->paged.cap; sa.err = ctx->d_err;
+            }
             prof_mark(ctx, KG_PROF_ATTN, 0, s);
             BIG_TRY(attn::std_decode(sa, s));
             prof_mark(ctx, KG_PROF_ATTN, 1, s);
@@ -534,7 +548,7 @@ cudaError_t run_layers(kg_ctx *ctx, int M, bool prefill, int n_seq, int T, cudaS
         // MLP
         // also clears alive counts; mlp_norm_gamma for forward_base (src/transformer.rs:2023-2026)
         BIG_TRY(bf::rmsnorm(g.x, n, M, nullptr, g.xb, g.xb2, false, s, g.alive,
-                            g.std_kv ? g.mg + (int64_t)l * n : nullptr));
+                            g.std_kv && !g.paged ? g.mg + (int64_t)l * n : nullptr));
         bf::Gemm u = gemm0();
         u.A = g.xb; u.A2 = g.xb2; u.lda = n; u.B = w1; u.ldb = n; u.M = M; u.N = m; u.K = n;
         u.epi = bf::EPI_RELU; u.Cb = g.hid; u.Cb2 = g.hid2; u.ldcb = m; u.row_alive = g.alive;

@@ -57,7 +57,7 @@ struct PagedState {
     int64_t total = 0;                                      // pages ever handed out
     int64_t cap = 0;                                        // device pool capacity (pages)
     int maxp = 0;                                           // device table width (pages per list)
-    float *pool = nullptr;                                  // [cap][2][16][kvd]
+    void *pool = nullptr;                                   // [cap][2][16][kvd] f32 (micro) or bf16
     int32_t *d_tab = nullptr;                               // [L][max_seqs][maxp], -1 = none
     std::vector<int32_t> h_tab;
     std::vector<int32_t> zero_list;                         // reused pages to zero before the next use
@@ -154,6 +154,7 @@ struct BigState {
     int32_t *slot_of = nullptr, *pos_of = nullptr, *tok_of = nullptr;
     // standard attention (kv_mode KG_KV_F32): bf16 K/V cache [slot][layer][pos][kv_dim]
     bool std_kv = false;
+    bool paged = false;  // std_kv rows in the PagedKVCache pool (kv_mode KG_KV_PAGED)
     __nv_bfloat16 *kcache = nullptr, *vcache = nullptr;
     // two-kernel decode attention scratch: e rows [max_seqs][nh][Sp] and
     // 16-position chunk maxima / sums [max_seqs][Sp / 16][nh]

@@ -32,8 +32,27 @@ int pcuda(kg_ctx *ctx, cudaError_t e, const char *what) {
                  std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-bool is_paged(const kg_ctx *ctx) { return ctx && ctx->micro && ctx->cfg.kv_mode == KG_KV_PAGED; }
-int64_t page_floats(const kg_ctx *ctx) { return 2 * kPage * ctx->kvd; }
+bool is_paged(const kg_ctx *ctx) {
+    return ctx && (ctx->micro || ctx->big_path) && ctx->cfg.kv_mode == KG_KV_PAGED;
+}
+// element size of the pool: f32 rows on the exact micro path, bf16 on the tensor-core path
+int64_t elem_bytes(const kg_ctx *ctx) { return ctx->micro ? 4 : 2; }
+int64_t page_bytes(const kg_ctx *ctx) { return 2 * kPage * ctx->kvd * elem_bytes(ctx); }
+
+// f32 <-> bf16 (round to nearest even) for the host-side row access of a bf16 pool
+uint16_t to_bf16_bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);  // NaN stays NaN
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+float from_bf16_bits(uint16_t h) {
+    const uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
 
 // alloc_page (:241-262): reuse from the free list (zeroed) or take the next
 // index; the reference grows its pool, here the pool's capacity bounds it.
@@ -82,7 +101,7 @@ cudaError_t paged_flush(kg_ctx *ctx, cudaStream_t s) {
         P.zero_list.erase(std::unique(P.zero_list.begin(), P.zero_list.end()), P.zero_list.end());
         const int n = (int)P.zero_list.size();
         cudaError_t e = cudaMemcpyAsync(P.d_zero, P.zero_list.data(), n * sizeof(int32_t), cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) e = zero_pages(P.pool, P.d_zero, n, page_floats(ctx), s);
+        if (e == cudaSuccess) e = zero_pages(static_cast<float *>(P.pool), P.d_zero, n, page_bytes(ctx) / 4, s);
         if (e != cudaSuccess) return e;
         P.zero_list.clear();
     }
@@ -110,7 +129,7 @@ cudaError_t paged_alloc(kg_ctx *ctx) {
     P.maxp = (int)(ctx->B / kPage + 1);
     const int64_t initial = (ctx->B / kPage + 1) * L;  // PagedKVCache::new (:217-219)
     P.cap = std::max<int64_t>(initial, 2 * S * L * P.maxp);
-    cudaError_t e = cudaMalloc(&P.pool, (size_t)P.cap * page_floats(ctx) * sizeof(float));
+    cudaError_t e = cudaMalloc(&P.pool, (size_t)P.cap * page_bytes(ctx));
     if (e == cudaSuccess) e = cudaMalloc(&P.d_tab, (size_t)L * S * P.maxp * sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMalloc(&P.d_zero, (size_t)P.cap * sizeof(int32_t));
     if (e != cudaSuccess) return e;
@@ -118,10 +137,12 @@ cudaError_t paged_alloc(kg_ctx *ctx) {
     ctx->allocs.push_back(P.d_tab);
     ctx->allocs.push_back(P.d_zero);
     P.h_tab.assign((size_t)L * S * P.maxp, -1);
-    ctx->margs.pool = P.pool;
-    ctx->margs.ptab = P.d_tab;
-    ctx->margs.maxp = P.maxp;
-    ctx->margs.n_pages = (int)P.cap;
+    if (ctx->micro) {  // the exact micro kernel reads the pool through its arguments
+        ctx->margs.pool = static_cast<float *>(P.pool);
+        ctx->margs.ptab = P.d_tab;
+        ctx->margs.maxp = P.maxp;
+        ctx->margs.n_pages = (int)P.cap;
+    }
     return cudaSuccess;
 }
 
@@ -155,7 +176,7 @@ int kg_paged_init(kg_ctx *ctx, int32_t max_sequences) {
     P.zero_list.clear();
     P.dirty = true;
     cudaError_t e = cudaSetDevice(ctx->device);
-    if (e == cudaSuccess) e = cudaMemsetAsync(P.pool, 0, (size_t)P.cap * page_floats(ctx) * sizeof(float), ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(P.pool, 0, (size_t)P.cap * page_bytes(ctx), ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) return pcuda(ctx, e, "paged pool clear");
     return KG_OK;
@@ -229,26 +250,35 @@ int kg_paged_reset(kg_ctx *ctx) {
     return KG_OK;
 }
 
-static int kv_page_row(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, float **krow) {
+static int kv_page_row(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, char **krow) {
     kg::PagedState &P = ctx->paged;
     if (layer < 0 || layer >= (int32_t)P.tables.size() || seq < 0 || pos < 0 ||
         (size_t)seq >= P.tables[layer].size() || (size_t)pos / kPage >= P.tables[layer][seq].size())
         return pfail(ctx, KG_ERR_INVALID_ARG, "no page for (layer, seq, pos)");
     const int64_t pg = P.tables[layer][seq][pos / kPage];
-    *krow = P.pool + (pg * 2 * kPage + pos % kPage) * ctx->kvd;
+    *krow = static_cast<char *>(P.pool) + (pg * 2 * kPage + pos % kPage) * ctx->kvd * elem_bytes(ctx);
     return KG_OK;
 }
 
 int kg_paged_write_kv(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, const float *k, const float *v) {
     if (!is_paged(ctx)) return ctx ? pfail(ctx, KG_ERR_UNSUPPORTED, "context is not kv_mode KG_KV_PAGED") : KG_ERR_INVALID_ARG;
     if (!k || !v) return pfail(ctx, KG_ERR_INVALID_ARG, "null K/V");
-    float *kr;
+    char *kr;
     if (int rc = kv_page_row(ctx, layer, seq, pos, &kr)) return rc;
+    const int64_t kvd = ctx->kvd, eb = elem_bytes(ctx);
+    std::vector<uint16_t> hk, hv;  // bf16 pools store the rows rounded to bf16
+    const void *sk = k, *sv = v;
+    if (eb == 2) {
+        hk.resize(kvd);
+        hv.resize(kvd);
+        for (int64_t j = 0; j < kvd; ++j) hk[j] = to_bf16_bits(k[j]), hv[j] = to_bf16_bits(v[j]);
+        sk = hk.data();
+        sv = hv.data();
+    }
     cudaError_t e = cudaSetDevice(ctx->device);
     if (e == cudaSuccess) e = kg::paged_flush(ctx, ctx->stream);
-    const size_t b = ctx->kvd * sizeof(float);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(kr, k, b, cudaMemcpyHostToDevice, ctx->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(kr + kPage * ctx->kvd, v, b, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(kr, sk, kvd * eb, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(kr + kPage * kvd * eb, sv, kvd * eb, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     return e == cudaSuccess ? KG_OK : pcuda(ctx, e, "paged write_kv");
 }
@@ -256,15 +286,20 @@ int kg_paged_write_kv(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, cons
 int kg_paged_read_kv(kg_ctx *ctx, int32_t layer, int32_t seq, int32_t pos, float *k, float *v) {
     if (!is_paged(ctx)) return ctx ? pfail(ctx, KG_ERR_UNSUPPORTED, "context is not kv_mode KG_KV_PAGED") : KG_ERR_INVALID_ARG;
     if (!k || !v) return pfail(ctx, KG_ERR_INVALID_ARG, "null K/V");
-    float *kr;
+    char *kr;
     if (int rc = kv_page_row(ctx, layer, seq, pos, &kr)) return rc;
+    const int64_t kvd = ctx->kvd, eb = elem_bytes(ctx);
+    std::vector<uint16_t> hk(eb == 2 ? kvd : 0), hv(eb == 2 ? kvd : 0);
+    void *dk = eb == 2 ? (void *)hk.data() : (void *)k, *dv = eb == 2 ? (void *)hv.data() : (void *)v;
     cudaError_t e = cudaSetDevice(ctx->device);
     if (e == cudaSuccess) e = kg::paged_flush(ctx, ctx->stream);
-    const size_t b = ctx->kvd * sizeof(float);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(k, kr, b, cudaMemcpyDeviceToHost, ctx->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(v, kr + kPage * ctx->kvd, b, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dk, kr, kvd * eb, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dv, kr + kPage * kvd * eb, kvd * eb, cudaMemcpyDeviceToHost, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-    return e == cudaSuccess ? KG_OK : pcuda(ctx, e, "paged read_kv");
+    if (e != cudaSuccess) return pcuda(ctx, e, "paged read_kv");
+    if (eb == 2)
+        for (int64_t j = 0; j < kvd; ++j) k[j] = from_bf16_bits(hk[j]), v[j] = from_bf16_bits(hv[j]);
+    return KG_OK;
 }
 
 int kg_paged_table(const kg_ctx *ctx, int32_t layer, int32_t seq, int32_t *pages_out, int32_t cap,

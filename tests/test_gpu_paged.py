@@ -151,3 +151,47 @@ def test_paged_write_read_and_errors(kg, orc):
     with pytest.raises(kg.KgError):
         be.kv_snapshot(0, 0, None)           # paged contexts roll back through their page tables
     be.close()
+
+
+def test_forward_paged_bf16_matches_oracle(kg, orc):
+    # forward_paged at model widths on the tensor-core path: bf16 K/V rows in
+    # pages of the pool, read through the page table by the standard-attention
+    # decode kernel; the prompt through the prefill path, then multi-position
+    # calls, decode steps (captured as a CUDA graph from the second call of a
+    # shape), forks inside and on page boundaries, and a rollback. Logits within
+    # 2e-2 of the oracle's f32 forward_paged on the same bf16-rounded weights
+    # (max |gpu - ref| / max |ref| per position); page bookkeeping identical.
+    cfg = kg.micro_config(vocab_size=96, block_size=64, n_embd=256, n_head=4, head_dim=64, n_kv_head=4,
+                          mlp_hidden=512, n_layer=4, kv_mode=kg.KG_KV_PAGED, weight_dtype=kg.KG_W_BF16, max_seqs=8)
+    be = kg.CudaBackend(cfg)
+    w = kg.bf16_round(kg.reference_weights(cfg, seed=11, scale_mode=1, std=0.02))
+    be.compile(w)
+    ocfg = orc.from_kg(cfg)
+    ref = orc.PagedKVCache(ocfg, 1)
+    rng = np.random.default_rng(8)
+
+    def step(seqs, starts, T):
+        toks = rng.integers(0, cfg.vocab_size, size=(len(seqs), T)).astype(np.int32)
+        got = be.forward_batch(toks, seq_ids=np.array(seqs, np.int32), start_pos=np.array(starts, np.int32))
+        for i, (s, p0) in enumerate(zip(seqs, starts)):
+            for t in range(T):
+                want = orc.forward_paged(ocfg, w, ref, s, int(toks[i, t]), p0 + t)
+                err = np.abs(got[i, t] - want).max() / np.abs(want).max()
+                assert err <= 2e-2, (s, p0 + t, err)
+        _same_state(be, ref)
+
+    step([0], [0], 24)                                           # prompt: the prefill path
+    step([0], [24], 8)                                           # 8 positions from 24
+    for t in range(32, 35):
+        step([0], [t], 1)                                        # decode steps
+    s1 = be.paged_fork(0, 32); assert s1 == ref.fork(0, 32)
+    s2 = be.paged_fork(0, 20); assert s2 == ref.fork(0, 20)      # 16..19 read as zeros
+    for d in range(3):
+        step([s1, s2], [32 + d, 20 + d], 1)
+    be.paged_rollback(s1, 20); ref.rollback(s1, 20)              # page 1 of s1 freed, reused zeroed
+    step([s1], [20], 6)
+    step([0, s1, s2], [35, 26, 23], 4)
+    k, v = be.paged_read_kv(2, 0, 30)                            # bf16 rows, widened
+    rk, rv = ref.read_kv(2, 0, 30)
+    assert np.abs(k - rk).max() <= 1e-2 * np.abs(rk).max() and np.abs(v - rv).max() <= 1e-2 * np.abs(rv).max()
+    be.close()
