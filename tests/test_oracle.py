@@ -297,3 +297,19 @@ def test_forced_codes_replay(orc):
     lf = orc.run_sequence_forced(cfg, w, toks, c2, 3, 3)
     assert np.array_equal(lf[:5], lo[:5])
     assert not np.array_equal(lf[5], lo[5])
+
+
+def test_forward_prefill_reference_cases(orc):
+    # src/transformer.rs:5376-5596 on the restatement: a prompt of 8, of 3 and
+    # of 1 token gives vocab_size finite logits, and decoding continues from
+    # the prompt's cache with finite logits (prefill_then_decode)
+    cfg = orc.config()
+    w = orc.weights(cfg, 42)
+    for prompt in (list(range(8)), [0, 1, 2], [5]):
+        out = orc.prefill_then_decode(cfg, w, np.array(prompt, np.int32))
+        assert out.shape == (1, cfg.vocab_size) and np.all(np.isfinite(out))
+    out = orc.prefill_then_decode(cfg, w, np.arange(4, dtype=np.int32), [0])
+    assert out.shape == (2, cfg.vocab_size) and np.all(np.isfinite(out))
+    # prefill differs from teacher-forced forward_base (bidirectional attention, double norm)
+    base = orc.run_sequence(cfg, orc.MODE_BASE, w, np.arange(4, dtype=np.int32))[0]
+    assert not np.array_equal(out[0], base[3])
