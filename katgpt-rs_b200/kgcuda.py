@@ -539,3 +539,40 @@ def sq_build_tables(params, kvd, eig, evals, d_eff):
     if rc:
         raise KgError(rc, "kg_sq_build_tables")
     return out
+
+
+class DDTreeBranchCache:
+    """DDTreeBranchCache (src/speculative/types.rs:218-290) over a context
+    created with kv_mode KG_KV_PAGED: the trunk is sequence 0, forks share
+    whole prefix pages, and the branch budget behaves as the reference's
+    (a fork past max_branches returns the source sequence; discarding a
+    branch other than the trunk frees its pages and its budget slot)."""
+
+    def __init__(self, backend, max_branches):
+        self.backend = backend
+        self.max_branches = max_branches
+        self.branch_count = 1  # sequence 0 = trunk
+        backend.paged_init(max_branches)  # PagedKVCache::new(config, max_branches)
+
+    def fork_branch(self, src, at_pos):
+        if self.branch_count >= self.max_branches:
+            return src  # budget exhausted: reuse the source
+        new_seq = self.backend.paged_fork(src, at_pos)
+        self.branch_count += 1
+        return new_seq
+
+    def forward_branch(self, seq_idx, token, pos):
+        """forward_paged of one token of a branch: logits [vocab]."""
+        return self.backend.forward(token, pos, seq=seq_idx)
+
+    def rollback_branch(self, seq_idx, at_pos):
+        self.backend.paged_rollback(seq_idx, at_pos)
+
+    def discard_branch(self, seq_idx):
+        self.backend.paged_rollback(seq_idx, 0)
+        if seq_idx > 0 and self.branch_count > 1:
+            self.branch_count -= 1
+
+    def reset(self):
+        self.backend.paged_reset()
+        self.branch_count = 1
