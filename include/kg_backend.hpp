@@ -69,12 +69,59 @@ class CudaBackend {
         if (rc != KG_OK) throw std::runtime_error(std::string("kg_forward_batch: ") + kg_last_error(ctx_));
     }
     kg_ctx *handle() { return ctx_; }
+    int32_t forward_vocab() const { return cfg_.vocab_size; }
 
    private:
     kg_config cfg_;
     kg_ctx *ctx_ = nullptr;
     int32_t seq_;
     std::vector<float> logits_;
+};
+
+// DDTreeBranchCache (src/speculative/types.rs:218-290) over a CudaBackend
+// built with kv_mode KG_KV_PAGED: sequence 0 is the trunk, forks share whole
+// prefix pages (PagedKVCache::fork), a fork past max_branches returns the
+// source sequence, and discarding a branch other than the trunk frees its
+// pages and its budget slot.
+class DDTreeBranchCache {
+   public:
+    DDTreeBranchCache(CudaBackend &backend, int32_t max_branches) : be_(backend), max_branches_(max_branches) {
+        check(kg_paged_init(be_.handle(), max_branches), "kg_paged_init");
+    }
+    int32_t fork_branch(int32_t from, int32_t at_pos) {
+        if (branch_count_ >= max_branches_) return from;  // budget exhausted: reuse the source
+        int32_t s = -1;
+        check(kg_paged_fork(be_.handle(), from, at_pos, &s), "kg_paged_fork");
+        ++branch_count_;
+        return s;
+    }
+    // forward_paged of one token of a branch: vocab_size logits
+    std::vector<float> forward_branch(int32_t seq_idx, int32_t token, int32_t pos) {
+        std::vector<float> logits(vocab());
+        check(kg_forward_batch(be_.handle(), 1, &seq_idx, &token, &pos, 1, logits.data(), nullptr), "forward_paged");
+        return logits;
+    }
+    void rollback_branch(int32_t seq_idx, int32_t at_pos) {
+        check(kg_paged_rollback(be_.handle(), seq_idx, at_pos), "kg_paged_rollback");
+    }
+    void discard_branch(int32_t seq_idx) {
+        rollback_branch(seq_idx, 0);
+        if (seq_idx > 0 && branch_count_ > 1) --branch_count_;
+    }
+    void reset() {
+        check(kg_paged_reset(be_.handle()), "kg_paged_reset");
+        branch_count_ = 1;
+    }
+    int32_t branch_count() const { return branch_count_; }
+
+   private:
+    void check(int rc, const char *what) {
+        if (rc != KG_OK) throw std::runtime_error(std::string(what) + ": " + kg_last_error(be_.handle()));
+    }
+    int32_t vocab() const { return be_.forward_vocab(); }
+    CudaBackend &be_;
+    int32_t max_branches_;
+    int32_t branch_count_ = 1;  // sequence 0 = trunk
 };
 
 }  // namespace katgpt
