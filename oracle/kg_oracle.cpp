@@ -938,13 +938,14 @@ struct SqTab {
     std::vector<float> eig;    // [kvd*kvd]
     std::vector<uint8_t> bits;  // [kvd]
     std::vector<int32_t> nlev;  // [kvd]
-    std::vector<float> cent;    // [kvd][kSqLevels]
+    std::vector<float> cent;    // [kvd][stride]
     int32_t d_eff = 0;
+    int stride = kSqLevels;     // centroid slots per dimension
 };
 
 // One layer of SpectralQuantKVCache::from_calibration (spectral_kv_cache.rs:99-347).
 static int sq_build_layer(const or_sq_params &P, int64_t kvd, int64_t layer, const float *eig_in, const float *eval_in,
-                          float d_eff_f, SqTab &T) {
+                          float d_eff_f, SqTab &T, int max_levels = kSqLevels) {
     auto ceil_to_size = [](float f) -> size_t {  // `f.ceil() as usize` (saturating)
         const float c = ceilf(f);
         if (!(c > 0.0f)) return 0;
@@ -994,12 +995,13 @@ static int sq_build_layer(const or_sq_params &P, int64_t kvd, int64_t layer, con
             for (size_t j = j0; j < j1; ++j) out.push_back(syn[s * kvd + j]);
         return out;
     };
+    T.stride = max_levels;
     T.nlev.assign(kvd, 0);
-    T.cent.assign(kvd * kSqLevels, 0.0f);
+    T.cent.assign(kvd * max_levels, 0.0f);
     auto put = [&](size_t j, const std::vector<float> &c) {
-        if (c.size() > (size_t)kSqLevels) return false;
+        if (c.size() > (size_t)max_levels) return false;
         T.nlev[j] = (int32_t)c.size();
-        std::copy(c.begin(), c.end(), &T.cent[j * kSqLevels]);
+        std::copy(c.begin(), c.end(), &T.cent[j * max_levels]);
         return true;
     };
     const std::vector<float> tail = sq_lloyd_fit(column_block(d_eff, kvd), tail_bits, P.lloyd_max_iter,
@@ -1083,7 +1085,7 @@ static void sq_store(const SqTab &T, int64_t kvd, const float *x, uint8_t *packe
     std::copy(x, x + kvd, xn.begin());
     scale_inplace(xn.data(), kvd, 1.0f / nrm);
     sq_rotate(T.eig.data(), kvd, xn.data(), r.data());
-    for (int64_t j = 0; j < kvd; ++j) idx[j] = sq_quantize(r[j], &T.cent[j * kSqLevels], T.nlev[j]);
+    for (int64_t j = 0; j < kvd; ++j) idx[j] = sq_quantize(r[j], &T.cent[j * T.stride], T.nlev[j]);
     sq_pack(idx.data(), T.bits.data(), kvd, packed);
 }
 
@@ -1095,7 +1097,7 @@ static void sq_dequant(const SqTab &T, int64_t kvd, const uint8_t *packed, float
         return;
     }
     sq_unpack(packed, kvd, T.bits.data(), kvd, idx.data());
-    for (int64_t j = 0; j < kvd; ++j) r[j] = idx[j] < T.nlev[j] ? T.cent[j * kSqLevels + idx[j]] : 0.0f;
+    for (int64_t j = 0; j < kvd; ++j) r[j] = idx[j] < T.nlev[j] ? T.cent[j * T.stride + idx[j]] : 0.0f;
     matmul(out, T.eig.data(), r.data(), kvd, kvd);
     scale_inplace(out, kvd, nrm);
 }
@@ -1917,6 +1919,34 @@ int64_t or_sq_roundtrip(int64_t kvd, const float *eig, const uint8_t *bits, cons
     int64_t tb = 0;
     for (int64_t j = 0; j < kvd; ++j) tb += bits[j];
     return (tb + 7) / 8;
+}
+
+// SpectralQuantKVCache::from_keys on keys[0..n_calib) (one layer, codebooks
+// of any width up to 8 bits), then store_key + dequantize_key_into of every
+// key: recon [n_keys][dim]. The configuration of the reference's quality
+// benchmark (tests/bench_octopus_goat.rs:346-440).
+int or_sq_quality_keys(const or_sq_params *P, int64_t dim, const float *keys, int64_t n_keys, int64_t n_calib,
+                       float *recon) {
+    if (!P || dim < 2 || n_keys < 1 || n_calib < 1 || n_calib > n_keys) return -1;
+    std::vector<double> cov(dim * dim, 0.0);
+    for (int64_t s = 0; s < n_calib; ++s)
+        for (int64_t i = 0; i < dim; ++i)
+            for (int64_t j = 0; j < dim; ++j) cov[i * dim + j] += (double)keys[s * dim + i] * (double)keys[s * dim + j];
+    const double scale = 1.0 / (double)n_calib;
+    for (auto &v : cov) v *= scale;
+    std::vector<float> ev, vec;
+    sq_jacobi(cov, dim, ev, vec);
+    SqTab T;
+    if (sq_build_layer(*P, dim, 0, vec.data(), ev.data(), sq_participation_ratio(ev.data(), dim), T, 256)) return -3;
+    std::vector<float> xn(dim), r(dim);
+    std::vector<uint8_t> idx(dim), packed(dim);
+    for (int64_t k = 0; k < n_keys; ++k) {
+        float nrm = 0.0f;
+        std::fill(packed.begin(), packed.end(), 0);
+        sq_store(T, dim, keys + k * dim, packed.data(), &nrm, xn, r, idx);
+        sq_dequant(T, dim, packed.data(), nrm, recon + k * dim, r, idx);
+    }
+    return 0;
 }
 
 // forward_quantized<SpectralQuantKVCache> (src/transformer.rs:4042-4233 with

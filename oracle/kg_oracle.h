@@ -154,6 +154,8 @@ int or_sq_build(const or_sq_params *P, int64_t kvd, int32_t L, const float *eig_
                 int32_t *deff_out);
 int64_t or_sq_roundtrip(int64_t kvd, const float *eig, const uint8_t *bits, const float *cent, const int32_t *nlev,
                         const float *x, uint8_t *packed, float *norm, float *deq);
+int or_sq_quality_keys(const or_sq_params *P, int64_t dim, const float *keys, int64_t n_keys, int64_t n_calib,
+                       float *recon);
 int or_run_sequence_sq(const or_config *c, const float *weights, const float *eig, const uint8_t *bits,
                        const float *cent, const int32_t *nlev, const int32_t *tokens, int32_t T, float *logits,
                        uint8_t *codes, float *norms);

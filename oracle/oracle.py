@@ -101,6 +101,7 @@ def lib():
             "or_forward_paged": (ctypes.c_int, [cp, P, P, P, I64, I32, I32, P]),
             "or_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
             "or_sq_jacobi": (ctypes.c_int, [P, I64, P, P]),
+            "or_sq_quality_keys": (ctypes.c_int, [ctypes.POINTER(OrSqParams), I64, P, I64, I64, P]),
             "or_sq_allocate": (None, [F32, F32, I64, ctypes.c_int, P, P]),
             "or_sq_waterfill": (None, [P, I64, I64, ctypes.c_int, ctypes.c_int, P]),
             "or_sq_lloyd_fit": (None, [P, I64, ctypes.c_int, ctypes.c_int, U64, P]),
@@ -613,4 +614,14 @@ def sq_unpack(packed, bits, n):
     bits = np.ascontiguousarray(bits, np.uint8)
     out = np.empty(n, np.uint8)
     lib().or_sq_unpack(_p(packed), packed.size, _p(bits), n, _p(out))
+    return out
+
+
+def sq_quality_keys(params, keys, n_calib):
+    """from_keys on keys[:n_calib], then store + dequantize of every key: reconstructions."""
+    keys = f32(keys)
+    out = np.empty_like(keys)
+    rc = lib().or_sq_quality_keys(ctypes.byref(params), keys.shape[1], _p(keys), keys.shape[0], n_calib, _p(out))
+    if rc:
+        raise RuntimeError(f"or_sq_quality_keys failed: {rc}")
     return out
