@@ -313,3 +313,29 @@ def test_forward_prefill_reference_cases(orc):
     # prefill differs from teacher-forced forward_base (bidirectional attention, double norm)
     base = orc.run_sequence(cfg, orc.MODE_BASE, w, np.arange(4, dtype=np.int32))[0]
     assert not np.array_equal(out[0], base[3])
+
+
+def test_published_turboquant_quality_bench022(orc):
+    # The reference's TurboQuant legacy comparison (tests/bench_octopus_goat.rs:
+    # 440-505, published in .benchmarks/022_octopus_goat.md section 3): 512 N(0,1)
+    # keys of dim 128 from Rng(42) stored with TurboQuantKVCache::new (rotation
+    # from the same Rng(42) stream), dequantize_key, per-key MSE and cosine.
+    # The keys are the rotation's own Gaussian draws, which is why these
+    # figures sit below the random-vector table: the restatement reproduces
+    # that (cosine within 2e-3, MSE within 4% of every published figure), and
+    # independent draws land at 0.941 / 0.983 / 0.995.
+    published = {2: (0.1790, 0.9048), 3: (0.0886, 0.9552), 4: (0.0512, 0.9760)}
+    dim = 128
+    keys = orc.normals(42, 512 * dim).reshape(512, dim)
+    rot = orc.rotation(dim, 42)
+    rot_t = np.ascontiguousarray(rot.T)
+    for bits, (mse_pub, cos_pub) in published.items():
+        cent, bnd = orc.codebook(dim, bits)[:2]
+        mses, coss = [], []
+        for i in range(512):
+            pk, nr = orc.tq_store(rot, bnd, bits, keys[i])
+            rec = orc.tq_dequant(rot_t, cent, bits, pk, nr)
+            mses.append(float(((keys[i] - rec) ** 2).sum(dtype=np.float32)) / dim)
+            coss.append(orc.dot(keys[i], rec) / np.sqrt(orc.dot(keys[i], keys[i]) * orc.dot(rec, rec)))
+        assert abs(np.mean(coss) - cos_pub) < 2e-3, (bits, np.mean(coss), cos_pub)
+        assert abs(np.mean(mses) - mse_pub) / mse_pub < 0.04, (bits, np.mean(mses), mse_pub)
