@@ -8,10 +8,12 @@
  * timed CPU baseline. Nothing in the product (libkgcuda) links or calls it.
  *
  * Parity pin: the reference cannot be compiled here (no Rust toolchain) and has
- * no golden files; the oracle is pinned against the reference's published
- * TurboQuant quality table (.docs/04_performance.md:323-328, inputs from
- * tests/bench_turboquant.rs:23-27) and the structural asserts of its unit
- * tests. See the test files under tests/ for each pin.
+ * no golden files; the oracle is checked against the structural asserts of its
+ * unit tests and, to three or four significant digits, against published
+ * reconstruction-quality tables (.benchmarks/022_octopus_goat.md: TurboQuant
+ * and SpectralQuant on seeded keys); the older TurboQuant table of
+ * .docs/04_performance.md:323-328 is not reproduced. See the test files under
+ * tests/ for each pin.
  *
  * All functions are plain C ABI (ctypes-friendly): pointers + sizes.
  */
