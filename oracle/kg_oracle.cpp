@@ -1865,6 +1865,21 @@ void or_sq_unpack(const uint8_t *p, int64_t plen, const uint8_t *bits, int64_t n
     sq_unpack(p, plen, bits, n, out);
 }
 
+// SP-KV pieces for the reference's own unit tests: the utility predictor
+// (utility_predictor.rs:51-87 with the weights of types.rs:224-258) and
+// attention_head_gated (sp_kv/forward.rs:166-245); bias NULL = no gate.
+void or_spkv_predict(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias, const float *h, float *util) {
+    const Predictor p = make_predictor(d_model, hidden, nkv, init_bias);
+    std::vector<float> buf(hidden);
+    for (int64_t i = 0; i < hidden; ++i) buf[i] = silu(dot(&p.w1[i * d_model], h, d_model) + p.b1[i]);
+    for (int64_t k = 0; k < nkv; ++k) util[k] = sigmoid(dot(&p.w2[k * hidden], buf.data(), hidden) + p.b2[k]);
+}
+void or_attention_head_gated(const float *q, const float *K, const float *V, float *out, float *scores, int64_t qoff,
+                             int64_t kvoff, int64_t kvd, int64_t hd, int64_t tn, float scale, const float *bias) {
+    std::vector<float> zero(tn, 0.0f);
+    attention_head_gated(q, K, V, out, scores, qoff, kvoff, kvd, hd, tn, scale, bias ? bias : zero.data());
+}
+
 // calibrate_eigenbasis (spectral.rs:226-278): covariance (1/N) sum x x^T in f64,
 // Jacobi, participation ratio. samples [n][dim].
 int or_sq_calibrate_eigenbasis(const float *samples, int64_t n, int64_t dim, float *eigvecs, float *eigvals,

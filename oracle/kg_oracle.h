@@ -142,6 +142,9 @@ int or_forward_paged(const or_config *c, const float *weights, float *pool, cons
  * tables of SpectralQuantKVCache::from_calibration ([L][kvd*kvd] eigenvectors,
  * [L][kvd] bits, [L][kvd][64] centroids, [L][kvd] level counts, [L] d_eff),
  * one store+dequantize round trip, and forward_quantized over the codec. */
+void or_spkv_predict(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias, const float *h, float *util);
+void or_attention_head_gated(const float *q, const float *K, const float *V, float *out, float *scores, int64_t qoff,
+                             int64_t kvoff, int64_t kvd, int64_t hd, int64_t tn, float scale, const float *bias);
 int or_sq_jacobi(const double *m, int64_t dim, float *evals, float *evecs);
 void or_sq_allocate(float d_eff, float avg_bits, int64_t head_dim, int max_bits, int32_t *b_high, int32_t *b_low);
 void or_sq_waterfill(const double *ev, int64_t d, int64_t total, int min_bits, int max_bits, uint8_t *out);

@@ -104,6 +104,8 @@ def lib():
             "or_forward_paged": (ctypes.c_int, [cp, P, P, P, I64, I32, I32, P]),
             "or_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
             "or_sq_jacobi": (ctypes.c_int, [P, I64, P, P]),
+            "or_spkv_predict": (None, [I64, I64, I64, F32, P, P]),
+            "or_attention_head_gated": (None, [P, P, P, P, P, I64, I64, I64, I64, I64, F32, P]),
             "or_sq_quality_keys": (ctypes.c_int, [ctypes.POINTER(OrSqParams), I64, P, I64, I64, P]),
             "or_sq_allocate": (None, [F32, F32, I64, ctypes.c_int, P, P]),
             "or_sq_waterfill": (None, [P, I64, I64, ctypes.c_int, ctypes.c_int, P]),
@@ -628,3 +630,21 @@ def sq_quality_keys(params, keys, n_calib):
     if rc:
         raise RuntimeError(f"or_sq_quality_keys failed: {rc}")
     return out
+
+
+def spkv_predict(d_model, hidden, nkv, init_bias, h):
+    """The SP-KV utility predictor (utility_predictor.rs:51-87) with its seeded weights: utilities [nkv]."""
+    h = f32(h)
+    out = np.empty(nkv, np.float32)
+    lib().or_spkv_predict(d_model, hidden, nkv, init_bias, _p(h), _p(out))
+    return out
+
+
+def attention_head_gated(q, K, V, kvd, hd, tn, scale, bias=None, qoff=0, kvoff=0):
+    """attention_head_gated (sp_kv/forward.rs:166-245): (out [len(q)], scores [tn])."""
+    q, K, V = f32(q), f32(K), f32(V)
+    out = np.zeros(q.size, np.float32)
+    scores = np.zeros(tn, np.float32)
+    b = None if bias is None else f32(bias)
+    lib().or_attention_head_gated(_p(q), _p(K), _p(V), _p(out), _p(scores), qoff, kvoff, kvd, hd, tn, scale, _p(b))
+    return out, scores

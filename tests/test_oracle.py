@@ -339,3 +339,19 @@ def test_published_turboquant_quality_bench022(orc):
             coss.append(orc.dot(keys[i], rec) / np.sqrt(orc.dot(keys[i], keys[i]) * orc.dot(rec, rec)))
         assert abs(np.mean(coss) - cos_pub) < 2e-3, (bits, np.mean(coss), cos_pub)
         assert abs(np.mean(mses) - mse_pub) / mse_pub < 0.04, (bits, np.mean(mses), mse_pub)
+
+
+def test_spkv_reference_cases(orc):
+    # src/sp_kv/utility_predictor.rs:240-272 and src/sp_kv/forward.rs:832-960
+    u = orc.spkv_predict(32, 16, 4, 5.0, np.ones(32, np.float32))
+    assert u.shape == (4,) and np.all((u > 0) & (u < 1))
+    assert np.all(orc.spkv_predict(32, 16, 4, 5.0, np.zeros(32, np.float32)) > 0.99)   # gates start open
+    hd, kvd, tn = 8, 16, 4                                                              # no gate = baseline
+    q, K, V = np.full(kvd, 0.1), np.full(tn * kvd, 0.2), np.full(tn * kvd, 0.3)
+    out, _ = orc.attention_head_gated(q, K, V, kvd, hd, tn, 1.0 / np.sqrt(hd))
+    assert np.all(np.abs(out[:hd] - 0.3) < 1e-4)
+    hd = kvd = 4                                                                        # a -inf bias prunes
+    q, K, V = np.ones(kvd), np.ones(tn * kvd), np.ones(tn * kvd)
+    out, sc = orc.attention_head_gated(q, K, V, kvd, hd, tn, 0.5, bias=[0.0, 0.0, -np.inf, 0.0])
+    assert np.all(np.abs(out[:hd] - 1.0) < 1e-4)
+    assert sc[0] + sc[1] + sc[3] > 0 and sc[2] < 1e-20
