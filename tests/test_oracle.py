@@ -355,3 +355,31 @@ def test_spkv_reference_cases(orc):
     out, sc = orc.attention_head_gated(q, K, V, kvd, hd, tn, 0.5, bias=[0.0, 0.0, -np.inf, 0.0])
     assert np.all(np.abs(out[:hd] - 1.0) < 1e-4)
     assert sc[0] + sc[1] + sc[3] > 0 and sc[2] < 1e-20
+
+
+def test_gamma_folding_matches_runtime_gammas(orc):
+    # src/transformer.rs:6683-6790 (proof_gamma_folding_forward_base): the MLP
+    # gamma folded into mlp_w1 (weights.rs:205-221) gives the run-time-gamma
+    # forward within 1e-5; the attention gamma stays at run time
+    cfg = orc.config(n_layer=2)
+    n, m, L, V, B = cfg.n_embd, cfg.mlp_hidden, cfg.n_layer, cfg.vocab_size, cfg.block_size
+    kvd = cfg.n_kv_head * cfg.head_dim
+    w = orc.weights(cfg, 42)
+    i = np.arange(n, dtype=np.float32)
+    ag = np.float32(0.5) + np.sin(i * np.float32(0.1)).astype(np.float32) * np.float32(0.8)
+    mg = np.float32(0.5) + np.cos(i * np.float32(0.15)).astype(np.float32) * np.float32(0.6)
+    w[-2 * L * n:-L * n] = np.tile(ag, L)
+    w[-L * n:] = np.tile(mg, L)
+    toks = np.array([26, 3, 9, 14, 1, 7, 20, 5], np.int32)
+    base = orc.run_sequence(cfg, orc.MODE_BASE, w, toks)[0]
+    folded = w.copy()
+    per_layer = 2 * n * n + 2 * kvd * n + 2 * m * n
+    for l in range(L):
+        o = V * n + B * n + l * per_layer + 2 * n * n + 2 * kvd * n     # mlp_w1 [m][n]
+        w1 = folded[o:o + m * n].reshape(m, n)
+        w1 *= mg[None, :]
+    folded[-L * n:] = 1.0
+    got = orc.run_sequence(cfg, orc.MODE_BASE, folded, toks)[0]
+    assert np.abs(got - base).max() < 1e-5 * max(1.0, np.abs(base).max())
+    plain = orc.run_sequence(cfg, orc.MODE_BASE, orc.weights(cfg, 42), toks)[0]
+    assert np.abs(plain - base).max() > 1e-3                            # the gammas matter
