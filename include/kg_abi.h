@@ -268,8 +268,9 @@ int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, c
  * lives on the host inside the context (the same integer state as the
  * reference: page indices, counts and free-list order match it call for call);
  * the pages live in a device pool of max(initial, 2 * max_seqs * n_layer *
- * (block_size/16 + 1)) pages, and an allocation past it returns KG_ERR_OOM
- * (the reference grows its Vec instead). A page taken from the free list is
+ * (block_size/16 + 1)) pages, bounded by 90% of the device memory left free
+ * at creation less 2 GiB, and an allocation past it returns KG_ERR_OOM (the
+ * reference grows its Vec instead). A page taken from the free list is
  * zeroed, as alloc_page does. Sequence indices run from 0 to the paged
  * sequence count (grown by ensure and fork), at most max_seqs.
  * kg_forward_batch / kg_forward_token on such a context are forward_paged

@@ -128,7 +128,19 @@ cudaError_t paged_alloc(kg_ctx *ctx) {
     const int64_t L = ctx->L, S = ctx->cfg.max_seqs;
     P.maxp = (int)(ctx->B / kPage + 1);
     const int64_t initial = (ctx->B / kPage + 1) * L;  // PagedKVCache::new (:217-219)
-    P.cap = std::max<int64_t>(initial, 2 * S * L * P.maxp);
+    // Two full page sets (every sequence at block_size, once more for forks),
+    // bounded by what the device has free: at model widths two full sets can
+    // exceed HBM, and a pool that runs out returns KG_ERR_OOM from ensure.
+    int64_t want = 2 * S * L * P.maxp;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
+        const int64_t reserve = int64_t(2) << 30;  // workspaces allocated on later calls
+        const int64_t fit = ((int64_t)free_b - reserve) / 10 * 9 / page_bytes(ctx);
+        want = std::min(want, std::max<int64_t>(fit, 0));
+    } else {
+        (void)cudaGetLastError();
+    }
+    P.cap = std::max<int64_t>(initial, want);
     cudaError_t e = cudaMalloc(&P.pool, (size_t)P.cap * page_bytes(ctx));
     if (e == cudaSuccess) e = cudaMalloc(&P.d_tab, (size_t)L * S * P.maxp * sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMalloc(&P.d_zero, (size_t)P.cap * sizeof(int32_t));
