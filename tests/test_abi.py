@@ -81,3 +81,34 @@ def test_cpp_trait_mirror_compiles(tmp_path):
     r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.join(ROOT, "include"), str(src)],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def _header_prototypes():
+    src = open(os.path.join(ROOT, "include", "kg_abi.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"\b(kg_\w+)\s*\(([^;{]*?)\)\s*;", src, re.S):
+        args = [a for a in " ".join(m.group(2).split()).split(",") if a.strip()]
+        protos[m.group(1)] = len(args)
+    return protos
+
+
+def _header_struct_fields(name):
+    src = open(os.path.join(ROOT, "include", "kg_abi.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    body = re.search(r"typedef struct \{([^}]*)\}\s*" + name + ";", src).group(1)
+    return re.findall(r"\b(\w+)\s*;", body)
+
+
+def test_rust_binding_matches_header():
+    # the Rust -sys block a maintainer would add binds every entry point with
+    # the header's parameter count, and its structs carry the header's fields in order
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    rust = doc[doc.index("```rust"):]
+    rust = rust[:rust.index("```", 7)]
+    bound = {m.group(1): len([a for a in " ".join(m.group(2).split()).split(",") if a.strip()])
+             for m in re.finditer(r"pub fn (kg_\w+)\(([^)]*)\)", rust, re.S)}
+    assert bound == _header_prototypes()
+    for c, r in (("kg_config", "KgConfig"), ("kg_sq_params", "KgSqParams")):
+        body = re.search(r"pub struct " + r + r" \{([^}]*)\}", rust).group(1)
+        assert re.findall(r"pub (\w+):", body) == _header_struct_fields(c), c
