@@ -146,3 +146,19 @@ def test_forward_paged_equals_flat_double_norm_path(orc, micro):
         lb = orc.forward_paged(cfg, w, b, 0, t, pos)
         assert np.array_equal(la, lb)
     assert a.layer_page_tables[0][0] != b.layer_page_tables[0][0]
+
+
+def _gqa_draft(orc):  # Config::gqa_draft() (crates/katgpt-types/src/config.rs:858-890)
+    return orc.config(vocab_size=4096, block_size=256, n_embd=64, n_head=8, head_dim=8, n_kv_head=2,
+                      mlp_hidden=256, n_layer=4, bos_token=0, temperature=0.8, sparse_threshold=0.8)
+
+
+def test_gqa_forward_and_forward_paged(orc):  # src/transformer.rs:4469-4485, 4981-5006
+    cfg = _gqa_draft(orc)
+    assert cfg.n_kv_head * cfg.head_dim < cfg.n_embd                  # :4512-4540: the cache uses kv_dim
+    w = orc.weights(cfg, 42)
+    flat = orc.run_sequence(cfg, orc.MODE_BASE, w, np.zeros(4, np.int32))[0]
+    assert flat.shape == (4, 4096) and np.all(np.isfinite(flat))
+    paged = orc.PagedKVCache(cfg, 1)
+    got = orc.forward_paged(cfg, w, paged, 0, 0, 0)
+    assert np.abs(got - flat[0]).max() < 2e-3
