@@ -383,3 +383,30 @@ def test_gamma_folding_matches_runtime_gammas(orc):
     assert np.abs(got - base).max() < 1e-5 * max(1.0, np.abs(base).max())
     plain = orc.run_sequence(cfg, orc.MODE_BASE, orc.weights(cfg, 42), toks)[0]
     assert np.abs(plain - base).max() > 1e-3                            # the gammas matter
+
+
+def test_turboquant_cache_reference_cases(orc):
+    # src/turboquant/kv_cache.rs:772-794, 902-926, 928-951 and codebook.rs:245-258,
+    # 284-293 at Config::micro() (kv_dim 16), 4-bit keys and values
+    dim, bits = 16, 4
+    rot = orc.rotation(dim)
+    c, b, _ = orc.codebook(dim, bits)
+    i = np.arange(dim, dtype=np.float32)
+
+    def roundtrip(x, scalar=False):
+        pk, nrm = orc.tq_store(rot, b, bits, x)
+        if scalar:
+            return orc.tq_dequant_scalar(rot, c, bits, pk, nrm)
+        return orc.tq_dequant(rot.T.copy(), c, bits, pk, nrm)
+
+    key = np.sin(i * np.float32(0.1) - np.float32(1.0)).astype(np.float32)
+    val = np.cos(i * np.float32(0.2)).astype(np.float32)
+    assert orc.cosine(key, roundtrip(key)) > 0.90 and orc.cosine(val, roundtrip(val)) > 0.85
+    k3 = np.sin(i * np.float32(0.3)).astype(np.float32)                  # the _into path vs the scalar one
+    assert np.abs(roundtrip(k3) - roundtrip(k3, scalar=True)).max() < 1e-5
+    for x in (np.sin(i).astype(np.float32), np.cos(i).astype(np.float32)):  # layers reconstruct independently
+        assert orc.cosine(x, roundtrip(x)) > 0.90
+    c64, b64, _ = orc.codebook(64, 4)
+    for v in (-0.5, -0.3, -0.1, 0.0, 0.1, 0.3, 0.5):                      # quantize -> dequantize
+        assert abs(c64[np.searchsorted(b64, np.float32(v), side="right")] - v) < 0.5
+    assert all(orc.codebook(64, bb)[2] > 0 for bb in range(2, 7))
