@@ -264,10 +264,11 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
         if ((rc = dalloc(ctx, &ctx->kb, kb.size()))) return bail(rc);
         if ((rc = dalloc(ctx, &ctx->vc, vc.size()))) return bail(rc);
         if ((rc = dalloc(ctx, &ctx->vb, vb.size()))) return bail(rc);
-        cudaMemcpy(ctx->kc, kc.data(), kc.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->kb, kb.data(), kb.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->vc, vc.data(), vc.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->vb, vb.data(), vb.size() * 4, cudaMemcpyHostToDevice);
+        e = cudaMemcpy(ctx->kc, kc.data(), kc.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->kb, kb.data(), kb.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->vc, vc.data(), vc.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->vb, vb.data(), vb.size() * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "upload codebooks"));
     }
     if (c.kv_mode == KG_KV_SPKV_TQ)
         kg::predictor_weights(ctx->n, ctx->ph, ctx->nkv, c.spkv_init_bias, ctx->h_pred);
@@ -321,20 +322,21 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     ctx->pack_floats = off;
     if (off * 4 > 200 * 1024) return bail(fail(ctx, KG_ERR_UNSUPPORTED, "micro weights exceed shared memory"));
     if ((rc = dalloc(ctx, &ctx->pack, off))) return bail(rc);
-    KG_CUDA(ctx, cudaMemset(ctx->pack, 0, off * 4));
-    if (tq) {
+    e = cudaMemset(ctx->pack, 0, off * 4);
+    if (e == cudaSuccess && tq) {
         std::vector<float> rt(kvd * kvd);
         for (int64_t i = 0; i < kvd; ++i)
             for (int64_t j = 0; j < kvd; ++j) rt[i * kvd + j] = ctx->h_rot[j * kvd + i];
-        cudaMemcpy(ctx->pack + a.off_rot, ctx->h_rot.data(), kvd * kvd * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->pack + a.off_rot_t, rt.data(), kvd * kvd * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->pack + a.off_kc, kc.data(), kc.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->pack + a.off_kb, kb.data(), kb.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->pack + a.off_vc, vc.data(), vc.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(ctx->pack + a.off_vb, vb.data(), vb.size() * 4, cudaMemcpyHostToDevice);
+        e = cudaMemcpy(ctx->pack + a.off_rot, ctx->h_rot.data(), kvd * kvd * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->pack + a.off_rot_t, rt.data(), kvd * kvd * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->pack + a.off_kc, kc.data(), kc.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->pack + a.off_kb, kb.data(), kb.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->pack + a.off_vc, vc.data(), vc.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ctx->pack + a.off_vb, vb.data(), vb.size() * 4, cudaMemcpyHostToDevice);
     }
-    if (!ctx->h_pred.empty())
-        cudaMemcpy(ctx->pack + a.off_pw1, ctx->h_pred.data(), ctx->h_pred.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && !ctx->h_pred.empty())
+        e = cudaMemcpy(ctx->pack + a.off_pw1, ctx->h_pred.data(), ctx->h_pred.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return bail(cuda_fail(ctx, e, "upload micro tables"));
     a.pack = ctx->pack;
     a.pack_floats = (int)ctx->pack_floats;
     a.L = (int)L;
