@@ -241,7 +241,9 @@ int kg_comm_destroy(kg_ctx *ctx);
  * sampled on the device from softmax_scaled probabilities, as kg_sample_dev)
  * receive every rank's rows, this rank's at offset rank. Every rank passes the
  * same n_seq and the same choice of outputs. Device pointers, enqueued on
- * `stream`; without a communicator it is the local step only. */
+ * `stream`; without a communicator it is the local step only. A rank whose
+ * local step fails still joins the gathers (its rows are then stale) and
+ * returns the error, so no other rank is left waiting in its gather. */
 int kg_decode_gather_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens,
                          const int32_t *positions, float *logits_all, int32_t *tokens_all, void *stream);
 

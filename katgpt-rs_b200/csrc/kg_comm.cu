@@ -110,35 +110,36 @@ int kg_decode_gather_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, con
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int64_t V = ctx->V, r = ctx->rank;
     float *probs = nullptr;
+    int rc = KG_OK;
     if (tokens_all) {
-        if (!ctx->probs_buf) {  // first use: a fixed buffer, so captured decode graphs stay valid
+        if (n_seq > ctx->cfg.max_seqs) {
+            rc = kg::fail(ctx, KG_ERR_INVALID_ARG, "n_seq exceeds max_seqs");
+        } else if (!ctx->probs_buf) {  // first use: a fixed buffer, so captured decode graphs stay valid
             cudaError_t e = cudaSetDevice(ctx->device);
             if (e == cudaSuccess) e = cudaMalloc(&ctx->probs_buf, (size_t)ctx->cfg.max_seqs * V * sizeof(float));
-            if (e != cudaSuccess) return kg::fail(ctx, KG_ERR_OOM, std::string("probs buffer: ") + cudaGetErrorString(e));
-            ctx->allocs.push_back(ctx->probs_buf);
+            if (e == cudaSuccess) ctx->allocs.push_back(ctx->probs_buf);
+            else rc = kg::fail(ctx, KG_ERR_OOM, std::string("probs buffer: ") + cudaGetErrorString(e));
         }
-        if (n_seq > ctx->cfg.max_seqs) return kg::fail(ctx, KG_ERR_INVALID_ARG, "n_seq exceeds max_seqs");
         probs = ctx->probs_buf;
     }
     float *my_logits = logits_all ? logits_all + r * n_seq * V : nullptr;
-    int rc = kg_forward_batch_dev(ctx, n_seq, seq_ids, tokens, positions, 1, my_logits, probs, stream);
-    if (rc) return rc;
-    if (tokens_all) {
-        rc = kg_sample_dev(ctx, n_seq, seq_ids, probs, V, tokens_all + r * n_seq, stream);
-        if (rc) return rc;
-    }
-    if (!ctx->comm || ctx->world == 1) return KG_OK;
+    if (rc == KG_OK) rc = kg_forward_batch_dev(ctx, n_seq, seq_ids, tokens, positions, 1, my_logits, probs, stream);
+    if (rc == KG_OK && tokens_all) rc = kg_sample_dev(ctx, n_seq, seq_ids, probs, V, tokens_all + r * n_seq, stream);
+    if (!ctx->comm || ctx->world == 1) return rc;
+    // The gathers are issued whatever happened above, so that a local error
+    // leaves no other rank waiting in its own gather (this rank's rows are then
+    // stale); the call still returns that error.
     const kg::NcclApi &api = kg::nccl();
     ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
     if (logits_all) {
         const ncclResult_t nr = api.all_gather(my_logits, logits_all, (size_t)n_seq * V, ncclFloat32, comm, s);
-        if (nr != ncclSuccess) return kg::nccl_fail(ctx, nr, "ncclAllGather (logits)");
+        if (nr != ncclSuccess && rc == KG_OK) rc = kg::nccl_fail(ctx, nr, "ncclAllGather (logits)");
     }
     if (tokens_all) {
         const ncclResult_t nr = api.all_gather(tokens_all + r * n_seq, tokens_all, (size_t)n_seq, ncclInt32, comm, s);
-        if (nr != ncclSuccess) return kg::nccl_fail(ctx, nr, "ncclAllGather (tokens)");
+        if (nr != ncclSuccess && rc == KG_OK) rc = kg::nccl_fail(ctx, nr, "ncclAllGather (tokens)");
     }
-    return KG_OK;
+    return rc;
 }
 
 }  // extern "C"
