@@ -2,7 +2,7 @@
 
 The oracle runs the reference forward in f32 on the same bf16-rounded
 weights; the device computes GEMMs with bf16 inputs and f32 accumulation and
-attention in the TurboQuant rotated domain. Bar (north star): logits within
+attention in the TurboQuant rotated domain. Bar: logits within
 2e-2 relative, measured per position as max|gpu - ref| / max|ref|.
 """
 import numpy as np

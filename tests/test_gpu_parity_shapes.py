@@ -1,7 +1,7 @@
 """GPU parity at the benchmark configurations' own shapes (bf16 path).
 
 The oracle runs the reference forward in f32 on the same bf16-rounded
-weights. Bars (north star): logits within 2e-2 relative per position; for the
+weights. Bars: logits within 2e-2 relative per position; for the
 quantized forward at every position against the oracle replaying the
 device's codes (the forced_oracle fixture), and from position 64 on also
 against the oracle's own codes (before that a single code flipped next to a
