@@ -706,7 +706,7 @@ __global__ void prefill_route_kernel(float *x, const float *xr, float *D, const 
         float *xp = x + ((int64_t)seq * T + p) * n;
         const float *rp = xr + ((int64_t)seq * T + p) * n;
         for (int j = tid; j < n; j += blockDim.x) d[j] = d[j] + (xp[j] - rp[j]);
-        if (!routing) continue;  // no cross-thread reads this round: each thread owns its j
+        if (!routing) continue;  // no cross-thread reads in this pass: each thread owns its j
         __syncthreads();
         float ss = 0.0f;
         for (int j = tid; j < n; j += blockDim.x) ss += d[j] * d[j];

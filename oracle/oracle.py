@@ -1,7 +1,7 @@
 """ctypes wrapper of the CPU oracle (test infrastructure only).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
-module, and only as the checker. It wraps oracle/_build/libkgoracle.so, a C++
+module, and only to check results or time the CPU baseline. It wraps oracle/_build/libkgoracle.so, a C++
 restatement of katgpt-rs's x86-64 AVX2 forward path (see kg_oracle.h).
 
 Parity pin: partial. The reference has no golden files and cannot be built
