@@ -112,3 +112,12 @@ def test_rust_binding_matches_header():
     for c, r in (("kg_config", "KgConfig"), ("kg_sq_params", "KgSqParams")):
         body = re.search(r"pub struct " + r + r" \{([^}]*)\}", rust).group(1)
         assert re.findall(r"pub (\w+):", body) == _header_struct_fields(c), c
+
+
+def test_python_mirror_signatures_match_header(kg):
+    # every entry point is bound in kgcuda with the header's parameter count
+    L = kg.lib()
+    for name, nargs in _header_prototypes().items():
+        fn = getattr(L, name)
+        assert fn.argtypes is not None, f"{name} has no ctypes signature"
+        assert len(fn.argtypes) == nargs, name
