@@ -115,9 +115,33 @@ def test_rust_binding_matches_header():
 
 
 def test_python_mirror_signatures_match_header(kg):
-    # every entry point is bound in kgcuda with the header's parameter count
+    # every entry point is bound in kgcuda with the header's parameters: same
+    # count, pointers as pointers, scalars of the same width and kind (an
+    # int32 bound where the C side reads int64 would pass garbage high bits)
+    src = open(os.path.join(ROOT, "include", "kg_abi.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    scalar = {"int32_t": ctypes.c_int32, "int": ctypes.c_int, "int64_t": ctypes.c_int64,
+              "uint64_t": ctypes.c_uint64, "float": ctypes.c_float}
+
+    def same(c_type, t):
+        if "*" in c_type:
+            return t in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(t, ctypes._Pointer)
+        if c_type == "void":
+            return t is None
+        want = scalar[c_type.replace("const ", "").strip()]
+        return ctypes.sizeof(t) == ctypes.sizeof(want) and (t is ctypes.c_float) == (want is ctypes.c_float)
+
     L = kg.lib()
-    for name, nargs in _header_prototypes().items():
+    protos = list(re.finditer(r"([\w \*]+?)\b(kg_\w+)\s*\(([^;{]*?)\)\s*;", src, re.S))
+    assert len(protos) == len(_header_prototypes())
+    for m in protos:
+        name = m.group(2)
+        args = [a.strip() for a in " ".join(m.group(3).split()).split(",") if a.strip()]
         fn = getattr(L, name)
-        assert fn.argtypes is not None, f"{name} has no ctypes signature"
-        assert len(fn.argtypes) == nargs, name
+        assert fn.argtypes is not None and len(fn.argtypes) == len(args), name
+        for a, t in zip(args, fn.argtypes):
+            c_type = a if "*" in a else a.rsplit(" ", 1)[0]
+            assert same(c_type, t), (name, a, t)
+        ret = " ".join(m.group(1).split())
+        if "*" not in ret and ret != "void":
+            assert same(ret, fn.restype), (name, ret, fn.restype)
