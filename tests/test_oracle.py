@@ -410,3 +410,38 @@ def test_turboquant_cache_reference_cases(orc):
     for v in (-0.5, -0.3, -0.1, 0.0, 0.1, 0.3, 0.5):                      # quantize -> dequantize
         assert abs(c64[np.searchsorted(b64, np.float32(v), side="right")] - v) < 0.5
     assert all(orc.codebook(64, bb)[2] > 0 for bb in range(2, 7))
+
+
+def test_oracle_bindings_match_header(orc):
+    # oracle.py binds the C restatement with kg_oracle.h's parameter types
+    import ctypes
+    import os
+    import re
+    src = open(os.path.join(os.path.dirname(orc.__file__), "kg_oracle.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"//[^\n]*", "", src)
+    scalar = {"int32_t": ctypes.c_int32, "int": ctypes.c_int, "int64_t": ctypes.c_int64,
+              "uint64_t": ctypes.c_uint64, "float": ctypes.c_float, "double": ctypes.c_double}
+
+    def same(c_type, t):
+        if "*" in c_type:
+            return t in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(t, ctypes._Pointer)
+        want = scalar[c_type.replace("const ", "").strip()]
+        return ctypes.sizeof(t) == ctypes.sizeof(want) and (t in (ctypes.c_float, ctypes.c_double)) == (
+            want in (ctypes.c_float, ctypes.c_double))
+
+    L = orc.lib()
+    n = 0
+    for m in re.finditer(r"([\w \*]+?)\b(or_\w+)\s*\(([^;{]*?)\)\s*;", src, re.S):
+        name = m.group(2)
+        args = [a.strip() for a in " ".join(m.group(3).split()).split(",") if a.strip() and a.strip() != "void"]
+        fn = getattr(L, name)
+        assert fn.argtypes is not None, f"{name} is not bound"
+        n += 1
+        assert len(fn.argtypes) == len(args), name
+        for a, t in zip(args, fn.argtypes):
+            assert same(a if "*" in a else a.rsplit(" ", 1)[0], t), (name, a, t)
+        ret = " ".join(m.group(1).split())
+        if "*" not in ret and ret != "void":
+            assert same(ret, fn.restype), (name, ret, fn.restype)
+    assert n >= 40
