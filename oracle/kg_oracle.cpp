@@ -322,6 +322,26 @@ static void matmul_relu(float *out, const float *w, const float *x, int64_t rows
         out[r] = s > 0.0f ? s : 0.0f;
     }
 }
+// LoraAdapter (crates/katgpt-types/src/lora.rs:5-12): A [rank][in_dim],
+// B [out_dim][rank]; lora_apply (:452-467): buf = A @ in (matmul, row dots),
+// then out[r] += (alpha / rank) * dot(B_r, buf), the product rounded before the add.
+struct Lora {
+    int64_t rank = 0, in_dim = 0, out_dim = 0;
+    float alpha = 0.0f;
+    std::vector<float> a, b;
+};
+static void lora_apply(float *out, const Lora &lo, const float *in, float *buf) {
+    const float scale = lo.alpha / (float)lo.rank;
+    matmul(buf, lo.a.data(), in, lo.rank, lo.in_dim);
+    for (int64_t r = 0; r < lo.out_dim; ++r) {
+        const float sum = dot(&lo.b[r * lo.rank], buf, lo.rank);
+        out[r] += scale * sum;
+    }
+}
+// LoraPair (lora.rs:470-490): [0] reader (forward_prefill), [1] writer
+// (forward_base); rank 0 = None
+static Lora g_lora[2];
+
 static void rmsnorm(float *x, int64_t n) {  // math.rs:56-69
     float ss = sum_sq(x, n);
     float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
@@ -1150,6 +1170,9 @@ struct Seq {
     // SpectralQuant codec (tables per layer); null = TurboQuant
     const std::vector<SqTab> *sqt = nullptr;
     std::vector<uint8_t> sq_idx;
+    // LoRA of forward_base (the pair's writer) and forward_prefill (its reader)
+    const Lora *lora_w = nullptr, *lora_r = nullptr;
+    std::vector<float> lbuf;
     // SP-KV
     const Predictor *pred = nullptr;
     std::vector<float> pbuf, hu, util, bias;
@@ -1166,6 +1189,9 @@ struct Seq {
         hidden.assign(d.m, 0.f); aval = hidden; aidx.assign(d.m, 0);
         logits.assign(d.V, 0.f);
         deltas.assign(d.nblocks, std::vector<float>(d.n, 0.f));
+        lora_r = g_lora[0].rank ? &g_lora[0] : nullptr;
+        lora_w = g_lora[1].rank ? &g_lora[1] : nullptr;
+        lbuf.assign(std::max<int64_t>(std::max(g_lora[0].rank, g_lora[1].rank), 1), 0.f);
         if (mode == OR_MODE_BASE) {
             Kc.assign(d.L * d.B * d.kvd, 0.f);
             Vc = Kc;
@@ -1229,15 +1255,19 @@ struct Seq {
     }
 
     // MLP block shared by all three forwards: xr2=x; norm; relu(W1); sparse/dense W2; += xr2
-    void mlp(const LayerW &lw, bool gamma_norm, const float *gamma) {
+    // with a LoRA: onto the post-ReLU hidden (before the alive count) and onto
+    // W2's output (transformer.rs:2036-2038, 2110-2112)
+    void mlp(const LayerW &lw, bool gamma_norm, const float *gamma, const Lora *lo = nullptr) {
         xr2 = x;
         if (gamma_norm) rmsnorm_gamma(x.data(), gamma, d.n);
         else rmsnorm(x.data(), d.n);
         matmul_relu(hidden.data(), lw.w1, x.data(), d.m, d.n);
+        if (lo) lora_apply(hidden.data(), *lo, x.data(), lbuf.data());
         int64_t alive = sparse_matmul(x.data(), lw.w2, hidden.data(), d.n, d.m, aidx.data(), aval.data());
         // transformer.rs:2080-2101: dense recompute when alive fraction > 1 - threshold
         if ((float)alive / (float)d.m > (1.0f - sparse_threshold))
             matmul(x.data(), lw.w2, hidden.data(), d.n, d.m);
+        if (lo) lora_apply(x.data(), *lo, hidden.data(), lbuf.data());
         add_inplace(x.data(), xr2.data(), d.n);
     }
     float sparse_threshold = 0.8f;
@@ -1249,9 +1279,11 @@ struct Seq {
             depth_route(x.data(), deltas, bidx, W->dq + l * d.n, W->dn + l * d.n, d.n, scaled);
     }
 
-    // transformer.rs:1821-2200 (forward_base, default features, lora=None);
+    // transformer.rs:1821-2200 (forward_base, default features);
     // kog_cpu_fusion applies attn_norm_gamma (:1893-1895) and mlp_norm_gamma
-    // (:2023-2026) at run time through rmsnorm_with_gamma
+    // (:2023-2026) at run time through rmsnorm_with_gamma. With a LoRA
+    // (lora_w) it is added after each of the six projections (:1904-1941,
+    // 2018-2020, 2036-2038, 2110-2112).
     void forward_base(int64_t tok, int64_t pos) {
         add_into(x.data(), W->wte + tok * d.n, W->wpe + pos * d.n, d.n);
         float scale = 1.0f / sqrtf((float)d.hd);
@@ -1260,8 +1292,11 @@ struct Seq {
             rmsnorm_gamma(x.data(), W->ag + l * d.n, d.n);
             xr = x;
             matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+            if (lora_w) lora_apply(q.data(), *lora_w, x.data(), lbuf.data());
             matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+            if (lora_w) lora_apply(k.data(), *lora_w, x.data(), lbuf.data());
             matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+            if (lora_w) lora_apply(v.data(), *lora_w, x.data(), lbuf.data());
             float *K = &Kc[l * d.B * d.kvd], *Vv = &Vc[l * d.B * d.kvd];
             std::memcpy(K + pos * d.kvd, k.data(), d.kvd * 4);
             std::memcpy(Vv + pos * d.kvd, v.data(), d.kvd * 4);
@@ -1271,14 +1306,16 @@ struct Seq {
                                d.kvd, d.hd, pos + 1, scale);
             }
             matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+            if (lora_w) lora_apply(x.data(), *lora_w, att.data(), lbuf.data());
             add_inplace(x.data(), xr.data(), d.n);
-            mlp(lw, true, W->mg + l * d.n);
+            mlp(lw, true, W->mg + l * d.n, lora_w);
             delta_route(l);
         }
         matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
     }
 
-    // transformer.rs:2606-3004 (forward_prefill, default features, lora None):
+    // transformer.rs:2606-3004 (forward_prefill, default features; the LoRA
+    // is the pair's reader, lora_r):
     // per layer, phase A over every prompt position (double rmsnorm, K/V into
     // the f32 cache, Q and the residual kept), then phase B over every
     // position: attention over ALL prompt positions (bidirectional), Wo +
@@ -1301,10 +1338,13 @@ struct Seq {
                 xr = x;
                 rmsnorm(x.data(), d.n);
                 matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+                if (lora_r) lora_apply(k.data(), *lora_r, x.data(), lbuf.data());  // :2681-2687
                 matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+                if (lora_r) lora_apply(v.data(), *lora_r, x.data(), lbuf.data());
                 std::memcpy(K + p * d.kvd, k.data(), d.kvd * 4);
                 std::memcpy(Vv + p * d.kvd, v.data(), d.kvd * 4);
                 matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+                if (lora_r) lora_apply(q.data(), *lora_r, x.data(), lbuf.data());  // :2738-2740
                 std::memcpy(&queries[p * d.n], q.data(), d.n * 4);
                 std::memcpy(&residuals[p * d.n], xr.data(), d.n * 4);
             }
@@ -1318,8 +1358,9 @@ struct Seq {
                                    scale);
                 }
                 matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+                if (lora_r) lora_apply(x.data(), *lora_r, att.data(), lbuf.data());  // :2901-2903
                 add_inplace(x.data(), xr.data(), d.n);
-                mlp(lw, false, nullptr);
+                mlp(lw, false, nullptr, lora_r);
                 delta_route(l);
                 if (d.L > 1) std::memcpy(&hidden[p * d.n], x.data(), d.n * 4);
             }
@@ -1863,6 +1904,40 @@ int64_t or_sq_nearest(float x, const float *centroids, int64_t n) {
 int64_t or_sq_pack(const uint8_t *idx, const uint8_t *bits, int64_t n, uint8_t *out) { return sq_pack(idx, bits, n, out); }
 void or_sq_unpack(const uint8_t *p, int64_t plen, const uint8_t *bits, int64_t n, uint8_t *out) {
     sq_unpack(p, plen, bits, n, out);
+}
+
+// LoraPair for the forwards that take one: which 0 = reader (forward_prefill),
+// 1 = writer (forward_base); rank 0 clears. The adapter must stay inside
+// every projection it is applied to (in_dim <= n_embd, out_dim <= n_embd and
+// <= kv_dim): the reference indexes past the output otherwise.
+int or_set_lora(int which, int64_t rank, int64_t in_dim, int64_t out_dim, float alpha, const float *a,
+                const float *b) {
+    if (which < 0 || which > 1 || rank < 0) return -1;
+    Lora &lo = g_lora[which];
+    if (rank == 0) {
+        lo = Lora();
+        return 0;
+    }
+    if (in_dim < 1 || out_dim < 1 || !a || !b) return -1;
+    lo.rank = rank;
+    lo.in_dim = in_dim;
+    lo.out_dim = out_dim;
+    lo.alpha = alpha;
+    lo.a.assign(a, a + rank * in_dim);
+    lo.b.assign(b, b + out_dim * rank);
+    return 0;
+}
+void or_lora_apply(int64_t rank, int64_t in_dim, int64_t out_dim, float alpha, const float *a, const float *b,
+                   const float *in, float *out) {
+    Lora lo;
+    lo.rank = rank;
+    lo.in_dim = in_dim;
+    lo.out_dim = out_dim;
+    lo.alpha = alpha;
+    lo.a.assign(a, a + rank * in_dim);
+    lo.b.assign(b, b + out_dim * rank);
+    std::vector<float> buf(rank);
+    lora_apply(out, lo, in, buf.data());
 }
 
 // SP-KV pieces for the reference's own unit tests: the utility predictor

@@ -142,6 +142,10 @@ int or_forward_paged(const or_config *c, const float *weights, float *pool, cons
  * tables of SpectralQuantKVCache::from_calibration ([L][kvd*kvd] eigenvectors,
  * [L][kvd] bits, [L][kvd][64] centroids, [L][kvd] level counts, [L] d_eff),
  * one store+dequantize round trip, and forward_quantized over the codec. */
+int or_set_lora(int which, int64_t rank, int64_t in_dim, int64_t out_dim, float alpha, const float *a,
+                const float *b);
+void or_lora_apply(int64_t rank, int64_t in_dim, int64_t out_dim, float alpha, const float *a, const float *b,
+                   const float *in, float *out);
 void or_spkv_predict(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias, const float *h, float *util);
 void or_attention_head_gated(const float *q, const float *K, const float *V, float *out, float *scores, int64_t qoff,
                              int64_t kvoff, int64_t kvd, int64_t hd, int64_t tn, float scale, const float *bias);

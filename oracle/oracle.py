@@ -105,6 +105,8 @@ def lib():
             "or_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
             "or_sq_jacobi": (ctypes.c_int, [P, I64, P, P]),
             "or_spkv_predict": (None, [I64, I64, I64, F32, P, P]),
+            "or_set_lora": (ctypes.c_int, [ctypes.c_int, I64, I64, I64, F32, P, P]),
+            "or_lora_apply": (None, [I64, I64, I64, F32, P, P, P, P]),
             "or_attention_head_gated": (None, [P, P, P, P, P, I64, I64, I64, I64, I64, F32, P]),
             "or_sq_quality_keys": (ctypes.c_int, [ctypes.POINTER(OrSqParams), I64, P, I64, I64, P]),
             "or_sq_allocate": (None, [F32, F32, I64, ctypes.c_int, P, P]),
@@ -648,3 +650,35 @@ def attention_head_gated(q, K, V, kvd, hd, tn, scale, bias=None, qoff=0, kvoff=0
     b = None if bias is None else f32(bias)
     lib().or_attention_head_gated(_p(q), _p(K), _p(V), _p(out), _p(scores), qoff, kvoff, kvd, hd, tn, scale, _p(b))
     return out, scores
+
+
+def lora_apply(a, b, alpha, x, out):
+    """lora_apply (crates/katgpt-types/src/lora.rs:452-467): out + (alpha/rank) * B @ (A @ x)."""
+    a, b, x = f32(a), f32(b), f32(x)
+    out = f32(out).copy()
+    rank, in_dim = a.shape
+    lib().or_lora_apply(rank, in_dim, b.shape[0], alpha, _p(a), _p(b), _p(x), _p(out))
+    return out
+
+
+class lora_pair:
+    """LoraPair (lora.rs:470-490) for the oracle's forwards while the block
+    runs: `reader` = (A, B, alpha) for forward_prefill, `writer` for
+    forward_base; None = no adapter."""
+
+    def __init__(self, reader=None, writer=None):
+        self.pair = (reader, writer)
+
+    def __enter__(self):
+        for which, ad in enumerate(self.pair):
+            if ad is not None:
+                a, b, alpha = f32(ad[0]), f32(ad[1]), float(ad[2])
+                rc = lib().or_set_lora(which, a.shape[0], a.shape[1], b.shape[0], alpha, _p(a), _p(b))
+                if rc:
+                    raise ValueError("bad LoRA adapter")
+        return self
+
+    def __exit__(self, *exc):
+        for which in (0, 1):
+            lib().or_set_lora(which, 0, 0, 0, 0.0, None, None)
+        return False

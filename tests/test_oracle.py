@@ -445,3 +445,49 @@ def test_oracle_bindings_match_header(orc):
         if "*" not in ret and ret != "void":
             assert same(ret, fn.restype), (name, ret, fn.restype)
     assert n >= 40
+
+
+def _adapter(n, rank, seed, scale=0.1):
+    rng = np.random.default_rng(seed)
+    return ((rng.standard_normal((rank, n)) * scale).astype(np.float32),
+            (rng.standard_normal((n, rank)) * scale).astype(np.float32), 8.0)
+
+
+def test_lora_apply_matches_its_definition(orc):
+    # lora_apply (crates/katgpt-types/src/lora.rs:452-467): out += (alpha / rank) * B @ (A @ x)
+    for rank, in_dim, out_dim in ((4, 16, 16), (3, 16, 16), (8, 12, 5), (16, 16, 16)):
+        rng = np.random.default_rng(rank * 100 + in_dim)
+        a = rng.standard_normal((rank, in_dim)).astype(np.float32)
+        b = rng.standard_normal((out_dim, rank)).astype(np.float32)
+        x = rng.standard_normal(in_dim).astype(np.float32)
+        out = rng.standard_normal(out_dim).astype(np.float32)
+        got = orc.lora_apply(a, b, 8.0, x, out)
+        want = out.astype(np.float64) + (8.0 / rank) * (b.astype(np.float64) @ (a.astype(np.float64) @ x))
+        assert np.abs(got - want).max() < 1e-5 * max(1.0, np.abs(want).max())
+
+
+def test_lora_pair_in_forward_base_and_prefill(orc):
+    # generate_with_prefill's LoraPair (src/transformer.rs:3010-3106): the
+    # reader acts in forward_prefill only, the writer in forward_base only;
+    # LoraPair::none() is the plain forward (:5570-5595); the reference's
+    # constant adapter (rank 4, alpha 8, every weight 0.1, :6012-6030) changes the logits
+    cfg = orc.config(n_layer=2)
+    w = orc.weights(cfg, 42)
+    prompt = np.array([26, 3, 9, 14, 1], np.int32)
+    cont = np.array([7, 20, 5], np.int32)
+    plain = orc.prefill_then_decode(cfg, w, prompt, cont)
+    with orc.lora_pair():
+        assert np.array_equal(orc.prefill_then_decode(cfg, w, prompt, cont), plain)
+    const = (np.full((4, 16), 0.1, np.float32), np.full((16, 4), 0.1, np.float32), 8.0)
+    with orc.lora_pair(writer=const):
+        wr = orc.prefill_then_decode(cfg, w, prompt, cont)
+        base_w = orc.run_sequence(cfg, orc.MODE_BASE, w, prompt)[0]
+    assert np.array_equal(wr[0], plain[0])                       # the prefill ignores the writer
+    assert np.abs(wr[1:] - plain[1:]).max() > 1e-3               # decode steps take it
+    assert np.abs(base_w - orc.run_sequence(cfg, orc.MODE_BASE, w, prompt)[0]).max() > 1e-3
+    with orc.lora_pair(reader=_adapter(16, 4, 1)):
+        rd = orc.prefill_then_decode(cfg, w, prompt, cont)
+    assert np.abs(rd[0] - plain[0]).max() > 1e-4                 # the prefill takes the reader
+    zero_b = (np.full((4, 16), 0.3, np.float32), np.zeros((16, 4), np.float32), 8.0)
+    with orc.lora_pair(reader=zero_b, writer=zero_b):            # B = 0 adds exact zeros
+        assert np.array_equal(orc.prefill_then_decode(cfg, w, prompt, cont), plain)
