@@ -262,6 +262,21 @@ int kg_forward_prefill(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const
 int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, int32_t T,
                            float *logits_out, void *stream);
 
+/* LoraPair (crates/katgpt-types/src/lora.rs:470-490) of generate_with_prefill:
+ * which 0 = the reader, applied by kg_forward_prefill (forward_prefill's
+ * `lora`), 1 = the writer, applied by kg_forward_batch / kg_forward_token
+ * (forward_base's `lora`, the decode half). The adapter is a LoraAdapter:
+ * A [rank][in_dim], B [out_dim][rank] (host f32, copied), alpha; lora_apply
+ * (lora.rs:452-467) adds (alpha / rank) * B @ (A @ input) after each of the
+ * six projections (Q, K, V, O, the post-ReLU W1 activations, W2), to the
+ * first out_dim outputs from the first in_dim inputs, in the reference's
+ * operation order. rank 0 removes the adapter (None: the plain forward).
+ * Exact micro path, kv_mode KG_KV_F32; rank, in_dim <= n_embd and out_dim <=
+ * min(n_embd, kv_dim) at most 16 each (the reference indexes past a
+ * projection's output otherwise). Synchronises the device. */
+int kg_set_lora(kg_ctx *ctx, int32_t which, int32_t rank, int32_t in_dim, int32_t out_dim, float alpha,
+                const float *a, const float *b);
+
 /* ---- PagedKVCache + forward_paged (contexts with kv_mode KG_KV_PAGED) ----
  * The reference's copy-on-write page store for DDTree branch exploration
  * (crates/katgpt-transformer/src/kv_cache.rs:187-420): f32 K/V in pages of 16

@@ -62,6 +62,14 @@ class CudaBackend {
     bool is_compiled() const { return kg_is_compiled(ctx_) != 0; }
     void recompile_hint() { /* weights are re-uploaded explicitly by compile() */ }
 
+    // LoraPair of generate_with_prefill: which 0 = reader (forward_prefill),
+    // 1 = writer (forward / forward_batch); rank 0 removes the adapter
+    void set_lora(int32_t which, int32_t rank, int32_t in_dim, int32_t out_dim, float alpha, const float *a,
+                  const float *b) {
+        int rc = kg_set_lora(ctx_, which, rank, in_dim, out_dim, alpha, a, b);
+        if (rc != KG_OK) throw std::runtime_error(std::string("kg_set_lora: ") + kg_last_error(ctx_));
+    }
+
     // batched extension: teacher-forced positions [start, start+T) of n_seq sequences
     void forward_batch(int32_t n_seq, const int32_t *seq_ids, const int32_t *tokens, const int32_t *start_pos,
                        int32_t T, float *logits, float *probs = nullptr) {

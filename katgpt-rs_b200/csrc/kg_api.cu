@@ -318,6 +318,12 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     a.off_sq_eig = (int)off; off += sqm ? L * kvd * kvd : 0;
     a.off_sq_cent = (int)off; off += sqm ? L * kvd * kg::kSqLevels : 0;
     a.off_sq_meta = (int)off; off += sqm ? L * kvd : 0;
+    // the LoraPair of forward_base / forward_prefill (kv_mode F32): two adapters
+    const int64_t lora_fl = c.kv_mode == KG_KV_F32 ? kg::kLoraMax * kg::kLoraMax : 0;
+    for (int w = 0; w < 2; ++w) {
+        a.off_lora_a[w] = (int)off; off += lora_fl;
+        a.off_lora_b[w] = (int)off; off += lora_fl;
+    }
     off = (off + 3) / 4 * 4;
     ctx->pack_floats = off;
     if (off * 4 > 200 * 1024) return bail(fail(ctx, KG_ERR_UNSUPPORTED, "micro weights exceed shared memory"));
@@ -1002,6 +1008,36 @@ int kg_set_mlp_hook(kg_ctx *ctx, float keep, uint64_t seed) {
     ctx->graphs.clear();
     ctx->hook_keep = keep > 0.0f ? std::min(keep, 1.0f) : 0.0f;
     ctx->hook_seed = seed;
+    return KG_OK;
+}
+
+// ---- LoraPair (crates/katgpt-types/src/lora.rs) on the exact micro path ----
+
+int kg_set_lora(kg_ctx *ctx, int32_t which, int32_t rank, int32_t in_dim, int32_t out_dim, float alpha,
+                const float *a, const float *b) {
+    if (!ctx) return KG_ERR_INVALID_ARG;
+    if (which < 0 || which > 1) return fail(ctx, KG_ERR_INVALID_ARG, "which: 0 = reader (forward_prefill), 1 = writer");
+    if (!ctx->micro || ctx->cfg.kv_mode != KG_KV_F32)
+        return fail(ctx, KG_ERR_UNSUPPORTED, "LoRA: forward_base / forward_prefill of the exact path (kv_mode F32)");
+    kg::MicroArgs &m = ctx->margs;
+    if (rank == 0) {
+        m.lora_rank[which] = 0;
+        return KG_OK;
+    }
+    const int32_t max_in = (int32_t)std::min<int64_t>(ctx->n, kg::kLoraMax);
+    const int32_t max_out = (int32_t)std::min<int64_t>(std::min(ctx->n, ctx->kvd), kg::kLoraMax);
+    if (rank < 1 || rank > kg::kLoraMax || in_dim < 1 || in_dim > max_in || out_dim < 1 || out_dim > max_out || !a ||
+        !b)
+        return fail(ctx, KG_ERR_INVALID_ARG, "LoRA adapter: rank 1..16, in_dim 1.." + std::to_string(max_in) +
+                                                 ", out_dim 1.." + std::to_string(max_out) + ", A and B given");
+    KG_CUDA(ctx, cudaSetDevice(ctx->device));
+    KG_CUDA(ctx, cudaDeviceSynchronize());  // no forward in flight reads the pack meanwhile
+    KG_CUDA(ctx, cudaMemcpy(ctx->pack + m.off_lora_a[which], a, (size_t)rank * in_dim * 4, cudaMemcpyHostToDevice));
+    KG_CUDA(ctx, cudaMemcpy(ctx->pack + m.off_lora_b[which], b, (size_t)out_dim * rank * 4, cudaMemcpyHostToDevice));
+    m.lora_rank[which] = rank;
+    m.lora_in[which] = in_dim;
+    m.lora_out[which] = out_dim;
+    m.lora_scale[which] = alpha / (float)rank;  // lora.rs:453
     return KG_OK;
 }
 

@@ -12,9 +12,33 @@
 // The chains are combined as ((acc0+acc1)+(acc2+acc3)) lane-wise and then
 // reduced by horizontal_sum_256 (simd/horizontal.rs:31-51):
 // ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)).
+//
+// The header also compiles as plain C++ (g++ -ffp-contract=off), so that the
+// CPU tests can hold these helpers against the oracle bit for bit.
 #pragma once
 #include <cstdint>
+#ifdef __CUDACC__
 #include <cuda_runtime.h>
+#else
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#define __device__
+#define __forceinline__ inline
+inline float __uint_as_float(uint32_t u) {
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+inline float __int_as_float(int32_t u) {
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+using std::isnan;
+using std::max;
+using std::min;
+#endif
 
 namespace kgx {
 
@@ -56,6 +80,44 @@ __device__ __forceinline__ float dot(const A &a, const B &b) {
 #pragma unroll
     for (int i = T0; i < LEN; ++i) sum = sum + a[i] * b[i];
     return sum;
+}
+
+// simd_dot_f32 for a run-time length len <= 16 (no 32-element chunks): the
+// 8-lane FMA chunks, +0 + hsum, then the scalar tail. Unrolled with
+// predicates so register arrays stay in registers; reads a[i], b[i] for i < len only.
+template <typename A, typename B>
+__device__ __forceinline__ float dot_rt16(const A &a, const B &b, int len) {
+    const int chunks = len >> 3;
+    float r[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) r[l] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+        if (c < chunks) {
+#pragma unroll
+            for (int l = 0; l < 8; ++l) r[l] = fmaf(a[8 * c + l], b[8 * c + l], r[l]);
+        }
+    float sum = 0.0f;
+    sum = sum + hsum8(r);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        if (i >= chunks * 8 && i < len) sum = sum + a[i] * b[i];
+    return sum;
+}
+
+// lora_apply (crates/katgpt-types/src/lora.rs:452-467) for an adapter of at
+// most 16 x 16 x rank 16: buf = A @ in (matmul: row dots over in_dim), then
+// out[r] += scale * dot(B_r, buf) for r < out_dim, the product rounded before
+// the add; scale = alpha / rank. A [rank][in_dim], B [out_dim][rank].
+template <typename O, typename I>
+__device__ __forceinline__ void lora_apply16(O &out, const I &in, const float *A, const float *B, int rank, int in_dim,
+                                             int out_dim, float scale) {
+    float buf[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) buf[j] = j < rank ? dot_rt16(A + j * in_dim, in, in_dim) : 0.0f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+        if (r < out_dim) out[r] = out[r] + scale * dot_rt16(B + r * rank, buf, rank);
 }
 
 // simd_sum_sq (simd/research.rs:298-338): 2 accumulators over 16-chunks.

@@ -41,7 +41,13 @@ struct MicroArgs {
     float *pool;
     const int32_t *ptab;
     int maxp, n_pages;
+    // LoraPair (crates/katgpt-types/src/lora.rs:470-490): [0] the reader
+    // (forward_prefill), [1] the writer (forward_base); A [rank][in_dim] at
+    // off_lora_a, B [out_dim][rank] at off_lora_b in the pack; rank 0 = none
+    int lora_rank[2], lora_in[2], lora_out[2], off_lora_a[2], off_lora_b[2];
+    float lora_scale[2];  // alpha / rank
 };
+constexpr int kLoraMax = 16;  // rank, in_dim and out_dim of a micro-path adapter
 
 inline bool kv_is_tq(int kv_mode) { return kv_mode == KG_KV_TQ || kv_mode == KG_KV_SPKV_TQ; }
 // modes that keep packed codes and norms per (layer, position)

@@ -239,7 +239,21 @@ __device__ __forceinline__ void route_block(float (&x)[N], const float (&delta)[
         }
 }
 
-template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE>
+// lora_apply (crates/katgpt-types/src/lora.rs:452-467) with adapter `w` of the
+// pack (kgx::lora_apply16: rank, in_dim, out_dim <= kLoraMax).
+template <int OUTN, int INN>
+__device__ __forceinline__ void lora_apply(float (&out)[OUTN], const float (&in)[INN], const MicroArgs &p, int w,
+                                           const float *sm) {
+    static_assert(OUTN >= kLoraMax && INN >= kLoraMax && kLoraMax == 16, "adapter wider than the arrays");
+    kgx::lora_apply16(out, in, sm + p.off_lora_a[w], sm + p.off_lora_b[w], p.lora_rank[w], p.lora_in[w],
+                      p.lora_out[w], p.lora_scale[w]);
+}
+
+// LORA: the pair's reader (MODE_PREFILL) or writer (MODE_BASE) is applied
+// after each of the six projections (src/transformer.rs:1904-1941, 2018-2020,
+// 2036-2038, 2110-2112; forward_prefill :2681-2687, 2738-2740, 2901-2903,
+// 2916-2918, 2949-2951).
+template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE, bool LORA = false>
 __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     constexpr int KVD = NKV * HD;
     constexpr int PH = (N / 4 > 16) ? N / 4 : 16;
@@ -341,6 +355,12 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         for (int r = 0; r < KVD; ++r) k[r] = kgx::dot<N>(wk + r * N, x);
 #pragma unroll
         for (int r = 0; r < KVD; ++r) v[r] = kgx::dot<N>(wv + r * N, x);
+        [[maybe_unused]] constexpr int LW = MODE == MODE_PREFILL ? 0 : 1;  // LoraPair: reader in prefill, writer in decode
+        if constexpr (LORA) {
+            lora_apply(q, x, p, LW, sm);
+            lora_apply(k, x, p, LW, sm);
+            lora_apply(v, x, p, LW, sm);
+        }
 
         // forward_paged: this layer's page list of the sequence; a position's K
         // row sits at page * 32 + pos % 16 rows of the pool, its V row 16 rows on
@@ -476,6 +496,7 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
         float xo[N];
 #pragma unroll
         for (int r = 0; r < N; ++r) xo[r] = kgx::dot<N>(wo + r * N, att);
+        if constexpr (LORA) lora_apply(xo, att, p, LW, sm);
 #pragma unroll
         for (int j = 0; j < N; ++j) x[j] = xo[j] + xr[j];
 
@@ -494,6 +515,12 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
             float s = kgx::dot<N>(w1 + r * N, x);
             hid[r] = s > 0.0f ? s : 0.0f;
             alive += hid[r] > 0.0f ? 1 : 0;
+        }
+        if constexpr (LORA) {  // onto the post-ReLU activations; sparse_matmul counts after it
+            lora_apply(hid, x, p, LW, sm);
+            alive = 0;
+#pragma unroll
+            for (int r = 0; r < M; ++r) alive += hid[r] > 0.0f ? 1 : 0;
         }
         if ((float)alive / (float)M > (1.0f - p.sparse_threshold)) {
 #pragma unroll
@@ -529,6 +556,7 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
                 x[r] = s;
             }
         }
+        if constexpr (LORA) lora_apply(x, hid, p, LW, sm);
 #pragma unroll
         for (int j = 0; j < N; ++j) x[j] = x[j] + xr2[j];
 
@@ -621,7 +649,7 @@ __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     }  // sequence groups
 }
 
-template <int MODE, int BLK = 16>
+template <int MODE, int BLK = 16, bool LORA = false>
 cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     const int T = a.T;
     const int SB = 128 / T;
@@ -629,7 +657,7 @@ cudaError_t launch_mode(const MicroArgs &a, cudaStream_t s) {
     const int blocks = (a.n_seq + SB - 1) / SB;
     const size_t smem =
         ((size_t)a.pack_floats + 128 * (BLK + 1) + (MODE == MODE_PREFILL ? 128 * 16 : 0)) * sizeof(float);
-    auto kfn = micro_forward<16, 4, 4, 4, 64, 27, BLK, MODE>;
+    auto kfn = micro_forward<16, 4, 4, 4, 64, 27, BLK, MODE, LORA>;
     cudaError_t e = dev::smem(kfn, smem);
     if (e != cudaSuccess) return e;
     const int n_sm = dev::sm_count(), per_sm = dev::occupancy(kfn, 128, smem);
@@ -668,14 +696,14 @@ int micro_supported(const kg_config &c) {
 cudaError_t launch_micro_prefill(const kg_config &c, const MicroArgs &a, cudaStream_t s) {
     if (a.n_seq <= 0) return cudaSuccess;
     if (a.T < 1 || a.T > 16 || c.kv_mode != KG_KV_F32 || a.start_pos) return cudaErrorInvalidValue;
-    return launch_mode<MODE_PREFILL>(a, s);
+    return a.lora_rank[0] > 0 ? launch_mode<MODE_PREFILL, 16, true>(a, s) : launch_mode<MODE_PREFILL>(a, s);
 }
 
 cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s) {
     if (a.n_seq <= 0) return cudaSuccess;
     if (a.T < 1 || a.T > 16) return cudaErrorInvalidValue;
     switch (c.kv_mode) {
-        case KG_KV_F32: return launch_mode<MODE_BASE>(a, s);
+        case KG_KV_F32: return a.lora_rank[1] > 0 ? launch_mode<MODE_BASE, 16, true>(a, s) : launch_mode<MODE_BASE>(a, s);
         case KG_KV_TQ: return launch_mode<MODE_QUANT>(a, s);
         case KG_KV_SPKV_TQ: return launch_mode<MODE_SPKV>(a, s);
         case KG_KV_PAGED:

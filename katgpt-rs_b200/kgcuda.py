@@ -105,6 +105,7 @@ def lib():
             "kg_kv_snapshot": (ctypes.c_int, [P, I32, I32, P, P]),
             "kg_kv_restore": (ctypes.c_int, [P, I32, I32, P, P]),
             "kg_set_mlp_hook": (ctypes.c_int, [P, F32, ctypes.c_uint64]),
+            "kg_set_lora": (ctypes.c_int, [P, I32, I32, I32, I32, F32, P, P]),
             "kg_rng_seed": (ctypes.c_int, [P, I32, ctypes.c_uint64]),
             "kg_rng_state": (ctypes.c_int, [P, I32, P]),
             "kg_sample_dev": (ctypes.c_int, [P, I32, P, P, I64, P, P]),
@@ -349,6 +350,20 @@ class CudaBackend:
 
     def kv_restore(self, seq, pos, src_dev, stream=None):
         self._check(lib().kg_kv_restore(self._h, seq, pos, ctypes.c_void_p(src_dev), stream))
+
+    def set_lora(self, which, a=None, b=None, alpha=0.0):
+        """LoraPair adapter (crates/katgpt-types/src/lora.rs): which 0 = reader
+        (forward_prefill), 1 = writer (forward_batch / forward); A [rank][in_dim],
+        B [out_dim][rank]; a None adapter removes it."""
+        if a is None:
+            self._check(lib().kg_set_lora(self._h, which, 0, 0, 0, 0.0, None, None))
+            return
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        if a.ndim != 2 or b.ndim != 2 or b.shape[1] != a.shape[0]:
+            raise ValueError("LoRA: A [rank][in_dim] and B [out_dim][rank]")
+        self._check(lib().kg_set_lora(self._h, which, a.shape[0], a.shape[1], b.shape[0], float(alpha),
+                                      _ptr(a), _ptr(b)))
 
     def set_mlp_hook(self, keep, seed=0):
         """Benchmark hook: Bernoulli(keep) sparse hidden activations after W1 (0 = off)."""
