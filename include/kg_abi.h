@@ -271,7 +271,8 @@ int kg_forward_prefill_dev(kg_ctx *ctx, int32_t n_seq, const int32_t *seq_ids, c
  * six projections (Q, K, V, O, the post-ReLU W1 activations, W2), to the
  * first out_dim outputs from the first in_dim inputs, in the reference's
  * operation order. rank 0 removes the adapter (None: the plain forward).
- * Exact micro path, kv_mode KG_KV_F32; rank, in_dim <= n_embd and out_dim <=
+ * Exact micro path: kv_mode KG_KV_F32, or KG_KV_SPKV_TQ for the writer
+ * (forward_sp_kv_quant's `lora`, src/sp_kv/forward.rs:610-822); rank, in_dim <= n_embd and out_dim <=
  * min(n_embd, kv_dim) at most 16 each (the reference indexes past a
  * projection's output otherwise). Synchronises the device. */
 int kg_set_lora(kg_ctx *ctx, int32_t which, int32_t rank, int32_t in_dim, int32_t out_dim, float alpha,

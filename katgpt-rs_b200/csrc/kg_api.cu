@@ -318,8 +318,10 @@ int kg_ctx_create(const kg_config *cfg, int device, kg_ctx **out) {
     a.off_sq_eig = (int)off; off += sqm ? L * kvd * kvd : 0;
     a.off_sq_cent = (int)off; off += sqm ? L * kvd * kg::kSqLevels : 0;
     a.off_sq_meta = (int)off; off += sqm ? L * kvd : 0;
-    // the LoraPair of forward_base / forward_prefill (kv_mode F32): two adapters
-    const int64_t lora_fl = c.kv_mode == KG_KV_F32 ? kg::kLoraMax * kg::kLoraMax : 0;
+    // the LoraPair of forward_base / forward_prefill (kv_mode F32) and the
+    // adapter of forward_sp_kv_quant: two adapters
+    const bool lora_ok = c.kv_mode == KG_KV_F32 || c.kv_mode == KG_KV_SPKV_TQ;
+    const int64_t lora_fl = lora_ok ? kg::kLoraMax * kg::kLoraMax : 0;
     for (int w = 0; w < 2; ++w) {
         a.off_lora_a[w] = (int)off; off += lora_fl;
         a.off_lora_b[w] = (int)off; off += lora_fl;
@@ -1017,8 +1019,10 @@ int kg_set_lora(kg_ctx *ctx, int32_t which, int32_t rank, int32_t in_dim, int32_
                 const float *a, const float *b) {
     if (!ctx) return KG_ERR_INVALID_ARG;
     if (which < 0 || which > 1) return fail(ctx, KG_ERR_INVALID_ARG, "which: 0 = reader (forward_prefill), 1 = writer");
-    if (!ctx->micro || ctx->cfg.kv_mode != KG_KV_F32)
-        return fail(ctx, KG_ERR_UNSUPPORTED, "LoRA: forward_base / forward_prefill of the exact path (kv_mode F32)");
+    const bool spkv = ctx->cfg.kv_mode == KG_KV_SPKV_TQ;
+    if (!ctx->micro || (ctx->cfg.kv_mode != KG_KV_F32 && !spkv) || (spkv && which == 0))
+        return fail(ctx, KG_ERR_UNSUPPORTED,
+                    "LoRA: the exact path's forward_base / forward_prefill (kv_mode F32) or forward_sp_kv_quant (writer)");
     kg::MicroArgs &m = ctx->margs;
     if (rank == 0) {
         m.lora_rank[which] = 0;

@@ -249,10 +249,11 @@ __device__ __forceinline__ void lora_apply(float (&out)[OUTN], const float (&in)
                       p.lora_out[w], p.lora_scale[w]);
 }
 
-// LORA: the pair's reader (MODE_PREFILL) or writer (MODE_BASE) is applied
-// after each of the six projections (src/transformer.rs:1904-1941, 2018-2020,
-// 2036-2038, 2110-2112; forward_prefill :2681-2687, 2738-2740, 2901-2903,
-// 2916-2918, 2949-2951).
+// LORA: the pair's reader (MODE_PREFILL) or writer (MODE_BASE, MODE_SPKV) is
+// applied after each of the six projections (src/transformer.rs:1904-1941,
+// 2018-2020, 2036-2038, 2110-2112; forward_prefill :2681-2687, 2738-2740,
+// 2901-2903, 2916-2918, 2949-2951; src/sp_kv/forward.rs:673-684, 753-756,
+// 769-771, 805-807).
 template <int N, int NH, int NKV, int HD, int M, int VOC, int BLK, int MODE, bool LORA = false>
 __global__ void __launch_bounds__(128, 3) micro_forward(const MicroArgs p) {
     constexpr int KVD = NKV * HD;
@@ -705,7 +706,7 @@ cudaError_t launch_micro(const kg_config &c, const MicroArgs &a, cudaStream_t s)
     switch (c.kv_mode) {
         case KG_KV_F32: return a.lora_rank[1] > 0 ? launch_mode<MODE_BASE, 16, true>(a, s) : launch_mode<MODE_BASE>(a, s);
         case KG_KV_TQ: return launch_mode<MODE_QUANT>(a, s);
-        case KG_KV_SPKV_TQ: return launch_mode<MODE_SPKV>(a, s);
+        case KG_KV_SPKV_TQ: return a.lora_rank[1] > 0 ? launch_mode<MODE_SPKV, 16, true>(a, s) : launch_mode<MODE_SPKV>(a, s);
         case KG_KV_PAGED:
             return c.block_size == 64 ? launch_mode<MODE_PAGED, 64>(a, s) : launch_mode<MODE_PAGED, 16>(a, s);
         case KG_KV_SQ: return launch_mode<MODE_SQ>(a, s);

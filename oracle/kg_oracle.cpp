@@ -1454,7 +1454,8 @@ struct Seq {
         matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
     }
 
-    // src/sp_kv/forward.rs:610-822 (forward_sp_kv_quant, Hard gate, default SpKvConfig)
+    // src/sp_kv/forward.rs:610-822 (forward_sp_kv_quant, Hard gate, default
+    // SpKvConfig; its `lora` is the pair's writer, lora_w)
     void forward_spkv(int64_t tok, int64_t pos) {
         const int64_t window = 128;
         const float threshold = 0.5f;
@@ -1473,8 +1474,11 @@ struct Seq {
             float u = hu[0];
             for (int64_t kh = 1; kh < d.nkv; ++kh) u = fmax_rs(u, hu[kh]);
             matmul(q.data(), lw.wq, x.data(), d.n, d.n);
+            if (lora_w) lora_apply(q.data(), *lora_w, x.data(), lbuf.data());  // forward.rs:673-684
             matmul(k.data(), lw.wk, x.data(), d.kvd, d.n);
+            if (lora_w) lora_apply(k.data(), *lora_w, x.data(), lbuf.data());
             matmul(v.data(), lw.wv, x.data(), d.kvd, d.n);
+            if (lora_w) lora_apply(v.data(), *lora_w, x.data(), lbuf.data());
             // write_gated(pos_is_in_window = true) — types.rs:505-527
             util[l * d.B + pos] = u;
             store_kv(l, pos);
@@ -1504,8 +1508,9 @@ struct Seq {
                                      g * d.hd, d.kvd, d.hd, tn, scale, bias.data());
             }
             matmul(x.data(), lw.wo, att.data(), d.n, d.n);
+            if (lora_w) lora_apply(x.data(), *lora_w, att.data(), lbuf.data());  // forward.rs:753-756
             add_inplace(x.data(), xr.data(), d.n);
-            mlp(lw, false, nullptr);
+            mlp(lw, false, nullptr, lora_w);  // :769-771, 805-807
         }
         matmul(logits.data(), W->lm_head, x.data(), d.V, d.n);
     }

@@ -491,3 +491,19 @@ def test_lora_pair_in_forward_base_and_prefill(orc):
     zero_b = (np.full((4, 16), 0.3, np.float32), np.zeros((16, 4), np.float32), 8.0)
     with orc.lora_pair(reader=zero_b, writer=zero_b):            # B = 0 adds exact zeros
         assert np.array_equal(orc.prefill_then_decode(cfg, w, prompt, cont), plain)
+
+
+def test_lora_in_forward_sp_kv_quant(orc):
+    # forward_sp_kv_quant takes the same optional adapter after the same six
+    # projections (src/sp_kv/forward.rs:673-684, 753-756, 769-771, 805-807)
+    cfg = orc.config(n_layer=2)
+    w = orc.weights(cfg, 42)
+    toks = np.array([26, 3, 9, 14, 1, 7], np.int32)
+    plain = orc.run_sequence(cfg, orc.MODE_SPKV, w, toks)
+    zero_b = (np.full((4, 16), 0.3, np.float32), np.zeros((16, 4), np.float32), 8.0)
+    with orc.lora_pair(writer=zero_b):
+        same = orc.run_sequence(cfg, orc.MODE_SPKV, w, toks)
+    assert np.array_equal(same[0], plain[0]) and np.array_equal(same[1], plain[1])
+    with orc.lora_pair(writer=_adapter(16, 4, 3)):
+        ad = orc.run_sequence(cfg, orc.MODE_SPKV, w, toks)
+    assert np.abs(ad[0] - plain[0]).max() > 1e-3

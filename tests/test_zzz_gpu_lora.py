@@ -65,3 +65,29 @@ def test_lora_writer_in_forward_base_and_removal(kg, orc):
     with pytest.raises(kg.KgError):
         be.set_lora(1, np.zeros((17, 16), np.float32), np.zeros((16, 17), np.float32), 8.0)  # rank > 16
     be.close()
+
+
+def test_lora_writer_in_forward_sp_kv_quant(kg, orc):
+    # forward_sp_kv_quant's adapter (src/sp_kv/forward.rs:610-822): layer-0
+    # codes and norms bit-identical (they depend on no exp), logits within 1e-5
+    # (the gated attention's libm expf), as the SP-KV tests without an adapter
+    n = 16
+    cfg = kg.micro_config(kv_mode=kg.KG_KV_SPKV_TQ, max_seqs=n, n_layer=2)
+    be = kg.CudaBackend(cfg)
+    w = kg.reference_weights(cfg, 42)
+    be.compile(w)
+    wr = _adapter(4, 16, 16, seed=3)
+    with pytest.raises(kg.KgError):
+        be.set_lora(0, *wr)                       # no forward_prefill over SP-KV codes
+    be.set_lora(1, *wr)
+    toks = np.random.default_rng(8).integers(1, 27, size=(n, 16)).astype(np.int32)
+    toks[:, 0] = 26
+    got = be.forward_batch(toks)
+    with orc.lora_pair(writer=wr):
+        for i in range(n):
+            ref, codes, norms, _ = orc.run_sequence(orc.from_kg(cfg), orc.MODE_SPKV, w, toks[i])
+            assert np.abs(got[i] - ref).max() / np.abs(ref).max() <= 1e-5
+            for t in range(16):
+                kp, vp, nr = be.kv_codes(i, 0, t)
+                assert np.array_equal(np.concatenate([kp, vp]), codes[0, t]) and np.array_equal(nr, norms[0, t])
+    be.close()
