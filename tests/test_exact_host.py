@@ -1,8 +1,9 @@
 """The exact-order helpers of the device code (katgpt-rs_b200/csrc/kg_exact.cuh:
-simd_dot_f32 at compile-time and run-time lengths, simd_sum_sq, and the LoRA
-update lora_apply16) compiled as plain C++ and held against the oracle's
-restatements bit for bit, on the CPU: the same source the exact micro kernels
-use, so their arithmetic is checked without a GPU."""
+simd_dot_f32 at compile-time and run-time lengths, simd_sum_sq, simd_sum_f32
+at run-time lengths, the Cephes exp lanes with and without the clamp and its
+scalar tail, and the LoRA update lora_apply16) compiled as plain C++ and held
+against the oracle's restatements bit for bit, on the CPU: the same source the
+exact micro kernels use, so their arithmetic is checked without a GPU."""
 import os
 import subprocess
 
@@ -19,6 +20,10 @@ DRIVER = r"""
 extern "C" {
 float or_dot(const float *a, const float *b, int64_t n);
 float or_sum_sq(const float *x, int64_t n);
+float or_sum(const float *x, int64_t n);
+void or_exp_inplace(float *x, int64_t n);
+float or_exp_sum_inplace(float *x, int64_t n);
+float or_scalar_exp(float x);
 void or_lora_apply(int64_t rank, int64_t in_dim, int64_t out_dim, float alpha, const float *a, const float *b,
                    const float *in, float *out);
 }
@@ -43,6 +48,27 @@ int main() {
         float a[16], b[16];
         for (int i = 0; i < 16; ++i) a[i] = nd(g), b[i] = nd(g);
         same(kgx::dot_rt16(a, b, len), or_dot(a, b, len));
+    }
+    // Cephes exp: vector lanes with the clamp (simd_exp_inplace), without it
+    // (the exp_sum variant), and the scalar tail; sums over run-time lengths
+    std::uniform_real_distribution<float> wide(-110.0f, 95.0f);
+    for (int t = 0; t < 4000; ++t) {
+        float v[8], e[8], f[8];
+        for (int l = 0; l < 8; ++l) v[l] = e[l] = f[l] = t % 2 ? wide(g) : nd(g) * 8.0f;
+        or_exp_inplace(e, 8);
+        or_exp_sum_inplace(f, 8);
+        for (int l = 0; l < 8; ++l) {
+            same(kgx::cephes_lane(v[l], true), e[l]);
+            same(kgx::cephes_lane(v[l], false), f[l]);
+            same(kgx::cephes_scalar(v[l]), or_scalar_exp(v[l]));
+        }
+    }
+    for (int t = 0; t < 3000; ++t) {
+        const int n = 1 + t % 64;
+        float x[64];
+        for (int i = 0; i < 64; ++i) x[i] = nd(g);
+        same(kgx::sum_rt<64>(x, n), or_sum(x, n));
+        if (n < 32) same(kgx::sum_small<31>(x, n), or_sum(x, n));
     }
     for (int t = 0; t < 5000; ++t) {
         const int rank = 1 + g() % 16, in_dim = 1 + g() % 16, out_dim = 1 + g() % 16;
