@@ -152,6 +152,10 @@ struct Ctx {
         if (a.lora_rank[1] > 0) launch<kg::MODE_BASE, true>(n_seq, T, ids, toks, start, logits);
         else launch<kg::MODE_BASE, false>(n_seq, T, ids, toks, start, logits);
     }
+    template <int MODE>
+    void run(int n_seq, int T, const int32_t *ids, const int32_t *toks, float *logits) {
+        launch<MODE, false>(n_seq, T, ids, toks, nullptr, logits);
+    }
     void quantized(int n_seq, int T, const int32_t *ids, const int32_t *toks, float *logits) {
         launch<kg::MODE_QUANT, false>(n_seq, T, ids, toks, nullptr, logits);
     }
@@ -285,6 +289,96 @@ void case_quant(int L, int bits, uint64_t seed) {
     std::printf("%ld %zu\n", count_diff(got.data(), ref.data(), got.size()) + (ctx.err ? 1 : 0), got.size());
 }
 
+// forward_paged of one sequence over 16 positions whose pages (one per
+// layer at block_size 16) sit out of order in the pool
+void case_paged(int L, uint64_t seed) {
+    const or_config c = micro(L);
+    std::vector<float> w(or_weights_count(&c));
+    or_weights_init(&c, 42, 0, 0.02f, w.data());
+    const int T = 16, maxp = B / 16 + 1, n_pages = L + 3, page = 2 * 16 * KVD;
+    std::vector<int32_t> toks = teacher_tokens(1, T, seed), ids(1, 0), ptab(L * maxp, -1);
+    std::vector<int64_t> table(L * maxp, -1);
+    for (int l = 0; l < L; ++l) ptab[l * maxp] = (int32_t)(table[l * maxp] = L + 1 - l);  // pages L+1 .. 2, < n_pages
+    Ctx ctx(L, 1, w);
+    std::vector<float> pool((size_t)n_pages * page, 0.0f), opool = pool;
+    ctx.a.pool = pool.data();
+    ctx.a.ptab = ptab.data();
+    ctx.a.maxp = maxp;
+    ctx.a.n_pages = n_pages;
+    std::vector<float> got((size_t)T * V), ref(got.size());
+    ctx.run<kg::MODE_PAGED>(1, T, ids.data(), toks.data(), got.data());
+    for (int t = 0; t < T; ++t) or_forward_paged(&c, w.data(), opool.data(), table.data(), maxp, toks[t], t, &ref[t * V]);
+    std::printf("%ld %zu\n", count_diff(got.data(), ref.data(), got.size()) + count_diff(pool.data(), opool.data(),
+                pool.size()) + (ctx.err ? 1 : 0), got.size() + pool.size());
+}
+
+// forward_quantized over the SpectralQuant codec: one calibration (the
+// eigenbasis of correlated synthetic keys) for every layer, as from_keys
+void case_sq(int L, float avg_bits, int water_fill, uint64_t seed) {
+    const or_config c = micro(L);
+    std::vector<float> w(or_weights_count(&c));
+    or_weights_init(&c, 42, 0, 0.02f, w.data());
+    std::mt19937 g(seed);
+    std::normal_distribution<float> nd(0.0f, 1.0f);
+    const int ns = 200;
+    std::vector<float> mix(KVD * KVD), X(ns * KVD, 0.0f);
+    for (auto &v : mix) v = nd(g) * 0.4f;
+    for (int s = 0; s < ns; ++s)
+        for (int i = 0; i < KVD; ++i) {
+            const float z = nd(g) * std::pow(1.5f, -(float)i);
+            for (int j = 0; j < KVD; ++j) X[s * KVD + j] += z * mix[i * KVD + j];
+        }
+    std::vector<float> ev(KVD * KVD), eval(KVD);
+    float de = 0.0f;
+    or_sq_calibrate_eigenbasis(X.data(), ns, KVD, ev.data(), eval.data(), &de);
+    std::vector<float> evL, evalL, deL(L, de);
+    for (int l = 0; l < L; ++l) {
+        evL.insert(evL.end(), ev.begin(), ev.end());
+        evalL.insert(evalL.end(), eval.begin(), eval.end());
+    }
+    or_sq_params P{42, 30, 100, avg_bits, 1, 8, 1, 6, water_fill};
+    std::vector<float> eig(L * KVD * KVD), cent(L * KVD * kg::kSqLevels);
+    std::vector<uint8_t> bits(L * KVD);
+    std::vector<int32_t> nlev(L * KVD), dout(L);
+    if (or_sq_build(&P, KVD, L, evL.data(), evalL.data(), deL.data(), eig.data(), bits.data(), cent.data(),
+                    nlev.data(), dout.data())) {
+        std::printf("1 1\n");
+        return;
+    }
+    const int n = 3, T = 16;
+    std::vector<int32_t> toks = teacher_tokens(n, T, seed), ids(n);
+    for (int i = 0; i < n; ++i) ids[i] = i;
+    Ctx ctx(L, n, w);
+    // the pack's SpectralQuant tables: [L][kvd*kvd], [L][kvd][64], [L][kvd] (bits | levels << 8)
+    const int base = (int)ctx.pack.size();
+    ctx.pack.resize(base + L * KVD * KVD + L * KVD * kg::kSqLevels + L * KVD + 4, 0.0f);
+    ctx.a.off_sq_eig = base;
+    ctx.a.off_sq_cent = base + L * KVD * KVD;
+    ctx.a.off_sq_meta = ctx.a.off_sq_cent + L * KVD * kg::kSqLevels;
+    std::memcpy(&ctx.pack[ctx.a.off_sq_eig], eig.data(), eig.size() * 4);
+    std::memcpy(&ctx.pack[ctx.a.off_sq_cent], cent.data(), cent.size() * 4);
+    for (int i = 0; i < L * KVD; ++i) {
+        const int32_t m = (int32_t)bits[i] | (nlev[i] << 8);
+        std::memcpy(&ctx.pack[ctx.a.off_sq_meta + i], &m, 4);
+    }
+    ctx.a.pack = ctx.pack.data();
+    ctx.a.pack_floats = (int)(ctx.pack.size() / 4 * 4);
+    ctx.a.kpl = ctx.a.vpl = KVD;
+    ctx.codes.assign((size_t)n * L * B * 2 * KVD, 0);
+    ctx.a.codes = ctx.codes.data();
+    std::vector<float> got((size_t)n * T * V), ref((size_t)T * V);
+    ctx.run<kg::MODE_SQ>(n, T, ids.data(), toks.data(), got.data());
+    long bad = ctx.err ? 1 : 0;
+    for (int i = 0; i < n; ++i) {
+        std::vector<uint8_t> codes((size_t)L * T * 2 * KVD);
+        std::vector<float> norms((size_t)L * T * 2);
+        or_run_sequence_sq(&c, w.data(), eig.data(), bits.data(), cent.data(), nlev.data(), &toks[i * T], T,
+                           ref.data(), codes.data(), norms.data());
+        bad += count_diff(&got[(size_t)i * T * V], ref.data(), ref.size());
+    }
+    std::printf("%ld %zu\n", bad, got.size());
+}
+
 }  // namespace
 
 int main() {
@@ -298,5 +392,9 @@ int main() {
     case_prefill(2, 5, &w3, nullptr, 43);         // reader only
     case_quant(1, 4, 50);                         // forward_quantized, 4-bit codes
     case_quant(4, 3, 51);                         // 3-bit, four layers (per-layer caches)
+    case_paged(1, 60);                            // forward_paged
+    case_paged(4, 61);
+    case_sq(2, 3.0f, 0, 70);                      // SpectralQuant, uniform widths
+    case_sq(3, 2.5f, 1, 71);                      // water-filled widths
     return 0;
 }

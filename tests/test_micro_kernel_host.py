@@ -3,16 +3,19 @@ kg_micro_kernel.cuh) run on host threads, one per CUDA thread of a block with
 a barrier for __syncthreads (tests/host/micro_forward_host.cpp), against the
 oracle on the CPU: forward_base teacher-forced over 16 positions, with and
 without a writer LoRA adapter; forward_prefill followed by single-token
-decode steps at 1 and 8 layers, with the LoraPair's reader and writer; and
-forward_quantized over 3- and 4-bit TurboQuant codes. Bar: bit-identical
-logits. The GPU tests run the same source compiled for sm_100a."""
+decode steps at 1 and 8 layers, with the LoraPair's reader and writer;
+forward_quantized over 3- and 4-bit TurboQuant codes; forward_paged with pages
+out of order in the pool (the pool's K/V rows compared too); and
+forward_quantized over the SpectralQuant codec, uniform and water-filled
+widths. Bar: bit-identical logits. The GPU tests run the same source compiled
+for sm_100a."""
 import os
 import subprocess
 
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-CASES = 9
+CASES = 13
 
 
 def test_micro_kernel_source_matches_oracle_on_host(orc, tmp_path):
