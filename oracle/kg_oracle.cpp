@@ -1954,6 +1954,15 @@ void or_spkv_predict(int64_t d_model, int64_t hidden, int64_t nkv, float init_bi
     for (int64_t i = 0; i < hidden; ++i) buf[i] = silu(dot(&p.w1[i * d_model], h, d_model) + p.b1[i]);
     for (int64_t k = 0; k < nkv; ++k) util[k] = sigmoid(dot(&p.w2[k * hidden], buf.data(), hidden) + p.b2[k]);
 }
+// The predictor's seeded weights (types.rs:224-258), w1 [hidden][d_model],
+// b1 [hidden], w2 [nkv][hidden], b2 [nkv], one after the other.
+void or_spkv_predictor_weights(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias, float *out) {
+    const Predictor p = make_predictor(d_model, hidden, nkv, init_bias);
+    for (const std::vector<float> *v : {&p.w1, &p.b1, &p.w2, &p.b2}) {
+        std::memcpy(out, v->data(), v->size() * 4);
+        out += v->size();
+    }
+}
 void or_attention_head_gated(const float *q, const float *K, const float *V, float *out, float *scores, int64_t qoff,
                              int64_t kvoff, int64_t kvd, int64_t hd, int64_t tn, float scale, const float *bias) {
     std::vector<float> zero(tn, 0.0f);

@@ -147,6 +147,7 @@ int or_set_lora(int which, int64_t rank, int64_t in_dim, int64_t out_dim, float 
 void or_lora_apply(int64_t rank, int64_t in_dim, int64_t out_dim, float alpha, const float *a, const float *b,
                    const float *in, float *out);
 void or_spkv_predict(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias, const float *h, float *util);
+void or_spkv_predictor_weights(int64_t d_model, int64_t hidden, int64_t nkv, float init_bias, float *out);
 void or_attention_head_gated(const float *q, const float *K, const float *V, float *out, float *scores, int64_t qoff,
                              int64_t kvoff, int64_t kvd, int64_t hd, int64_t tn, float scale, const float *bias);
 int or_sq_jacobi(const double *m, int64_t dim, float *evals, float *evecs);

@@ -105,6 +105,7 @@ def lib():
             "or_sq_calibrate_eigenbasis": (ctypes.c_int, [P, I64, I64, P, P, P]),
             "or_sq_jacobi": (ctypes.c_int, [P, I64, P, P]),
             "or_spkv_predict": (None, [I64, I64, I64, F32, P, P]),
+            "or_spkv_predictor_weights": (None, [I64, I64, I64, F32, P]),
             "or_set_lora": (ctypes.c_int, [ctypes.c_int, I64, I64, I64, F32, P, P]),
             "or_lora_apply": (None, [I64, I64, I64, F32, P, P, P, P]),
             "or_attention_head_gated": (None, [P, P, P, P, P, I64, I64, I64, I64, I64, F32, P]),

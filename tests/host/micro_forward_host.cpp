@@ -4,6 +4,7 @@
 // __syncthreads, the dynamic shared memory as one host buffer. Its logits are
 // compared bit for bit with the oracle's (test infrastructure: built and run
 // by tests/test_micro_kernel_host.py; prints "<mismatches> <values>" per case).
+#include <algorithm>
 #include <barrier>
 #include <cmath>
 #include <cstdint>
@@ -379,6 +380,54 @@ void case_sq(int L, float avg_bits, int water_fill, uint64_t seed) {
     std::printf("%ld %zu\n", bad, got.size());
 }
 
+// forward_sp_kv_quant (Hard gate, 3-bit codes) with and without a writer
+// adapter: layer-0 codes and norms bit-identical, logits within 1e-5 relative
+// (the gated attention calls libm expf); a value off that bar counts as a mismatch
+void case_spkv(int L, const Adapter *wr, uint64_t seed) {
+    const or_config c = micro(L);
+    std::vector<float> w(or_weights_count(&c));
+    or_weights_init(&c, 42, 0, 0.02f, w.data());
+    const int n = 3, T = 16, PH = 16, NKV = 4;
+    std::vector<int32_t> toks = teacher_tokens(n, T, seed), ids(n);
+    for (int i = 0; i < n; ++i) ids[i] = i;
+    Ctx ctx(L, n, w, 3, 3);
+    const int base = (int)ctx.pack.size();
+    ctx.pack.resize(base + PH * N + PH + NKV * PH + NKV + 4, 0.0f);
+    ctx.a.off_pw1 = base;
+    ctx.a.off_pb1 = base + PH * N;
+    ctx.a.off_pw2 = ctx.a.off_pb1 + PH;
+    ctx.a.off_pb2 = ctx.a.off_pw2 + NKV * PH;
+    or_spkv_predictor_weights(N, PH, NKV, 5.0f, &ctx.pack[base]);
+    ctx.a.pack = ctx.pack.data();
+    ctx.a.pack_floats = (int)(ctx.pack.size() / 4 * 4);
+    if (wr) ctx.set_lora(1, wr->rank, wr->in_dim, wr->out_dim, wr->alpha, wr->A.data(), wr->Bm.data());
+    std::vector<float> got((size_t)n * T * V), ref((size_t)T * V);
+    if (wr) ctx.launch<kg::MODE_SPKV, true>(n, T, ids.data(), toks.data(), nullptr, got.data());
+    else ctx.launch<kg::MODE_SPKV, false>(n, T, ids.data(), toks.data(), nullptr, got.data());
+    if (wr) or_set_lora(1, wr->rank, wr->in_dim, wr->out_dim, wr->alpha, wr->A.data(), wr->Bm.data());
+    long bad = ctx.err ? 1 : 0;
+    const int pl = ctx.a.kpl + ctx.a.vpl;
+    for (int i = 0; i < n; ++i) {
+        std::vector<uint8_t> codes((size_t)L * T * pl);
+        std::vector<float> norms((size_t)L * T * 2), util((size_t)L * T);
+        or_run_sequence(&c, OR_MODE_SPKV_QUANT, 3, 3, w.data(), &toks[i * T], T, ref.data(), codes.data(),
+                        norms.data(), util.data());
+        float mx = 0.0f, dmax = 0.0f;
+        for (int k = 0; k < T * V; ++k) {
+            mx = std::max(mx, std::fabs(ref[k]));
+            dmax = std::max(dmax, std::fabs(got[(size_t)i * T * V + k] - ref[k]));
+        }
+        bad += dmax > 1e-5f * mx;
+        for (int t = 0; t < T; ++t) {  // layer 0: slot i, positions t
+            const size_t row = (size_t)i * L * B + t;
+            bad += std::memcmp(&ctx.codes[row * pl], &codes[(size_t)t * pl], pl) != 0;
+            bad += std::memcmp(&ctx.norms[row * 2], &norms[(size_t)t * 2], 8) != 0;
+        }
+    }
+    or_set_lora(1, 0, 0, 0, 0.0f, nullptr, nullptr);
+    std::printf("%ld %d\n", bad, n * (1 + 2 * T));
+}
+
 }  // namespace
 
 int main() {
@@ -396,5 +445,7 @@ int main() {
     case_paged(4, 61);
     case_sq(2, 3.0f, 0, 70);                      // SpectralQuant, uniform widths
     case_sq(3, 2.5f, 1, 71);                      // water-filled widths
+    case_spkv(2, nullptr, 80);                    // forward_sp_kv_quant
+    case_spkv(2, &w4, 81);                        // with the writer adapter
     return 0;
 }

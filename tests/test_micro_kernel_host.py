@@ -7,7 +7,9 @@ decode steps at 1 and 8 layers, with the LoraPair's reader and writer;
 forward_quantized over 3- and 4-bit TurboQuant codes; forward_paged with pages
 out of order in the pool (the pool's K/V rows compared too); and
 forward_quantized over the SpectralQuant codec, uniform and water-filled
-widths. Bar: bit-identical logits. The GPU tests run the same source compiled
+widths; and forward_sp_kv_quant with and without the writer adapter. Bar:
+bit-identical logits (forward_sp_kv_quant: layer-0 codes and norms
+bit-identical, logits within 1e-5 relative, as its GPU tests). The GPU tests run the same source compiled
 for sm_100a."""
 import os
 import subprocess
@@ -15,7 +17,7 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-CASES = 13
+CASES = 15
 
 
 def test_micro_kernel_source_matches_oracle_on_host(orc, tmp_path):
